@@ -1,0 +1,179 @@
+/*
+ * lnet_b200 — C ABI of the B200-native ALPHABET forward path and the
+ * pole-residue Laplace layer.
+ *
+ * Conventions (all entry points):
+ *   - every tensor is a caller-owned, contiguous, row-major DEVICE buffer on
+ *     the current CUDA device; the library allocates nothing per call;
+ *   - work is enqueued on `stream` with no host synchronisation;
+ *   - the return value is LNET_OK or an error code; the message of the last
+ *     error on the calling thread is returned by lnet_b200_last_error();
+ *   - optional metadata pointers may be NULL (= absent);
+ *   - complex per-mode quantities are packed as [..., 2M] = [re(M) | im(M)].
+ *
+ * Reference interfaces each entry point replaces are cited as
+ * path:line relative to the reference project root (daehwa00/lnet-h200-imagenet1k-pg-ab).
+ */
+#ifndef LNET_B200_H
+#define LNET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *lnet_stream_t; /* == cudaStream_t */
+
+enum lnet_b200_status {
+  LNET_OK = 0,
+  LNET_ERR_INVALID_ARGUMENT = 1, /* maps to ValueError on the Python side */
+  LNET_ERR_UNSUPPORTED = 2,      /* shape/dtype outside what the kernels handle (TypeError) */
+  LNET_ERR_WORKSPACE = 3,        /* workspace too small */
+  LNET_ERR_CUDA = 4,             /* a CUDA launch or runtime call failed */
+};
+
+enum lnet_b200_dtype {
+  LNET_F32 = 0,
+  LNET_BF16 = 1,
+  LNET_F64 = 2,
+};
+
+/* Effective ALPHABET parameters, all fp32 device pointers.  Frames are the
+ * materialised constrained frames `block.frame.weight` ([D, 2M]).
+ * Names follow the reference state_dict (src/lnet/alphabet.py:66-125,
+ * src/lnet/pac_tight_frame_models.py:320-443,
+ * src/lnet/pac_laplace_native_input.py:98-138). */
+typedef struct lnet_b200_alphabet_params {
+  int32_t raw_input_dim; /* C   */
+  int32_t model_dim;     /* D   */
+  int32_t modes;         /* M   (frame is [D, 2M]) */
+  int32_t output_dim;    /* K   classes */
+  int32_t conv_kernel;   /* 5 */
+  int32_t conv_dilation; /* 4 */
+  const float *stem_projection;  /* [D, C]  stem.projection.weight */
+  const float *stem_conv_weight; /* [D, K5] stem.local.weight */
+  const float *stem_conv_bias;   /* [D]     stem.local.bias */
+  const float *writer_norm;      /* [D]     forward_block.norm.weight */
+  const float *writer_frame;     /* [D, 2M] forward_block.frame.weight */
+  const float *writer_raw_decay; /* [M] */
+  const float *writer_raw_frequency; /* [M] */
+  const float *writer_direct_scale;  /* [D] */
+  const float *writer_layer_scale;   /* [D] */
+  const float *reader_conv_weight;   /* [D, K5] second_local.weight */
+  const float *reader_conv_bias;     /* [D]     second_local.bias */
+  const float *reader_norm;          /* [D]     backward_block.norm.weight */
+  const float *reader_frame;         /* [D, 2M] backward_block.frame.weight */
+  const float *reader_raw_decay;     /* [M] */
+  const float *reader_raw_frequency; /* [M] */
+  const float *head_weight;          /* [K, 14M] head.classifier.weight */
+  const float *head_bias;            /* [K]      head.classifier.bias */
+} lnet_b200_alphabet_params;
+
+/* One forward request.  x is [B, T, C] in `x_dtype`; metadata are fp32:
+ *   time_delta [B, T] (finite, >= 0), observation_mask [B, T, obs_channels]
+ *   with obs_channels in {1, C}, valid_mask [B, T] (values in [0, 1]).
+ * `act_dtype` selects the storage type of the [B, T, D] activations that
+ * cross HBM between kernels (LNET_F32 or LNET_BF16); state, moments and all
+ * arithmetic are fp32. */
+typedef struct lnet_b200_alphabet_request {
+  int64_t batch;
+  int64_t steps;
+  int32_t x_dtype;
+  int32_t act_dtype;
+  const void *x;
+  const float *time_delta;
+  const float *observation_mask;
+  int32_t obs_channels;
+  const float *valid_mask;
+} lnet_b200_alphabet_request;
+
+/* Bytes of device workspace lnet_b200_alphabet_forward needs for `req`. */
+int lnet_b200_alphabet_workspace_size(const lnet_b200_alphabet_params *params,
+                                      const lnet_b200_alphabet_request *req,
+                                      size_t *bytes);
+
+/* Full `Alphabet.forward(inputs, time_delta=, observation_mask=, valid_mask=)`
+ * -> logits [B, K] fp32.  Replaces the eager/Triton dispatch of
+ * src/lnet/alphabet.py:350-416 (Alphabet.forward) and everything below it.
+ * Optional outputs (NULL = not wanted): writer_moments / reader_moments
+ * [B, 7M] raw (pre radial-log) moments. Workspace must be 256-byte aligned. */
+int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
+                               const lnet_b200_alphabet_request *req, void *workspace,
+                               size_t workspace_bytes, float *logits, float *writer_moments,
+                               float *reader_moments, lnet_stream_t stream);
+
+/* Stage entry points (same request/params conventions; intermediate tensors
+ * fp32 [B, T, D] unless noted). */
+
+/* ZOH coefficients a = exp(p dt), gamma = (a - 1)/p with p = -damping + i freq,
+ * damping = 1e-3 + (2 - 1e-3) sigmoid(raw_decay), freq = pi tanh(raw_frequency).
+ * dt == NULL -> unit grid, outputs [M]; else dt is [steps] and outputs are
+ * [steps, M].  Replaces src/lnet/pac_real2d_math.py:20-53 and
+ * src/lnet/pac_tight_frame_models.py:458-459,487-491. */
+int lnet_b200_zoh(const float *raw_decay, const float *raw_frequency, int32_t modes,
+                  const float *dt, int64_t steps, float *a_re, float *a_im, float *g_re,
+                  float *g_im, lnet_stream_t stream);
+
+/* Raw stem: first_local = valid * SiLU(DWConv(P (x * obs * valid))) (or the
+ * physical-time conv when time_delta is given).  Replaces
+ * AlphabetBackbone._edge_stem (src/lnet/alphabet_backbone.py:593-676). */
+int lnet_b200_stem(const lnet_b200_alphabet_params *params,
+                   const lnet_b200_alphabet_request *req, void *workspace,
+                   size_t workspace_bytes, float *first_local, lnet_stream_t stream);
+
+/* Tied writer block: stream v [B, T, D] and raw moments [B, 7M].  Replaces
+ * _TightFrameBlock.forward (src/lnet/pac_tight_frame_models.py:717-1507) as
+ * called by AlphabetBackbone._writer (src/lnet/alphabet_backbone.py:704-718). */
+int lnet_b200_writer(const lnet_b200_alphabet_params *params,
+                     const lnet_b200_alphabet_request *req, const float *first_local,
+                     void *workspace, size_t workspace_bytes, float *stream_out,
+                     float *moments, lnet_stream_t stream);
+
+/* Terminal reader: local conv of the masked writer stream, SiLU, mask,
+ * moments-only reader block -> raw moments [B, 7M].  Replaces
+ * AlphabetBackbone._terminal_reader (src/lnet/alphabet_backbone.py:872-992). */
+int lnet_b200_reader(const lnet_b200_alphabet_params *params,
+                     const lnet_b200_alphabet_request *req, const float *first_stream,
+                     void *workspace, size_t workspace_bytes, float *moments,
+                     lnet_stream_t stream);
+
+/* Head: radial-log of both moment banks, concatenation, affine readout.
+ * Replaces radial_log_lag124_moments + _ModalAffineHead
+ * (src/lnet/alphabet.py:29-63) and modal_affine_readout_inference
+ * (src/lnet/pac_triton_modal_affine_readout_inference.py:73-111). */
+int lnet_b200_head(const lnet_b200_alphabet_params *params, int64_t batch,
+                   const float *writer_moments, const float *reader_moments, float *logits,
+                   lnet_stream_t stream);
+
+/* Pole-residue Laplace layer in float64:
+ *   y_t = sum_{m,i} R[o, m, i] s_t[m, i] + D x_t + bias,
+ *   s_t[m, i] = exp(p_m dt) s_{t-1}[m, i] + dt phi1(p_m dt) x_t[i],
+ *   p_m = -(softplus(raw_decay_m) + min_decay).
+ * x and y are [B, T, Dm] in `x_dtype` (LNET_F32 or LNET_F64); parameters are
+ * float64: raw_decay [M], residues [Dm, M, Dm], direct [Dm, Dm], bias [Dm].
+ * Replaces PoleResidueTemporalMixing.forward (src/lnet/laplace.py:126-159). */
+int lnet_b200_laplace_workspace_size(int64_t batch, int64_t steps, int32_t model_dim,
+                                     int32_t modes, size_t *bytes);
+int lnet_b200_laplace_forward(const double *raw_decay, const double *residues,
+                              const double *direct, const double *bias, int32_t model_dim,
+                              int32_t modes, double dt, double min_decay, int32_t x_dtype,
+                              const void *x, int64_t batch, int64_t steps, void *y,
+                              void *workspace, size_t workspace_bytes, lnet_stream_t stream);
+
+/* Number of kernel launches the most recent successful lnet_b200_* call on
+ * this thread enqueued. */
+int lnet_b200_last_launch_count(void);
+
+/* Message of the last error on the calling thread ("" if none). */
+const char *lnet_b200_last_error(void);
+
+/* Library version string. */
+const char *lnet_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LNET_B200_H */

@@ -1,0 +1,383 @@
+// Orchestration of the ALPHABET forward path behind the lnet_b200 C ABI.
+//
+// Two routes share one workspace plan:
+//   * the general route (generic_kernels.cuh): one stage kernel per
+//     reference operation, used whenever time_delta is present and for the
+//     stage-level entry points;
+//   * the fused unit-grid route (fused_path.cuh): stem+writer and reader as
+//     single chunked-scan kernels, used by lnet_b200_alphabet_forward when no
+//     time_delta is given and the shape fits the fused kernels.
+#include <algorithm>
+
+#include "common.cuh"
+#include "fused_path.cuh"
+#include "generic_kernels.cuh"
+
+namespace lnet {
+
+constexpr int kScanChunk = 64;
+constexpr int kMomChunk = 64;
+
+static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), 148 * 32)); }
+
+// ---------------------------------------------------------------- validation
+static int check_params(const lnet_b200_alphabet_params *p) {
+  if (!p) return fail(LNET_ERR_INVALID_ARGUMENT, "params must not be NULL");
+  if (p->raw_input_dim < 1 || p->model_dim < 1 || p->modes < 1 || p->output_dim < 1)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "dimensions must be positive (C=%d D=%d M=%d K=%d)",
+                p->raw_input_dim, p->model_dim, p->modes, p->output_dim);
+  if (p->conv_kernel < 1 || p->conv_kernel > 16 || p->conv_dilation < 1)
+    return fail(LNET_ERR_UNSUPPORTED, "conv kernel %d / dilation %d unsupported", p->conv_kernel,
+                p->conv_dilation);
+  if ((p->conv_dilation * (p->conv_kernel - 1)) % 2 != 0)
+    return fail(LNET_ERR_UNSUPPORTED, "odd receptive span (same padding) is not supported");
+  const void *need[] = {p->stem_projection, p->stem_conv_weight, p->stem_conv_bias,
+                        p->writer_norm, p->writer_frame, p->writer_raw_decay,
+                        p->writer_raw_frequency, p->writer_direct_scale, p->writer_layer_scale,
+                        p->reader_conv_weight, p->reader_conv_bias, p->reader_norm,
+                        p->reader_frame, p->reader_raw_decay, p->reader_raw_frequency,
+                        p->head_weight, p->head_bias};
+  for (const void *q : need)
+    if (!q) return fail(LNET_ERR_INVALID_ARGUMENT, "a parameter pointer is NULL");
+  return LNET_OK;
+}
+
+static int check_request(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r) {
+  if (!r) return fail(LNET_ERR_INVALID_ARGUMENT, "request must not be NULL");
+  if (r->batch < 0 || r->steps < 0) return fail(LNET_ERR_INVALID_ARGUMENT, "negative batch/steps");
+  if (r->batch > 65535) return fail(LNET_ERR_UNSUPPORTED, "batch > 65535 per call");
+  if (r->x_dtype != LNET_F32 && r->x_dtype != LNET_BF16)
+    return fail(LNET_ERR_UNSUPPORTED, "x dtype must be float32 or bfloat16");
+  if (r->act_dtype != LNET_F32 && r->act_dtype != LNET_BF16)
+    return fail(LNET_ERR_UNSUPPORTED, "activation dtype must be float32 or bfloat16");
+  if (r->batch > 0 && r->steps > 0 && !r->x) return fail(LNET_ERR_INVALID_ARGUMENT, "x is NULL");
+  if (r->observation_mask && r->obs_channels != 1 && r->obs_channels != p->raw_input_dim)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "observation_mask channels must be 1 or C");
+  return LNET_OK;
+}
+
+// ---------------------------------------------------------------- workspace plan
+struct Plan {
+  float *xm = nullptr;        // [BT, C]   masked raw input
+  float *proj = nullptr;      // [BT, D]   projection / reader encoded
+  float *first_local = nullptr;  // [BT, D]
+  float *xhat = nullptr;      // [BT, D]
+  float *drive = nullptr;     // [BT, 2M]  drive, then states
+  float *stream = nullptr;    // [BT, D]   writer stream
+  float *modal = nullptr;     // [BT, D]
+  float *ts = nullptr;        // [BT]
+  float *carries = nullptr;   // [B, nchunk, 4M]
+  float *partial = nullptr;   // moment partials
+  float *a_tab = nullptr;     // [4][M] writer a_re, a_im, reader a_re, a_im
+  float *moments = nullptr;   // [2][B][7M]
+  float *feats = nullptr;     // [B, 14M]
+  FusedWorkspace fused;       // fused-route scratch
+};
+
+static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p,
+                         const lnet_b200_alphabet_request *r) {
+  const int64_t bt = r->batch * r->steps;
+  const int D = p->model_dim, M = p->modes, C = p->raw_input_dim;
+  const int64_t n_scan = cdiv(std::max<int64_t>(r->steps, 1), kScanChunk);
+  const int64_t n_mom = cdiv(std::max<int64_t>(r->steps, 1), kMomChunk);
+  pl.xm = ar.take<float>((size_t)bt * C);
+  pl.proj = ar.take<float>((size_t)bt * D);
+  pl.first_local = ar.take<float>((size_t)bt * D);
+  pl.xhat = ar.take<float>((size_t)bt * D);
+  pl.drive = ar.take<float>((size_t)bt * 2 * M);
+  pl.stream = ar.take<float>((size_t)bt * D);
+  pl.modal = ar.take<float>((size_t)bt * D);
+  pl.ts = ar.take<float>((size_t)bt);
+  pl.carries = ar.take<float>((size_t)r->batch * n_scan * 4 * M);
+  pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
+  pl.a_tab = ar.take<float>((size_t)4 * M);
+  pl.moments = ar.take<float>((size_t)2 * r->batch * 7 * M);
+  pl.feats = ar.take<float>((size_t)r->batch * 14 * M);
+}
+
+// ---------------------------------------------------------------- general-route stages
+template <typename TX>
+static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                        Plan &pl, float *first_local, cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const int C = p->raw_input_dim, D = p->model_dim;
+  const TX *x = (const TX *)r->x;
+  dim3 g((unsigned)cdiv(bt, 64), (unsigned)cdiv(D, 64));
+  if (r->observation_mask || r->valid_mask) {
+    mask_inputs_kernel<TX><<<grid_for(bt * C), 256, 0, st>>>(x, r->observation_mask,
+                                                             r->obs_channels, r->valid_mask,
+                                                             pl.xm, bt, C);
+    LNET_TRY(after_launch("mask_inputs_kernel"));
+    gemm_nt_kernel<float><<<g, 256, 0, st>>>(pl.xm, C, p->stem_projection, C, 1, pl.proj, D, bt,
+                                             D, C);
+  } else {
+    gemm_nt_kernel<TX><<<g, 256, 0, st>>>(x, C, p->stem_projection, C, 1, pl.proj, D, bt, D, C);
+  }
+  LNET_TRY(after_launch("gemm_nt_kernel(stem)"));
+  if (r->time_delta) {
+    timestamps_kernel<<<(unsigned)cdiv(B, 128), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
+    LNET_TRY(after_launch("timestamps_kernel"));
+    dwconv_physical_kernel<float><<<(unsigned)bt, 128, 0, st>>>(
+        pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, pl.ts, r->valid_mask,
+        first_local, T, D, p->conv_kernel, p->conv_dilation);
+    return after_launch("dwconv_physical_kernel(stem)");
+  }
+  dwconv_unit_kernel<float><<<grid_for(bt * D), 256, 0, st>>>(
+      pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask, first_local, B, T,
+      D, p->conv_kernel, p->conv_dilation);
+  return after_launch("dwconv_unit_kernel(stem)");
+}
+
+// Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
+static int block_scan_moments(const float *in, const float *norm, const float *frame,
+                              const float *raw_decay, const float *raw_freq, float *a_re,
+                              float *a_im, const float *event_mask, int obs_channels,
+                              const lnet_b200_alphabet_request *r, int D, int M, Plan &pl,
+                              float *moments, cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, norm, pl.xhat, bt, D);
+  LNET_TRY(after_launch("rmsnorm_kernel"));
+  dim3 g((unsigned)cdiv(bt, 64), (unsigned)cdiv(2 * M, 64));
+  gemm_nt_kernel<float><<<g, 256, 0, st>>>(pl.xhat, D, frame, 1, 2 * M, pl.drive, 2 * M, bt,
+                                           2 * M, D);
+  LNET_TRY(after_launch("gemm_nt_kernel(drive)"));
+  drive_kernel<<<grid_for(bt * M), 256, 0, st>>>(pl.drive, raw_decay, raw_freq, r->time_delta,
+                                                 event_mask, obs_channels, bt, M);
+  LNET_TRY(after_launch("drive_kernel"));
+  if (!r->time_delta) {
+    zoh_kernel<<<1, 128, 0, st>>>(raw_decay, raw_freq, M, nullptr, 1, a_re, a_im, nullptr,
+                                  nullptr);
+    LNET_TRY(after_launch("zoh_kernel"));
+  }
+  const int64_t n_scan = cdiv(T, kScanChunk);
+  const int threads = std::min(128, (int)cdiv(M, 32) * 32);
+  dim3 gs((unsigned)n_scan, (unsigned)B);
+  scan_local_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
+                                            r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
+  LNET_TRY(after_launch("scan_local_kernel"));
+  scan_carry_kernel<<<(unsigned)cdiv(B * M, 128), 128, 0, st>>>(pl.carries, B, M, n_scan);
+  LNET_TRY(after_launch("scan_carry_kernel"));
+  scan_apply_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
+                                            r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
+  LNET_TRY(after_launch("scan_apply_kernel"));
+  const int64_t n_mom = cdiv(T, kMomChunk);
+  dim3 gm((unsigned)n_mom, (unsigned)B);
+  if (r->time_delta) {
+    pt_moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, pl.ts, r->time_delta,
+                                                      r->valid_mask, pl.partial, T, M, n_mom);
+    LNET_TRY(after_launch("pt_moments_partial_kernel"));
+    pt_moments_finalize_kernel<<<(unsigned)B, threads, 0, st>>>(pl.partial, moments, M, n_mom);
+    return after_launch("pt_moments_finalize_kernel");
+  }
+  moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, r->valid_mask, pl.partial, T, M,
+                                                 kMomChunk, n_mom);
+  LNET_TRY(after_launch("moments_partial_kernel"));
+  moments_finalize_kernel<<<(unsigned)B, 256, 0, st>>>(pl.partial, r->valid_mask, moments, T, M,
+                                                       n_mom);
+  return after_launch("moments_finalize_kernel");
+}
+
+static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                          const float *first_local, Plan &pl, float *stream_out, float *moments,
+                          cudaStream_t st) {
+  const int64_t bt = r->batch * r->steps;
+  const int D = p->model_dim, M = p->modes;
+  LNET_TRY(block_scan_moments(first_local, p->writer_norm, p->writer_frame, p->writer_raw_decay,
+                              p->writer_raw_frequency, pl.a_tab, pl.a_tab + M,
+                              r->observation_mask, r->obs_channels, r, D, M, pl, moments, st));
+  dim3 g((unsigned)cdiv(bt, 64), (unsigned)cdiv(D, 64));
+  gemm_nt_kernel<float><<<g, 256, 0, st>>>(pl.drive, 2 * M, p->writer_frame, 2 * M, 1, pl.modal,
+                                           D, bt, D, 2 * M);
+  LNET_TRY(after_launch("gemm_nt_kernel(synthesis)"));
+  residual_kernel<<<grid_for(bt * D), 256, 0, st>>>(first_local, pl.xhat, pl.modal,
+                                                     p->writer_direct_scale,
+                                                     p->writer_layer_scale, stream_out, bt, D);
+  return after_launch("residual_kernel");
+}
+
+static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                          const float *first_stream, Plan &pl, float *moments, cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const int D = p->model_dim, M = p->modes;
+  if (r->time_delta) {
+    if (!pl.ts) return fail(LNET_ERR_INVALID_ARGUMENT, "timestamps missing");
+    timestamps_kernel<<<(unsigned)cdiv(B, 128), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
+    LNET_TRY(after_launch("timestamps_kernel"));
+    dwconv_physical_kernel<float><<<(unsigned)bt, 128, 0, st>>>(
+        first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, pl.ts,
+        r->valid_mask, pl.proj, T, D, p->conv_kernel, p->conv_dilation);
+    LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
+  } else {
+    dwconv_unit_kernel<float><<<grid_for(bt * D), 256, 0, st>>>(
+        first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, r->valid_mask,
+        pl.proj, B, T, D, p->conv_kernel, p->conv_dilation);
+    LNET_TRY(after_launch("dwconv_unit_kernel(reader)"));
+  }
+  // the reader block sees no observation mask (src/lnet/alphabet.py:384-389)
+  return block_scan_moments(pl.proj, p->reader_norm, p->reader_frame, p->reader_raw_decay,
+                            p->reader_raw_frequency, pl.a_tab + 2 * M, pl.a_tab + 3 * M, nullptr,
+                            1, r, D, M, pl, moments, st);
+}
+
+static int head_run(const lnet_b200_alphabet_params *p, int64_t B, const float *wm,
+                    const float *rm, float *feats, float *logits, cudaStream_t st) {
+  const int M = p->modes, K = p->output_dim;
+  head_features_kernel<<<grid_for(B * 14 * M), 256, 0, st>>>(wm, rm, feats, B, M);
+  LNET_TRY(after_launch("head_features_kernel"));
+  dim3 g((unsigned)cdiv(K, 8), (unsigned)B);
+  head_logits_kernel<<<g, 256, 0, st>>>(feats, p->head_weight, p->head_bias, logits, B, K,
+                                        14 * M);
+  return after_launch("head_logits_kernel");
+}
+
+static int plan_all(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                    void *ws, size_t ws_bytes, Plan &pl, bool fused) {
+  Arena measure(nullptr, 0);
+  Plan dummy;
+  if (fused)
+    plan_fused(measure, dummy.fused, p, r);
+  else
+    plan_generic(measure, dummy, p, r);
+  if (ws_bytes < measure.used || !ws)
+    return fail(LNET_ERR_WORKSPACE, "workspace of %zu bytes < required %zu", ws_bytes,
+                measure.used);
+  Arena ar(ws, ws_bytes);
+  if (fused)
+    plan_fused(ar, pl.fused, p, r);
+  else
+    plan_generic(ar, pl, p, r);
+  return LNET_OK;
+}
+
+static bool use_fused(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r) {
+  return !r->time_delta && fused_supported(p, r);
+}
+
+}  // namespace lnet
+
+using namespace lnet;
+
+extern "C" int lnet_b200_alphabet_workspace_size(const lnet_b200_alphabet_params *params,
+                                                 const lnet_b200_alphabet_request *req,
+                                                 size_t *bytes) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (!bytes) return fail(LNET_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+  Arena a(nullptr, 0), b(nullptr, 0);
+  Plan pa, pb;
+  plan_generic(a, pa, params, req);
+  size_t need = a.used;
+  if (use_fused(params, req)) {
+    plan_fused(b, pb.fused, params, req);
+    need = std::max(need, b.used);
+  }
+  *bytes = need;
+  return LNET_OK;
+}
+
+extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
+                                          const lnet_b200_alphabet_request *req, void *workspace,
+                                          size_t workspace_bytes, float *logits,
+                                          float *writer_moments, float *reader_moments,
+                                          lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (req->batch == 0) return LNET_OK;
+  if (req->steps == 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "sequences must contain at least one step");
+  if (!logits) return fail(LNET_ERR_INVALID_ARGUMENT, "logits is NULL");
+  auto st = (cudaStream_t)stream;
+  const int64_t B = req->batch;
+  const int M = params->modes;
+  Plan pl;
+  if (use_fused(params, req)) {
+    LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, true));
+    float *wm = writer_moments ? writer_moments : pl.fused.moments;
+    float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
+    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, st));
+    return fused_head(params, B, wm, rm, logits, st);
+  }
+  LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
+  float *wm = writer_moments ? writer_moments : pl.moments;
+  float *rm = reader_moments ? reader_moments : pl.moments + B * 7 * M;
+  if (req->x_dtype == LNET_BF16)
+    LNET_TRY(stem_generic<__nv_bfloat16>(params, req, pl, pl.first_local, st));
+  else
+    LNET_TRY(stem_generic<float>(params, req, pl, pl.first_local, st));
+  LNET_TRY(writer_generic(params, req, pl.first_local, pl, pl.stream, wm, st));
+  LNET_TRY(reader_generic(params, req, pl.stream, pl, rm, st));
+  return head_run(params, B, wm, rm, pl.feats, logits, st);
+}
+
+extern "C" int lnet_b200_stem(const lnet_b200_alphabet_params *params,
+                              const lnet_b200_alphabet_request *req, void *workspace,
+                              size_t workspace_bytes, float *first_local, lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (req->batch == 0 || req->steps == 0) return LNET_OK;
+  Plan pl;
+  LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
+  if (req->x_dtype == LNET_BF16)
+    return stem_generic<__nv_bfloat16>(params, req, pl, first_local, (cudaStream_t)stream);
+  return stem_generic<float>(params, req, pl, first_local, (cudaStream_t)stream);
+}
+
+extern "C" int lnet_b200_writer(const lnet_b200_alphabet_params *params,
+                                const lnet_b200_alphabet_request *req, const float *first_local,
+                                void *workspace, size_t workspace_bytes, float *stream_out,
+                                float *moments, lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (req->batch == 0 || req->steps == 0) return LNET_OK;
+  Plan pl;
+  LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
+  auto st = (cudaStream_t)stream;
+  if (req->time_delta) {
+    timestamps_kernel<<<(unsigned)cdiv(req->batch, 128), 128, 0, st>>>(req->time_delta, pl.ts,
+                                                                       req->batch, req->steps);
+    LNET_TRY(after_launch("timestamps_kernel"));
+  }
+  return writer_generic(params, req, first_local, pl, stream_out, moments, st);
+}
+
+extern "C" int lnet_b200_reader(const lnet_b200_alphabet_params *params,
+                                const lnet_b200_alphabet_request *req, const float *first_stream,
+                                void *workspace, size_t workspace_bytes, float *moments,
+                                lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (req->batch == 0 || req->steps == 0) return LNET_OK;
+  Plan pl;
+  LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
+  return reader_generic(params, req, first_stream, pl, moments, (cudaStream_t)stream);
+}
+
+extern "C" int lnet_b200_head(const lnet_b200_alphabet_params *params, int64_t batch,
+                              const float *writer_moments, const float *reader_moments,
+                              float *logits, lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  if (batch <= 0) return LNET_OK;
+  if (!writer_moments || !reader_moments || !logits)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "head: NULL tensor pointer");
+  return fused_head(params, batch, writer_moments, reader_moments, logits, (cudaStream_t)stream);
+}
+
+extern "C" int lnet_b200_zoh(const float *raw_decay, const float *raw_frequency, int32_t modes,
+                             const float *dt, int64_t steps, float *a_re, float *a_im,
+                             float *g_re, float *g_im, lnet_stream_t stream) {
+  reset_launches();
+  if (modes < 1) return fail(LNET_ERR_INVALID_ARGUMENT, "modes must be positive");
+  if (!raw_decay || !raw_frequency || !a_re || !a_im)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "zoh: NULL tensor pointer");
+  if (dt && steps < 1) return LNET_OK;
+  int64_t n = (dt ? steps : 1) * modes;
+  zoh_kernel<<<grid_for(n), 256, 0, (cudaStream_t)stream>>>(raw_decay, raw_frequency, modes, dt,
+                                                            steps, a_re, a_im, g_re, g_im);
+  return after_launch("zoh_kernel");
+}

@@ -1,0 +1,625 @@
+// Stage kernels of the general ALPHABET path (every metadata combination).
+//
+// Each kernel is one bandwidth-bound pass over [B, T, *] fp32 tensors; the
+// unit-grid fast path (fused_writer.cu / fused_reader.cu) replaces most of
+// them when no time_delta is given.
+#pragma once
+
+#include "common.cuh"
+
+namespace lnet {
+
+// ---------------------------------------------------------------- GEMM
+// C[r, n] = sum_k A[r, k] * Bm[n * ldbn + k * ldbk]   (fp32 FFMA, 64x64 tiles)
+template <typename TA>
+__global__ void __launch_bounds__(256) gemm_nt_kernel(const TA *__restrict__ A, int64_t lda,
+                                                      const float *__restrict__ Bm,
+                                                      int64_t ldbn, int64_t ldbk,
+                                                      float *__restrict__ C, int64_t ldc,
+                                                      int64_t rows, int n_cols, int k_dim) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t r0 = (int64_t)blockIdx.x * 64;
+  const int n0 = blockIdx.y * 64;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < k_dim; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      int r = i >> 4, c = i & 15;
+      int64_t gr = r0 + r;
+      int gk = k0 + c;
+      As[c][r] = (gr < rows && gk < k_dim) ? load_f(A, gr * lda + gk) : 0.f;
+      int gn = n0 + r;
+      Bs[c][r] = (gn < n_cols && gk < k_dim) ? Bm[(int64_t)gn * ldbn + (int64_t)gk * ldbk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t gr = r0 + ty * 4 + i;
+    if (gr >= rows) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int gn = n0 + tx * 4 + j;
+      if (gn < n_cols) C[gr * ldc + gn] = acc[i][j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- stem input mask
+// xm[b,t,c] = x[b,t,c] * obs[b,t,c|0] * valid[b,t]
+template <typename TX>
+__global__ void mask_inputs_kernel(const TX *__restrict__ x, const float *__restrict__ obs,
+                                   int obs_channels, const float *__restrict__ valid,
+                                   float *__restrict__ xm, int64_t tokens, int channels) {
+  int64_t n = tokens * channels;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t tok = i / channels;
+    int c = (int)(i - tok * channels);
+    float v = load_f(x, i);
+    if (obs) v *= obs[tok * obs_channels + (obs_channels == 1 ? 0 : c)];
+    if (valid) v *= valid[tok];
+    xm[i] = v;
+  }
+}
+
+// ---------------------------------------------------------------- unit-grid depthwise conv
+// out[b,t,d] = post[b,t] * SiLU(bias[d] + sum_k w[d,k] * pre[b,t] in[b, t + k*dil - pad, d])
+template <typename TI>
+__global__ void dwconv_unit_kernel(const TI *__restrict__ in, const float *__restrict__ w,
+                                   const float *__restrict__ bias,
+                                   const float *__restrict__ in_mask,
+                                   const float *__restrict__ out_mask, float *__restrict__ out,
+                                   int64_t batch, int64_t steps, int dim, int taps,
+                                   int dilation) {
+  const int pad = dilation * (taps - 1) / 2;
+  int64_t n = batch * steps * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t tok = i / dim;
+    int d = (int)(i - tok * dim);
+    int64_t b = tok / steps;
+    int64_t t = tok - b * steps;
+    float acc = 0.f;
+    for (int k = 0; k < taps; ++k) {
+      int64_t s = t + (int64_t)k * dilation - pad;
+      if (s < 0 || s >= steps) continue;
+      int64_t src = b * steps + s;
+      float v = load_f(in, src * dim + d);
+      if (in_mask) v *= in_mask[src];
+      acc = fmaf(w[d * taps + k], v, acc);
+    }
+    float y = silu_f(acc + bias[d]);
+    if (out_mask) y *= out_mask[tok];
+    out[i] = y;
+  }
+}
+
+// ---------------------------------------------------------------- timestamps
+// ts[b, t] = fp32(sum_{s<=t} double(dt[b, s]))  (CPU torch cumsum accumulates in double)
+__global__ void timestamps_kernel(const float *__restrict__ dt, float *__restrict__ ts,
+                                  int64_t batch, int64_t steps) {
+  int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  double acc = 0.0;
+  for (int64_t t = 0; t < steps; ++t) {
+    acc += (double)dt[b * steps + t];
+    ts[b * steps + t] = (float)acc;
+  }
+}
+
+// ---------------------------------------------------------------- physical-time depthwise conv
+// Restates _physical_time_depthwise_conv (src/lnet/alphabet_backbone.py:80-160).
+// One block per (token); threads over channels.  The sample positions are
+// shared by all channels and computed once per token by thread 0..taps-1.
+template <typename TI>
+__global__ void dwconv_physical_kernel(const TI *__restrict__ in, const float *__restrict__ w,
+                                       const float *__restrict__ bias,
+                                       const float *__restrict__ in_mask,
+                                       const float *__restrict__ ts,
+                                       const float *__restrict__ valid,
+                                       float *__restrict__ out, int64_t steps, int dim,
+                                       int taps, int dilation) {
+  __shared__ int64_t s_lo[16], s_hi[16];
+  __shared__ float s_w[16];
+  __shared__ int s_on[16];
+  const int64_t tok = blockIdx.x;
+  const int64_t b = tok / steps;
+  const int64_t t = tok - b * steps;
+  const float *row = ts + b * steps;
+  if (threadIdx.x < taps) {
+    int k = threadIdx.x;
+    float offset = (float)(k * dilation - dilation * (taps - 1) / 2);
+    float q = row[t] + offset;
+    int64_t up_u = lower_bound_f(row, steps, q);
+    int64_t up = up_u < steps - 1 ? up_u : steps - 1;
+    int64_t lo = up_u - 1;
+    lo = lo < 0 ? 0 : (lo > steps - 1 ? steps - 1 : lo);
+    float lt = row[lo], ut = row[up];
+    float dur = ut - lt;
+    float interp = dur > 0.f ? (q - lt) / fmaxf(dur, kFp32Tiny) : 0.f;
+    interp = fminf(fmaxf(interp, 0.f), 1.f);
+    bool on = (q >= row[0]) && (q <= row[steps - 1]);
+    if (valid) {
+      float lv = valid[b * steps + lo], uv = valid[b * steps + up];
+      const float eps8 = 8.0f * kFp32Eps;
+      float support = interp <= eps8 ? lv : (interp >= 1.0f - eps8 ? uv : lv * uv);
+      on = on && (support > 0.f);
+    }
+    s_lo[k] = b * steps + lo;
+    s_hi[k] = b * steps + up;
+    s_w[k] = interp;
+    s_on[k] = on;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    float acc = 0.f;
+    for (int k = 0; k < taps; ++k) {
+      float a = load_f(in, s_lo[k] * dim + d);
+      float c = load_f(in, s_hi[k] * dim + d);
+      if (in_mask) {
+        a *= in_mask[s_lo[k]];
+        c *= in_mask[s_hi[k]];
+      }
+      float v = s_on[k] ? lerp_torch(a, c, s_w[k]) : 0.f;
+      acc = fmaf(v, w[d * taps + k], acc);
+    }
+    float y = silu_f(acc + bias[d]);
+    if (valid) y *= valid[tok];
+    out[tok * dim + d] = y;
+  }
+}
+
+// ---------------------------------------------------------------- RMSNorm
+// One warp per token: out = x * rsqrt(mean(x^2) + eps) * g
+__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ g,
+                               float *__restrict__ out, int64_t tokens, int dim) {
+  int64_t tok = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  int lane = threadIdx.x & 31;
+  if (tok >= tokens) return;
+  const float *row = x + tok * dim;
+  float ss = 0.f;
+  for (int d = lane; d < dim; d += 32) ss = fmaf(row[d], row[d], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  float rs = rsqrtf(ss / (float)dim + kFp32Eps);
+  for (int d = lane; d < dim; d += 32) out[tok * dim + d] = row[d] * rs * g[d];
+}
+
+// ---------------------------------------------------------------- drive (gamma (x) e * mask)
+// e[tok, 0:M] / e[tok, M:2M] -> u in place; gamma from the per-mode table or per step.
+__global__ void drive_kernel(float *__restrict__ e, const float *__restrict__ raw_decay,
+                             const float *__restrict__ raw_freq, const float *__restrict__ dt,
+                             const float *__restrict__ event_mask, int obs_channels,
+                             int64_t tokens, int modes) {
+  int64_t n = tokens * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t tok = i / modes;
+    int m = (int)(i - tok * modes);
+    double damping, frequency;
+    mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+    Zoh z = zoh_eval(damping, frequency, dt ? (double)dt[tok] : 1.0);
+    float *row = e + tok * 2 * modes;
+    float er = row[m], ei = row[modes + m];
+    float ur = z.g_re * er - z.g_im * ei;
+    float ui = z.g_re * ei + z.g_im * er;
+    if (event_mask) {
+      // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
+      const float *om = event_mask + tok * obs_channels;
+      float mx = om[0];
+      for (int c = 1; c < obs_channels; ++c) mx = fmaxf(mx, om[c]);
+      ur *= mx;
+      ui *= mx;
+    }
+    row[m] = ur;
+    row[modes + m] = ui;
+  }
+}
+
+// ---------------------------------------------------------------- chunked scan
+// s_t = a_t s_{t-1} + u_t per (row, mode); three passes over chunks of `chunk` steps:
+//   local: chunk end state from zero + chunk transition product,
+//   carry: sequential combine over chunks,
+//   apply: rescan each chunk from its true carry-in (states overwrite u).
+__device__ __forceinline__ void step_coeff(const float *raw_decay, const float *raw_freq,
+                                           const float *a_tab_re, const float *a_tab_im,
+                                           const float *dt, int64_t tok, int m, float &ar,
+                                           float &ai) {
+  if (dt) {
+    double damping, frequency;
+    mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+    Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
+    ar = z.a_re;
+    ai = z.a_im;
+  } else {
+    ar = a_tab_re[m];
+    ai = a_tab_im[m];
+  }
+}
+
+__global__ void scan_local_kernel(const float *__restrict__ u, const float *__restrict__ raw_decay,
+                                  const float *__restrict__ raw_freq,
+                                  const float *__restrict__ a_re_tab,
+                                  const float *__restrict__ a_im_tab,
+                                  const float *__restrict__ dt, float *__restrict__ carries,
+                                  int64_t steps, int modes, int chunk, int64_t n_chunks) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * chunk;
+  const int64_t t1 = min(steps, t0 + chunk);
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    float sr = 0.f, si = 0.f, pr = 1.f, pi = 0.f;
+    for (int64_t t = t0; t < t1; ++t) {
+      int64_t tok = b * steps + t;
+      float ar, ai;
+      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, tok, m, ar, ai);
+      const float *row = u + tok * 2 * modes;
+      float nr = ar * sr - ai * si + row[m];
+      float ni = ai * sr + ar * si + row[modes + m];
+      sr = nr;
+      si = ni;
+      float qr = ar * pr - ai * pi;
+      float qi = ai * pr + ar * pi;
+      pr = qr;
+      pi = qi;
+    }
+    float *rec = carries + ((b * n_chunks + c) * 4) * modes;
+    rec[m] = sr;
+    rec[modes + m] = si;
+    rec[2 * modes + m] = pr;
+    rec[3 * modes + m] = pi;
+  }
+}
+
+__global__ void scan_carry_kernel(float *__restrict__ carries, int64_t batch, int modes,
+                                  int64_t n_chunks) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= batch * modes) return;
+  int64_t b = i / modes;
+  int m = (int)(i - b * modes);
+  float sr = 0.f, si = 0.f;
+  for (int64_t c = 0; c < n_chunks; ++c) {
+    float *rec = carries + ((b * n_chunks + c) * 4) * modes;
+    float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m], pi = rec[3 * modes + m];
+    rec[m] = sr;  // carry-in of chunk c
+    rec[modes + m] = si;
+    float nr = pr * sr - pi * si + er;
+    float ni = pi * sr + pr * si + ei;
+    sr = nr;
+    si = ni;
+  }
+}
+
+__global__ void scan_apply_kernel(float *__restrict__ u, const float *__restrict__ raw_decay,
+                                  const float *__restrict__ raw_freq,
+                                  const float *__restrict__ a_re_tab,
+                                  const float *__restrict__ a_im_tab,
+                                  const float *__restrict__ dt,
+                                  const float *__restrict__ carries, int64_t steps, int modes,
+                                  int chunk, int64_t n_chunks) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * chunk;
+  const int64_t t1 = min(steps, t0 + chunk);
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    const float *rec = carries + ((b * n_chunks + c) * 4) * modes;
+    float sr = rec[m], si = rec[modes + m];
+    for (int64_t t = t0; t < t1; ++t) {
+      int64_t tok = b * steps + t;
+      float ar, ai;
+      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, tok, m, ar, ai);
+      float *row = u + tok * 2 * modes;
+      float nr = ar * sr - ai * si + row[m];
+      float ni = ai * sr + ar * si + row[modes + m];
+      sr = nr;
+      si = ni;
+      row[m] = sr;
+      row[modes + m] = si;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- unit-grid moments
+// Partial sums over a chunk of steps of E, C1, C2, C4 (re, im), optionally
+// valid-weighted (_modal_moments / _masked_modal_moments,
+// src/lnet/pac_tight_frame_models.py:1632-1702).  partial layout [B, nchunk, 7M].
+__global__ void moments_partial_kernel(const float *__restrict__ s,
+                                       const float *__restrict__ valid,
+                                       float *__restrict__ partial, int64_t steps, int modes,
+                                       int chunk, int64_t n_chunks) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * chunk;
+  const int64_t t1 = min(steps, t0 + chunk);
+  const int lags[3] = {1, 2, 4};
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    float acc[7] = {0, 0, 0, 0, 0, 0, 0};
+    for (int64_t t = t0; t < t1; ++t) {
+      int64_t tok = b * steps + t;
+      const float *row = s + tok * 2 * modes;
+      float cr = row[m], ci = row[modes + m];
+      float wt = valid ? valid[tok] : 1.f;
+      acc[0] += (cr * cr + ci * ci) * wt;
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        if (t < lags[l]) continue;
+        const float *prow = row - (int64_t)lags[l] * 2 * modes;
+        float pr = prow[m], pi = prow[modes + m];
+        float w = valid ? wt * valid[tok - lags[l]] : 1.f;
+        acc[1 + 2 * l] += (cr * pr + ci * pi) * w;
+        acc[2 + 2 * l] += (ci * pr - cr * pi) * w;
+      }
+    }
+    float *out = partial + (b * n_chunks + c) * 7 * modes;
+#pragma unroll
+    for (int j = 0; j < 7; ++j) out[j * modes + m] = acc[j];
+  }
+}
+
+// One block per row: counts, then ordered reduction of the partials.
+__global__ void moments_finalize_kernel(const float *__restrict__ partial,
+                                        const float *__restrict__ valid,
+                                        float *__restrict__ moments, int64_t steps, int modes,
+                                        int64_t n_chunks) {
+  const int64_t b = blockIdx.x;
+  __shared__ double s_cnt[4];
+  __shared__ double red[4][32];
+  const int lags[3] = {1, 2, 4};
+  double cnt[4] = {0, 0, 0, 0};
+  if (valid) {
+    for (int64_t t = threadIdx.x; t < steps; t += blockDim.x) {
+      double v = valid[b * steps + t];
+      cnt[0] += v;
+      for (int l = 0; l < 3; ++l)
+        if (t >= lags[l]) cnt[1 + l] += v * (double)valid[b * steps + t - lags[l]];
+    }
+  }
+  // block reduce the 4 counts (warp shuffles then one warp)
+  for (int j = 0; j < 4; ++j) {
+    double v = cnt[j];
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[j][threadIdx.x >> 5] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 4) {
+    double v = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[threadIdx.x][w];
+    s_cnt[threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) {
+    int kind = j / modes;  // 0 = E, 1..6 = lag pairs
+    int lag_idx = kind == 0 ? -1 : (kind - 1) / 2;
+    double acc = 0.0;
+    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)partial[(b * n_chunks + c) * 7 * modes + j];
+    float outv;
+    if (lag_idx >= 0 && steps <= lags[lag_idx]) {
+      outv = 0.f;
+    } else if (valid) {
+      // counts are clamped at one (sum(...).clamp_min(1.0))
+      float cntf = (float)s_cnt[lag_idx + 1];
+      outv = (float)acc / fmaxf(cntf, 1.0f);
+    } else {
+      int64_t n = lag_idx < 0 ? steps : steps - lags[lag_idx];
+      outv = (float)(acc / (double)n);
+    }
+    moments[b * 7 * modes + j] = outv;
+  }
+}
+
+// ---------------------------------------------------------------- physical-time moments
+// Restates _physical_time_modal_moments / _interpolate_modal_state
+// (src/lnet/pac_tight_frame_models.py:1705-1833).  Per chunk of steps:
+// sample positions of the three lag queries are computed once per token,
+// then every mode accumulates.  partial layout per (b, chunk):
+// [8 * M mode sums (E_duration, E_event, C1r, C1i, C2r, C2i, C4r, C4i)] + [5 scalars:
+//  sum(dt*valid), sum(valid), pair weights of lags 1, 2, 4].
+constexpr int kPtChunk = 64;
+__global__ void pt_moments_partial_kernel(const float *__restrict__ s,
+                                          const float *__restrict__ ts,
+                                          const float *__restrict__ dt,
+                                          const float *__restrict__ valid,
+                                          float *__restrict__ partial, int64_t steps,
+                                          int modes, int64_t n_chunks) {
+  __shared__ int64_t s_lo[3][kPtChunk], s_hi[3][kPtChunk];
+  __shared__ float s_ip[3][kPtChunk], s_pw[3][kPtChunk];
+  __shared__ float s_dw[kPtChunk], s_v[kPtChunk];
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * kPtChunk;
+  const int n = (int)min((int64_t)kPtChunk, steps - t0);
+  const float *row = ts + b * steps;
+  const int rec = 8 * modes + 5;
+  for (int j = threadIdx.x; j < n * 3; j += blockDim.x) {
+    int i = j / 3, l = j - (j / 3) * 3;
+    int lag = l == 0 ? 1 : (l == 1 ? 2 : 4);
+    int64_t t = t0 + i;
+    int64_t tok = b * steps + t;
+    float q = row[t] - (float)lag;
+    int64_t up_u = lower_bound_f(row, steps, q);
+    int64_t up = up_u < steps - 1 ? up_u : steps - 1;
+    int64_t lo = up_u - 1;
+    lo = lo < 0 ? 0 : (lo > steps - 1 ? steps - 1 : lo);
+    float lt = row[lo], ut = row[up];
+    float span = ut - lt;
+    float ip = span > 0.f ? (q - lt) / fmaxf(span, kFp32Tiny) : 0.f;
+    ip = fminf(fmaxf(ip, 0.f), 1.f);
+    float lv = valid ? valid[b * steps + lo] : 1.f;
+    float uv = valid ? valid[b * steps + up] : 1.f;
+    const float eps8 = 8.0f * kFp32Eps;
+    float support = ip <= eps8 ? lv : (ip >= 1.0f - eps8 ? uv : lv * uv);
+    bool in_bounds = (q >= row[0]) && (q <= row[steps - 1]);
+    support = support * (in_bounds ? 1.f : 0.f);
+    float vt = valid ? valid[tok] : 1.f;
+    s_lo[l][i] = b * steps + lo;
+    s_hi[l][i] = b * steps + up;
+    s_ip[l][i] = ip;
+    s_pw[l][i] = dt[tok] * vt * support;
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int64_t tok = b * steps + t0 + i;
+    float vt = valid ? valid[tok] : 1.f;
+    s_dw[i] = dt[tok] * vt;
+    s_v[i] = vt;
+  }
+  __syncthreads();
+  float *out = partial + (b * n_chunks + c) * rec;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < n; ++i) {
+      int64_t tok = b * steps + t0 + i;
+      const float *cur = s + tok * 2 * modes;
+      float cr = cur[m], ci = cur[modes + m];
+      float e = cr * cr + ci * ci;
+      acc[0] += e * s_dw[i];
+      acc[1] += e * s_v[i];
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        const float *lo = s + s_lo[l][i] * 2 * modes;
+        const float *hi = s + s_hi[l][i] * 2 * modes;
+        float pr = lerp_torch(lo[m], hi[m], s_ip[l][i]);
+        float pi = lerp_torch(lo[modes + m], hi[modes + m], s_ip[l][i]);
+        float w = s_pw[l][i];
+        acc[2 + 2 * l] += (cr * pr + ci * pi) * w;
+        acc[3 + 2 * l] += (ci * pr - cr * pi) * w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j * modes + m] = acc[j];
+  }
+  if (threadIdx.x < 5) {
+    float acc = 0.f;
+    for (int i = 0; i < n; ++i) {
+      if (threadIdx.x == 0) acc += s_dw[i];
+      else if (threadIdx.x == 1) acc += s_v[i];
+      else acc += s_pw[threadIdx.x - 2][i];
+    }
+    out[8 * modes + threadIdx.x] = acc;
+  }
+}
+
+__global__ void pt_moments_finalize_kernel(const float *__restrict__ partial,
+                                           float *__restrict__ moments, int modes,
+                                           int64_t n_chunks) {
+  const int64_t b = blockIdx.x;
+  const int rec = 8 * modes + 5;
+  __shared__ double sc[5];
+  if (threadIdx.x < 5) {
+    double a = 0.0;
+    for (int64_t c = 0; c < n_chunks; ++c) a += (double)partial[(b * n_chunks + c) * rec + 8 * modes + threadIdx.x];
+    sc[threadIdx.x] = a;
+  }
+  __syncthreads();
+  const bool use_duration = sc[0] > 0.0;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      const float *p = partial + (b * n_chunks + c) * rec;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += (double)p[j * modes + m];
+    }
+    float *o = moments + b * 7 * modes;
+    float ecount = fmaxf((float)(use_duration ? sc[0] : sc[1]), 1.0f);
+    o[m] = (float)(use_duration ? acc[0] : acc[1]) / ecount;
+    for (int l = 0; l < 3; ++l) {
+      float pc = fmaxf((float)sc[2 + l], 1.0f);
+      o[(1 + 2 * l) * modes + m] = (float)acc[2 + 2 * l] / pc;
+      o[(2 + 2 * l) * modes + m] = (float)acc[3 + 2 * l] / pc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- writer residual
+// v = x + ls * (modal + ds * xhat)
+__global__ void residual_kernel(const float *__restrict__ x, const float *__restrict__ xhat,
+                                const float *__restrict__ modal, const float *__restrict__ ds,
+                                const float *__restrict__ ls, float *__restrict__ v,
+                                int64_t tokens, int dim) {
+  int64_t n = tokens * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int d = (int)(i % dim);
+    v[i] = x[i] + ls[d] * (modal[i] + ds[d] * xhat[i]);
+  }
+}
+
+// ---------------------------------------------------------------- head
+// logits[b, k] = bias[k] + sum_j G[k, j] f[b, j],  f = [radial_log(W), radial_log(R)]
+// (src/lnet/alphabet.py:29-63).  One block per (row, 8 classes); warp per class.
+__device__ __forceinline__ float radial_feature(const float *mom, int modes, int j) {
+  if (j < modes) return log1pf(fmaxf(mom[j], 0.f));
+  int pair = (j - modes) / (2 * modes);
+  int within = (j - modes) - pair * 2 * modes;
+  int base = modes + pair * 2 * modes;
+  int mm = within % modes;
+  float re = mom[base + mm], im = mom[base + modes + mm];
+  float r = sqrtf(fmaxf(re * re + im * im, kFp32Tiny));
+  float scale = log1pf(r) / r;
+  return scale * (within < modes ? re : im);
+}
+
+__global__ void head_features_kernel(const float *__restrict__ wm, const float *__restrict__ rm,
+                                     float *__restrict__ feats, int64_t batch, int modes) {
+  int64_t n = batch * 14 * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = i / (14 * modes);
+    int j = (int)(i - b * 14 * modes);
+    const float *src = j < 7 * modes ? wm + b * 7 * modes : rm + b * 7 * modes;
+    feats[i] = radial_feature(src, modes, j < 7 * modes ? j : j - 7 * modes);
+  }
+}
+
+__global__ void head_logits_kernel(const float *__restrict__ feats, const float *__restrict__ G,
+                                   const float *__restrict__ bias, float *__restrict__ logits,
+                                   int64_t batch, int classes, int width) {
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int k = blockIdx.x * (blockDim.x >> 5) + warp;
+  int64_t b = blockIdx.y;
+  if (k >= classes) return;
+  const float *f = feats + b * width;
+  const float *g = G + (int64_t)k * width;
+  float acc = 0.f;
+  for (int j = lane; j < width; j += 32) acc = fmaf(f[j], g[j], acc);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) logits[b * classes + k] = acc + bias[k];
+}
+
+// ---------------------------------------------------------------- ZOH table
+__global__ void zoh_kernel(const float *__restrict__ raw_decay, const float *__restrict__ raw_freq,
+                           int modes, const float *__restrict__ dt, int64_t steps,
+                           float *__restrict__ a_re, float *__restrict__ a_im,
+                           float *__restrict__ g_re, float *__restrict__ g_im) {
+  int64_t rows = dt ? steps : 1;
+  int64_t n = rows * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / modes;
+    int m = (int)(i - r * modes);
+    double damping, frequency;
+    mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+    Zoh z = zoh_eval(damping, frequency, dt ? (double)dt[r] : 1.0);
+    a_re[i] = z.a_re;
+    a_im[i] = z.a_im;
+    if (g_re) g_re[i] = z.g_re;
+    if (g_im) g_im[i] = z.g_im;
+  }
+}
+
+}  // namespace lnet

@@ -1,0 +1,170 @@
+// Pole-residue Laplace layer (PoleResidueTemporalMixing, src/lnet/laplace.py:55-159) in float64.
+//
+// Work split: the (mode, channel) state vector of one row is cut into
+// slices of kSlice entries; one CTA owns one (slice, row), runs its states
+// sequentially over T and contracts them with the matching residue slice
+// into a per-slice partial output [T, D].  A second kernel sums the slices in
+// a fixed order and adds the direct term and the bias, so the result is
+// deterministic.  No state ever reaches HBM.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace lnet {
+
+constexpr int kSlice = 256;  // state entries per CTA (= threads)
+constexpr int kStepTile = 32;
+constexpr int kOutTile = 16;
+
+__device__ __forceinline__ double softplus_d(double x) {
+  return x > 20.0 ? x : log1p(exp(x));
+}
+
+// dt * phi1(p dt) with the series branch of _phi1 (src/lnet/laplace.py:37-42)
+__device__ __forceinline__ void laplace_zoh(double raw_decay, double dt, double min_decay,
+                                            double &a, double &b) {
+  double pole = -(softplus_d(raw_decay) + min_decay);
+  double z = pole * dt;
+  double phi = fabs(z) < 1.0e-4 ? 1.0 + z / 2.0 + z * z / 6.0 : expm1(z) / z;
+  a = exp(z);
+  b = dt * phi;
+}
+
+template <typename TX>
+__global__ void __launch_bounds__(kSlice) laplace_slice_kernel(
+    const TX *__restrict__ x, const double *__restrict__ raw_decay,
+    const double *__restrict__ residues, int dim, int modes, double dt, double min_decay,
+    int64_t steps, double *__restrict__ partial) {
+  extern __shared__ double smem[];
+  double *s_state = smem;                        // [kStepTile][kSlice]
+  double *s_res = smem + kStepTile * kSlice;     // [kOutTile][kSlice]
+  const int slice = blockIdx.x;
+  const int64_t b = blockIdx.y;
+  const int64_t md = (int64_t)modes * dim;
+  const int j = threadIdx.x;
+  const int64_t k = (int64_t)slice * kSlice + j;
+  const bool live = k < md;
+  const int m = live ? (int)(k / dim) : 0;
+  const int i = live ? (int)(k - (int64_t)m * dim) : 0;
+  double a = 0.0, bcoef = 0.0;
+  if (live) laplace_zoh(raw_decay[m], dt, min_decay, a, bcoef);
+  double state = 0.0;
+  double *out_row = partial + ((int64_t)slice * gridDim.y + b) * steps * dim;
+  for (int64_t t0 = 0; t0 < steps; t0 += kStepTile) {
+    const int nt = (int)min((int64_t)kStepTile, steps - t0);
+    for (int tt = 0; tt < nt; ++tt) {
+      double xv = live ? (double)load_f(x, ((b * steps) + t0 + tt) * dim + i) : 0.0;
+      state = a * state + bcoef * xv;
+      s_state[tt * kSlice + j] = live ? state : 0.0;
+    }
+    for (int o0 = 0; o0 < dim; o0 += kOutTile) {
+      const int no = min(kOutTile, dim - o0);
+      __syncthreads();
+      for (int r = 0; r < no; ++r)
+        s_res[r * kSlice + j] = live ? residues[(int64_t)(o0 + r) * md + k] : 0.0;
+      __syncthreads();
+      for (int q = j; q < nt * no; q += kSlice) {
+        int tt = q / no, r = q - (q / no) * no;
+        const double *sv = s_state + tt * kSlice;
+        const double *rv = s_res + r * kSlice;
+        double acc = 0.0;
+#pragma unroll 8
+        for (int e = 0; e < kSlice; ++e) acc = fma(rv[e], sv[e], acc);
+        out_row[(t0 + tt) * dim + o0 + r] = acc;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <typename TX>
+__global__ void laplace_reduce_kernel(const TX *__restrict__ x, const double *__restrict__ partial,
+                                      const double *__restrict__ direct,
+                                      const double *__restrict__ bias, int dim, int n_slices,
+                                      int64_t tokens, TX *__restrict__ y) {
+  int64_t n = tokens * dim;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t tok = idx / dim;
+    int o = (int)(idx - tok * dim);
+    double acc = 0.0;
+    for (int s = 0; s < n_slices; ++s) acc += partial[(int64_t)s * n + idx];
+    double dsum = 0.0;
+    for (int i = 0; i < dim; ++i) dsum = fma((double)load_f(x, tok * dim + i), direct[o * dim + i], dsum);
+    double v = acc + dsum + bias[o];
+    if constexpr (sizeof(TX) == 8)
+      y[idx] = v;
+    else
+      y[idx] = (TX)(float)v;
+  }
+}
+
+static size_t laplace_partial_bytes(int64_t batch, int64_t steps, int dim, int modes) {
+  int64_t n_slices = cdiv((int64_t)modes * dim, kSlice);
+  return (size_t)n_slices * batch * steps * dim * sizeof(double);
+}
+
+template <typename TX>
+static int laplace_run(const double *raw_decay, const double *residues, const double *direct,
+                       const double *bias, int dim, int modes, double dt, double min_decay,
+                       const TX *x, int64_t batch, int64_t steps, TX *y, double *partial,
+                       cudaStream_t stream) {
+  int n_slices = (int)cdiv((int64_t)modes * dim, kSlice);
+  size_t smem = (size_t)(kStepTile + kOutTile) * kSlice * sizeof(double);
+  LNET_TRY(cuda_check(cudaFuncSetAttribute(laplace_slice_kernel<TX>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem),
+                      "cudaFuncSetAttribute(laplace_slice_kernel)"));
+  dim3 grid(n_slices, (unsigned)batch);
+  laplace_slice_kernel<TX><<<grid, kSlice, smem, stream>>>(x, raw_decay, residues, dim, modes,
+                                                           dt, min_decay, steps, partial);
+  LNET_TRY(after_launch("laplace_slice_kernel"));
+  int64_t n = batch * steps * dim;
+  int blocks = (int)std::min<int64_t>(cdiv(n, 256), 148 * 16);
+  laplace_reduce_kernel<TX><<<blocks, 256, 0, stream>>>(x, partial, direct, bias, dim, n_slices,
+                                                        batch * steps, y);
+  return after_launch("laplace_reduce_kernel");
+}
+
+}  // namespace lnet
+
+using namespace lnet;
+
+extern "C" int lnet_b200_laplace_workspace_size(int64_t batch, int64_t steps, int32_t model_dim,
+                                                int32_t modes, size_t *bytes) {
+  reset_launches();
+  if (!bytes) return fail(LNET_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+  if (batch < 0 || steps < 0 || model_dim < 1 || modes < 1)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "invalid laplace shape");
+  *bytes = laplace_partial_bytes(batch, steps, model_dim, modes);
+  return LNET_OK;
+}
+
+extern "C" int lnet_b200_laplace_forward(const double *raw_decay, const double *residues,
+                                         const double *direct, const double *bias,
+                                         int32_t model_dim, int32_t modes, double dt,
+                                         double min_decay, int32_t x_dtype, const void *x,
+                                         int64_t batch, int64_t steps, void *y, void *workspace,
+                                         size_t workspace_bytes, lnet_stream_t stream) {
+  reset_launches();
+  if (model_dim < 1 || modes < 1 || batch < 0 || steps < 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "invalid laplace shape (D=%d, M=%d, B=%lld, T=%lld)",
+                model_dim, modes, (long long)batch, (long long)steps);
+  if (batch == 0 || steps == 0) return LNET_OK;
+  if (!raw_decay || !residues || !direct || !bias || !x || !y)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: NULL tensor pointer");
+  if (batch > 65535) return fail(LNET_ERR_UNSUPPORTED, "laplace: batch > 65535");
+  size_t need = laplace_partial_bytes(batch, steps, model_dim, modes);
+  if (!workspace || workspace_bytes < need)
+    return fail(LNET_ERR_WORKSPACE, "laplace: workspace of %zu bytes < required %zu",
+                workspace_bytes, need);
+  auto st = (cudaStream_t)stream;
+  if (x_dtype == LNET_F64)
+    return laplace_run<double>(raw_decay, residues, direct, bias, model_dim, modes, dt, min_decay,
+                               (const double *)x, batch, steps, (double *)y, (double *)workspace,
+                               st);
+  if (x_dtype == LNET_F32)
+    return laplace_run<float>(raw_decay, residues, direct, bias, model_dim, modes, dt, min_decay,
+                              (const float *)x, batch, steps, (float *)y, (double *)workspace, st);
+  return fail(LNET_ERR_UNSUPPORTED, "laplace: x dtype must be float32 or float64");
+}

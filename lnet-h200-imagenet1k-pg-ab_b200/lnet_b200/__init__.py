@@ -1,0 +1,28 @@
+"""lnet_b200: B200-native (sm_100a) ALPHABET forward path and pole-residue
+Laplace layer behind the reference ``lnet`` module API.
+
+* :class:`B200Alphabet` — drop-in for ``lnet.Alphabet`` (same state_dict,
+  same forward signature and metadata errors).
+* :class:`B200PoleResidueTemporalMixing` — drop-in for
+  ``lnet.laplace.PoleResidueTemporalMixing``.
+* :mod:`lnet_b200.ops` — the same calls as ``torch.library`` custom ops
+  (``lnet_b200::alphabet_forward``, ``lnet_b200::laplace_forward``).
+
+All compute runs in the C-ABI CUDA library ``_lib/liblnet_b200.so`` built by
+:func:`lnet_b200.build.build`; there is no CPU fallback.
+"""
+
+from .alphabet import AlphabetConfig, B200Alphabet
+from .laplace import (
+    B200PoleResidueTemporalMixing,
+    LaplaceParameterError,
+    LaplaceShapeError,
+)
+
+__all__ = [
+    "AlphabetConfig",
+    "B200Alphabet",
+    "B200PoleResidueTemporalMixing",
+    "LaplaceParameterError",
+    "LaplaceShapeError",
+]

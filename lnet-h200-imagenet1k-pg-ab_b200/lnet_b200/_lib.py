@@ -1,0 +1,171 @@
+"""ctypes binding of the lnet_b200 C ABI (``include/lnet_b200.h``).
+
+The shared library is built in-tree by :mod:`lnet_b200.build`.  There is no
+CPU or Python fallback: if the library cannot be loaded, every entry point
+raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from . import build as _build
+
+LNET_OK = 0
+LNET_ERR_INVALID_ARGUMENT = 1
+LNET_ERR_UNSUPPORTED = 2
+LNET_ERR_WORKSPACE = 3
+LNET_ERR_CUDA = 4
+
+LNET_F32 = 0
+LNET_BF16 = 1
+LNET_F64 = 2
+
+_c_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+
+
+class AlphabetParams(ctypes.Structure):
+    _fields_ = [
+        ("raw_input_dim", _i32),
+        ("model_dim", _i32),
+        ("modes", _i32),
+        ("output_dim", _i32),
+        ("conv_kernel", _i32),
+        ("conv_dilation", _i32),
+        ("stem_projection", _c_p),
+        ("stem_conv_weight", _c_p),
+        ("stem_conv_bias", _c_p),
+        ("writer_norm", _c_p),
+        ("writer_frame", _c_p),
+        ("writer_raw_decay", _c_p),
+        ("writer_raw_frequency", _c_p),
+        ("writer_direct_scale", _c_p),
+        ("writer_layer_scale", _c_p),
+        ("reader_conv_weight", _c_p),
+        ("reader_conv_bias", _c_p),
+        ("reader_norm", _c_p),
+        ("reader_frame", _c_p),
+        ("reader_raw_decay", _c_p),
+        ("reader_raw_frequency", _c_p),
+        ("head_weight", _c_p),
+        ("head_bias", _c_p),
+    ]
+
+
+PARAM_POINTER_FIELDS = [name for name, _ in AlphabetParams._fields_[6:]]
+
+
+class AlphabetRequest(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64),
+        ("steps", _i64),
+        ("x_dtype", _i32),
+        ("act_dtype", _i32),
+        ("x", _c_p),
+        ("time_delta", _c_p),
+        ("observation_mask", _c_p),
+        ("obs_channels", _i32),
+        ("valid_mask", _c_p),
+    ]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "lnet_b200_alphabet_workspace_size": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest),
+         ctypes.POINTER(ctypes.c_size_t)],
+    ),
+    "lnet_b200_alphabet_forward": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
+         _c_p, _c_p, _c_p, _c_p],
+    ),
+    "lnet_b200_zoh": (ctypes.c_int, [_c_p, _c_p, _i32, _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p]),
+    "lnet_b200_stem": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
+         _c_p, _c_p],
+    ),
+    "lnet_b200_writer": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, _c_p,
+         ctypes.c_size_t, _c_p, _c_p, _c_p],
+    ),
+    "lnet_b200_reader": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, _c_p,
+         ctypes.c_size_t, _c_p, _c_p],
+    ),
+    "lnet_b200_head": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), _i64, _c_p, _c_p, _c_p, _c_p]
+    ),
+    "lnet_b200_laplace_workspace_size": (
+        ctypes.c_int, [_i64, _i64, _i32, _i32, ctypes.POINTER(ctypes.c_size_t)]
+    ),
+    "lnet_b200_laplace_forward": (
+        ctypes.c_int,
+        [_c_p, _c_p, _c_p, _c_p, _i32, _i32, ctypes.c_double, ctypes.c_double, _i32, _c_p, _i64,
+         _i64, _c_p, _c_p, ctypes.c_size_t, _c_p],
+    ),
+    "lnet_b200_last_launch_count": (ctypes.c_int, []),
+    "lnet_b200_last_error": (ctypes.c_char_p, []),
+    "lnet_b200_version": (ctypes.c_char_p, []),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library_path() -> Path:
+    return _build.LIB
+
+
+def load(auto_build: bool = True) -> ctypes.CDLL:
+    """Load (building first if the library is absent or stale and nvcc exists)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB
+        if auto_build and _build.needs_build():
+            try:
+                _build.build()
+            except RuntimeError:
+                if not path.exists():
+                    raise
+        if not path.exists():
+            raise RuntimeError(
+                f"lnet_b200 CUDA library missing at {path}; run lnet_b200.build.build()"
+            )
+        lib = ctypes.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().lnet_b200_last_error().decode()
+
+
+def last_launch_count() -> int:
+    return int(load().lnet_b200_last_launch_count())
+
+
+def check(status: int, what: str) -> None:
+    """Raise the Python exception matching a C status code."""
+    if status == LNET_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status == LNET_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    if status == LNET_ERR_UNSUPPORTED:
+        raise TypeError(msg)
+    raise RuntimeError(msg)

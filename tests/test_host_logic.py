@@ -1,0 +1,91 @@
+"""Host-side behaviour of the drop-in modules that needs no GPU."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from lnet_b200 import AlphabetConfig, B200Alphabet, B200PoleResidueTemporalMixing
+from lnet_b200.laplace import LaplaceParameterError, LaplaceShapeError
+
+
+def model(cin=3, d=8, m=4, k=5):
+    return B200Alphabet(AlphabetConfig(cin, d, m, k), k).eval()
+
+
+def test_modes_above_half_width_rejected():
+    with pytest.raises(RuntimeError):
+        B200Alphabet(AlphabetConfig(3, 8, 5, 2), 2)
+
+
+def test_state_dict_keys_match_reference_layout():
+    keys = set(model().state_dict())
+    for k in ("stem.projection.weight", "stem.local.weight", "stem.local.bias",
+              "forward_block.frame.parametrizations.weight.original",
+              "forward_block.direct_scale", "backward_block.layer_scale",
+              "head.classifier.weight", "second_local.bias"):
+        assert k in keys
+
+
+@pytest.mark.parametrize(
+    "kwargs,msg",
+    [
+        ({"time_delta": torch.ones(2, 7)}, "time_delta must have shape"),
+        ({"time_delta": -torch.ones(2, 6)}, "finite non-negative"),
+        ({"time_delta": torch.full((2, 6, 1), float("nan"))}, "finite non-negative"),
+        ({"observation_mask": torch.ones(2, 6, 2)}, "observation_mask must have shape"),
+        ({"observation_mask": 2 * torch.ones(2, 6, 3)}, "finite values in \\[0,1\\]"),
+        ({"valid_mask": torch.ones(2, 6, 3)}, "valid_mask must have shape"),
+        ({"valid_mask": -torch.ones(2, 6)}, "finite values in \\[0,1\\]"),
+    ],
+)
+def test_metadata_errors_mirror_reference(kwargs, msg):
+    m = model()
+    x = torch.randn(2, 6, 3)
+    with pytest.raises(ValueError, match=msg):
+        m._prepare_metadata(x, kwargs.get("time_delta"), kwargs.get("observation_mask"),
+                            kwargs.get("valid_mask"))
+
+
+def test_metadata_normalisation_shapes():
+    m = model()
+    x = torch.randn(2, 6, 3)
+    d, o, v = m._prepare_metadata(x, torch.ones(2, 6, 1), torch.ones(2, 6), torch.ones(2, 6, 1))
+    assert d.shape == (2, 6) and o.shape == (2, 6, 1) and v.shape == (2, 6)
+    d, o, v = m._prepare_metadata(x, None, torch.ones(2, 6, 3), None)
+    assert d is None and o.shape == (2, 6, 3) and v is None
+
+
+def test_cpu_inputs_fail_loudly():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        model()(torch.randn(2, 6, 3))
+
+
+def test_laplace_errors_mirror_reference():
+    layer = B200PoleResidueTemporalMixing(4, 3)
+    with pytest.raises(LaplaceShapeError):
+        layer(torch.randn(2, 5, 3))
+    with pytest.raises(LaplaceParameterError, match="strictly negative"):
+        layer.load_transfer_parameters(
+            poles=torch.tensor([-1.0, 0.5, -2.0], dtype=torch.float64),
+            residues=torch.zeros(4, 3, 4, dtype=torch.float64),
+            direct_term=torch.zeros(4, 4, dtype=torch.float64),
+            bias=torch.zeros(4, dtype=torch.float64),
+        )
+    with pytest.raises(LaplaceParameterError, match="residue tensor shape"):
+        layer.load_transfer_parameters(
+            poles=-torch.ones(3, dtype=torch.float64),
+            residues=torch.zeros(4, 2, 4, dtype=torch.float64),
+            direct_term=torch.zeros(4, 4, dtype=torch.float64),
+            bias=torch.zeros(4, dtype=torch.float64),
+        )
+
+
+def test_training_mode_refused():
+    m = B200Alphabet(AlphabetConfig(3, 8, 4, 5), 5)
+    with pytest.raises(RuntimeError):
+        m.train()
+        if torch.cuda.is_available():
+            m(torch.randn(2, 6, 3, device="cuda"))
+        else:
+            raise RuntimeError("CUDA")
