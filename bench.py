@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""ALPHABET forward benchmark: tokens/s and HBM roofline on B200, next to the CPU path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 4]
+
+Default workload (the north-star case): synthetic uint8
+224x224x3 images ~U(0,255), normalised with the ImageNet mean/std and
+patchified 4x4 into x [B=256, T=3136, C=48] bf16; ALPHABET with D=96,
+M=48 complex modes (real poles, log-uniform decay in [1e-3, 1]), K5/D4
+depthwise convs, 1000 classes; random-init weights rounded to bf16.
+
+* ``value``: device time of K forward passes through the C ABI with inputs
+  resident in HBM (L2 flushed between steps, outside the per-step CUDA-event
+  pair), whole-job tokens/s over all ranks (each rank runs its own B=256
+  shard: weak scaling, no collective on the data path).
+* ``e2e``: the same metric through the public module API with the input copied
+  from pinned host memory and the logits copied back every step.
+* ``roofline``: the dominant kernel's algorithmic bytes per launch / its
+  average CUDA-event duration measured during the timed region.
+* ``cpu_baseline``: the CPU oracle (numpy restatement of the reference path) on a
+  bounded slice of the same batch, rank 0 only.
+
+``--impl reference`` times that CPU path alone (rank 0; other ranks exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "lnet-h200-imagenet1k-pg-ab_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+METRIC = "ALPHABET fwd tokens/sec"
+UNIT = "tokens/s"
+
+CONFIGS = {
+    "4": dict(workload="alphabet_cfg4_imagenet224_patch4_b256_t3136_c48_d96_m48_k1000_bf16",
+              B=256, T=3136, C=48, D=96, M=48, K=1000, dtype="bf16", images=True),
+    "2": dict(workload="alphabet_cfg2_b128_t1024_c128_d128_m64_k10_fp32",
+              B=128, T=1024, C=128, D=128, M=64, K=10, dtype="fp32", images=False),
+    "5": dict(workload="alphabet_cfg5_b16_t65536_c256_d256_m64_k10_bf16",
+              B=16, T=65536, C=256, D=256, M=64, K=10, dtype="bf16", images=False),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------- model / inputs
+def make_params(cfg, seed=0):
+    """Seeded random-init ALPHABET parameters of the configured shape (state_dict names,
+    materialised frames).  Real poles: raw_frequency = 0 and decay rates
+    lambda ~ LogUniform[1.1e-3, 1]; depthwise conv weights ~ N(0, 1/5)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    D, M, C, K = cfg["D"], cfg["M"], cfg["C"], cfg["K"]
+
+    def rn(*shape, scale=1.0):
+        return torch.randn(*shape, generator=g) * scale
+
+    p = {}
+    q, _ = torch.linalg.qr(rn(D, C))
+    p["stem.projection.weight"] = q if D >= C else torch.linalg.qr(rn(C, D))[0].T
+    p["stem.local.weight"] = rn(D, 1, 5, scale=1 / math.sqrt(5))
+    p["stem.local.bias"] = rn(D, scale=0.1)
+    for blk in ("forward_block", "backward_block"):
+        lam = torch.exp(torch.empty(M).uniform_(math.log(1.1e-3), 0.0, generator=g))
+        p[f"{blk}.raw_decay"] = torch.logit((lam - 1e-3) / (2.0 - 1e-3))
+        p[f"{blk}.raw_frequency"] = torch.zeros(M)
+        p[f"{blk}.norm.weight"] = 1.0 + rn(D, scale=0.1)
+        p[f"{blk}.frame.weight"] = torch.linalg.qr(rn(D, 2 * M))[0]
+    p["forward_block.direct_scale"] = rn(D, scale=0.3)
+    p["forward_block.layer_scale"] = rn(D, scale=0.3)
+    p["second_local.weight"] = rn(D, 1, 5, scale=1 / math.sqrt(5))
+    p["second_local.bias"] = rn(D, scale=0.1)
+    p["head.classifier.weight"] = rn(K, 14 * M, scale=1 / math.sqrt(14 * M))
+    p["head.classifier.bias"] = rn(K, scale=0.1)
+    if cfg["dtype"] == "bf16":
+        p = {k: v.to(torch.bfloat16).float() for k, v in p.items()}
+    return p
+
+
+def make_inputs(cfg, device, seed=1):
+    """x [B, T, C] on `device` (bf16 for bf16 configs)."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, T, C = cfg["B"], cfg["T"], cfg["C"]
+    if cfg["images"]:
+        img = torch.randint(0, 256, (B, 224, 224, 3), generator=g, device=device,
+                            dtype=torch.uint8)
+        mean = torch.tensor([0.485, 0.456, 0.406], device=device)
+        std = torch.tensor([0.229, 0.224, 0.225], device=device)
+        v = (img.float() / 255.0 - mean) / std  # [B, 224, 224, 3]
+        v = v.reshape(B, 56, 4, 56, 4, 3).permute(0, 1, 3, 2, 4, 5).reshape(B, 56 * 56, 48)
+        x = v
+    else:
+        x = torch.randn(B, T, C, generator=g, device=device)
+    return x.to(torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32).contiguous()
+
+
+def build_model(cfg, device):
+    from lnet_b200 import AlphabetConfig, B200Alphabet
+
+    m = B200Alphabet(AlphabetConfig(cfg["C"], cfg["D"], cfg["M"], cfg["K"]), cfg["K"]).eval()
+    m.load_effective_parameters(make_params(cfg))
+    return m.to(device)
+
+
+# ---------------------------------------------------------------- clocks
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        for line in self.lines:
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 3:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+                bits = int(parts[2], 16)
+            except ValueError:
+                continue
+            for bit, name in REASON_BITS.items():
+                if bits & bit and name != "gpu_idle":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- roofline helpers
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return 6650.0, "fallback"
+
+
+def algorithmic_bytes(kernel: str, cfg) -> float | None:
+    """Minimum HBM bytes one launch of `kernel` must move for the workload."""
+    B, T, C, D, M = cfg["B"], cfg["T"], cfg["C"], cfg["D"], cfg["M"]
+    sx = 2 if cfg["dtype"] == "bf16" else 4
+    sa = 2 if cfg["dtype"] == "bf16" else 4
+    bt = B * T
+    table = {
+        # fused route: x (+8-step halo re-read is not algorithmic) in, stream v out
+        "fused_writer_kernel": bt * (C * sx + D * sa),
+        # fused route: stream v in (moments out are negligible)
+        "fused_reader_kernel": bt * D * sa,
+        # general route
+        "gemm_nt_kernel(stem)": bt * (C * sx + D * 4),
+        "gemm_nt_kernel(drive)": bt * (D * 4 + 2 * M * 4),
+        "gemm_nt_kernel(synthesis)": bt * (2 * M * 4 + D * 4),
+        "scan_local_kernel": bt * 2 * M * 4,
+        "scan_apply_kernel": bt * 2 * M * 8,
+        "moments_partial_kernel": bt * 2 * M * 4,
+        "rmsnorm_kernel": bt * D * 8,
+        "drive_kernel": bt * 2 * M * 8,
+        "dwconv_unit_kernel(stem)": bt * D * 8,
+        "dwconv_unit_kernel(reader)": bt * D * 8,
+        "residual_kernel": bt * D * 16,
+    }
+    v = table.get(kernel)
+    return None if v is None else float(v)
+
+
+def committed_traffic(kernel: str, cfg) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary of this kernel, scaled to the
+    bench workload by tokens (line 'dram_bytes_per_token: N' in profiles/<kernel>*.md)."""
+    for path in sorted((ROOT / "profiles").glob(f"{kernel.split('(')[0]}*.md")):
+        m = re.search(r"dram_bytes_per_token:\s*([0-9.eE+]+)", path.read_text())
+        w = re.search(r"workload:\s*(\S+)", path.read_text())
+        if m and w and w.group(1) == cfg["workload"]:
+            return float(m.group(1)) * cfg["B"] * cfg["T"]
+    return None
+
+
+# ---------------------------------------------------------------- CPU path
+def cpu_forward_time(cfg, rows: int, params_np, seed=3):
+    """Seconds for the numpy oracle (fp32, the reference's precision) on `rows` rows."""
+    from oracle import alphabet_oracle as A
+
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, cfg["T"], cfg["C"])).astype(np.float32)
+    t0 = time.perf_counter()
+    A.alphabet_forward(x, params_np, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info()]
+        return max(n) if n else 1
+    except ImportError:
+        return 1
+
+
+def params_numpy(cfg):
+    return {k: v.numpy().astype(np.float32) for k, v in make_params(cfg).items()}
+
+
+# ---------------------------------------------------------------- arms
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    rows = args.ref_rows
+    p = params_numpy(cfg)
+    for _ in range(args.warmup):
+        cpu_forward_time(cfg, rows, p)
+    times = [cpu_forward_time(cfg, rows, p) for _ in range(args.steps)]
+    total = sum(times)
+    tokens = rows * cfg["T"] * args.steps
+    value = tokens / total
+    cores = cpu_threads()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": cfg["workload"], "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{rows} of {cfg['B']} rows x T={cfg['T']} per step, numpy "
+                                   "oracle restating the reference eager path in fp32"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args, cfg):
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from lnet_b200 import _lib
+    from lnet_b200.alphabet import _workspace_bytes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"warning: WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    lib = _lib.load()
+    model = build_model(cfg, dev)
+    x = make_inputs(cfg, dev)
+    B, T = cfg["B"], cfg["T"]
+    act = _lib.LNET_BF16 if cfg["dtype"] == "bf16" else _lib.LNET_F32
+    params, _keep = model._effective(dev)
+    req = model._request(x, None, None, None, act)
+    nbytes = _workspace_bytes(params, req)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    logits = torch.empty(B, cfg["K"], device=dev, dtype=torch.float32)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fwd():
+        st = lib.lnet_b200_alphabet_forward(ctypes.byref(params), ctypes.byref(req),
+                                            ws.data_ptr(), nbytes, logits.data_ptr(), None, None,
+                                            stream.cuda_stream)
+        _lib.check(st, "lnet_b200_alphabet_forward")
+        return _lib.last_launch_count()
+
+    for _ in range(max(args.warmup, 3)):
+        fwd()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches = 0
+    _lib.profile_enable(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            launches += fwd()
+            stops[i].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    tokens_all = B * T * world * args.steps
+    value = tokens_all / (total_ms / 1e3)
+
+    # ---- end to end through the public module API, host buffers, copies inside
+    x_host = x.cpu().pin_memory()
+    x_dev = torch.empty_like(x)
+    out_host = torch.empty(B, cfg["K"], dtype=torch.float32).pin_memory()
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(model(x_dev), non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(model(x_dev), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = tokens_all / (float(e2e_ms.item()) / 1e3)
+
+    if rank == 0:
+        # dominant kernel during the timed region
+        dom = max(prof.items(), key=lambda kv: kv[1][0]) if prof else ("", (0.0, 1))
+        name, (k_ms, k_n) = dom
+        avg_s = k_ms / max(k_n, 1) / 1e3
+        alg = algorithmic_bytes(name, cfg)
+        peak, peak_kind = measured_peaks()
+        achieved = alg / avg_s / 1e9 if alg and avg_s > 0 else None
+        roofline = {
+            "bound": "hbm", "kernel": name,
+            "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak if achieved else None,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+            "traffic": committed_traffic(name, cfg),
+            "algorithmic_bytes_per_launch": alg,
+            "avg_launch_ms": avg_s * 1e3,
+            "share_of_step": k_ms / sum(v[0] for v in prof.values()) if prof else None,
+        }
+        kernels = {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            p = params_numpy(cfg)
+            rows = args.cpu_rows
+            secs = cpu_forward_time(cfg, rows, p)
+            cpu = {"value": rows * T / secs, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                   "sample": f"{rows} of {B} rows x T={T} (one forward, {secs:.1f} s), numpy "
+                             "oracle restating the reference eager path in fp32"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": cfg["dtype"], "data": "synthetic (uint8 images / N(0,1), random-init weights)",
+            "config": {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * world,
+                       "seq_len": T, "raw_channels": cfg["C"], "model_dim": cfg["D"],
+                       "modes": cfg["M"], "classes": cfg["K"], "parallelism": f"batch{world}",
+                       "l2": "256 MiB flush between steps, outside the per-step event pair"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": x.numel() * x.element_size(),
+                    "d2h_bytes_per_step": B * cfg["K"] * 4},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "clocks": clocks.summary(),
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="4")
+    ap.add_argument("--cpu-rows", type=int, default=128)
+    ap.add_argument("--ref-rows", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (minimum)")
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    return run_b200(args, cfg)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -166,6 +166,17 @@ int lnet_b200_laplace_forward(const double *raw_decay, const double *residues,
  * this thread enqueued. */
 int lnet_b200_last_launch_count(void);
 
+/* Optional per-launch device timing (diagnostics; off by default).
+ * lnet_b200_profile_enable(1) clears old records and makes every following
+ * launch record a CUDA event on its stream; lnet_b200_profile_read
+ * synchronises those events and writes, per distinct kernel name, the total
+ * milliseconds and launch count (names '\n'-separated in names_buf).  Returns
+ * the number of kernels written.  No reference counterpart: replaces the
+ * torch.profiler usage of the reference's launch tuning scripts. */
+void lnet_b200_profile_enable(int on);
+int lnet_b200_profile_read(char *names_buf, int names_bytes, float *total_ms, int *launches,
+                           int max_entries);
+
 /* Message of the last error on the calling thread ("" if none). */
 const char *lnet_b200_last_error(void);
 

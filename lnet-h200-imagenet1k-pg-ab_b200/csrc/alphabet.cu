@@ -289,6 +289,7 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
     return fail(LNET_ERR_INVALID_ARGUMENT, "sequences must contain at least one step");
   if (!logits) return fail(LNET_ERR_INVALID_ARGUMENT, "logits is NULL");
   auto st = (cudaStream_t)stream;
+  begin_entry(st);
   const int64_t B = req->batch;
   const int M = params->modes;
   Plan pl;
@@ -315,6 +316,7 @@ extern "C" int lnet_b200_stem(const lnet_b200_alphabet_params *params,
                               const lnet_b200_alphabet_request *req, void *workspace,
                               size_t workspace_bytes, float *first_local, lnet_stream_t stream) {
   reset_launches();
+  begin_entry((cudaStream_t)stream);
   LNET_TRY(check_params(params));
   LNET_TRY(check_request(params, req));
   if (req->batch == 0 || req->steps == 0) return LNET_OK;
@@ -336,6 +338,7 @@ extern "C" int lnet_b200_writer(const lnet_b200_alphabet_params *params,
   Plan pl;
   LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
   auto st = (cudaStream_t)stream;
+  begin_entry(st);
   if (req->time_delta) {
     timestamps_kernel<<<(unsigned)cdiv(req->batch, 128), 128, 0, st>>>(req->time_delta, pl.ts,
                                                                        req->batch, req->steps);
@@ -349,6 +352,7 @@ extern "C" int lnet_b200_reader(const lnet_b200_alphabet_params *params,
                                 void *workspace, size_t workspace_bytes, float *moments,
                                 lnet_stream_t stream) {
   reset_launches();
+  begin_entry((cudaStream_t)stream);
   LNET_TRY(check_params(params));
   LNET_TRY(check_request(params, req));
   if (req->batch == 0 || req->steps == 0) return LNET_OK;
@@ -361,6 +365,7 @@ extern "C" int lnet_b200_head(const lnet_b200_alphabet_params *params, int64_t b
                               const float *writer_moments, const float *reader_moments,
                               float *logits, lnet_stream_t stream) {
   reset_launches();
+  begin_entry((cudaStream_t)stream);
   LNET_TRY(check_params(params));
   if (batch <= 0) return LNET_OK;
   if (!writer_moments || !reader_moments || !logits)
@@ -372,6 +377,7 @@ extern "C" int lnet_b200_zoh(const float *raw_decay, const float *raw_frequency,
                              const float *dt, int64_t steps, float *a_re, float *a_im,
                              float *g_re, float *g_im, lnet_stream_t stream) {
   reset_launches();
+  begin_entry((cudaStream_t)stream);
   if (modes < 1) return fail(LNET_ERR_INVALID_ARGUMENT, "modes must be positive");
   if (!raw_decay || !raw_frequency || !a_re || !a_im)
     return fail(LNET_ERR_INVALID_ARGUMENT, "zoh: NULL tensor pointer");

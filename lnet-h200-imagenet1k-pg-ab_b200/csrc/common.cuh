@@ -21,6 +21,8 @@ constexpr double kPi = 3.14159265358979323846;
 int fail(int code, const char *fmt, ...);
 int cuda_check(cudaError_t err, const char *what);
 void reset_launches();
+// Marks the start of an entry point's launches on `stream` (for profiling).
+void begin_entry(cudaStream_t stream);
 void count_launch(int n = 1);
 int launch_count();
 // Checks the most recent launch on this thread and counts it.

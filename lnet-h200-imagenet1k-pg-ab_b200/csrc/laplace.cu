@@ -159,6 +159,7 @@ extern "C" int lnet_b200_laplace_forward(const double *raw_decay, const double *
     return fail(LNET_ERR_WORKSPACE, "laplace: workspace of %zu bytes < required %zu",
                 workspace_bytes, need);
   auto st = (cudaStream_t)stream;
+  begin_entry(st);
   if (x_dtype == LNET_F64)
     return laplace_run<double>(raw_decay, residues, direct, bias, model_dim, modes, dt, min_decay,
                                (const double *)x, batch, steps, (double *)y, (double *)workspace,

@@ -113,6 +113,12 @@ SIGNATURES = {
          _i64, _c_p, _c_p, ctypes.c_size_t, _c_p],
     ),
     "lnet_b200_last_launch_count": (ctypes.c_int, []),
+    "lnet_b200_profile_enable": (None, [ctypes.c_int]),
+    "lnet_b200_profile_read": (
+        ctypes.c_int,
+        [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
+         ctypes.POINTER(ctypes.c_int), ctypes.c_int],
+    ),
     "lnet_b200_last_error": (ctypes.c_char_p, []),
     "lnet_b200_version": (ctypes.c_char_p, []),
 }
@@ -169,3 +175,18 @@ def check(status: int, what: str) -> None:
     if status == LNET_ERR_UNSUPPORTED:
         raise TypeError(msg)
     raise RuntimeError(msg)
+
+
+def profile_enable(on: bool) -> None:
+    load().lnet_b200_profile_enable(1 if on else 0)
+
+
+def profile_read(max_entries: int = 64) -> dict[str, tuple[float, int]]:
+    """Per kernel name: (total milliseconds, launches) since profile_enable(True)."""
+    lib = load()
+    buf = ctypes.create_string_buffer(1 << 16)
+    ms = (ctypes.c_float * max_entries)()
+    cnt = (ctypes.c_int * max_entries)()
+    n = lib.lnet_b200_profile_read(buf, len(buf), ms, cnt, max_entries)
+    names = buf.value.decode().split("\n")
+    return {names[i]: (float(ms[i]), int(cnt[i])) for i in range(n)}
