@@ -132,60 +132,74 @@ REASON_BITS = {
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the timed region."""
+    """Samples SM clock and clock-event (throttle) reasons every ~5 ms during the timed
+    region through NVML (read-only queries); falls back to nvidia-smi at 200 ms."""
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
         self.thread = None
+
+    def _run_nvml(self, pynvml):
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+            try:
+                bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+            except AttributeError:
+                bits = int(pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h))
+            self.samples.append((sm, mx, bits))
+            self._stop.wait(0.005)
+
+    def _run_smi(self):
+        proc = subprocess.Popen(
+            ["nvidia-smi", f"--id={self.index}",
+             "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        try:
+            for line in proc.stdout:
+                parts = [p.strip() for p in line.split(",")]
+                try:
+                    self.samples.append((float(parts[0]), float(parts[1]), int(parts[2], 16)))
+                except (ValueError, IndexError):
+                    pass
+                if self._stop.is_set():
+                    break
+        finally:
+            proc.terminate()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}",
-                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (OSError, ValueError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            target = lambda: self._run_nvml(pynvml)  # noqa: E731
+        except Exception:  # noqa: BLE001
+            target = self._run_smi
+        self.thread = threading.Thread(target=target, daemon=True)
+        self.thread.start()
+        time.sleep(0.02)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread:
-                self.thread.join(timeout=2)
+        self._stop.set()
+        if self.thread:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        for line in self.lines:
-            parts = [s.strip() for s in line.split(",")]
-            if len(parts) < 3:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = max(mx, float(parts[1]))
-                bits = int(parts[2], 16)
-            except ValueError:
-                continue
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        reasons = set()
+        for _, _, bits in self.samples:
             for bit, name in REASON_BITS.items():
                 if bits & bit and name != "gpu_idle":
                     reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------- roofline helpers
@@ -363,6 +377,11 @@ def run_b200(args, cfg):
     value = tokens_all / (total_ms / 1e3)
 
     # ---- end to end through the public module API, host buffers, copies inside
+    if args.skip_e2e:
+        if rank == 0:
+            print(json.dumps({"value": value, "ms_per_step": total_ms / args.steps,
+                              "kernels": _lib_kernels(prof)}), flush=True)
+        return 0
     x_host = x.cpu().pin_memory()
     x_dev = torch.empty_like(x)
     out_host = torch.empty(B, cfg["K"], dtype=torch.float32).pin_memory()
@@ -437,6 +456,10 @@ def run_b200(args, cfg):
     return 0
 
 
+def _lib_kernels(prof):
+    return {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,11 +470,18 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=128)
     ap.add_argument("--ref-rows", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch override (small cases for profiling only)")
+    ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["B"] = args.batch
+        cfg["workload"] = cfg["workload"].replace(f"_b{CONFIGS[args.config]['B']}_",
+                                                  f"_b{args.batch}_")
     if args.impl == "reference":
         return run_reference(args, cfg)
     return run_b200(args, cfg)

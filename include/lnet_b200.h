@@ -104,6 +104,17 @@ int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
                                size_t workspace_bytes, float *logits, float *writer_moments,
                                float *reader_moments, lnet_stream_t stream);
 
+/* Route selection for lnet_b200_alphabet_forward (process-wide):
+ * 0 = automatic (the fused unit-grid kernels when the request has no
+ * metadata, bf16 activations and a compiled shape; the general route
+ * otherwise), 1 = general route only.  No reference counterpart: replaces the
+ * reference's per-instance fused-inference gates (src/lnet/alphabet.py:190-223,
+ * 257-348). */
+int lnet_b200_set_route(int route);
+/* Route the current setting picks for (params, req): 0 fused, 1 general, -1 invalid. */
+int lnet_b200_alphabet_route(const lnet_b200_alphabet_params *params,
+                             const lnet_b200_alphabet_request *req);
+
 /* Stage entry points (same request/params conventions; intermediate tensors
  * fp32 [B, T, D] unless noted). */
 

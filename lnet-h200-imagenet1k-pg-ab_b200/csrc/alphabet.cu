@@ -16,6 +16,14 @@
 namespace lnet {
 
 constexpr int kScanChunk = 64;
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+    return 148;
+  return n;
+}
 constexpr int kMomChunk = 64;
 
 static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), 148 * 32)); }
@@ -249,13 +257,27 @@ static int plan_all(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet
   return LNET_OK;
 }
 
+static int g_route = 0;  // 0 = automatic, 1 = general route only
+
 static bool use_fused(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r) {
-  return !r->time_delta && fused_supported(p, r);
+  return g_route == 0 && !r->time_delta && fused_supported(p, r);
 }
 
 }  // namespace lnet
 
 using namespace lnet;
+
+extern "C" int lnet_b200_set_route(int route) {
+  if (route != 0 && route != 1) return fail(LNET_ERR_INVALID_ARGUMENT, "route must be 0 or 1");
+  g_route = route;
+  return LNET_OK;
+}
+
+extern "C" int lnet_b200_alphabet_route(const lnet_b200_alphabet_params *params,
+                                        const lnet_b200_alphabet_request *req) {
+  if (check_params(params) != LNET_OK || check_request(params, req) != LNET_OK) return -1;
+  return use_fused(params, req) ? 0 : 1;
+}
 
 extern "C" int lnet_b200_alphabet_workspace_size(const lnet_b200_alphabet_params *params,
                                                  const lnet_b200_alphabet_request *req,

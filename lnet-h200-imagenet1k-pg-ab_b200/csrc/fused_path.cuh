@@ -1,28 +1,863 @@
-// Unit-grid fused route of the ALPHABET forward (placeholder until the fused
-// kernels land) and the scratch-free head kernel.
+// Fused unit-grid route of the ALPHABET forward on sm_100a.
+//
+// Work item = one chunk of kChunk (=128) consecutive steps of one batch row.
+// Items are claimed from an atomic counter in chunk-major order
+// (item = chunk * B + row), so the predecessor (row, chunk - 1) of every item
+// was claimed earlier by a running CTA: the decoupled look-back below always
+// makes progress.
+//
+// fused_writer_kernel (per item, one CTA of 256 threads, persistent):
+//   1. x rows [t0 - 8, t0 + 136) -> shared memory, no-swizzle K-major slabs;
+//   2. stem projection + dilated depthwise conv as ONE tcgen05 GEMM:
+//        acc[t, d] = sum_k sum_c x[t + 4k - 8, c] * (w[d, k] P[d, c]),
+//      the five taps are five row-shifted descriptors over the same tile;
+//   3. +bias, SiLU, RMSNorm (thread per step), xhat -> bf16 slab;
+//   4. drive GEMM in mode-major orientation: TMEM lane m holds the complex
+//      drive u_m(t) of mode m over all 128 steps (gamma is folded into the
+//      frame), so the scan reads TMEM without any transpose;
+//   5. per-mode sequential scan from zero -> chunk aggregate (last 4 states)
+//      published; look-back over predecessors yields the carry-in; the
+//      inclusive record is published; second pass from the true carry
+//      accumulates E, C1, C2, C4 and writes the states (bf16) as the A operand
+//      of
+//   6. the synthesis GEMM (token-major) and the residual epilogue
+//      v = x + ls (s W^T + ds xhat), stored as bf16.
+// fused_reader_kernel: the same skeleton on the writer stream: conv of the
+//   stream tile on CUDA cores, SiLU, RMSNorm, drive GEMM, scan, moments.
 #pragma once
+
+#include <cuda_bf16.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "generic_kernels.cuh"
+#include "sm100.cuh"
 
 namespace lnet {
 
+constexpr int kChunk = 128;
+constexpr int kHalo = 8;
+constexpr int kTaps = 5;
+constexpr int kXRows = kChunk + 2 * kHalo;
+constexpr int kFusedThreads = 256;
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kFlagAgg = 1, kFlagIncl = 2;
+constexpr uint32_t kErrMbar = 1, kErrLookback = 2;
+
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+// ---------------------------------------------------------------- workspace
 struct FusedWorkspace {
-  float *moments = nullptr;  // [2][B][7M]
+  float *moments = nullptr;            // [2][B][7M]
+  __nv_bfloat16 *q = nullptr;          // stem B operand   [5][C/8][D][8]
+  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][M][8]
+  __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][M][8]
+  __nv_bfloat16 *wsyn = nullptr;       // synthesis B      [2M/8][D][8]
+  float *consts = nullptr;             // [2][10M]: a_re, a_im, a^(L-i) re/im (i = 0..3)
+  __nv_bfloat16 *stream = nullptr;     // [B, T, D]
+  float *wpartial = nullptr;           // [B * nch][7M]
+  float *rpartial = nullptr;
+  float *wrec = nullptr;               // [B * nch][2][4][2M]
+  float *rrec = nullptr;
+  uint32_t *flags = nullptr;           // [2][B * nch] + counters[2] + error[2]
+  size_t flag_words = 0;
 };
+
+inline int64_t fused_chunks(int64_t steps) { return cdiv(steps, kChunk); }
 
 inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_params *p,
                        const lnet_b200_alphabet_request *r) {
-  w.moments = ar.take<float>((size_t)2 * r->batch * 7 * p->modes);
+  const int C = p->raw_input_dim, D = p->model_dim, M = p->modes;
+  const int64_t B = r->batch, nch = fused_chunks(std::max<int64_t>(r->steps, 1));
+  w.moments = ar.take<float>((size_t)2 * B * 7 * M);
+  w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
+  w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * M);
+  w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * M);
+  w.wsyn = ar.take<__nv_bfloat16>((size_t)2 * M * D);
+  w.consts = ar.take<float>((size_t)2 * 10 * M);
+  w.stream = ar.take<__nv_bfloat16>((size_t)B * r->steps * D);
+  w.wpartial = ar.take<float>((size_t)B * nch * 7 * M);
+  w.rpartial = ar.take<float>((size_t)B * nch * 7 * M);
+  w.wrec = ar.take<float>((size_t)B * nch * 16 * M);
+  w.rrec = ar.take<float>((size_t)B * nch * 16 * M);
+  w.flag_words = (size_t)2 * B * nch + 4;
+  w.flags = ar.take<uint32_t>(w.flag_words);
 }
 
-inline bool fused_supported(const lnet_b200_alphabet_params *, const lnet_b200_alphabet_request *) {
+// ---------------------------------------------------------------- operand preparation
+// Writes every bf16 operand in its shared-memory slab layout
+// (element (row, k) of an R-row K-major operand at ((k / 8) * R + row) * 8 + k % 8)
+// and the per-mode pole constants, all in double before one rounding.
+__device__ __forceinline__ void cmul_d(double ar, double ai, double br, double bi, double &cr,
+                                       double &ci) {
+  cr = ar * br - ai * bi;
+  ci = ar * bi + ai * br;
+}
+
+__global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace w) {
+  const int C = p.raw_input_dim, D = p.model_dim, M = p.modes, K5 = p.conv_kernel;
+  const int64_t n_q = (int64_t)kTaps * C * D;
+  const int64_t n_drive = (int64_t)2 * D * M;
+  const int64_t n_syn = (int64_t)2 * M * D;
+  const int64_t total = n_q + 2 * n_drive + n_syn + 2 * M;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < n_q) {  // Q_k[d][c] = w[d][k] * P[d][c]
+      int k = (int)(i / ((int64_t)C * D));
+      int rem = (int)(i - (int64_t)k * C * D);
+      int d = rem / C, c = rem - d * C;
+      double v = (double)p.stem_conv_weight[d * K5 + k] * (double)p.stem_projection[d * C + c];
+      w.q[(int64_t)k * C * D + ((c / 8) * D + d) * 8 + (c % 8)] = __float2bfloat16_rn((float)v);
+      continue;
+    }
+    int64_t j = i - n_q;
+    if (j < 2 * n_drive) {  // drive A rows = modes, K = d; gamma folded in
+      int blk = (int)(j / n_drive);
+      int64_t rem = j - blk * n_drive;
+      int part = (int)(rem / ((int64_t)D * M));
+      int rem2 = (int)(rem - (int64_t)part * D * M);
+      int d = rem2 / M, m = rem2 - d * M;
+      const float *frame = blk == 0 ? p.writer_frame : p.reader_frame;
+      double damping, frequency;
+      mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
+                blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
+                frequency);
+      Zoh z = zoh_eval(damping, frequency, 1.0);
+      double fr = frame[d * 2 * M + m], fi = frame[d * 2 * M + M + m];
+      double v = part == 0 ? (double)z.g_re * fr - (double)z.g_im * fi
+                           : (double)z.g_re * fi + (double)z.g_im * fr;
+      __nv_bfloat16 *dst = blk == 0 ? w.wdrive : w.rdrive;
+      dst[(int64_t)part * D * M + ((d / 8) * M + m) * 8 + (d % 8)] = __float2bfloat16_rn((float)v);
+      continue;
+    }
+    j -= 2 * n_drive;
+    if (j < n_syn) {  // synthesis B rows = d, K = 2M
+      int d = (int)(j / (2 * M)), jj = (int)(j - (int64_t)d * 2 * M);
+      w.wsyn[((jj / 8) * D + d) * 8 + (jj % 8)] = __float2bfloat16_rn(p.writer_frame[d * 2 * M + jj]);
+      continue;
+    }
+    j -= n_syn;  // per-mode constants of both blocks
+    int blk = (int)(j / M), m = (int)(j - (int64_t)blk * M);
+    double damping, frequency;
+    mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
+              blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
+              frequency);
+    Zoh z = zoh_eval(damping, frequency, 1.0);
+    // a^(L - i), i = 0..3: powers of the fp32 coefficient the scan multiplies by,
+    // accumulated in double so that carries match step-by-step propagation.
+    const double ar = (double)z.a_re, ai = (double)z.a_im;
+    double pr = 1.0, pi = 0.0;
+    float *k = w.consts + blk * 10 * M;
+    for (int step = 1; step <= kChunk; ++step) {
+      double nr, ni;
+      cmul_d(pr, pi, ar, ai, nr, ni);
+      pr = nr;
+      pi = ni;
+      int idx = kChunk - step;  // step == L - idx
+      if (idx < 4) {
+        k[2 * M + 2 * idx * M + m] = (float)pr;
+        k[2 * M + (2 * idx + 1) * M + m] = (float)pi;
+      }
+    }
+    k[m] = z.a_re;
+    k[M + m] = z.a_im;
+  }
+}
+
+// ---------------------------------------------------------------- shared-memory plans
+template <int C, int D, int M>
+struct WriterPlan {
+  static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 128 && D <= 256, "shape");
+  static constexpr int SLAB_AD = M * 16;
+  static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
+  static constexpr int SLAB_Q = D * 16;
+  static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
+  static constexpr int SLAB_WS = D * 16;
+  static constexpr int WS_BYTES = (2 * M / 8) * SLAB_WS;
+  static constexpr int SLAB_X = kXRows * 16 + 16;
+  static constexpr int X_BYTES = (C / 8) * SLAB_X;
+  static constexpr int FL_BYTES = kChunk * D * 2;
+  static constexpr int XF_BYTES = cmax(X_BYTES, FL_BYTES);
+  static constexpr int SLAB_XH = kChunk * 16;
+  static constexpr int XH_BYTES = (D / 8) * SLAB_XH;
+  static constexpr int SLAB_S = kChunk * 16 + 16;
+  static constexpr int S_BYTES = (2 * M / 8) * SLAB_S;
+  static constexpr int XS_BYTES = cmax(XH_BYTES, S_BYTES);
+  static constexpr int OFF_AD = 0;  // UMMA reads 128 rows of each drive slab: the tail
+  static constexpr int OFF_Q = OFF_AD + AD_BYTES;  // past the M real rows lands in Q
+  static constexpr int OFF_WS = OFF_Q + Q_BYTES;
+  static constexpr int OFF_XF = OFF_WS + WS_BYTES;
+  static constexpr int OFF_XS = OFF_XF + XF_BYTES;
+  static constexpr int OFF_RED = OFF_XS + XS_BYTES;          // float [2][128]
+  static constexpr int OFF_RS = OFF_RED + 2 * kChunk * 4;    // float [128]
+  static constexpr int OFF_MISC = OFF_RS + kChunk * 4;       // mbar, tmem base, item
+  static constexpr int BYTES = OFF_MISC + 64;
+  static constexpr int TMEM_COLS = 512;  // [0,128) stem/synthesis acc, [128,256) u re, [256,384) u im
+  static_assert(Q_BYTES >= (kChunk - M) * 16, "drive-operand tail must stay inside the stem slabs");
+};
+
+template <int D, int M>
+struct ReaderPlan {
+  static_assert(D % 32 == 0 && M % 8 == 0 && M <= 128 && D <= 256, "shape");
+  static constexpr int SLAB_AD = M * 16;
+  static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
+  static constexpr int PITCH = D * 2 + 16;  // stream tile row pitch (bank-conflict free)
+  static constexpr int V_BYTES = kXRows * PITCH;
+  static constexpr int SLAB_XH = kChunk * 16;
+  static constexpr int XH_BYTES = (D / 8) * SLAB_XH;
+  static constexpr int OFF_AD = 0;
+  static constexpr int OFF_V = OFF_AD + AD_BYTES;  // drive-operand tail lands in the tile
+  static constexpr int OFF_XH = OFF_V + V_BYTES;
+  static constexpr int OFF_RED = OFF_XH + XH_BYTES;
+  static constexpr int OFF_MISC = OFF_RED + 2 * kChunk * 4;
+  static constexpr int BYTES = OFF_MISC + 64;
+  // at most two CTAs per SM so that two 256-column TMEM allocations always fit
+  static constexpr int LAUNCH_BYTES = cmax(BYTES, 100 * 1024);
+  static constexpr int TMEM_COLS = 256;  // [0,128) u re, [128,256) u im
+  static_assert(V_BYTES >= (kChunk - M) * 16, "drive-operand tail must stay inside the tile");
+};
+
+struct FusedArgs {
+  const __nv_bfloat16 *in;  // writer: x [B,T,C]; reader: stream [B,T,D]
+  int64_t B, T;
+  int64_t n_chunks;
+  const __nv_bfloat16 *q, *drive, *syn;
+  const float *consts;      // 10M floats of this block
+  const float *conv_w, *conv_b, *norm, *ds, *ls;
+  __nv_bfloat16 *out;       // writer stream
+  float *partial;           // [B * nch][7M]
+  float *rec;               // [B * nch][2][4][2M]
+  uint32_t *flags;          // [B * nch]
+  uint32_t *counter;
+  uint32_t *error;
+};
+
+// 16-byte copy of prepared operands into shared memory.
+__device__ __forceinline__ void copy_smem(void *dst, const void *src, int bytes) {
+  const uint4 *s = reinterpret_cast<const uint4 *>(src);
+  uint4 *d = reinterpret_cast<uint4 *>(dst);
+  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = __ldg(s + i);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// ---------------------------------------------------------------- scan + look-back
+// Executed by the first SW = ceil(M/32) warps; thread tid owns mode tid (if < M).
+// u_re / u_im live in TMEM columns [col_re, col_re + 128) / [col_im, ...) of the
+// thread's own lane.  Returns the moment partial sums of this chunk in mom[7].
+template <int M, bool WRITE_STATES>
+__device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_im, int n,
+                                           int64_t row, int64_t chunk, int64_t n_chunks,
+                                           const float *consts, float *rec, uint32_t *flags,
+                                           uint32_t *error, uint8_t *s_slab, int slab_s,
+                                           float *mom) {
+  constexpr int SW = (M + 31) / 32;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const bool live = tid < M;
+  const int m = live ? tid : 0;
+  const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+  const float ar = consts[m], ai = consts[M + m];
+  // ---- pass 1: chunk-local scan from zero
+  float sr = 0.f, si = 0.f;
+  float l_r[4] = {0, 0, 0, 0}, l_i[4] = {0, 0, 0, 0};  // l[0] = last state
+  for (int c0 = 0; c0 < n; c0 += 16) {
+    float ur[16], ui[16];
+    sm100::tmem_ld16(lane_addr + col_re + c0, ur);
+    sm100::tmem_ld16(lane_addr + col_im + c0, ui);
+    sm100::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (c0 + i < n) {
+        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
+        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
+        sr = nr;
+        si = ni;
+        l_r[3] = l_r[2]; l_i[3] = l_i[2];
+        l_r[2] = l_r[1]; l_i[2] = l_i[1];
+        l_r[1] = l_r[0]; l_i[1] = l_i[0];
+        l_r[0] = sr; l_i[0] = si;
+      }
+    }
+  }
+  const int64_t item = row * n_chunks + chunk;  // record index (row-major)
+  float *my = rec + item * 16 * M;
+  if (live) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      my[(2 * i) * M + m] = l_r[i];
+      my[(2 * i + 1) * M + m] = l_i[i];
+    }
+    __threadfence();
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(SW * 32) : "memory");
+  if (tid == 0) sm100::st_release(flags + item, kFlagAgg);
+  // ---- look-back: true states at the last four steps of the previous chunk
+  float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
+  if (chunk > 0) {
+    const int64_t prev = item - 1;
+    uint32_t st = 0;
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+      st = sm100::ld_acquire(flags + prev);
+      if (st >= kFlagAgg) break;
+      __nanosleep(40);
+    }
+    if (st < kFlagAgg) {
+      if (tid == 0) atomicOr(error, kErrLookback);
+    } else if (st == kFlagIncl) {
+      const float *pr = rec + prev * 16 * M + 8 * M;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        p_r[i] = __ldcg(pr + (2 * i) * M + m);
+        p_i[i] = __ldcg(pr + (2 * i + 1) * M + m);
+      }
+    } else {
+      // X = true end state of chunk - 2, composed from aggregates back to an
+      // inclusive record (or the sequence start).
+      const float aLr = consts[2 * M + m], aLi = consts[3 * M + m];
+      float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
+      for (int64_t q = chunk - 2; q >= 0; --q) {
+        const int64_t qi = row * n_chunks + q;
+        uint32_t sq = 0;
+        for (uint32_t it = 0; it < kSpinLimit; ++it) {
+          sq = sm100::ld_acquire(flags + qi);
+          if (sq >= kFlagAgg) break;
+          __nanosleep(40);
+        }
+        if (sq < kFlagAgg) {
+          if (tid == 0) atomicOr(error, kErrLookback);
+          break;
+        }
+        const float *qr = rec + qi * 16 * M + (sq == kFlagIncl ? 8 * M : 0);
+        float er = __ldcg(qr + m), ei = __ldcg(qr + M + m);
+        xr = fmaf(mr, er, fmaf(-mi, ei, xr));
+        xi = fmaf(mr, ei, fmaf(mi, er, xi));
+        if (sq == kFlagIncl) break;
+        float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
+        mr = nr;
+        mi = ni;
+      }
+      const float *pa = rec + prev * 16 * M;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float gr = consts[2 * M + 2 * i * M + m], gi = consts[2 * M + (2 * i + 1) * M + m];
+        float lr = __ldcg(pa + (2 * i) * M + m), li = __ldcg(pa + (2 * i + 1) * M + m);
+        p_r[i] = lr + (gr * xr - gi * xi);
+        p_i[i] = li + (gr * xi + gi * xr);
+      }
+    }
+  }
+  // inclusive record of this chunk (only consumed when the chunk is full)
+  if (live) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float gr = consts[2 * M + 2 * i * M + m], gi = consts[2 * M + (2 * i + 1) * M + m];
+      my[8 * M + (2 * i) * M + m] = l_r[i] + (gr * p_r[0] - gi * p_i[0]);
+      my[8 * M + (2 * i + 1) * M + m] = l_i[i] + (gr * p_i[0] + gi * p_r[0]);
+    }
+    __threadfence();
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(SW * 32) : "memory");
+  if (tid == 0) sm100::st_release(flags + item, kFlagIncl);
+  // ---- pass 2: true states, moments, states for the synthesis GEMM
+  const bool hist = chunk > 0;
+  float h1r = p_r[0], h1i = p_i[0], h2r = p_r[1], h2i = p_i[1];
+  float h3r = p_r[2], h3i = p_i[2], h4r = p_r[3], h4i = p_i[3];
+  sr = p_r[0];
+  si = p_i[0];
+  float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
+  for (int c0 = 0; c0 < n; c0 += 16) {
+    float ur[16], ui[16];
+    sm100::tmem_ld16(lane_addr + col_re + c0, ur);
+    sm100::tmem_ld16(lane_addr + col_im + c0, ui);
+    sm100::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int t = c0 + i;
+      if (t < n) {
+        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
+        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
+        sr = nr;
+        si = ni;
+        e = fmaf(sr, sr, fmaf(si, si, e));
+        if (hist || t >= 1) {
+          c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
+          c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
+        }
+        if (hist || t >= 2) {
+          c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
+          c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
+        }
+        if (hist || t >= 4) {
+          c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
+          c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
+        }
+        h4r = h3r; h4i = h3i;
+        h3r = h2r; h3i = h2i;
+        h2r = h1r; h2i = h1i;
+        h1r = sr; h1i = si;
+        if constexpr (WRITE_STATES) {
+          if (live) {
+            __nv_bfloat16 *pr_ = reinterpret_cast<__nv_bfloat16 *>(
+                s_slab + (m / 8) * slab_s + t * 16 + (m % 8) * 2);
+            __nv_bfloat16 *pi_ = reinterpret_cast<__nv_bfloat16 *>(
+                s_slab + ((M + m) / 8) * slab_s + t * 16 + ((M + m) % 8) * 2);
+            *pr_ = __float2bfloat16_rn(sr);
+            *pi_ = __float2bfloat16_rn(si);
+          }
+        }
+      }
+    }
+  }
+  mom[0] = e;
+  mom[1] = c1r;
+  mom[2] = c1i;
+  mom[3] = c2r;
+  mom[4] = c2i;
+  mom[5] = c4r;
+  mom[6] = c4i;
+}
+
+// Issues one GEMM: `ksteps` K=16 steps of D[tmem] (+)= A * B^T.
+__device__ __forceinline__ void issue_gemm(uint32_t d_tmem, uint32_t a_addr, int a_slab,
+                                           uint32_t b_addr, int b_slab, int ksteps,
+                                           uint32_t idesc, bool accumulate_first) {
+  for (int kk = 0; kk < ksteps; ++kk) {
+    uint64_t ad = sm100::make_desc(a_addr + 2 * kk * a_slab, a_slab, 128);
+    uint64_t bd = sm100::make_desc(b_addr + 2 * kk * b_slab, b_slab, 128);
+    sm100::mma_bf16(d_tmem, ad, bd, idesc, (accumulate_first || kk > 0) ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void wait_mma(uint64_t *mbar, uint32_t &phase, uint32_t *error) {
+  if (!sm100::mbar_wait_bounded(mbar, phase, kSpinLimit)) {
+    if (threadIdx.x == 0) atomicOr(error, kErrMbar);
+  }
+  phase ^= 1u;
+  sm100::tc_fence_after();
+}
+
+// ---------------------------------------------------------------- writer kernel
+template <int C, int D, int M>
+__global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArgs a) {
+  using P = WriterPlan<C, D, M>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_MISC + 8);
+  int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);
+  float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
+  float *rs_s = reinterpret_cast<float *>(smem + P::OFF_RS);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t s_base = sm100::smem_u32(smem);
+
+  if (tid == 0) {
+    sm100::mbar_init(mbar, 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, P::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
+  copy_smem(smem + P::OFF_Q, a.q, P::Q_BYTES);
+  copy_smem(smem + P::OFF_WS, a.syn, P::WS_BYTES);
+  sm100::fence_proxy_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  uint32_t phase = 0;
+  const int row = 32 * (warp & 3) + lane;  // step within the chunk (TMEM lane)
+  const int half = warp >> 2;              // column half of the token-major epilogues
+  constexpr int HD = D / 2;
+  const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+  const int64_t total = a.B * a.n_chunks;
+
+  for (;;) {
+    if (tid == 0) *item_slot = (int64_t)atomicAdd(a.counter, 1u);
+    __syncthreads();
+    const int64_t item = *item_slot;
+    if (item >= total) break;
+    const int64_t chunk = item / a.B, b = item - chunk * a.B;
+    const int64_t t0 = chunk * kChunk;
+    const int n = (int)min((int64_t)kChunk, a.T - t0);
+
+    // 1. x tile (zero outside [0, T))
+    for (int i = tid; i < kXRows * (C / 8); i += kFusedThreads) {
+      int r = i / (C / 8), kc = i - (i / (C / 8)) * (C / 8);
+      int64_t tok = t0 - kHalo + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (tok >= 0 && tok < a.T)
+        v = __ldg(reinterpret_cast<const uint4 *>(a.in + ((b * a.T + tok) * C + kc * 8)));
+      *reinterpret_cast<uint4 *>(smem + P::OFF_XF + kc * P::SLAB_X + r * 16) = v;
+    }
+    sm100::fence_proxy_async_smem();
+    __syncthreads();
+    // 2. stem GEMM: five row-shifted views of the tile
+    if (tid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
+      for (int k = 0; k < kTaps; ++k)
+        issue_gemm(tbase, s_base + P::OFF_XF + 4 * k * 16, P::SLAB_X,
+                   s_base + P::OFF_Q + k * (C / 8) * P::SLAB_Q, P::SLAB_Q, C / 16, idesc, k > 0);
+      sm100::mma_commit(mbar);
+    }
+    wait_mma(mbar, phase, a.error);
+    // 3. bias + SiLU + RMSNorm (thread per step, two column halves)
+    float f[HD];
+#pragma unroll
+    for (int j = 0; j < HD / 16; ++j) sm100::tmem_ld16(lane_addr + half * HD + 16 * j, f + 16 * j);
+    sm100::tmem_ld_wait();
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+      f[i] = silu_f(f[i] + __ldg(a.conv_b + half * HD + i));
+      ss = fmaf(f[i], f[i], ss);
+    }
+    red[half * kChunk + row] = ss;
+    __syncthreads();
+    const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
+    if (half == 0) rs_s[row] = rs;
+#pragma unroll
+    for (int g = 0; g < HD / 8; ++g) {
+      const int d0 = half * HD + 8 * g;
+      uint4 xh, fl;
+      float h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * __ldg(a.norm + d0 + i);
+      xh.x = pack_bf16x2(h[0], h[1]);
+      xh.y = pack_bf16x2(h[2], h[3]);
+      xh.z = pack_bf16x2(h[4], h[5]);
+      xh.w = pack_bf16x2(h[6], h[7]);
+      fl.x = pack_bf16x2(f[8 * g + 0], f[8 * g + 1]);
+      fl.y = pack_bf16x2(f[8 * g + 2], f[8 * g + 3]);
+      fl.z = pack_bf16x2(f[8 * g + 4], f[8 * g + 5]);
+      fl.w = pack_bf16x2(f[8 * g + 6], f[8 * g + 7]);
+      *reinterpret_cast<uint4 *>(smem + P::OFF_XS + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
+      *reinterpret_cast<uint4 *>(smem + P::OFF_XF + row * (D * 2) + d0 * 2) = fl;
+    }
+    sm100::fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    // 4. drive GEMM, mode-major: lanes = modes, columns = steps
+    if (tid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 128);
+      for (int part = 0; part < 2; ++part)
+        issue_gemm(tbase + 128 + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
+                   P::SLAB_AD, s_base + P::OFF_XS, P::SLAB_XH, D / 16, idesc, false);
+      sm100::mma_commit(mbar);
+    }
+    wait_mma(mbar, phase, a.error);
+    // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
+    constexpr int SW = (M + 31) / 32;
+    if (warp < SW) {
+      float mom[7];
+      chunk_scan<M, true>(tbase, 128, 256, n, b, chunk, a.n_chunks, a.consts, a.rec, a.flags,
+                          a.error, smem + P::OFF_XS, P::SLAB_S, mom);
+      if (tid < M) {
+        float *dst = a.partial + (b * a.n_chunks + chunk) * 7 * M;
+#pragma unroll
+        for (int k = 0; k < 7; ++k) dst[k * M + tid] = mom[k];
+      }
+    }
+    sm100::fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    // 6. synthesis GEMM (token-major) into columns [0, D)
+    if (tid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
+      issue_gemm(tbase, s_base + P::OFF_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
+                 idesc, false);
+      sm100::mma_commit(mbar);
+    }
+    wait_mma(mbar, phase, a.error);
+    // 7. residual epilogue: v = fl + ls * (modal + ds * xhat), xhat = fl * rs * g
+    {
+      float modal[HD];
+#pragma unroll
+      for (int j = 0; j < HD / 16; ++j)
+        sm100::tmem_ld16(lane_addr + half * HD + 16 * j, modal + 16 * j);
+      sm100::tmem_ld_wait();
+      const float rsr = rs_s[row];
+      if (row < n) {
+        __nv_bfloat16 *dst = a.out + ((b * a.T + t0 + row) * D + half * HD);
+#pragma unroll
+        for (int g = 0; g < HD / 8; ++g) {
+          const int d0 = half * HD + 8 * g;
+          uint4 fl = *reinterpret_cast<const uint4 *>(smem + P::OFF_XF + row * (D * 2) + d0 * 2);
+          const __nv_bfloat16 *fv = reinterpret_cast<const __nv_bfloat16 *>(&fl);
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int d = d0 + i;
+            const float x = __bfloat162float(fv[i]);
+            const float xh = x * rsr * __ldg(a.norm + d);
+            o[i] = x + __ldg(a.ls + d) * (modal[8 * g + i] + __ldg(a.ds + d) * xh);
+          }
+          uint4 ov;
+          ov.x = pack_bf16x2(o[0], o[1]);
+          ov.y = pack_bf16x2(o[2], o[3]);
+          ov.z = pack_bf16x2(o[4], o[5]);
+          ov.w = pack_bf16x2(o[6], o[7]);
+          *reinterpret_cast<uint4 *>(dst + 8 * g) = ov;
+        }
+      }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tbase, P::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- reader kernel
+template <int D, int M>
+__global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArgs a) {
+  using P = ReaderPlan<D, M>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_MISC + 8);
+  int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);
+  float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t s_base = sm100::smem_u32(smem);
+
+  if (tid == 0) {
+    sm100::mbar_init(mbar, 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, P::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
+  sm100::fence_proxy_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  uint32_t phase = 0;
+  const int row = 32 * (warp & 3) + lane;
+  const int half = warp >> 2;
+  constexpr int HD = D / 2;
+  const int64_t total = a.B * a.n_chunks;
+
+  for (;;) {
+    if (tid == 0) *item_slot = (int64_t)atomicAdd(a.counter, 1u);
+    __syncthreads();
+    const int64_t item = *item_slot;
+    if (item >= total) break;
+    const int64_t chunk = item / a.B, b = item - chunk * a.B;
+    const int64_t t0 = chunk * kChunk;
+    const int n = (int)min((int64_t)kChunk, a.T - t0);
+
+    // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T)
+    for (int i = tid; i < kXRows * (D / 8); i += kFusedThreads) {
+      int r = i / (D / 8), kc = i - (i / (D / 8)) * (D / 8);
+      int64_t tok = t0 - kHalo + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (tok >= 0 && tok < a.T)
+        v = __ldcg(reinterpret_cast<const uint4 *>(a.in + ((b * a.T + tok) * D + kc * 8)));
+      *reinterpret_cast<uint4 *>(smem + P::OFF_V + r * P::PITCH + kc * 16) = v;
+    }
+    __syncthreads();
+    // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm
+    float f[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) f[i] = __ldg(a.conv_b + half * HD + i);
+#pragma unroll
+    for (int k = 0; k < kTaps; ++k) {
+      const uint8_t *src = smem + P::OFF_V + (row + 4 * k) * P::PITCH + half * HD * 2;
+#pragma unroll
+      for (int g = 0; g < HD / 8; ++g) {
+        uint4 v = *reinterpret_cast<const uint4 *>(src + g * 16);
+        const __nv_bfloat16 *vv = reinterpret_cast<const __nv_bfloat16 *>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          f[8 * g + i] = fmaf(__ldg(a.conv_w + (half * HD + 8 * g + i) * kTaps + k),
+                              __bfloat162float(vv[i]), f[8 * g + i]);
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+      f[i] = silu_f(f[i]);
+      ss = fmaf(f[i], f[i], ss);
+    }
+    red[half * kChunk + row] = ss;
+    __syncthreads();
+    const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
+#pragma unroll
+    for (int g = 0; g < HD / 8; ++g) {
+      const int d0 = half * HD + 8 * g;
+      float h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * __ldg(a.norm + d0 + i);
+      uint4 xh;
+      xh.x = pack_bf16x2(h[0], h[1]);
+      xh.y = pack_bf16x2(h[2], h[3]);
+      xh.z = pack_bf16x2(h[4], h[5]);
+      xh.w = pack_bf16x2(h[6], h[7]);
+      *reinterpret_cast<uint4 *>(smem + P::OFF_XH + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
+    }
+    sm100::fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    // 3. drive GEMM (mode-major)
+    if (tid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 128);
+      for (int part = 0; part < 2; ++part)
+        issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
+                   P::SLAB_AD, s_base + P::OFF_XH, P::SLAB_XH, D / 16, idesc, false);
+      sm100::mma_commit(mbar);
+    }
+    wait_mma(mbar, phase, a.error);
+    // 4. scan + look-back + moments
+    constexpr int SW = (M + 31) / 32;
+    if (warp < SW) {
+      float mom[7];
+      chunk_scan<M, false>(tbase, 0, 128, n, b, chunk, a.n_chunks, a.consts, a.rec, a.flags,
+                           a.error, nullptr, 0, mom);
+      if (tid < M) {
+        float *dst = a.partial + (b * a.n_chunks + chunk) * 7 * M;
+#pragma unroll
+        for (int k = 0; k < 7; ++k) dst[k * M + tid] = mom[k];
+      }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tbase, P::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- moments finalize
+// moments[blk][b][k*M + m] = sum_chunks partial / count   (count T or T - lag; 0 if T <= lag)
+__global__ void fused_finalize_kernel(const float *__restrict__ wpart,
+                                      const float *__restrict__ rpart, float *__restrict__ wm,
+                                      float *__restrict__ rm, int64_t steps, int modes,
+                                      int64_t n_chunks) {
+  const int64_t b = blockIdx.x;
+  const float *part = blockIdx.y == 0 ? wpart : rpart;
+  float *out = blockIdx.y == 0 ? wm : rm;
+  const int lags[3] = {1, 2, 4};
+  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) {
+    const int kind = j / modes;
+    double acc = 0.0;
+    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)part[(b * n_chunks + c) * 7 * modes + j];
+    float v;
+    if (kind == 0) {
+      v = (float)(acc / (double)steps);
+    } else {
+      const int lag = lags[(kind - 1) / 2];
+      v = steps <= lag ? 0.f : (float)(acc / (double)(steps - lag));
+    }
+    out[b * 7 * modes + j] = v;
+  }
+}
+
+// ---------------------------------------------------------------- dispatch
+struct FusedShapeKey {
+  int C, D, M;
+};
+constexpr FusedShapeKey kFusedShapes[] = {{48, 96, 48}};
+
+inline bool fused_supported(const lnet_b200_alphabet_params *p,
+                            const lnet_b200_alphabet_request *r) {
+  if (r->time_delta || r->observation_mask || r->valid_mask) return false;
+  if (r->x_dtype != LNET_BF16 || r->act_dtype != LNET_BF16) return false;
+  if (p->conv_kernel != kTaps || p->conv_dilation != 4) return false;
+  if (r->steps < 1 || r->batch < 1) return false;
+  if (r->batch * fused_chunks(r->steps) >= (int64_t)1 << 31) return false;
+  for (const auto &s : kFusedShapes)
+    if (s.C == p->raw_input_dim && s.D == p->model_dim && s.M == p->modes) return true;
   return false;
 }
 
-inline int fused_forward(const lnet_b200_alphabet_params *, const lnet_b200_alphabet_request *,
-                         FusedWorkspace &, float *, float *, cudaStream_t) {
-  return fail(LNET_ERR_UNSUPPORTED, "fused route not built");
+int sm_count();
+
+template <int C, int D, int M>
+int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                        FusedWorkspace &w, float *wm, float *rm, cudaStream_t st) {
+  using WP = WriterPlan<C, D, M>;
+  using RP = ReaderPlan<D, M>;
+  const int64_t B = r->batch, T = r->steps, nch = fused_chunks(T);
+  const int sms = sm_count();
+  fused_prepare_kernel<<<64, 256, 0, st>>>(*p, w);
+  LNET_TRY(after_launch("fused_prepare_kernel"));
+  LNET_TRY(cuda_check(cudaMemsetAsync(w.flags, 0, w.flag_words * sizeof(uint32_t), st),
+                      "cudaMemsetAsync(flags)"));
+  uint32_t *counters = w.flags + 2 * B * nch;
+  FusedArgs wa{};
+  wa.in = (const __nv_bfloat16 *)r->x;
+  wa.B = B;
+  wa.T = T;
+  wa.n_chunks = nch;
+  wa.q = w.q;
+  wa.drive = w.wdrive;
+  wa.syn = w.wsyn;
+  wa.consts = w.consts;
+  wa.conv_b = p->stem_conv_bias;
+  wa.norm = p->writer_norm;
+  wa.ds = p->writer_direct_scale;
+  wa.ls = p->writer_layer_scale;
+  wa.out = w.stream;
+  wa.partial = w.wpartial;
+  wa.rec = w.wrec;
+  wa.flags = w.flags;
+  wa.counter = counters;
+  wa.error = counters + 2;
+  LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_writer_kernel<C, D, M>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, WP::BYTES),
+                      "cudaFuncSetAttribute(fused_writer_kernel)"));
+  const int64_t items = B * nch;
+  fused_writer_kernel<C, D, M><<<(unsigned)std::min<int64_t>(items, sms), kFusedThreads,
+                                 WP::BYTES, st>>>(wa);
+  LNET_TRY(after_launch("fused_writer_kernel"));
+  FusedArgs ra = wa;
+  ra.in = w.stream;
+  ra.drive = w.rdrive;
+  ra.syn = nullptr;
+  ra.consts = w.consts + 10 * M;
+  ra.conv_w = p->reader_conv_weight;
+  ra.conv_b = p->reader_conv_bias;
+  ra.norm = p->reader_norm;
+  ra.out = nullptr;
+  ra.partial = w.rpartial;
+  ra.rec = w.rrec;
+  ra.flags = w.flags + B * nch;
+  ra.counter = counters + 1;
+  LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_reader_kernel<D, M>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           RP::LAUNCH_BYTES),
+                      "cudaFuncSetAttribute(fused_reader_kernel)"));
+  fused_reader_kernel<D, M><<<(unsigned)std::min<int64_t>(items, 2 * (int64_t)sms),
+                              kFusedThreads, RP::LAUNCH_BYTES, st>>>(ra);
+  LNET_TRY(after_launch("fused_reader_kernel"));
+  fused_finalize_kernel<<<dim3((unsigned)B, 2), 256, 0, st>>>(w.wpartial, w.rpartial, wm, rm, T,
+                                                               M, nch);
+  return after_launch("fused_finalize_kernel");
+}
+
+inline int fused_forward(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                         FusedWorkspace &w, float *wm, float *rm, cudaStream_t st) {
+  if (p->raw_input_dim == 48 && p->model_dim == 96 && p->modes == 48)
+    return fused_forward_shape<48, 96, 48>(p, r, w, wm, rm, st);
+  return fail(LNET_ERR_UNSUPPORTED, "no fused kernel instance for C=%d D=%d M=%d",
+              p->raw_input_dim, p->model_dim, p->modes);
 }
 
 // Head without scratch: every block rebuilds the radial-log features of its

@@ -85,6 +85,10 @@ SIGNATURES = {
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
          _c_p, _c_p, _c_p, _c_p],
     ),
+    "lnet_b200_set_route": (ctypes.c_int, [ctypes.c_int]),
+    "lnet_b200_alphabet_route": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest)]
+    ),
     "lnet_b200_zoh": (ctypes.c_int, [_c_p, _c_p, _i32, _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "lnet_b200_stem": (
         ctypes.c_int,
@@ -190,3 +194,11 @@ def profile_read(max_entries: int = 64) -> dict[str, tuple[float, int]]:
     n = lib.lnet_b200_profile_read(buf, len(buf), ms, cnt, max_entries)
     names = buf.value.decode().split("\n")
     return {names[i]: (float(ms[i]), int(cnt[i])) for i in range(n)}
+
+
+ROUTE_AUTO = 0
+ROUTE_GENERAL = 1
+
+
+def set_route(route: int) -> None:
+    check(load().lnet_b200_set_route(int(route)), "lnet_b200_set_route")
