@@ -173,6 +173,24 @@ int lnet_b200_laplace_forward(const double *raw_decay, const double *residues,
                               const void *x, int64_t batch, int64_t steps, void *y,
                               void *workspace, size_t workspace_bytes, lnet_stream_t stream);
 
+/* Allocation-free variant of lnet_b200_laplace_forward for callers that may
+ * not allocate device memory (foreign memory pools, plugin hosts that forbid
+ * cudaMalloc, real-time loops).  Same arguments minus the workspace: the
+ * scratch lives in a fixed array inside the library (see
+ * lnet_b200_laplace_noalloc_max_scratch_bytes; every GPU that loads the
+ * library holds it until exit).  Shapes needing more scratch than that
+ * (lnet_b200_laplace_workspace_size) fail with LNET_ERR_WORKSPACE.  The first
+ * call on a device looks up the array's device address; make that first call
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU race.  No counterpart in the reference. */
+size_t lnet_b200_laplace_noalloc_max_scratch_bytes(void);
+int lnet_b200_laplace_forward_noalloc(const double *raw_decay, const double *residues,
+                                      const double *direct, const double *bias,
+                                      int32_t model_dim, int32_t modes, double dt,
+                                      double min_decay, int32_t x_dtype, const void *x,
+                                      int64_t batch, int64_t steps, void *y,
+                                      lnet_stream_t stream);
+
 /* Number of kernel launches the most recent successful lnet_b200_* call on
  * this thread enqueued. */
 int lnet_b200_last_launch_count(void);

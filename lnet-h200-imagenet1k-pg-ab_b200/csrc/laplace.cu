@@ -8,6 +8,8 @@
 // deterministic.  No state ever reaches HBM.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace lnet {
@@ -168,4 +170,84 @@ extern "C" int lnet_b200_laplace_forward(const double *raw_decay, const double *
     return laplace_run<float>(raw_decay, residues, direct, bias, model_dim, modes, dt, min_decay,
                               (const float *)x, batch, steps, (float *)y, (double *)workspace, st);
   return fail(LNET_ERR_UNSUPPORTED, "laplace: x dtype must be float32 or float64");
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory at all: code running inside a
+// memory pool it does not own, plugins whose host framework forbids
+// cudaMalloc on the calling thread, or tight real-time loops where an
+// allocation (and its implicit synchronisation) is not allowed.  For them,
+// lnet_b200_laplace_forward_noalloc keeps the per-slice partial outputs in
+// the fixed array below instead of a caller workspace.
+//
+// The array lives in the library image: every GPU that loads the library
+// holds kNoAllocScratchBytes of it until the process exits.  Every call on a
+// device shares it; calls whose kernels overlap on the GPU (different
+// streams, or different host threads without ordering) race on it.  The
+// slice kernel writes every partial it later reads, so nothing has to be
+// cleared between calls; the array keeps the last call's contents.
+namespace lnet {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) double g_noalloc_scratch[kNoAllocScratchBytes / sizeof(double)];
+
+// Device address of g_noalloc_scratch per device.  In host code the symbol
+// name is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and reused.
+constexpr int kMaxDevices = 64;
+static double *g_noalloc_ptr[kMaxDevices] = {};
+static std::mutex g_noalloc_mutex;
+
+static int noalloc_scratch(double **out) {
+  int dev = 0;
+  LNET_TRY(cuda_check(cudaGetDevice(&dev), "cudaGetDevice"));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LNET_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    LNET_TRY(cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                        "cudaGetSymbolAddress(g_noalloc_scratch)"));
+    g_noalloc_ptr[dev] = static_cast<double *>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return LNET_OK;
+}
+
+}  // namespace lnet
+
+extern "C" size_t lnet_b200_laplace_noalloc_max_scratch_bytes(void) {
+  return lnet::kNoAllocScratchBytes;
+}
+
+extern "C" int lnet_b200_laplace_forward_noalloc(const double *raw_decay, const double *residues,
+                                                 const double *direct, const double *bias,
+                                                 int32_t model_dim, int32_t modes, double dt,
+                                                 double min_decay, int32_t x_dtype,
+                                                 const void *x, int64_t batch, int64_t steps,
+                                                 void *y, lnet_stream_t stream) {
+  reset_launches();
+  if (model_dim < 1 || modes < 1 || batch < 0 || steps < 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "invalid laplace shape (D=%d, M=%d, B=%lld, T=%lld)",
+                model_dim, modes, (long long)batch, (long long)steps);
+  if (batch == 0 || steps == 0) return LNET_OK;
+  if (!raw_decay || !residues || !direct || !bias || !x || !y)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: NULL tensor pointer");
+  if (batch > 65535) return fail(LNET_ERR_UNSUPPORTED, "laplace: batch > 65535");
+  if (x_dtype != LNET_F64 && x_dtype != LNET_F32)
+    return fail(LNET_ERR_UNSUPPORTED, "laplace: x dtype must be float32 or float64");
+  size_t need = laplace_partial_bytes(batch, steps, model_dim, modes);
+  if (need > kNoAllocScratchBytes)
+    return fail(LNET_ERR_WORKSPACE,
+                "laplace (no-alloc): this shape needs %zu bytes of scratch but the built-in "
+                "array holds %zu; use lnet_b200_laplace_forward with a caller workspace",
+                need, kNoAllocScratchBytes);
+  double *scratch = nullptr;
+  LNET_TRY(noalloc_scratch(&scratch));
+  auto st = (cudaStream_t)stream;
+  begin_entry(st);
+  if (x_dtype == LNET_F64)
+    return laplace_run<double>(raw_decay, residues, direct, bias, model_dim, modes, dt, min_decay,
+                               (const double *)x, batch, steps, (double *)y, scratch, st);
+  return laplace_run<float>(raw_decay, residues, direct, bias, model_dim, modes, dt, min_decay,
+                            (const float *)x, batch, steps, (float *)y, scratch, st);
 }
