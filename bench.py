@@ -376,11 +376,21 @@ def run_b200(args, cfg):
     tokens_all = B * T * world * args.steps
     value = tokens_all / (total_ms / 1e3)
 
+    trace = None
+    if args.trace:
+        _lib.trace_enable(True)
+        fwd()
+        torch.cuda.synchronize()
+        raw = _lib.trace_read()
+        _lib.trace_enable(False)
+        trace = {k: {ph: round(c / max(v["items"], 1)) for ph, c in v.items() if ph != "items"}
+                 | {"items": v["items"]} for k, v in raw.items()}
     # ---- end to end through the public module API, host buffers, copies inside
     if args.skip_e2e:
         if rank == 0:
             print(json.dumps({"value": value, "ms_per_step": total_ms / args.steps,
-                              "kernels": _lib_kernels(prof)}), flush=True)
+                              "kernels": _lib_kernels(prof), "trace_cycles_per_item": trace}),
+                  flush=True)
         return 0
     x_host = x.cpu().pin_memory()
     x_dev = torch.empty_like(x)
@@ -473,6 +483,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override (small cases for profiling only)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
+    ap.add_argument("--trace", action="store_true",
+                    help="after the timed region, one traced forward: per-phase cycles per item")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")

@@ -206,6 +206,16 @@ void lnet_b200_profile_enable(int on);
 int lnet_b200_profile_read(char *names_buf, int names_bytes, float *total_ms, int *launches,
                            int max_entries);
 
+/* Per-phase cycle tracing of the fused kernels (off by default).  Counters
+ * are the clock64 cycles thread 0 of every CTA spends per phase, summed over
+ * CTAs; slots (writer row 0, reader row 1): 0 claim, 1 tile load, 2 first GEMM
+ * wait, 3 token epilogue, 4 drive GEMM wait, 5 scan, 6 synthesis wait,
+ * 7 residual epilogue, 10 scan pass 1, 11 look-back, 12 scan pass 2,
+ * 15 items.  No reference counterpart (the reference profiles with
+ * torch.profiler, src/lnet/pac_launch_tuning.py). */
+int lnet_b200_trace_enable(int on);
+int lnet_b200_trace_read(unsigned long long *out /* [2][16] */);
+
 /* Message of the last error on the calling thread ("" if none). */
 const char *lnet_b200_last_error(void);
 

@@ -12,14 +12,16 @@
 //        acc[t, d] = sum_k sum_c x[t + 4k - 8, c] * (w[d, k] P[d, c]),
 //      the five taps are five row-shifted descriptors over the same tile;
 //   3. +bias, SiLU, RMSNorm (thread per step), xhat -> bf16 slab;
-//   4. drive GEMM in mode-major orientation: TMEM lane m holds the complex
-//      drive u_m(t) of mode m over all 128 steps (gamma is folded into the
-//      frame), so the scan reads TMEM without any transpose;
-//   5. per-mode sequential scan from zero -> chunk aggregate (last 4 states)
-//      published; look-back over predecessors yields the carry-in; the
-//      inclusive record is published; second pass from the true carry
-//      accumulates E, C1, C2, C4 and writes the states (bf16) as the A operand
-//      of
+//   4. drive GEMM in mode-major orientation: the A operand repeats the mode
+//      rows every 64 lanes, so every TMEM lane quarter holds the complex drive
+//      u_m(t) of 32 modes over all 128 steps (gamma is folded into the frame)
+//      and every warp can scan without a transpose;
+//   5. scan: each mode's 128 steps are cut into four sub-chunks of 32 scanned
+//      by four threads (one per warp pair); sub-chunk end states combine in
+//      shared memory into the chunk aggregate, which the last sub-chunk's warps
+//      publish and then resolve against their predecessors (decoupled
+//      look-back); a second pass from the true carries accumulates E, C1, C2,
+//      C4 and writes the states (bf16) as the A operand of
 //   6. the synthesis GEMM (token-major) and the residual epilogue
 //      v = x + ls (s W^T + ds xhat), stored as bf16.
 // fused_reader_kernel: the same skeleton on the writer stream: conv of the
@@ -37,6 +39,7 @@
 namespace lnet {
 
 constexpr int kChunk = 128;
+constexpr int kSub = 32;  // steps per scan sub-chunk (kChunk / 4)
 constexpr int kHalo = 8;
 constexpr int kTaps = 5;
 constexpr int kXRows = kChunk + 2 * kHalo;
@@ -45,16 +48,22 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kFlagAgg = 1, kFlagIncl = 2;
 constexpr uint32_t kErrMbar = 1, kErrLookback = 2;
 
+// Per-block pole constants (floats, M entries each):
+//   [0] a_re, [1] a_im, [2 + 2i] / [3 + 2i]  re/im of a^(128 - i),
+//   [10 + 2i] / [11 + 2i] re/im of a^(32 - i)  (i = 0..3), [18]/[19] a^64, [20]/[21] a^96.
+constexpr int kConsts = 22;
+constexpr int KC_AL = 2, KC_AS = 10, KC_A64 = 18, KC_A96 = 20;
+
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
 // ---------------------------------------------------------------- workspace
 struct FusedWorkspace {
   float *moments = nullptr;            // [2][B][7M]
   __nv_bfloat16 *q = nullptr;          // stem B operand   [5][C/8][D][8]
-  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][M][8]
-  __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][M][8]
+  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][128][8]
+  __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][128][8]
   __nv_bfloat16 *wsyn = nullptr;       // synthesis B      [2M/8][D][8]
-  float *consts = nullptr;             // [2][10M]: a_re, a_im, a^(L-i) re/im (i = 0..3)
+  float *consts = nullptr;             // [2][kConsts * M]
   __nv_bfloat16 *stream = nullptr;     // [B, T, D]
   float *wpartial = nullptr;           // [B * nch][7M]
   float *rpartial = nullptr;
@@ -72,10 +81,10 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   const int64_t B = r->batch, nch = fused_chunks(std::max<int64_t>(r->steps, 1));
   w.moments = ar.take<float>((size_t)2 * B * 7 * M);
   w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
-  w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * M);
-  w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * M);
+  w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
+  w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
   w.wsyn = ar.take<__nv_bfloat16>((size_t)2 * M * D);
-  w.consts = ar.take<float>((size_t)2 * 10 * M);
+  w.consts = ar.take<float>((size_t)2 * kConsts * M);
   w.stream = ar.take<__nv_bfloat16>((size_t)B * r->steps * D);
   w.wpartial = ar.take<float>((size_t)B * nch * 7 * M);
   w.rpartial = ar.take<float>((size_t)B * nch * 7 * M);
@@ -98,7 +107,7 @@ __device__ __forceinline__ void cmul_d(double ar, double ai, double br, double b
 __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace w) {
   const int C = p.raw_input_dim, D = p.model_dim, M = p.modes, K5 = p.conv_kernel;
   const int64_t n_q = (int64_t)kTaps * C * D;
-  const int64_t n_drive = (int64_t)2 * D * M;
+  const int64_t n_drive = (int64_t)2 * D * 128;  // per block: re/im x D x 128 lanes
   const int64_t n_syn = (int64_t)2 * M * D;
   const int64_t total = n_q + 2 * n_drive + n_syn + 2 * M;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -112,23 +121,27 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
       continue;
     }
     int64_t j = i - n_q;
-    if (j < 2 * n_drive) {  // drive A rows = modes, K = d; gamma folded in
+    if (j < 2 * n_drive) {  // drive A: lane r holds mode r % 64 (zero if >= M), K = d
       int blk = (int)(j / n_drive);
       int64_t rem = j - blk * n_drive;
-      int part = (int)(rem / ((int64_t)D * M));
-      int rem2 = (int)(rem - (int64_t)part * D * M);
-      int d = rem2 / M, m = rem2 - d * M;
-      const float *frame = blk == 0 ? p.writer_frame : p.reader_frame;
-      double damping, frequency;
-      mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
-                blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
-                frequency);
-      Zoh z = zoh_eval(damping, frequency, 1.0);
-      double fr = frame[d * 2 * M + m], fi = frame[d * 2 * M + M + m];
-      double v = part == 0 ? (double)z.g_re * fr - (double)z.g_im * fi
-                           : (double)z.g_re * fi + (double)z.g_im * fr;
+      int part = (int)(rem / ((int64_t)D * 128));
+      int rem2 = (int)(rem - (int64_t)part * D * 128);
+      int d = rem2 / 128, r = rem2 - d * 128;
+      int m = r % 64;
+      float out = 0.f;
+      if (m < M) {
+        const float *frame = blk == 0 ? p.writer_frame : p.reader_frame;
+        double damping, frequency;
+        mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
+                  blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
+                  frequency);
+        Zoh z = zoh_eval(damping, frequency, 1.0);
+        double fr = frame[d * 2 * M + m], fi = frame[d * 2 * M + M + m];
+        out = (float)(part == 0 ? (double)z.g_re * fr - (double)z.g_im * fi
+                                : (double)z.g_re * fi + (double)z.g_im * fr);
+      }
       __nv_bfloat16 *dst = blk == 0 ? w.wdrive : w.rdrive;
-      dst[(int64_t)part * D * M + ((d / 8) * M + m) * 8 + (d % 8)] = __float2bfloat16_rn((float)v);
+      dst[(int64_t)part * D * 128 + ((d / 8) * 128 + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
       continue;
     }
     j -= 2 * n_drive;
@@ -144,20 +157,24 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
               blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
               frequency);
     Zoh z = zoh_eval(damping, frequency, 1.0);
-    // a^(L - i), i = 0..3: powers of the fp32 coefficient the scan multiplies by,
-    // accumulated in double so that carries match step-by-step propagation.
+    // Powers of the fp32 coefficient the scan multiplies by, accumulated in
+    // double so that carries match step-by-step propagation.
     const double ar = (double)z.a_re, ai = (double)z.a_im;
     double pr = 1.0, pi = 0.0;
-    float *k = w.consts + blk * 10 * M;
+    float *k = w.consts + (int64_t)blk * kConsts * M;
     for (int step = 1; step <= kChunk; ++step) {
       double nr, ni;
       cmul_d(pr, pi, ar, ai, nr, ni);
       pr = nr;
       pi = ni;
-      int idx = kChunk - step;  // step == L - idx
-      if (idx < 4) {
-        k[2 * M + 2 * idx * M + m] = (float)pr;
-        k[2 * M + (2 * idx + 1) * M + m] = (float)pi;
+      int slot = -1;
+      if (step >= kChunk - 3) slot = KC_AL + 2 * (kChunk - step);
+      else if (step >= kSub - 3 && step <= kSub) slot = KC_AS + 2 * (kSub - step);
+      else if (step == 64) slot = KC_A64;
+      else if (step == 96) slot = KC_A96;
+      if (slot >= 0) {
+        k[slot * M + m] = (float)pr;
+        k[(slot + 1) * M + m] = (float)pi;
       }
     }
     k[m] = z.a_re;
@@ -166,10 +183,16 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
 }
 
 // ---------------------------------------------------------------- shared-memory plans
+// Scan scratch (floats): sub-chunk end states [4][2][64], last-four states
+// [4][8][64], carry block [8][64] (true last four states of the previous
+// chunk), moment sums [4][7][64].
+constexpr int kScanEnd = 0, kScanLast = 512, kScanCarry = 2560, kScanMom = 3072;
+constexpr int kScanFloats = 3072 + 4 * 7 * 64;
+
 template <int C, int D, int M>
 struct WriterPlan {
-  static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 128 && D <= 256, "shape");
-  static constexpr int SLAB_AD = M * 16;
+  static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
+  static constexpr int SLAB_AD = 128 * 16;
   static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
   static constexpr int SLAB_Q = D * 16;
   static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
@@ -184,38 +207,42 @@ struct WriterPlan {
   static constexpr int SLAB_S = kChunk * 16 + 16;
   static constexpr int S_BYTES = (2 * M / 8) * SLAB_S;
   static constexpr int XS_BYTES = cmax(XH_BYTES, S_BYTES);
-  static constexpr int OFF_AD = 0;  // UMMA reads 128 rows of each drive slab: the tail
-  static constexpr int OFF_Q = OFF_AD + AD_BYTES;  // past the M real rows lands in Q
+  static constexpr int OFF_AD = 0;
+  static constexpr int OFF_Q = OFF_AD + AD_BYTES;
   static constexpr int OFF_WS = OFF_Q + Q_BYTES;
   static constexpr int OFF_XF = OFF_WS + WS_BYTES;
   static constexpr int OFF_XS = OFF_XF + XF_BYTES;
-  static constexpr int OFF_RED = OFF_XS + XS_BYTES;          // float [2][128]
-  static constexpr int OFF_RS = OFF_RED + 2 * kChunk * 4;    // float [128]
-  static constexpr int OFF_MISC = OFF_RS + kChunk * 4;       // mbar, tmem base, item
+  static constexpr int OFF_SCAN = OFF_XS + XS_BYTES;              // float [kScanFloats]
+  static constexpr int OFF_PAR = OFF_SCAN + kScanFloats * 4;      // float [4][D]: bias, g, ds, ls
+  static constexpr int OFF_K = OFF_PAR + 4 * D * 4;               // float [kConsts * M]
+  static constexpr int OFF_RED = OFF_K + kConsts * M * 4;         // float [2][128]
+  static constexpr int OFF_RS = OFF_RED + 2 * kChunk * 4;         // float [128]
+  static constexpr int OFF_MISC = OFF_RS + kChunk * 4;            // mbar, tmem base, item
   static constexpr int BYTES = OFF_MISC + 64;
   static constexpr int TMEM_COLS = 512;  // [0,128) stem/synthesis acc, [128,256) u re, [256,384) u im
-  static_assert(Q_BYTES >= (kChunk - M) * 16, "drive-operand tail must stay inside the stem slabs");
 };
 
 template <int D, int M>
 struct ReaderPlan {
-  static_assert(D % 32 == 0 && M % 8 == 0 && M <= 128 && D <= 256, "shape");
-  static constexpr int SLAB_AD = M * 16;
+  static_assert(D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
+  static constexpr int SLAB_AD = 128 * 16;
   static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
   static constexpr int PITCH = D * 2 + 16;  // stream tile row pitch (bank-conflict free)
-  static constexpr int V_BYTES = kXRows * PITCH;
+  static constexpr int V_BYTES = cmax(kXRows * PITCH, kScanFloats * 4);  // tile, then scan scratch
   static constexpr int SLAB_XH = kChunk * 16;
   static constexpr int XH_BYTES = (D / 8) * SLAB_XH;
   static constexpr int OFF_AD = 0;
-  static constexpr int OFF_V = OFF_AD + AD_BYTES;  // drive-operand tail lands in the tile
+  static constexpr int OFF_V = OFF_AD + AD_BYTES;
   static constexpr int OFF_XH = OFF_V + V_BYTES;
-  static constexpr int OFF_RED = OFF_XH + XH_BYTES;
+  static constexpr int OFF_PAR = OFF_XH + XH_BYTES;               // float [7][D]: w(5), bias, g
+  static constexpr int OFF_K = OFF_PAR + 7 * D * 4;
+  static constexpr int OFF_RED = OFF_K + kConsts * M * 4;
   static constexpr int OFF_MISC = OFF_RED + 2 * kChunk * 4;
   static constexpr int BYTES = OFF_MISC + 64;
   // at most two CTAs per SM so that two 256-column TMEM allocations always fit
   static constexpr int LAUNCH_BYTES = cmax(BYTES, 100 * 1024);
   static constexpr int TMEM_COLS = 256;  // [0,128) u re, [128,256) u im
-  static_assert(V_BYTES >= (kChunk - M) * 16, "drive-operand tail must stay inside the tile");
+  static_assert(2 * (LAUNCH_BYTES + 1024) <= 228 * 1024, "two reader CTAs must fit one SM");
 };
 
 struct FusedArgs {
@@ -223,7 +250,7 @@ struct FusedArgs {
   int64_t B, T;
   int64_t n_chunks;
   const __nv_bfloat16 *q, *drive, *syn;
-  const float *consts;      // 10M floats of this block
+  const float *consts;      // kConsts * M floats of this block
   const float *conv_w, *conv_b, *norm, *ds, *ls;
   __nv_bfloat16 *out;       // writer stream
   float *partial;           // [B * nch][7M]
@@ -231,7 +258,24 @@ struct FusedArgs {
   uint32_t *flags;          // [B * nch]
   uint32_t *counter;
   uint32_t *error;
+  int trace;       // 1: accumulate per-phase cycles of CTA thread 0 into g_fused_trace
+  int kernel_id;   // 0 writer, 1 reader
 };
+
+// Per-phase cycle totals of thread 0 of every CTA (tracing; off by default).
+// Slots: 0 claim, 1 tile load, 2 first GEMM wait, 3 token epilogue, 4 drive GEMM
+// wait, 5 scan (whole), 6 synthesis wait, 7 residual epilogue, 10 scan pass 1,
+// 11 look-back, 12 scan pass 2, 15 items processed.
+static __device__ unsigned long long g_fused_trace[2][16];
+
+#define LNET_TRACE(slot)                                                        \
+  do {                                                                          \
+    if (a.trace && threadIdx.x == 0) {                                          \
+      unsigned long long _now = clock64();                                      \
+      atomicAdd(&g_fused_trace[a.kernel_id][slot], _now - t_last);              \
+      t_last = _now;                                                            \
+    }                                                                           \
+  } while (0)
 
 // 16-byte copy of prepared operands into shared memory.
 __device__ __forceinline__ void copy_smem(void *dst, const void *src, int bytes) {
@@ -239,187 +283,287 @@ __device__ __forceinline__ void copy_smem(void *dst, const void *src, int bytes)
   uint4 *d = reinterpret_cast<uint4 *>(dst);
   for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = __ldg(s + i);
 }
+__device__ __forceinline__ void copy_floats(float *dst, const float *src, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// SiLU with the hardware exponential (relative error ~1e-6, far inside the
+// bf16 activation rounding of this route).
+__device__ __forceinline__ float silu_fast(float v) { return v * __frcp_rn(1.0f + __expf(-v)); }
+
+__device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, float &cr,
+                                     float &ci) {  // c += a * b
+  cr = fmaf(ar, br, fmaf(-ai, bi, cr));
+  ci = fmaf(ar, bi, fmaf(ai, br, ci));
+}
+
+// Waits for the look-back flag of record `idx` to reach at least AGG; returns it (0 on timeout).
+__device__ __forceinline__ uint32_t wait_flag(const uint32_t *flags, int64_t idx) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    uint32_t st = sm100::ld_acquire(flags + idx);
+    if (st >= kFlagAgg) return st;
+    __nanosleep(32);
+  }
+  return 0;
+}
+
 // ---------------------------------------------------------------- scan + look-back
-// Executed by the first SW = ceil(M/32) warps; thread tid owns mode tid (if < M).
-// u_re / u_im live in TMEM columns [col_re, col_re + 128) / [col_im, ...) of the
-// thread's own lane.  Returns the moment partial sums of this chunk in mom[7].
+// Executed by all 256 threads.  Warp w reads TMEM lane quarter w % 4: modes
+// m = 32 * (w % 2) + lane (live if m < M) of sub-chunk q = (w % 4) / 2 + 2 * (w / 4),
+// steps [32 q, 32 q + 32).  u_re / u_im of the chunk live in TMEM columns
+// [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's moment partial
+// sums [7][M] to `partial`.
 template <int M, bool WRITE_STATES>
 __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_im, int n,
                                            int64_t row, int64_t chunk, int64_t n_chunks,
-                                           const float *consts, float *rec, uint32_t *flags,
+                                           const float *K, float *rec, uint32_t *flags,
                                            uint32_t *error, uint8_t *s_slab, int slab_s,
-                                           float *mom) {
-  constexpr int SW = (M + 31) / 32;
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const bool live = tid < M;
-  const int m = live ? tid : 0;
-  const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
-  const float ar = consts[m], ai = consts[M + m];
-  // ---- pass 1: chunk-local scan from zero
+                                           float *sc, float *partial, int trace, int kid) {
+  unsigned long long t_scan = trace ? clock64() : 0;
+  auto mark = [&](int slot) {
+    if (trace && threadIdx.x == 0) {
+      unsigned long long now = clock64();
+      atomicAdd(&g_fused_trace[kid][slot], now - t_scan);
+      t_scan = now;
+    }
+  };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Q = warp & 3;
+  const int q = (Q >> 1) + 2 * (warp >> 2);
+  const int m = 32 * (Q & 1) + lane;
+  const bool live = m < M;
+  const int mk = live ? m : 0;
+  const uint32_t lane_addr = tbase + ((uint32_t)(32 * Q) << 16);
+  const int s0 = kSub * q;
+  const int len = max(0, min(kSub, n - s0));
+  const float ar = K[mk], ai = K[M + mk];
+
+  // ---- pass 1: sub-chunk local scan from zero
+  float ur[kSub], ui[kSub];
+  if (len > 0) {
+    sm100::tmem_ld16(lane_addr + col_re + s0, ur);
+    sm100::tmem_ld16(lane_addr + col_im + s0, ui);
+    sm100::tmem_ld16(lane_addr + col_re + s0 + 16, ur + 16);
+    sm100::tmem_ld16(lane_addr + col_im + s0 + 16, ui + 16);
+    sm100::tmem_ld_wait();
+  }
   float sr = 0.f, si = 0.f;
   float l_r[4] = {0, 0, 0, 0}, l_i[4] = {0, 0, 0, 0};  // l[0] = last state
-  for (int c0 = 0; c0 < n; c0 += 16) {
-    float ur[16], ui[16];
-    sm100::tmem_ld16(lane_addr + col_re + c0, ur);
-    sm100::tmem_ld16(lane_addr + col_im + c0, ui);
-    sm100::tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (c0 + i < n) {
-        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
-        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
-        sr = nr;
-        si = ni;
-        l_r[3] = l_r[2]; l_i[3] = l_i[2];
-        l_r[2] = l_r[1]; l_i[2] = l_i[1];
-        l_r[1] = l_r[0]; l_i[1] = l_i[0];
-        l_r[0] = sr; l_i[0] = si;
-      }
+  for (int i = 0; i < kSub; ++i) {
+    if (i < len) {
+      float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
+      float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
+      sr = nr;
+      si = ni;
+      l_r[3] = l_r[2]; l_i[3] = l_i[2];
+      l_r[2] = l_r[1]; l_i[2] = l_i[1];
+      l_r[1] = l_r[0]; l_i[1] = l_i[0];
+      l_r[0] = sr; l_i[0] = si;
     }
   }
-  const int64_t item = row * n_chunks + chunk;  // record index (row-major)
-  float *my = rec + item * 16 * M;
   if (live) {
+    sc[kScanEnd + (2 * q) * 64 + m] = sr;
+    sc[kScanEnd + (2 * q + 1) * 64 + m] = si;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      my[(2 * i) * M + m] = l_r[i];
-      my[(2 * i + 1) * M + m] = l_i[i];
-    }
-    __threadfence();
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(SW * 32) : "memory");
-  if (tid == 0) sm100::st_release(flags + item, kFlagAgg);
-  // ---- look-back: true states at the last four steps of the previous chunk
-  float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
-  if (chunk > 0) {
-    const int64_t prev = item - 1;
-    uint32_t st = 0;
-    for (uint32_t it = 0; it < kSpinLimit; ++it) {
-      st = sm100::ld_acquire(flags + prev);
-      if (st >= kFlagAgg) break;
-      __nanosleep(40);
-    }
-    if (st < kFlagAgg) {
-      if (tid == 0) atomicOr(error, kErrLookback);
-    } else if (st == kFlagIncl) {
-      const float *pr = rec + prev * 16 * M + 8 * M;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        p_r[i] = __ldcg(pr + (2 * i) * M + m);
-        p_i[i] = __ldcg(pr + (2 * i + 1) * M + m);
-      }
-    } else {
-      // X = true end state of chunk - 2, composed from aggregates back to an
-      // inclusive record (or the sequence start).
-      const float aLr = consts[2 * M + m], aLi = consts[3 * M + m];
-      float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
-      for (int64_t q = chunk - 2; q >= 0; --q) {
-        const int64_t qi = row * n_chunks + q;
-        uint32_t sq = 0;
-        for (uint32_t it = 0; it < kSpinLimit; ++it) {
-          sq = sm100::ld_acquire(flags + qi);
-          if (sq >= kFlagAgg) break;
-          __nanosleep(40);
-        }
-        if (sq < kFlagAgg) {
-          if (tid == 0) atomicOr(error, kErrLookback);
-          break;
-        }
-        const float *qr = rec + qi * 16 * M + (sq == kFlagIncl ? 8 * M : 0);
-        float er = __ldcg(qr + m), ei = __ldcg(qr + M + m);
-        xr = fmaf(mr, er, fmaf(-mi, ei, xr));
-        xi = fmaf(mr, ei, fmaf(mi, er, xi));
-        if (sq == kFlagIncl) break;
-        float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
-        mr = nr;
-        mi = ni;
-      }
-      const float *pa = rec + prev * 16 * M;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float gr = consts[2 * M + 2 * i * M + m], gi = consts[2 * M + (2 * i + 1) * M + m];
-        float lr = __ldcg(pa + (2 * i) * M + m), li = __ldcg(pa + (2 * i + 1) * M + m);
-        p_r[i] = lr + (gr * xr - gi * xi);
-        p_i[i] = li + (gr * xi + gi * xr);
-      }
+    for (int k = 0; k < 4; ++k) {
+      sc[kScanLast + (8 * q + 2 * k) * 64 + m] = l_r[k];
+      sc[kScanLast + (8 * q + 2 * k + 1) * 64 + m] = l_i[k];
     }
   }
-  // inclusive record of this chunk (only consumed when the chunk is full)
-  if (live) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float gr = consts[2 * M + 2 * i * M + m], gi = consts[2 * M + (2 * i + 1) * M + m];
-      my[8 * M + (2 * i) * M + m] = l_r[i] + (gr * p_r[0] - gi * p_i[0]);
-      my[8 * M + (2 * i + 1) * M + m] = l_i[i] + (gr * p_i[0] + gi * p_r[0]);
-    }
-    __threadfence();
+  __syncthreads();
+  mark(10);
+  // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^32 c_j + e_j
+  const float a32r = K[(KC_AS + 0) * M + mk], a32i = K[(KC_AS + 1) * M + mk];
+  float cr = 0.f, ci = 0.f, cpr = 0.f, cpi = 0.f;  // c_q and c_{q-1}
+  for (int j = 0; j < q; ++j) {
+    cpr = cr;
+    cpi = ci;
+    float nr = sc[kScanEnd + (2 * j) * 64 + mk], ni = sc[kScanEnd + (2 * j + 1) * 64 + mk];
+    cmac(a32r, a32i, cr, ci, nr, ni);
+    cr = nr;
+    ci = ni;
   }
-  asm volatile("bar.sync 1, %0;" ::"r"(SW * 32) : "memory");
-  if (tid == 0) sm100::st_release(flags + item, kFlagIncl);
-  // ---- pass 2: true states, moments, states for the synthesis GEMM
-  const bool hist = chunk > 0;
-  float h1r = p_r[0], h1i = p_i[0], h2r = p_r[1], h2i = p_i[1];
-  float h3r = p_r[2], h3i = p_i[2], h4r = p_r[3], h4i = p_i[3];
-  sr = p_r[0];
-  si = p_i[0];
-  float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
-  for (int c0 = 0; c0 < n; c0 += 16) {
-    float ur[16], ui[16];
-    sm100::tmem_ld16(lane_addr + col_re + c0, ur);
-    sm100::tmem_ld16(lane_addr + col_im + c0, ui);
-    sm100::tmem_ld_wait();
+
+  // ---- aggregate, look-back and inclusive record: sub-chunk 3 (warps 6 and 7)
+  if (q == 3) {
+    const int64_t item = row * n_chunks + chunk;  // record index (row-major)
+    float *my = rec + item * 16 * M;
+    float g_r[4], g_i[4];  // chunk-local last four states
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int t = c0 + i;
-      if (t < n) {
-        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
-        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
-        sr = nr;
-        si = ni;
-        e = fmaf(sr, sr, fmaf(si, si, e));
-        if (hist || t >= 1) {
-          c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
-          c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
+    for (int k = 0; k < 4; ++k) {
+      const float pr = K[(KC_AS + 2 * k) * M + mk], pi = K[(KC_AS + 2 * k + 1) * M + mk];
+      g_r[k] = l_r[k];
+      g_i[k] = l_i[k];
+      cmac(pr, pi, cr, ci, g_r[k], g_i[k]);
+    }
+    if (live) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        my[(2 * k) * M + m] = g_r[k];
+        my[(2 * k + 1) * M + m] = g_i[k];
+      }
+      __threadfence();
+    }
+    asm volatile("bar.sync 1, 64;" ::: "memory");
+    if (tid == 192) sm100::st_release(flags + item, kFlagAgg);
+    float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
+    if (chunk > 0) {
+      const int64_t prev = item - 1;
+      const uint32_t st = wait_flag(flags, prev);
+      if (st == 0) {
+        if (tid == 192) atomicOr(error, kErrLookback);
+      } else if (st == kFlagIncl) {
+        const float *pr = rec + prev * 16 * M + 8 * M;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          p_r[k] = __ldcg(pr + (2 * k) * M + mk);
+          p_i[k] = __ldcg(pr + (2 * k + 1) * M + mk);
         }
-        if (hist || t >= 2) {
-          c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
-          c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
-        }
-        if (hist || t >= 4) {
-          c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
-          c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
-        }
-        h4r = h3r; h4i = h3i;
-        h3r = h2r; h3i = h2i;
-        h2r = h1r; h2i = h1i;
-        h1r = sr; h1i = si;
-        if constexpr (WRITE_STATES) {
-          if (live) {
-            __nv_bfloat16 *pr_ = reinterpret_cast<__nv_bfloat16 *>(
-                s_slab + (m / 8) * slab_s + t * 16 + (m % 8) * 2);
-            __nv_bfloat16 *pi_ = reinterpret_cast<__nv_bfloat16 *>(
-                s_slab + ((M + m) / 8) * slab_s + t * 16 + ((M + m) % 8) * 2);
-            *pr_ = __float2bfloat16_rn(sr);
-            *pi_ = __float2bfloat16_rn(si);
+      } else {
+        // X = true end state of chunk - 2, composed from aggregates back to an
+        // inclusive record (or the sequence start).
+        const float aLr = K[KC_AL * M + mk], aLi = K[(KC_AL + 1) * M + mk];
+        float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
+        for (int64_t qq = chunk - 2; qq >= 0; --qq) {
+          const int64_t qi = row * n_chunks + qq;
+          const uint32_t sq = wait_flag(flags, qi);
+          if (sq == 0) {
+            if (tid == 192) atomicOr(error, kErrLookback);
+            break;
           }
+          const float *qr = rec + qi * 16 * M + (sq == kFlagIncl ? 8 * M : 0);
+          cmac(mr, mi, __ldcg(qr + mk), __ldcg(qr + M + mk), xr, xi);
+          if (sq == kFlagIncl) break;
+          float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
+          mr = nr;
+          mi = ni;
+        }
+        const float *pa = rec + prev * 16 * M;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          p_r[k] = __ldcg(pa + (2 * k) * M + mk);
+          p_i[k] = __ldcg(pa + (2 * k + 1) * M + mk);
+          cmac(K[(KC_AL + 2 * k) * M + mk], K[(KC_AL + 2 * k + 1) * M + mk], xr, xi, p_r[k],
+               p_i[k]);
+        }
+      }
+    }
+    if (live) {
+      // inclusive record (only consumed when the chunk is full)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float vr = g_r[k], vi = g_i[k];
+        cmac(K[(KC_AL + 2 * k) * M + mk], K[(KC_AL + 2 * k + 1) * M + mk], p_r[0], p_i[0], vr,
+             vi);
+        my[8 * M + (2 * k) * M + m] = vr;
+        my[8 * M + (2 * k + 1) * M + m] = vi;
+      }
+      __threadfence();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        sc[kScanCarry + (2 * k) * 64 + m] = p_r[k];
+        sc[kScanCarry + (2 * k + 1) * 64 + m] = p_i[k];
+      }
+    }
+    asm volatile("bar.sync 1, 64;" ::: "memory");
+    if (tid == 192) sm100::st_release(flags + item, kFlagIncl);
+  }
+  __syncthreads();
+  mark(11);
+
+  // ---- pass 2 from the true state before this sub-chunk
+  const float car = sc[kScanCarry + mk], cai = sc[kScanCarry + 64 + mk];
+  // a^(32 q) and a^(32 (q - 1))
+  float pqr = 1.f, pqi = 0.f, pq1r = 1.f, pq1i = 0.f;
+  if (q == 1) { pqr = a32r; pqi = a32i; }
+  if (q == 2) { pqr = K[KC_A64 * M + mk]; pqi = K[(KC_A64 + 1) * M + mk]; pq1r = a32r; pq1i = a32i; }
+  if (q == 3) {
+    pqr = K[KC_A96 * M + mk]; pqi = K[(KC_A96 + 1) * M + mk];
+    pq1r = K[KC_A64 * M + mk]; pq1i = K[(KC_A64 + 1) * M + mk];
+  }
+  float h_r[4], h_i[4];  // true states at the four steps before this sub-chunk
+  if (q == 0) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      h_r[k] = sc[kScanCarry + (2 * k) * 64 + mk];
+      h_i[k] = sc[kScanCarry + (2 * k + 1) * 64 + mk];
+    }
+  } else {
+    float ipr = cpr, ipi = cpi;  // true state before sub-chunk q - 1
+    cmac(pq1r, pq1i, car, cai, ipr, ipi);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      h_r[k] = sc[kScanLast + (8 * (q - 1) + 2 * k) * 64 + mk];
+      h_i[k] = sc[kScanLast + (8 * (q - 1) + 2 * k + 1) * 64 + mk];
+      cmac(K[(KC_AS + 2 * k) * M + mk], K[(KC_AS + 2 * k + 1) * M + mk], ipr, ipi, h_r[k],
+           h_i[k]);
+    }
+  }
+  sr = cr;
+  si = ci;
+  cmac(pqr, pqi, car, cai, sr, si);
+  const bool hist = chunk > 0 || q > 0;
+  float h1r = h_r[0], h1i = h_i[0], h2r = h_r[1], h2i = h_i[1];
+  float h3r = h_r[2], h3i = h_i[2], h4r = h_r[3], h4i = h_i[3];
+  float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    if (i < len) {
+      float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
+      float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
+      sr = nr;
+      si = ni;
+      e = fmaf(sr, sr, fmaf(si, si, e));
+      if (hist || i >= 1) {
+        c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
+        c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
+      }
+      if (hist || i >= 2) {
+        c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
+        c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
+      }
+      if (hist || i >= 4) {
+        c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
+        c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
+      }
+      h4r = h3r; h4i = h3i;
+      h3r = h2r; h3i = h2i;
+      h2r = h1r; h2i = h1i;
+      h1r = sr; h1i = si;
+      if constexpr (WRITE_STATES) {
+        if (live) {
+          const int t = s0 + i;
+          *reinterpret_cast<__nv_bfloat16 *>(s_slab + (m / 8) * slab_s + t * 16 + (m % 8) * 2) =
+              __float2bfloat16_rn(sr);
+          *reinterpret_cast<__nv_bfloat16 *>(s_slab + ((M + m) / 8) * slab_s + t * 16 +
+                                             ((M + m) % 8) * 2) = __float2bfloat16_rn(si);
         }
       }
     }
   }
-  mom[0] = e;
-  mom[1] = c1r;
-  mom[2] = c1i;
-  mom[3] = c2r;
-  mom[4] = c2i;
-  mom[5] = c4r;
-  mom[6] = c4i;
+  mark(12);
+  if (live) {
+    float *mo = sc + kScanMom + q * 7 * 64 + m;
+    mo[0] = e;
+    mo[64] = c1r;
+    mo[128] = c1i;
+    mo[192] = c2r;
+    mo[256] = c2i;
+    mo[320] = c4r;
+    mo[384] = c4i;
+  }
+  __syncthreads();
+  for (int j = tid; j < 7 * M; j += kFusedThreads) {
+    const int k = j / M, mm = j - (j / M) * M;
+    const float *mo = sc + kScanMom + k * 64 + mm;
+    partial[j] = mo[0] + mo[7 * 64] + mo[14 * 64] + mo[21 * 64];
+  }
 }
 
 // Issues one GEMM: `ksteps` K=16 steps of D[tmem] (+)= A * B^T.
@@ -451,6 +595,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
   int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);
   float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
   float *rs_s = reinterpret_cast<float *>(smem + P::OFF_RS);
+  float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
+  const float *s_bias = par, *s_norm = par + D, *s_ds = par + 2 * D, *s_ls = par + 3 * D;
+  float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
+  float *s_scan = reinterpret_cast<float *>(smem + P::OFF_SCAN);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t s_base = sm100::smem_u32(smem);
 
@@ -465,6 +613,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
   copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
   copy_smem(smem + P::OFF_Q, a.q, P::Q_BYTES);
   copy_smem(smem + P::OFF_WS, a.syn, P::WS_BYTES);
+  copy_floats(par, a.conv_b, D);
+  copy_floats(par + D, a.norm, D);
+  copy_floats(par + 2 * D, a.ds, D);
+  copy_floats(par + 3 * D, a.ls, D);
+  copy_floats(s_k, a.consts, kConsts * M);
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
@@ -477,11 +630,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
   const int64_t total = a.B * a.n_chunks;
 
+  unsigned long long t_last = clock64();
   for (;;) {
     if (tid == 0) *item_slot = (int64_t)atomicAdd(a.counter, 1u);
     __syncthreads();
     const int64_t item = *item_slot;
     if (item >= total) break;
+    LNET_TRACE(0);
     const int64_t chunk = item / a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
@@ -497,6 +652,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
     }
     sm100::fence_proxy_async_smem();
     __syncthreads();
+    LNET_TRACE(1);
     // 2. stem GEMM: five row-shifted views of the tile
     if (tid == 0) {
       sm100::tc_fence_after();
@@ -507,6 +663,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
       sm100::mma_commit(mbar);
     }
     wait_mma(mbar, phase, a.error);
+    LNET_TRACE(2);
     // 3. bias + SiLU + RMSNorm (thread per step, two column halves)
     float f[HD];
 #pragma unroll
@@ -515,7 +672,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < HD; ++i) {
-      f[i] = silu_f(f[i] + __ldg(a.conv_b + half * HD + i));
+      f[i] = silu_fast(f[i] + s_bias[half * HD + i]);
       ss = fmaf(f[i], f[i], ss);
     }
     red[half * kChunk + row] = ss;
@@ -528,7 +685,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
       uint4 xh, fl;
       float h[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * __ldg(a.norm + d0 + i);
+      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * s_norm[d0 + i];
       xh.x = pack_bf16x2(h[0], h[1]);
       xh.y = pack_bf16x2(h[2], h[3]);
       xh.z = pack_bf16x2(h[4], h[5]);
@@ -543,7 +700,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
-    // 4. drive GEMM, mode-major: lanes = modes, columns = steps
+    LNET_TRACE(3);
+    // 4. drive GEMM, mode-major: lanes = modes (repeated every 64 lanes), columns = steps
     if (tid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 128);
@@ -553,21 +711,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
       sm100::mma_commit(mbar);
     }
     wait_mma(mbar, phase, a.error);
+    LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
-    constexpr int SW = (M + 31) / 32;
-    if (warp < SW) {
-      float mom[7];
-      chunk_scan<M, true>(tbase, 128, 256, n, b, chunk, a.n_chunks, a.consts, a.rec, a.flags,
-                          a.error, smem + P::OFF_XS, P::SLAB_S, mom);
-      if (tid < M) {
-        float *dst = a.partial + (b * a.n_chunks + chunk) * 7 * M;
-#pragma unroll
-        for (int k = 0; k < 7; ++k) dst[k * M + tid] = mom[k];
-      }
-    }
+    chunk_scan<M, true>(tbase, 128, 256, n, b, chunk, a.n_chunks, s_k, a.rec, a.flags, a.error,
+                        smem + P::OFF_XS, P::SLAB_S, s_scan,
+                        a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    LNET_TRACE(5);
     // 6. synthesis GEMM (token-major) into columns [0, D)
     if (tid == 0) {
       sm100::tc_fence_after();
@@ -577,6 +729,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
       sm100::mma_commit(mbar);
     }
     wait_mma(mbar, phase, a.error);
+    LNET_TRACE(6);
     // 7. residual epilogue: v = fl + ls * (modal + ds * xhat), xhat = fl * rs * g
     {
       float modal[HD];
@@ -597,8 +750,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
           for (int i = 0; i < 8; ++i) {
             const int d = d0 + i;
             const float x = __bfloat162float(fv[i]);
-            const float xh = x * rsr * __ldg(a.norm + d);
-            o[i] = x + __ldg(a.ls + d) * (modal[8 * g + i] + __ldg(a.ds + d) * xh);
+            const float xh = x * rsr * s_norm[d];
+            o[i] = x + s_ls[d] * (modal[8 * g + i] + s_ds[d] * xh);
           }
           uint4 ov;
           ov.x = pack_bf16x2(o[0], o[1]);
@@ -611,6 +764,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
     }
     sm100::tc_fence_before();
     __syncthreads();
+    LNET_TRACE(7);
+    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
   __syncthreads();
   if (warp == 0) {
@@ -628,6 +783,10 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_MISC + 8);
   int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);
   float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
+  float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
+  const float *s_w = par, *s_bias = par + kTaps * D, *s_norm = par + (kTaps + 1) * D;
+  float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
+  float *s_scan = reinterpret_cast<float *>(smem + P::OFF_V);  // tile is dead during the scan
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t s_base = sm100::smem_u32(smem);
 
@@ -640,6 +799,14 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     sm100::tmem_relinquish();
   }
   copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
+  // conv weights transposed to [tap][channel]
+  for (int i = tid; i < kTaps * D; i += kFusedThreads) {
+    const int k = i / D, d = i - (i / D) * D;
+    par[i] = __ldg(a.conv_w + d * kTaps + k);
+  }
+  copy_floats(par + kTaps * D, a.conv_b, D);
+  copy_floats(par + (kTaps + 1) * D, a.norm, D);
+  copy_floats(s_k, a.consts, kConsts * M);
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
@@ -651,11 +818,13 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   constexpr int HD = D / 2;
   const int64_t total = a.B * a.n_chunks;
 
+  unsigned long long t_last = clock64();
   for (;;) {
     if (tid == 0) *item_slot = (int64_t)atomicAdd(a.counter, 1u);
     __syncthreads();
     const int64_t item = *item_slot;
     if (item >= total) break;
+    LNET_TRACE(0);
     const int64_t chunk = item / a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
@@ -670,27 +839,28 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
       *reinterpret_cast<uint4 *>(smem + P::OFF_V + r * P::PITCH + kc * 16) = v;
     }
     __syncthreads();
+    LNET_TRACE(1);
     // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm
     float f[HD];
 #pragma unroll
-    for (int i = 0; i < HD; ++i) f[i] = __ldg(a.conv_b + half * HD + i);
+    for (int i = 0; i < HD; ++i) f[i] = s_bias[half * HD + i];
 #pragma unroll
     for (int k = 0; k < kTaps; ++k) {
       const uint8_t *src = smem + P::OFF_V + (row + 4 * k) * P::PITCH + half * HD * 2;
+      const float *wk = s_w + k * D + half * HD;
 #pragma unroll
       for (int g = 0; g < HD / 8; ++g) {
         uint4 v = *reinterpret_cast<const uint4 *>(src + g * 16);
         const __nv_bfloat16 *vv = reinterpret_cast<const __nv_bfloat16 *>(&v);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          f[8 * g + i] = fmaf(__ldg(a.conv_w + (half * HD + 8 * g + i) * kTaps + k),
-                              __bfloat162float(vv[i]), f[8 * g + i]);
+          f[8 * g + i] = fmaf(wk[8 * g + i], __bfloat162float(vv[i]), f[8 * g + i]);
       }
     }
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < HD; ++i) {
-      f[i] = silu_f(f[i]);
+      f[i] = silu_fast(f[i]);
       ss = fmaf(f[i], f[i], ss);
     }
     red[half * kChunk + row] = ss;
@@ -701,7 +871,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
       const int d0 = half * HD + 8 * g;
       float h[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * __ldg(a.norm + d0 + i);
+      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * s_norm[d0 + i];
       uint4 xh;
       xh.x = pack_bf16x2(h[0], h[1]);
       xh.y = pack_bf16x2(h[2], h[3]);
@@ -712,6 +882,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    LNET_TRACE(3);
     // 3. drive GEMM (mode-major)
     if (tid == 0) {
       sm100::tc_fence_after();
@@ -722,20 +893,15 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
       sm100::mma_commit(mbar);
     }
     wait_mma(mbar, phase, a.error);
+    LNET_TRACE(4);
     // 4. scan + look-back + moments
-    constexpr int SW = (M + 31) / 32;
-    if (warp < SW) {
-      float mom[7];
-      chunk_scan<M, false>(tbase, 0, 128, n, b, chunk, a.n_chunks, a.consts, a.rec, a.flags,
-                           a.error, nullptr, 0, mom);
-      if (tid < M) {
-        float *dst = a.partial + (b * a.n_chunks + chunk) * 7 * M;
-#pragma unroll
-        for (int k = 0; k < 7; ++k) dst[k * M + tid] = mom[k];
-      }
-    }
+    chunk_scan<M, false>(tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec, a.flags, a.error,
+                         nullptr, 0, s_scan, a.partial + (b * a.n_chunks + chunk) * 7 * M,
+                         a.trace, a.kernel_id);
     sm100::tc_fence_before();
     __syncthreads();
+    LNET_TRACE(5);
+    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
   __syncthreads();
   if (warp == 0) {
@@ -788,6 +954,7 @@ inline bool fused_supported(const lnet_b200_alphabet_params *p,
 }
 
 int sm_count();
+int fused_trace_enabled();
 
 template <int C, int D, int M>
 int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -820,6 +987,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.flags = w.flags;
   wa.counter = counters;
   wa.error = counters + 2;
+  wa.trace = fused_trace_enabled();
+  wa.kernel_id = 0;
   LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_writer_kernel<C, D, M>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, WP::BYTES),
                       "cudaFuncSetAttribute(fused_writer_kernel)"));
@@ -831,7 +1000,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   ra.in = w.stream;
   ra.drive = w.rdrive;
   ra.syn = nullptr;
-  ra.consts = w.consts + 10 * M;
+  ra.consts = w.consts + kConsts * M;
   ra.conv_w = p->reader_conv_weight;
   ra.conv_b = p->reader_conv_bias;
   ra.norm = p->reader_norm;
@@ -840,6 +1009,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   ra.rec = w.rrec;
   ra.flags = w.flags + B * nch;
   ra.counter = counters + 1;
+  ra.kernel_id = 1;
   LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_reader_kernel<D, M>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            RP::LAUNCH_BYTES),
@@ -904,3 +1074,29 @@ inline int fused_head(const lnet_b200_alphabet_params *p, int64_t B, const float
 }
 
 }  // namespace lnet
+
+namespace lnet {
+static int g_trace_on = 0;
+int fused_trace_enabled() { return g_trace_on; }
+}  // namespace lnet
+
+// Enable (1) / disable (0) per-phase cycle tracing of the fused kernels; enabling clears
+// the counters of the current device.
+extern "C" int lnet_b200_trace_enable(int on) {
+  lnet::g_trace_on = on != 0;
+  if (on) {
+    unsigned long long zero[32] = {};
+    return lnet::cuda_check(cudaMemcpyToSymbol(lnet::g_fused_trace, zero, sizeof(zero)),
+                            "cudaMemcpyToSymbol(g_fused_trace)");
+  }
+  return LNET_OK;
+}
+
+// Copies the 2 x 16 phase counters (writer, reader) of the current device to `out`
+// (synchronises the device).
+extern "C" int lnet_b200_trace_read(unsigned long long *out) {
+  if (!out) return lnet::fail(LNET_ERR_INVALID_ARGUMENT, "out is NULL");
+  return lnet::cuda_check(
+      cudaMemcpyFromSymbol(out, lnet::g_fused_trace, 32 * sizeof(unsigned long long)),
+      "cudaMemcpyFromSymbol(g_fused_trace)");
+}

@@ -122,6 +122,8 @@ SIGNATURES = {
         [_c_p, _c_p, _c_p, _c_p, _i32, _i32, ctypes.c_double, ctypes.c_double, _i32, _c_p, _i64,
          _i64, _c_p, _c_p],
     ),
+    "lnet_b200_trace_enable": (ctypes.c_int, [ctypes.c_int]),
+    "lnet_b200_trace_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
     "lnet_b200_last_launch_count": (ctypes.c_int, []),
     "lnet_b200_profile_enable": (None, [ctypes.c_int]),
     "lnet_b200_profile_read": (
@@ -208,3 +210,22 @@ ROUTE_GENERAL = 1
 
 def set_route(route: int) -> None:
     check(load().lnet_b200_set_route(int(route)), "lnet_b200_set_route")
+
+
+TRACE_SLOTS = {0: "claim", 1: "tile_load", 2: "first_gemm_wait", 3: "token_epilogue",
+               4: "drive_gemm_wait", 5: "scan", 6: "synthesis_wait", 7: "residual_epilogue",
+               10: "scan_pass1", 11: "lookback", 12: "scan_pass2", 15: "items"}
+
+
+def trace_enable(on: bool) -> None:
+    check(load().lnet_b200_trace_enable(1 if on else 0), "lnet_b200_trace_enable")
+
+
+def trace_read() -> dict[str, dict[str, int]]:
+    """Per kernel (writer, reader): phase -> summed cycles of CTA thread 0."""
+    buf = (ctypes.c_ulonglong * 32)()
+    check(load().lnet_b200_trace_read(buf), "lnet_b200_trace_read")
+    out = {}
+    for k, name in enumerate(("fused_writer_kernel", "fused_reader_kernel")):
+        out[name] = {TRACE_SLOTS[s]: int(buf[16 * k + s]) for s in TRACE_SLOTS}
+    return out
