@@ -294,7 +294,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 // SiLU with the hardware exponential (relative error ~1e-6, far inside the
 // bf16 activation rounding of this route).
-__device__ __forceinline__ float silu_fast(float v) { return v * __frcp_rn(1.0f + __expf(-v)); }
+__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 __device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, float &cr,
                                      float &ci) {  // c += a * b
@@ -408,10 +408,12 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
         my[(2 * k) * M + m] = g_r[k];
         my[(2 * k + 1) * M + m] = g_i[k];
       }
-      __threadfence();
     }
     asm volatile("bar.sync 1, 64;" ::: "memory");
-    if (tid == 192) sm100::st_release(flags + item, kFlagAgg);
+    if (tid == 192) {
+      __threadfence();
+      sm100::st_release(flags + item, kFlagAgg);
+    }
     float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
     if (chunk > 0) {
       const int64_t prev = item - 1;
@@ -464,7 +466,6 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
         my[8 * M + (2 * k) * M + m] = vr;
         my[8 * M + (2 * k + 1) * M + m] = vi;
       }
-      __threadfence();
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         sc[kScanCarry + (2 * k) * 64 + m] = p_r[k];
@@ -472,7 +473,10 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
       }
     }
     asm volatile("bar.sync 1, 64;" ::: "memory");
-    if (tid == 192) sm100::st_release(flags + item, kFlagIncl);
+    if (tid == 192) {
+      __threadfence();
+      sm100::st_release(flags + item, kFlagIncl);
+    }
   }
   __syncthreads();
   mark(11);
