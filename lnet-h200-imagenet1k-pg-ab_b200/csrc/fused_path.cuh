@@ -39,7 +39,6 @@
 namespace lnet {
 
 constexpr int kChunk = 128;
-constexpr int kSub = 32;  // steps per scan sub-chunk (kChunk / 4)
 constexpr int kHalo = 8;
 constexpr int kTaps = 5;
 constexpr int kXRows = kChunk + 2 * kHalo;
@@ -48,11 +47,26 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kFlagAgg = 1, kFlagIncl = 2;
 constexpr uint32_t kErrMbar = 1, kErrLookback = 2;
 
-// Per-block pole constants (floats, M entries each):
+// Per-block pole constants (floats, M entries each), SUB = steps per scan
+// sub-chunk of the block (64 writer, 32 reader):
 //   [0] a_re, [1] a_im, [2 + 2i] / [3 + 2i]  re/im of a^(128 - i),
-//   [10 + 2i] / [11 + 2i] re/im of a^(32 - i)  (i = 0..3), [18]/[19] a^64, [20]/[21] a^96.
+//   [10 + 2i] / [11 + 2i] re/im of a^(SUB - i)  (i = 0..3), [18]/[19] a^(2 SUB),
+//   [20]/[21] a^(3 SUB).
 constexpr int kConsts = 22;
-constexpr int KC_AL = 2, KC_AS = 10, KC_A64 = 18, KC_A96 = 20;
+constexpr int KC_AL = 2, KC_AS = 10, KC_A2S = 18, KC_A3S = 20;
+constexpr int kWriterSub = 64, kReaderSub = 32;
+constexpr int kWriterDriveRows = 64, kReaderDriveRows = 128;
+
+template <int NSUB>
+struct ScanLayout {
+  static constexpr int SUB = kChunk / NSUB;
+  static constexpr int END = 0;                   // [NSUB][2][64]
+  static constexpr int LAST = NSUB * 128;         // [NSUB][8][64]
+  static constexpr int CARRY = LAST + NSUB * 512; // [8][64]
+  static constexpr int MOM = CARRY + 512;         // [NSUB][7][64]
+  static constexpr int FLOATS = MOM + NSUB * 448;
+};
+
 
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
@@ -60,7 +74,7 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 struct FusedWorkspace {
   float *moments = nullptr;            // [2][B][7M]
   __nv_bfloat16 *q = nullptr;          // stem B operand   [5][C/8][D][8]
-  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][128][8]
+  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][64][8]
   __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][128][8]
   __nv_bfloat16 *wsyn = nullptr;       // synthesis B      [2M/8][D][8]
   float *consts = nullptr;             // [2][kConsts * M]
@@ -81,7 +95,7 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   const int64_t B = r->batch, nch = fused_chunks(std::max<int64_t>(r->steps, 1));
   w.moments = ar.take<float>((size_t)2 * B * 7 * M);
   w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
-  w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
+  w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * kWriterDriveRows);
   w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
   w.wsyn = ar.take<__nv_bfloat16>((size_t)2 * M * D);
   w.consts = ar.take<float>((size_t)2 * kConsts * M);
@@ -107,9 +121,11 @@ __device__ __forceinline__ void cmul_d(double ar, double ai, double br, double b
 __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace w) {
   const int C = p.raw_input_dim, D = p.model_dim, M = p.modes, K5 = p.conv_kernel;
   const int64_t n_q = (int64_t)kTaps * C * D;
-  const int64_t n_drive = (int64_t)2 * D * 128;  // per block: re/im x D x 128 lanes
+  // drive A rows per block: writer 64 (lanes 0..63), reader 128 (modes repeated every 64 lanes)
+  const int64_t n_wdrive = (int64_t)2 * D * kWriterDriveRows;
+  const int64_t n_rdrive = (int64_t)2 * D * kReaderDriveRows;
   const int64_t n_syn = (int64_t)2 * M * D;
-  const int64_t total = n_q + 2 * n_drive + n_syn + 2 * M;
+  const int64_t total = n_q + n_wdrive + n_rdrive + n_syn + 2 * M;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     if (i < n_q) {  // Q_k[d][c] = w[d][k] * P[d][c]
@@ -121,12 +137,13 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
       continue;
     }
     int64_t j = i - n_q;
-    if (j < 2 * n_drive) {  // drive A: lane r holds mode r % 64 (zero if >= M), K = d
-      int blk = (int)(j / n_drive);
-      int64_t rem = j - blk * n_drive;
-      int part = (int)(rem / ((int64_t)D * 128));
-      int rem2 = (int)(rem - (int64_t)part * D * 128);
-      int d = rem2 / 128, r = rem2 - d * 128;
+    if (j < n_wdrive + n_rdrive) {  // drive A: lane r holds mode r % 64 (zero if >= M), K = d
+      const int blk = j < n_wdrive ? 0 : 1;
+      const int R = blk == 0 ? kWriterDriveRows : kReaderDriveRows;
+      int64_t rem = blk == 0 ? j : j - n_wdrive;
+      int part = (int)(rem / ((int64_t)D * R));
+      int rem2 = (int)(rem - (int64_t)part * D * R);
+      int d = rem2 / R, r = rem2 - d * R;
       int m = r % 64;
       float out = 0.f;
       if (m < M) {
@@ -141,10 +158,10 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
                                 : (double)z.g_re * fi + (double)z.g_im * fr);
       }
       __nv_bfloat16 *dst = blk == 0 ? w.wdrive : w.rdrive;
-      dst[(int64_t)part * D * 128 + ((d / 8) * 128 + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
+      dst[(int64_t)part * D * R + ((d / 8) * R + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
       continue;
     }
-    j -= 2 * n_drive;
+    j -= n_wdrive + n_rdrive;
     if (j < n_syn) {  // synthesis B rows = d, K = 2M
       int d = (int)(j / (2 * M)), jj = (int)(j - (int64_t)d * 2 * M);
       w.wsyn[((jj / 8) * D + d) * 8 + (jj % 8)] = __float2bfloat16_rn(p.writer_frame[d * 2 * M + jj]);
@@ -167,14 +184,16 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
       cmul_d(pr, pi, ar, ai, nr, ni);
       pr = nr;
       pi = ni;
-      int slot = -1;
-      if (step >= kChunk - 3) slot = KC_AL + 2 * (kChunk - step);
-      else if (step >= kSub - 3 && step <= kSub) slot = KC_AS + 2 * (kSub - step);
-      else if (step == 64) slot = KC_A64;
-      else if (step == 96) slot = KC_A96;
-      if (slot >= 0) {
-        k[slot * M + m] = (float)pr;
-        k[(slot + 1) * M + m] = (float)pi;
+      const int sub = blk == 0 ? kWriterSub : kReaderSub;
+      int slots[4] = {-1, -1, -1, -1};
+      if (step >= kChunk - 3) slots[0] = KC_AL + 2 * (kChunk - step);
+      if (step >= sub - 3 && step <= sub) slots[1] = KC_AS + 2 * (sub - step);
+      if (step == 2 * sub) slots[2] = KC_A2S;
+      if (step == 3 * sub) slots[3] = KC_A3S;
+      for (int s = 0; s < 4; ++s) {
+        if (slots[s] < 0) continue;
+        k[slots[s] * M + m] = (float)pr;
+        k[(slots[s] + 1) * M + m] = (float)pi;
       }
     }
     k[m] = z.a_re;
@@ -183,52 +202,13 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
 }
 
 // ---------------------------------------------------------------- shared-memory plans
-// Scan scratch (floats): sub-chunk end states [4][2][64], last-four states
-// [4][8][64], carry block [8][64] (true last four states of the previous
-// chunk), moment sums [4][7][64].
-constexpr int kScanEnd = 0, kScanLast = 512, kScanCarry = 2560, kScanMom = 3072;
-constexpr int kScanFloats = 3072 + 4 * 7 * 64;
-
-template <int C, int D, int M>
-struct WriterPlan {
-  static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
-  static constexpr int SLAB_AD = 128 * 16;
-  static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
-  static constexpr int SLAB_Q = D * 16;
-  static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
-  static constexpr int SLAB_WS = D * 16;
-  static constexpr int WS_BYTES = (2 * M / 8) * SLAB_WS;
-  static constexpr int SLAB_X = kXRows * 16 + 16;
-  static constexpr int X_BYTES = (C / 8) * SLAB_X;
-  static constexpr int FL_BYTES = kChunk * D * 2;
-  static constexpr int XF_BYTES = cmax(X_BYTES, FL_BYTES);
-  static constexpr int SLAB_XH = kChunk * 16;
-  static constexpr int XH_BYTES = (D / 8) * SLAB_XH;
-  static constexpr int SLAB_S = kChunk * 16 + 16;
-  static constexpr int S_BYTES = (2 * M / 8) * SLAB_S;
-  static constexpr int XS_BYTES = cmax(XH_BYTES, S_BYTES);
-  static constexpr int OFF_AD = 0;
-  static constexpr int OFF_Q = OFF_AD + AD_BYTES;
-  static constexpr int OFF_WS = OFF_Q + Q_BYTES;
-  static constexpr int OFF_XF = OFF_WS + WS_BYTES;
-  static constexpr int OFF_XS = OFF_XF + XF_BYTES;
-  static constexpr int OFF_SCAN = OFF_XS + XS_BYTES;              // float [kScanFloats]
-  static constexpr int OFF_PAR = OFF_SCAN + kScanFloats * 4;      // float [4][D]: bias, g, ds, ls
-  static constexpr int OFF_K = OFF_PAR + 4 * D * 4;               // float [kConsts * M]
-  static constexpr int OFF_RED = OFF_K + kConsts * M * 4;         // float [2][128]
-  static constexpr int OFF_RS = OFF_RED + 2 * kChunk * 4;         // float [128]
-  static constexpr int OFF_MISC = OFF_RS + kChunk * 4;            // mbar, tmem base, item
-  static constexpr int BYTES = OFF_MISC + 64;
-  static constexpr int TMEM_COLS = 512;  // [0,128) stem/synthesis acc, [128,256) u re, [256,384) u im
-};
-
 template <int D, int M>
 struct ReaderPlan {
   static_assert(D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
   static constexpr int SLAB_AD = 128 * 16;
   static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
   static constexpr int PITCH = D * 2 + 16;  // stream tile row pitch (bank-conflict free)
-  static constexpr int V_BYTES = cmax(kXRows * PITCH, kScanFloats * 4);  // tile, then scan scratch
+  static constexpr int V_BYTES = cmax(kXRows * PITCH, ScanLayout<4>::FLOATS * 4);  // tile, then scan scratch
   static constexpr int SLAB_XH = kChunk * 16;
   static constexpr int XH_BYTES = (D / 8) * SLAB_XH;
   static constexpr int OFF_AD = 0;
@@ -313,17 +293,30 @@ __device__ __forceinline__ uint32_t wait_flag(const uint32_t *flags, int64_t idx
 }
 
 // ---------------------------------------------------------------- scan + look-back
-// Executed by all 256 threads.  Warp w reads TMEM lane quarter w % 4: modes
-// m = 32 * (w % 2) + lane (live if m < M) of sub-chunk q = (w % 4) / 2 + 2 * (w / 4),
-// steps [32 q, 32 q + 32).  u_re / u_im of the chunk live in TMEM columns
-// [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's moment partial
-// sums [7][M] to `partial`.
-template <int M, bool WRITE_STATES>
-__device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_im, int n,
-                                           int64_t row, int64_t chunk, int64_t n_chunks,
-                                           const float *K, float *rec, uint32_t *flags,
-                                           uint32_t *error, uint8_t *s_slab, int slab_s,
-                                           float *sc, float *partial, int trace, int kid) {
+// Executed by the 256 threads of one item stream (local thread id `ltid`).
+// NSUB = 4 (reader): the drive operand repeats the mode rows every 64 lanes, so
+//   local warp w reads lane quarter w % 4 = modes 32 * (w % 2) + lane of
+//   sub-chunk q = (w % 4) / 2 + 2 * (w / 4).
+// NSUB = 2 (writer): modes live in lanes 0..63 only; local warps with w % 4 < 2
+//   scan modes 32 * (w % 4) + lane of sub-chunk q = w / 4; the others only
+//   join the barriers.
+// Sub-chunk q covers steps [SUB q, SUB q + SUB), SUB = 128 / NSUB.  u_re / u_im
+// live in TMEM columns [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's
+// moment partial sums [7][M] to `partial`.
+
+__device__ __forceinline__ void group_sync(int id) {
+  asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory");
+}
+
+template <int M, bool WRITE_STATES, int NSUB>
+__device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, uint32_t tbase,
+                                           int col_re, int col_im, int n, int64_t row,
+                                           int64_t chunk, int64_t n_chunks, const float *K,
+                                           float *rec, uint32_t *flags, uint32_t *error,
+                                           uint8_t *s_slab, int slab_s, float *sc,
+                                           float *partial, int trace, int kid) {
+  using L = ScanLayout<NSUB>;
+  constexpr int SUB = L::SUB;
   unsigned long long t_scan = trace ? clock64() : 0;
   auto mark = [&](int slot) {
     if (trace && threadIdx.x == 0) {
@@ -332,75 +325,83 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
       t_scan = now;
     }
   };
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int Q = warp & 3;
-  const int q = (Q >> 1) + 2 * (warp >> 2);
-  const int m = 32 * (Q & 1) + lane;
-  const bool live = m < M;
+  const int lwarp = ltid >> 5, lane = ltid & 31;
+  const int Q = lwarp & 3;
+  int q, m;
+  bool scanner;
+  if constexpr (NSUB == 4) {
+    q = (Q >> 1) + 2 * (lwarp >> 2);
+    m = 32 * (Q & 1) + lane;
+    scanner = true;
+  } else {
+    q = lwarp >> 2;
+    m = 32 * Q + lane;
+    scanner = Q < 2;
+  }
+  const bool live = scanner && m < M;
   const int mk = live ? m : 0;
+  const int pub_tid = NSUB == 4 ? 192 : 128;  // first thread of the last sub-chunk
+  const bool publisher_group = scanner && q == NSUB - 1;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * Q) << 16);
-  const int s0 = kSub * q;
-  const int len = max(0, min(kSub, n - s0));
+  const int s0 = SUB * q;
+  const int len = scanner ? max(0, min(SUB, n - s0)) : 0;
   const float ar = K[mk], ai = K[M + mk];
 
   // ---- pass 1: sub-chunk local scan from zero
-  float ur[kSub], ui[kSub];
-  if (len > 0) {
-    sm100::tmem_ld16(lane_addr + col_re + s0, ur);
-    sm100::tmem_ld16(lane_addr + col_im + s0, ui);
-    sm100::tmem_ld16(lane_addr + col_re + s0 + 16, ur + 16);
-    sm100::tmem_ld16(lane_addr + col_im + s0 + 16, ui + 16);
-    sm100::tmem_ld_wait();
-  }
   float sr = 0.f, si = 0.f;
   float l_r[4] = {0, 0, 0, 0}, l_i[4] = {0, 0, 0, 0};  // l[0] = last state
+  for (int c0 = 0; c0 < len; c0 += 16) {
+    float ur[16], ui[16];
+    sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
+    sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
+    sm100::tmem_ld_wait();
 #pragma unroll
-  for (int i = 0; i < kSub; ++i) {
-    if (i < len) {
-      float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
-      float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
-      sr = nr;
-      si = ni;
-      l_r[3] = l_r[2]; l_i[3] = l_i[2];
-      l_r[2] = l_r[1]; l_i[2] = l_i[1];
-      l_r[1] = l_r[0]; l_i[1] = l_i[0];
-      l_r[0] = sr; l_i[0] = si;
+    for (int i = 0; i < 16; ++i) {
+      if (c0 + i < len) {
+        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
+        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
+        sr = nr;
+        si = ni;
+        l_r[3] = l_r[2]; l_i[3] = l_i[2];
+        l_r[2] = l_r[1]; l_i[2] = l_i[1];
+        l_r[1] = l_r[0]; l_i[1] = l_i[0];
+        l_r[0] = sr; l_i[0] = si;
+      }
     }
   }
   if (live) {
-    sc[kScanEnd + (2 * q) * 64 + m] = sr;
-    sc[kScanEnd + (2 * q + 1) * 64 + m] = si;
+    sc[L::END + (2 * q) * 64 + m] = sr;
+    sc[L::END + (2 * q + 1) * 64 + m] = si;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      sc[kScanLast + (8 * q + 2 * k) * 64 + m] = l_r[k];
-      sc[kScanLast + (8 * q + 2 * k + 1) * 64 + m] = l_i[k];
+      sc[L::LAST + (8 * q + 2 * k) * 64 + m] = l_r[k];
+      sc[L::LAST + (8 * q + 2 * k + 1) * 64 + m] = l_i[k];
     }
   }
-  __syncthreads();
+  group_sync(bar_group);
   mark(10);
-  // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^32 c_j + e_j
-  const float a32r = K[(KC_AS + 0) * M + mk], a32i = K[(KC_AS + 1) * M + mk];
+  // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^SUB c_j + e_j
+  const float asr = K[(KC_AS + 0) * M + mk], asi = K[(KC_AS + 1) * M + mk];
   float cr = 0.f, ci = 0.f, cpr = 0.f, cpi = 0.f;  // c_q and c_{q-1}
   for (int j = 0; j < q; ++j) {
     cpr = cr;
     cpi = ci;
-    float nr = sc[kScanEnd + (2 * j) * 64 + mk], ni = sc[kScanEnd + (2 * j + 1) * 64 + mk];
-    cmac(a32r, a32i, cr, ci, nr, ni);
+    float nr = sc[L::END + (2 * j) * 64 + mk], ni = sc[L::END + (2 * j + 1) * 64 + mk];
+    cmac(asr, asi, cr, ci, nr, ni);
     cr = nr;
     ci = ni;
   }
 
-  // ---- aggregate, look-back and inclusive record: sub-chunk 3 (warps 6 and 7)
-  if (q == 3) {
+  // ---- aggregate, look-back and inclusive record: threads of the last sub-chunk
+  if (publisher_group) {
     const int64_t item = row * n_chunks + chunk;  // record index (row-major)
     float *my = rec + item * 16 * M;
     float g_r[4], g_i[4];  // chunk-local last four states
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float pr = K[(KC_AS + 2 * k) * M + mk], pi = K[(KC_AS + 2 * k + 1) * M + mk];
       g_r[k] = l_r[k];
       g_i[k] = l_i[k];
-      cmac(pr, pi, cr, ci, g_r[k], g_i[k]);
+      cmac(K[(KC_AS + 2 * k) * M + mk], K[(KC_AS + 2 * k + 1) * M + mk], cr, ci, g_r[k], g_i[k]);
     }
     if (live) {
 #pragma unroll
@@ -409,8 +410,8 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
         my[(2 * k + 1) * M + m] = g_i[k];
       }
     }
-    asm volatile("bar.sync 1, 64;" ::: "memory");
-    if (tid == 192) {
+    asm volatile("bar.sync %0, 64;" ::"r"(bar_lb) : "memory");
+    if (ltid == pub_tid) {
       __threadfence();
       sm100::st_release(flags + item, kFlagAgg);
     }
@@ -419,7 +420,7 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
       const int64_t prev = item - 1;
       const uint32_t st = wait_flag(flags, prev);
       if (st == 0) {
-        if (tid == 192) atomicOr(error, kErrLookback);
+        if (ltid == pub_tid) atomicOr(error, kErrLookback);
       } else if (st == kFlagIncl) {
         const float *pr = rec + prev * 16 * M + 8 * M;
 #pragma unroll
@@ -436,7 +437,7 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
           const int64_t qi = row * n_chunks + qq;
           const uint32_t sq = wait_flag(flags, qi);
           if (sq == 0) {
-            if (tid == 192) atomicOr(error, kErrLookback);
+            if (ltid == pub_tid) atomicOr(error, kErrLookback);
             break;
           }
           const float *qr = rec + qi * 16 * M + (sq == kFlagIncl ? 8 * M : 0);
@@ -468,43 +469,43 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        sc[kScanCarry + (2 * k) * 64 + m] = p_r[k];
-        sc[kScanCarry + (2 * k + 1) * 64 + m] = p_i[k];
+        sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
+        sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
       }
     }
-    asm volatile("bar.sync 1, 64;" ::: "memory");
-    if (tid == 192) {
+    asm volatile("bar.sync %0, 64;" ::"r"(bar_lb) : "memory");
+    if (ltid == pub_tid) {
       __threadfence();
       sm100::st_release(flags + item, kFlagIncl);
     }
   }
-  __syncthreads();
+  group_sync(bar_group);
   mark(11);
 
   // ---- pass 2 from the true state before this sub-chunk
-  const float car = sc[kScanCarry + mk], cai = sc[kScanCarry + 64 + mk];
-  // a^(32 q) and a^(32 (q - 1))
+  const float car = sc[L::CARRY + mk], cai = sc[L::CARRY + 64 + mk];
+  // a^(SUB q) and a^(SUB (q - 1))
   float pqr = 1.f, pqi = 0.f, pq1r = 1.f, pq1i = 0.f;
-  if (q == 1) { pqr = a32r; pqi = a32i; }
-  if (q == 2) { pqr = K[KC_A64 * M + mk]; pqi = K[(KC_A64 + 1) * M + mk]; pq1r = a32r; pq1i = a32i; }
+  if (q == 1) { pqr = asr; pqi = asi; }
+  if (q == 2) { pqr = K[KC_A2S * M + mk]; pqi = K[(KC_A2S + 1) * M + mk]; pq1r = asr; pq1i = asi; }
   if (q == 3) {
-    pqr = K[KC_A96 * M + mk]; pqi = K[(KC_A96 + 1) * M + mk];
-    pq1r = K[KC_A64 * M + mk]; pq1i = K[(KC_A64 + 1) * M + mk];
+    pqr = K[KC_A3S * M + mk]; pqi = K[(KC_A3S + 1) * M + mk];
+    pq1r = K[KC_A2S * M + mk]; pq1i = K[(KC_A2S + 1) * M + mk];
   }
   float h_r[4], h_i[4];  // true states at the four steps before this sub-chunk
   if (q == 0) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      h_r[k] = sc[kScanCarry + (2 * k) * 64 + mk];
-      h_i[k] = sc[kScanCarry + (2 * k + 1) * 64 + mk];
+      h_r[k] = sc[L::CARRY + (2 * k) * 64 + mk];
+      h_i[k] = sc[L::CARRY + (2 * k + 1) * 64 + mk];
     }
   } else {
     float ipr = cpr, ipi = cpi;  // true state before sub-chunk q - 1
     cmac(pq1r, pq1i, car, cai, ipr, ipi);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      h_r[k] = sc[kScanLast + (8 * (q - 1) + 2 * k) * 64 + mk];
-      h_i[k] = sc[kScanLast + (8 * (q - 1) + 2 * k + 1) * 64 + mk];
+      h_r[k] = sc[L::LAST + (8 * (q - 1) + 2 * k) * 64 + mk];
+      h_i[k] = sc[L::LAST + (8 * (q - 1) + 2 * k + 1) * 64 + mk];
       cmac(K[(KC_AS + 2 * k) * M + mk], K[(KC_AS + 2 * k + 1) * M + mk], ipr, ipi, h_r[k],
            h_i[k]);
     }
@@ -516,44 +517,51 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
   float h1r = h_r[0], h1i = h_i[0], h2r = h_r[1], h2i = h_i[1];
   float h3r = h_r[2], h3i = h_i[2], h4r = h_r[3], h4i = h_i[3];
   float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
+  for (int c0 = 0; c0 < len; c0 += 16) {
+    float ur[16], ui[16];
+    sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
+    sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
+    sm100::tmem_ld_wait();
 #pragma unroll
-  for (int i = 0; i < kSub; ++i) {
-    if (i < len) {
-      float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
-      float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
-      sr = nr;
-      si = ni;
-      e = fmaf(sr, sr, fmaf(si, si, e));
-      if (hist || i >= 1) {
-        c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
-        c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
-      }
-      if (hist || i >= 2) {
-        c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
-        c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
-      }
-      if (hist || i >= 4) {
-        c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
-        c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
-      }
-      h4r = h3r; h4i = h3i;
-      h3r = h2r; h3i = h2i;
-      h2r = h1r; h2i = h1i;
-      h1r = sr; h1i = si;
-      if constexpr (WRITE_STATES) {
-        if (live) {
-          const int t = s0 + i;
-          *reinterpret_cast<__nv_bfloat16 *>(s_slab + (m / 8) * slab_s + t * 16 + (m % 8) * 2) =
-              __float2bfloat16_rn(sr);
-          *reinterpret_cast<__nv_bfloat16 *>(s_slab + ((M + m) / 8) * slab_s + t * 16 +
-                                             ((M + m) % 8) * 2) = __float2bfloat16_rn(si);
+    for (int i0 = 0; i0 < 16; ++i0) {
+      const int i = c0 + i0;
+      if (i < len) {
+        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i0]));
+        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i0]));
+        sr = nr;
+        si = ni;
+        e = fmaf(sr, sr, fmaf(si, si, e));
+        if (hist || i >= 1) {
+          c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
+          c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
+        }
+        if (hist || i >= 2) {
+          c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
+          c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
+        }
+        if (hist || i >= 4) {
+          c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
+          c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
+        }
+        h4r = h3r; h4i = h3i;
+        h3r = h2r; h3i = h2i;
+        h2r = h1r; h2i = h1i;
+        h1r = sr; h1i = si;
+        if constexpr (WRITE_STATES) {
+          if (live) {
+            const int t = s0 + i;
+            *reinterpret_cast<__nv_bfloat16 *>(s_slab + (m / 8) * slab_s + t * 16 +
+                                               (m % 8) * 2) = __float2bfloat16_rn(sr);
+            *reinterpret_cast<__nv_bfloat16 *>(s_slab + ((M + m) / 8) * slab_s + t * 16 +
+                                               ((M + m) % 8) * 2) = __float2bfloat16_rn(si);
+          }
         }
       }
     }
   }
   mark(12);
   if (live) {
-    float *mo = sc + kScanMom + q * 7 * 64 + m;
+    float *mo = sc + L::MOM + q * 7 * 64 + m;
     mo[0] = e;
     mo[64] = c1r;
     mo[128] = c1i;
@@ -562,11 +570,14 @@ __device__ __forceinline__ void chunk_scan(uint32_t tbase, int col_re, int col_i
     mo[320] = c4r;
     mo[384] = c4i;
   }
-  __syncthreads();
-  for (int j = tid; j < 7 * M; j += kFusedThreads) {
+  group_sync(bar_group);
+  for (int j = ltid; j < 7 * M; j += 256) {
     const int k = j / M, mm = j - (j / M) * M;
-    const float *mo = sc + kScanMom + k * 64 + mm;
-    partial[j] = mo[0] + mo[7 * 64] + mo[14 * 64] + mo[21 * 64];
+    const float *mo = sc + L::MOM + k * 64 + mm;
+    float acc = 0.f;
+#pragma unroll
+    for (int qq = 0; qq < NSUB; ++qq) acc += mo[qq * 7 * 64];
+    partial[j] = acc;
   }
 }
 
@@ -583,34 +594,86 @@ __device__ __forceinline__ void issue_gemm(uint32_t d_tmem, uint32_t a_addr, int
 
 __device__ __forceinline__ void wait_mma(uint64_t *mbar, uint32_t &phase, uint32_t *error) {
   if (!sm100::mbar_wait_bounded(mbar, phase, kSpinLimit)) {
-    if (threadIdx.x == 0) atomicOr(error, kErrMbar);
+    if (threadIdx.x % 256 == 0) atomicOr(error, kErrMbar);
   }
   phase ^= 1u;
   sm100::tc_fence_after();
 }
 
 // ---------------------------------------------------------------- writer kernel
+// One CTA of 512 threads per SM runs two independent item streams (threads
+// [0, 256) and [256, 512)).  The streams share the weight operands in shared
+// memory; each owns half of the TMEM columns, an mbarrier, named barriers and
+// its tile buffers, so one stream's GEMM waits, look-back and global-memory
+// latencies overlap the other stream's arithmetic.
+constexpr int kWriterStreams = 2;
+constexpr int kWriterNSub = 2;
+
 template <int C, int D, int M>
-__global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArgs a) {
+struct WriterPlan {
+  static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
+  // shared by both streams
+  static constexpr int SLAB_AD = 64 * 16;  // drive A rows = modes (lanes 0..63)
+  static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
+  static constexpr int SLAB_Q = D * 16;
+  static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
+  static constexpr int SLAB_WS = D * 16;
+  static constexpr int WS_BYTES = (2 * M / 8) * SLAB_WS;
+  static constexpr int OFF_AD = 0;  // UMMA reads 128 rows per drive slab: the tail lands in Q
+  static constexpr int OFF_Q = OFF_AD + AD_BYTES;
+  static constexpr int OFF_WS = OFF_Q + Q_BYTES;
+  static constexpr int OFF_PAR = OFF_WS + WS_BYTES;            // float [4][D]: bias, g, ds, ls
+  static constexpr int OFF_K = OFF_PAR + 4 * D * 4;            // float [kConsts * M]
+  static constexpr int SHARED_END = (OFF_K + kConsts * M * 4 + 127) / 128 * 128;
+  // per stream
+  static constexpr int SLAB_X = kXRows * 16 + 16;
+  static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, ScanLayout<kWriterNSub>::FLOATS * 4);
+  static constexpr int FL_BYTES = kChunk * D * 2;
+  static constexpr int SLAB_XH = kChunk * 16;
+  static constexpr int SLAB_S = kChunk * 16 + 16;
+  static constexpr int XS_BYTES = cmax((D / 8) * SLAB_XH, (2 * M / 8) * SLAB_S);
+  static constexpr int G_X = 0;                       // x tile, then scan scratch
+  static constexpr int G_FL = G_X + X_BYTES;          // bf16 [128][D] stem output
+  static constexpr int G_XS = G_FL + FL_BYTES;        // xhat slab, then state slab
+  static constexpr int G_RED = G_XS + XS_BYTES;       // float [2][128]
+  static constexpr int G_RS = G_RED + 2 * kChunk * 4; // float [128]
+  static constexpr int G_MISC = G_RS + kChunk * 4;    // mbar, item
+  static constexpr int G_BYTES = (G_MISC + 64 + 127) / 128 * 128;
+  static constexpr int OFF_TMEM_SLOT = SHARED_END + kWriterStreams * G_BYTES;
+  static constexpr int BYTES = OFF_TMEM_SLOT + 16;
+  static constexpr int TMEM_COLS = 512;  // 256 per stream: u re [0,128), u im [128,256);
+                                         // stem and synthesis accumulators reuse [0, D)
+  static_assert(BYTES <= 232448, "writer shared memory exceeds 227 KB");
+  static_assert(Q_BYTES >= 64 * 16, "drive-operand tail must stay inside the stem slabs");
+};
+
+template <int C, int D, int M>
+__global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
+    fused_writer_kernel(FusedArgs a) {
   using P = WriterPlan<C, D, M>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_MISC + 8);
-  int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);
-  float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
-  float *rs_s = reinterpret_cast<float *>(smem + P::OFF_RS);
+  const int tid = threadIdx.x;
+  const int g = tid / kFusedThreads, ltid = tid % kFusedThreads;
+  const int lwarp = ltid >> 5, lane = ltid & 31;
+  uint8_t *gs = smem + P::SHARED_END + g * P::G_BYTES;
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC);
+  int64_t *item_slot = reinterpret_cast<int64_t *>(gs + P::G_MISC + 8);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_TMEM_SLOT);
+  float *red = reinterpret_cast<float *>(gs + P::G_RED);
+  float *rs_s = reinterpret_cast<float *>(gs + P::G_RS);
   float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
   const float *s_bias = par, *s_norm = par + D, *s_ds = par + 2 * D, *s_ls = par + 3 * D;
   float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
-  float *s_scan = reinterpret_cast<float *>(smem + P::OFF_SCAN);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float *s_scan = reinterpret_cast<float *>(gs + P::G_X);  // x tile is dead during the scan
   const uint32_t s_base = sm100::smem_u32(smem);
+  const uint32_t g_base = sm100::smem_u32(gs);
+  const int bar_group = 1 + g, bar_lb = 3 + g;
 
-  if (tid == 0) {
+  if (ltid == 0) {
     sm100::mbar_init(mbar, 1);
     sm100::fence_barrier_init();
   }
-  if (warp == 0) {
+  if (tid < 32) {
     sm100::tmem_alloc(tmem_slot, P::TMEM_COLS);
     sm100::tmem_relinquish();
   }
@@ -626,18 +689,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
-  const uint32_t tbase = *tmem_slot;
+  const uint32_t tbase = *tmem_slot + 256u * g;
   uint32_t phase = 0;
-  const int row = 32 * (warp & 3) + lane;  // step within the chunk (TMEM lane)
-  const int half = warp >> 2;              // column half of the token-major epilogues
+  const int row = 32 * (lwarp & 3) + lane;  // step within the chunk (TMEM lane)
+  const int half = lwarp >> 2;              // column half of the token-major epilogues
   constexpr int HD = D / 2;
-  const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+  const uint32_t lane_addr = tbase + ((uint32_t)(32 * (lwarp & 3)) << 16);
   const int64_t total = a.B * a.n_chunks;
 
   unsigned long long t_last = clock64();
   for (;;) {
-    if (tid == 0) *item_slot = (int64_t)atomicAdd(a.counter, 1u);
-    __syncthreads();
+    if (ltid == 0) *item_slot = (int64_t)atomicAdd(a.counter, 1u);
+    group_sync(bar_group);
     const int64_t item = *item_slot;
     if (item >= total) break;
     LNET_TRACE(0);
@@ -646,89 +709,94 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
     const int n = (int)min((int64_t)kChunk, a.T - t0);
 
     // 1. x tile (zero outside [0, T))
-    for (int i = tid; i < kXRows * (C / 8); i += kFusedThreads) {
+    for (int i = ltid; i < kXRows * (C / 8); i += kFusedThreads) {
       int r = i / (C / 8), kc = i - (i / (C / 8)) * (C / 8);
       int64_t tok = t0 - kHalo + r;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (tok >= 0 && tok < a.T)
         v = __ldg(reinterpret_cast<const uint4 *>(a.in + ((b * a.T + tok) * C + kc * 8)));
-      *reinterpret_cast<uint4 *>(smem + P::OFF_XF + kc * P::SLAB_X + r * 16) = v;
+      *reinterpret_cast<uint4 *>(gs + P::G_X + kc * P::SLAB_X + r * 16) = v;
     }
     sm100::fence_proxy_async_smem();
-    __syncthreads();
+    group_sync(bar_group);
     LNET_TRACE(1);
     // 2. stem GEMM: five row-shifted views of the tile
-    if (tid == 0) {
+    if (ltid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
       for (int k = 0; k < kTaps; ++k)
-        issue_gemm(tbase, s_base + P::OFF_XF + 4 * k * 16, P::SLAB_X,
+        issue_gemm(tbase, g_base + P::G_X + 4 * k * 16, P::SLAB_X,
                    s_base + P::OFF_Q + k * (C / 8) * P::SLAB_Q, P::SLAB_Q, C / 16, idesc, k > 0);
       sm100::mma_commit(mbar);
     }
     wait_mma(mbar, phase, a.error);
     LNET_TRACE(2);
     // 3. bias + SiLU + RMSNorm (thread per step, two column halves)
-    float f[HD];
+    {
+      float f[HD];
 #pragma unroll
-    for (int j = 0; j < HD / 16; ++j) sm100::tmem_ld16(lane_addr + half * HD + 16 * j, f + 16 * j);
-    sm100::tmem_ld_wait();
-    float ss = 0.f;
+      for (int j = 0; j < HD / 16; ++j)
+        sm100::tmem_ld16(lane_addr + half * HD + 16 * j, f + 16 * j);
+      sm100::tmem_ld_wait();
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < HD; ++i) {
-      f[i] = silu_fast(f[i] + s_bias[half * HD + i]);
-      ss = fmaf(f[i], f[i], ss);
-    }
-    red[half * kChunk + row] = ss;
-    __syncthreads();
-    const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
-    if (half == 0) rs_s[row] = rs;
+      for (int i = 0; i < HD; ++i) {
+        f[i] = silu_fast(f[i] + s_bias[half * HD + i]);
+        ss = fmaf(f[i], f[i], ss);
+      }
+      red[half * kChunk + row] = ss;
+      group_sync(bar_group);
+      const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
+      if (half == 0) rs_s[row] = rs;
 #pragma unroll
-    for (int g = 0; g < HD / 8; ++g) {
-      const int d0 = half * HD + 8 * g;
-      uint4 xh, fl;
-      float h[8];
+      for (int gq = 0; gq < HD / 8; ++gq) {
+        const int d0 = half * HD + 8 * gq;
+        uint4 xh, fl;
+        float h[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * s_norm[d0 + i];
-      xh.x = pack_bf16x2(h[0], h[1]);
-      xh.y = pack_bf16x2(h[2], h[3]);
-      xh.z = pack_bf16x2(h[4], h[5]);
-      xh.w = pack_bf16x2(h[6], h[7]);
-      fl.x = pack_bf16x2(f[8 * g + 0], f[8 * g + 1]);
-      fl.y = pack_bf16x2(f[8 * g + 2], f[8 * g + 3]);
-      fl.z = pack_bf16x2(f[8 * g + 4], f[8 * g + 5]);
-      fl.w = pack_bf16x2(f[8 * g + 6], f[8 * g + 7]);
-      *reinterpret_cast<uint4 *>(smem + P::OFF_XS + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
-      *reinterpret_cast<uint4 *>(smem + P::OFF_XF + row * (D * 2) + d0 * 2) = fl;
+        for (int i = 0; i < 8; ++i) h[i] = f[8 * gq + i] * rs * s_norm[d0 + i];
+        xh.x = pack_bf16x2(h[0], h[1]);
+        xh.y = pack_bf16x2(h[2], h[3]);
+        xh.z = pack_bf16x2(h[4], h[5]);
+        xh.w = pack_bf16x2(h[6], h[7]);
+        fl.x = pack_bf16x2(f[8 * gq + 0], f[8 * gq + 1]);
+        fl.y = pack_bf16x2(f[8 * gq + 2], f[8 * gq + 3]);
+        fl.z = pack_bf16x2(f[8 * gq + 4], f[8 * gq + 5]);
+        fl.w = pack_bf16x2(f[8 * gq + 6], f[8 * gq + 7]);
+        *reinterpret_cast<uint4 *>(gs + P::G_XS + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
+        *reinterpret_cast<uint4 *>(gs + P::G_FL + row * (D * 2) + d0 * 2) = fl;
+      }
     }
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
-    __syncthreads();
+    group_sync(bar_group);
     LNET_TRACE(3);
-    // 4. drive GEMM, mode-major: lanes = modes (repeated every 64 lanes), columns = steps
-    if (tid == 0) {
+    // 4. drive GEMM, mode-major: lanes = modes, columns = steps (overwrites the stem acc)
+    if (ltid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 128);
       for (int part = 0; part < 2; ++part)
-        issue_gemm(tbase + 128 + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
-                   P::SLAB_AD, s_base + P::OFF_XS, P::SLAB_XH, D / 16, idesc, false);
+        issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
+                   P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
     }
     wait_mma(mbar, phase, a.error);
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
-    chunk_scan<M, true>(tbase, 128, 256, n, b, chunk, a.n_chunks, s_k, a.rec, a.flags, a.error,
-                        smem + P::OFF_XS, P::SLAB_S, s_scan,
-                        a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id);
+    chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
+                                     a.n_chunks, s_k, a.rec, a.flags, a.error, gs + P::G_XS,
+                                     P::SLAB_S, s_scan,
+                                     a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace,
+                                     a.kernel_id);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
-    __syncthreads();
+    group_sync(bar_group);
     LNET_TRACE(5);
     // 6. synthesis GEMM (token-major) into columns [0, D)
-    if (tid == 0) {
+    if (ltid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
-      issue_gemm(tbase, s_base + P::OFF_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
+      issue_gemm(tbase, g_base + P::G_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
     }
@@ -745,9 +813,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
       if (row < n) {
         __nv_bfloat16 *dst = a.out + ((b * a.T + t0 + row) * D + half * HD);
 #pragma unroll
-        for (int g = 0; g < HD / 8; ++g) {
-          const int d0 = half * HD + 8 * g;
-          uint4 fl = *reinterpret_cast<const uint4 *>(smem + P::OFF_XF + row * (D * 2) + d0 * 2);
+        for (int gq = 0; gq < HD / 8; ++gq) {
+          const int d0 = half * HD + 8 * gq;
+          uint4 fl = *reinterpret_cast<const uint4 *>(gs + P::G_FL + row * (D * 2) + d0 * 2);
           const __nv_bfloat16 *fv = reinterpret_cast<const __nv_bfloat16 *>(&fl);
           float o[8];
 #pragma unroll
@@ -755,26 +823,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_writer_kernel(FusedArg
             const int d = d0 + i;
             const float x = __bfloat162float(fv[i]);
             const float xh = x * rsr * s_norm[d];
-            o[i] = x + s_ls[d] * (modal[8 * g + i] + s_ds[d] * xh);
+            o[i] = x + s_ls[d] * (modal[8 * gq + i] + s_ds[d] * xh);
           }
           uint4 ov;
           ov.x = pack_bf16x2(o[0], o[1]);
           ov.y = pack_bf16x2(o[2], o[3]);
           ov.z = pack_bf16x2(o[4], o[5]);
           ov.w = pack_bf16x2(o[6], o[7]);
-          *reinterpret_cast<uint4 *>(dst + 8 * g) = ov;
+          *reinterpret_cast<uint4 *>(dst + 8 * gq) = ov;
         }
       }
     }
     sm100::tc_fence_before();
-    __syncthreads();
+    group_sync(bar_group);
     LNET_TRACE(7);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
   __syncthreads();
-  if (warp == 0) {
+  if (tid < 32) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tbase, P::TMEM_COLS);
+    sm100::tmem_dealloc(*tmem_slot, P::TMEM_COLS);
   }
 }
 
@@ -899,9 +967,9 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     wait_mma(mbar, phase, a.error);
     LNET_TRACE(4);
     // 4. scan + look-back + moments
-    chunk_scan<M, false>(tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec, a.flags, a.error,
-                         nullptr, 0, s_scan, a.partial + (b * a.n_chunks + chunk) * 7 * M,
-                         a.trace, a.kernel_id);
+    chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
+                            a.flags, a.error, nullptr, 0, s_scan,
+                            a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id);
     sm100::tc_fence_before();
     __syncthreads();
     LNET_TRACE(5);
@@ -997,8 +1065,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, WP::BYTES),
                       "cudaFuncSetAttribute(fused_writer_kernel)"));
   const int64_t items = B * nch;
-  fused_writer_kernel<C, D, M><<<(unsigned)std::min<int64_t>(items, sms), kFusedThreads,
-                                 WP::BYTES, st>>>(wa);
+  fused_writer_kernel<C, D, M><<<(unsigned)std::min<int64_t>(cdiv(items, kWriterStreams), sms),
+                                 kFusedThreads * kWriterStreams, WP::BYTES, st>>>(wa);
   LNET_TRY(after_launch("fused_writer_kernel"));
   FusedArgs ra = wa;
   ra.in = w.stream;
