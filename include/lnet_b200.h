@@ -115,6 +115,18 @@ int lnet_b200_set_route(int route);
 int lnet_b200_alphabet_route(const lnet_b200_alphabet_params *params,
                              const lnet_b200_alphabet_request *req);
 
+/* Device-side status of the last lnet_b200_alphabet_forward that ran the fused
+ * route in `workspace` (synchronises the device; 0 for the general route).
+ * Every wait inside the fused kernels is bounded; a wait that gave up sets a
+ * bit: 1 << 0..3 MMA completion (writer stem, writer drive, writer synthesis,
+ * reader drive), 1 << 4 / 1 << 5 look-back (writer / reader).  Nonzero means the
+ * results of that call are invalid.  No reference counterpart (the reference
+ * has no device-side waits). */
+int lnet_b200_alphabet_device_status(const lnet_b200_alphabet_params *params,
+                                     const lnet_b200_alphabet_request *req,
+                                     const void *workspace, size_t workspace_bytes,
+                                     uint32_t *status);
+
 /* Stage entry points (same request/params conventions; intermediate tensors
  * fp32 [B, T, D] unless noted). */
 

@@ -279,6 +279,23 @@ extern "C" int lnet_b200_alphabet_route(const lnet_b200_alphabet_params *params,
   return use_fused(params, req) ? 0 : 1;
 }
 
+extern "C" int lnet_b200_alphabet_device_status(const lnet_b200_alphabet_params *params,
+                                                const lnet_b200_alphabet_request *req,
+                                                const void *workspace, size_t workspace_bytes,
+                                                uint32_t *status) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (!status) return fail(LNET_ERR_INVALID_ARGUMENT, "status must not be NULL");
+  *status = 0;
+  if (!use_fused(params, req) || req->batch == 0 || req->steps == 0) return LNET_OK;
+  Plan pl;
+  LNET_TRY(plan_all(params, req, const_cast<void *>(workspace), workspace_bytes, pl, true));
+  const uint32_t *err = pl.fused.flags + 2 * req->batch * fused_chunks(req->steps) + 2;
+  return cuda_check(cudaMemcpy(status, err, sizeof(uint32_t), cudaMemcpyDeviceToHost),
+                    "cudaMemcpy(device status)");
+}
+
 extern "C" int lnet_b200_alphabet_workspace_size(const lnet_b200_alphabet_params *params,
                                                  const lnet_b200_alphabet_request *req,
                                                  size_t *bytes) {

@@ -43,9 +43,12 @@ constexpr int kHalo = 8;
 constexpr int kTaps = 5;
 constexpr int kXRows = kChunk + 2 * kHalo;
 constexpr int kFusedThreads = 256;
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSpinLimit = 1u << 20;
 constexpr uint32_t kFlagAgg = 1, kFlagIncl = 2;
-constexpr uint32_t kErrMbar = 1, kErrLookback = 2;
+// Device error bits (first error word of the fused route's flag block):
+// bit 0..3: an MMA completion wait gave up (writer stem, writer drive, writer
+// synthesis, reader drive); bit 4 / 5: a look-back wait gave up (writer / reader).
+constexpr uint32_t kErrLookback = 1u << 4;
 
 // Per-block pole constants (floats, M entries each), SUB = steps per scan
 // sub-chunk of the block (64 writer, 32 reader):
@@ -420,7 +423,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
       const int64_t prev = item - 1;
       const uint32_t st = wait_flag(flags, prev);
       if (st == 0) {
-        if (ltid == pub_tid) atomicOr(error, kErrLookback);
+        if (ltid == pub_tid) atomicOr(error, kErrLookback << kid);
       } else if (st == kFlagIncl) {
         const float *pr = rec + prev * 16 * M + 8 * M;
 #pragma unroll
@@ -437,7 +440,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
           const int64_t qi = row * n_chunks + qq;
           const uint32_t sq = wait_flag(flags, qi);
           if (sq == 0) {
-            if (ltid == pub_tid) atomicOr(error, kErrLookback);
+            if (ltid == pub_tid) atomicOr(error, kErrLookback << kid);
             break;
           }
           const float *qr = rec + qi * 16 * M + (sq == kFlagIncl ? 8 * M : 0);
@@ -592,9 +595,10 @@ __device__ __forceinline__ void issue_gemm(uint32_t d_tmem, uint32_t a_addr, int
   }
 }
 
-__device__ __forceinline__ void wait_mma(uint64_t *mbar, uint32_t &phase, uint32_t *error) {
+__device__ __forceinline__ void wait_mma(uint64_t *mbar, uint32_t &phase, uint32_t *error,
+                                         uint32_t site) {
   if (!sm100::mbar_wait_bounded(mbar, phase, kSpinLimit)) {
-    if (threadIdx.x % 256 == 0) atomicOr(error, kErrMbar);
+    if (threadIdx.x % 256 == 0) atomicOr(error, 1u << site);
   }
   phase ^= 1u;
   sm100::tc_fence_after();
@@ -729,7 +733,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                    s_base + P::OFF_Q + k * (C / 8) * P::SLAB_Q, P::SLAB_Q, C / 16, idesc, k > 0);
       sm100::mma_commit(mbar);
     }
-    wait_mma(mbar, phase, a.error);
+    wait_mma(mbar, phase, a.error, 0);
     LNET_TRACE(2);
     // 3. bias + SiLU + RMSNorm (thread per step, two column halves)
     {
@@ -780,7 +784,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                    P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
     }
-    wait_mma(mbar, phase, a.error);
+    wait_mma(mbar, phase, a.error, 1);
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
     chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
@@ -800,7 +804,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                  idesc, false);
       sm100::mma_commit(mbar);
     }
-    wait_mma(mbar, phase, a.error);
+    wait_mma(mbar, phase, a.error, 2);
     LNET_TRACE(6);
     // 7. residual epilogue: v = fl + ls * (modal + ds * xhat), xhat = fl * rs * g
     {
@@ -964,7 +968,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
                    P::SLAB_AD, s_base + P::OFF_XH, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
     }
-    wait_mma(mbar, phase, a.error);
+    wait_mma(mbar, phase, a.error, 3);
     LNET_TRACE(4);
     // 4. scan + look-back + moments
     chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,

@@ -85,6 +85,11 @@ SIGNATURES = {
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
          _c_p, _c_p, _c_p, _c_p],
     ),
+    "lnet_b200_alphabet_device_status": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
+         ctypes.POINTER(ctypes.c_uint32)],
+    ),
     "lnet_b200_set_route": (ctypes.c_int, [ctypes.c_int]),
     "lnet_b200_alphabet_route": (
         ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest)]
