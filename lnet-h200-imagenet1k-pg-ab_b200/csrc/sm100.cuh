@@ -22,7 +22,7 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -31,6 +31,8 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with `parity` to complete; gives up after `limit` polls.
+// test_wait never suspends the thread, so the bound is a bound in time too
+// (try_wait may block for an implementation-defined interval per poll).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   uint32_t limit) {
   for (uint32_t i = 0; i < limit; ++i) {
