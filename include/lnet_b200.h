@@ -227,6 +227,9 @@ int lnet_b200_profile_read(char *names_buf, int names_bytes, float *total_ms, in
  * torch.profiler, src/lnet/pac_launch_tuning.py). */
 int lnet_b200_trace_enable(int on);
 int lnet_b200_trace_read(unsigned long long *out /* [2][16] */);
+/* Same, ordered on `stream` only (out must be pinned host memory): observes the
+ * counters of fused kernels still running on another stream. */
+int lnet_b200_trace_read_async(unsigned long long *out, lnet_stream_t stream);
 
 /* Message of the last error on the calling thread ("" if none). */
 const char *lnet_b200_last_error(void);

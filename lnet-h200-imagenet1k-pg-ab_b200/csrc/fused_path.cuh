@@ -700,6 +700,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   constexpr int HD = D / 2;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (lwarp & 3)) << 16);
   const int64_t total = a.B * a.n_chunks;
+  if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
 
   unsigned long long t_last = clock64();
   for (;;) {
@@ -843,6 +844,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     LNET_TRACE(7);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
+  if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
   __syncthreads();
   if (tid < 32) {
     sm100::tc_fence_after();
@@ -1175,4 +1177,16 @@ extern "C" int lnet_b200_trace_read(unsigned long long *out) {
   return lnet::cuda_check(
       cudaMemcpyFromSymbol(out, lnet::g_fused_trace, 32 * sizeof(unsigned long long)),
       "cudaMemcpyFromSymbol(g_fused_trace)");
+}
+
+// Same as lnet_b200_trace_read, ordered on `stream` only (pinned `out`), so it can
+// observe the counters of kernels still running on another stream.
+extern "C" int lnet_b200_trace_read_async(unsigned long long *out, lnet_stream_t stream) {
+  if (!out) return lnet::fail(LNET_ERR_INVALID_ARGUMENT, "out is NULL");
+  cudaStream_t st = (cudaStream_t)stream;
+  LNET_TRY(lnet::cuda_check(cudaMemcpyFromSymbolAsync(out, lnet::g_fused_trace,
+                                                      32 * sizeof(unsigned long long), 0,
+                                                      cudaMemcpyDeviceToHost, st),
+                            "cudaMemcpyFromSymbolAsync(g_fused_trace)"));
+  return lnet::cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
 }

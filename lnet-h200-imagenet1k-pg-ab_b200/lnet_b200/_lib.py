@@ -129,6 +129,7 @@ SIGNATURES = {
     ),
     "lnet_b200_trace_enable": (ctypes.c_int, [ctypes.c_int]),
     "lnet_b200_trace_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
+    "lnet_b200_trace_read_async": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ulonglong), _c_p]),
     "lnet_b200_last_launch_count": (ctypes.c_int, []),
     "lnet_b200_profile_enable": (None, [ctypes.c_int]),
     "lnet_b200_profile_read": (
