@@ -1155,6 +1155,7 @@ inline int fused_head(const lnet_b200_alphabet_params *p, int64_t B, const float
 
 namespace lnet {
 static int g_trace_on = 0;
+static unsigned long long *g_trace_dev = nullptr;
 int fused_trace_enabled() { return g_trace_on; }
 }  // namespace lnet
 
@@ -1163,6 +1164,10 @@ int fused_trace_enabled() { return g_trace_on; }
 extern "C" int lnet_b200_trace_enable(int on) {
   lnet::g_trace_on = on != 0;
   if (on) {
+    void *p = nullptr;
+    LNET_TRY(lnet::cuda_check(cudaGetSymbolAddress(&p, lnet::g_fused_trace),
+                              "cudaGetSymbolAddress(g_fused_trace)"));
+    lnet::g_trace_dev = static_cast<unsigned long long *>(p);
     unsigned long long zero[32] = {};
     return lnet::cuda_check(cudaMemcpyToSymbol(lnet::g_fused_trace, zero, sizeof(zero)),
                             "cudaMemcpyToSymbol(g_fused_trace)");
@@ -1180,13 +1185,14 @@ extern "C" int lnet_b200_trace_read(unsigned long long *out) {
 }
 
 // Same as lnet_b200_trace_read, ordered on `stream` only (pinned `out`), so it can
-// observe the counters of kernels still running on another stream.
+// observe the counters of kernels still running on another stream.  Call
+// lnet_b200_trace_enable(1) first (it resolves the counters' device address).
 extern "C" int lnet_b200_trace_read_async(unsigned long long *out, lnet_stream_t stream) {
   if (!out) return lnet::fail(LNET_ERR_INVALID_ARGUMENT, "out is NULL");
+  if (!lnet::g_trace_dev) return lnet::fail(LNET_ERR_INVALID_ARGUMENT, "tracing not enabled");
   cudaStream_t st = (cudaStream_t)stream;
-  LNET_TRY(lnet::cuda_check(cudaMemcpyFromSymbolAsync(out, lnet::g_fused_trace,
-                                                      32 * sizeof(unsigned long long), 0,
-                                                      cudaMemcpyDeviceToHost, st),
-                            "cudaMemcpyFromSymbolAsync(g_fused_trace)"));
+  LNET_TRY(lnet::cuda_check(cudaMemcpyAsync(out, lnet::g_trace_dev, 32 * sizeof(unsigned long long),
+                                            cudaMemcpyDeviceToHost, st),
+                            "cudaMemcpyAsync(trace)"));
   return lnet::cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
 }
