@@ -849,6 +849,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   if (tid < 32) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(*tmem_slot, P::TMEM_COLS);
+    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1ull);
   }
 }
 
@@ -895,6 +896,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   const int half = warp >> 2;
   constexpr int HD = D / 2;
   const int64_t total = a.B * a.n_chunks;
+  if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
 
   unsigned long long t_last = clock64();
   for (;;) {
@@ -981,10 +983,12 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     LNET_TRACE(5);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
+  if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
   __syncthreads();
   if (warp == 0) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tbase, P::TMEM_COLS);
+    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1ull);
   }
 }
 
