@@ -845,11 +845,13 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
   if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
+  if (a.trace && lane == 0) atomicAdd(&g_fused_trace[a.kernel_id][8], 1ull);
   __syncthreads();
+  if (a.trace && lane == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1ull);
   if (tid < 32) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(*tmem_slot, P::TMEM_COLS);
-    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1ull);
+    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1000ull);
   }
 }
 
