@@ -307,8 +307,12 @@ __device__ __forceinline__ uint32_t wait_flag(const uint32_t *flags, int64_t idx
 // live in TMEM columns [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's
 // moment partial sums [7][M] to `partial`.
 
+// Named barrier over one 256-thread item stream.  The non-aligned form counts
+// threads, so it stays correct when a warp reaches it diverged (e.g. after a
+// single-lane MMA issue); the aligned `bar.sync` would count each divergent
+// part of a warp as a separate warp arrival.
 __device__ __forceinline__ void group_sync(int id) {
-  asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory");
+  asm volatile("barrier.sync %0, 256;" ::"r"(id) : "memory");
 }
 
 template <int M, bool WRITE_STATES, int NSUB>
@@ -413,7 +417,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         my[(2 * k + 1) * M + m] = g_i[k];
       }
     }
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_lb) : "memory");
+    asm volatile("barrier.sync %0, 64;" ::"r"(bar_lb) : "memory");
     if (ltid == pub_tid) {
       __threadfence();
       sm100::st_release(flags + item, kFlagAgg);
@@ -476,7 +480,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
       }
     }
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_lb) : "memory");
+    asm volatile("barrier.sync %0, 64;" ::"r"(bar_lb) : "memory");
     if (ltid == pub_tid) {
       __threadfence();
       sm100::st_release(flags + item, kFlagIncl);
