@@ -354,25 +354,41 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   const int len = scanner ? max(0, min(SUB, n - s0)) : 0;
   const float ar = K[mk], ai = K[M + mk];
 
-  // ---- pass 1: sub-chunk local scan from zero
+  // ---- pass 1: sub-chunk local scan from zero (32-step pieces: 4 TMEM loads, one wait)
   float sr = 0.f, si = 0.f;
   float l_r[4] = {0, 0, 0, 0}, l_i[4] = {0, 0, 0, 0};  // l[0] = last state
-  for (int c0 = 0; c0 < len; c0 += 16) {
-    float ur[16], ui[16];
+  for (int c0 = 0; c0 < len; c0 += 32) {
+    float ur[32], ui[32];
     sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
+    sm100::tmem_ld16(lane_addr + col_re + s0 + c0 + 16, ur + 16);
     sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
+    sm100::tmem_ld16(lane_addr + col_im + s0 + c0 + 16, ui + 16);
     sm100::tmem_ld_wait();
+    if (c0 + 32 <= len) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (c0 + i < len) {
+      for (int i = 0; i < 32; ++i) {
         float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
         float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
         sr = nr;
         si = ni;
-        l_r[3] = l_r[2]; l_i[3] = l_i[2];
-        l_r[2] = l_r[1]; l_i[2] = l_i[1];
-        l_r[1] = l_r[0]; l_i[1] = l_i[0];
-        l_r[0] = sr; l_i[0] = si;
+        if (i >= 28) {
+          l_r[31 - i] = sr;
+          l_i[31 - i] = si;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (c0 + i < len) {
+          float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
+          float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
+          sr = nr;
+          si = ni;
+          l_r[3] = l_r[2]; l_i[3] = l_i[2];
+          l_r[2] = l_r[1]; l_i[2] = l_i[1];
+          l_r[1] = l_r[0]; l_i[1] = l_i[0];
+          l_r[0] = sr; l_i[0] = si;
+        }
       }
     }
   }
@@ -520,50 +536,51 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   sr = cr;
   si = ci;
   cmac(pqr, pqi, car, cai, sr, si);
-  const bool hist = chunk > 0 || q > 0;
+  // History before the sequence start is exactly zero (the carry of chunk 0 is
+  // zero), so lag products that reach before step 0 contribute nothing and
+  // need no guard; the counts T - lag are applied when the moments are finalised.
   float h1r = h_r[0], h1i = h_i[0], h2r = h_r[1], h2i = h_i[1];
   float h3r = h_r[2], h3i = h_i[2], h4r = h_r[3], h4i = h_i[3];
   float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
-  for (int c0 = 0; c0 < len; c0 += 16) {
-    float ur[16], ui[16];
-    sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
-    sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
-    sm100::tmem_ld_wait();
-#pragma unroll
-    for (int i0 = 0; i0 < 16; ++i0) {
-      const int i = c0 + i0;
-      if (i < len) {
-        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i0]));
-        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i0]));
-        sr = nr;
-        si = ni;
-        e = fmaf(sr, sr, fmaf(si, si, e));
-        if (hist || i >= 1) {
-          c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
-          c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
-        }
-        if (hist || i >= 2) {
-          c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
-          c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
-        }
-        if (hist || i >= 4) {
-          c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
-          c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
-        }
-        h4r = h3r; h4i = h3i;
-        h3r = h2r; h3i = h2i;
-        h2r = h1r; h2i = h1i;
-        h1r = sr; h1i = si;
-        if constexpr (WRITE_STATES) {
-          if (live) {
-            const int t = s0 + i;
-            *reinterpret_cast<__nv_bfloat16 *>(s_slab + (m / 8) * slab_s + t * 16 +
-                                               (m % 8) * 2) = __float2bfloat16_rn(sr);
-            *reinterpret_cast<__nv_bfloat16 *>(s_slab + ((M + m) / 8) * slab_s + t * 16 +
-                                               ((M + m) % 8) * 2) = __float2bfloat16_rn(si);
-          }
-        }
+  auto step2 = [&](float u_re, float u_im, int t) {
+    float nr = fmaf(ar, sr, fmaf(-ai, si, u_re));
+    float ni = fmaf(ai, sr, fmaf(ar, si, u_im));
+    sr = nr;
+    si = ni;
+    e = fmaf(sr, sr, fmaf(si, si, e));
+    c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
+    c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
+    c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
+    c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
+    c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
+    c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
+    h4r = h3r; h4i = h3i;
+    h3r = h2r; h3i = h2i;
+    h2r = h1r; h2i = h1i;
+    h1r = sr; h1i = si;
+    if constexpr (WRITE_STATES) {
+      if (live) {
+        *reinterpret_cast<__nv_bfloat16 *>(s_slab + (m / 8) * slab_s + t * 16 + (m % 8) * 2) =
+            __float2bfloat16_rn(sr);
+        *reinterpret_cast<__nv_bfloat16 *>(s_slab + ((M + m) / 8) * slab_s + t * 16 +
+                                           ((M + m) % 8) * 2) = __float2bfloat16_rn(si);
       }
+    }
+  };
+  for (int c0 = 0; c0 < len; c0 += 32) {
+    float ur[32], ui[32];
+    sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
+    sm100::tmem_ld16(lane_addr + col_re + s0 + c0 + 16, ur + 16);
+    sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
+    sm100::tmem_ld16(lane_addr + col_im + s0 + c0 + 16, ui + 16);
+    sm100::tmem_ld_wait();
+    if (c0 + 32 <= len) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) step2(ur[i], ui[i], s0 + c0 + i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (c0 + i < len) step2(ur[i], ui[i], s0 + c0 + i);
     }
   }
   mark(12);
