@@ -275,6 +275,38 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+
+// Loads rows [t0 - 8, t0 + 136) of one batch row of a [B, T, W] bf16 tensor
+// (W = 8 * CHUNKS) into shared memory, zero outside [0, T): all global loads of
+// a thread are issued before its shared-memory stores.  `dst(r, kc)` gives the
+// destination of 16-byte chunk kc of tile row r.
+template <int CHUNKS, typename Dst>
+__device__ __forceinline__ void load_rows(const __nv_bfloat16 *src, int64_t b, int64_t T,
+                                          int64_t t0, int ltid, Dst dst) {
+  constexpr int TOTAL = kXRows * CHUNKS;
+  constexpr int PER = (TOTAL + kFusedThreads - 1) / kFusedThreads;
+  uint4 v[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = ltid + k * kFusedThreads;
+    v[k] = make_uint4(0, 0, 0, 0);
+    if (i < TOTAL) {
+      const int r = i / CHUNKS, kc = i - (i / CHUNKS) * CHUNKS;
+      const int64_t tok = t0 - kHalo + r;
+      if (tok >= 0 && tok < T)
+        v[k] = __ldcg(reinterpret_cast<const uint4 *>(src + ((b * T + tok) * (8 * CHUNKS) + kc * 8)));
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = ltid + k * kFusedThreads;
+    if (i < TOTAL) {
+      const int r = i / CHUNKS, kc = i - (i / CHUNKS) * CHUNKS;
+      *reinterpret_cast<uint4 *>(dst(r, kc)) = v[k];
+    }
+  }
+}
+
 // SiLU with the hardware exponential (relative error ~1e-6, far inside the
 // bf16 activation rounding of this route).
 __device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
@@ -542,7 +574,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   float h1r = h_r[0], h1i = h_i[0], h2r = h_r[1], h2i = h_i[1];
   float h3r = h_r[2], h3i = h_i[2], h4r = h_r[3], h4i = h_i[3];
   float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
-  auto step2 = [&](float u_re, float u_im, int t) {
+  auto step2 = [&](float u_re, float u_im) {
     float nr = fmaf(ar, sr, fmaf(-ai, si, u_re));
     float ni = fmaf(ai, sr, fmaf(ar, si, u_im));
     sr = nr;
@@ -558,14 +590,11 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     h3r = h2r; h3i = h2i;
     h2r = h1r; h2i = h1i;
     h1r = sr; h1i = si;
-    if constexpr (WRITE_STATES) {
-      if (live) {
-        *reinterpret_cast<__nv_bfloat16 *>(s_slab + (m / 8) * slab_s + t * 16 + (m % 8) * 2) =
-            __float2bfloat16_rn(sr);
-        *reinterpret_cast<__nv_bfloat16 *>(s_slab + ((M + m) / 8) * slab_s + t * 16 +
-                                           ((M + m) % 8) * 2) = __float2bfloat16_rn(si);
-      }
-    }
+  };
+  // State slab for the synthesis GEMM, M-major (steps contiguous): element
+  // (t, j) at (j / 8) * slab_s + (t / 8) * 128 + (j % 8) * 16 + (t % 8) * 2.
+  auto s_addr = [&](int t, int j) {
+    return s_slab + (j / 8) * slab_s + (t / 8) * 128 + (j % 8) * 16 + (t % 8) * 2;
   };
   for (int c0 = 0; c0 < len; c0 += 32) {
     float ur[32], ui[32];
@@ -576,11 +605,41 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     sm100::tmem_ld_wait();
     if (c0 + 32 <= len) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) step2(ur[i], ui[i], s0 + c0 + i);
+      for (int g8 = 0; g8 < 4; ++g8) {
+        float br[8], bi[8];
+#pragma unroll
+        for (int i8 = 0; i8 < 8; ++i8) {
+          step2(ur[8 * g8 + i8], ui[8 * g8 + i8]);
+          br[i8] = sr;
+          bi[i8] = si;
+        }
+        if constexpr (WRITE_STATES) {
+          if (live) {
+            const int t = s0 + c0 + 8 * g8;
+            uint4 vr, vi;
+            vr.x = pack_bf16x2(br[0], br[1]); vr.y = pack_bf16x2(br[2], br[3]);
+            vr.z = pack_bf16x2(br[4], br[5]); vr.w = pack_bf16x2(br[6], br[7]);
+            vi.x = pack_bf16x2(bi[0], bi[1]); vi.y = pack_bf16x2(bi[2], bi[3]);
+            vi.z = pack_bf16x2(bi[4], bi[5]); vi.w = pack_bf16x2(bi[6], bi[7]);
+            *reinterpret_cast<uint4 *>(s_addr(t, m)) = vr;
+            *reinterpret_cast<uint4 *>(s_addr(t, M + m)) = vi;
+          }
+        }
+      }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (c0 + i < len) step2(ur[i], ui[i], s0 + c0 + i);
+      for (int i = 0; i < 32; ++i) {
+        if (c0 + i < len) {
+          step2(ur[i], ui[i]);
+          if constexpr (WRITE_STATES) {
+            if (live) {
+              const int t = s0 + c0 + i;
+              *reinterpret_cast<__nv_bfloat16 *>(s_addr(t, m)) = __float2bfloat16_rn(sr);
+              *reinterpret_cast<__nv_bfloat16 *>(s_addr(t, M + m)) = __float2bfloat16_rn(si);
+            }
+          }
+        }
+      }
     }
   }
   mark(12);
@@ -655,7 +714,7 @@ struct WriterPlan {
   static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, ScanLayout<kWriterNSub>::FLOATS * 4);
   static constexpr int FL_BYTES = kChunk * D * 2;
   static constexpr int SLAB_XH = kChunk * 16;
-  static constexpr int SLAB_S = kChunk * 16 + 16;
+  static constexpr int SLAB_S = kChunk * 16;  // state slab: one 8-column K group, M-major
   static constexpr int XS_BYTES = cmax((D / 8) * SLAB_XH, (2 * M / 8) * SLAB_S);
   static constexpr int G_X = 0;                       // x tile, then scan scratch
   static constexpr int G_FL = G_X + X_BYTES;          // bf16 [128][D] stem output
@@ -735,14 +794,8 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     const int n = (int)min((int64_t)kChunk, a.T - t0);
 
     // 1. x tile (zero outside [0, T))
-    for (int i = ltid; i < kXRows * (C / 8); i += kFusedThreads) {
-      int r = i / (C / 8), kc = i - (i / (C / 8)) * (C / 8);
-      int64_t tok = t0 - kHalo + r;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (tok >= 0 && tok < a.T)
-        v = __ldg(reinterpret_cast<const uint4 *>(a.in + ((b * a.T + tok) * C + kc * 8)));
-      *reinterpret_cast<uint4 *>(gs + P::G_X + kc * P::SLAB_X + r * 16) = v;
-    }
+    load_rows<C / 8>(a.in, b, a.T, t0, ltid,
+                     [&](int r, int kc) { return gs + P::G_X + kc * P::SLAB_X + r * 16; });
     sm100::fence_proxy_async_smem();
     group_sync(bar_group);
     LNET_TRACE(1);
@@ -821,7 +874,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     // 6. synthesis GEMM (token-major) into columns [0, D)
     if (ltid == 0) {
       sm100::tc_fence_after();
-      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D, /*a_mn_major=*/true);
       issue_gemm(tbase, g_base + P::G_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
@@ -933,14 +986,8 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     const int n = (int)min((int64_t)kChunk, a.T - t0);
 
     // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T)
-    for (int i = tid; i < kXRows * (D / 8); i += kFusedThreads) {
-      int r = i / (D / 8), kc = i - (i / (D / 8)) * (D / 8);
-      int64_t tok = t0 - kHalo + r;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (tok >= 0 && tok < a.T)
-        v = __ldcg(reinterpret_cast<const uint4 *>(a.in + ((b * a.T + tok) * D + kc * 8)));
-      *reinterpret_cast<uint4 *>(smem + P::OFF_V + r * P::PITCH + kc * 16) = v;
-    }
+    load_rows<D / 8>(a.in, b, a.T, t0, tid,
+                     [&](int r, int kc) { return smem + P::OFF_V + r * P::PITCH + kc * 16; });
     __syncthreads();
     LNET_TRACE(1);
     // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm

@@ -87,10 +87,12 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
 }
 
 // Instruction descriptor of kind::f16 with bf16 A/B, fp32 accumulate, K-major A and B.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+// `a_mn_major`: A stored M-major (M contiguous within 8-element core rows) instead of K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool a_mn_major = false) {
   return (1u << 4)                        // D format f32
          | (1u << 7)                      // A format bf16
          | (1u << 10)                     // B format bf16
+         | ((a_mn_major ? 1u : 0u) << 15) // A major-ness
          | ((uint32_t)(n >> 3) << 17)     // N / 8
          | ((uint32_t)(m >> 4) << 24);    // M / 16
 }
