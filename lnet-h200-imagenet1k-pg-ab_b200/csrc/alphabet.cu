@@ -8,6 +8,8 @@
 //     single chunked-scan kernels, used by lnet_b200_alphabet_forward when no
 //     time_delta is given and the shape fits the fused kernels.
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 
 #include "common.cuh"
 #include "fused_path.cuh"
@@ -16,6 +18,21 @@
 namespace lnet {
 
 constexpr int kScanChunk = 64;
+
+// Tag of the look-back records of one forward call.  Starts from a
+// time-derived value so that stale words left in a reused workspace by another
+// process are not mistaken for this call's (a collision needs an exact 32-bit
+// match); 0 is never used.
+static std::atomic<uint32_t> g_epoch{0};
+uint32_t next_epoch() {
+  uint32_t e = g_epoch.fetch_add(1) + 1;
+  if (e == 1) {
+    uint32_t seed = (uint32_t)std::chrono::steady_clock::now().time_since_epoch().count() | 1u;
+    g_epoch.store(seed);
+    e = seed;
+  }
+  return e == 0 ? next_epoch() : e;
+}
 
 int sm_count() {
   int dev = 0, n = 0;
@@ -291,7 +308,7 @@ extern "C" int lnet_b200_alphabet_device_status(const lnet_b200_alphabet_params 
   if (!use_fused(params, req) || req->batch == 0 || req->steps == 0) return LNET_OK;
   Plan pl;
   LNET_TRY(plan_all(params, req, const_cast<void *>(workspace), workspace_bytes, pl, true));
-  const uint32_t *err = pl.fused.flags + 2 * req->batch * fused_chunks(req->steps) + 2;
+  const uint32_t *err = pl.fused.flags + 2;
   return cuda_check(cudaMemcpy(status, err, sizeof(uint32_t), cudaMemcpyDeviceToHost),
                     "cudaMemcpy(device status)");
 }

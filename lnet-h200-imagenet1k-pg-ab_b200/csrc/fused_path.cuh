@@ -44,7 +44,6 @@ constexpr int kTaps = 5;
 constexpr int kXRows = kChunk + 2 * kHalo;
 constexpr int kFusedThreads = 256;
 constexpr uint32_t kSpinLimit = 1u << 20;
-constexpr uint32_t kFlagAgg = 1, kFlagIncl = 2;
 // Device error bits (first error word of the fused route's flag block):
 // bit 0..3: an MMA completion wait gave up (writer stem, writer drive, writer
 // synthesis, reader drive); bit 4 / 5: a look-back wait gave up (writer / reader).
@@ -84,9 +83,11 @@ struct FusedWorkspace {
   __nv_bfloat16 *stream = nullptr;     // [B, T, D]
   float *wpartial = nullptr;           // [B * nch][7M]
   float *rpartial = nullptr;
-  float *wrec = nullptr;               // [B * nch][2][4][2M]
-  float *rrec = nullptr;
-  uint32_t *flags = nullptr;           // [2][B * nch] + counters[2] + error[2]
+  // look-back records [B * nch][2 (aggregate, inclusive)][4 states][2 (re, im)][M];
+  // each entry = (state bits) | (epoch << 32), single-copy atomic 8-byte words
+  unsigned long long *wrec = nullptr;
+  unsigned long long *rrec = nullptr;
+  uint32_t *flags = nullptr;           // counters[2] + error[2]
   size_t flag_words = 0;
 };
 
@@ -105,9 +106,9 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   w.stream = ar.take<__nv_bfloat16>((size_t)B * r->steps * D);
   w.wpartial = ar.take<float>((size_t)B * nch * 7 * M);
   w.rpartial = ar.take<float>((size_t)B * nch * 7 * M);
-  w.wrec = ar.take<float>((size_t)B * nch * 16 * M);
-  w.rrec = ar.take<float>((size_t)B * nch * 16 * M);
-  w.flag_words = (size_t)2 * B * nch + 4;
+  w.wrec = ar.take<unsigned long long>((size_t)B * nch * 16 * M);
+  w.rrec = ar.take<unsigned long long>((size_t)B * nch * 16 * M);
+  w.flag_words = 4;
   w.flags = ar.take<uint32_t>(w.flag_words);
 }
 
@@ -237,8 +238,8 @@ struct FusedArgs {
   const float *conv_w, *conv_b, *norm, *ds, *ls;
   __nv_bfloat16 *out;       // writer stream
   float *partial;           // [B * nch][7M]
-  float *rec;               // [B * nch][2][4][2M]
-  uint32_t *flags;          // [B * nch]
+  unsigned long long *rec;  // [B * nch][2][4][2][M] tagged look-back records
+  uint32_t epoch;           // tag of this call's records
   uint32_t *counter;
   uint32_t *error;
   int trace;       // 1: accumulate per-phase cycles of CTA thread 0 into g_fused_trace
@@ -317,14 +318,16 @@ __device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, flo
   ci = fmaf(ar, bi, fmaf(ai, br, ci));
 }
 
-// Waits for the look-back flag of record `idx` to reach at least AGG; returns it (0 on timeout).
-__device__ __forceinline__ uint32_t wait_flag(const uint32_t *flags, int64_t idx) {
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    uint32_t st = sm100::ld_acquire(flags + idx);
-    if (st >= kFlagAgg) return st;
-    __nanosleep(32);
-  }
-  return 0;
+// Tagged look-back words: (fp32 bits) | (epoch << 32), written and read as one
+// 64-bit access (single-copy atomic), so a reader that sees this call's epoch
+// also sees the value written with it -- no flags and no fences are needed.
+__device__ __forceinline__ void st_tag(unsigned long long *p, float v, uint32_t epoch) {
+  __stcg(p, ((unsigned long long)epoch << 32) | __float_as_uint(v));
+}
+__device__ __forceinline__ bool ld_tag(const unsigned long long *p, uint32_t epoch, float &v) {
+  const unsigned long long x = __ldcg(p);
+  v = __uint_as_float((uint32_t)x);
+  return (uint32_t)(x >> 32) == epoch;
 }
 
 // ---------------------------------------------------------------- scan + look-back
@@ -351,7 +354,8 @@ template <int M, bool WRITE_STATES, int NSUB>
 __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, uint32_t tbase,
                                            int col_re, int col_im, int n, int64_t row,
                                            int64_t chunk, int64_t n_chunks, const float *K,
-                                           float *rec, uint32_t *flags, uint32_t *error,
+                                           unsigned long long *rec, uint32_t epoch,
+                                           uint32_t *error,
                                            uint8_t *s_slab, int slab_s, float *sc,
                                            float *partial, int trace, int kid) {
   using L = ScanLayout<NSUB>;
@@ -379,7 +383,6 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   }
   const bool live = scanner && m < M;
   const int mk = live ? m : 0;
-  const int pub_tid = NSUB == 4 ? 192 : 128;  // first thread of the last sub-chunk
   const bool publisher_group = scanner && q == NSUB - 1;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * Q) << 16);
   const int s0 = SUB * q;
@@ -447,91 +450,94 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     ci = ni;
   }
 
-  // ---- aggregate, look-back and inclusive record: threads of the last sub-chunk
-  if (publisher_group) {
+  // ---- aggregate, look-back and inclusive record: threads of the last sub-chunk.
+  // Record layout per item: [agg | incl][state k = 0..3][re | im][M]; state 0 is
+  // the chunk's last state.
+  if (publisher_group && live) {
     const int64_t item = row * n_chunks + chunk;  // record index (row-major)
-    float *my = rec + item * 16 * M;
+    unsigned long long *my = rec + item * 16 * M;
     float g_r[4], g_i[4];  // chunk-local last four states
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       g_r[k] = l_r[k];
       g_i[k] = l_i[k];
-      cmac(K[(KC_AS + 2 * k) * M + mk], K[(KC_AS + 2 * k + 1) * M + mk], cr, ci, g_r[k], g_i[k]);
-    }
-    if (live) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        my[(2 * k) * M + m] = g_r[k];
-        my[(2 * k + 1) * M + m] = g_i[k];
-      }
-    }
-    asm volatile("barrier.sync %0, 64;" ::"r"(bar_lb) : "memory");
-    if (ltid == pub_tid) {
-      __threadfence();
-      sm100::st_release(flags + item, kFlagAgg);
+      cmac(K[(KC_AS + 2 * k) * M + m], K[(KC_AS + 2 * k + 1) * M + m], cr, ci, g_r[k], g_i[k]);
+      st_tag(my + (2 * k) * M + m, g_r[k], epoch);
+      st_tag(my + (2 * k + 1) * M + m, g_i[k], epoch);
     }
     float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
     if (chunk > 0) {
-      const int64_t prev = item - 1;
-      const uint32_t st = wait_flag(flags, prev);
-      if (st == 0) {
-        if (ltid == pub_tid) atomicOr(error, kErrLookback << kid);
-      } else if (st == kFlagIncl) {
-        const float *pr = rec + prev * 16 * M + 8 * M;
+      const unsigned long long *pv = rec + (item - 1) * 16 * M;
+      const float aLr = K[KC_AL * M + m], aLi = K[(KC_AL + 1) * M + m];
+      bool done = false;
+      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+        bool ok = true;  // inclusive record of the previous chunk
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          p_r[k] = __ldcg(pr + (2 * k) * M + mk);
-          p_i[k] = __ldcg(pr + (2 * k + 1) * M + mk);
+          ok &= ld_tag(pv + 8 * M + (2 * k) * M + m, epoch, p_r[k]);
+          ok &= ld_tag(pv + 8 * M + (2 * k + 1) * M + m, epoch, p_i[k]);
         }
-      } else {
-        // X = true end state of chunk - 2, composed from aggregates back to an
-        // inclusive record (or the sequence start).
-        const float aLr = K[KC_AL * M + mk], aLi = K[(KC_AL + 1) * M + mk];
+        if (ok) {
+          done = true;
+          break;
+        }
+        ok = true;  // its aggregate, completed by the true end X of chunk - 2
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          ok &= ld_tag(pv + (2 * k) * M + m, epoch, p_r[k]);
+          ok &= ld_tag(pv + (2 * k + 1) * M + m, epoch, p_i[k]);
+        }
+        if (!ok) {
+          __nanosleep(32);
+          continue;
+        }
         float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
-        for (int64_t qq = chunk - 2; qq >= 0; --qq) {
-          const int64_t qi = row * n_chunks + qq;
-          const uint32_t sq = wait_flag(flags, qi);
-          if (sq == 0) {
-            if (ltid == pub_tid) atomicOr(error, kErrLookback << kid);
-            break;
+        bool walk_ok = true;
+        for (int64_t qq = chunk - 2; qq >= 0 && walk_ok; --qq) {
+          const unsigned long long *qv = rec + (row * n_chunks + qq) * 16 * M;
+          bool found = false;
+          for (uint32_t jt = 0; jt < kSpinLimit; ++jt) {
+            float er, ei;
+            if (ld_tag(qv + 8 * M + m, epoch, er) && ld_tag(qv + 9 * M + m, epoch, ei)) {
+              cmac(mr, mi, er, ei, xr, xi);
+              qq = -1;  // inclusive: the walk ends here
+              found = true;
+              break;
+            }
+            if (ld_tag(qv + m, epoch, er) && ld_tag(qv + M + m, epoch, ei)) {
+              cmac(mr, mi, er, ei, xr, xi);
+              float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
+              mr = nr;
+              mi = ni;
+              found = true;
+              break;
+            }
+            __nanosleep(32);
           }
-          const float *qr = rec + qi * 16 * M + (sq == kFlagIncl ? 8 * M : 0);
-          cmac(mr, mi, __ldcg(qr + mk), __ldcg(qr + M + mk), xr, xi);
-          if (sq == kFlagIncl) break;
-          float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
-          mr = nr;
-          mi = ni;
+          if (!found) walk_ok = false;
         }
-        const float *pa = rec + prev * 16 * M;
+        if (!walk_ok) break;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          p_r[k] = __ldcg(pa + (2 * k) * M + mk);
-          p_i[k] = __ldcg(pa + (2 * k + 1) * M + mk);
-          cmac(K[(KC_AL + 2 * k) * M + mk], K[(KC_AL + 2 * k + 1) * M + mk], xr, xi, p_r[k],
+        for (int k = 0; k < 4; ++k)
+          cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], xr, xi, p_r[k],
                p_i[k]);
-        }
+        done = true;
+      }
+      if (!done) {
+        atomicOr(error, kErrLookback << kid);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) p_r[k] = p_i[k] = 0.f;
       }
     }
-    if (live) {
-      // inclusive record (only consumed when the chunk is full)
+    // inclusive record (only consumed when the chunk is full)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float vr = g_r[k], vi = g_i[k];
-        cmac(K[(KC_AL + 2 * k) * M + mk], K[(KC_AL + 2 * k + 1) * M + mk], p_r[0], p_i[0], vr,
-             vi);
-        my[8 * M + (2 * k) * M + m] = vr;
-        my[8 * M + (2 * k + 1) * M + m] = vi;
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
-        sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
-      }
-    }
-    asm volatile("barrier.sync %0, 64;" ::"r"(bar_lb) : "memory");
-    if (ltid == pub_tid) {
-      __threadfence();
-      sm100::st_release(flags + item, kFlagIncl);
+    for (int k = 0; k < 4; ++k) {
+      float vr = g_r[k], vi = g_i[k];
+      cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], p_r[0], p_i[0], vr, vi);
+      st_tag(my + 8 * M + (2 * k) * M + m, vr, epoch);
+      st_tag(my + 8 * M + (2 * k + 1) * M + m, vi, epoch);
+      sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
+      sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
     }
   }
   group_sync(bar_group);
@@ -863,7 +869,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
     chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
-                                     a.n_chunks, s_k, a.rec, a.flags, a.error, gs + P::G_XS,
+                                     a.n_chunks, s_k, a.rec, a.epoch, a.error, gs + P::G_XS,
                                      P::SLAB_S, s_scan,
                                      a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace,
                                      a.kernel_id);
@@ -1046,7 +1052,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     LNET_TRACE(4);
     // 4. scan + look-back + moments
     chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
-                            a.flags, a.error, nullptr, 0, s_scan,
+                            a.epoch, a.error, nullptr, 0, s_scan,
                             a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id);
     sm100::tc_fence_before();
     __syncthreads();
@@ -1106,6 +1112,7 @@ inline bool fused_supported(const lnet_b200_alphabet_params *p,
 }
 
 int sm_count();
+uint32_t next_epoch();
 int fused_trace_enabled();
 
 template <int C, int D, int M>
@@ -1119,7 +1126,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   LNET_TRY(after_launch("fused_prepare_kernel"));
   LNET_TRY(cuda_check(cudaMemsetAsync(w.flags, 0, w.flag_words * sizeof(uint32_t), st),
                       "cudaMemsetAsync(flags)"));
-  uint32_t *counters = w.flags + 2 * B * nch;
+  uint32_t *counters = w.flags;
+  const uint32_t epoch = next_epoch();
   FusedArgs wa{};
   wa.in = (const __nv_bfloat16 *)r->x;
   wa.B = B;
@@ -1136,7 +1144,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.out = w.stream;
   wa.partial = w.wpartial;
   wa.rec = w.wrec;
-  wa.flags = w.flags;
+  wa.epoch = epoch;
   wa.counter = counters;
   wa.error = counters + 2;
   wa.trace = fused_trace_enabled();
@@ -1159,7 +1167,6 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   ra.out = nullptr;
   ra.partial = w.rpartial;
   ra.rec = w.rrec;
-  ra.flags = w.flags + B * nch;
   ra.counter = counters + 1;
   ra.kernel_id = 1;
   LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_reader_kernel<D, M>,
