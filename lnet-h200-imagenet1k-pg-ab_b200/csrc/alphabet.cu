@@ -246,13 +246,10 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
 
 static int head_run(const lnet_b200_alphabet_params *p, int64_t B, const float *wm,
                     const float *rm, float *feats, float *logits, cudaStream_t st) {
-  const int M = p->modes, K = p->output_dim;
+  const int M = p->modes;
   head_features_kernel<<<grid_for(B * 14 * M), 256, 0, st>>>(wm, rm, feats, B, M);
   LNET_TRY(after_launch("head_features_kernel"));
-  dim3 g((unsigned)cdiv(K, 8), (unsigned)B);
-  head_logits_kernel<<<g, 256, 0, st>>>(feats, p->head_weight, p->head_bias, logits, B, K,
-                                        14 * M);
-  return after_launch("head_logits_kernel");
+  return head_gemm(feats, B, 14 * M, p->head_weight, p->head_bias, logits, p->output_dim, st);
 }
 
 static int plan_all(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -354,7 +351,8 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
     float *wm = writer_moments ? writer_moments : pl.fused.moments;
     float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
     LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, st));
-    return fused_head(params, B, wm, rm, logits, st);
+    return head_gemm(pl.fused.feats, B, 14 * M, params->head_weight, params->head_bias, logits,
+                     params->output_dim, st);
   }
   LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
   float *wm = writer_moments ? writer_moments : pl.moments;

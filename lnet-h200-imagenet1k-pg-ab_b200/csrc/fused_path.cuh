@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "generic_kernels.cuh"
+#include "head_gemm.cuh"
 #include "sm100.cuh"
 
 namespace lnet {
@@ -75,6 +76,7 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 // ---------------------------------------------------------------- workspace
 struct FusedWorkspace {
   float *moments = nullptr;            // [2][B][7M]
+  float *feats = nullptr;              // [B][14M] radial-log features
   __nv_bfloat16 *q = nullptr;          // stem B operand   [5][C/8][D][8]
   __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][64][8]
   __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][128][8]
@@ -98,6 +100,7 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   const int C = p->raw_input_dim, D = p->model_dim, M = p->modes;
   const int64_t B = r->batch, nch = fused_chunks(std::max<int64_t>(r->steps, 1));
   w.moments = ar.take<float>((size_t)2 * B * 7 * M);
+  w.feats = ar.take<float>((size_t)B * 14 * M);
   w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
   w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * kWriterDriveRows);
   w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
@@ -1069,27 +1072,44 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
 }
 
 // ---------------------------------------------------------------- moments finalize
-// moments[blk][b][k*M + m] = sum_chunks partial / count   (count T or T - lag; 0 if T <= lag)
+// Per (row, block, mode): sums the chunk partials in order, divides by the
+// counts (T, or T - lag; 0 if T <= lag) and writes the raw moments
+// [b][k*M + m] and the radial-log features of src/lnet/alphabet.py:29-46 into
+// feats[b][blk * 7M + k*M + m].
 __global__ void fused_finalize_kernel(const float *__restrict__ wpart,
                                       const float *__restrict__ rpart, float *__restrict__ wm,
-                                      float *__restrict__ rm, int64_t steps, int modes,
-                                      int64_t n_chunks) {
+                                      float *__restrict__ rm, float *__restrict__ feats,
+                                      int64_t steps, int modes, int64_t n_chunks) {
   const int64_t b = blockIdx.x;
-  const float *part = blockIdx.y == 0 ? wpart : rpart;
-  float *out = blockIdx.y == 0 ? wm : rm;
+  const int blk = blockIdx.y;
+  const float *part = blk == 0 ? wpart : rpart;
+  float *out = blk == 0 ? wm : rm;
   const int lags[3] = {1, 2, 4};
-  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) {
-    const int kind = j / modes;
-    double acc = 0.0;
-    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)part[(b * n_chunks + c) * 7 * modes + j];
-    float v;
-    if (kind == 0) {
-      v = (float)(acc / (double)steps);
-    } else {
-      const int lag = lags[(kind - 1) / 2];
-      v = steps <= lag ? 0.f : (float)(acc / (double)(steps - lag));
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    float v[7];
+#pragma unroll
+    for (int k = 0; k < 7; ++k) {
+      double acc = 0.0;
+      for (int64_t c = 0; c < n_chunks; ++c)
+        acc += (double)part[(b * n_chunks + c) * 7 * modes + k * modes + m];
+      if (k == 0) {
+        v[k] = (float)(acc / (double)steps);
+      } else {
+        const int lag = lags[(k - 1) / 2];
+        v[k] = steps <= lag ? 0.f : (float)(acc / (double)(steps - lag));
+      }
+      out[b * 7 * modes + k * modes + m] = v[k];
     }
-    out[b * 7 * modes + j] = v;
+    float *f = feats + b * 14 * modes + blk * 7 * modes;
+    f[m] = log1pf(fmaxf(v[0], 0.f));
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      const float re = v[1 + 2 * l], im = v[2 + 2 * l];
+      const float r = sqrtf(fmaxf(re * re + im * im, kFp32Tiny));
+      const float sc = log1pf(r) / r;
+      f[(1 + 2 * l) * modes + m] = sc * re;
+      f[(2 + 2 * l) * modes + m] = sc * im;
+    }
   }
 }
 
@@ -1176,8 +1196,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   fused_reader_kernel<D, M><<<(unsigned)std::min<int64_t>(items, 2 * (int64_t)sms),
                               kFusedThreads, RP::LAUNCH_BYTES, st>>>(ra);
   LNET_TRY(after_launch("fused_reader_kernel"));
-  fused_finalize_kernel<<<dim3((unsigned)B, 2), 256, 0, st>>>(w.wpartial, w.rpartial, wm, rm, T,
-                                                               M, nch);
+  fused_finalize_kernel<<<dim3((unsigned)B, 2), 64, 0, st>>>(w.wpartial, w.rpartial, wm, rm,
+                                                              w.feats, T, M, nch);
   return after_launch("fused_finalize_kernel");
 }
 
