@@ -1080,37 +1080,29 @@ __global__ void fused_finalize_kernel(const float *__restrict__ wpart,
                                       const float *__restrict__ rpart, float *__restrict__ wm,
                                       float *__restrict__ rm, float *__restrict__ feats,
                                       int64_t steps, int modes, int64_t n_chunks) {
+  extern __shared__ float mom[];  // [7M]
   const int64_t b = blockIdx.x;
   const int blk = blockIdx.y;
   const float *part = blk == 0 ? wpart : rpart;
   float *out = blk == 0 ? wm : rm;
   const int lags[3] = {1, 2, 4};
-  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    float v[7];
-#pragma unroll
-    for (int k = 0; k < 7; ++k) {
-      double acc = 0.0;
-      for (int64_t c = 0; c < n_chunks; ++c)
-        acc += (double)part[(b * n_chunks + c) * 7 * modes + k * modes + m];
-      if (k == 0) {
-        v[k] = (float)(acc / (double)steps);
-      } else {
-        const int lag = lags[(k - 1) / 2];
-        v[k] = steps <= lag ? 0.f : (float)(acc / (double)(steps - lag));
-      }
-      out[b * 7 * modes + k * modes + m] = v[k];
+  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) {
+    const int k = j / modes;
+    double acc = 0.0;
+    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)part[(b * n_chunks + c) * 7 * modes + j];
+    float v;
+    if (k == 0) {
+      v = (float)(acc / (double)steps);
+    } else {
+      const int lag = lags[(k - 1) / 2];
+      v = steps <= lag ? 0.f : (float)(acc / (double)(steps - lag));
     }
-    float *f = feats + b * 14 * modes + blk * 7 * modes;
-    f[m] = log1pf(fmaxf(v[0], 0.f));
-#pragma unroll
-    for (int l = 0; l < 3; ++l) {
-      const float re = v[1 + 2 * l], im = v[2 + 2 * l];
-      const float r = sqrtf(fmaxf(re * re + im * im, kFp32Tiny));
-      const float sc = log1pf(r) / r;
-      f[(1 + 2 * l) * modes + m] = sc * re;
-      f[(2 + 2 * l) * modes + m] = sc * im;
-    }
+    out[b * 7 * modes + j] = v;
+    mom[j] = v;
   }
+  __syncthreads();
+  float *f = feats + b * 14 * modes + blk * 7 * modes;
+  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) f[j] = radial_feature(mom, modes, j);
 }
 
 // ---------------------------------------------------------------- dispatch
@@ -1196,8 +1188,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   fused_reader_kernel<D, M><<<(unsigned)std::min<int64_t>(items, 2 * (int64_t)sms),
                               kFusedThreads, RP::LAUNCH_BYTES, st>>>(ra);
   LNET_TRY(after_launch("fused_reader_kernel"));
-  fused_finalize_kernel<<<dim3((unsigned)B, 2), 64, 0, st>>>(w.wpartial, w.rpartial, wm, rm,
-                                                              w.feats, T, M, nch);
+  fused_finalize_kernel<<<dim3((unsigned)B, 2), 256, 7 * M * sizeof(float), st>>>(
+      w.wpartial, w.rpartial, wm, rm, w.feats, T, M, nch);
   return after_launch("fused_finalize_kernel");
 }
 

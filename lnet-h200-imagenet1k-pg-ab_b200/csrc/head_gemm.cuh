@@ -81,38 +81,55 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
   uint32_t phase = 0;
   bool timed_out = false;
   const int nblk = (width + kHeadKB - 1) / kHeadKB;
-  for (int kb = 0; kb < nblk; ++kb) {
+  // operands of block kb are loaded into registers one block ahead, so their
+  // global latency overlaps the previous block's MMAs
+  float av[kHeadKB], bv[kHeadKB / 2];
+  auto fetch = [&](int kb) {
     const int k0 = kb * kHeadKB;
 #pragma unroll
-    for (int c = 0; c < kHeadKB / 8; ++c) {  // A: my row, 64 columns
-      float v[8];
+    for (int c = 0; c < kHeadKB / 8; ++c) {
       if (frow) {
-        load8(frow, k0 + 8 * c, width, v);
+        load8(frow, k0 + 8 * c, width, av + 8 * c);
       } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        for (int i = 0; i < 8; ++i) av[8 * c + i] = 0.f;
       }
+    }
+#pragma unroll
+    for (int c = 0; c < kHeadKB / 16; ++c) {
+      const int cc = bhalf * (kHeadKB / 16) + c;
+      if (grow) {
+        load8(grow, k0 + 8 * cc, width, bv + 8 * c);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bv[8 * c + i] = 0.f;
+      }
+    }
+  };
+  fetch(0);
+  for (int kb = 0; kb < nblk; ++kb) {
+    if (kb > 0) {  // MMAs of block kb - 1 still read the slabs
+      if (!sm100::mbar_wait_bounded(mbar, phase, 1u << 20)) timed_out = true;
+      phase ^= 1u;
+      sm100::tc_fence_after();
+    }
+#pragma unroll
+    for (int c = 0; c < kHeadKB / 8; ++c) {
       uint4 hi, lo;
-      split_bf16x8(v, hi, lo);
+      split_bf16x8(av + 8 * c, hi, lo);
       *reinterpret_cast<uint4 *>(a_hi + c * kHeadSlabA + tid * 16) = hi;
       *reinterpret_cast<uint4 *>(a_lo + c * kHeadSlabA + tid * 16) = lo;
     }
 #pragma unroll
-    for (int c = 0; c < kHeadKB / 16; ++c) {  // B: my class row, 32 columns
+    for (int c = 0; c < kHeadKB / 16; ++c) {
       const int cc = bhalf * (kHeadKB / 16) + c;
-      float v[8];
-      if (grow) {
-        load8(grow, k0 + 8 * cc, width, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-      }
       uint4 hi, lo;
-      split_bf16x8(v, hi, lo);
+      split_bf16x8(bv + 8 * c, hi, lo);
       *reinterpret_cast<uint4 *>(b_hi + cc * kHeadSlabB + brow * 16) = hi;
       *reinterpret_cast<uint4 *>(b_lo + cc * kHeadSlabB + brow * 16) = lo;
     }
     sm100::fence_proxy_async_smem();
+    sm100::tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       sm100::tc_fence_after();
@@ -130,10 +147,10 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
       }
       sm100::mma_commit(mbar);
     }
-    if (!sm100::mbar_wait_bounded(mbar, phase, 1u << 20)) timed_out = true;
-    phase ^= 1u;
-    sm100::tc_fence_after();
+    if (kb + 1 < nblk) fetch(kb + 1);
   }
+  if (!sm100::mbar_wait_bounded(mbar, phase, 1u << 20)) timed_out = true;
+  sm100::tc_fence_after();
   // epilogue: thread tid owns row r0 + tid (TMEM lane tid)
   float acc[kHeadN];
 #pragma unroll

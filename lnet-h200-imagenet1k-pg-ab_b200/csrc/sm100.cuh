@@ -37,7 +37,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
                                                   uint32_t limit) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_test(bar, parity)) return true;
-    if (i > 64) __nanosleep(32);
+    if (i > 4096) __nanosleep(64);  // short waits (MMA completion) never sleep
   }
   return false;
 }
