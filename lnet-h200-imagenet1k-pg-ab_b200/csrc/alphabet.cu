@@ -96,6 +96,7 @@ struct Plan {
   float *a_tab = nullptr;     // [4][M] writer a_re, a_im, reader a_re, a_im
   float *moments = nullptr;   // [2][B][7M]
   float *feats = nullptr;     // [B, 14M]
+  float *head_partial = nullptr;  // split-K partial logits
   FusedWorkspace fused;       // fused-route scratch
 };
 
@@ -118,6 +119,7 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.a_tab = ar.take<float>((size_t)4 * M);
   pl.moments = ar.take<float>((size_t)2 * r->batch * 7 * M);
   pl.feats = ar.take<float>((size_t)r->batch * 14 * M);
+  pl.head_partial = ar.take<float>(head_partial_floats(r->batch, p->output_dim));
 }
 
 // ---------------------------------------------------------------- general-route stages
@@ -245,11 +247,13 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
 }
 
 static int head_run(const lnet_b200_alphabet_params *p, int64_t B, const float *wm,
-                    const float *rm, float *feats, float *logits, cudaStream_t st) {
+                    const float *rm, float *feats, float *partial, float *logits,
+                    cudaStream_t st) {
   const int M = p->modes;
   head_features_kernel<<<grid_for(B * 14 * M), 256, 0, st>>>(wm, rm, feats, B, M);
   LNET_TRY(after_launch("head_features_kernel"));
-  return head_gemm(feats, B, 14 * M, p->head_weight, p->head_bias, logits, p->output_dim, st);
+  return head_gemm(feats, B, 14 * M, p->head_weight, p->head_bias, logits, p->output_dim, partial,
+                   st);
 }
 
 static int plan_all(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -352,7 +356,7 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
     float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
     LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, st));
     return head_gemm(pl.fused.feats, B, 14 * M, params->head_weight, params->head_bias, logits,
-                     params->output_dim, st);
+                     params->output_dim, pl.fused.head_partial, st);
   }
   LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
   float *wm = writer_moments ? writer_moments : pl.moments;
@@ -363,7 +367,7 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
     LNET_TRY(stem_generic<float>(params, req, pl, pl.first_local, st));
   LNET_TRY(writer_generic(params, req, pl.first_local, pl, pl.stream, wm, st));
   LNET_TRY(reader_generic(params, req, pl.stream, pl, rm, st));
-  return head_run(params, B, wm, rm, pl.feats, logits, st);
+  return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st);
 }
 
 extern "C" int lnet_b200_stem(const lnet_b200_alphabet_params *params,

@@ -77,6 +77,7 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 struct FusedWorkspace {
   float *moments = nullptr;            // [2][B][7M]
   float *feats = nullptr;              // [B][14M] radial-log features
+  float *head_partial = nullptr;       // split-K partial logits
   __nv_bfloat16 *q = nullptr;          // stem B operand   [5][C/8][D][8]
   __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][64][8]
   __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][128][8]
@@ -101,6 +102,7 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   const int64_t B = r->batch, nch = fused_chunks(std::max<int64_t>(r->steps, 1));
   w.moments = ar.take<float>((size_t)2 * B * 7 * M);
   w.feats = ar.take<float>((size_t)B * 14 * M);
+  w.head_partial = ar.take<float>(head_partial_floats(B, p->output_dim));
   w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
   w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * kWriterDriveRows);
   w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);

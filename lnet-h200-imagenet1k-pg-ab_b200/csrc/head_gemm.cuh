@@ -12,6 +12,8 @@
 
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -50,9 +52,11 @@ __device__ __forceinline__ void load8(const float *row, int k, int width, float 
   }
 }
 
+// Split-K: CTA z covers K blocks [z * bpc, (z + 1) * bpc) and writes its partial
+// tile to partial[z][B][K].
 __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
     const float *__restrict__ F, int64_t B, int width, const float *__restrict__ G,
-    const float *__restrict__ bias, float *__restrict__ logits, int K) {
+    float *__restrict__ partial, int K, int blocks_per_cta) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *a_hi = smem, *a_lo = smem + kHeadABytes;
   uint8_t *b_hi = smem + 2 * kHeadABytes, *b_lo = b_hi + kHeadBBytes;
@@ -80,12 +84,14 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
   const float *grow = cls < K ? G + (int64_t)cls * width : nullptr;
   uint32_t phase = 0;
   bool timed_out = false;
-  const int nblk = (width + kHeadKB - 1) / kHeadKB;
+  const int total_blk = (width + kHeadKB - 1) / kHeadKB;
+  const int kb_begin = blockIdx.z * blocks_per_cta;
+  const int nblk = max(0, min(blocks_per_cta, total_blk - kb_begin));
   // operands of block kb are loaded into registers one block ahead, so their
   // global latency overlaps the previous block's MMAs
   float av[kHeadKB], bv[kHeadKB / 2];
   auto fetch = [&](int kb) {
-    const int k0 = kb * kHeadKB;
+    const int k0 = (kb_begin + kb) * kHeadKB;
 #pragma unroll
     for (int c = 0; c < kHeadKB / 8; ++c) {
       if (frow) {
@@ -149,7 +155,7 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
     }
     if (kb + 1 < nblk) fetch(kb + 1);
   }
-  if (!sm100::mbar_wait_bounded(mbar, phase, 1u << 20)) timed_out = true;
+  if (nblk > 0 && !sm100::mbar_wait_bounded(mbar, phase, 1u << 20)) timed_out = true;
   sm100::tc_fence_after();
   // epilogue: thread tid owns row r0 + tid (TMEM lane tid)
   float acc[kHeadN];
@@ -158,10 +164,11 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
     sm100::tmem_ld16(tbase + ((uint32_t)(32 * warp) << 16) + 16 * j, acc + 16 * j);
   sm100::tmem_ld_wait();
   if (row < B) {
+    float *dst = partial + ((int64_t)blockIdx.z * B + row) * K;
 #pragma unroll
     for (int j = 0; j < kHeadN; ++j) {
       const int c = n0 + j;
-      if (c < K) logits[row * K + c] = timed_out ? __int_as_float(0x7fc00000) : acc[j] + __ldg(bias + c);
+      if (c < K) dst[c] = timed_out ? __int_as_float(0x7fc00000) : (nblk > 0 ? acc[j] : 0.f);
     }
   }
   sm100::tc_fence_before();
@@ -172,15 +179,37 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
   }
 }
 
-// logits [B, K] from features [B, width]; a wait that gives up writes NaN logits.
+// logits[b, k] = bias[k] + sum_z partial[z][b][k], summed in a fixed order.
+__global__ void head_reduce_kernel(const float *__restrict__ partial, const float *__restrict__ bias,
+                                   float *__restrict__ logits, int64_t n, int K, int splits) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = __ldg(bias + (int)(i % K));
+    for (int z = 0; z < splits; ++z) acc += partial[z * n + i];
+    logits[i] = acc;
+  }
+}
+
+constexpr int kHeadSplits = 4;
+
+inline size_t head_partial_floats(int64_t B, int K) { return (size_t)kHeadSplits * B * K; }
+
+// logits [B, K] from features [B, width]; `partial` holds head_partial_floats(B, K)
+// floats.  A wait that gives up writes NaN logits.
 inline int head_gemm(const float *feats, int64_t B, int width, const float *G, const float *bias,
-                     float *logits, int K, cudaStream_t st) {
+                     float *logits, int K, float *partial, cudaStream_t st) {
   LNET_TRY(cuda_check(cudaFuncSetAttribute(head_gemm_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem),
                       "cudaFuncSetAttribute(head_gemm_kernel)"));
-  dim3 grid((unsigned)cdiv(B, kHeadRows), (unsigned)cdiv(K, kHeadN));
-  head_gemm_kernel<<<grid, kHeadThreads, kHeadSmem, st>>>(feats, B, width, G, bias, logits, K);
-  return after_launch("head_gemm_kernel");
+  const int total_blk = (width + kHeadKB - 1) / kHeadKB;
+  const int bpc = (total_blk + kHeadSplits - 1) / kHeadSplits;
+  dim3 grid((unsigned)cdiv(B, kHeadRows), (unsigned)cdiv(K, kHeadN), kHeadSplits);
+  head_gemm_kernel<<<grid, kHeadThreads, kHeadSmem, st>>>(feats, B, width, G, partial, K, bpc);
+  LNET_TRY(after_launch("head_gemm_kernel"));
+  const int64_t n = B * K;
+  const int blocks = (int)std::min<int64_t>(cdiv(n, 256), 148 * 8);
+  head_reduce_kernel<<<blocks, 256, 0, st>>>(partial, bias, logits, n, K, kHeadSplits);
+  return after_launch("head_reduce_kernel");
 }
 
 }  // namespace lnet
