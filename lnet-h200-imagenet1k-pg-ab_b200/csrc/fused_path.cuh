@@ -57,7 +57,8 @@ constexpr uint32_t kErrLookback = 1u << 4;
 //   [20]/[21] a^(3 SUB).
 constexpr int kConsts = 22;
 constexpr int KC_AL = 2, KC_AS = 10, KC_A2S = 18, KC_A3S = 20;
-constexpr int kWriterSub = 32, kReaderSub = 32;
+constexpr int kWriterSub = 64, kReaderSub = 32;
+constexpr int kWriterNSub = 2;
 constexpr int kWriterDriveRows = 64, kReaderDriveRows = 128;
 
 template <int NSUB>
@@ -695,370 +696,6 @@ __device__ __forceinline__ void wait_mma(uint64_t *mbar, uint32_t &phase, uint32
   sm100::tc_fence_after();
 }
 
-// ---------------------------------------------------------------- paired scan (writer)
-// Modes live in TMEM lanes 0..63.  Local warps w with w % 4 < 2 scan: thread
-// (w, lane) owns mode m = 32 (w % 4) + lane and TWO sub-chunks of 32 steps,
-// q0 = 2 (w / 4) and q1 = q0 + 1, carried together as the two halves of
-// FP32x2 registers (same lane, different TMEM columns), so every recurrence
-// and lag-product step is one packed FMA for both sub-chunks.  The other local
-// warps only join the barriers.  Scratch (floats): END [4][2][64] at 0, LAST
-// [4][8][64] at 512, CARRY [8][64] at 2560; the moment sums [4][7][64] reuse
-// [0, 1792) after END / LAST are consumed.
-struct PairLayout {
-  static constexpr int END = 0, LAST = 512, CARRY = 2560, MOM = 0, FLOATS = 3072;
-};
-
-__device__ __forceinline__ float2 ff2(float a, float b) { return make_float2(a, b); }
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-
-template <int M>
-__device__ __forceinline__ void chunk_scan_pair(int ltid, int bar_group, uint32_t tbase,
-                                                int col_re, int col_im, int n, int64_t row,
-                                                int64_t chunk, int64_t n_chunks, const float *K,
-                                                unsigned long long *rec, uint32_t epoch,
-                                                uint32_t *error, uint8_t *s_slab, int slab_s,
-                                                float *sc, float *partial, int trace, int kid) {
-  using L = PairLayout;
-  constexpr int SUB = 32;
-  unsigned long long t_scan = trace ? clock64() : 0;
-  auto mark = [&](int slot) {
-    if (trace && threadIdx.x == 0) {
-      unsigned long long now = clock64();
-      atomicAdd(&g_fused_trace[kid][slot], now - t_scan);
-      t_scan = now;
-    }
-  };
-  const int lwarp = ltid >> 5, lane = ltid & 31;
-  const int Q = lwarp & 3, g = lwarp >> 2;
-  const bool scanner = Q < 2;
-  const int m = 32 * Q + lane;
-  const bool live = scanner && m < M;
-  const int mk = live ? m : 0;
-  const int q0 = 2 * g, q1 = q0 + 1;
-  const int s0 = SUB * q0, s1 = SUB * q1;
-  const int len0 = scanner ? max(0, min(SUB, n - s0)) : 0;
-  const int len1 = scanner ? max(0, min(SUB, n - s1)) : 0;
-  const uint32_t lane_addr = tbase + ((uint32_t)(32 * Q) << 16);
-  const float ar = K[mk], ai = K[M + mk];
-  const float2 ar2 = ff2(ar, ar), ai2 = ff2(ai, ai), nai2 = ff2(-ai, -ai);
-  const float2 neg1 = ff2(-1.f, -1.f);
-
-  // ---- pass 1: local scans of both sub-chunks from zero
-  float2 sr = ff2(0.f, 0.f), si = ff2(0.f, 0.f);
-  float2 l_r[4], l_i[4];  // l[0] = last state (x: q0, y: q1)
-#pragma unroll
-  for (int k = 0; k < 4; ++k) l_r[k] = l_i[k] = ff2(0.f, 0.f);
-  for (int c0 = 0; c0 < len0; c0 += 8) {
-    float ur0[8], ur1[8], ui0[8], ui1[8];
-    sm100::tmem_ld8(lane_addr + col_re + s0 + c0, ur0);
-    sm100::tmem_ld8(lane_addr + col_re + s1 + c0, ur1);
-    sm100::tmem_ld8(lane_addr + col_im + s0 + c0, ui0);
-    sm100::tmem_ld8(lane_addr + col_im + s1 + c0, ui1);
-    sm100::tmem_ld_wait();
-    if (c0 + 8 <= len1) {  // both sub-chunks full over this piece
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 nr = fma2(ar2, sr, fma2(nai2, si, ff2(ur0[i], ur1[i])));
-        const float2 ni = fma2(ai2, sr, fma2(ar2, si, ff2(ui0[i], ui1[i])));
-        sr = nr;
-        si = ni;
-        if (c0 == SUB - 8 && i >= 4) {
-          l_r[7 - i] = sr;
-          l_i[7 - i] = si;
-        }
-      }
-    } else {  // ragged last chunk: scalar per sub-chunk
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (c0 + i < len0) {
-          const float nr = fmaf(ar, sr.x, fmaf(-ai, si.x, ur0[i]));
-          const float ni = fmaf(ai, sr.x, fmaf(ar, si.x, ui0[i]));
-          sr.x = nr;
-          si.x = ni;
-          l_r[3].x = l_r[2].x; l_i[3].x = l_i[2].x;
-          l_r[2].x = l_r[1].x; l_i[2].x = l_i[1].x;
-          l_r[1].x = l_r[0].x; l_i[1].x = l_i[0].x;
-          l_r[0].x = sr.x; l_i[0].x = si.x;
-        }
-        if (c0 + i < len1) {
-          const float nr = fmaf(ar, sr.y, fmaf(-ai, si.y, ur1[i]));
-          const float ni = fmaf(ai, sr.y, fmaf(ar, si.y, ui1[i]));
-          sr.y = nr;
-          si.y = ni;
-          l_r[3].y = l_r[2].y; l_i[3].y = l_i[2].y;
-          l_r[2].y = l_r[1].y; l_i[2].y = l_i[1].y;
-          l_r[1].y = l_r[0].y; l_i[1].y = l_i[0].y;
-          l_r[0].y = sr.y; l_i[0].y = si.y;
-        }
-      }
-    }
-  }
-  if (live) {
-    sc[L::END + (2 * q0) * 64 + m] = sr.x;
-    sc[L::END + (2 * q0 + 1) * 64 + m] = si.x;
-    sc[L::END + (2 * q1) * 64 + m] = sr.y;
-    sc[L::END + (2 * q1 + 1) * 64 + m] = si.y;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      sc[L::LAST + (8 * q0 + 2 * k) * 64 + m] = l_r[k].x;
-      sc[L::LAST + (8 * q0 + 2 * k + 1) * 64 + m] = l_i[k].x;
-      sc[L::LAST + (8 * q1 + 2 * k) * 64 + m] = l_r[k].y;
-      sc[L::LAST + (8 * q1 + 2 * k + 1) * 64 + m] = l_i[k].y;
-    }
-  }
-  group_sync(bar_group);
-  mark(10);
-  // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^32 c_j + e_j
-  const float asr = K[(KC_AS + 0) * M + mk], asi = K[(KC_AS + 1) * M + mk];
-  float c0r = 0.f, c0i = 0.f, cpr = 0.f, cpi = 0.f;  // c_{q0}, c_{q0 - 1}
-  for (int j = 0; j < q0; ++j) {
-    cpr = c0r;
-    cpi = c0i;
-    float nr = sc[L::END + (2 * j) * 64 + mk], ni = sc[L::END + (2 * j + 1) * 64 + mk];
-    cmac(asr, asi, c0r, c0i, nr, ni);
-    c0r = nr;
-    c0i = ni;
-  }
-  float c1r = sc[L::END + (2 * q0) * 64 + mk], c1i = sc[L::END + (2 * q0 + 1) * 64 + mk];
-  cmac(asr, asi, c0r, c0i, c1r, c1i);  // c_{q1} = a^32 c_{q0} + e_{q0}
-
-  // ---- aggregate, look-back and inclusive record: sub-chunk 3 = the y half of g == 1
-  if (g == 1 && live) {
-    const int64_t item = row * n_chunks + chunk;
-    unsigned long long *my = rec + item * 16 * M;
-    float g_r[4], g_i[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      g_r[k] = l_r[k].y;
-      g_i[k] = l_i[k].y;
-      cmac(K[(KC_AS + 2 * k) * M + m], K[(KC_AS + 2 * k + 1) * M + m], c1r, c1i, g_r[k], g_i[k]);
-      st_tag(my + (2 * k) * M + m, g_r[k], epoch);
-      st_tag(my + (2 * k + 1) * M + m, g_i[k], epoch);
-    }
-    float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
-    if (chunk > 0) {
-      const unsigned long long *pv = rec + (item - 1) * 16 * M;
-      const float aLr = K[KC_AL * M + m], aLi = K[(KC_AL + 1) * M + m];
-      bool done = false;
-      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
-        bool ok = true;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          ok &= ld_tag(pv + 8 * M + (2 * k) * M + m, epoch, p_r[k]);
-          ok &= ld_tag(pv + 8 * M + (2 * k + 1) * M + m, epoch, p_i[k]);
-        }
-        if (ok) {
-          done = true;
-          break;
-        }
-        ok = true;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          ok &= ld_tag(pv + (2 * k) * M + m, epoch, p_r[k]);
-          ok &= ld_tag(pv + (2 * k + 1) * M + m, epoch, p_i[k]);
-        }
-        if (!ok) {
-          __nanosleep(32);
-          continue;
-        }
-        float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
-        bool walk_ok = true;
-        for (int64_t qq = chunk - 2; qq >= 0 && walk_ok; --qq) {
-          const unsigned long long *qv = rec + (row * n_chunks + qq) * 16 * M;
-          bool found = false;
-          for (uint32_t jt = 0; jt < kSpinLimit; ++jt) {
-            float er, ei;
-            if (ld_tag(qv + 8 * M + m, epoch, er) && ld_tag(qv + 9 * M + m, epoch, ei)) {
-              cmac(mr, mi, er, ei, xr, xi);
-              qq = -1;
-              found = true;
-              break;
-            }
-            if (ld_tag(qv + m, epoch, er) && ld_tag(qv + M + m, epoch, ei)) {
-              cmac(mr, mi, er, ei, xr, xi);
-              float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
-              mr = nr;
-              mi = ni;
-              found = true;
-              break;
-            }
-            __nanosleep(32);
-          }
-          if (!found) walk_ok = false;
-        }
-        if (!walk_ok) break;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], xr, xi, p_r[k],
-               p_i[k]);
-        done = true;
-      }
-      if (!done) {
-        atomicOr(error, kErrLookback << kid);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) p_r[k] = p_i[k] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float vr = g_r[k], vi = g_i[k];
-      cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], p_r[0], p_i[0], vr, vi);
-      st_tag(my + 8 * M + (2 * k) * M + m, vr, epoch);
-      st_tag(my + 8 * M + (2 * k + 1) * M + m, vi, epoch);
-      sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
-      sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
-    }
-  }
-  group_sync(bar_group);
-  mark(11);
-
-  // ---- pass 2 from the true states before q0 and q1
-  const float car = sc[L::CARRY + mk], cai = sc[L::CARRY + 64 + mk];
-  // a^(32 q0), a^(32 (q0 - 1)) and a^(32 q1)
-  float pq0r = 1.f, pq0i = 0.f, pqmr = 1.f, pqmi = 0.f, pq1r = asr, pq1i = asi;
-  if (q0 == 2) {
-    pq0r = K[KC_A2S * M + mk]; pq0i = K[(KC_A2S + 1) * M + mk];
-    pqmr = asr; pqmi = asi;
-    pq1r = K[KC_A3S * M + mk]; pq1i = K[(KC_A3S + 1) * M + mk];
-  }
-  float x0r = c0r, x0i = c0i;  // true state before q0
-  cmac(pq0r, pq0i, car, cai, x0r, x0i);
-  float x1r = c1r, x1i = c1i;  // true state before q1
-  cmac(pq1r, pq1i, car, cai, x1r, x1i);
-  float2 h_r[4], h_i[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float ar_k = K[(KC_AS + 2 * k) * M + mk], ai_k = K[(KC_AS + 2 * k + 1) * M + mk];
-    float hr0, hi0;
-    if (q0 == 0) {
-      hr0 = sc[L::CARRY + (2 * k) * 64 + mk];
-      hi0 = sc[L::CARRY + (2 * k + 1) * 64 + mk];
-    } else {
-      float ipr = cpr, ipi = cpi;  // true state before q0 - 1
-      cmac(pqmr, pqmi, car, cai, ipr, ipi);
-      hr0 = sc[L::LAST + (8 * (q0 - 1) + 2 * k) * 64 + mk];
-      hi0 = sc[L::LAST + (8 * (q0 - 1) + 2 * k + 1) * 64 + mk];
-      cmac(ar_k, ai_k, ipr, ipi, hr0, hi0);
-    }
-    float hr1 = l_r[k].x, hi1 = l_i[k].x;  // last states of q0, made true
-    cmac(ar_k, ai_k, x0r, x0i, hr1, hi1);
-    h_r[k] = ff2(hr0, hr1);
-    h_i[k] = ff2(hi0, hi1);
-  }
-  group_sync(bar_group);  // END / LAST consumed: the moment sums may reuse them
-  sr = ff2(x0r, x1r);
-  si = ff2(x0i, x1i);
-  float2 h1r = h_r[0], h1i = h_i[0], h2r = h_r[1], h2i = h_i[1];
-  float2 h3r = h_r[2], h3i = h_i[2], h4r = h_r[3], h4i = h_i[3];
-  float2 e = ff2(0.f, 0.f), k1r = e, k1i = e, k2r = e, k2i = e, k4r = e, k4i = e;
-  auto s_addr = [&](int t, int j) {
-    return s_slab + (j / 8) * slab_s + (t / 8) * 128 + (j % 8) * 16 + (t % 8) * 2;
-  };
-  for (int c0 = 0; c0 < len0; c0 += 8) {
-    float ur0[8], ur1[8], ui0[8], ui1[8];
-    sm100::tmem_ld8(lane_addr + col_re + s0 + c0, ur0);
-    sm100::tmem_ld8(lane_addr + col_re + s1 + c0, ur1);
-    sm100::tmem_ld8(lane_addr + col_im + s0 + c0, ui0);
-    sm100::tmem_ld8(lane_addr + col_im + s1 + c0, ui1);
-    sm100::tmem_ld_wait();
-    if (c0 + 8 <= len1) {
-      float2 br[8], bi[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 nr = fma2(ar2, sr, fma2(nai2, si, ff2(ur0[i], ur1[i])));
-        const float2 ni = fma2(ai2, sr, fma2(ar2, si, ff2(ui0[i], ui1[i])));
-        sr = nr;
-        si = ni;
-        const float2 nsr = __fmul2_rn(sr, neg1);
-        e = fma2(sr, sr, fma2(si, si, e));
-        k1r = fma2(sr, h1r, fma2(si, h1i, k1r));
-        k1i = fma2(si, h1r, fma2(nsr, h1i, k1i));
-        k2r = fma2(sr, h2r, fma2(si, h2i, k2r));
-        k2i = fma2(si, h2r, fma2(nsr, h2i, k2i));
-        k4r = fma2(sr, h4r, fma2(si, h4i, k4r));
-        k4i = fma2(si, h4r, fma2(nsr, h4i, k4i));
-        h4r = h3r; h4i = h3i;
-        h3r = h2r; h3i = h2i;
-        h2r = h1r; h2i = h1i;
-        h1r = sr; h1i = si;
-        br[i] = sr;
-        bi[i] = si;
-      }
-      if (live) {
-        uint4 v;
-        v.x = pack_bf16x2(br[0].x, br[1].x); v.y = pack_bf16x2(br[2].x, br[3].x);
-        v.z = pack_bf16x2(br[4].x, br[5].x); v.w = pack_bf16x2(br[6].x, br[7].x);
-        *reinterpret_cast<uint4 *>(s_addr(s0 + c0, m)) = v;
-        v.x = pack_bf16x2(br[0].y, br[1].y); v.y = pack_bf16x2(br[2].y, br[3].y);
-        v.z = pack_bf16x2(br[4].y, br[5].y); v.w = pack_bf16x2(br[6].y, br[7].y);
-        *reinterpret_cast<uint4 *>(s_addr(s1 + c0, m)) = v;
-        v.x = pack_bf16x2(bi[0].x, bi[1].x); v.y = pack_bf16x2(bi[2].x, bi[3].x);
-        v.z = pack_bf16x2(bi[4].x, bi[5].x); v.w = pack_bf16x2(bi[6].x, bi[7].x);
-        *reinterpret_cast<uint4 *>(s_addr(s0 + c0, M + m)) = v;
-        v.x = pack_bf16x2(bi[0].y, bi[1].y); v.y = pack_bf16x2(bi[2].y, bi[3].y);
-        v.z = pack_bf16x2(bi[4].y, bi[5].y); v.w = pack_bf16x2(bi[6].y, bi[7].y);
-        *reinterpret_cast<uint4 *>(s_addr(s1 + c0, M + m)) = v;
-      }
-    } else {  // ragged last chunk: scalar per sub-chunk
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-#pragma unroll
-        for (int hlf = 0; hlf < 2; ++hlf) {
-          const int lenh = hlf ? len1 : len0;
-          if (c0 + i >= lenh) continue;
-          float &srr = hlf ? sr.y : sr.x, &sii = hlf ? si.y : si.x;
-          const float u_re = hlf ? ur1[i] : ur0[i], u_im = hlf ? ui1[i] : ui0[i];
-          const float nr = fmaf(ar, srr, fmaf(-ai, sii, u_re));
-          const float ni = fmaf(ai, srr, fmaf(ar, sii, u_im));
-          srr = nr;
-          sii = ni;
-          float &ee = hlf ? e.y : e.x;
-          ee = fmaf(srr, srr, fmaf(sii, sii, ee));
-          float &a1r = hlf ? k1r.y : k1r.x, &a1i = hlf ? k1i.y : k1i.x;
-          float &a2r = hlf ? k2r.y : k2r.x, &a2i = hlf ? k2i.y : k2i.x;
-          float &a4r = hlf ? k4r.y : k4r.x, &a4i = hlf ? k4i.y : k4i.x;
-          float &g1r = hlf ? h1r.y : h1r.x, &g1i = hlf ? h1i.y : h1i.x;
-          float &g2r = hlf ? h2r.y : h2r.x, &g2i = hlf ? h2i.y : h2i.x;
-          float &g3r = hlf ? h3r.y : h3r.x, &g3i = hlf ? h3i.y : h3i.x;
-          float &g4r = hlf ? h4r.y : h4r.x, &g4i = hlf ? h4i.y : h4i.x;
-          a1r = fmaf(srr, g1r, fmaf(sii, g1i, a1r));
-          a1i = fmaf(sii, g1r, fmaf(-srr, g1i, a1i));
-          a2r = fmaf(srr, g2r, fmaf(sii, g2i, a2r));
-          a2i = fmaf(sii, g2r, fmaf(-srr, g2i, a2i));
-          a4r = fmaf(srr, g4r, fmaf(sii, g4i, a4r));
-          a4i = fmaf(sii, g4r, fmaf(-srr, g4i, a4i));
-          g4r = g3r; g4i = g3i;
-          g3r = g2r; g3i = g2i;
-          g2r = g1r; g2i = g1i;
-          g1r = srr; g1i = sii;
-          if (live) {
-            const int t = (hlf ? s1 : s0) + c0 + i;
-            *reinterpret_cast<__nv_bfloat16 *>(s_addr(t, m)) = __float2bfloat16_rn(srr);
-            *reinterpret_cast<__nv_bfloat16 *>(s_addr(t, M + m)) = __float2bfloat16_rn(sii);
-          }
-        }
-      }
-    }
-  }
-  mark(12);
-  if (live) {
-    float *mo0 = sc + L::MOM + q0 * 7 * 64 + m, *mo1 = sc + L::MOM + q1 * 7 * 64 + m;
-    mo0[0] = e.x; mo1[0] = e.y;
-    mo0[64] = k1r.x; mo1[64] = k1r.y;
-    mo0[128] = k1i.x; mo1[128] = k1i.y;
-    mo0[192] = k2r.x; mo1[192] = k2r.y;
-    mo0[256] = k2i.x; mo1[256] = k2i.y;
-    mo0[320] = k4r.x; mo1[320] = k4r.y;
-    mo0[384] = k4i.x; mo1[384] = k4i.y;
-  }
-  group_sync(bar_group);
-  for (int j = ltid; j < 7 * M; j += 256) {
-    const int k = j / M, mm = j - (j / M) * M;
-    const float *mo = sc + L::MOM + k * 64 + mm;
-    partial[j] = mo[0] + mo[7 * 64] + mo[14 * 64] + mo[21 * 64];
-  }
-}
-
 // ---------------------------------------------------------------- writer kernel
 // One CTA of 512 threads per SM runs two independent item streams (threads
 // [0, 256) and [256, 512)).  The streams share the weight operands in shared
@@ -1085,7 +722,7 @@ struct WriterPlan {
   static constexpr int SHARED_END = (OFF_K + kConsts * M * 4 + 127) / 128 * 128;
   // per stream
   static constexpr int SLAB_X = kXRows * 16 + 16;
-  static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, PairLayout::FLOATS * 4);
+  static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, ScanLayout<kWriterNSub>::FLOATS * 4);
   static constexpr int FL_BYTES = kChunk * D * 2;
   static constexpr int SLAB_XH = kChunk * 16;
   static constexpr int SLAB_S = kChunk * 16;  // state slab: one 8-column K group, M-major
@@ -1164,7 +801,6 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
-    if (ltid == 0) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LNET_TRACE(0);
     const int64_t chunk = item / a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
@@ -1235,13 +871,17 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
         issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
                    P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
+      // claim the next item while the drive GEMM runs
+      item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     }
     wait_mma(mbar, phase, a.error, 1);
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
-    chunk_scan_pair<M>(ltid, bar_group, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
-                       a.epoch, a.error, gs + P::G_XS, P::SLAB_S, s_scan,
-                       a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id);
+    chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
+                                     a.n_chunks, s_k, a.rec, a.epoch, a.error, gs + P::G_XS,
+                                     P::SLAB_S, s_scan,
+                                     a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace,
+                                     a.kernel_id);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     group_sync(bar_group);
@@ -1355,7 +995,6 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
-    if (tid == 0) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LNET_TRACE(0);
     const int64_t chunk = item / a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
@@ -1417,6 +1056,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
         issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
                    P::SLAB_AD, s_base + P::OFF_XH, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
+      item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);  // overlaps the GEMM
     }
     wait_mma(mbar, phase, a.error, 3);
     LNET_TRACE(4);
