@@ -7,6 +7,7 @@ Laplace layer behind the reference ``lnet`` module API.
   ``lnet.laplace.PoleResidueTemporalMixing``.
 * :mod:`lnet_b200.ops` — the same calls as ``torch.library`` custom ops
   (``lnet_b200::alphabet_forward``, ``lnet_b200::laplace_forward``).
+* :mod:`lnet_b200.sharding` — batch sharding over one process per GPU.
 
 All compute runs in the C-ABI CUDA library ``_lib/liblnet_b200.so`` built by
 :func:`lnet_b200.build.build`; there is no CPU fallback.
