@@ -57,9 +57,9 @@ constexpr uint32_t kErrLookback = 1u << 4;
 //   [20]/[21] a^(3 SUB).
 constexpr int kConsts = 22;
 constexpr int KC_AL = 2, KC_AS = 10, KC_A2S = 18, KC_A3S = 20;
-constexpr int kWriterSub = 64, kReaderSub = 32;
-constexpr int kWriterNSub = 2;
-constexpr int kWriterDriveRows = 64, kReaderDriveRows = 128;
+constexpr int kWriterSub = 32, kReaderSub = 32;
+constexpr int kWriterNSub = 4;
+constexpr int kWriterDriveRows = 128, kReaderDriveRows = 128;
 
 template <int NSUB>
 struct ScanLayout {
@@ -131,7 +131,7 @@ __device__ __forceinline__ void cmul_d(double ar, double ai, double br, double b
 __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace w) {
   const int C = p.raw_input_dim, D = p.model_dim, M = p.modes, K5 = p.conv_kernel;
   const int64_t n_q = (int64_t)kTaps * C * D;
-  // drive A rows per block: writer 64 (lanes 0..63), reader 128 (modes repeated every 64 lanes)
+  // drive A rows per block: 128 (modes repeated every 64 lanes)
   const int64_t n_wdrive = (int64_t)2 * D * kWriterDriveRows;
   const int64_t n_rdrive = (int64_t)2 * D * kReaderDriveRows;
   const int64_t n_syn = (int64_t)2 * M * D;
@@ -218,9 +218,10 @@ struct ReaderPlan {
   static constexpr int SLAB_AD = 128 * 16;
   static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
   static constexpr int PITCH = D * 2 + 16;  // stream tile row pitch (bank-conflict free)
-  static constexpr int V_BYTES = cmax(kXRows * PITCH, ScanLayout<4>::FLOATS * 4);  // tile, then scan scratch
+  static constexpr int V_BYTES = kXRows * PITCH;  // stream tile (next item's after the conv)
   static constexpr int SLAB_XH = kChunk * 16;
-  static constexpr int XH_BYTES = (D / 8) * SLAB_XH;
+  // xhat slab, then (once the drive GEMM has read it) the scan scratch
+  static constexpr int XH_BYTES = cmax((D / 8) * SLAB_XH, ScanLayout<4>::FLOATS * 4);
   static constexpr int OFF_AD = 0;
   static constexpr int OFF_V = OFF_AD + AD_BYTES;
   static constexpr int OFF_XH = OFF_V + V_BYTES;
@@ -254,7 +255,8 @@ struct FusedArgs {
 
 // Per-phase cycle totals of thread 0 of every CTA (tracing; off by default).
 // Slots: 0 claim, 1 tile load, 2 first GEMM wait, 3 token epilogue, 4 drive GEMM
-// wait, 5 scan (whole), 6 synthesis wait, 7 residual epilogue, 10 scan pass 1,
+// wait, 5 scan (whole), 6 synthesis wait, 7 residual epilogue, 8 look-backs
+// resolved by the prefetched record, 9 look-backs (chunk > 0), 10 scan pass 1,
 // 11 look-back, 12 scan pass 2, 15 items processed.
 static __device__ unsigned long long g_fused_trace[2][16];
 
@@ -277,6 +279,9 @@ __device__ __forceinline__ void copy_floats(float *dst, const float *src, int n)
   for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
+// Two floats -> packed bf16x2 (a in the low half), round to nearest even.
+// (An integer-arithmetic rounding measured slower: the conversion pipe is not
+// the limit here.)
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&h);
@@ -314,9 +319,36 @@ __device__ __forceinline__ void load_rows(const __nv_bfloat16 *src, int64_t b, i
   }
 }
 
-// SiLU with the hardware exponential (relative error ~1e-6, far inside the
-// bf16 activation rounding of this route).
-__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+// Asynchronous form of load_rows (cp.async into `dst(r, kc)`, shared-memory
+// addresses); the caller waits with cp_async_wait_all.
+template <int CHUNKS, typename Dst>
+__device__ __forceinline__ void load_rows_async(const __nv_bfloat16 *src, int64_t b, int64_t T,
+                                                int64_t t0, int ltid, Dst dst) {
+  constexpr int TOTAL = kXRows * CHUNKS;
+  for (int i = ltid; i < TOTAL; i += kFusedThreads) {
+    const int r = i / CHUNKS, kc = i - (i / CHUNKS) * CHUNKS;
+    const int64_t tok = t0 - kHalo + r;
+    const bool in = tok >= 0 && tok < T;
+    const __nv_bfloat16 *p = in ? src + ((b * T + tok) * (8 * CHUNKS) + kc * 8) : src;
+    sm100::cp_async16(dst(r, kc), p, in ? 16u : 0u);
+  }
+}
+
+// SiLU for the bf16 route: v/2 + (v/2) tanh(v/2) with one tanh.approx, i.e.
+// one multi-function-unit operation per element instead of an exponential and
+// a reciprocal (the epilogues are bound by that unit: 9 % faster end to end).
+// Absolute error ~|v| 2^-11, below the bf16 rounding of the stored activation.
+// LNET_SILU_EXP2 selects the exponential form (relative error ~1e-6).
+__device__ __forceinline__ float silu_fast(float v) {
+#if defined(LNET_SILU_EXP2)
+  return __fdividef(v, 1.0f + __expf(-v));
+#else
+  const float h = 0.5f * v;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+#endif
+}
 
 __device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, float &cr,
                                      float &ci) {  // c += a * b
@@ -338,12 +370,13 @@ __device__ __forceinline__ bool ld_tag(const unsigned long long *p, uint32_t epo
 
 // ---------------------------------------------------------------- scan + look-back
 // Executed by the 256 threads of one item stream (local thread id `ltid`).
-// NSUB = 4 (reader): the drive operand repeats the mode rows every 64 lanes, so
-//   local warp w reads lane quarter w % 4 = modes 32 * (w % 2) + lane of
-//   sub-chunk q = (w % 4) / 2 + 2 * (w / 4).
-// NSUB = 2 (writer): modes live in lanes 0..63 only; local warps with w % 4 < 2
-//   scan modes 32 * (w % 4) + lane of sub-chunk q = w / 4; the others only
-//   join the barriers.
+// NSUB = 4 (writer and reader): the drive operand repeats the mode rows every
+//   64 lanes, so local warp w reads lane quarter w % 4 = modes 32 * (w % 2) +
+//   lane of sub-chunk q = (w % 4) / 2 + 2 * (w / 4): all four SM sub-partitions
+//   scan.
+// NSUB = 2 (drive rows in lanes 0..63 only): local warps with w % 4 < 2 scan
+//   modes 32 * (w % 4) + lane of sub-chunk q = w / 4; the others only join the
+//   barriers.
 // Sub-chunk q covers steps [SUB q, SUB q + SUB), SUB = 128 / NSUB.  u_re / u_im
 // live in TMEM columns [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's
 // moment partial sums [7][M] to `partial`.
@@ -356,6 +389,38 @@ __device__ __forceinline__ void group_sync(int id) {
   asm volatile("barrier.sync %0, 256;" ::"r"(id) : "memory");
 }
 
+// The previous chunk's inclusive record, loaded by the publishing threads
+// before the scan starts (its producer has usually finished by then), so the
+// look-back costs no memory round trip when the tags already match.
+struct LookbackPrefetch {
+  unsigned long long w[8];  // [state k][re | im] of the inclusive record
+};
+
+template <int M, int NSUB>
+__device__ __forceinline__ void lookback_prefetch(int ltid, const unsigned long long *rec,
+                                                  int64_t row, int64_t chunk, int64_t n_chunks,
+                                                  LookbackPrefetch &p) {
+  const int lwarp = ltid >> 5, lane = ltid & 31, Q = lwarp & 3;
+  int q, m;
+  bool scanner;
+  if constexpr (NSUB == 4) {
+    q = (Q >> 1) + 2 * (lwarp >> 2);
+    m = 32 * (Q & 1) + lane;
+    scanner = true;
+  } else {
+    q = lwarp >> 2;
+    m = 32 * Q + lane;
+    scanner = Q < 2;
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) p.w[k] = 0ull;
+  if (scanner && q == NSUB - 1 && m < M && chunk > 0) {
+    const unsigned long long *pv = rec + (row * n_chunks + chunk - 1) * 16 * M + 8 * M + m;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) p.w[k] = __ldcg(pv + k * M);
+  }
+}
+
 template <int M, bool WRITE_STATES, int NSUB>
 __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, uint32_t tbase,
                                            int col_re, int col_im, int n, int64_t row,
@@ -363,7 +428,8 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
                                            unsigned long long *rec, uint32_t epoch,
                                            uint32_t *error,
                                            uint8_t *s_slab, int slab_s, float *sc,
-                                           float *partial, int trace, int kid) {
+                                           float *partial, int trace, int kid,
+                                           const LookbackPrefetch &pre) {
   using L = ScanLayout<NSUB>;
   constexpr int SUB = L::SUB;
   unsigned long long t_scan = trace ? clock64() : 0;
@@ -475,7 +541,18 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     if (chunk > 0) {
       const unsigned long long *pv = rec + (item - 1) * 16 * M;
       const float aLr = K[KC_AL * M + m], aLi = K[(KC_AL + 1) * M + m];
-      bool done = false;
+      bool done = true;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const unsigned long long xr = pre.w[2 * k], xi = pre.w[2 * k + 1];
+        done &= (uint32_t)(xr >> 32) == epoch && (uint32_t)(xi >> 32) == epoch;
+        p_r[k] = __uint_as_float((uint32_t)xr);
+        p_i[k] = __uint_as_float((uint32_t)xi);
+      }
+      if (trace && m == 0) {
+        atomicAdd(&g_fused_trace[kid][9], 1ull);
+        if (done) atomicAdd(&g_fused_trace[kid][8], 1ull);
+      }
       for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
         bool ok = true;  // inclusive record of the previous chunk
 #pragma unroll
@@ -708,13 +785,13 @@ template <int C, int D, int M>
 struct WriterPlan {
   static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
   // shared by both streams
-  static constexpr int SLAB_AD = 64 * 16;  // drive A rows = modes (lanes 0..63)
+  static constexpr int SLAB_AD = 128 * 16;  // drive A rows: modes repeated every 64 lanes
   static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
   static constexpr int SLAB_Q = D * 16;
   static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
   static constexpr int SLAB_WS = D * 16;
   static constexpr int WS_BYTES = (2 * M / 8) * SLAB_WS;
-  static constexpr int OFF_AD = 0;  // UMMA reads 128 rows per drive slab: the tail lands in Q
+  static constexpr int OFF_AD = 0;
   static constexpr int OFF_Q = OFF_AD + AD_BYTES;
   static constexpr int OFF_WS = OFF_Q + Q_BYTES;
   static constexpr int OFF_PAR = OFF_WS + WS_BYTES;            // float [4][D]: bias, g, ds, ls
@@ -723,13 +800,11 @@ struct WriterPlan {
   // per stream
   static constexpr int SLAB_X = kXRows * 16 + 16;
   static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, ScanLayout<kWriterNSub>::FLOATS * 4);
-  static constexpr int FL_BYTES = kChunk * D * 2;
   static constexpr int SLAB_XH = kChunk * 16;
   static constexpr int SLAB_S = kChunk * 16;  // state slab: one 8-column K group, M-major
   static constexpr int XS_BYTES = cmax((D / 8) * SLAB_XH, (2 * M / 8) * SLAB_S);
-  static constexpr int G_X = 0;                       // x tile, then scan scratch
-  static constexpr int G_FL = G_X + X_BYTES;          // bf16 [128][D] stem output
-  static constexpr int G_XS = G_FL + FL_BYTES;        // xhat slab, then state slab
+  static constexpr int G_X = 0;                       // x tile, scan scratch, next x tile
+  static constexpr int G_XS = G_X + X_BYTES;          // xhat slab, then state slab
   static constexpr int G_RED = G_XS + XS_BYTES;       // float [2][128]
   static constexpr int G_RS = G_RED + 2 * kChunk * 4; // float [128]
   static constexpr int G_MISC = G_RS + kChunk * 4;    // mbar, item
@@ -739,7 +814,6 @@ struct WriterPlan {
   static constexpr int TMEM_COLS = 512;  // 256 per stream: u re [0,128), u im [128,256);
                                          // stem and synthesis accumulators reuse [0, D)
   static_assert(BYTES <= 232448, "writer shared memory exceeds 227 KB");
-  static_assert(Q_BYTES >= 64 * 16, "drive-operand tail must stay inside the stem slabs");
 };
 
 template <int C, int D, int M>
@@ -796,8 +870,17 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   unsigned long long t_last = clock64();
   // Items are claimed one ahead (alternating slots): iteration k processes
   // item_slot[k & 1] and claims the next into item_slot[(k + 1) & 1].
+  // The x tile of an item is copied one item ahead (cp.async into the x
+  // region, which is free once the previous item's scan has finished).
+  auto issue_tile = [&](int64_t it) {
+    const int64_t ch = it / a.B, bb = it - ch * a.B;
+    load_rows_async<C / 8>(a.in, bb, a.T, ch * kChunk, ltid, [&](int r, int kc) {
+      return g_base + P::G_X + kc * P::SLAB_X + r * 16;
+    });
+  };
   if (ltid == 0) item_slot[0] = (int64_t)atomicAdd(a.counter, 1u);
   group_sync(bar_group);
+  if (item_slot[0] < total) issue_tile(item_slot[0]);
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
@@ -805,10 +888,10 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     const int64_t chunk = item / a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
+    __nv_bfloat16 *out_row = a.out + ((b * a.T + t0 + row) * D + half * HD);
 
-    // 1. x tile (zero outside [0, T))
-    load_rows<C / 8>(a.in, b, a.T, t0, ltid,
-                     [&](int r, int kc) { return gs + P::G_X + kc * P::SLAB_X + r * 16; });
+    // 1. x tile (zero outside [0, T)), issued one item ahead
+    sm100::cp_async_wait_all();
     sm100::fence_proxy_async_smem();
     group_sync(bar_group);
     LNET_TRACE(1);
@@ -856,7 +939,8 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
         fl.z = pack_bf16x2(f[8 * gq + 4], f[8 * gq + 5]);
         fl.w = pack_bf16x2(f[8 * gq + 6], f[8 * gq + 7]);
         *reinterpret_cast<uint4 *>(gs + P::G_XS + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
-        *reinterpret_cast<uint4 *>(gs + P::G_FL + row * (D * 2) + d0 * 2) = fl;
+        // the stem output waits in the output rows (L2) for the residual epilogue
+        if (row < n) *reinterpret_cast<uint4 *>(out_row + 8 * gq) = fl;
       }
     }
     sm100::fence_proxy_async_smem();
@@ -874,6 +958,8 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
       // claim the next item while the drive GEMM runs
       item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     }
+    LookbackPrefetch pre;
+    lookback_prefetch<M, kWriterNSub>(ltid, a.rec, b, chunk, a.n_chunks, pre);
     wait_mma(mbar, phase, a.error, 1);
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
@@ -881,18 +967,28 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                                      a.n_chunks, s_k, a.rec, a.epoch, a.error, gs + P::G_XS,
                                      P::SLAB_S, s_scan,
                                      a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace,
-                                     a.kernel_id);
+                                     a.kernel_id, pre);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     group_sync(bar_group);
     LNET_TRACE(5);
-    // 6. synthesis GEMM (token-major) into columns [0, D)
+    // 6. synthesis GEMM (token-major) into columns [0, D); meanwhile the next
+    // item's x tile and this row's stem output are fetched
     if (ltid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D, /*a_mn_major=*/true);
       issue_gemm(tbase, g_base + P::G_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
+    }
+    {
+      const int64_t next = item_slot[(iter + 1) & 1];
+      if (next < total) issue_tile(next);
+    }
+    uint4 flv[HD / 8];
+    if (row < n) {
+#pragma unroll
+      for (int gq = 0; gq < HD / 8; ++gq) flv[gq] = *reinterpret_cast<const uint4 *>(out_row + 8 * gq);
     }
     wait_mma(mbar, phase, a.error, 2);
     LNET_TRACE(6);
@@ -905,12 +1001,10 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
       sm100::tmem_ld_wait();
       const float rsr = rs_s[row];
       if (row < n) {
-        __nv_bfloat16 *dst = a.out + ((b * a.T + t0 + row) * D + half * HD);
 #pragma unroll
         for (int gq = 0; gq < HD / 8; ++gq) {
           const int d0 = half * HD + 8 * gq;
-          uint4 fl = *reinterpret_cast<const uint4 *>(gs + P::G_FL + row * (D * 2) + d0 * 2);
-          const __nv_bfloat16 *fv = reinterpret_cast<const __nv_bfloat16 *>(&fl);
+          const __nv_bfloat16 *fv = reinterpret_cast<const __nv_bfloat16 *>(&flv[gq]);
           float o[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -924,7 +1018,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
           ov.y = pack_bf16x2(o[2], o[3]);
           ov.z = pack_bf16x2(o[4], o[5]);
           ov.w = pack_bf16x2(o[6], o[7]);
-          *reinterpret_cast<uint4 *>(dst + 8 * gq) = ov;
+          *reinterpret_cast<uint4 *>(out_row + 8 * gq) = ov;
         }
       }
     }
@@ -934,13 +1028,10 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
   if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
-  if (a.trace && lane == 0) atomicAdd(&g_fused_trace[a.kernel_id][8], 1ull);
   __syncthreads();
-  if (a.trace && lane == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1ull);
   if (tid < 32) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(*tmem_slot, P::TMEM_COLS);
-    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1000ull);
   }
 }
 
@@ -956,7 +1047,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
   const float *s_w = par, *s_bias = par + kTaps * D, *s_norm = par + (kTaps + 1) * D;
   float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
-  float *s_scan = reinterpret_cast<float *>(smem + P::OFF_V);  // tile is dead during the scan
+  float *s_scan = reinterpret_cast<float *>(smem + P::OFF_XH);  // xhat is dead during the scan
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t s_base = sm100::smem_u32(smem);
 
@@ -990,8 +1081,17 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
 
   unsigned long long t_last = clock64();
+  // Stream tiles are copied one item ahead (cp.async into the tile region,
+  // issued as soon as the conv of the current item has read it).
+  auto issue_tile = [&](int64_t it) {
+    const int64_t ch = it / a.B, bb = it - ch * a.B;
+    load_rows_async<D / 8>(a.in, bb, a.T, ch * kChunk, tid, [&](int r, int kc) {
+      return s_base + P::OFF_V + r * P::PITCH + kc * 16;
+    });
+  };
   if (tid == 0) item_slot[0] = (int64_t)atomicAdd(a.counter, 1u);
   __syncthreads();
+  if (item_slot[0] < total) issue_tile(item_slot[0]);
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
@@ -1000,10 +1100,10 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
 
-    // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T)
-    load_rows<D / 8>(a.in, b, a.T, t0, tid,
-                     [&](int r, int kc) { return smem + P::OFF_V + r * P::PITCH + kc * 16; });
+    // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T), issued one item ahead
+    sm100::cp_async_wait_all();
     __syncthreads();
+    if (tid == 0) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LNET_TRACE(1);
     // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm
     float f[HD];
@@ -1030,6 +1130,10 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     }
     red[half * kChunk + row] = ss;
     __syncthreads();
+    {  // every thread has read the tile: copy the next item's
+      const int64_t next = item_slot[(iter + 1) & 1];
+      if (next < total) issue_tile(next);
+    }
     const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
 #pragma unroll
     for (int g = 0; g < HD / 8; ++g) {
@@ -1056,14 +1160,16 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
         issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
                    P::SLAB_AD, s_base + P::OFF_XH, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
-      item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);  // overlaps the GEMM
     }
+    LookbackPrefetch pre;
+    lookback_prefetch<M, 4>(tid, a.rec, b, chunk, a.n_chunks, pre);
     wait_mma(mbar, phase, a.error, 3);
     LNET_TRACE(4);
     // 4. scan + look-back + moments
     chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
                             a.epoch, a.error, nullptr, 0, s_scan,
-                            a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id);
+                            a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id,
+                            pre);
     sm100::tc_fence_before();
     __syncthreads();
     LNET_TRACE(5);
@@ -1074,7 +1180,6 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   if (warp == 0) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tbase, P::TMEM_COLS);
-    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][9], 1ull);
   }
 }
 

@@ -47,6 +47,16 @@ __device__ __forceinline__ void fence_barrier_init() {
 }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (UMMA reads).
+// 16-byte global -> shared asynchronous copy (cp.async, L2 only); `src_bytes`
+// 0 copies nothing and zero-fills the 16 destination bytes.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

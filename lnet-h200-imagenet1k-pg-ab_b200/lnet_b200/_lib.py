@@ -220,7 +220,7 @@ def set_route(route: int) -> None:
 
 TRACE_SLOTS = {0: "claim", 1: "tile_load", 2: "first_gemm_wait", 3: "token_epilogue",
                4: "drive_gemm_wait", 5: "scan", 6: "synthesis_wait", 7: "residual_epilogue",
-               10: "scan_pass1", 11: "lookback", 12: "scan_pass2", 15: "items"}
+               8: "lookback_prefetch_hits", 9: "lookbacks", 10: "scan_pass1", 11: "lookback", 12: "scan_pass2", 15: "items"}
 
 
 def trace_enable(on: bool) -> None:
