@@ -37,7 +37,7 @@ int after_launch(const char *what);
 // ---------------------------------------------------------------- loads
 __device__ __forceinline__ float load_f(const float *p, int64_t i) { return p[i]; }
 __device__ __forceinline__ float load_f(const __nv_bfloat16 *p, int64_t i) {
-  return __bfloat162float(p[i]);
+  return __uint_as_float((uint32_t)__bfloat16_as_ushort(p[i]) << 16);  // exact widening
 }
 __device__ __forceinline__ double load_f(const double *p, int64_t i) { return p[i]; }
 __device__ __forceinline__ void store_f(float *p, int64_t i, float v) { p[i] = v; }

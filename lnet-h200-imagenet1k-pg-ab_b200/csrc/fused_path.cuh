@@ -279,6 +279,18 @@ __device__ __forceinline__ void copy_floats(float *dst, const float *src, int n)
   for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
+// Eight bf16 (one 16-byte vector) -> float, exactly: a bf16 is the upper half
+// of the float with the same value, so the widening is a shift or a mask on
+// the integer pipe instead of a conversion instruction.
+__device__ __forceinline__ void bf16x8_to_float(const uint4 &v, float *f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
 // Two floats -> packed bf16x2 (a in the low half), round to nearest even.
 // (An integer-arithmetic rounding measured slower: the conversion pipe is not
 // the limit here.)
@@ -416,8 +428,10 @@ __device__ __forceinline__ void lookback_prefetch(int ltid, const unsigned long 
   for (int k = 0; k < 8; ++k) p.w[k] = 0ull;
   if (scanner && q == NSUB - 1 && m < M && chunk > 0) {
     const unsigned long long *pv = rec + (row * n_chunks + chunk - 1) * 16 * M + 8 * M + m;
+    // volatile: issued here, not sunk to the first use behind the scan's barriers
 #pragma unroll
-    for (int k = 0; k < 8; ++k) p.w[k] = __ldcg(pv + k * M);
+    for (int k = 0; k < 8; ++k)
+      asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(p.w[k]) : "l"(pv + k * M));
   }
 }
 
@@ -955,9 +969,10 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
         issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
                    P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16, idesc, false);
       sm100::mma_commit(mbar);
-      // claim the next item while the drive GEMM runs
-      item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     }
+    // the last thread claims the next item while the drive GEMM runs (off the
+    // MMA-issuing thread, whose barrier arrival gates the stream)
+    if (ltid == kFusedThreads - 1) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LookbackPrefetch pre;
     lookback_prefetch<M, kWriterNSub>(ltid, a.rec, b, chunk, a.n_chunks, pre);
     wait_mma(mbar, phase, a.error, 1);
@@ -1004,12 +1019,13 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 #pragma unroll
         for (int gq = 0; gq < HD / 8; ++gq) {
           const int d0 = half * HD + 8 * gq;
-          const __nv_bfloat16 *fv = reinterpret_cast<const __nv_bfloat16 *>(&flv[gq]);
+          float fv[8];
+          bf16x8_to_float(flv[gq], fv);
           float o[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int d = d0 + i;
-            const float x = __bfloat162float(fv[i]);
+            const float x = fv[i];
             const float xh = x * rsr * s_norm[d];
             o[i] = x + s_ls[d] * (modal[8 * gq + i] + s_ds[d] * xh);
           }
@@ -1103,7 +1119,8 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T), issued one item ahead
     sm100::cp_async_wait_all();
     __syncthreads();
-    if (tid == 0) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
+    // the last thread claims the next item (its latency overlaps the conv)
+    if (tid == kFusedThreads - 1) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LNET_TRACE(1);
     // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm
     float f[HD];
@@ -1115,11 +1132,11 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
       const float *wk = s_w + k * D + half * HD;
 #pragma unroll
       for (int g = 0; g < HD / 8; ++g) {
-        uint4 v = *reinterpret_cast<const uint4 *>(src + g * 16);
-        const __nv_bfloat16 *vv = reinterpret_cast<const __nv_bfloat16 *>(&v);
+        const uint4 v = *reinterpret_cast<const uint4 *>(src + g * 16);
+        float vv[8];
+        bf16x8_to_float(v, vv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          f[8 * g + i] = fmaf(wk[8 * g + i], __bfloat162float(vv[i]), f[8 * g + i]);
+        for (int i = 0; i < 8; ++i) f[8 * g + i] = fmaf(wk[8 * g + i], vv[i], f[8 * g + i]);
       }
     }
     float ss = 0.f;
