@@ -28,9 +28,12 @@
 //   stream tile on CUDA cores, SiLU, RMSNorm, drive GEMM, scan, moments.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "generic_kernels.cuh"
@@ -47,7 +50,9 @@ constexpr int kFusedThreads = 256;
 constexpr uint32_t kSpinLimit = 1u << 20;
 // Device error bits (first error word of the fused route's flag block):
 // bit 0..3: an MMA completion wait gave up (writer stem, writer drive, writer
-// synthesis, reader drive); bit 4 / 5: a look-back wait gave up (writer / reader).
+// synthesis, reader drive); bit 4 / 5: a look-back wait gave up (writer / reader);
+// bit 6 / 7: a tile (TMA) wait gave up (writer / reader).
+constexpr uint32_t kErrTile = 1u << 6;
 constexpr uint32_t kErrLookback = 1u << 4;
 
 // Per-block pole constants (floats, M entries each), SUB = steps per scan
@@ -217,8 +222,8 @@ struct ReaderPlan {
   static_assert(D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
   static constexpr int SLAB_AD = 128 * 16;
   static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
-  static constexpr int PITCH = D * 2 + 16;  // stream tile row pitch (bank-conflict free)
-  static constexpr int V_BYTES = kXRows * PITCH;  // stream tile (next item's after the conv)
+  static constexpr int SLAB_V = kXRows * 16;  // stream tile: K-major slabs of 8 channels (one TMA box)
+  static constexpr int V_BYTES = (D / 8) * SLAB_V;  // (the next item's after the conv)
   static constexpr int SLAB_XH = kChunk * 16;
   // xhat slab, then (once the drive GEMM has read it) the scan scratch
   static constexpr int XH_BYTES = cmax((D / 8) * SLAB_XH, ScanLayout<4>::FLOATS * 4);
@@ -234,9 +239,11 @@ struct ReaderPlan {
   static constexpr int LAUNCH_BYTES = cmax(BYTES, 100 * 1024);
   static constexpr int TMEM_COLS = 256;  // [0,128) u re, [128,256) u im
   static_assert(2 * (LAUNCH_BYTES + 1024) <= 228 * 1024, "two reader CTAs must fit one SM");
+  static_assert(OFF_V % 128 == 0 && SLAB_V % 128 == 0, "TMA destinations must be 128-byte aligned");
 };
 
 struct FusedArgs {
+  CUtensorMap tmap;         // 3-D map of `in` ([B][T][W] bf16), box 8 x 144 x 1
   const __nv_bfloat16 *in;  // writer: x [B,T,C]; reader: stream [B,T,D]
   int64_t B, T;
   int64_t n_chunks;
@@ -300,52 +307,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 }
 
 
-// Loads rows [t0 - 8, t0 + 136) of one batch row of a [B, T, W] bf16 tensor
-// (W = 8 * CHUNKS) into shared memory, zero outside [0, T): all global loads of
-// a thread are issued before its shared-memory stores.  `dst(r, kc)` gives the
-// destination of 16-byte chunk kc of tile row r.
-template <int CHUNKS, typename Dst>
-__device__ __forceinline__ void load_rows(const __nv_bfloat16 *src, int64_t b, int64_t T,
-                                          int64_t t0, int ltid, Dst dst) {
-  constexpr int TOTAL = kXRows * CHUNKS;
-  constexpr int PER = (TOTAL + kFusedThreads - 1) / kFusedThreads;
-  uint4 v[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int i = ltid + k * kFusedThreads;
-    v[k] = make_uint4(0, 0, 0, 0);
-    if (i < TOTAL) {
-      const int r = i / CHUNKS, kc = i - (i / CHUNKS) * CHUNKS;
-      const int64_t tok = t0 - kHalo + r;
-      if (tok >= 0 && tok < T)
-        v[k] = __ldcg(reinterpret_cast<const uint4 *>(src + ((b * T + tok) * (8 * CHUNKS) + kc * 8)));
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int i = ltid + k * kFusedThreads;
-    if (i < TOTAL) {
-      const int r = i / CHUNKS, kc = i - (i / CHUNKS) * CHUNKS;
-      *reinterpret_cast<uint4 *>(dst(r, kc)) = v[k];
-    }
-  }
-}
-
-// Asynchronous form of load_rows (cp.async into `dst(r, kc)`, shared-memory
-// addresses); the caller waits with cp_async_wait_all.
-template <int CHUNKS, typename Dst>
-__device__ __forceinline__ void load_rows_async(const __nv_bfloat16 *src, int64_t b, int64_t T,
-                                                int64_t t0, int ltid, Dst dst) {
-  constexpr int TOTAL = kXRows * CHUNKS;
-  for (int i = ltid; i < TOTAL; i += kFusedThreads) {
-    const int r = i / CHUNKS, kc = i - (i / CHUNKS) * CHUNKS;
-    const int64_t tok = t0 - kHalo + r;
-    const bool in = tok >= 0 && tok < T;
-    const __nv_bfloat16 *p = in ? src + ((b * T + tok) * (8 * CHUNKS) + kc * 8) : src;
-    sm100::cp_async16(dst(r, kc), p, in ? 16u : 0u);
-  }
-}
-
 // SiLU for the bf16 route: v/2 + (v/2) tanh(v/2) with one tanh.approx, i.e.
 // one multi-function-unit operation per element instead of an exponential and
 // a reciprocal (the epilogues are bound by that unit: 9 % faster end to end).
@@ -391,7 +352,8 @@ __device__ __forceinline__ bool ld_tag(const unsigned long long *p, uint32_t epo
 //   barriers.
 // Sub-chunk q covers steps [SUB q, SUB q + SUB), SUB = 128 / NSUB.  u_re / u_im
 // live in TMEM columns [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's
-// moment partial sums [7][M] to `partial`.
+// moment partial sums [7][M] to `partial` (or leaves the per-sub-chunk sums in
+// `mom_out` for the caller to reduce with reduce_moments).
 
 // Named barrier over one 256-thread item stream.  The non-aligned form counts
 // threads, so it stays correct when a warp reaches it diverged (e.g. after a
@@ -443,7 +405,8 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
                                            uint32_t *error,
                                            uint8_t *s_slab, int slab_s, float *sc,
                                            float *partial, int trace, int kid,
-                                           const LookbackPrefetch &pre) {
+                                           const LookbackPrefetch &pre,
+                                           float *mom_out = nullptr) {
   using L = ScanLayout<NSUB>;
   constexpr int SUB = L::SUB;
   unsigned long long t_scan = trace ? clock64() : 0;
@@ -524,17 +487,34 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   }
   group_sync(bar_group);
   mark(10);
+#if defined(LNET_LB_DEBUG)
+  const bool dbg = trace && ltid == 192;
+  unsigned long long d0 = clock64(), d1 = 0, d2 = 0, d3 = 0;
+#endif
   // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^SUB c_j + e_j
-  const float asr = K[(KC_AS + 0) * M + mk], asi = K[(KC_AS + 1) * M + mk];
+  // (all end states loaded at once, then the short dependent chain)
+  const float asr = K[KC_AS * M + mk], asi = K[(KC_AS + 1) * M + mk];
   float cr = 0.f, ci = 0.f, cpr = 0.f, cpi = 0.f;  // c_q and c_{q-1}
-  for (int j = 0; j < q; ++j) {
-    cpr = cr;
-    cpi = ci;
-    float nr = sc[L::END + (2 * j) * 64 + mk], ni = sc[L::END + (2 * j + 1) * 64 + mk];
-    cmac(asr, asi, cr, ci, nr, ni);
-    cr = nr;
-    ci = ni;
+  float e_r[NSUB - 1], e_i[NSUB - 1];
+#pragma unroll
+  for (int j = 0; j < NSUB - 1; ++j) {
+    e_r[j] = j < q ? sc[L::END + (2 * j) * 64 + mk] : 0.f;
+    e_i[j] = j < q ? sc[L::END + (2 * j + 1) * 64 + mk] : 0.f;
   }
+#pragma unroll
+  for (int j = 0; j < NSUB - 1; ++j) {
+    if (j < q) {
+      cpr = cr;
+      cpi = ci;
+      float nr = e_r[j], ni = e_i[j];
+      cmac(asr, asi, cr, ci, nr, ni);
+      cr = nr;
+      ci = ni;
+    }
+  }
+#if defined(LNET_LB_DEBUG)
+  if (dbg) d1 = clock64();
+#endif
 
   // ---- aggregate, look-back and inclusive record: threads of the last sub-chunk.
   // Record layout per item: [agg | incl][state k = 0..3][re | im][M]; state 0 is
@@ -551,6 +531,9 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
       st_tag(my + (2 * k) * M + m, g_r[k], epoch);
       st_tag(my + (2 * k + 1) * M + m, g_i[k], epoch);
     }
+#if defined(LNET_LB_DEBUG)
+    if (dbg) d2 = clock64();
+#endif
     float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
     if (chunk > 0) {
       const unsigned long long *pv = rec + (item - 1) * 16 * M;
@@ -563,10 +546,12 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         p_r[k] = __uint_as_float((uint32_t)xr);
         p_i[k] = __uint_as_float((uint32_t)xi);
       }
+#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
       if (trace && m == 0) {
         atomicAdd(&g_fused_trace[kid][9], 1ull);
         if (done) atomicAdd(&g_fused_trace[kid][8], 1ull);
       }
+#endif
       for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
         bool ok = true;  // inclusive record of the previous chunk
 #pragma unroll
@@ -636,8 +621,20 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
       sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
       sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
     }
+#if defined(LNET_LB_DEBUG)
+    if (dbg) d3 = clock64();
+#endif
   }
   group_sync(bar_group);
+#if defined(LNET_LB_DEBUG)
+  if (dbg) {
+    const unsigned long long d4 = clock64();
+    atomicAdd(&g_fused_trace[kid][8], d1 - d0);
+    atomicAdd(&g_fused_trace[kid][9], d2 - d1);
+    atomicAdd(&g_fused_trace[kid][13], d3 - d2);
+    atomicAdd(&g_fused_trace[kid][14], d4 - d3);
+  }
+#endif
   mark(11);
 
   // ---- pass 2 from the true state before this sub-chunk
@@ -746,8 +743,10 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     }
   }
   mark(12);
+  // moment partials per sub-chunk: [NSUB][7][64], reduced below, or by the
+  // caller from `mom_out` after its own barrier (no extra barrier here)
   if (live) {
-    float *mo = sc + L::MOM + q * 7 * 64 + m;
+    float *mo = (mom_out ? mom_out : sc + L::MOM) + q * 7 * 64 + m;
     mo[0] = e;
     mo[64] = c1r;
     mo[128] = c1i;
@@ -756,6 +755,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     mo[320] = c4r;
     mo[384] = c4i;
   }
+  if (mom_out) return;
   group_sync(bar_group);
   for (int j = ltid; j < 7 * M; j += 256) {
     const int k = j / M, mm = j - (j / M) * M;
@@ -763,6 +763,18 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     float acc = 0.f;
 #pragma unroll
     for (int qq = 0; qq < NSUB; ++qq) acc += mo[qq * 7 * 64];
+    partial[j] = acc;
+  }
+}
+
+// Sums the per-sub-chunk moment partials [NSUB][7][64] into partial[7][M].
+template <int M, int NSUB>
+__device__ __forceinline__ void reduce_moments(int ltid, const float *mom, float *partial) {
+  for (int j = ltid; j < 7 * M; j += kFusedThreads) {
+    const int k = j / M, mm = j - (j / M) * M;
+    float acc = 0.f;
+#pragma unroll
+    for (int qq = 0; qq < NSUB; ++qq) acc += mom[qq * 7 * 64 + k * 64 + mm];
     partial[j] = acc;
   }
 }
@@ -812,7 +824,7 @@ struct WriterPlan {
   static constexpr int OFF_K = OFF_PAR + 4 * D * 4;            // float [kConsts * M]
   static constexpr int SHARED_END = (OFF_K + kConsts * M * 4 + 127) / 128 * 128;
   // per stream
-  static constexpr int SLAB_X = kXRows * 16 + 16;
+  static constexpr int SLAB_X = kXRows * 16;  // one TMA box; 128-byte multiple
   static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, ScanLayout<kWriterNSub>::FLOATS * 4);
   static constexpr int SLAB_XH = kChunk * 16;
   static constexpr int SLAB_S = kChunk * 16;  // state slab: one 8-column K group, M-major
@@ -821,18 +833,21 @@ struct WriterPlan {
   static constexpr int G_XS = G_X + X_BYTES;          // xhat slab, then state slab
   static constexpr int G_RED = G_XS + XS_BYTES;       // float [2][128]
   static constexpr int G_RS = G_RED + 2 * kChunk * 4; // float [128]
-  static constexpr int G_MISC = G_RS + kChunk * 4;    // mbar, item
+  static constexpr int G_MOM = G_RS + kChunk * 4;     // float [NSUB][7][64] moment partials
+  static constexpr int G_MISC = G_MOM + kWriterNSub * 7 * 64 * 4;  // mbar, item
   static constexpr int G_BYTES = (G_MISC + 64 + 127) / 128 * 128;
   static constexpr int OFF_TMEM_SLOT = SHARED_END + kWriterStreams * G_BYTES;
   static constexpr int BYTES = OFF_TMEM_SLOT + 16;
   static constexpr int TMEM_COLS = 512;  // 256 per stream: u re [0,128), u im [128,256);
                                          // stem and synthesis accumulators reuse [0, D)
   static_assert(BYTES <= 232448, "writer shared memory exceeds 227 KB");
+  static_assert(SLAB_X % 128 == 0 && SHARED_END % 128 == 0 && G_BYTES % 128 == 0,
+                "TMA destinations must be 128-byte aligned");
 };
 
 template <int C, int D, int M>
 __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
-    fused_writer_kernel(FusedArgs a) {
+    fused_writer_kernel(const __grid_constant__ FusedArgs a) {
   using P = WriterPlan<C, D, M>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
@@ -841,9 +856,11 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   uint8_t *gs = smem + P::SHARED_END + g * P::G_BYTES;
   uint64_t *mbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC);
   int64_t *item_slot = reinterpret_cast<int64_t *>(gs + P::G_MISC + 8);  // [2]
+  uint64_t *tbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC + 24);     // x tile arrival
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_TMEM_SLOT);
   float *red = reinterpret_cast<float *>(gs + P::G_RED);
   float *rs_s = reinterpret_cast<float *>(gs + P::G_RS);
+  float *s_mom = reinterpret_cast<float *>(gs + P::G_MOM);
   float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
   const float *s_bias = par, *s_norm = par + D, *s_ds = par + 2 * D, *s_ls = par + 3 * D;
   float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
@@ -854,6 +871,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 
   if (ltid == 0) {
     sm100::mbar_init(mbar, 1);
+    sm100::mbar_init(tbar, 1);
     sm100::fence_barrier_init();
   }
   if (tid < 32) {
@@ -879,38 +897,43 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   constexpr int HD = D / 2;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (lwarp & 3)) << 16);
   const int64_t total = a.B * a.n_chunks;
+#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
+#endif
 
   unsigned long long t_last = clock64();
   // Items are claimed one ahead (alternating slots): iteration k processes
   // item_slot[k & 1] and claims the next into item_slot[(k + 1) & 1].
-  // The x tile of an item is copied one item ahead (cp.async into the x
-  // region, which is free once the previous item's scan has finished).
+  // The x tile of an item is fetched one item ahead by TMA (one 8-channel box
+  // of rows [t0 - 8, t0 + 136) per K slab, zero outside [0, T)) into the x
+  // region, free once the previous item's scan has finished.  Thread 0 only.
+  uint32_t tphase = 0;
   auto issue_tile = [&](int64_t it) {
-    const int64_t ch = it / a.B, bb = it - ch * a.B;
-    load_rows_async<C / 8>(a.in, bb, a.T, ch * kChunk, ltid, [&](int r, int kc) {
-      return g_base + P::G_X + kc * P::SLAB_X + r * 16;
-    });
+    const int64_t ch = (uint32_t)it / (uint32_t)a.B, bb = it - ch * a.B;  // items < 2^31
+    sm100::mbar_arrive_expect_tx(tbar, (C / 8) * kXRows * 16);
+#pragma unroll
+    for (int kc = 0; kc < C / 8; ++kc)
+      sm100::tma_load_3d(g_base + P::G_X + kc * P::SLAB_X, &a.tmap, tbar, kc * 8,
+                         (int)(ch * kChunk - kHalo), (int)bb);
   };
   if (ltid == 0) item_slot[0] = (int64_t)atomicAdd(a.counter, 1u);
   group_sync(bar_group);
-  if (item_slot[0] < total) issue_tile(item_slot[0]);
+  if (ltid == 0 && item_slot[0] < total) issue_tile(item_slot[0]);
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
     LNET_TRACE(0);
-    const int64_t chunk = item / a.B, b = item - chunk * a.B;
+    const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
     __nv_bfloat16 *out_row = a.out + ((b * a.T + t0 + row) * D + half * HD);
 
-    // 1. x tile (zero outside [0, T)), issued one item ahead
-    sm100::cp_async_wait_all();
-    sm100::fence_proxy_async_smem();
-    group_sync(bar_group);
     LNET_TRACE(1);
-    // 2. stem GEMM: five row-shifted views of the tile
+    // 1-2. x tile (TMA, issued one item ahead), then the stem GEMM: five
+    // row-shifted views of the tile
     if (ltid == 0) {
+      if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit)) atomicOr(a.error, kErrTile);
+      tphase ^= 1u;
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
       for (int k = 0; k < kTaps; ++k)
@@ -982,7 +1005,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                                      a.n_chunks, s_k, a.rec, a.epoch, a.error, gs + P::G_XS,
                                      P::SLAB_S, s_scan,
                                      a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace,
-                                     a.kernel_id, pre);
+                                     a.kernel_id, pre, s_mom);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     group_sync(bar_group);
@@ -996,16 +1019,34 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                  idesc, false);
       sm100::mma_commit(mbar);
     }
-    {
+#if defined(LNET_SYN_DEBUG)
+    unsigned long long y0 = clock64();
+#endif
+    if (ltid == 0) {
       const int64_t next = item_slot[(iter + 1) & 1];
       if (next < total) issue_tile(next);
     }
+#if defined(LNET_SYN_DEBUG)
+    unsigned long long y1 = clock64();
+#endif
     uint4 flv[HD / 8];
     if (row < n) {
 #pragma unroll
       for (int gq = 0; gq < HD / 8; ++gq) flv[gq] = *reinterpret_cast<const uint4 *>(out_row + 8 * gq);
     }
+    reduce_moments<M, kWriterNSub>(ltid, s_mom, a.partial + (b * a.n_chunks + chunk) * 7 * M);
+#if defined(LNET_SYN_DEBUG)
+    unsigned long long y2 = clock64();
+#endif
     wait_mma(mbar, phase, a.error, 2);
+#if defined(LNET_SYN_DEBUG)
+    if (a.trace && ltid == 0) {
+      unsigned long long y3 = clock64();
+      atomicAdd(&g_fused_trace[0][8], y1 - y0);
+      atomicAdd(&g_fused_trace[0][9], y2 - y1);
+      atomicAdd(&g_fused_trace[0][13], y3 - y2);
+    }
+#endif
     LNET_TRACE(6);
     // 7. residual epilogue: v = fl + ls * (modal + ds * xhat), xhat = fl * rs * g
     {
@@ -1043,7 +1084,9 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     LNET_TRACE(7);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
+#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
+#endif
   __syncthreads();
   if (tid < 32) {
     sm100::tc_fence_after();
@@ -1053,12 +1096,14 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 
 // ---------------------------------------------------------------- reader kernel
 template <int D, int M>
-__global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArgs a) {
+__global__ void __launch_bounds__(kFusedThreads, 2)
+    fused_reader_kernel(const __grid_constant__ FusedArgs a) {
   using P = ReaderPlan<D, M>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_MISC + 8);
-  int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);
+  int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);  // [2]
+  uint64_t *tbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC + 32);      // tile arrival
   float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
   float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
   const float *s_w = par, *s_bias = par + kTaps * D, *s_norm = par + (kTaps + 1) * D;
@@ -1069,6 +1114,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
 
   if (tid == 0) {
     sm100::mbar_init(mbar, 1);
+    sm100::mbar_init(tbar, 1);
     sm100::fence_barrier_init();
   }
   if (warp == 0) {
@@ -1094,31 +1140,38 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
   const int half = warp >> 2;
   constexpr int HD = D / 2;
   const int64_t total = a.B * a.n_chunks;
+#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
+#endif
 
   unsigned long long t_last = clock64();
-  // Stream tiles are copied one item ahead (cp.async into the tile region,
-  // issued as soon as the conv of the current item has read it).
+  // Stream tiles are fetched one item ahead by TMA (thread 0; one 8-channel
+  // box per K slab), issued as soon as the conv of the current item has read
+  // the tile region.
+  uint32_t tphase = 0;
   auto issue_tile = [&](int64_t it) {
-    const int64_t ch = it / a.B, bb = it - ch * a.B;
-    load_rows_async<D / 8>(a.in, bb, a.T, ch * kChunk, tid, [&](int r, int kc) {
-      return s_base + P::OFF_V + r * P::PITCH + kc * 16;
-    });
+    const int64_t ch = (uint32_t)it / (uint32_t)a.B, bb = it - ch * a.B;  // items < 2^31
+    sm100::mbar_arrive_expect_tx(tbar, (D / 8) * kXRows * 16);
+#pragma unroll
+    for (int kc = 0; kc < D / 8; ++kc)
+      sm100::tma_load_3d(s_base + P::OFF_V + kc * P::SLAB_V, &a.tmap, tbar, kc * 8,
+                         (int)(ch * kChunk - kHalo), (int)bb);
   };
   if (tid == 0) item_slot[0] = (int64_t)atomicAdd(a.counter, 1u);
   __syncthreads();
-  if (item_slot[0] < total) issue_tile(item_slot[0]);
+  if (tid == 0 && item_slot[0] < total) issue_tile(item_slot[0]);
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
     LNET_TRACE(0);
-    const int64_t chunk = item / a.B, b = item - chunk * a.B;
+    const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
 
     // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T), issued one item ahead
-    sm100::cp_async_wait_all();
-    __syncthreads();
+    if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && tid == 0)
+      atomicOr(a.error, kErrTile << 1);
+    tphase ^= 1u;
     // the last thread claims the next item (its latency overlaps the conv)
     if (tid == kFusedThreads - 1) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LNET_TRACE(1);
@@ -1128,11 +1181,11 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     for (int i = 0; i < HD; ++i) f[i] = s_bias[half * HD + i];
 #pragma unroll
     for (int k = 0; k < kTaps; ++k) {
-      const uint8_t *src = smem + P::OFF_V + (row + 4 * k) * P::PITCH + half * HD * 2;
+      const uint8_t *src = smem + P::OFF_V + (half * HD / 8) * P::SLAB_V + (row + 4 * k) * 16;
       const float *wk = s_w + k * D + half * HD;
 #pragma unroll
       for (int g = 0; g < HD / 8; ++g) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(src + g * 16);
+        const uint4 v = *reinterpret_cast<const uint4 *>(src + g * P::SLAB_V);
         float vv[8];
         bf16x8_to_float(v, vv);
 #pragma unroll
@@ -1147,7 +1200,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     }
     red[half * kChunk + row] = ss;
     __syncthreads();
-    {  // every thread has read the tile: copy the next item's
+    if (tid == 0) {  // every thread has read the tile: fetch the next item's
       const int64_t next = item_slot[(iter + 1) & 1];
       if (next < total) issue_tile(next);
     }
@@ -1192,7 +1245,9 @@ __global__ void __launch_bounds__(kFusedThreads, 2) fused_reader_kernel(FusedArg
     LNET_TRACE(5);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
+#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
+#endif
   __syncthreads();
   if (warp == 0) {
     sm100::tc_fence_after();
@@ -1246,6 +1301,7 @@ inline bool fused_supported(const lnet_b200_alphabet_params *p,
   if (r->x_dtype != LNET_BF16 || r->act_dtype != LNET_BF16) return false;
   if (p->conv_kernel != kTaps || p->conv_dilation != 4) return false;
   if (r->steps < 1 || r->batch < 1) return false;
+  if (reinterpret_cast<uintptr_t>(r->x) % 16 != 0) return false;  // TMA source
   if (r->batch * fused_chunks(r->steps) >= (int64_t)1 << 31) return false;
   for (const auto &s : kFusedShapes)
     if (s.C == p->raw_input_dim && s.D == p->model_dim && s.M == p->modes) return true;
@@ -1255,6 +1311,33 @@ inline bool fused_supported(const lnet_b200_alphabet_params *p,
 int sm_count();
 uint32_t next_epoch();
 int fused_trace_enabled();
+
+// Tiled 3-D tensor map of a [B][T][W] bf16 tensor with an 8 x 144 x 1 box
+// (one K slab of a tile), zero fill outside the tensor.  The driver entry
+// point is resolved once through the runtime.
+inline int encode_tile_map(CUtensorMap *map, const void *base, int64_t B, int64_t T, int W) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!encode) return fail(LNET_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[2] = {(cuuint64_t)W * 2, (cuuint64_t)T * W * 2};
+  const cuuint32_t box[3] = {8, (cuuint32_t)kXRows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) return fail(LNET_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)res);
+  return LNET_OK;
+}
 
 template <int C, int D, int M>
 int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -1271,6 +1354,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   const uint32_t epoch = next_epoch();
   FusedArgs wa{};
   wa.in = (const __nv_bfloat16 *)r->x;
+  LNET_TRY(encode_tile_map(&wa.tmap, r->x, B, T, C));
   wa.B = B;
   wa.T = T;
   wa.n_chunks = nch;
@@ -1299,6 +1383,9 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   LNET_TRY(after_launch("fused_writer_kernel"));
   FusedArgs ra = wa;
   ra.in = w.stream;
+  if (reinterpret_cast<uintptr_t>(w.stream) % 16 != 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  LNET_TRY(encode_tile_map(&ra.tmap, w.stream, B, T, D));
   ra.drive = w.rdrive;
   ra.syn = nullptr;
   ra.consts = w.consts + kConsts * M;

@@ -1,6 +1,7 @@
 // Thin inline-PTX wrappers for the sm_100a features the fused kernels use:
-// mbarriers, tcgen05 (TMEM allocation, UMMA issue/commit, TMEM loads) and
-// acquire/release flag accesses.  Every wait is bounded.
+// mbarriers, TMA tensor loads (never multicast), tcgen05 (TMEM allocation,
+// UMMA issue/commit, TMEM loads) and acquire/release flag accesses.  Every
+// wait is bounded.
 #pragma once
 
 #include <stdint.h>
@@ -42,21 +43,31 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   return false;
 }
 
+// One arrival that also announces `bytes` of asynchronous transfers.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+// 3-D tiled tensor load (no multicast) into this CTA's shared memory; completes
+// `bytes` on `bar`.  c0 (innermost) times the element size must be a multiple
+// of 16 bytes; c1 / c2 may lie outside the tensor (zero fill).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint64_t *bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (UMMA reads).
-// 16-byte global -> shared asynchronous copy (cp.async, L2 only); `src_bytes`
-// 0 copies nothing and zero-fills the 16 destination bytes.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
