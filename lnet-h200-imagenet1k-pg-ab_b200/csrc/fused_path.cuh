@@ -65,6 +65,13 @@ constexpr int KC_AL = 2, KC_AS = 10, KC_A2S = 18, KC_A3S = 20;
 constexpr int kWriterSub = 32, kReaderSub = 32;
 constexpr int kWriterNSub = 4;
 constexpr int kWriterDriveRows = 128, kReaderDriveRows = 128;
+// Thread (of an item stream) that issues the next tile's TMA copies: not
+// thread 0, whose async-unit instructions queue behind its MMAs.
+#if defined(LNET_TILE_ISSUER0)
+constexpr int kTileIssuer = 0;
+#else
+constexpr int kTileIssuer = 32;
+#endif
 
 template <int NSUB>
 struct ScanLayout {
@@ -1022,7 +1029,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 #if defined(LNET_SYN_DEBUG)
     unsigned long long y0 = clock64();
 #endif
-    if (ltid == 0) {
+    if (ltid == kTileIssuer) {
       const int64_t next = item_slot[(iter + 1) & 1];
       if (next < total) issue_tile(next);
     }
@@ -1034,6 +1041,9 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 #pragma unroll
       for (int gq = 0; gq < HD / 8; ++gq) flv[gq] = *reinterpret_cast<const uint4 *>(out_row + 8 * gq);
     }
+#if defined(LNET_SYN_DEBUG)
+    unsigned long long y1b = clock64();
+#endif
     reduce_moments<M, kWriterNSub>(ltid, s_mom, a.partial + (b * a.n_chunks + chunk) * 7 * M);
 #if defined(LNET_SYN_DEBUG)
     unsigned long long y2 = clock64();
@@ -1042,8 +1052,8 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 #if defined(LNET_SYN_DEBUG)
     if (a.trace && ltid == 0) {
       unsigned long long y3 = clock64();
-      atomicAdd(&g_fused_trace[0][8], y1 - y0);
-      atomicAdd(&g_fused_trace[0][9], y2 - y1);
+      atomicAdd(&g_fused_trace[0][8], y1b - y1);
+      atomicAdd(&g_fused_trace[0][9], y2 - y1b);
       atomicAdd(&g_fused_trace[0][13], y3 - y2);
     }
 #endif
@@ -1200,7 +1210,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
     }
     red[half * kChunk + row] = ss;
     __syncthreads();
-    if (tid == 0) {  // every thread has read the tile: fetch the next item's
+    if (tid == kTileIssuer) {  // every thread has read the tile: fetch the next item's
       const int64_t next = item_slot[(iter + 1) & 1];
       if (next < total) issue_tile(next);
     }
