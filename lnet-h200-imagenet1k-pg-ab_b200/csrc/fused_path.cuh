@@ -97,8 +97,12 @@ struct FusedWorkspace {
   __nv_bfloat16 *wsyn = nullptr;       // synthesis B      [2M/8][D][8]
   float *consts = nullptr;             // [2][kConsts * M]
   __nv_bfloat16 *stream = nullptr;     // [B, T, D]
-  float *wpartial = nullptr;           // [B * nch][7M]
-  float *rpartial = nullptr;
+  // per-row moment sums [2 (writer, reader)][B][7M]: every item adds its
+  // chunk's partial moments (fp64 atomics: the sum of a row's ~T/128 fp32
+  // partials is exact in double for any realistic spread, so the result does
+  // not depend on the order of the additions)
+  double *rowsum = nullptr;
+  int64_t rowsum_len = 0;
   // look-back records [B * nch][2 (aggregate, inclusive)][4 states][2 (re, im)][M];
   // each entry = (state bits) | (epoch << 32), single-copy atomic 8-byte words
   unsigned long long *wrec = nullptr;
@@ -122,8 +126,8 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   w.wsyn = ar.take<__nv_bfloat16>((size_t)2 * M * D);
   w.consts = ar.take<float>((size_t)2 * kConsts * M);
   w.stream = ar.take<__nv_bfloat16>((size_t)B * r->steps * D);
-  w.wpartial = ar.take<float>((size_t)B * nch * 7 * M);
-  w.rpartial = ar.take<float>((size_t)B * nch * 7 * M);
+  w.rowsum_len = 2 * B * 7 * M;
+  w.rowsum = ar.take<double>((size_t)w.rowsum_len);
   w.wrec = ar.take<unsigned long long>((size_t)B * nch * 16 * M);
   w.rrec = ar.take<unsigned long long>((size_t)B * nch * 16 * M);
   w.flag_words = 4;
@@ -142,55 +146,66 @@ __device__ __forceinline__ void cmul_d(double ar, double ai, double br, double b
 
 __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace w) {
   const int C = p.raw_input_dim, D = p.model_dim, M = p.modes, K5 = p.conv_kernel;
-  const int64_t n_q = (int64_t)kTaps * C * D;
+  // per-mode ZOH input gains of both blocks, once per CTA (M <= 64)
+  __shared__ float zg[2][2][64];  // [block][re | im][mode]
+  for (int i = threadIdx.x; i < 2 * M; i += blockDim.x) {
+    const int blk = i / M, m = i - (i / M) * M;
+    double damping, frequency;
+    mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
+              blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
+              frequency);
+    const Zoh z = zoh_eval(damping, frequency, 1.0);
+    zg[blk][0][m] = z.g_re;
+    zg[blk][1][m] = z.g_im;
+  }
+  __syncthreads();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < w.rowsum_len;
+       i += (int64_t)gridDim.x * blockDim.x)
+    w.rowsum[i] = 0.0;
+  // every index below 2^31 (operand sizes of one block): 32-bit arithmetic
+  const int n_q = kTaps * C * D;
   // drive A rows per block: 128 (modes repeated every 64 lanes)
-  const int64_t n_wdrive = (int64_t)2 * D * kWriterDriveRows;
-  const int64_t n_rdrive = (int64_t)2 * D * kReaderDriveRows;
-  const int64_t n_syn = (int64_t)2 * M * D;
-  const int64_t total = n_q + n_wdrive + n_rdrive + n_syn + 2 * M;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  const int n_wdrive = 2 * D * kWriterDriveRows;
+  const int n_rdrive = 2 * D * kReaderDriveRows;
+  const int n_syn = 2 * M * D;
+  const int total = n_q + n_wdrive + n_rdrive + n_syn + 2 * M;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     if (i < n_q) {  // Q_k[d][c] = w[d][k] * P[d][c]
-      int k = (int)(i / ((int64_t)C * D));
-      int rem = (int)(i - (int64_t)k * C * D);
+      const int k = i / (C * D);
+      const int rem = i - k * C * D;
       int d = rem / C, c = rem - d * C;
       double v = (double)p.stem_conv_weight[d * K5 + k] * (double)p.stem_projection[d * C + c];
-      w.q[(int64_t)k * C * D + ((c / 8) * D + d) * 8 + (c % 8)] = __float2bfloat16_rn((float)v);
+      w.q[k * C * D + ((c / 8) * D + d) * 8 + (c % 8)] = __float2bfloat16_rn((float)v);
       continue;
     }
-    int64_t j = i - n_q;
+    int j = i - n_q;
     if (j < n_wdrive + n_rdrive) {  // drive A: lane r holds mode r % 64 (zero if >= M), K = d
       const int blk = j < n_wdrive ? 0 : 1;
       const int R = blk == 0 ? kWriterDriveRows : kReaderDriveRows;
-      int64_t rem = blk == 0 ? j : j - n_wdrive;
-      int part = (int)(rem / ((int64_t)D * R));
-      int rem2 = (int)(rem - (int64_t)part * D * R);
+      const int rem = blk == 0 ? j : j - n_wdrive;
+      const int part = rem / (D * R);
+      const int rem2 = rem - part * D * R;
       int d = rem2 / R, r = rem2 - d * R;
       int m = r % 64;
       float out = 0.f;
       if (m < M) {
         const float *frame = blk == 0 ? p.writer_frame : p.reader_frame;
-        double damping, frequency;
-        mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
-                  blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
-                  frequency);
-        Zoh z = zoh_eval(damping, frequency, 1.0);
+        const double gr = zg[blk][0][m], gi = zg[blk][1][m];
         double fr = frame[d * 2 * M + m], fi = frame[d * 2 * M + M + m];
-        out = (float)(part == 0 ? (double)z.g_re * fr - (double)z.g_im * fi
-                                : (double)z.g_re * fi + (double)z.g_im * fr);
+        out = (float)(part == 0 ? gr * fr - gi * fi : gr * fi + gi * fr);
       }
       __nv_bfloat16 *dst = blk == 0 ? w.wdrive : w.rdrive;
-      dst[(int64_t)part * D * R + ((d / 8) * R + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
+      dst[part * D * R + ((d / 8) * R + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
       continue;
     }
     j -= n_wdrive + n_rdrive;
     if (j < n_syn) {  // synthesis B rows = d, K = 2M
-      int d = (int)(j / (2 * M)), jj = (int)(j - (int64_t)d * 2 * M);
+      const int d = j / (2 * M), jj = j - d * 2 * M;
       w.wsyn[((jj / 8) * D + d) * 8 + (jj % 8)] = __float2bfloat16_rn(p.writer_frame[d * 2 * M + jj]);
       continue;
     }
     j -= n_syn;  // per-mode constants of both blocks
-    int blk = (int)(j / M), m = (int)(j - (int64_t)blk * M);
+    const int blk = j / M, m = j - blk * M;
     double damping, frequency;
     mode_pole(blk == 0 ? p.writer_raw_decay[m] : p.reader_raw_decay[m],
               blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
@@ -200,7 +215,7 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
     // double so that carries match step-by-step propagation.
     const double ar = (double)z.a_re, ai = (double)z.a_im;
     double pr = 1.0, pi = 0.0;
-    float *k = w.consts + (int64_t)blk * kConsts * M;
+    float *k = w.consts + blk * kConsts * M;
     for (int step = 1; step <= kChunk; ++step) {
       double nr, ni;
       cmul_d(pr, pi, ar, ai, nr, ni);
@@ -258,7 +273,7 @@ struct FusedArgs {
   const float *consts;      // kConsts * M floats of this block
   const float *conv_w, *conv_b, *norm, *ds, *ls;
   __nv_bfloat16 *out;       // writer stream
-  float *partial;           // [B * nch][7M]
+  double *rowsum;           // this block's per-row moment sums [B][7M]
   unsigned long long *rec;  // [B * nch][2][4][2][M] tagged look-back records
   uint32_t epoch;           // tag of this call's records
   uint32_t *counter;
@@ -359,8 +374,8 @@ __device__ __forceinline__ bool ld_tag(const unsigned long long *p, uint32_t epo
 //   barriers.
 // Sub-chunk q covers steps [SUB q, SUB q + SUB), SUB = 128 / NSUB.  u_re / u_im
 // live in TMEM columns [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's
-// moment partial sums [7][M] to `partial` (or leaves the per-sub-chunk sums in
-// `mom_out` for the caller to reduce with reduce_moments).
+// moment partial sums [7][M] to the row's sums `rowsum` (or leaves the
+// per-sub-chunk sums in `mom_out` for the caller to add with reduce_moments).
 
 // Named barrier over one 256-thread item stream.  The non-aligned form counts
 // threads, so it stays correct when a warp reaches it diverged (e.g. after a
@@ -411,7 +426,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
                                            unsigned long long *rec, uint32_t epoch,
                                            uint32_t *error,
                                            uint8_t *s_slab, int slab_s, float *sc,
-                                           float *partial, int trace, int kid,
+                                           double *rowsum, int trace, int kid,
                                            const LookbackPrefetch &pre,
                                            float *mom_out = nullptr) {
   using L = ScanLayout<NSUB>;
@@ -770,19 +785,20 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
     float acc = 0.f;
 #pragma unroll
     for (int qq = 0; qq < NSUB; ++qq) acc += mo[qq * 7 * 64];
-    partial[j] = acc;
+    atomicAdd(rowsum + j, (double)acc);
   }
 }
 
-// Sums the per-sub-chunk moment partials [NSUB][7][64] into partial[7][M].
+// Adds the per-sub-chunk moment partials [NSUB][7][64] of one chunk to the
+// row's sums rowsum[7][M].
 template <int M, int NSUB>
-__device__ __forceinline__ void reduce_moments(int ltid, const float *mom, float *partial) {
+__device__ __forceinline__ void reduce_moments(int ltid, const float *mom, double *rowsum) {
   for (int j = ltid; j < 7 * M; j += kFusedThreads) {
     const int k = j / M, mm = j - (j / M) * M;
     float acc = 0.f;
 #pragma unroll
     for (int qq = 0; qq < NSUB; ++qq) acc += mom[qq * 7 * 64 + k * 64 + mm];
-    partial[j] = acc;
+    atomicAdd(rowsum + j, (double)acc);
   }
 }
 
@@ -1011,7 +1027,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
                                      a.n_chunks, s_k, a.rec, a.epoch, a.error, gs + P::G_XS,
                                      P::SLAB_S, s_scan,
-                                     a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace,
+                                     a.rowsum + b * 7 * M, a.trace,
                                      a.kernel_id, pre, s_mom);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
@@ -1044,7 +1060,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
 #if defined(LNET_SYN_DEBUG)
     unsigned long long y1b = clock64();
 #endif
-    reduce_moments<M, kWriterNSub>(ltid, s_mom, a.partial + (b * a.n_chunks + chunk) * 7 * M);
+    reduce_moments<M, kWriterNSub>(ltid, s_mom, a.rowsum + b * 7 * M);
 #if defined(LNET_SYN_DEBUG)
     unsigned long long y2 = clock64();
 #endif
@@ -1248,7 +1264,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
     // 4. scan + look-back + moments
     chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
                             a.epoch, a.error, nullptr, 0, s_scan,
-                            a.partial + (b * a.n_chunks + chunk) * 7 * M, a.trace, a.kernel_id,
+                            a.rowsum + b * 7 * M, a.trace, a.kernel_id,
                             pre);
     sm100::tc_fence_before();
     __syncthreads();
@@ -1266,37 +1282,45 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
 }
 
 // ---------------------------------------------------------------- moments finalize
-// Per (row, block, mode): sums the chunk partials in order, divides by the
-// counts (T, or T - lag; 0 if T <= lag) and writes the raw moments
-// [b][k*M + m] and the radial-log features of src/lnet/alphabet.py:29-46 into
-// feats[b][blk * 7M + k*M + m].
-__global__ void fused_finalize_kernel(const float *__restrict__ wpart,
-                                      const float *__restrict__ rpart, float *__restrict__ wm,
+// Moment k of the row sums divided by its count (T, or T - lag; 0 if T <= lag).
+__device__ __forceinline__ float finalize_moment(const double *rs, int modes, int j,
+                                                 int64_t steps) {
+  const int k = j / modes;
+  if (k == 0) return (float)(rs[j] / (double)steps);
+  const int lag = k <= 2 ? 1 : (k <= 4 ? 2 : 4);
+  return steps <= lag ? 0.f : (float)(rs[j] / (double)(steps - lag));
+}
+
+// One thread per (row, feature): raw moments [b][k*M + m] of both blocks and
+// the radial-log features of src/lnet/alphabet.py:29-46 (the arithmetic of
+// radial_feature) into feats[b][blk * 7M + j].
+__global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *__restrict__ wm,
                                       float *__restrict__ rm, float *__restrict__ feats,
-                                      int64_t steps, int modes, int64_t n_chunks) {
-  extern __shared__ float mom[];  // [7M]
-  const int64_t b = blockIdx.x;
-  const int blk = blockIdx.y;
-  const float *part = blk == 0 ? wpart : rpart;
-  float *out = blk == 0 ? wm : rm;
-  const int lags[3] = {1, 2, 4};
-  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) {
-    const int k = j / modes;
-    double acc = 0.0;
-    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)part[(b * n_chunks + c) * 7 * modes + j];
-    float v;
-    if (k == 0) {
-      v = (float)(acc / (double)steps);
+                                      int64_t batch, int64_t steps, int modes) {
+  const int W = 7 * modes;
+  const int64_t n = batch * 2 * W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / (2 * W);
+    const int jj = (int)(i - b * 2 * W), blk = jj >= W ? 1 : 0, j = jj - blk * W;
+    const double *rs = rowsum + (blk * batch + b) * W;
+    const float v = finalize_moment(rs, modes, j, steps);
+    (blk == 0 ? wm : rm)[b * W + j] = v;
+    float f;
+    if (j < modes) {
+      f = log1pf(fmaxf(v, 0.f));
     } else {
-      const int lag = lags[(k - 1) / 2];
-      v = steps <= lag ? 0.f : (float)(acc / (double)(steps - lag));
+      const int pair = (j - modes) / (2 * modes);
+      const int within = (j - modes) - pair * 2 * modes;
+      const int base = modes + pair * 2 * modes, mm = within % modes;
+      const float re = finalize_moment(rs, modes, base + mm, steps);
+      const float im = finalize_moment(rs, modes, base + modes + mm, steps);
+      const float r = sqrtf(fmaxf(re * re + im * im, kFp32Tiny));
+      const float scale = log1pf(r) / r;
+      f = scale * (within < modes ? re : im);
     }
-    out[b * 7 * modes + j] = v;
-    mom[j] = v;
+    feats[b * 2 * W + jj] = f;
   }
-  __syncthreads();
-  float *f = feats + b * 14 * modes + blk * 7 * modes;
-  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) f[j] = radial_feature(mom, modes, j);
 }
 
 // ---------------------------------------------------------------- dispatch
@@ -1313,6 +1337,7 @@ inline bool fused_supported(const lnet_b200_alphabet_params *p,
   if (r->steps < 1 || r->batch < 1) return false;
   if (reinterpret_cast<uintptr_t>(r->x) % 16 != 0) return false;  // TMA source
   if (r->batch * fused_chunks(r->steps) >= (int64_t)1 << 31) return false;
+  if (r->batch * 14 * p->modes >= (int64_t)1 << 31) return false;
   for (const auto &s : kFusedShapes)
     if (s.C == p->raw_input_dim && s.D == p->model_dim && s.M == p->modes) return true;
   return false;
@@ -1356,7 +1381,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   using RP = ReaderPlan<D, M>;
   const int64_t B = r->batch, T = r->steps, nch = fused_chunks(T);
   const int sms = sm_count();
-  fused_prepare_kernel<<<64, 256, 0, st>>>(*p, w);
+  fused_prepare_kernel<<<sms, 256, 0, st>>>(*p, w);
   LNET_TRY(after_launch("fused_prepare_kernel"));
   LNET_TRY(cuda_check(cudaMemsetAsync(w.flags, 0, w.flag_words * sizeof(uint32_t), st),
                       "cudaMemsetAsync(flags)"));
@@ -1377,7 +1402,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.ds = p->writer_direct_scale;
   wa.ls = p->writer_layer_scale;
   wa.out = w.stream;
-  wa.partial = w.wpartial;
+  wa.rowsum = w.rowsum;
   wa.rec = w.wrec;
   wa.epoch = epoch;
   wa.counter = counters;
@@ -1403,7 +1428,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   ra.conv_b = p->reader_conv_bias;
   ra.norm = p->reader_norm;
   ra.out = nullptr;
-  ra.partial = w.rpartial;
+  ra.rowsum = w.rowsum + B * 7 * M;
   ra.rec = w.rrec;
   ra.counter = counters + 1;
   ra.kernel_id = 1;
@@ -1414,8 +1439,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   fused_reader_kernel<D, M><<<(unsigned)std::min<int64_t>(items, 2 * (int64_t)sms),
                               kFusedThreads, RP::LAUNCH_BYTES, st>>>(ra);
   LNET_TRY(after_launch("fused_reader_kernel"));
-  fused_finalize_kernel<<<dim3((unsigned)B, 2), 256, 7 * M * sizeof(float), st>>>(
-      w.wpartial, w.rpartial, wm, rm, w.feats, T, M, nch);
+  fused_finalize_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * 14 * M, 256), 8 * sms), 256, 0,
+                          st>>>(w.rowsum, wm, rm, w.feats, B, T, M);
   return after_launch("fused_finalize_kernel");
 }
 

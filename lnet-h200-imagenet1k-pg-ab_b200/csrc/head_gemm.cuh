@@ -190,7 +190,7 @@ __global__ void head_reduce_kernel(const float *__restrict__ partial, const floa
   }
 }
 
-constexpr int kHeadSplits = 4;
+constexpr int kHeadSplits = 4;  // measured best at B=256, K=1000 (6 and 11 are slower)
 
 inline size_t head_partial_floats(int64_t B, int K) { return (size_t)kHeadSplits * B * K; }
 
