@@ -170,6 +170,19 @@ int lnet_b200_head(const lnet_b200_alphabet_params *params, int64_t batch,
                    const float *writer_moments, const float *reader_moments, float *logits,
                    lnet_stream_t stream);
 
+/* Input pipeline of the image configuration: uint8 images [B, H, W, 3]
+ * (device) -> tokens [B, (H/p)(W/p), 3 p^2] (`tokens_dtype` LNET_BF16 or
+ * LNET_F32), per element v = (u / 255 - mean[ch]) / std[ch] in fp32 (IEEE
+ * divisions) and token channel (i * p + j) * 3 + ch for pixel (i, j) of the
+ * patch.  `mean` and `std` are HOST arrays of 3 floats.  Replaces the
+ * harness transform ConvertImageDtype(float32) + Normalize(mean, std)
+ * (scripts/train_alphabet2d_imagenet100.py:292-310) followed by the 4x4
+ * patchify reshape, so that a caller can copy uint8 images (half the bytes of
+ * bf16 tokens) to the device. */
+int lnet_b200_patchify_images(const uint8_t *images, int64_t batch, int32_t height,
+                              int32_t width, int32_t patch, const float *mean, const float *std,
+                              void *tokens, int32_t tokens_dtype, lnet_stream_t stream);
+
 /* Pole-residue Laplace layer in float64:
  *   y_t = sum_{m,i} R[o, m, i] s_t[m, i] + D x_t + bias,
  *   s_t[m, i] = exp(p_m dt) s_{t-1}[m, i] + dt phi1(p_m dt) x_t[i],

@@ -8,6 +8,10 @@ Laplace layer behind the reference ``lnet`` module API.
 * :mod:`lnet_b200.ops` — the same calls as ``torch.library`` custom ops
   (``lnet_b200::alphabet_forward``, ``lnet_b200::laplace_forward``).
 * :mod:`lnet_b200.sharding` — batch sharding over one process per GPU.
+* :mod:`lnet_b200.images` — uint8 images -> normalised 4x4 patch tokens on the
+  GPU (:meth:`B200Alphabet.forward_images`).
+* :mod:`lnet_b200.pipeline` — host-fed serving loop overlapping the copies of
+  the next batch with the current forward.
 
 All compute runs in the C-ABI CUDA library ``_lib/liblnet_b200.so`` built by
 :func:`lnet_b200.build.build`; there is no CPU fallback.

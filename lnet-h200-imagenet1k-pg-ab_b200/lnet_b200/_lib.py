@@ -113,6 +113,11 @@ SIGNATURES = {
     "lnet_b200_head": (
         ctypes.c_int, [ctypes.POINTER(AlphabetParams), _i64, _c_p, _c_p, _c_p, _c_p]
     ),
+    "lnet_b200_patchify_images": (
+        ctypes.c_int,
+        [_c_p, _i64, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_float),
+         ctypes.POINTER(ctypes.c_float), _c_p, _i32, _c_p],
+    ),
     "lnet_b200_laplace_workspace_size": (
         ctypes.c_int, [_i64, _i64, _i32, _i32, ctypes.POINTER(ctypes.c_size_t)]
     ),

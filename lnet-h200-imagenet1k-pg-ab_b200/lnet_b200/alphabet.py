@@ -320,6 +320,17 @@ class B200Alphabet(nn.Module):
             return logits, wm, rm
         return logits
 
+    def forward_images(self, images: Tensor, *, mean=None, std=None, patch: int = 4,
+                       dtype: torch.dtype = torch.bfloat16, return_moments: bool = False):
+        """Forward from uint8 images [B, H, W, 3] on CUDA: normalise + patchify on
+        the GPU (:func:`lnet_b200.images.patchify_images`, bit-identical to the
+        harness transform), then :meth:`forward` on the tokens."""
+        from .images import IMAGENET_MEAN, IMAGENET_STD, patchify_images
+
+        x = patchify_images(images, mean=IMAGENET_MEAN if mean is None else mean,
+                            std=IMAGENET_STD if std is None else std, patch=patch, dtype=dtype)
+        return self.forward(x, return_moments=return_moments)
+
 
 def _has_param(module: nn.Module, name: str) -> bool:
     try:

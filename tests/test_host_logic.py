@@ -89,3 +89,19 @@ def test_training_mode_refused():
             m(torch.randn(2, 6, 3, device="cuda"))
         else:
             raise RuntimeError("CUDA")
+
+
+def test_patchify_reference_layout():
+    """Token channel (i * p + j) * 3 + ch of patch (pr, pc) is pixel (pr p + i, pc p + j, ch),
+    normalised as (u / 255 - mean) / std in fp32."""
+    from lnet_b200.images import patchify_images_reference
+
+    g = torch.Generator().manual_seed(0)
+    img = torch.randint(0, 256, (2, 6, 8, 3), generator=g, dtype=torch.uint8)
+    mean, std = (0.1, 0.2, 0.3), (0.5, 0.25, 2.0)
+    x = patchify_images_reference(img, mean=mean, std=std, patch=2, dtype=torch.float32)
+    assert x.shape == (2, 3 * 4, 12)
+    for b, pr, pc, i, j, ch in [(0, 0, 0, 0, 0, 0), (1, 2, 3, 1, 0, 2), (0, 1, 2, 1, 1, 1)]:
+        u = torch.tensor(float(img[b, pr * 2 + i, pc * 2 + j, ch]))
+        want = (u / 255.0 - torch.tensor(mean[ch])) / torch.tensor(std[ch])
+        assert x[b, pr * 4 + pc, (i * 2 + j) * 3 + ch] == want
