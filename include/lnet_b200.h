@@ -115,6 +115,25 @@ int lnet_b200_set_route(int route);
 int lnet_b200_alphabet_route(const lnet_b200_alphabet_params *params,
                              const lnet_b200_alphabet_request *req);
 
+/* Prepared static inference (replaces Alphabet.prepare_for_inference_,
+ * src/lnet/alphabet.py:190-222): lnet_b200_alphabet_prepare writes the fused
+ * route's prepared operands (bf16 GEMM operand slabs with the ZOH gains folded
+ * in, pole constants) for `params` into `workspace`; they sit at the start of
+ * the workspace at offsets that depend on (C, D, M) only.
+ * lnet_b200_alphabet_forward_prepared is lnet_b200_alphabet_forward without
+ * rebuilding them: valid while the parameters are unchanged and for every
+ * request whose workspace size (lnet_b200_alphabet_workspace_size) fits in
+ * `workspace_bytes`.  Requests that take the general route ignore the
+ * preparation.  Calls sharing a workspace must be ordered (one stream). */
+int lnet_b200_alphabet_prepare(const lnet_b200_alphabet_params *params,
+                               const lnet_b200_alphabet_request *req, void *workspace,
+                               size_t workspace_bytes, lnet_stream_t stream);
+int lnet_b200_alphabet_forward_prepared(const lnet_b200_alphabet_params *params,
+                                        const lnet_b200_alphabet_request *req, void *workspace,
+                                        size_t workspace_bytes, float *logits,
+                                        float *writer_moments, float *reader_moments,
+                                        lnet_stream_t stream);
+
 /* Device-side status of the last lnet_b200_alphabet_forward that ran the fused
  * route in `workspace` (synchronises the device; 0 for the general route).
  * Every wait inside the fused kernels is bounded; a wait that gave up sets a

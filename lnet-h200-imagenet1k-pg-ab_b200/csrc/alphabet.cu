@@ -333,11 +333,10 @@ extern "C" int lnet_b200_alphabet_workspace_size(const lnet_b200_alphabet_params
   return LNET_OK;
 }
 
-extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
-                                          const lnet_b200_alphabet_request *req, void *workspace,
-                                          size_t workspace_bytes, float *logits,
-                                          float *writer_moments, float *reader_moments,
-                                          lnet_stream_t stream) {
+static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
+                                 const lnet_b200_alphabet_request *req, void *workspace,
+                                 size_t workspace_bytes, float *logits, float *writer_moments,
+                                 float *reader_moments, bool prepared, lnet_stream_t stream) {
   reset_launches();
   LNET_TRY(check_params(params));
   LNET_TRY(check_request(params, req));
@@ -354,7 +353,7 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
     LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, true));
     float *wm = writer_moments ? writer_moments : pl.fused.moments;
     float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
-    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, st));
+    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, prepared, st));
     return head_gemm(pl.fused.feats, B, 14 * M, params->head_weight, params->head_bias, logits,
                      params->output_dim, pl.fused.head_partial, st);
   }
@@ -368,6 +367,38 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
   LNET_TRY(writer_generic(params, req, pl.first_local, pl, pl.stream, wm, st));
   LNET_TRY(reader_generic(params, req, pl.stream, pl, rm, st));
   return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st);
+}
+
+extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
+                                          const lnet_b200_alphabet_request *req, void *workspace,
+                                          size_t workspace_bytes, float *logits,
+                                          float *writer_moments, float *reader_moments,
+                                          lnet_stream_t stream) {
+  return alphabet_forward_impl(params, req, workspace, workspace_bytes, logits, writer_moments,
+                               reader_moments, false, stream);
+}
+
+extern "C" int lnet_b200_alphabet_prepare(const lnet_b200_alphabet_params *params,
+                                          const lnet_b200_alphabet_request *req, void *workspace,
+                                          size_t workspace_bytes, lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  auto st = (cudaStream_t)stream;
+  begin_entry(st);
+  if (req->batch == 0 || req->steps == 0 || !use_fused(params, req)) return LNET_OK;
+  Plan pl;
+  LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, true));
+  return fused_prepare(params, pl.fused, st);
+}
+
+extern "C" int lnet_b200_alphabet_forward_prepared(const lnet_b200_alphabet_params *params,
+                                                   const lnet_b200_alphabet_request *req,
+                                                   void *workspace, size_t workspace_bytes,
+                                                   float *logits, float *writer_moments,
+                                                   float *reader_moments, lnet_stream_t stream) {
+  return alphabet_forward_impl(params, req, workspace, workspace_bytes, logits, writer_moments,
+                               reader_moments, true, stream);
 }
 
 extern "C" int lnet_b200_stem(const lnet_b200_alphabet_params *params,

@@ -117,19 +117,21 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
                        const lnet_b200_alphabet_request *r) {
   const int C = p->raw_input_dim, D = p->model_dim, M = p->modes;
   const int64_t B = r->batch, nch = fused_chunks(std::max<int64_t>(r->steps, 1));
-  w.moments = ar.take<float>((size_t)2 * B * 7 * M);
-  w.feats = ar.take<float>((size_t)B * 14 * M);
-  w.head_partial = ar.take<float>(head_partial_floats(B, p->output_dim));
+  // prepared operands first: their offsets depend on (C, D, M) only, so a
+  // workspace prepared once serves every batch and length it is large enough for
   w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
   w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * kWriterDriveRows);
   w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
   w.wsyn = ar.take<__nv_bfloat16>((size_t)2 * M * D);
   w.consts = ar.take<float>((size_t)2 * kConsts * M);
+  w.moments = ar.take<float>((size_t)2 * B * 7 * M);
+  w.feats = ar.take<float>((size_t)B * 14 * M);
+  w.head_partial = ar.take<float>(head_partial_floats(B, p->output_dim));
   w.stream = ar.take<__nv_bfloat16>((size_t)B * r->steps * D);
-  w.rowsum_len = 2 * B * 7 * M;
-  w.rowsum = ar.take<double>((size_t)w.rowsum_len);
   w.wrec = ar.take<unsigned long long>((size_t)B * nch * 16 * M);
   w.rrec = ar.take<unsigned long long>((size_t)B * nch * 16 * M);
+  w.rowsum_len = 2 * B * 7 * M;  // zeroed with the flags by one memset per call
+  w.rowsum = ar.take<double>((size_t)w.rowsum_len);
   w.flag_words = 4;
   w.flags = ar.take<uint32_t>(w.flag_words);
 }
@@ -159,9 +161,6 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
     zg[blk][1][m] = z.g_im;
   }
   __syncthreads();
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < w.rowsum_len;
-       i += (int64_t)gridDim.x * blockDim.x)
-    w.rowsum[i] = 0.0;
   // every index below 2^31 (operand sizes of one block): 32-bit arithmetic
   const int n_q = kTaps * C * D;
   // drive A rows per block: 128 (modes repeated every 64 lanes)
@@ -1374,17 +1373,28 @@ inline int encode_tile_map(CUtensorMap *map, const void *base, int64_t B, int64_
   return LNET_OK;
 }
 
+// Writes the prepared operands (bf16 slabs, pole constants) of `p` into `w`.
+inline int fused_prepare(const lnet_b200_alphabet_params *p, FusedWorkspace &w, cudaStream_t st) {
+  fused_prepare_kernel<<<sm_count(), 256, 0, st>>>(*p, w);
+  return after_launch("fused_prepare_kernel");
+}
+
+// `prepared`: the operands in `w` were written by fused_prepare for these
+// parameters (lnet_b200_alphabet_prepare) and are not rebuilt.
 template <int C, int D, int M>
 int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
-                        FusedWorkspace &w, float *wm, float *rm, cudaStream_t st) {
+                        FusedWorkspace &w, float *wm, float *rm, bool prepared, cudaStream_t st) {
   using WP = WriterPlan<C, D, M>;
   using RP = ReaderPlan<D, M>;
   const int64_t B = r->batch, T = r->steps, nch = fused_chunks(T);
   const int sms = sm_count();
-  fused_prepare_kernel<<<sms, 256, 0, st>>>(*p, w);
-  LNET_TRY(after_launch("fused_prepare_kernel"));
-  LNET_TRY(cuda_check(cudaMemsetAsync(w.flags, 0, w.flag_words * sizeof(uint32_t), st),
-                      "cudaMemsetAsync(flags)"));
+  if (!prepared) LNET_TRY(fused_prepare(p, w, st));
+  // per-call state: the row moment sums and, right behind them, counters and error words
+  LNET_TRY(cuda_check(cudaMemsetAsync(w.rowsum, 0,
+                                      reinterpret_cast<char *>(w.flags + w.flag_words) -
+                                          reinterpret_cast<char *>(w.rowsum),
+                                      st),
+                      "cudaMemsetAsync(row sums, flags)"));
   uint32_t *counters = w.flags;
   const uint32_t epoch = next_epoch();
   FusedArgs wa{};
@@ -1445,9 +1455,9 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 }
 
 inline int fused_forward(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
-                         FusedWorkspace &w, float *wm, float *rm, cudaStream_t st) {
+                         FusedWorkspace &w, float *wm, float *rm, bool prepared, cudaStream_t st) {
   if (p->raw_input_dim == 48 && p->model_dim == 96 && p->modes == 48)
-    return fused_forward_shape<48, 96, 48>(p, r, w, wm, rm, st);
+    return fused_forward_shape<48, 96, 48>(p, r, w, wm, rm, prepared, st);
   return fail(LNET_ERR_UNSUPPORTED, "no fused kernel instance for C=%d D=%d M=%d",
               p->raw_input_dim, p->model_dim, p->modes);
 }

@@ -151,6 +151,8 @@ class B200Alphabet(nn.Module):
                                       groups=model_dim)
         self._cache_key = None
         self._cache = None
+        self._prepare_spec = None  # (batch, length) once prepare_for_inference_ ran
+        self._prep = None          # persistent workspace of the prepared path
 
     # ------------------------------------------------------------ construction helpers
     @classmethod
@@ -320,6 +322,22 @@ class B200Alphabet(nn.Module):
             return logits, wm, rm
         return logits
 
+    @torch.no_grad()
+    def prepare_for_inference_(self, *, sequence_length: int, batch_size: int,
+                               use_static_poles: bool = True) -> B200Alphabet:
+        """Prepared static inference (the reference's ``Alphabet.prepare_for_inference_``,
+        src/lnet/alphabet.py:190-222): later forwards keep one workspace and build the
+        fused route's operands (bf16 GEMM slabs with the ZOH gains folded in, pole
+        constants; ``lnet_b200_alphabet_prepare``) once instead of per call, rebuilding
+        them only when a parameter changes (version counters) or the workspace grows.
+        ``batch_size`` x ``sequence_length`` sizes the workspace up front; larger
+        requests grow it.  ``use_static_poles=False`` turns preparation off.  Calls of a
+        prepared module must be ordered on one CUDA stream (they share the workspace)."""
+        self.eval()
+        self._prepare_spec = (int(batch_size), int(sequence_length)) if use_static_poles else None
+        self._prep = None
+        return self
+
     def forward_images(self, images: Tensor, *, mean=None, std=None, patch: int = 4,
                        dtype: torch.dtype = torch.bfloat16, return_moments: bool = False):
         """Forward from uint8 images [B, H, W, 3] on CUDA: normalise + patchify on
@@ -355,15 +373,47 @@ def alphabet_forward_raw(model: B200Alphabet, x: Tensor, delta, obs, valid, act_
         wm = torch.empty(b, 7 * m, device=x.device, dtype=torch.float32)
         rm = torch.empty(b, 7 * m, device=x.device, dtype=torch.float32)
     nbytes = _workspace_bytes(params, req)
-    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
+    if getattr(model, "_prepare_spec", None) is not None:
+        ws, nbytes = _prepared_workspace(model, params, req, nbytes, x.device, stream)
+        fn, name = lib.lnet_b200_alphabet_forward_prepared, "lnet_b200_alphabet_forward_prepared"
+    else:
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+        fn, name = lib.lnet_b200_alphabet_forward, "lnet_b200_alphabet_forward"
     with torch.cuda.device(x.device):
-        st = lib.lnet_b200_alphabet_forward(
-            ctypes_ref(params), ctypes_ref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
-            None if wm is None else wm.data_ptr(), None if rm is None else rm.data_ptr(), stream,
-        )
-    _lib.check(st, "lnet_b200_alphabet_forward")
+        st = fn(ctypes_ref(params), ctypes_ref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
+                None if wm is None else wm.data_ptr(), None if rm is None else rm.data_ptr(),
+                stream)
+    _lib.check(st, name)
     return logits, wm, rm
+
+
+def _prepared_workspace(model, params, req, need: int, device, stream):
+    """The prepared module's persistent workspace, (re)prepared when the parameters
+    changed, the request needs more room, or the request takes the fused route and
+    the operands have not been built yet."""
+    lib = _lib.load()
+    fused = lib.lnet_b200_alphabet_route(ctypes_ref(params), ctypes_ref(req)) == 0
+    prep = model._prep
+    key = (device, model._cache_key)
+    if prep is None or prep["key"] != key or prep["cap"] < need:
+        b, t = model._prepare_spec
+        sized = _lib.AlphabetRequest(batch=b, steps=t, x_dtype=req.x_dtype,
+                                     act_dtype=req.act_dtype, x=req.x,
+                                     obs_channels=req.obs_channels)
+        cap = max(need, _workspace_bytes(params, sized))
+        if prep is not None and prep["key"][0] == device and prep["cap"] >= cap:
+            ws, cap = prep["ws"], prep["cap"]  # parameters changed: rebuild in place
+        else:
+            ws = torch.empty(max(cap, 1), dtype=torch.uint8, device=device)
+        prep = model._prep = {"key": key, "ws": ws, "cap": cap, "fused": False}
+    if fused and not prep["fused"]:
+        with torch.cuda.device(device):
+            _lib.check(lib.lnet_b200_alphabet_prepare(ctypes_ref(params), ctypes_ref(req),
+                                                      prep["ws"].data_ptr(), prep["cap"], stream),
+                       "lnet_b200_alphabet_prepare")
+        prep["fused"] = True
+    return prep["ws"], prep["cap"]
 
 
 def _workspace_bytes(params, req) -> int:
