@@ -11,6 +11,9 @@
 #include <atomic>
 #include <chrono>
 
+#include <type_traits>
+
+#include "blas.cuh"
 #include "common.cuh"
 #include "fused_path.cuh"
 #include "generic_kernels.cuh"
@@ -44,6 +47,14 @@ int sm_count() {
 constexpr int kMomChunk = 64;
 
 static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), 148 * 32)); }
+// Token-major elementwise kernels: blocks stride over tokens, threads over the
+// channels of a token.
+static unsigned token_grid(int64_t tokens) {
+  // one block per token (a serial token loop per block leaves the loads of
+  // consecutive tokens unoverlapped); the kernels stride past 2^31 - 1
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(tokens, INT32_MAX));
+}
+static unsigned token_block(int width) { return (unsigned)std::min(256, std::max(32, (width + 31) / 32 * 32)); }
 
 // ---------------------------------------------------------------- validation
 static int check_params(const lnet_b200_alphabet_params *p) {
@@ -93,7 +104,8 @@ struct Plan {
   float *ts = nullptr;        // [BT]
   float *carries = nullptr;   // [B, nchunk, 4M]
   float *partial = nullptr;   // moment partials
-  float *a_tab = nullptr;     // [4][M] writer a_re, a_im, reader a_re, a_im
+  float *a_tab = nullptr;     // [8][M] a_re, a_im (writer, reader), then g_re, g_im (writer, reader)
+  __nv_bfloat16 *w_bf16 = nullptr;  // [D, C] stem projection in bf16 (bf16 inputs)
   float *moments = nullptr;   // [2][B][7M]
   float *feats = nullptr;     // [B, 14M]
   float *head_partial = nullptr;  // split-K partial logits
@@ -116,7 +128,8 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.ts = ar.take<float>((size_t)bt);
   pl.carries = ar.take<float>((size_t)r->batch * n_scan * 4 * M);
   pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
-  pl.a_tab = ar.take<float>((size_t)4 * M);
+  pl.a_tab = ar.take<float>((size_t)8 * M);
+  pl.w_bf16 = ar.take<__nv_bfloat16>((size_t)D * C);
   pl.moments = ar.take<float>((size_t)2 * r->batch * 7 * M);
   pl.feats = ar.take<float>((size_t)r->batch * 14 * M);
   pl.head_partial = ar.take<float>(head_partial_floats(r->batch, p->output_dim));
@@ -129,18 +142,23 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const int C = p->raw_input_dim, D = p->model_dim;
   const TX *x = (const TX *)r->x;
-  dim3 g((unsigned)cdiv(bt, 64), (unsigned)cdiv(D, 64));
+  const bool tf32 = r->act_dtype == LNET_BF16;
   if (r->observation_mask || r->valid_mask) {
-    mask_inputs_kernel<TX><<<grid_for(bt * C), 256, 0, st>>>(x, r->observation_mask,
-                                                             r->obs_channels, r->valid_mask,
-                                                             pl.xm, bt, C);
+    mask_inputs_kernel<TX><<<token_grid(bt), token_block(C), 0, st>>>(
+        x, r->observation_mask, r->obs_channels, r->valid_mask, pl.xm, bt, C);
     LNET_TRY(after_launch("mask_inputs_kernel"));
-    gemm_nt_kernel<float><<<g, 256, 0, st>>>(pl.xm, C, p->stem_projection, C, 1, pl.proj, D, bt,
-                                             D, C);
-  } else {
-    gemm_nt_kernel<TX><<<g, 256, 0, st>>>(x, C, p->stem_projection, C, 1, pl.proj, D, bt, D, C);
+    LNET_TRY(gemm_rows(st, pl.xm, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, pl.proj, D,
+                       bt, D, C, tf32, "cublas(stem)"));
+  } else if (std::is_same<TX, float>::value) {
+    LNET_TRY(gemm_rows(st, x, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, pl.proj, D, bt,
+                       D, C, tf32, "cublas(stem)"));
+  } else {  // bf16 x: bf16 x bf16 -> fp32 (the weights rounded to bf16, as under autocast)
+    to_bf16_kernel<<<grid_for((int64_t)D * C), 256, 0, st>>>(p->stem_projection, pl.w_bf16,
+                                                             (int64_t)D * C);
+    LNET_TRY(after_launch("to_bf16_kernel"));
+    LNET_TRY(gemm_rows(st, x, CUDA_R_16BF, C, pl.w_bf16, CUDA_R_16BF, C, 1, pl.proj, D, bt, D, C,
+                       false, "cublas(stem)"));
   }
-  LNET_TRY(after_launch("gemm_nt_kernel(stem)"));
   if (r->time_delta) {
     timestamps_kernel<<<(unsigned)cdiv(B, 128), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
     LNET_TRY(after_launch("timestamps_kernel"));
@@ -149,7 +167,7 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
         first_local, T, D, p->conv_kernel, p->conv_dilation);
     return after_launch("dwconv_physical_kernel(stem)");
   }
-  dwconv_unit_kernel<float><<<grid_for(bt * D), 256, 0, st>>>(
+  dwconv_unit_kernel<float><<<token_grid(bt), token_block(D), 0, st>>>(
       pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask, first_local, B, T,
       D, p->conv_kernel, p->conv_dilation);
   return after_launch("dwconv_unit_kernel(stem)");
@@ -158,24 +176,23 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 // Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
 static int block_scan_moments(const float *in, const float *norm, const float *frame,
                               const float *raw_decay, const float *raw_freq, float *a_re,
-                              float *a_im, const float *event_mask, int obs_channels,
+                              float *a_im, float *g_re, float *g_im, const float *event_mask,
+                              int obs_channels,
                               const lnet_b200_alphabet_request *r, int D, int M, Plan &pl,
                               float *moments, cudaStream_t st) {
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, norm, pl.xhat, bt, D);
   LNET_TRY(after_launch("rmsnorm_kernel"));
-  dim3 g((unsigned)cdiv(bt, 64), (unsigned)cdiv(2 * M, 64));
-  gemm_nt_kernel<float><<<g, 256, 0, st>>>(pl.xhat, D, frame, 1, 2 * M, pl.drive, 2 * M, bt,
-                                           2 * M, D);
-  LNET_TRY(after_launch("gemm_nt_kernel(drive)"));
-  drive_kernel<<<grid_for(bt * M), 256, 0, st>>>(pl.drive, raw_decay, raw_freq, r->time_delta,
-                                                 event_mask, obs_channels, bt, M);
-  LNET_TRY(after_launch("drive_kernel"));
-  if (!r->time_delta) {
-    zoh_kernel<<<1, 128, 0, st>>>(raw_decay, raw_freq, M, nullptr, 1, a_re, a_im, nullptr,
-                                  nullptr);
+  LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
+                     bt, 2 * M, D, r->act_dtype == LNET_BF16, "cublas(drive)"));
+  if (!r->time_delta) {  // per-mode a and gamma tables (static poles)
+    zoh_kernel<<<1, 128, 0, st>>>(raw_decay, raw_freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
     LNET_TRY(after_launch("zoh_kernel"));
   }
+  drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(pl.drive, raw_decay, raw_freq,
+                                                          r->time_delta, g_re, g_im, event_mask,
+                                                          obs_channels, bt, M);
+  LNET_TRY(after_launch("drive_kernel"));
   const int64_t n_scan = cdiv(T, kScanChunk);
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   dim3 gs((unsigned)n_scan, (unsigned)B);
@@ -211,12 +228,11 @@ static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
   const int D = p->model_dim, M = p->modes;
   LNET_TRY(block_scan_moments(first_local, p->writer_norm, p->writer_frame, p->writer_raw_decay,
                               p->writer_raw_frequency, pl.a_tab, pl.a_tab + M,
+                              pl.a_tab + 4 * M, pl.a_tab + 5 * M,
                               r->observation_mask, r->obs_channels, r, D, M, pl, moments, st));
-  dim3 g((unsigned)cdiv(bt, 64), (unsigned)cdiv(D, 64));
-  gemm_nt_kernel<float><<<g, 256, 0, st>>>(pl.drive, 2 * M, p->writer_frame, 2 * M, 1, pl.modal,
-                                           D, bt, D, 2 * M);
-  LNET_TRY(after_launch("gemm_nt_kernel(synthesis)"));
-  residual_kernel<<<grid_for(bt * D), 256, 0, st>>>(first_local, pl.xhat, pl.modal,
+  LNET_TRY(gemm_rows(st, pl.drive, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
+                     pl.modal, D, bt, D, 2 * M, r->act_dtype == LNET_BF16, "cublas(synthesis)"));
+  residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(first_local, pl.xhat, pl.modal,
                                                      p->writer_direct_scale,
                                                      p->writer_layer_scale, stream_out, bt, D);
   return after_launch("residual_kernel");
@@ -235,14 +251,15 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
         r->valid_mask, pl.proj, T, D, p->conv_kernel, p->conv_dilation);
     LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
   } else {
-    dwconv_unit_kernel<float><<<grid_for(bt * D), 256, 0, st>>>(
+    dwconv_unit_kernel<float><<<token_grid(bt), token_block(D), 0, st>>>(
         first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, r->valid_mask,
         pl.proj, B, T, D, p->conv_kernel, p->conv_dilation);
     LNET_TRY(after_launch("dwconv_unit_kernel(reader)"));
   }
   // the reader block sees no observation mask (src/lnet/alphabet.py:384-389)
   return block_scan_moments(pl.proj, p->reader_norm, p->reader_frame, p->reader_raw_decay,
-                            p->reader_raw_frequency, pl.a_tab + 2 * M, pl.a_tab + 3 * M, nullptr,
+                            p->reader_raw_frequency, pl.a_tab + 2 * M, pl.a_tab + 3 * M,
+                            pl.a_tab + 6 * M, pl.a_tab + 7 * M, nullptr,
                             1, r, D, M, pl, moments, st);
 }
 

@@ -1,0 +1,64 @@
+// Plain library GEMMs of the general route (cuBLAS): the stem projection, the
+// drive projection and the synthesis of every request the fused route does
+// not take.  fp32 requests compute in fp32 (CUBLAS_COMPUTE_32F, no tensor-core
+// rounding, the precision of the reference's fp32 matmuls); bf16 requests use
+// TF32 tensor cores (more mantissa than the bf16 operands of the reference's
+// autocast matmuls).
+#pragma once
+
+#include <cublas_v2.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace lnet {
+
+// One handle per (host thread, device), created on first use and kept.
+inline int blas_handle(cublasHandle_t *out) {
+  thread_local std::unordered_map<int, cublasHandle_t> handles;
+  int dev = 0;
+  LNET_TRY(cuda_check(cudaGetDevice(&dev), "cudaGetDevice"));
+  auto it = handles.find(dev);
+  if (it == handles.end()) {
+    cublasHandle_t h = nullptr;
+    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS)
+      return fail(LNET_ERR_CUDA, "cublasCreate failed on device %d", dev);
+    it = handles.emplace(dev, h).first;
+  }
+  *out = it->second;
+  return LNET_OK;
+}
+
+// C[rows, n] (row-major, leading dimension ldc) = A[rows, k] (row-major, lda) * B^T,
+// with element (j, kk) of B at Bm[j * ldbn + kk * ldbk] (one of ldbn, ldbk is 1).
+inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t lda, const void *Bm,
+                     cudaDataType tb, int64_t ldbn, int64_t ldbk, float *C, int64_t ldc,
+                     int64_t rows, int n, int k, bool tf32, const char *what) {
+  if (rows == 0 || n == 0) return LNET_OK;
+  if (rows > INT32_MAX) return fail(LNET_ERR_UNSUPPORTED, "%s: %lld rows", what, (long long)rows);
+  cublasHandle_t h;
+  LNET_TRY(blas_handle(&h));
+  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS)
+    return fail(LNET_ERR_CUDA, "cublasSetStream failed");
+  // column-major view: C^T (n x rows) = B (n x k) * A^T (k x rows)
+  cublasOperation_t op_b;
+  int ld_b;
+  if (ldbn == 1) {
+    op_b = CUBLAS_OP_N;
+    ld_b = (int)ldbk;
+  } else {
+    op_b = CUBLAS_OP_T;
+    ld_b = (int)ldbn;
+  }
+  const float alpha = 1.f, beta = 0.f;
+  const cublasStatus_t s = cublasGemmEx(
+      h, op_b, CUBLAS_OP_N, n, (int)rows, k, &alpha, Bm, tb, ld_b, A, ta, (int)lda, &beta, C,
+      CUDA_R_32F, (int)ldc, tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F,
+      CUBLAS_GEMM_DEFAULT);
+  if (s != CUBLAS_STATUS_SUCCESS) return fail(LNET_ERR_CUDA, "%s: cublasGemmEx status %d", what, (int)s);
+  return after_library(what);
+}
+
+}  // namespace lnet

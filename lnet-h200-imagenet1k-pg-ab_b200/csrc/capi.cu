@@ -63,6 +63,15 @@ void begin_entry(cudaStream_t stream) {
 void count_launch(int n) { g_launches += n; }
 int launch_count() { return g_launches; }
 
+int after_library(const char *what) {
+  if (g_prof_on) {
+    cudaEvent_t e = prof_event();
+    cudaEventRecord(e, g_stream);
+    g_prof.push_back({what, e});
+  }
+  return LNET_OK;
+}
+
 int after_launch(const char *what) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return fail(LNET_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(err));

@@ -27,6 +27,9 @@ void count_launch(int n = 1);
 int launch_count();
 // Checks the most recent launch on this thread and counts it.
 int after_launch(const char *what);
+// After a library call (cuBLAS): profiling record only, not counted as a launch
+// of this library's kernels.
+int after_library(const char *what);
 
 #define LNET_TRY(expr)              \
   do {                              \

@@ -1,66 +1,20 @@
 // Stage kernels of the general ALPHABET path (every metadata combination).
 //
-// Each kernel is one bandwidth-bound pass over [B, T, *] fp32 tensors; the
-// unit-grid fast path (fused_writer.cu / fused_reader.cu) replaces most of
-// them when no time_delta is given.
+// Each kernel is one bandwidth-bound pass over [B, T, *] fp32 tensors (the
+// projections are library GEMMs, blas.cuh); the fused route (fused_path.cuh)
+// replaces them for the compiled shapes without metadata.
 #pragma once
 
 #include "common.cuh"
 
 namespace lnet {
 
-// ---------------------------------------------------------------- GEMM
-// C[r, n] = sum_k A[r, k] * Bm[n * ldbn + k * ldbk]   (fp32 FFMA, 64x64 tiles)
-template <typename TA>
-__global__ void __launch_bounds__(256) gemm_nt_kernel(const TA *__restrict__ A, int64_t lda,
-                                                      const float *__restrict__ Bm,
-                                                      int64_t ldbn, int64_t ldbk,
-                                                      float *__restrict__ C, int64_t ldc,
-                                                      int64_t rows, int n_cols, int k_dim) {
-  __shared__ float As[16][64 + 4];
-  __shared__ float Bs[16][64 + 4];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int64_t r0 = (int64_t)blockIdx.x * 64;
-  const int n0 = blockIdx.y * 64;
-  float acc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  for (int k0 = 0; k0 < k_dim; k0 += 16) {
-    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-      int r = i >> 4, c = i & 15;
-      int64_t gr = r0 + r;
-      int gk = k0 + c;
-      As[c][r] = (gr < rows && gk < k_dim) ? load_f(A, gr * lda + gk) : 0.f;
-      int gn = n0 + r;
-      Bs[c][r] = (gn < n_cols && gk < k_dim) ? Bm[(int64_t)gn * ldbn + (int64_t)gk * ldbk] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    int64_t gr = r0 + ty * 4 + i;
-    if (gr >= rows) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      int gn = n0 + tx * 4 + j;
-      if (gn < n_cols) C[gr * ldc + gn] = acc[i][j];
-    }
-  }
+// ---------------------------------------------------------------- fp32 -> bf16 copy
+__global__ void to_bf16_kernel(const float *__restrict__ src, __nv_bfloat16 *__restrict__ dst,
+                               int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
 }
 
 // ---------------------------------------------------------------- stem input mask
@@ -69,15 +23,15 @@ template <typename TX>
 __global__ void mask_inputs_kernel(const TX *__restrict__ x, const float *__restrict__ obs,
                                    int obs_channels, const float *__restrict__ valid,
                                    float *__restrict__ xm, int64_t tokens, int channels) {
-  int64_t n = tokens * channels;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t tok = i / channels;
-    int c = (int)(i - tok * channels);
-    float v = load_f(x, i);
-    if (obs) v *= obs[tok * obs_channels + (obs_channels == 1 ? 0 : c)];
-    if (valid) v *= valid[tok];
-    xm[i] = v;
+  // block-stride over tokens, threads over channels (no per-element division)
+  for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+    for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+      const int64_t i = tok * channels + c;
+      float v = load_f(x, i);
+      if (obs) v *= obs[tok * obs_channels + (obs_channels == 1 ? 0 : c)];
+      if (valid) v *= valid[tok];
+      xm[i] = v;
+    }
   }
 }
 
@@ -91,25 +45,23 @@ __global__ void dwconv_unit_kernel(const TI *__restrict__ in, const float *__res
                                    int64_t batch, int64_t steps, int dim, int taps,
                                    int dilation) {
   const int pad = dilation * (taps - 1) / 2;
-  int64_t n = batch * steps * dim;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t tok = i / dim;
-    int d = (int)(i - tok * dim);
-    int64_t b = tok / steps;
-    int64_t t = tok - b * steps;
-    float acc = 0.f;
-    for (int k = 0; k < taps; ++k) {
-      int64_t s = t + (int64_t)k * dilation - pad;
-      if (s < 0 || s >= steps) continue;
-      int64_t src = b * steps + s;
-      float v = load_f(in, src * dim + d);
-      if (in_mask) v *= in_mask[src];
-      acc = fmaf(w[d * taps + k], v, acc);
+  // block-stride over tokens, threads over channels (coalesced, one division per token)
+  for (int64_t tok = blockIdx.x; tok < batch * steps; tok += gridDim.x) {
+    const int64_t b = tok / steps, t = tok - b * steps;
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+      float acc = 0.f;
+      for (int k = 0; k < taps; ++k) {
+        const int64_t s = t + (int64_t)k * dilation - pad;
+        if (s < 0 || s >= steps) continue;
+        const int64_t src = b * steps + s;
+        float v = load_f(in, src * dim + d);
+        if (in_mask) v *= in_mask[src];
+        acc = fmaf(w[d * taps + k], v, acc);
+      }
+      float y = silu_f(acc + bias[d]);
+      if (out_mask) y *= out_mask[tok];
+      out[tok * dim + d] = y;
     }
-    float y = silu_f(acc + bias[d]);
-    if (out_mask) y *= out_mask[tok];
-    out[i] = y;
   }
 }
 
@@ -206,22 +158,30 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 
 // ---------------------------------------------------------------- drive (gamma (x) e * mask)
 // e[tok, 0:M] / e[tok, M:2M] -> u in place; gamma from the per-mode table or per step.
+// Without dt the gains are the per-mode table g_tab_re/im (zoh_kernel); with dt
+// they are evaluated per step.
 __global__ void drive_kernel(float *__restrict__ e, const float *__restrict__ raw_decay,
                              const float *__restrict__ raw_freq, const float *__restrict__ dt,
+                             const float *__restrict__ g_tab_re, const float *__restrict__ g_tab_im,
                              const float *__restrict__ event_mask, int obs_channels,
                              int64_t tokens, int modes) {
-  int64_t n = tokens * modes;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t tok = i / modes;
-    int m = (int)(i - tok * modes);
-    double damping, frequency;
-    mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
-    Zoh z = zoh_eval(damping, frequency, dt ? (double)dt[tok] : 1.0);
+  for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    float gr, gi;
+    if (dt) {
+      double damping, frequency;
+      mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+      const Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
+      gr = z.g_re;
+      gi = z.g_im;
+    } else {
+      gr = g_tab_re[m];
+      gi = g_tab_im[m];
+    }
     float *row = e + tok * 2 * modes;
     float er = row[m], ei = row[modes + m];
-    float ur = z.g_re * er - z.g_im * ei;
-    float ui = z.g_re * ei + z.g_im * er;
+    float ur = gr * er - gi * ei;
+    float ui = gr * ei + gi * er;
     if (event_mask) {
       // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
       const float *om = event_mask + tok * obs_channels;
@@ -232,6 +192,7 @@ __global__ void drive_kernel(float *__restrict__ e, const float *__restrict__ ra
     }
     row[m] = ur;
     row[modes + m] = ui;
+   }
   }
 }
 
@@ -550,17 +511,17 @@ __global__ void residual_kernel(const float *__restrict__ x, const float *__rest
                                 const float *__restrict__ modal, const float *__restrict__ ds,
                                 const float *__restrict__ ls, float *__restrict__ v,
                                 int64_t tokens, int dim) {
-  int64_t n = tokens * dim;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int d = (int)(i % dim);
-    v[i] = x[i] + ls[d] * (modal[i] + ds[d] * xhat[i]);
+  for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+      const int64_t i = tok * dim + d;
+      v[i] = x[i] + ls[d] * (modal[i] + ds[d] * xhat[i]);
+    }
   }
 }
 
-// ---------------------------------------------------------------- head
-// logits[b, k] = bias[k] + sum_j G[k, j] f[b, j],  f = [radial_log(W), radial_log(R)]
-// (src/lnet/alphabet.py:29-63).  One block per (row, 8 classes); warp per class.
+// ---------------------------------------------------------------- head features
+// Radial-log feature j of one row's moments (src/lnet/alphabet.py:29-46); the
+// affine head itself is head_gemm.cuh.
 __device__ __forceinline__ float radial_feature(const float *mom, int modes, int j) {
   if (j < modes) return log1pf(fmaxf(mom[j], 0.f));
   int pair = (j - modes) / (2 * modes);
@@ -585,21 +546,6 @@ __global__ void head_features_kernel(const float *__restrict__ wm, const float *
   }
 }
 
-__global__ void head_logits_kernel(const float *__restrict__ feats, const float *__restrict__ G,
-                                   const float *__restrict__ bias, float *__restrict__ logits,
-                                   int64_t batch, int classes, int width) {
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int k = blockIdx.x * (blockDim.x >> 5) + warp;
-  int64_t b = blockIdx.y;
-  if (k >= classes) return;
-  const float *f = feats + b * width;
-  const float *g = G + (int64_t)k * width;
-  float acc = 0.f;
-  for (int j = lane; j < width; j += 32) acc = fmaf(f[j], g[j], acc);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) logits[b * classes + k] = acc + bias[k];
-}
 
 // ---------------------------------------------------------------- ZOH table
 __global__ void zoh_kernel(const float *__restrict__ raw_decay, const float *__restrict__ raw_freq,

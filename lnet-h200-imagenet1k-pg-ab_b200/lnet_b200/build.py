@@ -71,7 +71,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if verbose and out:
             print(out.decode())
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
+    cmd = [nvcc, ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcublas"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed: {' '.join(cmd)}\n{res.stdout}{res.stderr}")
