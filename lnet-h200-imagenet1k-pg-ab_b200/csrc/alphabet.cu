@@ -50,9 +50,8 @@ static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64
 // Token-major elementwise kernels: blocks stride over tokens, threads over the
 // channels of a token.
 static unsigned token_grid(int64_t tokens) {
-  // one block per token (a serial token loop per block leaves the loads of
-  // consecutive tokens unoverlapped); the kernels stride past 2^31 - 1
-  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(tokens, INT32_MAX));
+  // capped: one block per token measured slower (block scheduling) at 2^20 tokens
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(tokens, 148 * 64));
 }
 static unsigned token_block(int width) { return (unsigned)std::min(256, std::max(32, (width + 31) / 32 * 32)); }
 
