@@ -202,6 +202,50 @@ int lnet_b200_patchify_images(const uint8_t *images, int64_t batch, int32_t heig
                               int32_t width, int32_t patch, const float *mean, const float *std,
                               void *tokens, int32_t tokens_dtype, lnet_stream_t stream);
 
+/* Time-split pieces (the sequence split over ranks of lnet_b200.timesplit).
+ * Each works on one rank's slice of steps of every row: req->batch rows of
+ * req->steps = Ts steps, no metadata (static poles), fp32 tensors; workspace
+ * sized by lnet_b200_alphabet_workspace_size for the same request.  GEMMs use
+ * TF32 when req->act_dtype is LNET_BF16.  Together with lnet_b200_stem and
+ * lnet_b200_head they restate lnet_b200_alphabet_forward on a slice with the
+ * carry-in and lag history of the preceding steps supplied by the caller.
+ *
+ * block_drive: u [B,Ts,2M] = gamma (x) (RMSNorm_block(in) frame_block) and
+ *   optionally x-hat [B,Ts,D] (block 0 writer, 1 reader);
+ *   (src/lnet/pac_tight_frame_models.py:1038-1039,1145-1149).
+ * block_scan: in place, u -> states s_t = a s_{t-1} + u_t starting from
+ *   `init` [B,2M] (the state before the slice; NULL = zero)
+ *   (src/lnet/pac_recurrence.py:191-212).
+ * block_moment_sums: raw sums [B,7M] (fp64) of E, C1, C2, C4 over the slice,
+ *   lag products reaching before the slice taken from `history` [B,4,2M]
+ *   (states at steps -1..-4; NULL = sequence start); dividing the all-rank
+ *   sums by T and T - lag gives the raw moments
+ *   (src/lnet/pac_tight_frame_models.py:1632-1657).
+ * writer_output: stream [B,Ts,D] = x + ls (s frame^T + ds x-hat)
+ *   (src/lnet/pac_tight_frame_models.py:1480,1490,1503-1507).
+ * depthwise_conv_silu: SiLU(bias + K5/d4 depthwise conv) of in [B,Ts,D], zero
+ *   padding at the slice edges (callers pass a slice with a +-8-step halo);
+ *   which 0 = stem.local, 1 = second_local (src/lnet/alphabet_backbone.py:872-992). */
+int lnet_b200_block_drive(const lnet_b200_alphabet_params *params,
+                          const lnet_b200_alphabet_request *req, int32_t block, const float *in,
+                          void *workspace, size_t workspace_bytes, float *u_out, float *xhat_out,
+                          lnet_stream_t stream);
+int lnet_b200_block_scan(const lnet_b200_alphabet_params *params,
+                         const lnet_b200_alphabet_request *req, int32_t block, float *u_states,
+                         const float *init, void *workspace, size_t workspace_bytes,
+                         lnet_stream_t stream);
+int lnet_b200_block_moment_sums(const lnet_b200_alphabet_params *params,
+                                const lnet_b200_alphabet_request *req, const float *states,
+                                const float *history, void *workspace, size_t workspace_bytes,
+                                double *sums, lnet_stream_t stream);
+int lnet_b200_writer_output(const lnet_b200_alphabet_params *params,
+                            const lnet_b200_alphabet_request *req, const float *states,
+                            const float *xhat, const float *first_local, void *workspace,
+                            size_t workspace_bytes, float *stream_out, lnet_stream_t stream);
+int lnet_b200_depthwise_conv_silu(const lnet_b200_alphabet_params *params,
+                                  const lnet_b200_alphabet_request *req, int32_t which,
+                                  const float *in, float *out, lnet_stream_t stream);
+
 /* Pole-residue Laplace layer in float64:
  *   y_t = sum_{m,i} R[o, m, i] s_t[m, i] + D x_t + bias,
  *   s_t[m, i] = exp(p_m dt) s_{t-1}[m, i] + dt phi1(p_m dt) x_t[i],

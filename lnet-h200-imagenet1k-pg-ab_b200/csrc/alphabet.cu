@@ -198,7 +198,8 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   scan_local_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
                                             r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_local_kernel"));
-  scan_carry_kernel<<<(unsigned)cdiv(B * M, 128), 128, 0, st>>>(pl.carries, B, M, n_scan);
+  scan_carry_kernel<<<(unsigned)cdiv(B * M, 128), 128, 0, st>>>(pl.carries, B, M, n_scan,
+                                                                nullptr);
   LNET_TRY(after_launch("scan_carry_kernel"));
   scan_apply_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
                                             r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
@@ -213,7 +214,7 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
     return after_launch("pt_moments_finalize_kernel");
   }
   moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, r->valid_mask, pl.partial, T, M,
-                                                 kMomChunk, n_mom);
+                                                 kMomChunk, n_mom, nullptr);
   LNET_TRY(after_launch("moments_partial_kernel"));
   moments_finalize_kernel<<<(unsigned)B, 256, 0, st>>>(pl.partial, r->valid_mask, moments, T, M,
                                                        n_mom);
@@ -476,6 +477,152 @@ extern "C" int lnet_b200_head(const lnet_b200_alphabet_params *params, int64_t b
   if (!writer_moments || !reader_moments || !logits)
     return fail(LNET_ERR_INVALID_ARGUMENT, "head: NULL tensor pointer");
   return fused_head(params, batch, writer_moments, reader_moments, logits, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------- time-split pieces
+// One rank's slice of steps of every row (lnet_b200.timesplit): the pieces of
+// the general route with the slice's carry-in and lag history exposed.  No
+// metadata (static poles); tensors are fp32 [B, Ts, *] for req->batch rows of
+// req->steps = Ts steps; `workspace` is sized by lnet_b200_alphabet_workspace_size
+// for the same request.
+static int slice_entry(const lnet_b200_alphabet_params *params,
+                       const lnet_b200_alphabet_request *req, void *workspace,
+                       size_t workspace_bytes, Plan &pl, cudaStream_t st) {
+  reset_launches();
+  begin_entry(st);
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (req->time_delta || req->observation_mask || req->valid_mask)
+    return fail(LNET_ERR_UNSUPPORTED, "time-split pieces take no metadata");
+  return plan_all(params, req, workspace, workspace_bytes, pl, false);
+}
+
+struct BlockParams {
+  const float *norm, *frame, *decay, *freq;
+};
+static BlockParams block_params(const lnet_b200_alphabet_params *p, int block) {
+  return block == 0 ? BlockParams{p->writer_norm, p->writer_frame, p->writer_raw_decay,
+                                  p->writer_raw_frequency}
+                    : BlockParams{p->reader_norm, p->reader_frame, p->reader_raw_decay,
+                                  p->reader_raw_frequency};
+}
+
+extern "C" int lnet_b200_block_drive(const lnet_b200_alphabet_params *params,
+                                     const lnet_b200_alphabet_request *req, int32_t block,
+                                     const float *in, void *workspace, size_t workspace_bytes,
+                                     float *u_out, float *xhat_out, lnet_stream_t stream) {
+  auto st = (cudaStream_t)stream;
+  Plan pl;
+  LNET_TRY(slice_entry(params, req, workspace, workspace_bytes, pl, st));
+  if (block != 0 && block != 1) return fail(LNET_ERR_INVALID_ARGUMENT, "block must be 0 or 1");
+  if (!in || !u_out) return fail(LNET_ERR_INVALID_ARGUMENT, "block_drive: NULL tensor pointer");
+  const int64_t bt = req->batch * req->steps;
+  if (bt == 0) return LNET_OK;
+  const int D = params->model_dim, M = params->modes;
+  const BlockParams bp = block_params(params, block);
+  float *xhat = xhat_out ? xhat_out : pl.xhat;
+  rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, bp.norm, xhat, bt, D);
+  LNET_TRY(after_launch("rmsnorm_kernel"));
+  LNET_TRY(gemm_rows(st, xhat, CUDA_R_32F, D, bp.frame, CUDA_R_32F, 1, 2 * M, u_out, 2 * M, bt,
+                     2 * M, D, req->act_dtype == LNET_BF16, "cublas(drive)"));
+  float *a_re = pl.a_tab, *a_im = pl.a_tab + M, *g_re = pl.a_tab + 4 * M, *g_im = pl.a_tab + 5 * M;
+  zoh_kernel<<<1, 128, 0, st>>>(bp.decay, bp.freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
+  LNET_TRY(after_launch("zoh_kernel"));
+  drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(u_out, bp.decay, bp.freq, nullptr, g_re,
+                                                          g_im, nullptr, 1, bt, M);
+  return after_launch("drive_kernel");
+}
+
+extern "C" int lnet_b200_block_scan(const lnet_b200_alphabet_params *params,
+                                    const lnet_b200_alphabet_request *req, int32_t block,
+                                    float *u_states, const float *init, void *workspace,
+                                    size_t workspace_bytes, lnet_stream_t stream) {
+  auto st = (cudaStream_t)stream;
+  Plan pl;
+  LNET_TRY(slice_entry(params, req, workspace, workspace_bytes, pl, st));
+  if (block != 0 && block != 1) return fail(LNET_ERR_INVALID_ARGUMENT, "block must be 0 or 1");
+  if (!u_states) return fail(LNET_ERR_INVALID_ARGUMENT, "block_scan: NULL tensor pointer");
+  const int64_t B = req->batch, T = req->steps;
+  if (B * T == 0) return LNET_OK;
+  const int M = params->modes;
+  const BlockParams bp = block_params(params, block);
+  float *a_re = pl.a_tab, *a_im = pl.a_tab + M;
+  zoh_kernel<<<1, 128, 0, st>>>(bp.decay, bp.freq, M, nullptr, 1, a_re, a_im, nullptr, nullptr);
+  LNET_TRY(after_launch("zoh_kernel"));
+  const int64_t n_scan = cdiv(T, kScanChunk);
+  const int threads = std::min(128, (int)cdiv(M, 32) * 32);
+  dim3 gs((unsigned)n_scan, (unsigned)B);
+  scan_local_kernel<<<gs, threads, 0, st>>>(u_states, bp.decay, bp.freq, a_re, a_im, nullptr,
+                                            pl.carries, T, M, kScanChunk, n_scan);
+  LNET_TRY(after_launch("scan_local_kernel"));
+  scan_carry_kernel<<<(unsigned)cdiv(B * M, 128), 128, 0, st>>>(pl.carries, B, M, n_scan, init);
+  LNET_TRY(after_launch("scan_carry_kernel"));
+  scan_apply_kernel<<<gs, threads, 0, st>>>(u_states, bp.decay, bp.freq, a_re, a_im, nullptr,
+                                            pl.carries, T, M, kScanChunk, n_scan);
+  return after_launch("scan_apply_kernel");
+}
+
+extern "C" int lnet_b200_block_moment_sums(const lnet_b200_alphabet_params *params,
+                                           const lnet_b200_alphabet_request *req,
+                                           const float *states, const float *history,
+                                           void *workspace, size_t workspace_bytes, double *sums,
+                                           lnet_stream_t stream) {
+  auto st = (cudaStream_t)stream;
+  Plan pl;
+  LNET_TRY(slice_entry(params, req, workspace, workspace_bytes, pl, st));
+  if (!states || !sums) return fail(LNET_ERR_INVALID_ARGUMENT, "moment_sums: NULL tensor pointer");
+  const int64_t B = req->batch, T = req->steps;
+  if (B * T == 0) return LNET_OK;
+  const int M = params->modes;
+  const int64_t n_mom = cdiv(T, kMomChunk);
+  const int threads = std::min(128, (int)cdiv(M, 32) * 32);
+  dim3 gm((unsigned)n_mom, (unsigned)B);
+  moments_partial_kernel<<<gm, threads, 0, st>>>(states, nullptr, pl.partial, T, M, kMomChunk,
+                                                 n_mom, history);
+  LNET_TRY(after_launch("moments_partial_kernel"));
+  moment_sums_kernel<<<grid_for(B * 7 * M), 256, 0, st>>>(pl.partial, sums, B, M, n_mom);
+  return after_launch("moment_sums_kernel");
+}
+
+extern "C" int lnet_b200_writer_output(const lnet_b200_alphabet_params *params,
+                                       const lnet_b200_alphabet_request *req, const float *states,
+                                       const float *xhat, const float *first_local,
+                                       void *workspace, size_t workspace_bytes, float *stream_out,
+                                       lnet_stream_t stream) {
+  auto st = (cudaStream_t)stream;
+  Plan pl;
+  LNET_TRY(slice_entry(params, req, workspace, workspace_bytes, pl, st));
+  if (!states || !xhat || !first_local || !stream_out)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "writer_output: NULL tensor pointer");
+  const int64_t bt = req->batch * req->steps;
+  if (bt == 0) return LNET_OK;
+  const int D = params->model_dim, M = params->modes;
+  LNET_TRY(gemm_rows(st, states, CUDA_R_32F, 2 * M, params->writer_frame, CUDA_R_32F, 2 * M, 1,
+                     pl.modal, D, bt, D, 2 * M, req->act_dtype == LNET_BF16, "cublas(synthesis)"));
+  residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
+      first_local, xhat, pl.modal, params->writer_direct_scale, params->writer_layer_scale,
+      stream_out, bt, D);
+  return after_launch("residual_kernel");
+}
+
+extern "C" int lnet_b200_depthwise_conv_silu(const lnet_b200_alphabet_params *params,
+                                             const lnet_b200_alphabet_request *req, int32_t which,
+                                             const float *in, float *out, lnet_stream_t stream) {
+  reset_launches();
+  auto st = (cudaStream_t)stream;
+  begin_entry(st);
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (which != 0 && which != 1) return fail(LNET_ERR_INVALID_ARGUMENT, "which must be 0 or 1");
+  if (!in || !out) return fail(LNET_ERR_INVALID_ARGUMENT, "conv: NULL tensor pointer");
+  const int64_t B = req->batch, T = req->steps;
+  if (B * T == 0) return LNET_OK;
+  const int D = params->model_dim;
+  dwconv_unit_kernel<float><<<token_grid(B * T), token_block(D), 0, st>>>(
+      in, which == 0 ? params->stem_conv_weight : params->reader_conv_weight,
+      which == 0 ? params->stem_conv_bias : params->reader_conv_bias, nullptr, nullptr, out, B, T,
+      D, params->conv_kernel, params->conv_dilation);
+  return after_launch("dwconv_unit_kernel");
 }
 
 extern "C" int lnet_b200_zoh(const float *raw_decay, const float *raw_frequency, int32_t modes,

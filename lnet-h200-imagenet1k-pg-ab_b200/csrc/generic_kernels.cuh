@@ -250,13 +250,15 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
   }
 }
 
+// `init` (optional, [B, 2M] re | im): the state before step 0 (a time slice's
+// carry-in); zero when NULL.
 __global__ void scan_carry_kernel(float *__restrict__ carries, int64_t batch, int modes,
-                                  int64_t n_chunks) {
+                                  int64_t n_chunks, const float *__restrict__ init) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= batch * modes) return;
   int64_t b = i / modes;
   int m = (int)(i - b * modes);
-  float sr = 0.f, si = 0.f;
+  float sr = init ? init[b * 2 * modes + m] : 0.f, si = init ? init[b * 2 * modes + modes + m] : 0.f;
   for (int64_t c = 0; c < n_chunks; ++c) {
     float *rec = carries + ((b * n_chunks + c) * 4) * modes;
     float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m], pi = rec[3 * modes + m];
@@ -301,10 +303,14 @@ __global__ void scan_apply_kernel(float *__restrict__ u, const float *__restrict
 // Partial sums over a chunk of steps of E, C1, C2, C4 (re, im), optionally
 // valid-weighted (_modal_moments / _masked_modal_moments,
 // src/lnet/pac_tight_frame_models.py:1632-1702).  partial layout [B, nchunk, 7M].
+// `hist` (optional, [B, 4, 2M]): the states at steps -1 .. -4 of a time slice,
+// so lag products across the slice start are counted; without it they are
+// skipped (sequence start).
 __global__ void moments_partial_kernel(const float *__restrict__ s,
                                        const float *__restrict__ valid,
                                        float *__restrict__ partial, int64_t steps, int modes,
-                                       int chunk, int64_t n_chunks) {
+                                       int chunk, int64_t n_chunks,
+                                       const float *__restrict__ hist) {
   const int64_t c = blockIdx.x, b = blockIdx.y;
   const int64_t t0 = c * chunk;
   const int64_t t1 = min(steps, t0 + chunk);
@@ -319,8 +325,14 @@ __global__ void moments_partial_kernel(const float *__restrict__ s,
       acc[0] += (cr * cr + ci * ci) * wt;
 #pragma unroll
       for (int l = 0; l < 3; ++l) {
-        if (t < lags[l]) continue;
-        const float *prow = row - (int64_t)lags[l] * 2 * modes;
+        const float *prow;
+        if (t >= lags[l]) {
+          prow = row - (int64_t)lags[l] * 2 * modes;
+        } else if (hist) {
+          prow = hist + (b * 4 + (lags[l] - t - 1)) * 2 * modes;
+        } else {
+          continue;
+        }
         float pr = prow[m], pi = prow[modes + m];
         float w = valid ? wt * valid[tok - lags[l]] : 1.f;
         acc[1 + 2 * l] += (cr * pr + ci * pi) * w;
@@ -330,6 +342,21 @@ __global__ void moments_partial_kernel(const float *__restrict__ s,
     float *out = partial + (b * n_chunks + c) * 7 * modes;
 #pragma unroll
     for (int j = 0; j < 7; ++j) out[j * modes + m] = acc[j];
+  }
+}
+
+// Raw (unnormalised) moment sums of each row, the chunk partials added in
+// order in double: sums [B, 7M] (time-split ranks all-reduce these).
+__global__ void moment_sums_kernel(const float *__restrict__ partial, double *__restrict__ sums,
+                                   int64_t batch, int modes, int64_t n_chunks) {
+  const int64_t n = batch * 7 * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / (7 * modes);
+    const int j = (int)(i - b * 7 * modes);
+    double acc = 0.0;
+    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)partial[(b * n_chunks + c) * 7 * modes + j];
+    sums[i] = acc;
   }
 }
 

@@ -8,6 +8,8 @@ Laplace layer behind the reference ``lnet`` module API.
 * :mod:`lnet_b200.ops` — the same calls as ``torch.library`` custom ops
   (``lnet_b200::alphabet_forward``, ``lnet_b200::laplace_forward``).
 * :mod:`lnet_b200.sharding` — batch sharding over one process per GPU.
+* :mod:`lnet_b200.timesplit` — sequence split over ranks (one carry exchange
+  per block) for requests with fewer rows than GPUs.
 * :mod:`lnet_b200.images` — uint8 images -> normalised 4x4 patch tokens on the
   GPU (:meth:`B200Alphabet.forward_images`).
 * :mod:`lnet_b200.pipeline` — host-fed serving loop overlapping the copies of

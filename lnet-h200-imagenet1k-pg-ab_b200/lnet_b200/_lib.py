@@ -128,6 +128,21 @@ SIGNATURES = {
         [_c_p, _i64, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_float),
          ctypes.POINTER(ctypes.c_float), _c_p, _i32, _c_p],
     ),
+    "lnet_b200_block_drive": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _i32, _c_p, _c_p, ctypes.c_size_t, _c_p, _c_p, _c_p],
+    ),
+    "lnet_b200_block_scan": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _i32, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p],
+    ),
+    "lnet_b200_block_moment_sums": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p, _c_p],
+    ),
+    "lnet_b200_writer_output": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p, _c_p],
+    ),
+    "lnet_b200_depthwise_conv_silu": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _i32, _c_p, _c_p, _c_p],
+    ),
     "lnet_b200_laplace_workspace_size": (
         ctypes.c_int, [_i64, _i64, _i32, _i32, ctypes.POINTER(ctypes.c_size_t)]
     ),
