@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """ALPHABET forward benchmark: tokens/s and HBM roofline on B200, next to the CPU path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 4|1|2|3|5]
 
 Default workload (the north-star case): synthetic uint8
 224x224x3 images ~U(0,255), normalised with the ImageNet mean/std and
@@ -53,6 +53,11 @@ CONFIGS = {
               B=128, T=1024, C=128, D=128, M=64, K=10, dtype="fp32", images=False),
     "5": dict(workload="alphabet_cfg5_b16_t65536_c256_d256_m64_k10_bf16",
               B=16, T=65536, C=256, D=256, M=64, K=10, dtype="bf16", images=False),
+    # timed through the module API only (run_module): metadata / the Laplace layer
+    "3": dict(workload="alphabet_cfg3_b64_t2048_c64_d64_m32_k10_fp32_dt_obs_valid",
+              B=64, T=2048, C=64, D=64, M=32, K=10, dtype="fp32", images=False, meta=True),
+    "1": dict(workload="laplace_cfg1_b64_t512_c16_per_channel8_fp32", B=64, T=512, C=16,
+              per_channel=8, dtype="fp32", laplace=True),
 }
 
 
@@ -316,6 +321,89 @@ def run_reference(args, cfg):
     return 0
 
 
+def run_module(args, cfg):
+    """Configs 1 and 3 (one GPU): K forwards through the module API with the
+    inputs resident in HBM, L2 flushed between steps, CUDA events per step.
+    Config 3 carries all metadata (Delta t ~ Exp(1) clipped to [0.05, 4],
+    channel observation mask ~ Bernoulli(0.8), right-padded valid lengths
+    ~ U(T/2, T)); config 1 is the pole-residue Laplace layer with 8 real poles
+    per channel (p = -e^u, u ~ U(ln 0.01, 0)), block-diagonal residues."""
+    import math
+
+    import torch
+
+    from lnet_b200 import _lib
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "configs 1 and 3 are timed on the GPU path only; the reference arm "
+                          "times config 4 (and 2, 5)"}), flush=True)
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(5)
+    B, T = cfg["B"], cfg["T"]
+    if cfg.get("laplace"):
+        from lnet_b200 import B200PoleResidueTemporalMixing
+
+        c, per = cfg["C"], cfg["per_channel"]
+        u = torch.empty(c, per, dtype=torch.float64).uniform_(math.log(0.01), 0.0, generator=g)
+        poles = -torch.exp(u).reshape(-1)
+        r = torch.randn(c, per, generator=g, dtype=torch.float64) / math.sqrt(per)
+        residues = torch.zeros(c, c * per, c, dtype=torch.float64)
+        for ch in range(c):
+            residues[ch, ch * per:(ch + 1) * per, ch] = r[ch]
+        layer = B200PoleResidueTemporalMixing(c, c * per)
+        layer.load_transfer_parameters(poles=poles, residues=residues,
+                                       direct_term=torch.diag(torch.randn(c, generator=g,
+                                                                          dtype=torch.float64)),
+                                       bias=torch.zeros(c, dtype=torch.float64))
+        layer = layer.to(dev)
+        x = torch.randn(B, T, c, generator=g).to(dev)
+        fwd = lambda: layer(x)  # noqa: E731
+    else:
+        model = build_model(cfg, dev)
+        x = make_inputs(cfg, dev)
+        dt = (-torch.log(torch.rand(B, T, generator=g).clamp_min(1e-12))).clamp(0.05, 4.0)
+        obs = (torch.rand(B, T, cfg["C"], generator=g) < 0.8).float()
+        lengths = torch.randint(T // 2, T + 1, (B,), generator=g)
+        valid = (torch.arange(T).view(1, -1) < lengths.view(-1, 1)).float()
+        meta = {"time_delta": dt.to(dev), "observation_mask": obs.to(dev),
+                "valid_mask": valid.to(dev)}
+        # serving setup of the reference's compiled inference wrapper
+        # (alphabet_backbone.py:1225-1243): metadata validated once, not per call
+        model.validate_metadata = False
+        fwd = lambda: model(x, **meta)  # noqa: E731
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            fwd()
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        _lib.profile_enable(True)
+        with ClockSampler(0) as clocks:
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record()
+                fwd()
+                stops[i].record()
+            torch.cuda.synchronize()
+        prof = _lib.profile_read()
+        _lib.profile_enable(False)
+    total_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, stops))
+    print(json.dumps({
+        "metric": METRIC if not cfg.get("laplace") else "Laplace layer fwd tokens/sec",
+        "value": B * T * args.steps / (total_ms / 1e3), "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "dtype": cfg["dtype"], "data": "synthetic",
+        "config": {"workload": cfg["workload"], "path": "module API (general route)",
+                   "metadata_validation": False if cfg.get("meta") else None,
+                   "l2": "256 MiB flush between steps, outside the per-step event pair"},
+        "clocks": clocks.summary(), "kernels": _lib_kernels(prof)}), flush=True)
+    return 0
+
+
 def run_b200(args, cfg):
     import ctypes
 
@@ -551,8 +639,10 @@ def main():
         cfg["B"] = args.batch
         cfg["workload"] = cfg["workload"].replace(f"_b{CONFIGS[args.config]['B']}_",
                                                   f"_b{args.batch}_")
-    if args.impl == "reference":
+    if args.impl == "reference" and not (cfg.get("meta") or cfg.get("laplace")):
         return run_reference(args, cfg)
+    if cfg.get("meta") or cfg.get("laplace"):
+        return run_module(args, cfg)
     return run_b200(args, cfg)
 
 

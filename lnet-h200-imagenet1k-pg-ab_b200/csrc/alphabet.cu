@@ -159,7 +159,7 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                        false, "cublas(stem)"));
   }
   if (r->time_delta) {
-    timestamps_kernel<<<(unsigned)cdiv(B, 128), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
+    timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
     LNET_TRY(after_launch("timestamps_kernel"));
     dwconv_physical_kernel<float><<<(unsigned)bt, 128, 0, st>>>(
         pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, pl.ts, r->valid_mask,
@@ -244,7 +244,7 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
   const int D = p->model_dim, M = p->modes;
   if (r->time_delta) {
     if (!pl.ts) return fail(LNET_ERR_INVALID_ARGUMENT, "timestamps missing");
-    timestamps_kernel<<<(unsigned)cdiv(B, 128), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
+    timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
     LNET_TRY(after_launch("timestamps_kernel"));
     dwconv_physical_kernel<float><<<(unsigned)bt, 128, 0, st>>>(
         first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, pl.ts,
@@ -446,7 +446,7 @@ extern "C" int lnet_b200_writer(const lnet_b200_alphabet_params *params,
   auto st = (cudaStream_t)stream;
   begin_entry(st);
   if (req->time_delta) {
-    timestamps_kernel<<<(unsigned)cdiv(req->batch, 128), 128, 0, st>>>(req->time_delta, pl.ts,
+    timestamps_kernel<<<(unsigned)cdiv(req->batch, 4), 128, 0, st>>>(req->time_delta, pl.ts,
                                                                        req->batch, req->steps);
     LNET_TRY(after_launch("timestamps_kernel"));
   }

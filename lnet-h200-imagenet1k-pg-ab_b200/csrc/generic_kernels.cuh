@@ -67,14 +67,25 @@ __global__ void dwconv_unit_kernel(const TI *__restrict__ in, const float *__res
 
 // ---------------------------------------------------------------- timestamps
 // ts[b, t] = fp32(sum_{s<=t} double(dt[b, s]))  (CPU torch cumsum accumulates in double)
+// One warp per row: the lanes load 32 steps at once (coalesced), lane 0 adds
+// them in step order (the sequential double sum, bit for bit).
 __global__ void timestamps_kernel(const float *__restrict__ dt, float *__restrict__ ts,
                                   int64_t batch, int64_t steps) {
-  int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t b = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (b >= batch) return;
   double acc = 0.0;
-  for (int64_t t = 0; t < steps; ++t) {
-    acc += (double)dt[b * steps + t];
-    ts[b * steps + t] = (float)acc;
+  for (int64_t t0 = 0; t0 < steps; t0 += 32) {
+    const int64_t t = t0 + lane;
+    const float v = t < steps ? dt[b * steps + t] : 0.f;
+    const int n = (int)min((int64_t)32, steps - t0);
+    for (int k = 0; k < n; ++k) {
+      const float vk = __shfl_sync(0xffffffffu, v, k);
+      if (lane == 0) {
+        acc += (double)vk;
+        ts[b * steps + t0 + k] = (float)acc;
+      }
+    }
   }
 }
 

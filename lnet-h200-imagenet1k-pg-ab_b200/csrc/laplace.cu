@@ -17,6 +17,10 @@ namespace lnet {
 constexpr int kSlice = 256;  // state entries per CTA (= threads)
 constexpr int kStepTile = 32;
 constexpr int kOutTile = 16;
+// Row pitch of the state and residue tiles in shared memory: an odd number of
+// doubles, so the 16 residue rows (and 2 state rows) one warp reads for one
+// entry e fall in distinct banks (a pitch of kSlice put them all in one).
+constexpr int kPitch = kSlice + 1;
 
 __device__ __forceinline__ double softplus_d(double x) {
   return x > 20.0 ? x : log1p(exp(x));
@@ -38,8 +42,9 @@ __global__ void __launch_bounds__(kSlice) laplace_slice_kernel(
     const double *__restrict__ residues, int dim, int modes, double dt, double min_decay,
     int64_t steps, double *__restrict__ partial) {
   extern __shared__ double smem[];
-  double *s_state = smem;                        // [kStepTile][kSlice]
-  double *s_res = smem + kStepTile * kSlice;     // [kOutTile][kSlice]
+  double *s_state = smem;                        // [kStepTile][kPitch]
+  double *s_res = smem + kStepTile * kPitch;     // [kOutTile][kPitch]
+  double *s_x = s_res + kOutTile * kPitch;       // [kStepTile][dim] input tile
   const int slice = blockIdx.x;
   const int64_t b = blockIdx.y;
   const int64_t md = (int64_t)modes * dim;
@@ -54,21 +59,25 @@ __global__ void __launch_bounds__(kSlice) laplace_slice_kernel(
   double *out_row = partial + ((int64_t)slice * gridDim.y + b) * steps * dim;
   for (int64_t t0 = 0; t0 < steps; t0 += kStepTile) {
     const int nt = (int)min((int64_t)kStepTile, steps - t0);
+    // the input tile, loaded by all threads at once (no load on the recurrence chain)
+    for (int e = j; e < nt * dim; e += kSlice)
+      s_x[e] = (double)load_f(x, (b * steps + t0) * dim + e);
+    __syncthreads();
     for (int tt = 0; tt < nt; ++tt) {
-      double xv = live ? (double)load_f(x, ((b * steps) + t0 + tt) * dim + i) : 0.0;
+      const double xv = live ? s_x[tt * dim + i] : 0.0;
       state = a * state + bcoef * xv;
-      s_state[tt * kSlice + j] = live ? state : 0.0;
+      s_state[tt * kPitch + j] = live ? state : 0.0;
     }
     for (int o0 = 0; o0 < dim; o0 += kOutTile) {
       const int no = min(kOutTile, dim - o0);
       __syncthreads();
       for (int r = 0; r < no; ++r)
-        s_res[r * kSlice + j] = live ? residues[(int64_t)(o0 + r) * md + k] : 0.0;
+        s_res[r * kPitch + j] = live ? residues[(int64_t)(o0 + r) * md + k] : 0.0;
       __syncthreads();
       for (int q = j; q < nt * no; q += kSlice) {
         int tt = q / no, r = q - (q / no) * no;
-        const double *sv = s_state + tt * kSlice;
-        const double *rv = s_res + r * kSlice;
+        const double *sv = s_state + tt * kPitch;
+        const double *rv = s_res + r * kPitch;
         double acc = 0.0;
 #pragma unroll 8
         for (int e = 0; e < kSlice; ++e) acc = fma(rv[e], sv[e], acc);
@@ -112,7 +121,10 @@ static int laplace_run(const double *raw_decay, const double *residues, const do
                        const TX *x, int64_t batch, int64_t steps, TX *y, double *partial,
                        cudaStream_t stream) {
   int n_slices = (int)cdiv((int64_t)modes * dim, kSlice);
-  size_t smem = (size_t)(kStepTile + kOutTile) * kSlice * sizeof(double);
+  const size_t smem =
+      ((size_t)(kStepTile + kOutTile) * kPitch + (size_t)kStepTile * dim) * sizeof(double);
+  if (smem > 232448)
+    return fail(LNET_ERR_UNSUPPORTED, "laplace: model_dim %d too large for the input tile", dim);
   LNET_TRY(cuda_check(cudaFuncSetAttribute(laplace_slice_kernel<TX>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem),

@@ -243,18 +243,19 @@ class B200Alphabet(nn.Module):
 
     # ------------------------------------------------------------ metadata (reference semantics)
     def _prepare_metadata(self, inputs, time_delta, observation_mask, valid_mask):
-        """Shape/value validation of src/lnet/alphabet_backbone.py:522-591."""
+        """Shape/value validation of src/lnet/alphabet_backbone.py:522-591.  The value
+        checks are evaluated on the device and read back with one synchronisation."""
         bt = inputs.shape[:2]
         dev = inputs.device
         delta = obs = valid = None
+        checks: list[tuple[Tensor, str]] = []
         if time_delta is not None:
             if time_delta.shape not in (bt, (*bt, 1)):
                 raise ValueError("time_delta must have shape [B,N] or [B,N,1]")
             delta = time_delta.to(device=dev, dtype=torch.float32).reshape(bt).contiguous()
-            if self.validate_metadata and (
-                not torch.isfinite(delta).all() or bool((delta < 0).any())
-            ):
-                raise ValueError("time_delta must contain finite non-negative values")
+            if self.validate_metadata:
+                checks.append(((~torch.isfinite(delta)) | (delta < 0),
+                               "time_delta must contain finite non-negative values"))
         if observation_mask is not None:
             if observation_mask.shape not in (bt, (*bt, 1), inputs.shape):
                 raise ValueError(
@@ -265,18 +266,21 @@ class B200Alphabet(nn.Module):
             if obs.ndim == 2:
                 obs = obs.unsqueeze(-1)
             obs = obs.contiguous()
-            if self.validate_metadata and (
-                not torch.isfinite(obs).all() or bool(((obs < 0) | (obs > 1)).any())
-            ):
-                raise ValueError("observation_mask must contain finite values in [0,1]")
+            if self.validate_metadata:
+                checks.append(((~torch.isfinite(obs)) | (obs < 0) | (obs > 1),
+                               "observation_mask must contain finite values in [0,1]"))
         if valid_mask is not None:
             if valid_mask.shape not in (bt, (*bt, 1)):
                 raise ValueError("valid_mask must have shape [B,N] or [B,N,1]")
             valid = valid_mask.to(device=dev, dtype=torch.float32).reshape(bt).contiguous()
-            if self.validate_metadata and (
-                not torch.isfinite(valid).all() or bool(((valid < 0) | (valid > 1)).any())
-            ):
-                raise ValueError("valid_mask must contain finite values in [0,1]")
+            if self.validate_metadata:
+                checks.append(((~torch.isfinite(valid)) | (valid < 0) | (valid > 1),
+                               "valid_mask must contain finite values in [0,1]"))
+        if checks:
+            bad = torch.stack([c.any() for c, _ in checks]).cpu()  # one synchronisation
+            for flag, (_, message) in zip(bad.tolist(), checks):
+                if flag:
+                    raise ValueError(message)
         return delta, obs, valid
 
     def _request(self, x: Tensor, delta, obs, valid, act_dtype: int) -> _lib.AlphabetRequest:
