@@ -53,6 +53,9 @@ static unsigned token_grid(int64_t tokens) {
   // capped: one block per token measured slower (block scheduling) at 2^20 tokens
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>(tokens, 148 * 64));
 }
+static unsigned dw_grid(int64_t batch, int64_t steps) {
+  return (unsigned)(batch * cdiv(steps, kDwTile));  // rows x step tiles
+}
 static unsigned token_block(int width) { return (unsigned)std::min(256, std::max(32, (width + 31) / 32 * 32)); }
 
 // ---------------------------------------------------------------- validation
@@ -166,7 +169,7 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
         first_local, T, D, p->conv_kernel, p->conv_dilation);
     return after_launch("dwconv_physical_kernel(stem)");
   }
-  dwconv_unit_kernel<float><<<token_grid(bt), token_block(D), 0, st>>>(
+  dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
       pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask, first_local, B, T,
       D, p->conv_kernel, p->conv_dilation);
   return after_launch("dwconv_unit_kernel(stem)");
@@ -251,7 +254,7 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
         r->valid_mask, pl.proj, T, D, p->conv_kernel, p->conv_dilation);
     LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
   } else {
-    dwconv_unit_kernel<float><<<token_grid(bt), token_block(D), 0, st>>>(
+    dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
         first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, r->valid_mask,
         pl.proj, B, T, D, p->conv_kernel, p->conv_dilation);
     LNET_TRY(after_launch("dwconv_unit_kernel(reader)"));
@@ -618,7 +621,7 @@ extern "C" int lnet_b200_depthwise_conv_silu(const lnet_b200_alphabet_params *pa
   const int64_t B = req->batch, T = req->steps;
   if (B * T == 0) return LNET_OK;
   const int D = params->model_dim;
-  dwconv_unit_kernel<float><<<token_grid(B * T), token_block(D), 0, st>>>(
+  dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
       in, which == 0 ? params->stem_conv_weight : params->reader_conv_weight,
       which == 0 ? params->stem_conv_bias : params->reader_conv_bias, nullptr, nullptr, out, B, T,
       D, params->conv_kernel, params->conv_dilation);

@@ -36,6 +36,7 @@ __global__ void mask_inputs_kernel(const TX *__restrict__ x, const float *__rest
 }
 
 // ---------------------------------------------------------------- unit-grid depthwise conv
+constexpr int kDwTile = 16;  // steps per block
 // out[b,t,d] = post[b,t] * SiLU(bias[d] + sum_k w[d,k] * pre[b,t] in[b, t + k*dil - pad, d])
 template <typename TI>
 __global__ void dwconv_unit_kernel(const TI *__restrict__ in, const float *__restrict__ w,
@@ -44,23 +45,30 @@ __global__ void dwconv_unit_kernel(const TI *__restrict__ in, const float *__res
                                    const float *__restrict__ out_mask, float *__restrict__ out,
                                    int64_t batch, int64_t steps, int dim, int taps,
                                    int dilation) {
+  // block (step tile, row): kDwTile consecutive steps of one row, threads over
+  // channels (the taps of neighbouring steps overlap and hit L1; no division)
   const int pad = dilation * (taps - 1) / 2;
-  // block-stride over tokens, threads over channels (coalesced, one division per token)
-  for (int64_t tok = blockIdx.x; tok < batch * steps; tok += gridDim.x) {
-    const int64_t b = tok / steps, t = tok - b * steps;
-    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+  const unsigned tiles = (unsigned)((steps + kDwTile - 1) / kDwTile);
+  const int64_t b = blockIdx.x / tiles;  // grid = rows x tiles, flattened
+  const int64_t t_begin = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kDwTile;
+  const int64_t t_end = min(steps, t_begin + kDwTile);
+  const TI *row_in = in + b * steps * dim;
+  float *row_out = out + b * steps * dim;
+  const float *im = in_mask ? in_mask + b * steps : nullptr;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    const float bd = bias[d];
+    for (int64_t t = t_begin; t < t_end; ++t) {
       float acc = 0.f;
       for (int k = 0; k < taps; ++k) {
         const int64_t s = t + (int64_t)k * dilation - pad;
         if (s < 0 || s >= steps) continue;
-        const int64_t src = b * steps + s;
-        float v = load_f(in, src * dim + d);
-        if (in_mask) v *= in_mask[src];
+        float v = load_f(row_in, s * dim + d);
+        if (im) v *= im[s];
         acc = fmaf(w[d * taps + k], v, acc);
       }
-      float y = silu_f(acc + bias[d]);
-      if (out_mask) y *= out_mask[tok];
-      out[tok * dim + d] = y;
+      float y = silu_f(acc + bd);
+      if (out_mask) y *= out_mask[b * steps + t];
+      row_out[t * dim + d] = y;
     }
   }
 }
