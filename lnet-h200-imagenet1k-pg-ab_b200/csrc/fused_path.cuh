@@ -67,11 +67,7 @@ constexpr int kWriterNSub = 4;
 constexpr int kWriterDriveRows = 128, kReaderDriveRows = 128;
 // Thread (of an item stream) that issues the next tile's TMA copies: not
 // thread 0, whose async-unit instructions queue behind its MMAs.
-#if defined(LNET_TILE_ISSUER0)
-constexpr int kTileIssuer = 0;
-#else
 constexpr int kTileIssuer = 32;
-#endif
 
 template <int NSUB>
 struct ScanLayout {
@@ -508,10 +504,6 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   }
   group_sync(bar_group);
   mark(10);
-#if defined(LNET_LB_DEBUG)
-  const bool dbg = trace && ltid == 192;
-  unsigned long long d0 = clock64(), d1 = 0, d2 = 0, d3 = 0;
-#endif
   // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^SUB c_j + e_j
   // (all end states loaded at once, then the short dependent chain)
   const float asr = K[KC_AS * M + mk], asi = K[(KC_AS + 1) * M + mk];
@@ -533,9 +525,6 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
       ci = ni;
     }
   }
-#if defined(LNET_LB_DEBUG)
-  if (dbg) d1 = clock64();
-#endif
 
   // ---- aggregate, look-back and inclusive record: threads of the last sub-chunk.
   // Record layout per item: [agg | incl][state k = 0..3][re | im][M]; state 0 is
@@ -552,9 +541,6 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
       st_tag(my + (2 * k) * M + m, g_r[k], epoch);
       st_tag(my + (2 * k + 1) * M + m, g_i[k], epoch);
     }
-#if defined(LNET_LB_DEBUG)
-    if (dbg) d2 = clock64();
-#endif
     float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
     if (chunk > 0) {
       const unsigned long long *pv = rec + (item - 1) * 16 * M;
@@ -567,12 +553,10 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         p_r[k] = __uint_as_float((uint32_t)xr);
         p_i[k] = __uint_as_float((uint32_t)xi);
       }
-#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
       if (trace && m == 0) {
         atomicAdd(&g_fused_trace[kid][9], 1ull);
         if (done) atomicAdd(&g_fused_trace[kid][8], 1ull);
       }
-#endif
       for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
         bool ok = true;  // inclusive record of the previous chunk
 #pragma unroll
@@ -642,20 +626,8 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
       sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
       sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
     }
-#if defined(LNET_LB_DEBUG)
-    if (dbg) d3 = clock64();
-#endif
   }
   group_sync(bar_group);
-#if defined(LNET_LB_DEBUG)
-  if (dbg) {
-    const unsigned long long d4 = clock64();
-    atomicAdd(&g_fused_trace[kid][8], d1 - d0);
-    atomicAdd(&g_fused_trace[kid][9], d2 - d1);
-    atomicAdd(&g_fused_trace[kid][13], d3 - d2);
-    atomicAdd(&g_fused_trace[kid][14], d4 - d3);
-  }
-#endif
   mark(11);
 
   // ---- pass 2 from the true state before this sub-chunk
@@ -919,9 +891,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
   constexpr int HD = D / 2;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (lwarp & 3)) << 16);
   const int64_t total = a.B * a.n_chunks;
-#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
-#endif
 
   unsigned long long t_last = clock64();
   // Items are claimed one ahead (alternating slots): iteration k processes
@@ -1041,37 +1011,17 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
                  idesc, false);
       sm100::mma_commit(mbar);
     }
-#if defined(LNET_SYN_DEBUG)
-    unsigned long long y0 = clock64();
-#endif
     if (ltid == kTileIssuer) {
       const int64_t next = item_slot[(iter + 1) & 1];
       if (next < total) issue_tile(next);
     }
-#if defined(LNET_SYN_DEBUG)
-    unsigned long long y1 = clock64();
-#endif
     uint4 flv[HD / 8];
     if (row < n) {
 #pragma unroll
       for (int gq = 0; gq < HD / 8; ++gq) flv[gq] = *reinterpret_cast<const uint4 *>(out_row + 8 * gq);
     }
-#if defined(LNET_SYN_DEBUG)
-    unsigned long long y1b = clock64();
-#endif
     reduce_moments<M, kWriterNSub>(ltid, s_mom, a.rowsum + b * 7 * M);
-#if defined(LNET_SYN_DEBUG)
-    unsigned long long y2 = clock64();
-#endif
     wait_mma(mbar, phase, a.error, 2);
-#if defined(LNET_SYN_DEBUG)
-    if (a.trace && ltid == 0) {
-      unsigned long long y3 = clock64();
-      atomicAdd(&g_fused_trace[0][8], y1b - y1);
-      atomicAdd(&g_fused_trace[0][9], y2 - y1b);
-      atomicAdd(&g_fused_trace[0][13], y3 - y2);
-    }
-#endif
     LNET_TRACE(6);
     // 7. residual epilogue: v = fl + ls * (modal + ds * xhat), xhat = fl * rs * g
     {
@@ -1109,9 +1059,7 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     LNET_TRACE(7);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
-#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
-#endif
   __syncthreads();
   if (tid < 32) {
     sm100::tc_fence_after();
@@ -1165,9 +1113,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
   const int half = warp >> 2;
   constexpr int HD = D / 2;
   const int64_t total = a.B * a.n_chunks;
-#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
-#endif
 
   unsigned long long t_last = clock64();
   // Stream tiles are fetched one item ahead by TMA (thread 0; one 8-channel
@@ -1270,9 +1216,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
     LNET_TRACE(5);
     if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
   }
-#if !defined(LNET_LB_DEBUG) && !defined(LNET_SYN_DEBUG)
   if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
-#endif
   __syncthreads();
   if (warp == 0) {
     sm100::tc_fence_after();
