@@ -22,10 +22,9 @@ namespace lnet {
 
 constexpr int kScanChunk = 64;
 
-// Tag of the look-back records of one forward call.  Starts from a
-// time-derived value so that stale words left in a reused workspace by another
-// process are not mistaken for this call's (a collision needs an exact 32-bit
-// match); 0 is never used.
+// Host part of the look-back record tags (record_tag): starts from a
+// time-derived value and increments per call, so stale words left in a reused
+// workspace by earlier calls or processes do not match (0 is never used).
 static std::atomic<uint32_t> g_epoch{0};
 uint32_t next_epoch() {
   uint32_t e = g_epoch.fetch_add(1) + 1;

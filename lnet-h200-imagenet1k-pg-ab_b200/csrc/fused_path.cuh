@@ -105,6 +105,11 @@ struct FusedWorkspace {
   unsigned long long *rrec = nullptr;
   uint32_t *flags = nullptr;           // counters[2] + error[2]
   size_t flag_words = 0;
+  // Replay counter of the look-back tags, kept in the workspace and advanced
+  // on the device at the end of every call (fused_finalize_kernel), so that
+  // replays of a captured CUDA graph (same host arguments) still tag their
+  // records differently (record_tag).
+  uint32_t *epoch_word = nullptr;
 };
 
 inline int64_t fused_chunks(int64_t steps) { return cdiv(steps, kChunk); }
@@ -130,6 +135,7 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   w.rowsum = ar.take<double>((size_t)w.rowsum_len);
   w.flag_words = 4;
   w.flags = ar.take<uint32_t>(w.flag_words);
+  w.epoch_word = ar.take<uint32_t>(1);
 }
 
 // ---------------------------------------------------------------- operand preparation
@@ -270,7 +276,8 @@ struct FusedArgs {
   __nv_bfloat16 *out;       // writer stream
   double *rowsum;           // this block's per-row moment sums [B][7M]
   unsigned long long *rec;  // [B * nch][2][4][2][M] tagged look-back records
-  uint32_t epoch;           // tag of this call's records
+  uint32_t epoch;           // host part of this call's record tag (fresh per call)
+  const uint32_t *epoch_word;  // device part (replay counter, see record_tag)
   uint32_t *counter;
   uint32_t *error;
   int trace;       // 1: accumulate per-phase cycles of CTA thread 0 into g_fused_trace
@@ -346,6 +353,15 @@ __device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, flo
   ci = fmaf(ar, bi, fmaf(ai, br, ci));
 }
 
+// Tag of one call's look-back records: the host's per-call epoch (time-seeded,
+// never repeated in a process) mixed with the workspace's replay counter (so
+// that replays of a captured graph differ too).  Never 0: zero-filled memory
+// must not read as a published record.
+__device__ __forceinline__ uint32_t record_tag(uint32_t host_epoch, const uint32_t *epoch_word) {
+  const uint32_t t = host_epoch ^ (__ldcg(epoch_word) * 0x9E3779B1u);
+  return t == 0u ? 0x5BD1E995u : t;
+}
+
 // Tagged look-back words: (fp32 bits) | (epoch << 32), written and read as one
 // 64-bit access (single-copy atomic), so a reader that sees this call's epoch
 // also sees the value written with it -- no flags and no fences are needed.
@@ -418,7 +434,8 @@ template <int M, bool WRITE_STATES, int NSUB>
 __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, uint32_t tbase,
                                            int col_re, int col_im, int n, int64_t row,
                                            int64_t chunk, int64_t n_chunks, const float *K,
-                                           unsigned long long *rec, uint32_t epoch,
+                                           unsigned long long *rec, uint32_t host_epoch,
+                                           const uint32_t *epoch_word,
                                            uint32_t *error,
                                            uint8_t *s_slab, int slab_s, float *sc,
                                            double *rowsum, int trace, int kid,
@@ -530,6 +547,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   // Record layout per item: [agg | incl][state k = 0..3][re | im][M]; state 0 is
   // the chunk's last state.
   if (publisher_group && live) {
+    const uint32_t epoch = record_tag(host_epoch, epoch_word);  // this call's record tag
     const int64_t item = row * n_chunks + chunk;  // record index (row-major)
     unsigned long long *my = rec + item * 16 * M;
     float g_r[4], g_i[4];  // chunk-local last four states
@@ -994,7 +1012,8 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
     chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
-                                     a.n_chunks, s_k, a.rec, a.epoch, a.error, gs + P::G_XS,
+                                     a.n_chunks, s_k, a.rec, a.epoch, a.epoch_word, a.error,
+                                     gs + P::G_XS,
                                      P::SLAB_S, s_scan,
                                      a.rowsum + b * 7 * M, a.trace,
                                      a.kernel_id, pre, s_mom);
@@ -1208,7 +1227,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
     LNET_TRACE(4);
     // 4. scan + look-back + moments
     chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
-                            a.epoch, a.error, nullptr, 0, s_scan,
+                            a.epoch, a.epoch_word, a.error, nullptr, 0, s_scan,
                             a.rowsum + b * 7 * M, a.trace, a.kernel_id,
                             pre);
     sm100::tc_fence_before();
@@ -1237,9 +1256,15 @@ __device__ __forceinline__ float finalize_moment(const double *rs, int modes, in
 // One thread per (row, feature): raw moments [b][k*M + m] of both blocks and
 // the radial-log features of src/lnet/alphabet.py:29-46 (the arithmetic of
 // radial_feature) into feats[b][blk * 7M + j].
+// Also advances the look-back epoch for the next call (never 0).
 __global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *__restrict__ wm,
                                       float *__restrict__ rm, float *__restrict__ feats,
-                                      int64_t batch, int64_t steps, int modes) {
+                                      int64_t batch, int64_t steps, int modes,
+                                      uint32_t *__restrict__ epoch_word) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint32_t e = *epoch_word + 1u;
+    *epoch_word = e == 0u ? 1u : e;
+  }
   const int W = 7 * modes;
   const int64_t n = batch * 2 * W;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -1340,7 +1365,6 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                                       st),
                       "cudaMemsetAsync(row sums, flags)"));
   uint32_t *counters = w.flags;
-  const uint32_t epoch = next_epoch();
   FusedArgs wa{};
   wa.in = (const __nv_bfloat16 *)r->x;
   LNET_TRY(encode_tile_map(&wa.tmap, r->x, B, T, C));
@@ -1358,7 +1382,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.out = w.stream;
   wa.rowsum = w.rowsum;
   wa.rec = w.wrec;
-  wa.epoch = epoch;
+  wa.epoch = next_epoch();
+  wa.epoch_word = w.epoch_word;
   wa.counter = counters;
   wa.error = counters + 2;
   wa.trace = fused_trace_enabled();
@@ -1394,7 +1419,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                               kFusedThreads, RP::LAUNCH_BYTES, st>>>(ra);
   LNET_TRY(after_launch("fused_reader_kernel"));
   fused_finalize_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * 14 * M, 256), 8 * sms), 256, 0,
-                          st>>>(w.rowsum, wm, rm, w.feats, B, T, M);
+                          st>>>(w.rowsum, wm, rm, w.feats, B, T, M, w.epoch_word);
   return after_launch("fused_finalize_kernel");
 }
 

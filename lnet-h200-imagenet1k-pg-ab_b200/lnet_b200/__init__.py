@@ -14,6 +14,7 @@ Laplace layer behind the reference ``lnet`` module API.
   GPU (:meth:`B200Alphabet.forward_images`).
 * :mod:`lnet_b200.pipeline` — host-fed serving loop overlapping the copies of
   the next batch with the current forward.
+* :mod:`lnet_b200.graph` — CUDA-graph capture and replay of a prepared forward.
 
 All compute runs in the C-ABI CUDA library ``_lib/liblnet_b200.so`` built by
 :func:`lnet_b200.build.build`; there is no CPU fallback.
