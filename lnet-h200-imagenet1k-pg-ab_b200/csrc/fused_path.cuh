@@ -2,30 +2,38 @@
 //
 // Work item = one chunk of kChunk (=128) consecutive steps of one batch row.
 // Items are claimed from an atomic counter in chunk-major order
-// (item = chunk * B + row), so the predecessor (row, chunk - 1) of every item
-// was claimed earlier by a running CTA: the decoupled look-back below always
-// makes progress.
+// (item = chunk * B + row), one item ahead, so the predecessor (row, chunk - 1)
+// of every item was claimed earlier by a running CTA: the decoupled look-back
+// below always makes progress.
 //
-// fused_writer_kernel (per item, one CTA of 256 threads, persistent):
-//   1. x rows [t0 - 8, t0 + 136) -> shared memory, no-swizzle K-major slabs;
+// fused_writer_kernel (persistent, one CTA of 512 threads per SM = two
+// independent item streams of 256 threads sharing the weight operands):
+//   1. x rows [t0 - 8, t0 + 136) by TMA (3-D tensor map, one 8-channel box per
+//      no-swizzle K-major slab, zero fill outside [0, T)), fetched one item
+//      ahead into the tile region;
 //   2. stem projection + dilated depthwise conv as ONE tcgen05 GEMM:
 //        acc[t, d] = sum_k sum_c x[t + 4k - 8, c] * (w[d, k] P[d, c]),
 //      the five taps are five row-shifted descriptors over the same tile;
-//   3. +bias, SiLU, RMSNorm (thread per step), xhat -> bf16 slab;
+//   3. +bias, SiLU, RMSNorm (thread per step, two threads per row), xhat ->
+//      bf16 slab; the bf16 stem output waits in the output rows (L2);
 //   4. drive GEMM in mode-major orientation: the A operand repeats the mode
 //      rows every 64 lanes, so every TMEM lane quarter holds the complex drive
 //      u_m(t) of 32 modes over all 128 steps (gamma is folded into the frame)
 //      and every warp can scan without a transpose;
 //   5. scan: each mode's 128 steps are cut into four sub-chunks of 32 scanned
-//      by four threads (one per warp pair); sub-chunk end states combine in
-//      shared memory into the chunk aggregate, which the last sub-chunk's warps
-//      publish and then resolve against their predecessors (decoupled
-//      look-back); a second pass from the true carries accumulates E, C1, C2,
-//      C4 and writes the states (bf16) as the A operand of
-//   6. the synthesis GEMM (token-major) and the residual epilogue
+//      by four threads; sub-chunk end states combine in shared memory into the
+//      chunk aggregate, which the last sub-chunk's threads publish and then
+//      resolve against their predecessors (decoupled look-back over tagged
+//      records, the predecessor's inclusive record prefetched); a second pass
+//      from the true carries accumulates E, C1, C2, C4 and writes the states
+//      (bf16) as the A operand of
+//   6. the synthesis GEMM (token-major), during which the chunk's moments are
+//      added to the row's fp64 sums, and the residual epilogue
 //      v = x + ls (s W^T + ds xhat), stored as bf16.
-// fused_reader_kernel: the same skeleton on the writer stream: conv of the
-//   stream tile on CUDA cores, SiLU, RMSNorm, drive GEMM, scan, moments.
+// fused_reader_kernel (two CTAs of 256 threads per SM): the same skeleton on
+//   the writer stream: TMA tile, conv on CUDA cores, SiLU, RMSNorm, drive
+//   GEMM, scan, moments.
+// fused_finalize_kernel: moments and radial-log features from the row sums.
 #pragma once
 
 #include <cuda.h>
