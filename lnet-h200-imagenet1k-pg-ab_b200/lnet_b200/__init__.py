@@ -5,8 +5,11 @@ Laplace layer behind the reference ``lnet`` module API.
   same forward signature and metadata errors).
 * :class:`B200PoleResidueTemporalMixing` — drop-in for
   ``lnet.laplace.PoleResidueTemporalMixing``.
-* :mod:`lnet_b200.ops` — the same calls as ``torch.library`` custom ops
-  (``lnet_b200::alphabet_forward``, ``lnet_b200::laplace_forward``).
+* :mod:`lnet_b200.ops` — the same calls as ``torch.library`` custom ops with
+  ``register_fake`` meta kernels (``lnet_b200::alphabet_forward``,
+  ``lnet_b200::laplace_forward``, ``lnet_b200::patchify_images``).
+* :mod:`lnet_b200.inference` — ``prepare_compiled_inference`` /
+  ``prepare_maskless_inference`` with the reference's call surface.
 * :mod:`lnet_b200.sharding` — batch sharding over one process per GPU.
 * :mod:`lnet_b200.timesplit` — sequence split over ranks (one carry exchange
   per block) for requests with fewer rows than GPUs.
@@ -20,7 +23,9 @@ All compute runs in the C-ABI CUDA library ``_lib/liblnet_b200.so`` built by
 :func:`lnet_b200.build.build`; there is no CPU fallback.
 """
 
+from . import ops  # registers the lnet_b200:: custom ops
 from .alphabet import AlphabetConfig, B200Alphabet
+from .inference import prepare_compiled_inference, prepare_maskless_inference
 from .laplace import (
     B200PoleResidueTemporalMixing,
     LaplaceParameterError,
@@ -33,4 +38,7 @@ __all__ = [
     "B200PoleResidueTemporalMixing",
     "LaplaceParameterError",
     "LaplaceShapeError",
+    "ops",
+    "prepare_compiled_inference",
+    "prepare_maskless_inference",
 ]

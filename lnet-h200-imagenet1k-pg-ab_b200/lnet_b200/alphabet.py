@@ -326,6 +326,15 @@ class B200Alphabet(nn.Module):
             return logits, wm, rm
         return logits
 
+    def op_arguments(self, device: torch.device | None = None) -> tuple[list[Tensor], list[int]]:
+        """``(weights, dims)`` for ``torch.ops.lnet_b200.alphabet_forward``: the effective
+        fp32 tensors in :data:`lnet_b200.ops.ALPHABET_WEIGHTS` order and the six sizes."""
+        device = torch.device(device) if device is not None else self.head.classifier.weight.device
+        params, tensors = self._effective(device)
+        dims = [params.raw_input_dim, params.model_dim, params.modes, params.output_dim,
+                params.conv_kernel, params.conv_dilation]
+        return [tensors[name] for name in _lib.PARAM_POINTER_FIELDS], dims
+
     @torch.no_grad()
     def prepare_for_inference_(self, *, sequence_length: int, batch_size: int,
                                use_static_poles: bool = True) -> B200Alphabet:

@@ -36,7 +36,12 @@ def patchify_images(images: Tensor, *, mean=IMAGENET_MEAN, std=IMAGENET_STD, pat
     b, h, w, _ = images.shape
     if h % patch or w % patch:
         raise ValueError(f"image {h}x{w} is not divisible by patch {patch}")
-    images = images.contiguous()
+    return _launch(images.contiguous(), mean, std, patch, dtype)
+
+
+def _launch(images: Tensor, mean, std, patch: int, dtype: torch.dtype) -> Tensor:
+    """One ``lnet_b200_patchify_images`` call on the current stream (checked arguments)."""
+    b, h, w, _ = images.shape
     out = torch.empty(b, (h // patch) * (w // patch), 3 * patch * patch, dtype=dtype,
                       device=images.device)
     m = (ctypes.c_float * 3)(*[float(v) for v in mean])

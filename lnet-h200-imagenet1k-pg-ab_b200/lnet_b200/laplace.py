@@ -115,29 +115,36 @@ class B200PoleResidueTemporalMixing(nn.Module):
 
 
 def laplace_forward_raw(layer: B200PoleResidueTemporalMixing, x: Tensor) -> Tensor:
+    """One ``lnet_b200_laplace_forward`` call with ``layer``'s parameters."""
+    dev = x.device
+
+    def f64(p: Tensor) -> Tensor:
+        return p.detach().to(device=dev, dtype=torch.float64).contiguous()
+
+    return _launch(x, f64(layer.raw_decay), f64(layer.residues), f64(layer.direct_term),
+                   f64(layer.bias), layer.modes, float(layer.dt), float(layer.min_decay))
+
+
+def _launch(x: Tensor, raw: Tensor, res: Tensor, direct: Tensor, bias: Tensor, modes: int,
+            dt: float, min_decay: float) -> Tensor:
+    """The C-ABI call on the current stream: contiguous float64 parameters on x's device."""
     lib = _lib.load()
     dev = x.device
     b, t, d = x.shape
     y = torch.empty_like(x)
     if b == 0 or t == 0:
         return y
-
-    def f64(p: Tensor) -> Tensor:
-        return p.detach().to(device=dev, dtype=torch.float64).contiguous()
-
-    raw, res, direct, bias = (f64(layer.raw_decay), f64(layer.residues), f64(layer.direct_term),
-                              f64(layer.bias))
     n = ctypes.c_size_t(0)
-    _lib.check(lib.lnet_b200_laplace_workspace_size(b, t, d, layer.modes, ctypes.byref(n)),
+    _lib.check(lib.lnet_b200_laplace_workspace_size(b, t, d, modes, ctypes.byref(n)),
                "lnet_b200_laplace_workspace_size")
     ws = torch.empty(max(int(n.value), 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
     dtype = _lib.LNET_F64 if x.dtype == torch.float64 else _lib.LNET_F32
     with torch.cuda.device(dev):
         st = lib.lnet_b200_laplace_forward(
-            raw.data_ptr(), res.data_ptr(), direct.data_ptr(), bias.data_ptr(), d, layer.modes,
-            float(layer.dt), float(layer.min_decay), dtype, x.data_ptr(), b, t, y.data_ptr(),
-            ws.data_ptr(), int(n.value), stream,
+            raw.data_ptr(), res.data_ptr(), direct.data_ptr(), bias.data_ptr(), d, modes, dt,
+            min_decay, dtype, x.data_ptr(), b, t, y.data_ptr(), ws.data_ptr(), int(n.value),
+            stream,
         )
     _lib.check(st, "lnet_b200_laplace_forward")
     return y
