@@ -239,16 +239,16 @@ def algorithmic_bytes(kernel: str, cfg) -> float | None:
         # fused route: stream v in (moments out are negligible)
         "fused_reader_kernel": bt * D * sa,
         # general route
-        "gemm_nt_kernel(stem)": bt * (C * sx + D * 4),
-        "gemm_nt_kernel(drive)": bt * (D * 4 + 2 * M * 4),
-        "gemm_nt_kernel(synthesis)": bt * (2 * M * 4 + D * 4),
+        "cublas(stem)": bt * (C * sx + D * 4),
+        "cublas(drive)": bt * (D * 4 + 2 * M * 4),
+        "cublas(synthesis)": bt * (2 * M * 4 + D * 4),
         "scan_local_kernel": bt * 2 * M * 4,
         "scan_apply_kernel": bt * 2 * M * 8,
         "moments_partial_kernel": bt * 2 * M * 4,
         "rmsnorm_kernel": bt * D * 8,
         "drive_kernel": bt * 2 * M * 8,
-        "dwconv_unit_kernel(stem)": bt * D * 8,
-        "dwconv_unit_kernel(reader)": bt * D * 8,
+        "depthwise_conv(stem)": bt * D * 8,
+        "depthwise_conv(reader)": bt * D * 8,
         "residual_kernel": bt * D * 16,
     }
     v = table.get(kernel)

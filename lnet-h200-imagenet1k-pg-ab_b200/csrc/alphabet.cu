@@ -57,6 +57,32 @@ static unsigned dw_grid(int64_t batch, int64_t steps) {
 }
 static unsigned token_block(int width) { return (unsigned)std::min(256, std::max(32, (width + 31) / 32 * 32)); }
 
+static dim3 carry_grid(int64_t batch, int modes) {
+  return dim3((unsigned)cdiv(modes, 32), (unsigned)batch);
+}
+
+// Depthwise conv + SiLU over [B, T, D] fp32 (see dwconv_unit_kernel); the
+// shared-memory tile kernel for the canonical K5 d4 geometry on aligned rows.
+static int depthwise_conv(const float *in, const float *w, const float *bias,
+                          const float *in_mask, const float *out_mask, float *out, int64_t B,
+                          int64_t T, int D, int taps, int dilation, cudaStream_t st,
+                          const char *what) {
+  const bool quad = taps == 5 && dilation == 4 && D % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(bias) % 16 == 0;
+  if (quad) {
+    const dim3 grid((unsigned)(B * cdiv(T, kDwTileSteps)), (unsigned)cdiv(D, kDwTileChans));
+    dwconv_tile_kernel<5, 4><<<grid, kDwTileThreads, 0, st>>>(in, w, bias, in_mask, out_mask, out,
+                                                             T, D);
+  } else {
+    dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
+        in, w, bias, in_mask, out_mask, out, B, T, D, taps, dilation);
+  }
+  return after_launch(what);
+}
+
+
 // ---------------------------------------------------------------- validation
 static int check_params(const lnet_b200_alphabet_params *p) {
   if (!p) return fail(LNET_ERR_INVALID_ARGUMENT, "params must not be NULL");
@@ -168,10 +194,9 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
         first_local, T, D, p->conv_kernel, p->conv_dilation);
     return after_launch("dwconv_physical_kernel(stem)");
   }
-  dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
-      pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask, first_local, B, T,
-      D, p->conv_kernel, p->conv_dilation);
-  return after_launch("dwconv_unit_kernel(stem)");
+  return depthwise_conv(pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
+                        first_local, B, T, D, p->conv_kernel, p->conv_dilation, st,
+                        "depthwise_conv(stem)");
 }
 
 // Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
@@ -200,7 +225,7 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   scan_local_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
                                             r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_local_kernel"));
-  scan_carry_kernel<<<(unsigned)cdiv(B * M, 128), 128, 0, st>>>(pl.carries, B, M, n_scan,
+  scan_carry_kernel<<<carry_grid(B, M), 32 * kCarryParts, 0, st>>>(pl.carries, B, M, n_scan,
                                                                 nullptr);
   LNET_TRY(after_launch("scan_carry_kernel"));
   scan_apply_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
@@ -253,10 +278,9 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
         r->valid_mask, pl.proj, T, D, p->conv_kernel, p->conv_dilation);
     LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
   } else {
-    dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
-        first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, r->valid_mask,
-        pl.proj, B, T, D, p->conv_kernel, p->conv_dilation);
-    LNET_TRY(after_launch("dwconv_unit_kernel(reader)"));
+    LNET_TRY(depthwise_conv(first_stream, p->reader_conv_weight, p->reader_conv_bias,
+                            r->valid_mask, r->valid_mask, pl.proj, B, T, D, p->conv_kernel,
+                            p->conv_dilation, st, "depthwise_conv(reader)"));
   }
   // the reader block sees no observation mask (src/lnet/alphabet.py:384-389)
   return block_scan_moments(pl.proj, p->reader_norm, p->reader_frame, p->reader_raw_decay,
@@ -557,7 +581,7 @@ extern "C" int lnet_b200_block_scan(const lnet_b200_alphabet_params *params,
   scan_local_kernel<<<gs, threads, 0, st>>>(u_states, bp.decay, bp.freq, a_re, a_im, nullptr,
                                             pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_local_kernel"));
-  scan_carry_kernel<<<(unsigned)cdiv(B * M, 128), 128, 0, st>>>(pl.carries, B, M, n_scan, init);
+  scan_carry_kernel<<<carry_grid(B, M), 32 * kCarryParts, 0, st>>>(pl.carries, B, M, n_scan, init);
   LNET_TRY(after_launch("scan_carry_kernel"));
   scan_apply_kernel<<<gs, threads, 0, st>>>(u_states, bp.decay, bp.freq, a_re, a_im, nullptr,
                                             pl.carries, T, M, kScanChunk, n_scan);
@@ -620,11 +644,10 @@ extern "C" int lnet_b200_depthwise_conv_silu(const lnet_b200_alphabet_params *pa
   const int64_t B = req->batch, T = req->steps;
   if (B * T == 0) return LNET_OK;
   const int D = params->model_dim;
-  dwconv_unit_kernel<float><<<dw_grid(B, T), token_block(D), 0, st>>>(
-      in, which == 0 ? params->stem_conv_weight : params->reader_conv_weight,
-      which == 0 ? params->stem_conv_bias : params->reader_conv_bias, nullptr, nullptr, out, B, T,
-      D, params->conv_kernel, params->conv_dilation);
-  return after_launch("dwconv_unit_kernel");
+  return depthwise_conv(in, which == 0 ? params->stem_conv_weight : params->reader_conv_weight,
+                        which == 0 ? params->stem_conv_bias : params->reader_conv_bias, nullptr,
+                        nullptr, out, B, T, D, params->conv_kernel, params->conv_dilation, st,
+                        "depthwise_conv");
 }
 
 extern "C" int lnet_b200_zoh(const float *raw_decay, const float *raw_frequency, int32_t modes,

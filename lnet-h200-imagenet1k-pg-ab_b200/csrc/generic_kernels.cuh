@@ -73,6 +73,77 @@ __global__ void dwconv_unit_kernel(const TI *__restrict__ in, const float *__res
   }
 }
 
+// Shared-memory tile form of the same conv for the canonical geometry (TAPS
+// taps, dilation DIL, fp32, dim % 4 == 0, 16-byte aligned rows).  Block =
+// (row, kDwTileSteps steps, kDwTileChans channels): the block stages the
+// kDwTileSteps + 2 PAD input steps of its channels with independent float4 loads
+// (every load in flight at once), then each thread produces outputs of one
+// channel quad from shared memory.  Same arithmetic as dwconv_unit_kernel, term
+// for term: taps outside the sequence read 0 and fmaf(w, 0, acc) == acc.
+constexpr int kDwTileSteps = 32, kDwTileChans = 64, kDwTileThreads = 128;
+template <int TAPS, int DIL>
+__global__ void __launch_bounds__(kDwTileThreads) dwconv_tile_kernel(
+    const float *__restrict__ in, const float *__restrict__ w, const float *__restrict__ bias,
+    const float *__restrict__ in_mask, const float *__restrict__ out_mask,
+    float *__restrict__ out, int64_t steps, int dim) {
+  constexpr int PAD = DIL * (TAPS - 1) / 2;
+  constexpr int ROWS = kDwTileSteps + 2 * PAD;
+  constexpr int Q = kDwTileChans / 4;
+  __shared__ float4 tile[ROWS][Q];
+  const int quads = dim >> 2;
+  const int qbase = blockIdx.y * Q;
+  const int nq = min(Q, quads - qbase);
+  const unsigned tiles = (unsigned)((steps + kDwTileSteps - 1) / kDwTileSteps);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t t0 = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kDwTileSteps;
+  const float4 *row = reinterpret_cast<const float4 *>(in + b * steps * dim) + qbase;
+  for (int i = threadIdx.x; i < ROWS * Q; i += kDwTileThreads) {
+    const int r = i / Q, qq = i - (i / Q) * Q;
+    const int64_t s = t0 - PAD + r;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (qq < nq && s >= 0 && s < steps) {
+      v = __ldg(row + s * quads + qq);
+      if (in_mask) {
+        const float mk = in_mask[b * steps + s];
+        v.x *= mk; v.y *= mk; v.z *= mk; v.w *= mk;
+      }
+    }
+    tile[r][qq] = v;
+  }
+  __syncthreads();
+  const int q = threadIdx.x % Q, g = threadIdx.x / Q;
+  if (q >= nq) return;
+  const int c = 4 * (qbase + q);
+  float wk[4][TAPS];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) wk[j][k] = w[(c + j) * TAPS + k];
+  const float4 bd = reinterpret_cast<const float4 *>(bias)[qbase + q];
+  float4 *orow = reinterpret_cast<float4 *>(out + b * steps * dim) + qbase + q;
+#pragma unroll 2
+  for (int i = g; i < kDwTileSteps; i += kDwTileThreads / Q) {
+    const int64_t t = t0 + i;
+    if (t >= steps) break;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) {
+      const float4 v = tile[i + k * DIL][q];
+      a0 = fmaf(wk[0][k], v.x, a0);
+      a1 = fmaf(wk[1][k], v.y, a1);
+      a2 = fmaf(wk[2][k], v.z, a2);
+      a3 = fmaf(wk[3][k], v.w, a3);
+    }
+    float4 y = make_float4(silu_f(a0 + bd.x), silu_f(a1 + bd.y), silu_f(a2 + bd.z),
+                           silu_f(a3 + bd.w));
+    if (out_mask) {
+      const float mk = out_mask[b * steps + t];
+      y.x *= mk; y.y *= mk; y.z *= mk; y.w *= mk;
+    }
+    orow[t * quads] = y;
+  }
+}
+
 // ---------------------------------------------------------------- timestamps
 // ts[b, t] = fp32(sum_{s<=t} double(dt[b, s]))  (CPU torch cumsum accumulates in double)
 // One warp per row: the lanes load 32 steps at once (coalesced), lane 0 adds
@@ -269,22 +340,67 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
   }
 }
 
-// `init` (optional, [B, 2M] re | im): the state before step 0 (a time slice's
-// carry-in); zero when NULL.
-__global__ void scan_carry_kernel(float *__restrict__ carries, int64_t batch, int modes,
-                                  int64_t n_chunks, const float *__restrict__ init) {
-  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= batch * modes) return;
-  int64_t b = i / modes;
-  int m = (int)(i - b * modes);
-  float sr = init ? init[b * 2 * modes + m] : 0.f, si = init ? init[b * 2 * modes + modes + m] : 0.f;
-  for (int64_t c = 0; c < n_chunks; ++c) {
-    float *rec = carries + ((b * n_chunks + c) * 4) * modes;
-    float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m], pi = rec[3 * modes + m];
+// Carry pass over the per-chunk records [B, nchunk, {E re, E im, P re, P im}, M]
+// (chunk c maps its entry state s to P s + E): rewrites E with the carry-in of
+// each chunk.  `init` (optional, [B, 2M] re | im): the state before step 0 (a
+// time slice's carry-in); zero when NULL.
+//
+// Block (32 modes, kCarryParts ranges of chunks), grid (mode groups, rows).
+// Three phases instead of one serial pass over all chunks: each thread composes
+// the maps of its range; one thread per mode chains the kCarryParts composed
+// maps; each thread re-walks its range from its carry-in.  The chain length
+// drops from nchunk to 2 nchunk / kCarryParts + kCarryParts dependent steps.
+constexpr int kCarryParts = 32;
+__global__ void __launch_bounds__(32 * kCarryParts) scan_carry_kernel(
+    float *__restrict__ carries, int64_t batch, int modes, int64_t n_chunks,
+    const float *__restrict__ init) {
+  __shared__ float sm[4][kCarryParts][33];
+  const int lane = threadIdx.x & 31, part = threadIdx.x >> 5;
+  const int m = blockIdx.x * 32 + lane;
+  const int64_t b = blockIdx.y;
+  const bool on = m < modes;
+  const int64_t per = (n_chunks + kCarryParts - 1) / kCarryParts;
+  const int64_t c0 = min(n_chunks, part * per), c1 = min(n_chunks, c0 + per);
+  float *base = carries + b * n_chunks * 4 * modes;
+  float Pr = 1.f, Pi = 0.f, Er = 0.f, Ei = 0.f;
+  if (on) {
+    for (int64_t c = c0; c < c1; ++c) {
+      const float *rec = base + c * 4 * modes;
+      const float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m],
+                  pi = rec[3 * modes + m];
+      const float nPr = pr * Pr - pi * Pi, nPi = pi * Pr + pr * Pi;
+      const float nEr = pr * Er - pi * Ei + er, nEi = pi * Er + pr * Ei + ei;
+      Pr = nPr; Pi = nPi; Er = nEr; Ei = nEi;
+    }
+  }
+  sm[0][part][lane] = Pr;
+  sm[1][part][lane] = Pi;
+  sm[2][part][lane] = Er;
+  sm[3][part][lane] = Ei;
+  __syncthreads();
+  if (part == 0 && on) {
+    float sr = init ? init[b * 2 * modes + m] : 0.f;
+    float si = init ? init[b * 2 * modes + modes + m] : 0.f;
+    for (int k = 0; k < kCarryParts; ++k) {
+      const float pr = sm[0][k][lane], pi = sm[1][k][lane], er = sm[2][k][lane],
+                  ei = sm[3][k][lane];
+      sm[2][k][lane] = sr;  // carry-in of range k
+      sm[3][k][lane] = si;
+      const float nr = pr * sr - pi * si + er, ni = pi * sr + pr * si + ei;
+      sr = nr;
+      si = ni;
+    }
+  }
+  __syncthreads();
+  if (!on) return;
+  float sr = sm[2][part][lane], si = sm[3][part][lane];
+  for (int64_t c = c0; c < c1; ++c) {
+    float *rec = base + c * 4 * modes;
+    const float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m],
+                pi = rec[3 * modes + m];
     rec[m] = sr;  // carry-in of chunk c
     rec[modes + m] = si;
-    float nr = pr * sr - pi * si + er;
-    float ni = pi * sr + pr * si + ei;
+    const float nr = pr * sr - pi * si + er, ni = pi * sr + pr * si + ei;
     sr = nr;
     si = ni;
   }
