@@ -44,6 +44,7 @@ int sm_count() {
   return n;
 }
 constexpr int kMomChunk = 64;
+static_assert(kMomChunk == kScanChunk, "fused scan + moments partials share the chunking");
 
 static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), 148 * 32)); }
 // Token-major elementwise kernels: blocks stride over tokens, threads over the
@@ -131,6 +132,8 @@ struct Plan {
   float *ts = nullptr;        // [BT]
   float *carries = nullptr;   // [B, nchunk, 4M]
   float *partial = nullptr;   // moment partials
+  float *edges = nullptr;     // [B, nchunk, 8, 2M] first / last four states of each chunk
+  float *wfold = nullptr;     // [D, 2M] drive frame with the ZOH gains folded in
   float *a_tab = nullptr;     // [8][M] a_re, a_im (writer, reader), then g_re, g_im (writer, reader)
   __nv_bfloat16 *w_bf16 = nullptr;  // [D, C] stem projection in bf16 (bf16 inputs)
   float *moments = nullptr;   // [2][B][7M]
@@ -155,6 +158,8 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.ts = ar.take<float>((size_t)bt);
   pl.carries = ar.take<float>((size_t)r->batch * n_scan * 4 * M);
   pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
+  pl.edges = ar.take<float>((size_t)r->batch * n_scan * 16 * M);
+  pl.wfold = ar.take<float>((size_t)D * 2 * M);
   pl.a_tab = ar.take<float>((size_t)8 * M);
   pl.w_bf16 = ar.take<__nv_bfloat16>((size_t)D * C);
   pl.moments = ar.take<float>((size_t)2 * r->batch * 7 * M);
@@ -200,25 +205,36 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 }
 
 // Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
+// `write_states`: leave the states in pl.drive (the writer's synthesis reads them).
 static int block_scan_moments(const float *in, const float *norm, const float *frame,
                               const float *raw_decay, const float *raw_freq, float *a_re,
                               float *a_im, float *g_re, float *g_im, const float *event_mask,
                               int obs_channels,
                               const lnet_b200_alphabet_request *r, int D, int M, Plan &pl,
-                              float *moments, cudaStream_t st) {
+                              float *moments, bool write_states, cudaStream_t st) {
   const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const bool tf32 = r->act_dtype == LNET_BF16;
   rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, norm, pl.xhat, bt, D);
   LNET_TRY(after_launch("rmsnorm_kernel"));
-  LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
-                     bt, 2 * M, D, r->act_dtype == LNET_BF16, "cublas(drive)"));
   if (!r->time_delta) {  // per-mode a and gamma tables (static poles)
     zoh_kernel<<<1, 128, 0, st>>>(raw_decay, raw_freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
     LNET_TRY(after_launch("zoh_kernel"));
   }
-  drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(pl.drive, raw_decay, raw_freq,
-                                                          r->time_delta, g_re, g_im, event_mask,
-                                                          obs_channels, bt, M);
-  LNET_TRY(after_launch("drive_kernel"));
+  if (!r->time_delta && !event_mask) {
+    // u = g (x^ W) in one GEMM over the gain-folded frame
+    fold_gain_kernel<<<grid_for((int64_t)D * M), 256, 0, st>>>(frame, g_re, g_im, pl.wfold, D,
+                                                              M);
+    LNET_TRY(after_launch("fold_gain_kernel"));
+    LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, pl.drive,
+                       2 * M, bt, 2 * M, D, tf32, "cublas(drive)"));
+  } else {
+    LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
+                       bt, 2 * M, D, tf32, "cublas(drive)"));
+    drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(pl.drive, raw_decay, raw_freq,
+                                                            r->time_delta, g_re, g_im, event_mask,
+                                                            obs_channels, bt, M);
+    LNET_TRY(after_launch("drive_kernel"));
+  }
   const int64_t n_scan = cdiv(T, kScanChunk);
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   dim3 gs((unsigned)n_scan, (unsigned)B);
@@ -228,24 +244,36 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   scan_carry_kernel<<<carry_grid(B, M), 32 * kCarryParts, 0, st>>>(pl.carries, B, M, n_scan,
                                                                 nullptr);
   LNET_TRY(after_launch("scan_carry_kernel"));
+  if (!r->time_delta) {
+    if (write_states)
+      scan_apply_moments_kernel<true><<<gs, threads, 0, st>>>(
+          pl.drive, a_re, a_im, pl.carries, r->valid_mask, pl.partial, pl.edges, T, M,
+          kScanChunk, n_scan);
+    else
+      scan_apply_moments_kernel<false><<<gs, threads, 0, st>>>(
+          pl.drive, a_re, a_im, pl.carries, r->valid_mask, pl.partial, pl.edges, T, M,
+          kScanChunk, n_scan);
+    LNET_TRY(after_launch("scan_apply_moments_kernel"));
+    if (n_scan > 1) {
+      moments_edges_kernel<<<grid_for(B * (n_scan - 1) * M), 256, 0, st>>>(
+          pl.partial, pl.edges, r->valid_mask, B, T, M, kScanChunk, n_scan);
+      LNET_TRY(after_launch("moments_edges_kernel"));
+    }
+    const dim3 gf((unsigned)cdiv(7 * M, 32), (unsigned)B);
+    moments_finalize_kernel<<<gf, 32 * kFinalParts, 0, st>>>(pl.partial, r->valid_mask, moments,
+                                                            T, M, n_scan);
+    return after_launch("moments_finalize_kernel");
+  }
   scan_apply_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
                                             r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_apply_kernel"));
   const int64_t n_mom = cdiv(T, kMomChunk);
   dim3 gm((unsigned)n_mom, (unsigned)B);
-  if (r->time_delta) {
-    pt_moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, pl.ts, r->time_delta,
-                                                      r->valid_mask, pl.partial, T, M, n_mom);
-    LNET_TRY(after_launch("pt_moments_partial_kernel"));
-    pt_moments_finalize_kernel<<<(unsigned)B, threads, 0, st>>>(pl.partial, moments, M, n_mom);
-    return after_launch("pt_moments_finalize_kernel");
-  }
-  moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, r->valid_mask, pl.partial, T, M,
-                                                 kMomChunk, n_mom, nullptr);
-  LNET_TRY(after_launch("moments_partial_kernel"));
-  moments_finalize_kernel<<<(unsigned)B, 256, 0, st>>>(pl.partial, r->valid_mask, moments, T, M,
-                                                       n_mom);
-  return after_launch("moments_finalize_kernel");
+  pt_moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, pl.ts, r->time_delta,
+                                                    r->valid_mask, pl.partial, T, M, n_mom);
+  LNET_TRY(after_launch("pt_moments_partial_kernel"));
+  pt_moments_finalize_kernel<<<(unsigned)B, threads, 0, st>>>(pl.partial, moments, M, n_mom);
+  return after_launch("pt_moments_finalize_kernel");
 }
 
 static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -256,7 +284,8 @@ static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
   LNET_TRY(block_scan_moments(first_local, p->writer_norm, p->writer_frame, p->writer_raw_decay,
                               p->writer_raw_frequency, pl.a_tab, pl.a_tab + M,
                               pl.a_tab + 4 * M, pl.a_tab + 5 * M,
-                              r->observation_mask, r->obs_channels, r, D, M, pl, moments, st));
+                              r->observation_mask, r->obs_channels, r, D, M, pl, moments,
+                              /*write_states=*/true, st));
   LNET_TRY(gemm_rows(st, pl.drive, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
                      pl.modal, D, bt, D, 2 * M, r->act_dtype == LNET_BF16, "cublas(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(first_local, pl.xhat, pl.modal,
@@ -286,7 +315,7 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
   return block_scan_moments(pl.proj, p->reader_norm, p->reader_frame, p->reader_raw_decay,
                             p->reader_raw_frequency, pl.a_tab + 2 * M, pl.a_tab + 3 * M,
                             pl.a_tab + 6 * M, pl.a_tab + 7 * M, nullptr,
-                            1, r, D, M, pl, moments, st);
+                            1, r, D, M, pl, moments, /*write_states=*/false, st);
 }
 
 static int head_run(const lnet_b200_alphabet_params *p, int64_t B, const float *wm,
@@ -549,14 +578,14 @@ extern "C" int lnet_b200_block_drive(const lnet_b200_alphabet_params *params,
   float *xhat = xhat_out ? xhat_out : pl.xhat;
   rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, bp.norm, xhat, bt, D);
   LNET_TRY(after_launch("rmsnorm_kernel"));
-  LNET_TRY(gemm_rows(st, xhat, CUDA_R_32F, D, bp.frame, CUDA_R_32F, 1, 2 * M, u_out, 2 * M, bt,
-                     2 * M, D, req->act_dtype == LNET_BF16, "cublas(drive)"));
+  // the same arithmetic as the unsplit forward: one GEMM over the gain-folded frame
   float *a_re = pl.a_tab, *a_im = pl.a_tab + M, *g_re = pl.a_tab + 4 * M, *g_im = pl.a_tab + 5 * M;
   zoh_kernel<<<1, 128, 0, st>>>(bp.decay, bp.freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
   LNET_TRY(after_launch("zoh_kernel"));
-  drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(u_out, bp.decay, bp.freq, nullptr, g_re,
-                                                          g_im, nullptr, 1, bt, M);
-  return after_launch("drive_kernel");
+  fold_gain_kernel<<<grid_for((int64_t)D * M), 256, 0, st>>>(bp.frame, g_re, g_im, pl.wfold, D, M);
+  LNET_TRY(after_launch("fold_gain_kernel"));
+  return gemm_rows(st, xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, u_out, 2 * M, bt,
+                   2 * M, D, req->act_dtype == LNET_BF16, "cublas(drive)");
 }
 
 extern "C" int lnet_b200_block_scan(const lnet_b200_alphabet_params *params,

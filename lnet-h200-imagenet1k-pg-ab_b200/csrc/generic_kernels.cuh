@@ -495,54 +495,199 @@ __global__ void moment_sums_kernel(const float *__restrict__ partial, double *__
   }
 }
 
-// One block per row: counts, then ordered reduction of the partials.
-__global__ void moments_finalize_kernel(const float *__restrict__ partial,
-                                        const float *__restrict__ valid,
-                                        float *__restrict__ moments, int64_t steps, int modes,
-                                        int64_t n_chunks) {
-  const int64_t b = blockIdx.x;
-  __shared__ double s_cnt[4];
-  __shared__ double red[4][32];
+// Scan apply pass with the moments accumulated on the fly (static poles): per
+// (chunk, row) block, each thread walks one mode through the chunk from its
+// carry-in, optionally writes the states in place over u (WRITE_STATES; the
+// writer's synthesis GEMM reads them, the reader needs moments only), and sums
+// E and the lag-1/2/4 products (valid-weighted when `valid`) over the pairs
+// that lie inside the chunk, holding the last four states in registers.  The
+// chunk's first and last four states go to `edges` [B, nchunk, 8, 2M] so that
+// moments_edges_kernel adds the pairs that straddle two chunks.  partial
+// layout [B, nchunk, 7M]; products as in moments_partial_kernel.
+template <bool WRITE_STATES>
+__global__ void scan_apply_moments_kernel(float *__restrict__ u, const float *__restrict__ a_re_tab,
+                                          const float *__restrict__ a_im_tab,
+                                          const float *__restrict__ carries,
+                                          const float *__restrict__ valid,
+                                          float *__restrict__ partial, float *__restrict__ edges,
+                                          int64_t steps, int modes, int chunk, int64_t n_chunks) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * chunk;
+  const int len = (int)min((int64_t)chunk, steps - t0);
+  const int64_t M2 = 2 * modes;
+  float *ed = edges + (b * n_chunks + c) * 8 * M2;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    const float ar = a_re_tab[m], ai = a_im_tab[m];
+    const float *rec = carries + ((b * n_chunks + c) * 4) * modes;
+    float sr = rec[m], si = rec[modes + m];
+    float hr0 = 0.f, hi0 = 0.f, hr1 = 0.f, hi1 = 0.f, hr2 = 0.f, hi2 = 0.f, hr3 = 0.f, hi3 = 0.f;
+    float e0 = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
+    float *row = u + (b * steps + t0) * M2;
+    const float *vrow = valid ? valid + b * steps + t0 : nullptr;
+    for (int i = 0; i < len; ++i, row += M2) {
+      const float nr = ar * sr - ai * si + row[m];
+      const float ni = ai * sr + ar * si + row[modes + m];
+      sr = nr;
+      si = ni;
+      if (WRITE_STATES) {
+        row[m] = sr;
+        row[modes + m] = si;
+      }
+      const float wt = vrow ? vrow[i] : 1.f;
+      e0 += (sr * sr + si * si) * wt;
+      if (i >= 1) {
+        const float w = vrow ? wt * vrow[i - 1] : 1.f;
+        c1r += (sr * hr0 + si * hi0) * w;
+        c1i += (si * hr0 - sr * hi0) * w;
+      }
+      if (i >= 2) {
+        const float w = vrow ? wt * vrow[i - 2] : 1.f;
+        c2r += (sr * hr1 + si * hi1) * w;
+        c2i += (si * hr1 - sr * hi1) * w;
+      }
+      if (i >= 4) {
+        const float w = vrow ? wt * vrow[i - 4] : 1.f;
+        c4r += (sr * hr3 + si * hi3) * w;
+        c4i += (si * hr3 - sr * hi3) * w;
+      }
+      if (i < 4) {
+        ed[i * M2 + m] = sr;
+        ed[i * M2 + modes + m] = si;
+      }
+      if (i >= len - 4) {  // slots 4..7 hold the chunk's last four states
+        const int k = i - len + 8;
+        ed[k * M2 + m] = sr;
+        ed[k * M2 + modes + m] = si;
+      }
+      hr3 = hr2; hi3 = hi2; hr2 = hr1; hi2 = hi1; hr1 = hr0; hi1 = hi0; hr0 = sr; hi0 = si;
+    }
+    float *out = partial + (b * n_chunks + c) * 7 * modes;
+    out[m] = e0;
+    out[modes + m] = c1r;
+    out[2 * modes + m] = c1i;
+    out[3 * modes + m] = c2r;
+    out[4 * modes + m] = c2i;
+    out[5 * modes + m] = c4r;
+    out[6 * modes + m] = c4i;
+  }
+}
+
+// Adds to each chunk's partial the lag pairs that straddle its start: for chunk
+// c >= 1 and lag l, the pairs (t0 + i, t0 + i - l), i < l, whose earlier state
+// is among the previous chunk's last four (`edges` slots 4..7).  One thread per
+// (row, chunk >= 1, mode).
+__global__ void moments_edges_kernel(float *__restrict__ partial, const float *__restrict__ edges,
+                                     const float *__restrict__ valid, int64_t batch,
+                                     int64_t steps, int modes, int chunk, int64_t n_chunks) {
+  const int64_t n = batch * (n_chunks - 1) * modes;
+  const int64_t M2 = 2 * modes;
   const int lags[3] = {1, 2, 4};
-  double cnt[4] = {0, 0, 0, 0};
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t bc = idx / modes;
+    const int m = (int)(idx - bc * modes);
+    const int64_t b = bc / (n_chunks - 1);
+    const int64_t c = bc - b * (n_chunks - 1) + 1;
+    const int64_t t0 = c * chunk;
+    const int len = (int)min((int64_t)chunk, steps - t0);
+    const float *cur = edges + (b * n_chunks + c) * 8 * M2;
+    const float *prv = edges + (b * n_chunks + c - 1) * 8 * M2;
+    float *out = partial + (b * n_chunks + c) * 7 * modes;
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      const int lag = lags[l];
+      float re = 0.f, im = 0.f;
+      for (int i = 0; i < lag && i < len; ++i) {
+        const int k = i - lag + 8;  // previous chunk's slot of step t0 + i - lag
+        const float cr = cur[i * M2 + m], ci = cur[i * M2 + modes + m];
+        const float pr = prv[k * M2 + m], pi = prv[k * M2 + modes + m];
+        const float w = valid ? valid[b * steps + t0 + i] * valid[b * steps + t0 + i - lag] : 1.f;
+        re += (cr * pr + ci * pi) * w;
+        im += (ci * pr - cr * pi) * w;
+      }
+      out[(1 + 2 * l) * modes + m] += re;
+      out[(2 + 2 * l) * modes + m] += im;
+    }
+  }
+}
+
+// Normalised moments [B, 7M] from the chunk partials (edge pairs included);
+// valid counts clamped at one (_masked_modal_moments, sum(...).clamp_min(1.0)),
+// else divided by the pair count.  Grid (ceil(7M / 32), B); block = 32 features
+// x kFinalParts chunk ranges summed in double, combined in range order.
+constexpr int kFinalParts = 32;
+__global__ void __launch_bounds__(32 * kFinalParts) moments_finalize_kernel(
+    const float *__restrict__ partial, const float *__restrict__ valid,
+    float *__restrict__ moments, int64_t steps, int modes, int64_t n_chunks) {
+  const int64_t b = blockIdx.y;
+  const int lane = threadIdx.x & 31, part = threadIdx.x >> 5;
+  __shared__ double s_cnt[4];
+  __shared__ double red[kFinalParts][33];
+  const int lags[3] = {1, 2, 4};
   if (valid) {
+    double cnt[4] = {0, 0, 0, 0};
     for (int64_t t = threadIdx.x; t < steps; t += blockDim.x) {
-      double v = valid[b * steps + t];
+      const double v = valid[b * steps + t];
       cnt[0] += v;
       for (int l = 0; l < 3; ++l)
         if (t >= lags[l]) cnt[1 + l] += v * (double)valid[b * steps + t - lags[l]];
     }
-  }
-  // block reduce the 4 counts (warp shuffles then one warp)
-  for (int j = 0; j < 4; ++j) {
-    double v = cnt[j];
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if ((threadIdx.x & 31) == 0) red[j][threadIdx.x >> 5] = v;
-  }
-  __syncthreads();
-  if (threadIdx.x < 4) {
-    double v = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[threadIdx.x][w];
-    s_cnt[threadIdx.x] = v;
-  }
-  __syncthreads();
-  for (int j = threadIdx.x; j < 7 * modes; j += blockDim.x) {
-    int kind = j / modes;  // 0 = E, 1..6 = lag pairs
-    int lag_idx = kind == 0 ? -1 : (kind - 1) / 2;
-    double acc = 0.0;
-    for (int64_t c = 0; c < n_chunks; ++c) acc += (double)partial[(b * n_chunks + c) * 7 * modes + j];
-    float outv;
-    if (lag_idx >= 0 && steps <= lags[lag_idx]) {
-      outv = 0.f;
-    } else if (valid) {
-      // counts are clamped at one (sum(...).clamp_min(1.0))
-      float cntf = (float)s_cnt[lag_idx + 1];
-      outv = (float)acc / fmaxf(cntf, 1.0f);
-    } else {
-      int64_t n = lag_idx < 0 ? steps : steps - lags[lag_idx];
-      outv = (float)(acc / (double)n);
+    for (int k = 0; k < 4; ++k) {
+      double v = cnt[k];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[part][k] = v;
     }
-    moments[b * 7 * modes + j] = outv;
+    __syncthreads();
+    if (threadIdx.x < 4) {
+      double v = 0;
+      for (int w = 0; w < kFinalParts; ++w) v += red[w][threadIdx.x];
+      s_cnt[threadIdx.x] = v;
+    }
+    __syncthreads();
+  }
+  const int j = blockIdx.x * 32 + lane;
+  const bool on = j < 7 * modes;
+  const int64_t per = (n_chunks + kFinalParts - 1) / kFinalParts;
+  const int64_t c0 = min(n_chunks, part * per), c1 = min(n_chunks, c0 + per);
+  double acc = 0.0;
+  if (on)
+    for (int64_t c = c0; c < c1; ++c) acc += (double)partial[(b * n_chunks + c) * 7 * modes + j];
+  __syncthreads();
+  red[part][lane] = acc;
+  __syncthreads();
+  if (part != 0 || !on) return;
+  double total = 0.0;
+  for (int w = 0; w < kFinalParts; ++w) total += red[w][lane];
+  const int kind = j / modes;  // 0 = E, 1..6 = lag pairs (re, im)
+  const int lag_idx = kind == 0 ? -1 : (kind - 1) / 2;
+  float outv;
+  if (lag_idx >= 0 && steps <= lags[lag_idx]) {
+    outv = 0.f;
+  } else if (valid) {
+    const float cntf = (float)s_cnt[lag_idx + 1];
+    outv = (float)total / fmaxf(cntf, 1.0f);
+  } else {
+    const int64_t n = lag_idx < 0 ? steps : steps - lags[lag_idx];
+    outv = (float)(total / (double)n);
+  }
+  moments[b * 7 * modes + j] = outv;
+}
+
+// Gains folded into the drive frame (static poles, no event mask):
+// out[:, m] = g_re W_re - g_im W_im, out[:, M + m] = g_re W_im + g_im W_re, so
+// the drive GEMM yields u = g (x^ W) directly (frame [D, 2M] row-major).
+__global__ void fold_gain_kernel(const float *__restrict__ frame, const float *__restrict__ g_re,
+                                 const float *__restrict__ g_im, float *__restrict__ out, int dim,
+                                 int modes) {
+  const int64_t n = (int64_t)dim * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t d = i / modes;
+    const int m = (int)(i - d * modes);
+    const float *w = frame + d * 2 * modes;
+    const float wr = w[m], wi = w[modes + m];
+    out[d * 2 * modes + m] = g_re[m] * wr - g_im[m] * wi;
+    out[d * 2 * modes + modes + m] = g_re[m] * wi + g_im[m] * wr;
   }
 }
 
