@@ -134,13 +134,14 @@ int lnet_b200_alphabet_forward_prepared(const lnet_b200_alphabet_params *params,
                                         float *writer_moments, float *reader_moments,
                                         lnet_stream_t stream);
 
-/* Device-side status of the last lnet_b200_alphabet_forward that ran the fused
- * route in `workspace` (synchronises the device; 0 for the general route).
- * Every wait inside the fused kernels is bounded; a wait that gave up sets a
- * bit: 1 << 0..3 MMA completion (writer stem, writer drive, writer synthesis,
- * reader drive), 1 << 4 / 1 << 5 look-back (writer / reader).  Nonzero means the
- * results of that call are invalid.  No reference counterpart (the reference
- * has no device-side waits). */
+/* Device-side status of the last lnet_b200_alphabet_forward in `workspace`
+ * for this request's route (synchronises the device).  Every wait inside the
+ * kernels is bounded; a wait that gave up sets a bit: 1 << 0..3 MMA completion
+ * (writer stem, writer drive, writer synthesis, reader drive), 1 << 4 / 1 << 5
+ * look-back (writer / reader), 1 << 6 / 1 << 7 tile loads (writer / reader) on
+ * the fused route; 1 << 8 a bulk input copy of the general route's conv +
+ * RMSNorm kernel.  Nonzero means the results of that call are invalid.  No
+ * reference counterpart (the reference has no device-side waits). */
 int lnet_b200_alphabet_device_status(const lnet_b200_alphabet_params *params,
                                      const lnet_b200_alphabet_request *req,
                                      const void *workspace, size_t workspace_bytes,

@@ -134,6 +134,7 @@ struct Plan {
   float *partial = nullptr;   // moment partials
   float *edges = nullptr;     // [B, nchunk, 8, 2M] first / last four states of each chunk
   float *wfold = nullptr;     // [D, 2M] drive frame with the ZOH gains folded in
+  uint32_t *status = nullptr; // general-route device error bits (zeroed per forward)
   float *a_tab = nullptr;     // [8][M] a_re, a_im (writer, reader), then g_re, g_im (writer, reader)
   __nv_bfloat16 *w_bf16 = nullptr;  // [D, C] stem projection in bf16 (bf16 inputs)
   float *moments = nullptr;   // [2][B][7M]
@@ -160,6 +161,7 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
   pl.edges = ar.take<float>((size_t)r->batch * n_scan * 16 * M);
   pl.wfold = ar.take<float>((size_t)D * 2 * M);
+  pl.status = ar.take<uint32_t>(4);
   pl.a_tab = ar.take<float>((size_t)8 * M);
   pl.w_bf16 = ar.take<__nv_bfloat16>((size_t)D * C);
   pl.moments = ar.take<float>((size_t)2 * r->batch * 7 * M);
@@ -168,10 +170,11 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
 }
 
 // ---------------------------------------------------------------- general-route stages
+// Stem projection x W^T -> pl.proj (inputs masked first when metadata asks).
 template <typename TX>
-static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
-                        Plan &pl, float *first_local, cudaStream_t st) {
-  const int64_t B = r->batch, T = r->steps, bt = B * T;
+static int stem_projection(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                           Plan &pl, cudaStream_t st) {
+  const int64_t bt = r->batch * r->steps;
   const int C = p->raw_input_dim, D = p->model_dim;
   const TX *x = (const TX *)r->x;
   const bool tf32 = r->act_dtype == LNET_BF16;
@@ -191,6 +194,15 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
     LNET_TRY(gemm_rows(st, x, CUDA_R_16BF, C, pl.w_bf16, CUDA_R_16BF, C, 1, pl.proj, D, bt, D, C,
                        false, "cublas(stem)"));
   }
+  return LNET_OK;
+}
+
+template <typename TX>
+static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                        Plan &pl, float *first_local, cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const int D = p->model_dim;
+  LNET_TRY(stem_projection<TX>(p, r, pl, st));
   if (r->time_delta) {
     timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
     LNET_TRY(after_launch("timestamps_kernel"));
@@ -206,16 +218,20 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 
 // Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
 // `write_states`: leave the states in pl.drive (the writer's synthesis reads them).
+// `normed`: pl.xhat already holds RMSNorm(in).
 static int block_scan_moments(const float *in, const float *norm, const float *frame,
                               const float *raw_decay, const float *raw_freq, float *a_re,
                               float *a_im, float *g_re, float *g_im, const float *event_mask,
                               int obs_channels,
                               const lnet_b200_alphabet_request *r, int D, int M, Plan &pl,
-                              float *moments, bool write_states, cudaStream_t st) {
+                              float *moments, bool write_states, cudaStream_t st,
+                              bool normed = false) {
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const bool tf32 = r->act_dtype == LNET_BF16;
-  rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, norm, pl.xhat, bt, D);
-  LNET_TRY(after_launch("rmsnorm_kernel"));
+  if (!normed) {  // else pl.xhat holds RMSNorm(in) already (conv_norm)
+    rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, norm, pl.xhat, bt, D);
+    LNET_TRY(after_launch("rmsnorm_kernel"));
+  }
   if (!r->time_delta) {  // per-mode a and gamma tables (static poles)
     zoh_kernel<<<1, 128, 0, st>>>(raw_decay, raw_freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
     LNET_TRY(after_launch("zoh_kernel"));
@@ -274,6 +290,77 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   LNET_TRY(after_launch("pt_moments_partial_kernel"));
   pt_moments_finalize_kernel<<<(unsigned)B, threads, 0, st>>>(pl.partial, moments, M, n_mom);
   return after_launch("pt_moments_finalize_kernel");
+}
+
+// Whether the conv + RMSNorm kernel applies (canonical K5 d4 conv on aligned
+// fp32 rows, 4 | D <= 256, step-indexed convs).
+static bool conv_norm_ok(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                         const Plan &pl) {
+  auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  const int D = p->model_dim;
+  return !r->time_delta && p->conv_kernel == 5 && p->conv_dilation == 4 && D % 4 == 0 &&
+         D <= 256 && al(pl.proj) && al(pl.stream) && al(pl.xhat) && al(p->stem_conv_bias) &&
+         al(p->reader_conv_bias) && al(p->writer_norm) && al(p->reader_norm) &&
+         al(p->writer_layer_scale) && al(p->writer_direct_scale);
+}
+
+static int conv_norm(const float *in, const float *w, const float *bias, const float *in_mask,
+                     const float *out_mask, const float *g, const float *ls, const float *ds,
+                     float *xhat, float *base, uint32_t *status, int64_t B, int64_t T, int D,
+                     cudaStream_t st, const char *what) {
+  constexpr int rows = kDnSteps + 16;
+  static_assert(kDnParts <= 32 && kDnSteps * kDnParts == kDnThreads, "reduction layout");
+  const size_t smem = dwconv_norm_smem(rows, D / 4);
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device
+  int dev = 0;
+  LNET_TRY(cuda_check(cudaGetDevice(&dev), "cudaGetDevice"));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set.load() & bit)) {
+    LNET_TRY(cuda_check(cudaFuncSetAttribute(dwconv_norm_kernel<5, 4>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)dwconv_norm_smem(rows, 64)),
+                        "cudaFuncSetAttribute(dwconv_norm_kernel)"));
+    attr_set.fetch_or(bit);
+  }
+  const int64_t tiles = B * cdiv(T, kDnSteps);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)sm_count() * kDnBlocksPerSM);
+  dwconv_norm_kernel<5, 4><<<grid, kDnThreads, smem, st>>>(
+      in, w, bias, in_mask, out_mask, g, ls, ds, xhat, base, nullptr, B, T, D, status);
+  return after_launch(what);
+}
+
+// The whole general route with the conv + RMSNorm kernel (conv_norm_ok): the
+// stem conv writes xhat and the writer's residual base straight into the
+// stream buffer, the synthesis GEMM accumulates ls (s W^T) onto it (beta = 1,
+// ls folded into the frame rows), and the reader conv writes its xhat only.
+template <typename TX>
+static int forward_generic_normed(const lnet_b200_alphabet_params *p,
+                                  const lnet_b200_alphabet_request *r, Plan &pl, float *wm,
+                                  float *rm, cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const int D = p->model_dim, M = p->modes;
+  const bool tf32 = r->act_dtype == LNET_BF16;
+  LNET_TRY(stem_projection<TX>(p, r, pl, st));
+  LNET_TRY(conv_norm(pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
+                     p->writer_norm, p->writer_layer_scale, p->writer_direct_scale, pl.xhat,
+                     pl.stream, pl.status, B, T, D, st, "conv_norm(stem)"));
+  LNET_TRY(block_scan_moments(nullptr, p->writer_norm, p->writer_frame, p->writer_raw_decay,
+                              p->writer_raw_frequency, pl.a_tab, pl.a_tab + M,
+                              pl.a_tab + 4 * M, pl.a_tab + 5 * M, r->observation_mask,
+                              r->obs_channels, r, D, M, pl, wm, /*write_states=*/true, st,
+                              /*normed=*/true));
+  scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(
+      p->writer_frame, p->writer_layer_scale, pl.wfold, D, 2 * M);
+  LNET_TRY(after_launch("scale_rows_kernel"));
+  LNET_TRY(gemm_rows(st, pl.drive, CUDA_R_32F, 2 * M, pl.wfold, CUDA_R_32F, 2 * M, 1, pl.stream,
+                     D, bt, D, 2 * M, tf32, "cublas(synthesis)", /*beta=*/1.f));
+  LNET_TRY(conv_norm(pl.stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
+                     r->valid_mask, p->reader_norm, nullptr, nullptr, pl.xhat, nullptr,
+                     pl.status, B, T, D, st, "conv_norm(reader)"));
+  return block_scan_moments(nullptr, p->reader_norm, p->reader_frame, p->reader_raw_decay,
+                            p->reader_raw_frequency, pl.a_tab + 2 * M, pl.a_tab + 3 * M,
+                            pl.a_tab + 6 * M, pl.a_tab + 7 * M, nullptr, 1, r, D, M, pl, rm,
+                            /*write_states=*/false, st, /*normed=*/true);
 }
 
 static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -378,10 +465,11 @@ extern "C" int lnet_b200_alphabet_device_status(const lnet_b200_alphabet_params 
   LNET_TRY(check_request(params, req));
   if (!status) return fail(LNET_ERR_INVALID_ARGUMENT, "status must not be NULL");
   *status = 0;
-  if (!use_fused(params, req) || req->batch == 0 || req->steps == 0) return LNET_OK;
+  if (req->batch == 0 || req->steps == 0) return LNET_OK;
+  const bool fused = use_fused(params, req);
   Plan pl;
-  LNET_TRY(plan_all(params, req, const_cast<void *>(workspace), workspace_bytes, pl, true));
-  const uint32_t *err = pl.fused.flags + 2;
+  LNET_TRY(plan_all(params, req, const_cast<void *>(workspace), workspace_bytes, pl, fused));
+  const uint32_t *err = fused ? pl.fused.flags + 2 : pl.status;
   return cuda_check(cudaMemcpy(status, err, sizeof(uint32_t), cudaMemcpyDeviceToHost),
                     "cudaMemcpy(device status)");
 }
@@ -432,6 +520,14 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
   LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
   float *wm = writer_moments ? writer_moments : pl.moments;
   float *rm = reader_moments ? reader_moments : pl.moments + B * 7 * M;
+  LNET_TRY(cuda_check(cudaMemsetAsync(pl.status, 0, sizeof(uint32_t), st), "cudaMemsetAsync"));
+  if (conv_norm_ok(params, req, pl)) {
+    if (req->x_dtype == LNET_BF16)
+      LNET_TRY(forward_generic_normed<__nv_bfloat16>(params, req, pl, wm, rm, st));
+    else
+      LNET_TRY(forward_generic_normed<float>(params, req, pl, wm, rm, st));
+    return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st);
+  }
   if (req->x_dtype == LNET_BF16)
     LNET_TRY(stem_generic<__nv_bfloat16>(params, req, pl, pl.first_local, st));
   else

@@ -31,11 +31,12 @@ inline int blas_handle(cublasHandle_t *out) {
   return LNET_OK;
 }
 
-// C[rows, n] (row-major, leading dimension ldc) = A[rows, k] (row-major, lda) * B^T,
+// C[rows, n] (row-major, leading dimension ldc) = A[rows, k] (row-major, lda) * B^T + beta C,
 // with element (j, kk) of B at Bm[j * ldbn + kk * ldbk] (one of ldbn, ldbk is 1).
 inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t lda, const void *Bm,
                      cudaDataType tb, int64_t ldbn, int64_t ldbk, float *C, int64_t ldc,
-                     int64_t rows, int n, int k, bool tf32, const char *what) {
+                     int64_t rows, int n, int k, bool tf32, const char *what,
+                     float beta = 0.f) {
   if (rows == 0 || n == 0) return LNET_OK;
   if (rows > INT32_MAX) return fail(LNET_ERR_UNSUPPORTED, "%s: %lld rows", what, (long long)rows);
   cublasHandle_t h;
@@ -52,7 +53,7 @@ inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t ld
     op_b = CUBLAS_OP_T;
     ld_b = (int)ldbn;
   }
-  const float alpha = 1.f, beta = 0.f;
+  const float alpha = 1.f;
   const cublasStatus_t s = cublasGemmEx(
       h, op_b, CUBLAS_OP_N, n, (int)rows, k, &alpha, Bm, tb, ld_b, A, ta, (int)lda, &beta, C,
       CUDA_R_32F, (int)ldc, tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F,

@@ -6,6 +6,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace lnet {
 
@@ -142,6 +143,189 @@ __global__ void __launch_bounds__(kDwTileThreads) dwconv_tile_kernel(
     }
     orow[t * quads] = y;
   }
+}
+
+// Depthwise conv + SiLU + RMSNorm in one pass (canonical geometry, dim % 4 == 0,
+// dim <= 256) over tiles of kDnSteps steps x all channels of one row: the
+// per-step sum of squares reduced through shared memory (each quad's four
+// squares, strided partial sums, a shuffle tree), xhat = y rs g written
+// directly, the conv output y itself only when `y_out` is given.  With `base`,
+// also writes the writer's residual base y + ls (ds xhat) (the synthesis GEMM
+// adds ls (s W^T) on top).
+//
+// A tile's input steps [t0 - PAD, t0 + kDnSteps + PAD) are one contiguous span
+// of memory, brought into shared memory by one bulk TMA copy on an mbarrier.
+// Persistent blocks walk the tiles with two buffers: the copy of the next tile
+// is in flight while the current one is computed.  Thread 0 waits (bounded) and
+// tells the block through shared memory; on timeout it sets kErrBulk in
+// `status`, waits once more for the copies still in flight, and the block
+// returns.  Shared memory: two input tiles [kDnSteps + 2 PAD][dim],
+// [kDnSteps][dim / 4] squares, [kDnSteps] scales, two mbarriers, a flag.
+constexpr int kDnSteps = 16, kDnThreads = 256, kDnMaxPer = 4, kDnParts = kDnThreads / kDnSteps;
+constexpr int kDnBlocksPerSM = 3;
+constexpr uint32_t kErrBulk = 1u << 8;
+constexpr uint32_t kBulkSpinLimit = 1u << 20;
+__host__ __device__ constexpr size_t dwconv_norm_smem(int rows, int quads) {
+  return 2 * (size_t)rows * quads * 16 + (size_t)kDnSteps * quads * 4 + kDnSteps * 4 + 32;
+}
+template <int TAPS, int DIL>
+__global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel(
+    const float *__restrict__ in, const float *__restrict__ w, const float *__restrict__ bias,
+    const float *__restrict__ in_mask, const float *__restrict__ out_mask,
+    const float *__restrict__ g, const float *__restrict__ ls, const float *__restrict__ ds,
+    float *__restrict__ xhat, float *__restrict__ base, float *__restrict__ y_out, int64_t batch,
+    int64_t steps, int dim, uint32_t *__restrict__ status) {
+  constexpr int PAD = DIL * (TAPS - 1) / 2;
+  constexpr int ROWS = kDnSteps + 2 * PAD;
+  extern __shared__ float4 dn_smem[];
+  const int quads = dim >> 2;
+  const int groups = kDnThreads / quads;
+  float4 *tiles = dn_smem;                                           // [2][ROWS][quads]
+  float *sq = reinterpret_cast<float *>(tiles + 2 * ROWS * quads);   // [kDnSteps][quads]
+  float *rs_s = sq + kDnSteps * quads;                               // [kDnSteps]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(rs_s + kDnSteps);    // [2]
+  volatile uint32_t *fail_flag = reinterpret_cast<uint32_t *>(bars + 2);
+  const int64_t per_row = (steps + kDnSteps - 1) / kDnSteps;
+  const int64_t total = batch * per_row;
+  const int q = threadIdx.x % quads, grp = threadIdx.x / quads;
+  const bool active = grp < groups;
+
+  auto issue = [&](int64_t id, int buf) {
+    const int64_t b = id / per_row, first = (id - b * per_row) * kDnSteps - PAD;
+    const int64_t lo = max((int64_t)0, first), hi = min(steps, first + ROWS);
+    const uint32_t bytes = (uint32_t)((hi - lo) * dim * 4);
+    sm100::mbar_arrive_expect_tx(&bars[buf], bytes);
+    sm100::bulk_load(sm100::smem_u32(tiles + buf * ROWS * quads + (lo - first) * quads),
+                     in + (b * steps + lo) * dim, bytes, &bars[buf]);
+  };
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    sm100::fence_barrier_init();
+    *fail_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && (int64_t)blockIdx.x < total) issue(blockIdx.x, 0);
+
+  // per-thread constants
+  float wk[4][TAPS];
+  float4 bd = make_float4(0.f, 0.f, 0.f, 0.f), gq = bd, lq = bd, dq = bd;
+  if (active) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int k = 0; k < TAPS; ++k) wk[j][k] = w[(4 * q + j) * TAPS + k];
+    bd = reinterpret_cast<const float4 *>(bias)[q];
+    gq = reinterpret_cast<const float4 *>(g)[q];
+    if (base) {
+      lq = reinterpret_cast<const float4 *>(ls)[q];
+      dq = reinterpret_cast<const float4 *>(ds)[q];
+    }
+  }
+
+  int k = 0;
+  for (int64_t id = blockIdx.x; id < total; id += gridDim.x, ++k) {
+    const int cur = k & 1;
+    const int64_t nxt = id + gridDim.x;
+    if (threadIdx.x == 0) {
+      if (nxt < total) {
+        sm100::fence_proxy_async_smem();  // this buffer's last generic writes before the copy
+        issue(nxt, cur ^ 1);
+      }
+      if (!sm100::mbar_wait_bounded(&bars[cur], (k >> 1) & 1, kBulkSpinLimit)) {
+        atomicOr(status, kErrBulk);
+        sm100::mbar_wait_bounded(&bars[cur], (k >> 1) & 1, kBulkSpinLimit);
+        if (nxt < total) sm100::mbar_wait_bounded(&bars[cur ^ 1], ((k + 1) >> 1) & 1, kBulkSpinLimit);
+        *fail_flag = 1;
+      }
+    }
+    __syncthreads();
+    if (*fail_flag) return;
+    const int64_t b = id / per_row, t0 = (id - b * per_row) * kDnSteps, first = t0 - PAD;
+    const int64_t lo = max((int64_t)0, first), hi = min(steps, first + ROWS);
+    float4 *tile = tiles + cur * ROWS * quads;
+    if (lo > first || hi < first + ROWS || in_mask) {
+      for (int i = threadIdx.x; i < ROWS * quads; i += kDnThreads) {
+        const int64_t s = first + i / quads;
+        if (s < lo || s >= hi) {
+          tile[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else if (in_mask) {
+          const float mk = in_mask[b * steps + s];
+          float4 v = tile[i];
+          v.x *= mk; v.y *= mk; v.z *= mk; v.w *= mk;
+          tile[i] = v;
+        }
+      }
+      __syncthreads();
+    }
+    float4 y[kDnMaxPer];
+    if (active) {
+#pragma unroll
+      for (int n = 0; n < kDnMaxPer; ++n) {
+        const int i = grp + n * groups;
+        if (i >= kDnSteps) break;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < TAPS; ++kk) {
+          const float4 v = tile[(i + kk * DIL) * quads + q];
+          a0 = fmaf(wk[0][kk], v.x, a0);
+          a1 = fmaf(wk[1][kk], v.y, a1);
+          a2 = fmaf(wk[2][kk], v.z, a2);
+          a3 = fmaf(wk[3][kk], v.w, a3);
+        }
+        float4 yy = make_float4(silu_f(a0 + bd.x), silu_f(a1 + bd.y), silu_f(a2 + bd.z),
+                                silu_f(a3 + bd.w));
+        if (out_mask) {
+          const float mk = t0 + i < steps ? out_mask[b * steps + t0 + i] : 0.f;
+          yy.x *= mk; yy.y *= mk; yy.z *= mk; yy.w *= mk;
+        }
+        y[n] = yy;
+        sq[i * quads + q] = fmaf(yy.w, yy.w, fmaf(yy.z, yy.z, fmaf(yy.y, yy.y, yy.x * yy.x)));
+      }
+    }
+    __syncthreads();
+    {  // per step: kDnParts threads sum strided quads, then a shuffle tree
+      const int i = threadIdx.x / kDnParts, part = threadIdx.x % kDnParts;
+      float ss = 0.f;
+      for (int qq = part; qq < quads; qq += kDnParts) ss += sq[i * quads + qq];
+#pragma unroll
+      for (int o = kDnParts / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (part == 0) rs_s[i] = rsqrtf(ss / (float)dim + kFp32Eps);
+    }
+    __syncthreads();
+    if (active) {
+      const int64_t tile_off = (b * steps + t0) * quads + q;
+      float4 *xo = reinterpret_cast<float4 *>(xhat) + tile_off;
+      float4 *yo = y_out ? reinterpret_cast<float4 *>(y_out) + tile_off : nullptr;
+      float4 *bo = base ? reinterpret_cast<float4 *>(base) + tile_off : nullptr;
+      const int n_steps = (int)min((int64_t)kDnSteps, steps - t0);
+#pragma unroll
+      for (int n = 0; n < kDnMaxPer; ++n) {
+        const int i = grp + n * groups;
+        if (i >= n_steps) break;
+        const int off = i * quads;
+        const float r = rs_s[i];
+        const float4 yy = y[n];
+        const float4 xh = make_float4(yy.x * r * gq.x, yy.y * r * gq.y, yy.z * r * gq.z,
+                                      yy.w * r * gq.w);
+        xo[off] = xh;
+        if (yo) yo[off] = yy;
+        if (bo)
+          bo[off] = make_float4(yy.x + lq.x * (dq.x * xh.x), yy.y + lq.y * (dq.y * xh.y),
+                                yy.z + lq.z * (dq.z * xh.z), yy.w + lq.w * (dq.w * xh.w));
+      }
+    }
+    __syncthreads();  // the tile, squares and scales are reused next iteration
+  }
+}
+
+// out[d, j] = scale[d] * frame[d, j] for a [dim, n] row-major frame.
+__global__ void scale_rows_kernel(const float *__restrict__ frame, const float *__restrict__ scale,
+                                  float *__restrict__ out, int dim, int n) {
+  const int64_t total = (int64_t)dim * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = scale[i / n] * frame[i];
 }
 
 // ---------------------------------------------------------------- timestamps

@@ -63,6 +63,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint
       : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory (no multicast); both
+// addresses 16-byte aligned, `bytes` a multiple of 16; completes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

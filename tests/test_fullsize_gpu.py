@@ -8,7 +8,8 @@ do not need the oracle to run at that size:
   oracle (tolerances as in test_parity_gpu: 1e-4 fp32, 2e-2 bf16);
 * route agreement: at config 4 the fused route must agree with the general
   route on the same bf16 inputs (2e-2);
-* device status: no bounded wait inside the fused kernels gave up.
+* device status: no bounded wait inside the kernels gave up (fused route at
+  config 4, the general route's bulk input copies at config 2).
 
 Config 1 (Laplace layer) is checked entirely against the oracle.
 """
@@ -105,8 +106,9 @@ def test_config2_full_fp32(cuda_device):
     cfg = bench.CONFIGS["2"]
     model, x = _model_and_input(cfg, cuda_device)
     with torch.no_grad():
-        logits = model(x)
+        logits, status = _forward_with_status(model, x)  # general route: bulk-copy waits
         sub = model(x[[3, 100]].contiguous())
+    assert status == 0
     assert rel_err(sub.cpu().numpy(), logits[[3, 100]].cpu().numpy()) <= 1e-5
     ref = _oracle_rows(cfg, x, [3, 100])
     assert rel_err(logits[[3, 100]].cpu().numpy(), ref) <= 1e-4
