@@ -130,9 +130,8 @@ struct Plan {
   float *stream = nullptr;    // [BT, D]   writer stream
   float *modal = nullptr;     // [BT, D]
   float *ts = nullptr;        // [BT]
-  float *carries = nullptr;   // [B, nchunk, 4M]
+  float *carries = nullptr;   // [B, nchunk, kRecFloats, M] scan records
   float *partial = nullptr;   // moment partials
-  float *edges = nullptr;     // [B, nchunk, 8, 2M] first / last four states of each chunk
   float *wfold = nullptr;     // [D, 2M] drive frame with the ZOH gains folded in
   uint32_t *status = nullptr; // general-route device error bits (zeroed per forward)
   float *a_tab = nullptr;     // [8][M] a_re, a_im (writer, reader), then g_re, g_im (writer, reader)
@@ -157,9 +156,8 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.stream = ar.take<float>((size_t)bt * D);
   pl.modal = ar.take<float>((size_t)bt * D);
   pl.ts = ar.take<float>((size_t)bt);
-  pl.carries = ar.take<float>((size_t)r->batch * n_scan * 4 * M);
+  pl.carries = ar.take<float>((size_t)r->batch * n_scan * kRecFloats * M);
   pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
-  pl.edges = ar.take<float>((size_t)r->batch * n_scan * 16 * M);
   pl.wfold = ar.take<float>((size_t)D * 2 * M);
   pl.status = ar.take<uint32_t>(4);
   pl.a_tab = ar.take<float>((size_t)8 * M);
@@ -263,18 +261,11 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   if (!r->time_delta) {
     if (write_states)
       scan_apply_moments_kernel<true><<<gs, threads, 0, st>>>(
-          pl.drive, a_re, a_im, pl.carries, r->valid_mask, pl.partial, pl.edges, T, M,
-          kScanChunk, n_scan);
+          pl.drive, a_re, a_im, pl.carries, r->valid_mask, pl.partial, T, M, kScanChunk, n_scan);
     else
       scan_apply_moments_kernel<false><<<gs, threads, 0, st>>>(
-          pl.drive, a_re, a_im, pl.carries, r->valid_mask, pl.partial, pl.edges, T, M,
-          kScanChunk, n_scan);
+          pl.drive, a_re, a_im, pl.carries, r->valid_mask, pl.partial, T, M, kScanChunk, n_scan);
     LNET_TRY(after_launch("scan_apply_moments_kernel"));
-    if (n_scan > 1) {
-      moments_edges_kernel<<<grid_for(B * (n_scan - 1) * M), 256, 0, st>>>(
-          pl.partial, pl.edges, r->valid_mask, B, T, M, kScanChunk, n_scan);
-      LNET_TRY(after_launch("moments_edges_kernel"));
-    }
     const dim3 gf((unsigned)cdiv(7 * M, 32), (unsigned)B);
     moments_finalize_kernel<<<gf, 32 * kFinalParts, 0, st>>>(pl.partial, r->valid_mask, moments,
                                                             T, M, n_scan);

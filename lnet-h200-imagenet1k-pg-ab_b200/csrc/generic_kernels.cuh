@@ -491,6 +491,11 @@ __device__ __forceinline__ void step_coeff(const float *raw_decay, const float *
   }
 }
 
+// Per-chunk scan records [B, nchunk, kRecFloats, M]: E re/im (the chunk's map
+// s -> P s + E; the carry pass rewrites E with the chunk's carry-in), P re/im,
+// then the last four zero-start ("local") states of the chunk, re/im each, in
+// step order (slots 4..11).
+constexpr int kRecFloats = 12;
 __global__ void scan_local_kernel(const float *__restrict__ u, const float *__restrict__ raw_decay,
                                   const float *__restrict__ raw_freq,
                                   const float *__restrict__ a_re_tab,
@@ -502,7 +507,9 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
   const int64_t t1 = min(steps, t0 + chunk);
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
     float sr = 0.f, si = 0.f, pr = 1.f, pi = 0.f;
-    for (int64_t t = t0; t < t1; ++t) {
+    float *rec = carries + (b * n_chunks + c) * kRecFloats * modes;
+    const int64_t t_tail = max(t0, t1 - 4);
+    auto step = [&](int64_t t) {
       int64_t tok = b * steps + t;
       float ar, ai;
       step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, tok, m, ar, ai);
@@ -515,8 +522,14 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
       float qi = ai * pr + ar * pi;
       pr = qr;
       pi = qi;
+    };
+    for (int64_t t = t0; t < t_tail; ++t) step(t);
+    for (int64_t t = t_tail; t < t1; ++t) {  // local tail states (slot 0 = fourth-to-last step)
+      step(t);
+      const int slot = (int)(t - (t1 - 4));
+      rec[(4 + 2 * slot) * modes + m] = sr;
+      rec[(5 + 2 * slot) * modes + m] = si;
     }
-    float *rec = carries + ((b * n_chunks + c) * 4) * modes;
     rec[m] = sr;
     rec[modes + m] = si;
     rec[2 * modes + m] = pr;
@@ -524,9 +537,8 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
   }
 }
 
-// Carry pass over the per-chunk records [B, nchunk, {E re, E im, P re, P im}, M]
-// (chunk c maps its entry state s to P s + E): rewrites E with the carry-in of
-// each chunk.  `init` (optional, [B, 2M] re | im): the state before step 0 (a
+// Carry pass over the per-chunk records (kRecFloats; chunk c maps its entry
+// state s to P s + E): rewrites E with the carry-in of each chunk.  `init` (optional, [B, 2M] re | im): the state before step 0 (a
 // time slice's carry-in); zero when NULL.
 //
 // Block (32 modes, kCarryParts ranges of chunks), grid (mode groups, rows).
@@ -545,11 +557,11 @@ __global__ void __launch_bounds__(32 * kCarryParts) scan_carry_kernel(
   const bool on = m < modes;
   const int64_t per = (n_chunks + kCarryParts - 1) / kCarryParts;
   const int64_t c0 = min(n_chunks, part * per), c1 = min(n_chunks, c0 + per);
-  float *base = carries + b * n_chunks * 4 * modes;
+  float *base = carries + b * n_chunks * kRecFloats * modes;
   float Pr = 1.f, Pi = 0.f, Er = 0.f, Ei = 0.f;
   if (on) {
     for (int64_t c = c0; c < c1; ++c) {
-      const float *rec = base + c * 4 * modes;
+      const float *rec = base + c * kRecFloats * modes;
       const float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m],
                   pi = rec[3 * modes + m];
       const float nPr = pr * Pr - pi * Pi, nPi = pi * Pr + pr * Pi;
@@ -579,7 +591,7 @@ __global__ void __launch_bounds__(32 * kCarryParts) scan_carry_kernel(
   if (!on) return;
   float sr = sm[2][part][lane], si = sm[3][part][lane];
   for (int64_t c = c0; c < c1; ++c) {
-    float *rec = base + c * 4 * modes;
+    float *rec = base + c * kRecFloats * modes;
     const float er = rec[m], ei = rec[modes + m], pr = rec[2 * modes + m],
                 pi = rec[3 * modes + m];
     rec[m] = sr;  // carry-in of chunk c
@@ -601,7 +613,7 @@ __global__ void scan_apply_kernel(float *__restrict__ u, const float *__restrict
   const int64_t t0 = c * chunk;
   const int64_t t1 = min(steps, t0 + chunk);
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    const float *rec = carries + ((b * n_chunks + c) * 4) * modes;
+    const float *rec = carries + (b * n_chunks + c) * kRecFloats * modes;
     float sr = rec[m], si = rec[modes + m];
     for (int64_t t = t0; t < t1; ++t) {
       int64_t tok = b * steps + t;
@@ -683,67 +695,94 @@ __global__ void moment_sums_kernel(const float *__restrict__ partial, double *__
 // (chunk, row) block, each thread walks one mode through the chunk from its
 // carry-in, optionally writes the states in place over u (WRITE_STATES; the
 // writer's synthesis GEMM reads them, the reader needs moments only), and sums
-// E and the lag-1/2/4 products (valid-weighted when `valid`) over the pairs
-// that lie inside the chunk, holding the last four states in registers.  The
-// chunk's first and last four states go to `edges` [B, nchunk, 8, 2M] so that
-// moments_edges_kernel adds the pairs that straddle two chunks.  partial
-// layout [B, nchunk, 7M]; products as in moments_partial_kernel.
+// E and the lag-1/2/4 products (valid-weighted when `valid`), holding the last
+// four states in registers.  A chunk c > 0 starts that history from the true
+// states of the previous chunk's last four steps, rebuilt from its record:
+// local tail state + a^(L - k) x its carry-in (L = chunk, every chunk but the
+// last is full), so the pairs straddling the chunk start are counted here.
+// u is read eight steps ahead of the recurrence.  partial layout [B, nchunk,
+// 7M]; products as in moments_partial_kernel.
 template <bool WRITE_STATES>
 __global__ void scan_apply_moments_kernel(float *__restrict__ u, const float *__restrict__ a_re_tab,
                                           const float *__restrict__ a_im_tab,
                                           const float *__restrict__ carries,
                                           const float *__restrict__ valid,
-                                          float *__restrict__ partial, float *__restrict__ edges,
-                                          int64_t steps, int modes, int chunk, int64_t n_chunks) {
+                                          float *__restrict__ partial, int64_t steps, int modes,
+                                          int chunk, int64_t n_chunks) {
   const int64_t c = blockIdx.x, b = blockIdx.y;
   const int64_t t0 = c * chunk;
   const int len = (int)min((int64_t)chunk, steps - t0);
   const int64_t M2 = 2 * modes;
-  float *ed = edges + (b * n_chunks + c) * 8 * M2;
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
     const float ar = a_re_tab[m], ai = a_im_tab[m];
-    const float *rec = carries + ((b * n_chunks + c) * 4) * modes;
+    const float *rec = carries + (b * n_chunks + c) * kRecFloats * modes;
     float sr = rec[m], si = rec[modes + m];
+    // h0 = state at t - 1, h1 at t - 2, h2 at t - 3, h3 at t - 4
     float hr0 = 0.f, hi0 = 0.f, hr1 = 0.f, hi1 = 0.f, hr2 = 0.f, hi2 = 0.f, hr3 = 0.f, hi3 = 0.f;
+    if (c > 0) {
+      const float *prv = carries + (b * n_chunks + c - 1) * kRecFloats * modes;
+      const float cr = prv[m], ci = prv[modes + m];  // carry-in of chunk c - 1
+      float pr = 1.f, pi = 0.f;                       // a^j, j = 1 .. chunk
+      for (int j = 1; j <= chunk - 4; ++j) {
+        const float qr = ar * pr - ai * pi, qi = ai * pr + ar * pi;
+        pr = qr;
+        pi = qi;
+      }
+      float tr[4], ti[4];
+#pragma unroll
+      for (int slot = 0; slot < 4; ++slot) {  // local step chunk - 4 + slot: a^(chunk - 3 + slot)
+        const float qr = ar * pr - ai * pi, qi = ai * pr + ar * pi;
+        pr = qr;
+        pi = qi;
+        const float lr = prv[(4 + 2 * slot) * modes + m], li = prv[(5 + 2 * slot) * modes + m];
+        tr[slot] = lr + (pr * cr - pi * ci);
+        ti[slot] = li + (pi * cr + pr * ci);
+      }
+      hr0 = tr[3]; hi0 = ti[3]; hr1 = tr[2]; hi1 = ti[2];
+      hr2 = tr[1]; hi2 = ti[1]; hr3 = tr[0]; hi3 = ti[0];
+    }
     float e0 = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
     float *row = u + (b * steps + t0) * M2;
     const float *vrow = valid ? valid + b * steps + t0 : nullptr;
-    for (int i = 0; i < len; ++i, row += M2) {
-      const float nr = ar * sr - ai * si + row[m];
-      const float ni = ai * sr + ar * si + row[modes + m];
-      sr = nr;
-      si = ni;
-      if (WRITE_STATES) {
-        row[m] = sr;
-        row[modes + m] = si;
+    const int reach = c > 0 ? 4 : 0;  // history steps available before the chunk
+    for (int i0 = 0; i0 < len; i0 += 8) {
+      float ur[8], ui[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        ur[k] = i0 + k < len ? row[(i0 + k) * M2 + m] : 0.f;
+        ui[k] = i0 + k < len ? row[(i0 + k) * M2 + modes + m] : 0.f;
       }
-      const float wt = vrow ? vrow[i] : 1.f;
-      e0 += (sr * sr + si * si) * wt;
-      if (i >= 1) {
-        const float w = vrow ? wt * vrow[i - 1] : 1.f;
-        c1r += (sr * hr0 + si * hi0) * w;
-        c1i += (si * hr0 - sr * hi0) * w;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k;
+        if (i >= len) break;
+        const float nr = ar * sr - ai * si + ur[k];
+        const float ni = ai * sr + ar * si + ui[k];
+        sr = nr;
+        si = ni;
+        if (WRITE_STATES) {
+          row[i * M2 + m] = sr;
+          row[i * M2 + modes + m] = si;
+        }
+        const float wt = vrow ? vrow[i] : 1.f;
+        e0 += (sr * sr + si * si) * wt;
+        if (i + reach >= 1) {
+          const float w = vrow ? wt * vrow[i - 1] : 1.f;
+          c1r += (sr * hr0 + si * hi0) * w;
+          c1i += (si * hr0 - sr * hi0) * w;
+        }
+        if (i + reach >= 2) {
+          const float w = vrow ? wt * vrow[i - 2] : 1.f;
+          c2r += (sr * hr1 + si * hi1) * w;
+          c2i += (si * hr1 - sr * hi1) * w;
+        }
+        if (i + reach >= 4) {
+          const float w = vrow ? wt * vrow[i - 4] : 1.f;
+          c4r += (sr * hr3 + si * hi3) * w;
+          c4i += (si * hr3 - sr * hi3) * w;
+        }
+        hr3 = hr2; hi3 = hi2; hr2 = hr1; hi2 = hi1; hr1 = hr0; hi1 = hi0; hr0 = sr; hi0 = si;
       }
-      if (i >= 2) {
-        const float w = vrow ? wt * vrow[i - 2] : 1.f;
-        c2r += (sr * hr1 + si * hi1) * w;
-        c2i += (si * hr1 - sr * hi1) * w;
-      }
-      if (i >= 4) {
-        const float w = vrow ? wt * vrow[i - 4] : 1.f;
-        c4r += (sr * hr3 + si * hi3) * w;
-        c4i += (si * hr3 - sr * hi3) * w;
-      }
-      if (i < 4) {
-        ed[i * M2 + m] = sr;
-        ed[i * M2 + modes + m] = si;
-      }
-      if (i >= len - 4) {  // slots 4..7 hold the chunk's last four states
-        const int k = i - len + 8;
-        ed[k * M2 + m] = sr;
-        ed[k * M2 + modes + m] = si;
-      }
-      hr3 = hr2; hi3 = hi2; hr2 = hr1; hi2 = hi1; hr1 = hr0; hi1 = hi0; hr0 = sr; hi0 = si;
     }
     float *out = partial + (b * n_chunks + c) * 7 * modes;
     out[m] = e0;
@@ -756,46 +795,7 @@ __global__ void scan_apply_moments_kernel(float *__restrict__ u, const float *__
   }
 }
 
-// Adds to each chunk's partial the lag pairs that straddle its start: for chunk
-// c >= 1 and lag l, the pairs (t0 + i, t0 + i - l), i < l, whose earlier state
-// is among the previous chunk's last four (`edges` slots 4..7).  One thread per
-// (row, chunk >= 1, mode).
-__global__ void moments_edges_kernel(float *__restrict__ partial, const float *__restrict__ edges,
-                                     const float *__restrict__ valid, int64_t batch,
-                                     int64_t steps, int modes, int chunk, int64_t n_chunks) {
-  const int64_t n = batch * (n_chunks - 1) * modes;
-  const int64_t M2 = 2 * modes;
-  const int lags[3] = {1, 2, 4};
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t bc = idx / modes;
-    const int m = (int)(idx - bc * modes);
-    const int64_t b = bc / (n_chunks - 1);
-    const int64_t c = bc - b * (n_chunks - 1) + 1;
-    const int64_t t0 = c * chunk;
-    const int len = (int)min((int64_t)chunk, steps - t0);
-    const float *cur = edges + (b * n_chunks + c) * 8 * M2;
-    const float *prv = edges + (b * n_chunks + c - 1) * 8 * M2;
-    float *out = partial + (b * n_chunks + c) * 7 * modes;
-#pragma unroll
-    for (int l = 0; l < 3; ++l) {
-      const int lag = lags[l];
-      float re = 0.f, im = 0.f;
-      for (int i = 0; i < lag && i < len; ++i) {
-        const int k = i - lag + 8;  // previous chunk's slot of step t0 + i - lag
-        const float cr = cur[i * M2 + m], ci = cur[i * M2 + modes + m];
-        const float pr = prv[k * M2 + m], pi = prv[k * M2 + modes + m];
-        const float w = valid ? valid[b * steps + t0 + i] * valid[b * steps + t0 + i - lag] : 1.f;
-        re += (cr * pr + ci * pi) * w;
-        im += (ci * pr - cr * pi) * w;
-      }
-      out[(1 + 2 * l) * modes + m] += re;
-      out[(2 + 2 * l) * modes + m] += im;
-    }
-  }
-}
-
-// Normalised moments [B, 7M] from the chunk partials (edge pairs included);
+// Normalised moments [B, 7M] from the chunk partials;
 // valid counts clamped at one (_masked_modal_moments, sum(...).clamp_min(1.0)),
 // else divided by the pair count.  Grid (ceil(7M / 32), B); block = 32 features
 // x kFinalParts chunk ranges summed in double, combined in range order.
