@@ -204,7 +204,7 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   if (r->time_delta) {
     timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
     LNET_TRY(after_launch("timestamps_kernel"));
-    dwconv_physical_kernel<float><<<(unsigned)bt, 128, 0, st>>>(
+    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
         pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, pl.ts, r->valid_mask,
         first_local, T, D, p->conv_kernel, p->conv_dilation);
     return after_launch("dwconv_physical_kernel(stem)");
@@ -279,7 +279,8 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   pt_moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, pl.ts, r->time_delta,
                                                     r->valid_mask, pl.partial, T, M, n_mom);
   LNET_TRY(after_launch("pt_moments_partial_kernel"));
-  pt_moments_finalize_kernel<<<(unsigned)B, threads, 0, st>>>(pl.partial, moments, M, n_mom);
+  pt_moments_finalize_kernel<<<dim3((unsigned)cdiv(M, 32), (unsigned)B), 32 * kPtFinalParts, 0,
+                               st>>>(pl.partial, moments, M, n_mom);
   return after_launch("pt_moments_finalize_kernel");
 }
 
@@ -372,15 +373,19 @@ static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
   return after_launch("residual_kernel");
 }
 
+// `ts_ready`: pl.ts already holds this request's timestamps (whole forward).
 static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
-                          const float *first_stream, Plan &pl, float *moments, cudaStream_t st) {
+                          const float *first_stream, Plan &pl, float *moments, cudaStream_t st,
+                          bool ts_ready = false) {
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const int D = p->model_dim, M = p->modes;
   if (r->time_delta) {
     if (!pl.ts) return fail(LNET_ERR_INVALID_ARGUMENT, "timestamps missing");
-    timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
-    LNET_TRY(after_launch("timestamps_kernel"));
-    dwconv_physical_kernel<float><<<(unsigned)bt, 128, 0, st>>>(
+    if (!ts_ready) {
+      timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
+      LNET_TRY(after_launch("timestamps_kernel"));
+    }
+    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
         first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, pl.ts,
         r->valid_mask, pl.proj, T, D, p->conv_kernel, p->conv_dilation);
     LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
@@ -524,7 +529,7 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
   else
     LNET_TRY(stem_generic<float>(params, req, pl, pl.first_local, st));
   LNET_TRY(writer_generic(params, req, pl.first_local, pl, pl.stream, wm, st));
-  LNET_TRY(reader_generic(params, req, pl.stream, pl, rm, st));
+  LNET_TRY(reader_generic(params, req, pl.stream, pl, rm, st, /*ts_ready=*/true));
   return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st);
 }
 

@@ -965,34 +965,56 @@ __global__ void pt_moments_partial_kernel(const float *__restrict__ s,
   }
 }
 
-__global__ void pt_moments_finalize_kernel(const float *__restrict__ partial,
-                                           float *__restrict__ moments, int modes,
-                                           int64_t n_chunks) {
-  const int64_t b = blockIdx.x;
+// Grid (ceil(M / 32), B); block = 32 modes x kPtFinalParts chunk ranges summed
+// in double and combined in range order (the five per-row scalars likewise).
+constexpr int kPtFinalParts = 8;
+__global__ void __launch_bounds__(32 * kPtFinalParts) pt_moments_finalize_kernel(
+    const float *__restrict__ partial, float *__restrict__ moments, int modes, int64_t n_chunks) {
+  const int64_t b = blockIdx.y;
+  const int lane = threadIdx.x & 31, part = threadIdx.x >> 5;
+  const int m = blockIdx.x * 32 + lane;
   const int rec = 8 * modes + 5;
+  __shared__ double red[kPtFinalParts][8][33];
+  __shared__ double sc_part[kPtFinalParts][5];
   __shared__ double sc[5];
-  if (threadIdx.x < 5) {
-    double a = 0.0;
-    for (int64_t c = 0; c < n_chunks; ++c) a += (double)partial[(b * n_chunks + c) * rec + 8 * modes + threadIdx.x];
-    sc[threadIdx.x] = a;
-  }
-  __syncthreads();
-  const bool use_duration = sc[0] > 0.0;
-  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int64_t c = 0; c < n_chunks; ++c) {
-      const float *p = partial + (b * n_chunks + c) * rec;
+  const int64_t per = (n_chunks + kPtFinalParts - 1) / kPtFinalParts;
+  const int64_t c0 = min(n_chunks, part * per), c1 = min(n_chunks, c0 + per);
+  double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  double sa = 0.0;
+  for (int64_t c = c0; c < c1; ++c) {
+    const float *p = partial + (b * n_chunks + c) * rec;
+    if (m < modes) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] += (double)p[j * modes + m];
     }
-    float *o = moments + b * 7 * modes;
-    float ecount = fmaxf((float)(use_duration ? sc[0] : sc[1]), 1.0f);
-    o[m] = (float)(use_duration ? acc[0] : acc[1]) / ecount;
-    for (int l = 0; l < 3; ++l) {
-      float pc = fmaxf((float)sc[2 + l], 1.0f);
-      o[(1 + 2 * l) * modes + m] = (float)acc[2 + 2 * l] / pc;
-      o[(2 + 2 * l) * modes + m] = (float)acc[3 + 2 * l] / pc;
-    }
+    if (lane < 5) sa += (double)p[8 * modes + lane];
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[part][j][lane] = acc[j];
+  if (lane < 5) sc_part[part][lane] = sa;
+  __syncthreads();
+  if (threadIdx.x < 5) {
+    double a = 0.0;
+    for (int w = 0; w < kPtFinalParts; ++w) a += sc_part[w][threadIdx.x];
+    sc[threadIdx.x] = a;
+  }
+  __syncthreads();
+  if (part != 0 || m >= modes) return;
+  double tot[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    double a = 0.0;
+    for (int w = 0; w < kPtFinalParts; ++w) a += red[w][j][lane];
+    tot[j] = a;
+  }
+  const bool use_duration = sc[0] > 0.0;
+  float *o = moments + b * 7 * modes;
+  const float ecount = fmaxf((float)(use_duration ? sc[0] : sc[1]), 1.0f);
+  o[m] = (float)(use_duration ? tot[0] : tot[1]) / ecount;
+  for (int l = 0; l < 3; ++l) {
+    const float pc = fmaxf((float)sc[2 + l], 1.0f);
+    o[(1 + 2 * l) * modes + m] = (float)tot[2 + 2 * l] / pc;
+    o[(2 + 2 * l) * modes + m] = (float)tot[3 + 2 * l] / pc;
   }
 }
 
