@@ -17,6 +17,8 @@ namespace lnet {
 constexpr int kSlice = 256;  // state entries per CTA (= threads)
 constexpr int kStepTile = 32;
 constexpr int kOutTile = 16;
+static_assert(kSlice == 256 && kStepTile == 32 && kOutTile == 16,
+              "the contraction maps 8 warps x 4 steps and 4 output quads x 8 K parts");
 // Row pitch of the state and residue tiles in shared memory: an odd number of
 // doubles, so the 16 residue rows (and 2 state rows) one warp reads for one
 // entry e fall in distinct banks (a pitch of kSlice put them all in one).
@@ -74,14 +76,48 @@ __global__ void __launch_bounds__(kSlice) laplace_slice_kernel(
       for (int r = 0; r < no; ++r)
         s_res[r * kPitch + j] = live ? residues[(int64_t)(o0 + r) * md + k] : 0.0;
       __syncthreads();
-      for (int q = j; q < nt * no; q += kSlice) {
-        int tt = q / no, r = q - (q / no) * no;
-        const double *sv = s_state + tt * kPitch;
-        const double *rv = s_res + r * kPitch;
-        double acc = 0.0;
-#pragma unroll 8
-        for (int e = 0; e < kSlice; ++e) acc = fma(rv[e], sv[e], acc);
-        out_row[(t0 + tt) * dim + o0 + r] = acc;
+      // Register-blocked contraction: warp w owns steps 4w..4w+3; lane = (output
+      // quad os, K part kp); each thread accumulates a 4 x 4 block over the
+      // entries e = kp mod 8 (consecutive kp read consecutive doubles), then
+      // the 8 K parts are summed by a shuffle tree.  Four FMAs per two shared
+      // loads instead of one per two.
+      {
+        const int warp = j >> 5, lane = j & 31;
+        const int os = lane & 3, kp = lane >> 2;
+        const int tb = warp * 4;
+        double acc[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int v = 0; v < 4; ++v) acc[u][v] = 0.0;
+#pragma unroll 4
+        for (int e = kp; e < kSlice; e += 8) {
+          double sv[4], rv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) sv[u] = s_state[(tb + u) * kPitch + e];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) rv[v] = s_res[(os * 4 + v) * kPitch + e];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[u][v] = fma(rv[v], sv[u], acc[u][v]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1)
+              acc[u][v] += __shfl_xor_sync(0xffffffffu, acc[u][v], o);
+        if (kp == 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int tt = tb + u, r = os * 4 + v;
+              if (tt < nt && r < no) out_row[(t0 + tt) * dim + o0 + r] = acc[u][v];
+            }
+        }
       }
     }
     __syncthreads();
