@@ -133,6 +133,7 @@ struct Plan {
   float *carries = nullptr;   // [B, nchunk, kRecFloats, M] scan records
   float *partial = nullptr;   // moment partials
   float *wfold = nullptr;     // [D, 2M] drive frame with the ZOH gains folded in
+  __nv_bfloat16 *wfold_bf16 = nullptr;  // the same in bf16 (bf16 drive GEMM)
   uint32_t *status = nullptr; // general-route device error bits (zeroed per forward)
   float *a_tab = nullptr;     // [8][M] a_re, a_im (writer, reader), then g_re, g_im (writer, reader)
   __nv_bfloat16 *w_bf16 = nullptr;  // [D, C] stem projection in bf16 (bf16 inputs)
@@ -159,6 +160,7 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.carries = ar.take<float>((size_t)r->batch * n_scan * kRecFloats * M);
   pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
   pl.wfold = ar.take<float>((size_t)D * 2 * M);
+  pl.wfold_bf16 = ar.take<__nv_bfloat16>((size_t)D * 2 * M);
   pl.status = ar.take<uint32_t>(4);
   pl.a_tab = ar.take<float>((size_t)8 * M);
   pl.w_bf16 = ar.take<__nv_bfloat16>((size_t)D * C);
@@ -169,6 +171,22 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
 
 // ---------------------------------------------------------------- general-route stages
 // Stem projection x W^T -> pl.proj (inputs masked first when metadata asks).
+// The shapes the conv + RMSNorm forward (forward_generic_normed) serves:
+// step-indexed requests, canonical K5 d4 conv, 4 | D <= 256.  The slice entry
+// points follow the same arithmetic for them.
+static bool normed_route(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r) {
+  const int D = p->model_dim;
+  return !r->time_delta && p->conv_kernel == 5 && p->conv_dilation == 4 && D % 4 == 0 &&
+         D <= 256;
+}
+
+// bf16 drive operands (xhat and the gain-folded frame in bf16) for bf16
+// requests on that route without an event mask.
+static bool half_drive(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r) {
+  return normed_route(p, r) && r->act_dtype == LNET_BF16 && p->model_dim % 8 == 0 &&
+         !r->observation_mask;
+}
+
 template <typename TX>
 static int stem_projection(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
                            Plan &pl, cudaStream_t st) {
@@ -216,14 +234,15 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 
 // Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
 // `write_states`: leave the states in pl.drive (the writer's synthesis reads them).
-// `normed`: pl.xhat already holds RMSNorm(in).
+// `normed`: pl.xhat already holds RMSNorm(in); `xhat_bf16`: in bf16 (static
+// poles and no event mask only: the drive GEMM then runs bf16 x bf16).
 static int block_scan_moments(const float *in, const float *norm, const float *frame,
                               const float *raw_decay, const float *raw_freq, float *a_re,
                               float *a_im, float *g_re, float *g_im, const float *event_mask,
                               int obs_channels,
                               const lnet_b200_alphabet_request *r, int D, int M, Plan &pl,
                               float *moments, bool write_states, cudaStream_t st,
-                              bool normed = false) {
+                              bool normed = false, bool xhat_bf16 = false) {
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const bool tf32 = r->act_dtype == LNET_BF16;
   if (!normed) {  // else pl.xhat holds RMSNorm(in) already (conv_norm)
@@ -236,11 +255,15 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   }
   if (!r->time_delta && !event_mask) {
     // u = g (x^ W) in one GEMM over the gain-folded frame
-    fold_gain_kernel<<<grid_for((int64_t)D * M), 256, 0, st>>>(frame, g_re, g_im, pl.wfold, D,
-                                                              M);
+    fold_gain_kernel<<<grid_for((int64_t)D * M), 256, 0, st>>>(
+        frame, g_re, g_im, pl.wfold, xhat_bf16 ? pl.wfold_bf16 : nullptr, D, M);
     LNET_TRY(after_launch("fold_gain_kernel"));
-    LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, pl.drive,
-                       2 * M, bt, 2 * M, D, tf32, "cublas(drive)"));
+    if (xhat_bf16)  // bf16 x bf16 tensor-core GEMM, fp32 accumulation
+      LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_16BF, D, pl.wfold_bf16, CUDA_R_16BF, 1, 2 * M,
+                         pl.drive, 2 * M, bt, 2 * M, D, false, "cublas(drive)"));
+    else
+      LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, pl.drive,
+                         2 * M, bt, 2 * M, D, tf32, "cublas(drive)"));
   } else {
     LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
                        bt, 2 * M, D, tf32, "cublas(drive)"));
@@ -289,35 +312,34 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
 static bool conv_norm_ok(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
                          const Plan &pl) {
   auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
-  const int D = p->model_dim;
-  return !r->time_delta && p->conv_kernel == 5 && p->conv_dilation == 4 && D % 4 == 0 &&
-         D <= 256 && al(pl.proj) && al(pl.stream) && al(pl.xhat) && al(p->stem_conv_bias) &&
-         al(p->reader_conv_bias) && al(p->writer_norm) && al(p->reader_norm) &&
-         al(p->writer_layer_scale) && al(p->writer_direct_scale);
+  return normed_route(p, r) && al(pl.proj) && al(pl.stream) && al(pl.xhat) &&
+         al(p->stem_conv_bias) && al(p->reader_conv_bias) && al(p->writer_norm) &&
+         al(p->reader_norm) && al(p->writer_layer_scale) && al(p->writer_direct_scale);
 }
 
-static int conv_norm(const float *in, const float *w, const float *bias, const float *in_mask,
+template <typename TIN, typename TXH>
+static int conv_norm(const TIN *in, const float *w, const float *bias, const float *in_mask,
                      const float *out_mask, const float *g, const float *ls, const float *ds,
-                     float *xhat, float *base, uint32_t *status, int64_t B, int64_t T, int D,
+                     TXH *xhat, float *base, uint32_t *status, int64_t B, int64_t T, int D,
                      cudaStream_t st, const char *what) {
   constexpr int rows = kDnSteps + 16;
   static_assert(kDnParts <= 32 && kDnSteps * kDnParts == kDnThreads, "reduction layout");
-  const size_t smem = dwconv_norm_smem(rows, D / 4);
-  static std::atomic<uint64_t> attr_set{0};  // one bit per device
+  const size_t smem = dwconv_norm_smem(rows, D / 4, sizeof(TIN));
+  auto kernel = dwconv_norm_kernel<5, 4, TIN, TXH>;
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device, per instantiation
   int dev = 0;
   LNET_TRY(cuda_check(cudaGetDevice(&dev), "cudaGetDevice"));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load() & bit)) {
-    LNET_TRY(cuda_check(cudaFuncSetAttribute(dwconv_norm_kernel<5, 4>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)dwconv_norm_smem(rows, 64)),
+    LNET_TRY(cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)dwconv_norm_smem(rows, 64, sizeof(TIN))),
                         "cudaFuncSetAttribute(dwconv_norm_kernel)"));
     attr_set.fetch_or(bit);
   }
   const int64_t tiles = B * cdiv(T, kDnSteps);
   const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)sm_count() * kDnBlocksPerSM);
-  dwconv_norm_kernel<5, 4><<<grid, kDnThreads, smem, st>>>(
-      in, w, bias, in_mask, out_mask, g, ls, ds, xhat, base, nullptr, B, T, D, status);
+  kernel<<<grid, kDnThreads, smem, st>>>(in, w, bias, in_mask, out_mask, g, ls, ds, xhat, base,
+                                         nullptr, B, T, D, status);
   return after_launch(what);
 }
 
@@ -332,27 +354,44 @@ static int forward_generic_normed(const lnet_b200_alphabet_params *p,
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const int D = p->model_dim, M = p->modes;
   const bool tf32 = r->act_dtype == LNET_BF16;
+  // bf16 requests: xhat in bf16 and the drive GEMMs bf16 x bf16 with fp32
+  // accumulation (the operand precision of the fused route); the projection,
+  // the stream and the states stay fp32 (the time-split pieces compute the
+  // same arithmetic: lnet_b200_block_drive rounds xhat the same way).
+  const bool half = half_drive(p, r);
   LNET_TRY(stem_projection<TX>(p, r, pl, st));
-  LNET_TRY(conv_norm(pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
-                     p->writer_norm, p->writer_layer_scale, p->writer_direct_scale, pl.xhat,
-                     pl.stream, pl.status, B, T, D, st, "conv_norm(stem)"));
+  const float *ls = p->writer_layer_scale, *ds = p->writer_direct_scale;
+  __nv_bfloat16 *xh16 = reinterpret_cast<__nv_bfloat16 *>(pl.xhat);
+  if (half)
+    LNET_TRY(conv_norm((const float *)pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr,
+                       r->valid_mask, p->writer_norm, ls, ds, xh16, pl.stream, pl.status, B, T,
+                       D, st, "conv_norm(stem)"));
+  else
+    LNET_TRY(conv_norm((const float *)pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr,
+                       r->valid_mask, p->writer_norm, ls, ds, pl.xhat, pl.stream, pl.status, B,
+                       T, D, st, "conv_norm(stem)"));
   LNET_TRY(block_scan_moments(nullptr, p->writer_norm, p->writer_frame, p->writer_raw_decay,
                               p->writer_raw_frequency, pl.a_tab, pl.a_tab + M,
                               pl.a_tab + 4 * M, pl.a_tab + 5 * M, r->observation_mask,
                               r->obs_channels, r, D, M, pl, wm, /*write_states=*/true, st,
-                              /*normed=*/true));
+                              /*normed=*/true, /*xhat_bf16=*/half));
   scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(
       p->writer_frame, p->writer_layer_scale, pl.wfold, D, 2 * M);
   LNET_TRY(after_launch("scale_rows_kernel"));
   LNET_TRY(gemm_rows(st, pl.drive, CUDA_R_32F, 2 * M, pl.wfold, CUDA_R_32F, 2 * M, 1, pl.stream,
                      D, bt, D, 2 * M, tf32, "cublas(synthesis)", /*beta=*/1.f));
-  LNET_TRY(conv_norm(pl.stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
-                     r->valid_mask, p->reader_norm, nullptr, nullptr, pl.xhat, nullptr,
-                     pl.status, B, T, D, st, "conv_norm(reader)"));
+  if (half)
+    LNET_TRY(conv_norm((const float *)pl.stream, p->reader_conv_weight, p->reader_conv_bias,
+                       r->valid_mask, r->valid_mask, p->reader_norm, nullptr, nullptr, xh16,
+                       nullptr, pl.status, B, T, D, st, "conv_norm(reader)"));
+  else
+    LNET_TRY(conv_norm((const float *)pl.stream, p->reader_conv_weight, p->reader_conv_bias,
+                       r->valid_mask, r->valid_mask, p->reader_norm, nullptr, nullptr, pl.xhat,
+                       nullptr, pl.status, B, T, D, st, "conv_norm(reader)"));
   return block_scan_moments(nullptr, p->reader_norm, p->reader_frame, p->reader_raw_decay,
                             p->reader_raw_frequency, pl.a_tab + 2 * M, pl.a_tab + 3 * M,
                             pl.a_tab + 6 * M, pl.a_tab + 7 * M, nullptr, 1, r, D, M, pl, rm,
-                            /*write_states=*/false, st, /*normed=*/true);
+                            /*write_states=*/false, st, /*normed=*/true, /*xhat_bf16=*/half);
 }
 
 static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -670,12 +709,22 @@ extern "C" int lnet_b200_block_drive(const lnet_b200_alphabet_params *params,
   float *xhat = xhat_out ? xhat_out : pl.xhat;
   rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, bp.norm, xhat, bt, D);
   LNET_TRY(after_launch("rmsnorm_kernel"));
-  // the same arithmetic as the unsplit forward: one GEMM over the gain-folded frame
+  // the same arithmetic as the unsplit forward: one GEMM over the gain-folded
+  // frame, bf16 operands for bf16 requests (half_drive)
   float *a_re = pl.a_tab, *a_im = pl.a_tab + M, *g_re = pl.a_tab + 4 * M, *g_im = pl.a_tab + 5 * M;
   zoh_kernel<<<1, 128, 0, st>>>(bp.decay, bp.freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
   LNET_TRY(after_launch("zoh_kernel"));
-  fold_gain_kernel<<<grid_for((int64_t)D * M), 256, 0, st>>>(bp.frame, g_re, g_im, pl.wfold, D, M);
+  const bool half = half_drive(params, req);
+  fold_gain_kernel<<<grid_for((int64_t)D * M), 256, 0, st>>>(
+      bp.frame, g_re, g_im, pl.wfold, half ? pl.wfold_bf16 : nullptr, D, M);
   LNET_TRY(after_launch("fold_gain_kernel"));
+  if (half) {
+    __nv_bfloat16 *xh16 = reinterpret_cast<__nv_bfloat16 *>(pl.proj);
+    to_bf16_kernel<<<grid_for(bt * D), 256, 0, st>>>(xhat, xh16, bt * D);
+    LNET_TRY(after_launch("to_bf16_kernel"));
+    return gemm_rows(st, xh16, CUDA_R_16BF, D, pl.wfold_bf16, CUDA_R_16BF, 1, 2 * M, u_out, 2 * M,
+                     bt, 2 * M, D, false, "cublas(drive)");
+  }
   return gemm_rows(st, xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, u_out, 2 * M, bt,
                    2 * M, D, req->act_dtype == LNET_BF16, "cublas(drive)");
 }
@@ -744,8 +793,21 @@ extern "C" int lnet_b200_writer_output(const lnet_b200_alphabet_params *params,
   const int64_t bt = req->batch * req->steps;
   if (bt == 0) return LNET_OK;
   const int D = params->model_dim, M = params->modes;
+  const bool tf32 = req->act_dtype == LNET_BF16;
+  if (normed_route(params, req)) {  // the unsplit forward's arithmetic (forward_generic_normed)
+    residual_base_kernel<<<grid_for(bt * D), 256, 0, st>>>(first_local, xhat,
+                                                           params->writer_direct_scale,
+                                                           params->writer_layer_scale, stream_out,
+                                                           bt, D);
+    LNET_TRY(after_launch("residual_base_kernel"));
+    scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(
+        params->writer_frame, params->writer_layer_scale, pl.wfold, D, 2 * M);
+    LNET_TRY(after_launch("scale_rows_kernel"));
+    return gemm_rows(st, states, CUDA_R_32F, 2 * M, pl.wfold, CUDA_R_32F, 2 * M, 1, stream_out,
+                     D, bt, D, 2 * M, tf32, "cublas(synthesis)", /*beta=*/1.f);
+  }
   LNET_TRY(gemm_rows(st, states, CUDA_R_32F, 2 * M, params->writer_frame, CUDA_R_32F, 2 * M, 1,
-                     pl.modal, D, bt, D, 2 * M, req->act_dtype == LNET_BF16, "cublas(synthesis)"));
+                     pl.modal, D, bt, D, 2 * M, tf32, "cublas(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
       first_local, xhat, pl.modal, params->writer_direct_scale, params->writer_layer_scale,
       stream_out, bt, D);

@@ -33,10 +33,11 @@ inline int blas_handle(cublasHandle_t *out) {
 
 // C[rows, n] (row-major, leading dimension ldc) = A[rows, k] (row-major, lda) * B^T + beta C,
 // with element (j, kk) of B at Bm[j * ldbn + kk * ldbk] (one of ldbn, ldbk is 1).
-inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t lda, const void *Bm,
-                     cudaDataType tb, int64_t ldbn, int64_t ldbk, float *C, int64_t ldc,
-                     int64_t rows, int n, int k, bool tf32, const char *what,
-                     float beta = 0.f) {
+// C of type `tc` (fp32, or bf16 for bf16 A and B); accumulation is fp32.
+inline int gemm_rows_t(cudaStream_t st, const void *A, cudaDataType ta, int64_t lda,
+                       const void *Bm, cudaDataType tb, int64_t ldbn, int64_t ldbk, void *C,
+                       cudaDataType tc, int64_t ldc, int64_t rows, int n, int k, bool tf32,
+                       const char *what, float beta = 0.f) {
   if (rows == 0 || n == 0) return LNET_OK;
   if (rows > INT32_MAX) return fail(LNET_ERR_UNSUPPORTED, "%s: %lld rows", what, (long long)rows);
   cublasHandle_t h;
@@ -56,10 +57,18 @@ inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t ld
   const float alpha = 1.f;
   const cublasStatus_t s = cublasGemmEx(
       h, op_b, CUBLAS_OP_N, n, (int)rows, k, &alpha, Bm, tb, ld_b, A, ta, (int)lda, &beta, C,
-      CUDA_R_32F, (int)ldc, tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F,
+      tc, (int)ldc, tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F,
       CUBLAS_GEMM_DEFAULT);
   if (s != CUBLAS_STATUS_SUCCESS) return fail(LNET_ERR_CUDA, "%s: cublasGemmEx status %d", what, (int)s);
   return after_library(what);
+}
+
+inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t lda, const void *Bm,
+                     cudaDataType tb, int64_t ldbn, int64_t ldbk, float *C, int64_t ldc,
+                     int64_t rows, int n, int k, bool tf32, const char *what,
+                     float beta = 0.f) {
+  return gemm_rows_t(st, A, ta, lda, Bm, tb, ldbn, ldbk, C, CUDA_R_32F, ldc, rows, n, k, tf32,
+                     what, beta);
 }
 
 }  // namespace lnet

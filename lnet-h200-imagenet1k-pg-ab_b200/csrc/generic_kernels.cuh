@@ -165,22 +165,44 @@ constexpr int kDnSteps = 16, kDnThreads = 256, kDnMaxPer = 4, kDnParts = kDnThre
 constexpr int kDnBlocksPerSM = 3;
 constexpr uint32_t kErrBulk = 1u << 8;
 constexpr uint32_t kBulkSpinLimit = 1u << 20;
-__host__ __device__ constexpr size_t dwconv_norm_smem(int rows, int quads) {
-  return 2 * (size_t)rows * quads * 16 + (size_t)kDnSteps * quads * 4 + kDnSteps * 4 + 32;
+__host__ __device__ constexpr size_t dwconv_norm_smem(int rows, int quads, int elem_bytes) {
+  return 2 * (size_t)rows * quads * 4 * elem_bytes + (size_t)kDnSteps * quads * 4 +
+         kDnSteps * 4 + 32;
 }
-template <int TAPS, int DIL>
+// Four consecutive channels of T as one shared-memory / global element.
+template <typename T> struct Quad4;
+template <> struct Quad4<float> {
+  using V = float4;
+  __device__ static float4 get(V v) { return v; }
+  __device__ static V put(float4 f) { return f; }
+};
+template <> struct Quad4<__nv_bfloat16> {
+  using V = uint2;
+  __device__ static float4 get(V v) {
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+  }
+  __device__ static V put(float4 f) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y), hi = __floats2bfloat162_rn(f.z, f.w);
+    return make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
+                      *reinterpret_cast<const uint32_t *>(&hi));
+  }
+};
+template <int TAPS, int DIL, typename TIN, typename TXH>
 __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel(
-    const float *__restrict__ in, const float *__restrict__ w, const float *__restrict__ bias,
+    const TIN *__restrict__ in, const float *__restrict__ w, const float *__restrict__ bias,
     const float *__restrict__ in_mask, const float *__restrict__ out_mask,
     const float *__restrict__ g, const float *__restrict__ ls, const float *__restrict__ ds,
-    float *__restrict__ xhat, float *__restrict__ base, float *__restrict__ y_out, int64_t batch,
+    TXH *__restrict__ xhat, float *__restrict__ base, float *__restrict__ y_out, int64_t batch,
     int64_t steps, int dim, uint32_t *__restrict__ status) {
   constexpr int PAD = DIL * (TAPS - 1) / 2;
   constexpr int ROWS = kDnSteps + 2 * PAD;
+  using QI = Quad4<TIN>;
+  using VI = typename QI::V;
   extern __shared__ float4 dn_smem[];
   const int quads = dim >> 2;
   const int groups = kDnThreads / quads;
-  float4 *tiles = dn_smem;                                           // [2][ROWS][quads]
+  VI *tiles = reinterpret_cast<VI *>(dn_smem);                       // [2][ROWS][quads]
   float *sq = reinterpret_cast<float *>(tiles + 2 * ROWS * quads);   // [kDnSteps][quads]
   float *rs_s = sq + kDnSteps * quads;                               // [kDnSteps]
   uint64_t *bars = reinterpret_cast<uint64_t *>(rs_s + kDnSteps);    // [2]
@@ -193,7 +215,7 @@ __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel
   auto issue = [&](int64_t id, int buf) {
     const int64_t b = id / per_row, first = (id - b * per_row) * kDnSteps - PAD;
     const int64_t lo = max((int64_t)0, first), hi = min(steps, first + ROWS);
-    const uint32_t bytes = (uint32_t)((hi - lo) * dim * 4);
+    const uint32_t bytes = (uint32_t)((hi - lo) * dim * (int64_t)sizeof(TIN));
     sm100::mbar_arrive_expect_tx(&bars[buf], bytes);
     sm100::bulk_load(sm100::smem_u32(tiles + buf * ROWS * quads + (lo - first) * quads),
                      in + (b * steps + lo) * dim, bytes, &bars[buf]);
@@ -243,17 +265,17 @@ __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel
     if (*fail_flag) return;
     const int64_t b = id / per_row, t0 = (id - b * per_row) * kDnSteps, first = t0 - PAD;
     const int64_t lo = max((int64_t)0, first), hi = min(steps, first + ROWS);
-    float4 *tile = tiles + cur * ROWS * quads;
+    VI *tile = tiles + cur * ROWS * quads;
     if (lo > first || hi < first + ROWS || in_mask) {
       for (int i = threadIdx.x; i < ROWS * quads; i += kDnThreads) {
         const int64_t s = first + i / quads;
         if (s < lo || s >= hi) {
-          tile[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else if (in_mask) {
+          tile[i] = QI::put(make_float4(0.f, 0.f, 0.f, 0.f));
+        } else if (in_mask) {  // (re-rounded for bf16 input)
           const float mk = in_mask[b * steps + s];
-          float4 v = tile[i];
+          float4 v = QI::get(tile[i]);
           v.x *= mk; v.y *= mk; v.z *= mk; v.w *= mk;
-          tile[i] = v;
+          tile[i] = QI::put(v);
         }
       }
       __syncthreads();
@@ -267,7 +289,7 @@ __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
         for (int kk = 0; kk < TAPS; ++kk) {
-          const float4 v = tile[(i + kk * DIL) * quads + q];
+          const float4 v = QI::get(tile[(i + kk * DIL) * quads + q]);
           a0 = fmaf(wk[0][kk], v.x, a0);
           a1 = fmaf(wk[1][kk], v.y, a1);
           a2 = fmaf(wk[2][kk], v.z, a2);
@@ -295,7 +317,7 @@ __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel
     __syncthreads();
     if (active) {
       const int64_t tile_off = (b * steps + t0) * quads + q;
-      float4 *xo = reinterpret_cast<float4 *>(xhat) + tile_off;
+      auto *xo = reinterpret_cast<typename Quad4<TXH>::V *>(xhat) + tile_off;
       float4 *yo = y_out ? reinterpret_cast<float4 *>(y_out) + tile_off : nullptr;
       float4 *bo = base ? reinterpret_cast<float4 *>(base) + tile_off : nullptr;
       const int n_steps = (int)min((int64_t)kDnSteps, steps - t0);
@@ -308,7 +330,7 @@ __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel
         const float4 yy = y[n];
         const float4 xh = make_float4(yy.x * r * gq.x, yy.y * r * gq.y, yy.z * r * gq.z,
                                       yy.w * r * gq.w);
-        xo[off] = xh;
+        xo[off] = Quad4<TXH>::put(xh);
         if (yo) yo[off] = yy;
         if (bo)
           bo[off] = make_float4(yy.x + lq.x * (dq.x * xh.x), yy.y + lq.y * (dq.y * xh.y),
@@ -316,6 +338,19 @@ __global__ void __launch_bounds__(kDnThreads, kDnBlocksPerSM) dwconv_norm_kernel
       }
     }
     __syncthreads();  // the tile, squares and scales are reused next iteration
+  }
+}
+
+// The writer's residual base v = x + ls (ds xhat) (dwconv_norm_kernel's `base`
+// formula), for the slice entry points.
+__global__ void residual_base_kernel(const float *__restrict__ x, const float *__restrict__ xhat,
+                                     const float *__restrict__ ds, const float *__restrict__ ls,
+                                     float *__restrict__ v, int64_t tokens, int dim) {
+  const int64_t n = tokens * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % dim);
+    v[i] = x[i] + ls[d] * (ds[d] * xhat[i]);
   }
 }
 
@@ -860,9 +895,10 @@ __global__ void __launch_bounds__(32 * kFinalParts) moments_finalize_kernel(
 // Gains folded into the drive frame (static poles, no event mask):
 // out[:, m] = g_re W_re - g_im W_im, out[:, M + m] = g_re W_im + g_im W_re, so
 // the drive GEMM yields u = g (x^ W) directly (frame [D, 2M] row-major).
+// `out_bf16` (optional): the same frame rounded to bf16, for a bf16 drive GEMM.
 __global__ void fold_gain_kernel(const float *__restrict__ frame, const float *__restrict__ g_re,
-                                 const float *__restrict__ g_im, float *__restrict__ out, int dim,
-                                 int modes) {
+                                 const float *__restrict__ g_im, float *__restrict__ out,
+                                 __nv_bfloat16 *__restrict__ out_bf16, int dim, int modes) {
   const int64_t n = (int64_t)dim * modes;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -870,8 +906,13 @@ __global__ void fold_gain_kernel(const float *__restrict__ frame, const float *_
     const int m = (int)(i - d * modes);
     const float *w = frame + d * 2 * modes;
     const float wr = w[m], wi = w[modes + m];
-    out[d * 2 * modes + m] = g_re[m] * wr - g_im[m] * wi;
-    out[d * 2 * modes + modes + m] = g_re[m] * wi + g_im[m] * wr;
+    const float fr = g_re[m] * wr - g_im[m] * wi, fi = g_re[m] * wi + g_im[m] * wr;
+    out[d * 2 * modes + m] = fr;
+    out[d * 2 * modes + modes + m] = fi;
+    if (out_bf16) {
+      out_bf16[d * 2 * modes + m] = __float2bfloat16_rn(fr);
+      out_bf16[d * 2 * modes + modes + m] = __float2bfloat16_rn(fi);
+    }
   }
 }
 
