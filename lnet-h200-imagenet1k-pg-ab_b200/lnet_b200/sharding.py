@@ -40,13 +40,17 @@ def sharded_forward(forward: Callable[..., torch.Tensor], inputs: torch.Tensor, 
                     valid_mask: torch.Tensor | None = None, group=None,
                     gather: bool = True) -> torch.Tensor:
     """Run `forward` on this rank's rows of the full request and, if `gather`,
-    return the logits of the whole batch on every rank (row order preserved)."""
+    return the outputs of the whole batch on every rank (row order preserved):
+    logits [B, K] of a B200Alphabet, or the [B, T, D] output of a
+    B200PoleResidueTemporalMixing, whose rows are independent as well."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
-    local = forward(shard_rows(inputs, world, rank).contiguous(),
-                    time_delta=shard_rows(time_delta, world, rank),
-                    observation_mask=shard_rows(observation_mask, world, rank),
-                    valid_mask=shard_rows(valid_mask, world, rank))
+    meta = {name: shard_rows(t, world, rank) for name, t in
+            (("time_delta", time_delta), ("observation_mask", observation_mask),
+             ("valid_mask", valid_mask)) if t is not None}
+    # metadata keywords only when given, so modules without them (the Laplace
+    # layer's forward(inputs)) shard the same way
+    local = forward(shard_rows(inputs, world, rank).contiguous(), **meta)
     if not gather or world == 1:
         return local
     batch = inputs.shape[0]

@@ -45,6 +45,12 @@ def _stand_in(x, time_delta=None, observation_mask=None, valid_mask=None):
     return y
 
 
+def _seq_stand_in(x):
+    """A per-row sequence map without metadata keywords (the Laplace layer's
+    forward(inputs) -> [B, T, D] shape)."""
+    return torch.cumsum(x, dim=1) * 0.5 + x.sum(dim=-1, keepdim=True)
+
+
 def _worker(rank, world, port, batch, die_rank, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -58,6 +64,8 @@ def _worker(rank, world, port, batch, die_rank, q):
             raise SystemExit(3)  # this rank leaves before the collective
         out = sharded_forward(_stand_in, x, valid_mask=valid)
         ok = torch.allclose(out, _stand_in(x, valid_mask=valid), atol=1e-6)
+        seq = sharded_forward(_seq_stand_in, x)
+        ok = ok and seq.shape == x.shape and torch.allclose(seq, _seq_stand_in(x), atol=1e-6)
         q.put((rank, "ok" if ok else "mismatch"))
     except SystemExit:
         q.put((rank, "left"))
