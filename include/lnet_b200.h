@@ -308,6 +308,50 @@ int lnet_b200_trace_read(unsigned long long *out /* [2][16] */);
  * counters of fused kernels still running on another stream. */
 int lnet_b200_trace_read_async(unsigned long long *out, lnet_stream_t stream);
 
+/* ---------------------------------------------------------------- training
+ * Backward pass of the ALPHABET forward (the reference trains through torch
+ * autograd over its custom ops: register_autograd in
+ * src/lnet/pac_triton_recurrence_op.py:603-684 and the VJP kernels of
+ * src/lnet/pac_triton_parallel_static_recurrence_lag124_training.py:488-876).
+ * Static-pole requests without observation masks (valid masks allowed);
+ * fp32 throughout.  lnet_b200_alphabet_train_forward computes the logits and
+ * keeps every activation the backward needs in `workspace` (sized by
+ * lnet_b200_alphabet_train_workspace_size); lnet_b200_alphabet_backward then
+ * writes dL/dparameter for dL/dlogits [B, K] into caller buffers shaped like
+ * the parameters (frames: the gradient at the materialised [D, 2M] weight).
+ * The workspace must not be reused between the two calls. */
+typedef struct lnet_b200_alphabet_grads {
+  float *stem_projection;
+  float *stem_conv_weight;
+  float *stem_conv_bias;
+  float *writer_norm;
+  float *writer_frame;
+  float *writer_raw_decay;
+  float *writer_raw_frequency;
+  float *writer_direct_scale;
+  float *writer_layer_scale;
+  float *reader_conv_weight;
+  float *reader_conv_bias;
+  float *reader_norm;
+  float *reader_frame;
+  float *reader_raw_decay;
+  float *reader_raw_frequency;
+  float *head_weight;
+  float *head_bias;
+} lnet_b200_alphabet_grads;
+
+int lnet_b200_alphabet_train_workspace_size(const lnet_b200_alphabet_params *params,
+                                            const lnet_b200_alphabet_request *req,
+                                            size_t *bytes);
+int lnet_b200_alphabet_train_forward(const lnet_b200_alphabet_params *params,
+                                     const lnet_b200_alphabet_request *req, void *workspace,
+                                     size_t workspace_bytes, float *logits,
+                                     lnet_stream_t stream);
+int lnet_b200_alphabet_backward(const lnet_b200_alphabet_params *params,
+                                const lnet_b200_alphabet_request *req, void *workspace,
+                                size_t workspace_bytes, const float *dlogits,
+                                const lnet_b200_alphabet_grads *grads, lnet_stream_t stream);
+
 /* Message of the last error on the calling thread ("" if none). */
 const char *lnet_b200_last_error(void);
 

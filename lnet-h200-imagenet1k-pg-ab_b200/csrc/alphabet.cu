@@ -847,3 +847,6 @@ extern "C" int lnet_b200_zoh(const float *raw_decay, const float *raw_frequency,
                                                             steps, a_re, a_im, g_re, g_im);
   return after_launch("zoh_kernel");
 }
+
+// ---------------------------------------------------------------- training path
+#include "train_path.cuh"

@@ -1,0 +1,737 @@
+// Training path of the general route: a forward that keeps its activations
+// and the backward pass (VJP) of every stage, for static-pole requests
+// without observation masks (valid masks allowed), all in fp32.
+//
+// Forward (lnet_b200_alphabet_train_forward): the general-route stages with
+// separate buffers per block, full-fp32 GEMMs.  Kept in the workspace:
+// stem input x32 [BT, C], proj / y1 / xhat1 / modal / v / y2 / xhat2 [BT, D],
+// writer and reader states s1 / s2 [BT, 2M], moments, features, per-mode
+// a / g tables.
+//
+// Backward (lnet_b200_alphabet_backward), the adjoint of each stage in reverse
+// order (the same restatement as the numpy backward oracle):
+//   head GEMMs -> radial-log VJP -> moments VJP (per-step state gradient)
+//   -> reverse chunked scan lambda_t = dS_t + conj(a) lambda_{t+1}, with the
+//      drive gradient de = conj(g) lambda and the per-mode sums for da, dg
+//   -> pole chain rule (ZOH a = exp(p), g = (a - 1) / p, p = -damping + i freq)
+//   -> drive GEMMs (dxhat = de F^T, dF += xhat^T de) -> RMSNorm VJP
+//   -> conv + SiLU VJP (recomputing the pre-activation) -> ...
+// The writer's synthesis + residual adds ls (dv F) to its state gradient and
+// ls (dv^T s1) to its frame gradient.  Every reduction over tokens is
+// deterministic: per-part partial sums then an ordered final sum in double.
+#pragma once
+
+namespace lnet {
+
+// ---------------------------------------------------------------- plan
+struct TrainPlan {
+  float *x32, *proj, *y1, *xh1, *s1, *modal, *v, *y2, *xh2, *s2;
+  float *m1, *m2, *feats, *a_tab;  // a_tab: [8][M] as in the general route
+  // scratch
+  float *carries, *partial, *wfold, *head_partial;
+  float *dS, *dX, *dY, *dV, *rs, *dfeats, *dm, *counts, *colpart, *polepart, *wls;
+};
+
+constexpr int kColParts = 256;  // row parts of a column reduction
+
+static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params *p,
+                       const lnet_b200_alphabet_request *r) {
+  const int64_t B = r->batch, bt = B * r->steps;
+  const int C = p->raw_input_dim, D = p->model_dim, M = p->modes, K = p->output_dim;
+  const int64_t n_scan = cdiv(std::max<int64_t>(r->steps, 1), kScanChunk);
+  auto f = [&](size_t n) { return ar.take<float>(n); };
+  tp.x32 = f((size_t)bt * C);
+  tp.proj = f((size_t)bt * D);
+  tp.y1 = f((size_t)bt * D);
+  tp.xh1 = f((size_t)bt * D);
+  tp.s1 = f((size_t)bt * 2 * M);
+  tp.modal = f((size_t)bt * D);
+  tp.v = f((size_t)bt * D);
+  tp.y2 = f((size_t)bt * D);
+  tp.xh2 = f((size_t)bt * D);
+  tp.s2 = f((size_t)bt * 2 * M);
+  tp.m1 = f((size_t)B * 7 * M);
+  tp.m2 = f((size_t)B * 7 * M);
+  tp.feats = f((size_t)B * 14 * M);
+  tp.a_tab = f((size_t)8 * M);
+  tp.carries = f((size_t)B * n_scan * kRecFloats * M);
+  tp.partial = f((size_t)B * n_scan * 7 * M);
+  tp.wfold = f((size_t)D * 2 * M);
+  tp.head_partial = f(head_partial_floats(B, K));
+  tp.dS = f((size_t)bt * 2 * M);
+  tp.dX = f((size_t)bt * D);
+  tp.dY = f((size_t)bt * D);
+  tp.dV = f((size_t)bt * D);
+  tp.rs = f((size_t)bt);
+  tp.dfeats = f((size_t)B * 14 * M);
+  tp.dm = f((size_t)2 * B * 7 * M);
+  tp.counts = f((size_t)B * 4);
+  tp.colpart = f((size_t)kColParts * 6 * std::max({D, C, 14 * M, K}));
+  tp.polepart = f((size_t)B * n_scan * 4 * M);
+  tp.wls = f((size_t)D * 2 * M);
+}
+
+static bool train_supported(const lnet_b200_alphabet_request *r) {
+  return !r->time_delta && !r->observation_mask;
+}
+
+// A Plan view of the training buffers for block_scan_moments.
+static Plan block_view(const TrainPlan &tp, float *xhat, float *states) {
+  Plan pl;
+  pl.xhat = xhat;
+  pl.drive = states;
+  pl.carries = tp.carries;
+  pl.partial = tp.partial;
+  pl.wfold = tp.wfold;
+  return pl;
+}
+
+// ---------------------------------------------------------------- forward
+template <typename TX>
+static int train_forward_impl(const lnet_b200_alphabet_params *p,
+                              const lnet_b200_alphabet_request *r, TrainPlan &tp, float *logits,
+                              cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const int C = p->raw_input_dim, D = p->model_dim, M = p->modes;
+  lnet_b200_alphabet_request rq = *r;
+  rq.act_dtype = LNET_F32;  // full-fp32 GEMMs
+  mask_inputs_kernel<TX><<<token_grid(bt), token_block(C), 0, st>>>(
+      (const TX *)r->x, nullptr, 1, r->valid_mask, tp.x32, bt, C);
+  LNET_TRY(after_launch("mask_inputs_kernel"));
+  LNET_TRY(gemm_rows(st, tp.x32, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, tp.proj, D,
+                     bt, D, C, false, "cublas(stem)"));
+  LNET_TRY(depthwise_conv(tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
+                          tp.y1, B, T, D, p->conv_kernel, p->conv_dilation, st,
+                          "depthwise_conv(stem)"));
+  Plan pw = block_view(tp, tp.xh1, tp.s1);
+  LNET_TRY(block_scan_moments(tp.y1, p->writer_norm, p->writer_frame, p->writer_raw_decay,
+                              p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
+                              tp.a_tab + 5 * M, nullptr, 1, &rq, D, M, pw, tp.m1,
+                              /*write_states=*/true, st));
+  LNET_TRY(gemm_rows(st, tp.s1, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
+                     tp.modal, D, bt, D, 2 * M, false, "cublas(synthesis)"));
+  residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
+      tp.y1, tp.xh1, tp.modal, p->writer_direct_scale, p->writer_layer_scale, tp.v, bt, D);
+  LNET_TRY(after_launch("residual_kernel"));
+  LNET_TRY(depthwise_conv(tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
+                          r->valid_mask, tp.y2, B, T, D, p->conv_kernel, p->conv_dilation, st,
+                          "depthwise_conv(reader)"));
+  Plan pr = block_view(tp, tp.xh2, tp.s2);
+  LNET_TRY(block_scan_moments(tp.y2, p->reader_norm, p->reader_frame, p->reader_raw_decay,
+                              p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
+                              tp.a_tab + 6 * M, tp.a_tab + 7 * M, nullptr, 1, &rq, D, M, pr,
+                              tp.m2, /*write_states=*/true, st));
+  return head_run(p, B, tp.m1, tp.m2, tp.feats, tp.head_partial, logits, st);
+}
+
+// ---------------------------------------------------------------- backward kernels
+// Column sums of value(row, col) over rows: partial[part][col] over a row
+// range per part, then colsum_final_kernel adds the parts in order (double).
+struct ColPlain {
+  const float *a;
+  int width;
+  __device__ float operator()(int64_t row, int col) const { return a[row * width + col]; }
+};
+struct ColProd {  // a * b (* c[col]) (+ d e[col]) style products of the synthesis scales
+  const float *dv, *modal, *xh, *ls, *ds;
+  int width, which;  // 0: dv (modal + ds xh), 1: dv ls xh
+  __device__ float operator()(int64_t row, int col) const {
+    const int64_t i = row * width + col;
+    return which == 0 ? dv[i] * (modal[i] + ds[col] * xh[i]) : dv[i] * ls[col] * xh[i];
+  }
+};
+struct ColRmsGamma {  // dxhat * y * rs
+  const float *dxh, *y, *rs;
+  int width;
+  __device__ float operator()(int64_t row, int col) const {
+    const int64_t i = row * width + col;
+    return dxh[i] * y[i] * rs[row];
+  }
+};
+struct ColConvW {  // dz[t, d] * xin[t + k dil - pad, d] (masked input), col = d * taps + k
+  const float *dz, *xin, *in_mask;
+  int64_t steps;
+  int dim, taps, dil;
+  __device__ float operator()(int64_t row, int col) const {
+    const int d = col / taps, k = col - (col / taps) * taps;
+    const int64_t b = row / steps, t = row - b * steps;
+    const int64_t s = t + (int64_t)k * dil - (int64_t)dil * (taps - 1) / 2;
+    if (s < 0 || s >= steps) return 0.f;
+    float x = xin[(b * steps + s) * dim + d];
+    if (in_mask) x *= in_mask[b * steps + s];
+    return dz[row * dim + d] * x;
+  }
+};
+
+template <typename F>
+__global__ void colsum_partial_kernel(F f, int64_t rows, int width, float *__restrict__ partial) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int part = blockIdx.y;
+  if (col >= width) return;
+  const int64_t per = (rows + gridDim.y - 1) / gridDim.y;
+  const int64_t r0 = min(rows, part * per), r1 = min(rows, r0 + per);
+  float acc = 0.f;
+  for (int64_t row = r0; row < r1; ++row) acc += f(row, col);
+  partial[(int64_t)part * width + col] = acc;
+}
+
+__global__ void colsum_final_kernel(const float *__restrict__ partial, int parts, int width,
+                                    float *__restrict__ out) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= width) return;
+  double acc = 0.0;
+  for (int q = 0; q < parts; ++q) acc += (double)partial[(int64_t)q * width + col];
+  out[col] = (float)acc;
+}
+
+template <typename F>
+static int colsum(F f, int64_t rows, int width, float *partial, float *out, cudaStream_t st,
+                  const char *what) {
+  const int parts = (int)std::max<int64_t>(1, std::min<int64_t>(kColParts, cdiv(rows, 64)));
+  const dim3 grid((unsigned)cdiv(width, 64), (unsigned)parts);
+  colsum_partial_kernel<F><<<grid, 64, 0, st>>>(f, rows, width, partial);
+  LNET_TRY(after_launch(what));
+  colsum_final_kernel<<<(unsigned)cdiv(width, 64), 64, 0, st>>>(partial, parts, width, out);
+  return after_launch("colsum_final_kernel");
+}
+
+// VJP of radial_feature for both blocks: dm [2][B][7M] from dfeats [B][14M].
+__global__ void radial_backward_kernel(const float *__restrict__ m1, const float *__restrict__ m2,
+                                       const float *__restrict__ dfeats, float *__restrict__ dm,
+                                       int64_t batch, int modes) {
+  const int64_t n = 2 * batch * 7 * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t blk = i / (batch * 7 * modes);
+    const int64_t rem = i - blk * batch * 7 * modes;
+    const int64_t b = rem / (7 * modes);
+    const int j = (int)(rem - b * 7 * modes);
+    const float *mom = (blk == 0 ? m1 : m2) + b * 7 * modes;
+    const float *df = dfeats + b * 14 * modes + blk * 7 * modes;
+    float out;
+    if (j < modes) {
+      const float e = mom[j];
+      out = e > 0.f ? df[j] / (1.0f + e) : 0.f;
+    } else {
+      const int pair = (j - modes) / (2 * modes);
+      const int within = (j - modes) - pair * 2 * modes;
+      const int base = modes + pair * 2 * modes;
+      const int mm = within % modes;
+      const float re = mom[base + mm], im = mom[base + modes + mm];
+      const float gre = df[base + mm], gim = df[base + modes + mm];
+      const float q = re * re + im * im;
+      const float r = sqrtf(fmaxf(q, kFp32Tiny));
+      const float sc = log1pf(r) / r;
+      const float kk = q > kFp32Tiny ? (r / (1.0f + r) - log1pf(r)) / (r * r * r) : 0.f;
+      out = within < modes ? gre * (sc + re * re * kk) + gim * (im * re * kk)
+                           : gre * (re * im * kk) + gim * (sc + im * im * kk);
+    }
+    dm[i] = out;
+  }
+}
+
+// Per-row pair counts for the masked moments: [B][4] = max(sum v, 1) and
+// max(sum v_t v_{t-l}, 1) for l = 1, 2, 4 (T and T - l without a mask).
+__global__ void moment_counts_kernel(const float *__restrict__ valid, int64_t steps,
+                                     float *__restrict__ counts) {
+  const int64_t b = blockIdx.x;
+  const int lags[3] = {1, 2, 4};
+  __shared__ double red[4][32];
+  double c[4] = {0, 0, 0, 0};
+  for (int64_t t = threadIdx.x; t < steps; t += blockDim.x) {
+    const double v = valid[b * steps + t];
+    c[0] += v;
+    for (int l = 0; l < 3; ++l)
+      if (t >= lags[l]) c[1 + l] += v * (double)valid[b * steps + t - lags[l]];
+  }
+  for (int k = 0; k < 4; ++k) {
+    double x = c[k];
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if ((threadIdx.x & 31) == 0) red[k][threadIdx.x >> 5] = x;
+  }
+  __syncthreads();
+  if (threadIdx.x < 4) {
+    double x = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) x += red[threadIdx.x][w];
+    counts[b * 4 + threadIdx.x] = fmaxf((float)x, 1.0f);
+  }
+}
+
+// State gradient of the (masked) moments, one thread per (token, mode):
+// dS_t += 2 s_t dE w_t / c0 + sum_l [pairs with t as the current state and as
+// the earlier one] (w = v_t v_{t-l}).  `accumulate`: add to dS.
+__global__ void moments_backward_kernel(const float *__restrict__ s, const float *__restrict__ dm,
+                                        const float *__restrict__ valid,
+                                        const float *__restrict__ counts,
+                                        float *__restrict__ dS, int64_t batch, int64_t steps,
+                                        int modes, int accumulate) {
+  const int lags[3] = {1, 2, 4};
+  const int64_t n = batch * steps * modes;
+  const int64_t M2 = 2 * modes;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tok = i / modes;
+    const int m = (int)(i - tok * modes);
+    const int64_t b = tok / steps, t = tok - b * steps;
+    const float *g = dm + b * 7 * modes;
+    const float *row = s + tok * M2;
+    const float cr = row[m], ci = row[modes + m];
+    const float vt = valid ? valid[tok] : 1.f;
+    const float c0 = valid ? counts[b * 4] : (float)steps;
+    float gr = 2.f * cr * g[m] * vt / c0, gi = 2.f * ci * g[m] * vt / c0;
+    for (int l = 0; l < 3; ++l) {
+      const int lag = lags[l];
+      if (steps <= lag) continue;
+      const float dr = g[(1 + 2 * l) * modes + m], di = g[(2 + 2 * l) * modes + m];
+      const float cl = valid ? counts[b * 4 + 1 + l] : (float)(steps - lag);
+      if (t >= lag) {  // t as the current state, s_{t-lag} as the earlier one
+        const float *pr_ = row - lag * M2;
+        const float pr = pr_[m], pi = pr_[modes + m];
+        const float w = valid ? vt * valid[tok - lag] : 1.f;
+        gr += (dr * pr - di * pi) * w / cl;
+        gi += (dr * pi + di * pr) * w / cl;
+      }
+      if (t + lag < steps) {  // t as the earlier state of s_{t+lag}
+        const float *nx = row + lag * M2;
+        const float nr = nx[m], ni = nx[modes + m];
+        const float w = valid ? vt * valid[tok + lag] : 1.f;
+        gr += (dr * nr + di * ni) * w / cl;
+        gi += (dr * ni - di * nr) * w / cl;
+      }
+    }
+    float *out = dS + tok * M2;
+    if (accumulate) {
+      out[m] += gr;
+      out[modes + m] += gi;
+    } else {
+      out[m] = gr;
+      out[modes + m] = gi;
+    }
+  }
+}
+
+// Reverse scan, local pass: per (chunk, row), lambda from a zero state after
+// the chunk walked backwards; records at the reversed chunk index so that
+// scan_carry_kernel (forward composition order) yields each chunk's lambda
+// entering from the later steps.  Record: E = local lambda at the chunk start,
+// P = conj(a)^len.
+__global__ void rscan_local_kernel(const float *__restrict__ dS, const float *__restrict__ a_re,
+                                   const float *__restrict__ a_im, float *__restrict__ rec_all,
+                                   int64_t steps, int modes, int chunk, int64_t n_chunks) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * chunk, t1 = min(steps, t0 + chunk);
+  const int64_t M2 = 2 * modes;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    const float ar = a_re[m], ai = a_im[m];
+    float lr = 0.f, li = 0.f, pr = 1.f, pi = 0.f;
+    for (int64_t t = t1 - 1; t >= t0; --t) {
+      const float *row = dS + (b * steps + t) * M2;
+      const float nr = row[m] + ar * lr + ai * li;
+      const float ni = row[modes + m] + ar * li - ai * lr;
+      lr = nr;
+      li = ni;
+      const float qr = ar * pr + ai * pi, qi = ar * pi - ai * pr;  // conj(a) P
+      pr = qr;
+      pi = qi;
+    }
+    float *rec = rec_all + (b * n_chunks + (n_chunks - 1 - c)) * kRecFloats * modes;
+    rec[m] = lr;
+    rec[modes + m] = li;
+    rec[2 * modes + m] = pr;
+    rec[3 * modes + m] = pi;
+  }
+}
+
+// Reverse scan, apply pass: walks each chunk backwards from the lambda that
+// enters it, writes de = conj(g) lambda over dS, and sums per (row, chunk,
+// mode) da = lambda x s_{t-1} and dg = lambda x e_t (real-pair form; e_t =
+// (s_t - a s_{t-1}) / g) into polepart [B, nchunk, 4, M].
+__global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restrict__ s,
+                                   const float *__restrict__ a_re, const float *__restrict__ a_im,
+                                   const float *__restrict__ g_re, const float *__restrict__ g_im,
+                                   const float *__restrict__ rec_all,
+                                   float *__restrict__ polepart, int64_t steps, int modes,
+                                   int chunk, int64_t n_chunks) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * chunk, t1 = min(steps, t0 + chunk);
+  const int64_t M2 = 2 * modes;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    const float ar = a_re[m], ai = a_im[m], gr = g_re[m], gi = g_im[m];
+    const float gden = gr * gr + gi * gi;
+    const float *rec = rec_all + (b * n_chunks + (n_chunks - 1 - c)) * kRecFloats * modes;
+    float lr = rec[m], li = rec[modes + m];  // lambda_{t1}
+    float dar = 0.f, dai = 0.f, dgr = 0.f, dgi = 0.f;
+    for (int64_t t = t1 - 1; t >= t0; --t) {
+      float *row = dS + (b * steps + t) * M2;
+      const float nr = row[m] + ar * lr + ai * li;
+      const float ni = row[modes + m] + ar * li - ai * lr;
+      lr = nr;
+      li = ni;
+      const float *st_ = s + (b * steps + t) * M2;
+      const float sr = st_[m], si = st_[modes + m];
+      float pr = 0.f, pi = 0.f;
+      if (t > 0) {
+        pr = st_[m - M2];
+        pi = st_[modes + m - M2];
+      }
+      dar += lr * pr + li * pi;
+      dai += -lr * pi + li * pr;
+      const float ur = sr - (ar * pr - ai * pi), ui = si - (ai * pr + ar * pi);
+      const float er = (ur * gr + ui * gi) / gden, ei = (ui * gr - ur * gi) / gden;
+      dgr += lr * er + li * ei;
+      dgi += -lr * ei + li * er;
+      row[m] = lr * gr + li * gi;  // de = conj(g) lambda
+      row[modes + m] = -lr * gi + li * gr;
+    }
+    float *pp = polepart + (b * n_chunks + c) * 4 * modes;
+    pp[m] = dar;
+    pp[modes + m] = dai;
+    pp[2 * modes + m] = dgr;
+    pp[3 * modes + m] = dgi;
+  }
+}
+
+// d raw_decay, d raw_frequency from the summed da, dg of every (row, chunk):
+// dL/dp by the Cauchy-Riemann form of a'(p) = a and g'(p) = (a p - (a - 1)) / p^2
+// (dt = 1), then damping = dmin + (dmax - dmin) sigmoid(raw), freq = pi tanh(raw).
+__global__ void pole_backward_kernel(const float *__restrict__ polepart, int64_t parts, int modes,
+                                     const float *__restrict__ raw_decay,
+                                     const float *__restrict__ raw_freq,
+                                     float *__restrict__ d_decay, float *__restrict__ d_freq) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= modes) return;
+  double s[4] = {0, 0, 0, 0};
+  for (int64_t q = 0; q < parts; ++q)
+    for (int k = 0; k < 4; ++k) s[k] += (double)polepart[(q * 4 + k) * modes + m];
+  const double sig = 1.0 / (1.0 + exp(-(double)raw_decay[m]));
+  const double damping = kDampingMin + (kDampingMax - kDampingMin) * sig;
+  const double th = tanh((double)raw_freq[m]);
+  const double pr = -damping, pi = kPi * th;
+  const double ea = exp(pr);
+  const double ar = ea * cos(pi), ai = ea * sin(pi);
+  // fg = (a p - (a - 1)) / p^2
+  const double apr = ar * pr - ai * pi, api = ar * pi + ai * pr;
+  const double nr = apr - (ar - 1.0), ni = api - ai;
+  const double p2r = pr * pr - pi * pi, p2i = 2.0 * pr * pi;
+  const double den = p2r * p2r + p2i * p2i;
+  const double fgr = (nr * p2r + ni * p2i) / den, fgi = (ni * p2r - nr * p2i) / den;
+  const double dpr = s[0] * ar + s[1] * ai + s[2] * fgr + s[3] * fgi;
+  const double dpi = -s[0] * ai + s[1] * ar - s[2] * fgi + s[3] * fgr;
+  d_decay[m] = (float)(-dpr * (kDampingMax - kDampingMin) * sig * (1.0 - sig));
+  d_freq[m] = (float)(dpi * kPi * (1.0 - th * th));
+}
+
+// RMSNorm VJP, one warp per token: dy = rs g dxh - y rs^3 sum(g dxh y) / D
+// (+ add); also stores rs for the gain's column sum.
+__global__ void rms_backward_kernel(const float *__restrict__ y, const float *__restrict__ dxh,
+                                    const float *__restrict__ g, const float *__restrict__ add,
+                                    float *__restrict__ dy, float *__restrict__ rs_out,
+                                    int64_t tokens, int dim) {
+  const int64_t tok = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (tok >= tokens) return;
+  const float *yr = y + tok * dim, *dr = dxh + tok * dim;
+  float ss = 0.f, dot = 0.f;
+  for (int d = lane; d < dim; d += 32) {
+    ss = fmaf(yr[d], yr[d], ss);
+    dot = fmaf(dr[d] * g[d], yr[d], dot);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  }
+  const float rs = rsqrtf(ss / (float)dim + kFp32Eps);
+  const float k = rs * rs * rs * dot / (float)dim;
+  for (int d = lane; d < dim; d += 32) {
+    float v = rs * g[d] * dr[d] - yr[d] * k;
+    if (add) v += add[tok * dim + d];
+    dy[tok * dim + d] = v;
+  }
+  if (lane == 0) rs_out[tok] = rs;
+}
+
+// Conv + SiLU VJP, pre-activation gradient: dz = dy * out_mask * silu'(z),
+// z = bias + sum_k w_k in[t + k dil - pad] * in_mask (recomputed).
+__global__ void conv_dz_kernel(const float *__restrict__ in, const float *__restrict__ w,
+                               const float *__restrict__ bias, const float *__restrict__ in_mask,
+                               const float *__restrict__ out_mask, const float *__restrict__ dy,
+                               float *__restrict__ dz, int64_t batch, int64_t steps, int dim,
+                               int taps, int dil) {
+  const int64_t n = batch * steps * dim;
+  const int pad = dil * (taps - 1) / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tok = i / dim;
+    const int d = (int)(i - tok * dim);
+    const int64_t b = tok / steps, t = tok - b * steps;
+    float z = 0.f;
+    for (int k = 0; k < taps; ++k) {
+      const int64_t s = t + (int64_t)k * dil - pad;
+      if (s < 0 || s >= steps) continue;
+      float v = in[(b * steps + s) * dim + d];
+      if (in_mask) v *= in_mask[b * steps + s];
+      z = fmaf(w[d * taps + k], v, z);
+    }
+    z += bias[d];
+    const float sg = 1.0f / (1.0f + expf(-z));
+    float gz = dy[i] * sg * (1.0f + z * (1.0f - sg));
+    if (out_mask) gz *= out_mask[tok];
+    dz[i] = gz;
+  }
+}
+
+// Input gradient of the depthwise conv: dx[s] = in_mask[s] sum_k w_k dz[s - k dil + pad].
+__global__ void conv_dx_kernel(const float *__restrict__ dz, const float *__restrict__ w,
+                               const float *__restrict__ in_mask, float *__restrict__ dx,
+                               int64_t batch, int64_t steps, int dim, int taps, int dil) {
+  const int64_t n = batch * steps * dim;
+  const int pad = dil * (taps - 1) / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tok = i / dim;
+    const int d = (int)(i - tok * dim);
+    const int64_t b = tok / steps, s = tok - b * steps;
+    float acc = 0.f;
+    for (int k = 0; k < taps; ++k) {
+      const int64_t t = s - (int64_t)k * dil + pad;
+      if (t < 0 || t >= steps) continue;
+      acc = fmaf(w[d * taps + k], dz[(b * steps + t) * dim + d], acc);
+    }
+    if (in_mask) acc *= in_mask[tok];
+    dx[i] = acc;
+  }
+}
+
+// dxh_res = dv ls ds (the residual's xhat path).
+__global__ void residual_dxh_kernel(const float *__restrict__ dv, const float *__restrict__ ls,
+                                    const float *__restrict__ ds, float *__restrict__ dxh,
+                                    int64_t tokens, int dim) {
+  const int64_t n = tokens * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % dim);
+    dxh[i] = dv[i] * ls[d] * ds[d];
+  }
+}
+
+// ---------------------------------------------------------------- backward orchestration
+// C[n1, n2] (row-major) = sum_r A[r, n1] Bm[r, n2] (+ beta C): the weight
+// gradients (A [R, n1], Bm [R, n2] row-major).
+static int gemm_wgrad(cudaStream_t st, const float *A, int64_t n1, const float *Bm, int64_t n2,
+                      float *C, int64_t R, float beta, const char *what) {
+  if (R == 0 || n1 == 0 || n2 == 0) return LNET_OK;
+  if (R > INT32_MAX) return fail(LNET_ERR_UNSUPPORTED, "%s: %lld rows", what, (long long)R);
+  cublasHandle_t h;
+  LNET_TRY(blas_handle(&h));
+  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS)
+    return fail(LNET_ERR_CUDA, "cublasSetStream failed");
+  // column-major: C^T [n2 x n1] = Bm_cm [n2 x R] * (A_cm [n1 x R])^T
+  const float alpha = 1.f;
+  const cublasStatus_t s = cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_T, (int)n2, (int)n1, (int)R,
+                                        &alpha, Bm, CUDA_R_32F, (int)n2, A, CUDA_R_32F, (int)n1,
+                                        &beta, C, CUDA_R_32F, (int)n2, CUBLAS_COMPUTE_32F,
+                                        CUBLAS_GEMM_DEFAULT);
+  if (s != CUBLAS_STATUS_SUCCESS) return fail(LNET_ERR_CUDA, "%s: cublasGemmEx status %d", what, (int)s);
+  return after_library(what);
+}
+
+// One block's backward from its state gradient in tp.dS (already holding the
+// moments' and, for the writer, the synthesis' contributions): reverse scan,
+// pole gradients, drive GEMMs.  dxh receives de F^T (+ beta dxh); dframe
+// receives xhat^T de (+ beta_frame dframe).
+static int block_backward(const TrainPlan &tp, const float *states, const float *xh,
+                          const float *frame, const float *raw_decay, const float *raw_freq,
+                          const float *a_re, const float *a_im, const float *g_re,
+                          const float *g_im, float *dxh, float dxh_beta, float *dframe,
+                          float frame_beta, float *d_decay, float *d_freq, int64_t B, int64_t T,
+                          int D, int M, cudaStream_t st) {
+  const int64_t n_scan = cdiv(T, kScanChunk);
+  const int threads = std::min(128, (int)cdiv(M, 32) * 32);
+  const dim3 gs((unsigned)n_scan, (unsigned)B);
+  rscan_local_kernel<<<gs, threads, 0, st>>>(tp.dS, a_re, a_im, tp.carries, T, M, kScanChunk,
+                                             n_scan);
+  LNET_TRY(after_launch("rscan_local_kernel"));
+  scan_carry_kernel<<<dim3((unsigned)cdiv(M, 32), (unsigned)B), 32 * kCarryParts, 0, st>>>(
+      tp.carries, B, M, n_scan, nullptr);
+  LNET_TRY(after_launch("scan_carry_kernel"));
+  rscan_apply_kernel<<<gs, threads, 0, st>>>(tp.dS, states, a_re, a_im, g_re, g_im, tp.carries,
+                                             tp.polepart, T, M, kScanChunk, n_scan);
+  LNET_TRY(after_launch("rscan_apply_kernel"));
+  pole_backward_kernel<<<(unsigned)cdiv(M, 64), 64, 0, st>>>(tp.polepart, B * n_scan, M,
+                                                             raw_decay, raw_freq, d_decay,
+                                                             d_freq);
+  LNET_TRY(after_launch("pole_backward_kernel"));
+  const int64_t bt = B * T;
+  LNET_TRY(gemm_rows(st, tp.dS, CUDA_R_32F, 2 * M, frame, CUDA_R_32F, 2 * M, 1, dxh, D, bt, D,
+                     2 * M, false, "cublas(d xhat)", dxh_beta));
+  return gemm_wgrad(st, xh, D, tp.dS, 2 * M, dframe, bt, frame_beta, "cublas(d frame)");
+}
+
+static int conv_backward(const TrainPlan &tp, const float *in, const float *w, const float *bias,
+                         const float *in_mask, const float *out_mask, const float *dy, float *dx,
+                         float *dw, float *db, int64_t B, int64_t T, int D, int taps, int dil,
+                         cudaStream_t st) {
+  const int64_t bt = B * T;
+  float *dz = tp.dY;  // dy is consumed element-wise in place
+  conv_dz_kernel<<<grid_for(bt * D), 256, 0, st>>>(in, w, bias, in_mask, out_mask, dy, dz, B, T,
+                                                   D, taps, dil);
+  LNET_TRY(after_launch("conv_dz_kernel"));
+  conv_dx_kernel<<<grid_for(bt * D), 256, 0, st>>>(dz, w, in_mask, dx, B, T, D, taps, dil);
+  LNET_TRY(after_launch("conv_dx_kernel"));
+  LNET_TRY(colsum(ColConvW{dz, in, in_mask, T, D, taps, dil}, bt, D * taps, tp.colpart, dw, st,
+                  "colsum(conv w)"));
+  return colsum(ColPlain{dz, D}, bt, D, tp.colpart, db, st, "colsum(conv b)");
+}
+
+static int train_backward_impl(const lnet_b200_alphabet_params *p,
+                               const lnet_b200_alphabet_request *r, TrainPlan &tp,
+                               const float *dlogits, const lnet_b200_alphabet_grads *gd,
+                               cudaStream_t st) {
+  const int64_t B = r->batch, T = r->steps, bt = B * T;
+  const int C = p->raw_input_dim, D = p->model_dim, M = p->modes, K = p->output_dim;
+  const int taps = p->conv_kernel, dil = p->conv_dilation;
+  const float *valid = r->valid_mask;
+  // head
+  LNET_TRY(gemm_wgrad(st, dlogits, K, tp.feats, 14 * M, gd->head_weight, B, 0.f,
+                      "cublas(d head)"));
+  LNET_TRY(colsum(ColPlain{dlogits, K}, B, K, tp.colpart, gd->head_bias, st, "colsum(head b)"));
+  LNET_TRY(gemm_rows(st, dlogits, CUDA_R_32F, K, p->head_weight, CUDA_R_32F, 1, 14 * M, tp.dfeats,
+                     14 * M, B, 14 * M, K, false, "cublas(d feats)"));
+  radial_backward_kernel<<<grid_for(2 * B * 7 * M), 256, 0, st>>>(tp.m1, tp.m2, tp.dfeats, tp.dm,
+                                                                  B, M);
+  LNET_TRY(after_launch("radial_backward_kernel"));
+  if (valid) {
+    moment_counts_kernel<<<(unsigned)B, 256, 0, st>>>(valid, T, tp.counts);
+    LNET_TRY(after_launch("moment_counts_kernel"));
+  }
+  const float *dm1 = tp.dm, *dm2 = tp.dm + B * 7 * M;
+  // reader block
+  moments_backward_kernel<<<grid_for(bt * M), 256, 0, st>>>(tp.s2, dm2, valid, tp.counts, tp.dS,
+                                                            B, T, M, 0);
+  LNET_TRY(after_launch("moments_backward_kernel"));
+  LNET_TRY(block_backward(tp, tp.s2, tp.xh2, p->reader_frame, p->reader_raw_decay,
+                          p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
+                          tp.a_tab + 6 * M, tp.a_tab + 7 * M, tp.dX, 0.f, gd->reader_frame, 0.f,
+                          gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, st));
+  rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y2, tp.dX, p->reader_norm,
+                                                             nullptr, tp.dY, tp.rs, bt, D);
+  LNET_TRY(after_launch("rms_backward_kernel"));
+  LNET_TRY(colsum(ColRmsGamma{tp.dX, tp.y2, tp.rs, D}, bt, D, tp.colpart, gd->reader_norm, st,
+                  "colsum(reader norm)"));
+  // reader conv: input v (masked), dv out
+  LNET_TRY(conv_backward(tp, tp.v, p->reader_conv_weight, p->reader_conv_bias, valid, valid,
+                         tp.dY, tp.dV, gd->reader_conv_weight, gd->reader_conv_bias, B, T, D,
+                         taps, dil, st));
+  // writer synthesis + residual: v = y1 + ls (s1 F^T + ds xh1)
+  const float *ls = p->writer_layer_scale, *ds = p->writer_direct_scale;
+  LNET_TRY(colsum(ColProd{tp.dV, tp.modal, tp.xh1, ls, ds, D, 0}, bt, D, tp.colpart,
+                  gd->writer_layer_scale, st, "colsum(layer scale)"));
+  LNET_TRY(colsum(ColProd{tp.dV, tp.modal, tp.xh1, ls, ds, D, 1}, bt, D, tp.colpart,
+                  gd->writer_direct_scale, st, "colsum(direct scale)"));
+  scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(p->writer_frame, ls, tp.wls, D,
+                                                                   2 * M);
+  LNET_TRY(after_launch("scale_rows_kernel"));
+  // dS1 = dv (ls F) + moments VJP
+  LNET_TRY(gemm_rows(st, tp.dV, CUDA_R_32F, D, tp.wls, CUDA_R_32F, 1, 2 * M, tp.dS, 2 * M, bt,
+                     2 * M, D, false, "cublas(d states synth)"));
+  moments_backward_kernel<<<grid_for(bt * M), 256, 0, st>>>(tp.s1, dm1, valid, tp.counts, tp.dS,
+                                                            B, T, M, 1);
+  LNET_TRY(after_launch("moments_backward_kernel"));
+  // dF1 = ls (dv^T s1) (+ the drive part below)
+  LNET_TRY(gemm_wgrad(st, tp.dV, D, tp.s1, 2 * M, gd->writer_frame, bt, 0.f,
+                      "cublas(d frame synth)"));
+  scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(gd->writer_frame, ls,
+                                                                   gd->writer_frame, D, 2 * M);
+  LNET_TRY(after_launch("scale_rows_kernel"));
+  residual_dxh_kernel<<<grid_for(bt * D), 256, 0, st>>>(tp.dV, ls, ds, tp.dX, bt, D);
+  LNET_TRY(after_launch("residual_dxh_kernel"));
+  LNET_TRY(block_backward(tp, tp.s1, tp.xh1, p->writer_frame, p->writer_raw_decay,
+                          p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
+                          tp.a_tab + 5 * M, tp.dX, 1.f, gd->writer_frame, 1.f,
+                          gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, st));
+  // writer RMSNorm: dy1 = rms VJP + dv (residual identity)
+  rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y1, tp.dX, p->writer_norm, tp.dV,
+                                                             tp.dY, tp.rs, bt, D);
+  LNET_TRY(after_launch("rms_backward_kernel"));
+  LNET_TRY(colsum(ColRmsGamma{tp.dX, tp.y1, tp.rs, D}, bt, D, tp.colpart, gd->writer_norm, st,
+                  "colsum(writer norm)"));
+  // stem conv: input proj (no input mask), output mask valid; dproj -> tp.dV
+  LNET_TRY(conv_backward(tp, tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, valid,
+                         tp.dY, tp.dV, gd->stem_conv_weight, gd->stem_conv_bias, B, T, D, taps,
+                         dil, st));
+  return gemm_wgrad(st, tp.dV, D, tp.x32, C, gd->stem_projection, bt, 0.f,
+                    "cublas(d projection)");
+}
+
+static int train_entry(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
+                       void *ws, size_t ws_bytes, TrainPlan &tp) {
+  LNET_TRY(check_params(p));
+  LNET_TRY(check_request(p, r));
+  if (!train_supported(r))
+    return fail(LNET_ERR_UNSUPPORTED,
+                "training path: time_delta and observation_mask are not supported");
+  Arena ar(ws, ws_bytes);
+  plan_train(ar, tp, p, r);
+  if (!ws || !ar.ok())
+    return fail(LNET_ERR_WORKSPACE, "training workspace of %zu bytes < required %zu", ws_bytes,
+                ar.used);
+  return LNET_OK;
+}
+
+}  // namespace lnet
+
+extern "C" int lnet_b200_alphabet_train_workspace_size(const lnet_b200_alphabet_params *params,
+                                                       const lnet_b200_alphabet_request *req,
+                                                       size_t *bytes) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (!bytes) return fail(LNET_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+  Arena a(nullptr, 0);
+  TrainPlan tp;
+  plan_train(a, tp, params, req);
+  *bytes = a.used;
+  return LNET_OK;
+}
+
+extern "C" int lnet_b200_alphabet_train_forward(const lnet_b200_alphabet_params *params,
+                                                const lnet_b200_alphabet_request *req,
+                                                void *workspace, size_t workspace_bytes,
+                                                float *logits, lnet_stream_t stream) {
+  reset_launches();
+  auto st = (cudaStream_t)stream;
+  begin_entry(st);
+  TrainPlan tp;
+  LNET_TRY(train_entry(params, req, workspace, workspace_bytes, tp));
+  if (!logits) return fail(LNET_ERR_INVALID_ARGUMENT, "logits must not be NULL");
+  if (req->batch == 0 || req->steps == 0) return LNET_OK;
+  if (req->x_dtype == LNET_BF16)
+    return train_forward_impl<__nv_bfloat16>(params, req, tp, logits, st);
+  return train_forward_impl<float>(params, req, tp, logits, st);
+}
+
+extern "C" int lnet_b200_alphabet_backward(const lnet_b200_alphabet_params *params,
+                                           const lnet_b200_alphabet_request *req,
+                                           void *workspace, size_t workspace_bytes,
+                                           const float *dlogits,
+                                           const lnet_b200_alphabet_grads *grads,
+                                           lnet_stream_t stream) {
+  reset_launches();
+  auto st = (cudaStream_t)stream;
+  begin_entry(st);
+  TrainPlan tp;
+  LNET_TRY(train_entry(params, req, workspace, workspace_bytes, tp));
+  if (!dlogits || !grads) return fail(LNET_ERR_INVALID_ARGUMENT, "NULL dlogits or grads");
+  const float *const need[] = {grads->stem_projection, grads->stem_conv_weight,
+                               grads->stem_conv_bias, grads->writer_norm, grads->writer_frame,
+                               grads->writer_raw_decay, grads->writer_raw_frequency,
+                               grads->writer_direct_scale, grads->writer_layer_scale,
+                               grads->reader_conv_weight, grads->reader_conv_bias,
+                               grads->reader_norm, grads->reader_frame, grads->reader_raw_decay,
+                               grads->reader_raw_frequency, grads->head_weight, grads->head_bias};
+  for (const float *q : need)
+    if (!q) return fail(LNET_ERR_INVALID_ARGUMENT, "a gradient pointer is NULL");
+  if (req->batch == 0 || req->steps == 0) return LNET_OK;
+  return train_backward_impl(params, req, tp, dlogits, grads, st);
+}

@@ -73,8 +73,28 @@ class AlphabetRequest(ctypes.Structure):
     ]
 
 
+class AlphabetGrads(ctypes.Structure):
+    """Output pointers of lnet_b200_alphabet_backward, in PARAM_POINTER_FIELDS order."""
+    _fields_ = [(name, _c_p) for name in PARAM_POINTER_FIELDS]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
+    "lnet_b200_alphabet_train_workspace_size": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest),
+         ctypes.POINTER(ctypes.c_size_t)],
+    ),
+    "lnet_b200_alphabet_train_forward": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
+         _c_p, _c_p],
+    ),
+    "lnet_b200_alphabet_backward": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
+         _c_p, ctypes.POINTER(AlphabetGrads), _c_p],
+    ),
     "lnet_b200_alphabet_workspace_size": (
         ctypes.c_int,
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest),

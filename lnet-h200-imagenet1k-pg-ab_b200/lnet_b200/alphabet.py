@@ -314,7 +314,17 @@ class B200Alphabet(nn.Module):
         if inputs.dtype not in (torch.float32, torch.bfloat16):
             raise TypeError(f"inputs must be float32 or bfloat16, got {inputs.dtype}")
         if self.training and torch.is_grad_enabled():
-            raise RuntimeError("B200Alphabet is an inference module; call .eval() first")
+            # training: the fp32 forward that keeps its activations, with the
+            # B200 backward (lnet_b200.training); static poles, no observation mask
+            if time_delta is not None or observation_mask is not None:
+                raise NotImplementedError(
+                    "training supports valid_mask only (no time_delta / observation_mask)")
+            if return_moments:
+                raise NotImplementedError("return_moments is an inference option")
+            _, _, valid = self._prepare_metadata(inputs, None, None, valid_mask)
+            from .training import train_forward
+
+            return train_forward(self, inputs, valid).to(self.head.classifier.weight.dtype)
         delta, obs, valid = self._prepare_metadata(inputs, time_delta, observation_mask,
                                                    valid_mask)
         x = inputs.contiguous()

@@ -1,0 +1,114 @@
+"""Backward pass on the GPU against gradients from the reference's autograd.
+
+``tests/golden/grad_*.npz`` hold dL/dparameter of ``L = sum(logits * dlogits)``
+from the reference ``lnet.Alphabet`` in float64 (evaluated at the stored float32
+parameters; ``tests/golden/make_grad_golden.py``).  ``B200Alphabet`` in
+training mode runs ``lnet_b200_alphabet_train_forward`` and, on
+``loss.backward()``, ``lnet_b200_alphabet_backward`` (fp32).  Bounds: logits
+1e-5 relative, every parameter gradient 2e-4 relative (normwise per tensor;
+fp32 against float64 over sequences up to 300 steps).  Also: the training
+forward equals the inference forward; the oracle VJP agrees at a size the
+goldens do not cover; the unsupported metadata raises.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import golden_params, load_golden, rel_err
+
+from lnet_b200 import AlphabetConfig, B200Alphabet
+from oracle import alphabet_grad_oracle as G
+
+pytestmark = pytest.mark.gpu
+
+CASES = ["grad_plain", "grad_real_poles", "grad_long", "grad_valid"]
+
+
+def _model(z, device):
+    b, t, cin, d, m, k = (int(v) for v in z["meta.shape"])
+    model = B200Alphabet(AlphabetConfig(cin, d, m, k), k)
+    model.load_effective_parameters({k2: torch.from_numpy(v) for k2, v in golden_params(z).items()})
+    return model.to(device).train()
+
+
+def _grads(model, x, dlogits, valid=None):
+    model.zero_grad(set_to_none=True)
+    logits = model(x, valid_mask=valid)
+    (logits * dlogits).sum().backward()
+    out = {name: p.grad for name, p in model.named_parameters() if p.grad is not None}
+    return logits.detach(), out
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_backward_matches_reference_autograd(name, cuda_device):
+    z = load_golden(name)
+    model = _model(z, cuda_device)
+    x = torch.from_numpy(z["in.x"]).to(cuda_device)
+    dl = torch.from_numpy(z["in.dlogits"]).to(cuda_device)
+    valid = torch.from_numpy(z["in.valid_mask"]).to(cuda_device) if "in.valid_mask" in z else None
+    logits, grads = _grads(model, x, dl, valid)
+    assert rel_err(logits.cpu().numpy(), z["out.logits"]) <= 1e-5
+    checked = 0
+    for key in z:
+        if not key.startswith("g."):
+            continue
+        pname = key[2:]
+        got = grads[pname].cpu().numpy().reshape(z[key].shape)
+        assert rel_err(got, z[key]) <= 2e-4, (pname, rel_err(got, z[key]))
+        checked += 1
+    assert checked == 17
+
+
+def test_training_forward_equals_inference(cuda_device):
+    z = load_golden("grad_long")
+    model = _model(z, cuda_device)
+    x = torch.from_numpy(z["in.x"]).to(cuda_device)
+    train_logits = model(x).detach()
+    with torch.no_grad():
+        model.eval()
+        infer = model(x)
+    assert rel_err(train_logits.cpu().numpy(), infer.cpu().numpy()) <= 1e-5
+
+
+def test_backward_larger_case_against_oracle(cuda_device):
+    """Several scan chunks per row, D = 32, M = 16, a valid mask with ragged
+    lengths: the CUDA backward against the float64 oracle VJP."""
+    g = torch.Generator().manual_seed(21)
+    b, t, cin, d, m, k = 3, 517, 8, 32, 16, 6
+    model = B200Alphabet(AlphabetConfig(cin, d, m, k), k)
+    with torch.no_grad():
+        for blk in (model.forward_block, model.backward_block):
+            blk.raw_decay.copy_(torch.randn(m, generator=g) * 2.0)
+            blk.raw_frequency.copy_(torch.randn(m, generator=g) * 0.8)
+            blk.norm.weight.copy_(1.0 + 0.2 * torch.randn(d, generator=g))
+        model.forward_block.direct_scale.copy_(0.5 * torch.randn(d, generator=g))
+        model.forward_block.layer_scale.copy_(0.5 * torch.randn(d, generator=g))
+        for conv in (model.stem.local, model.second_local):
+            conv.weight.copy_(torch.randn(conv.weight.shape, generator=g) / 5 ** 0.5)
+            conv.bias.copy_(0.1 * torch.randn(d, generator=g))
+    for blk in (model.forward_block, model.backward_block):  # plain frames: comparable grads
+        B200Alphabet._set_frame(blk, blk.frame_matrix().detach())
+    x = torch.randn(b, t, cin, generator=g)
+    lengths = torch.tensor([t, 300, 77])
+    valid = (torch.arange(t).view(1, -1) < lengths.view(-1, 1)).float()
+    dl = torch.randn(b, k, generator=g)
+    model = model.to(cuda_device).train()
+    _, grads = _grads(model, x.to(cuda_device), dl.to(cuda_device), valid.to(cuda_device))
+    params = {n: p.detach().cpu().numpy() for n, p in model.named_parameters()}
+    params.update({n: model.get_buffer(n).cpu().numpy()
+                   for n in ("backward_block.direct_scale", "backward_block.layer_scale")})
+    ref = G.alphabet_backward(x.numpy(), params, dl.numpy(), valid_mask=valid.numpy())
+    assert len(ref) == 17
+    for name, gref in ref.items():
+        got = grads[name].cpu().numpy().reshape(gref.shape)
+        assert rel_err(got, gref) <= 5e-4, (name, rel_err(got, gref))
+
+
+def test_training_rejects_unsupported_metadata(cuda_device):
+    z = load_golden("grad_plain")
+    model = _model(z, cuda_device)
+    x = torch.from_numpy(z["in.x"]).to(cuda_device)
+    with pytest.raises(NotImplementedError):
+        model(x, time_delta=torch.ones(x.shape[:2], device=cuda_device))

@@ -81,14 +81,12 @@ def test_laplace_errors_mirror_reference():
         )
 
 
-def test_training_mode_refused():
-    m = B200Alphabet(AlphabetConfig(3, 8, 4, 5), 5)
-    with pytest.raises(RuntimeError):
-        m.train()
-        if torch.cuda.is_available():
-            m(torch.randn(2, 6, 3, device="cuda"))
-        else:
-            raise RuntimeError("CUDA")
+def test_training_mode_needs_cuda():
+    """Training mode runs the B200 forward/backward; a CPU input is refused, not
+    run on a CPU fallback."""
+    m = B200Alphabet(AlphabetConfig(3, 8, 4, 5), 5).train()
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.randn(2, 6, 3))
 
 
 def test_patchify_reference_layout():
