@@ -29,10 +29,14 @@ struct TrainPlan {
   float *m1, *m2, *feats, *a_tab;  // a_tab: [8][M] as in the general route
   // scratch
   float *carries, *partial, *wfold, *head_partial;
-  float *dS, *dX, *dY, *dV, *rs, *dfeats, *dm, *counts, *colpart, *polepart, *wls;
+  float *dS, *dX, *dY, *dV, *rs, *dfeats, *dm, *counts, *colpart, *polepart, *polesum, *wls;
 };
 
-constexpr int kColParts = 256;  // row parts of a column reduction
+constexpr int kColParts = 148 * 8;  // row parts of a column reduction (at most)
+constexpr int kBwdTile = 16;        // steps per block of the token-wise backward kernels
+constexpr int kWgTile = 128;        // steps per block of the conv weight-gradient partials
+constexpr int kMbTile = 64;         // steps per block of the moments VJP
+constexpr int kCbTile = 32;         // steps per block of the fused conv VJP
 
 static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params *p,
                        const lnet_b200_alphabet_request *r) {
@@ -66,8 +70,11 @@ static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params
   tp.dfeats = f((size_t)B * 14 * M);
   tp.dm = f((size_t)2 * B * 7 * M);
   tp.counts = f((size_t)B * 4);
-  tp.colpart = f((size_t)kColParts * 6 * std::max({D, C, 14 * M, K}));
+  const int64_t wg_parts = B * cdiv(std::max<int64_t>(r->steps, 1), kCbTile);
+  tp.colpart = f((size_t)std::max<int64_t>((int64_t)kColParts * 6 * std::max({D, C, 14 * M, K}),
+                                           wg_parts * D * (p->conv_kernel + 1)));
   tp.polepart = f((size_t)B * n_scan * 4 * M);
+  tp.polesum = f((size_t)std::max(4 * M, D * (p->conv_kernel + 1)));
   tp.wls = f((size_t)D * 2 * M);
 }
 
@@ -93,13 +100,15 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
                               cudaStream_t st) {
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const int C = p->raw_input_dim, D = p->model_dim, M = p->modes;
-  lnet_b200_alphabet_request rq = *r;
-  rq.act_dtype = LNET_F32;  // full-fp32 GEMMs
+  // GEMM precision as in the inference route: exact fp32 for fp32 requests,
+  // TF32 tensor cores for bf16 requests
+  const bool tf32 = r->act_dtype == LNET_BF16;
+  const lnet_b200_alphabet_request rq = *r;
   mask_inputs_kernel<TX><<<token_grid(bt), token_block(C), 0, st>>>(
       (const TX *)r->x, nullptr, 1, r->valid_mask, tp.x32, bt, C);
   LNET_TRY(after_launch("mask_inputs_kernel"));
   LNET_TRY(gemm_rows(st, tp.x32, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, tp.proj, D,
-                     bt, D, C, false, "cublas(stem)"));
+                     bt, D, C, tf32, "cublas(stem)"));
   LNET_TRY(depthwise_conv(tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
                           tp.y1, B, T, D, p->conv_kernel, p->conv_dilation, st,
                           "depthwise_conv(stem)"));
@@ -109,7 +118,7 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
                               tp.a_tab + 5 * M, nullptr, 1, &rq, D, M, pw, tp.m1,
                               /*write_states=*/true, st));
   LNET_TRY(gemm_rows(st, tp.s1, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
-                     tp.modal, D, bt, D, 2 * M, false, "cublas(synthesis)"));
+                     tp.modal, D, bt, D, 2 * M, tf32, "cublas(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
       tp.y1, tp.xh1, tp.modal, p->writer_direct_scale, p->writer_layer_scale, tp.v, bt, D);
   LNET_TRY(after_launch("residual_kernel"));
@@ -163,35 +172,71 @@ struct ColConvW {  // dz[t, d] * xin[t + k dil - pad, d] (masked input), col = d
   }
 };
 
+// Block = 32 columns x 8 row lanes; each lane sums every 8th row of its part,
+// then the 8 lanes are added in order through shared memory.
 template <typename F>
-__global__ void colsum_partial_kernel(F f, int64_t rows, int width, float *__restrict__ partial) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(256) colsum_partial_kernel(F f, int64_t rows, int width,
+                                                             float *__restrict__ partial) {
+  __shared__ float red[8][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  const int lane_row = threadIdx.y;
   const int part = blockIdx.y;
-  if (col >= width) return;
   const int64_t per = (rows + gridDim.y - 1) / gridDim.y;
   const int64_t r0 = min(rows, part * per), r1 = min(rows, r0 + per);
-  float acc = 0.f;
-  for (int64_t row = r0; row < r1; ++row) acc += f(row, col);
-  partial[(int64_t)part * width + col] = acc;
+  float a0 = 0.f, a1 = 0.f;
+  if (col < width) {
+    int64_t row = r0 + lane_row;
+    for (; row + 8 < r1; row += 16) {
+      a0 += f(row, col);
+      a1 += f(row + 8, col);
+    }
+    if (row < r1) a0 += f(row, col);
+  }
+  red[lane_row][threadIdx.x] = a0 + a1;
+  __syncthreads();
+  if (lane_row == 0 && col < width) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += red[k][threadIdx.x];
+    partial[(int64_t)part * width + col] = acc;
+  }
 }
 
-__global__ void colsum_final_kernel(const float *__restrict__ partial, int parts, int width,
-                                    float *__restrict__ out) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= width) return;
+// Block = 32 columns x 32 lanes; lane j sums parts j, j + 32, ... in double,
+// the lanes are then added in order.
+__global__ void __launch_bounds__(1024) colsum_final_kernel(const float *__restrict__ partial,
+                                                            int parts, int width,
+                                                            float *__restrict__ out) {
+  __shared__ double red[32][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
   double acc = 0.0;
-  for (int q = 0; q < parts; ++q) acc += (double)partial[(int64_t)q * width + col];
-  out[col] = (float)acc;
+  if (col < width)
+    for (int q = threadIdx.y; q < parts; q += 32) acc += (double)partial[(int64_t)q * width + col];
+  red[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && col < width) {
+    double total = 0.0;
+    for (int k = 0; k < 32; ++k) total += red[k][threadIdx.x];
+    out[col] = (float)total;
+  }
 }
 
 template <typename F>
 static int colsum(F f, int64_t rows, int width, float *partial, float *out, cudaStream_t st,
                   const char *what) {
-  const int parts = (int)std::max<int64_t>(1, std::min<int64_t>(kColParts, cdiv(rows, 64)));
-  const dim3 grid((unsigned)cdiv(width, 64), (unsigned)parts);
-  colsum_partial_kernel<F><<<grid, 64, 0, st>>>(f, rows, width, partial);
+  const int parts = (int)std::max<int64_t>(1, std::min<int64_t>(kColParts, cdiv(rows, 128)));
+  const dim3 grid((unsigned)cdiv(width, 32), (unsigned)parts);
+  colsum_partial_kernel<F><<<grid, dim3(32, 8), 0, st>>>(f, rows, width, partial);
   LNET_TRY(after_launch(what));
-  colsum_final_kernel<<<(unsigned)cdiv(width, 64), 64, 0, st>>>(partial, parts, width, out);
+  colsum_final_kernel<<<(unsigned)cdiv(width, 32), dim3(32, 32), 0, st>>>(partial, parts, width,
+                                                                          out);
+  return after_launch("colsum_final_kernel");
+}
+
+// The same final reduction for partials written by other kernels.
+static int colsum_finish(const float *partial, int parts, int width, float *out, cudaStream_t st) {
+  colsum_final_kernel<<<(unsigned)cdiv(width, 32), dim3(32, 32), 0, st>>>(partial, parts, width,
+                                                                          out);
   return after_launch("colsum_final_kernel");
 }
 
@@ -265,47 +310,80 @@ __global__ void moments_backward_kernel(const float *__restrict__ s, const float
                                         const float *__restrict__ counts,
                                         float *__restrict__ dS, int64_t batch, int64_t steps,
                                         int modes, int accumulate) {
-  const int lags[3] = {1, 2, 4};
-  const int64_t n = batch * steps * modes;
+  // block = (row, kMbTile steps), threads over modes; each thread streams its
+  // mode through the tile with states t-4 .. t+8 in registers (w[4] = step
+  // t), so every state is loaded once per tile (+ 12 halo steps).
   const int64_t M2 = 2 * modes;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tok = i / modes;
-    const int m = (int)(i - tok * modes);
-    const int64_t b = tok / steps, t = tok - b * steps;
-    const float *g = dm + b * 7 * modes;
-    const float *row = s + tok * M2;
-    const float cr = row[m], ci = row[modes + m];
-    const float vt = valid ? valid[tok] : 1.f;
-    const float c0 = valid ? counts[b * 4] : (float)steps;
-    float gr = 2.f * cr * g[m] * vt / c0, gi = 2.f * ci * g[m] * vt / c0;
+  const unsigned tiles = (unsigned)((steps + kMbTile - 1) / kMbTile);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t t_begin = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kMbTile;
+  const int64_t t_end = min(steps, t_begin + kMbTile);
+  const float *g = dm + b * 7 * modes;
+  const float *vrow = valid ? valid + b * steps : nullptr;
+  const float c0 = valid ? counts[b * 4] : (float)steps;
+  float cl[3];
+  const int lags[3] = {1, 2, 4};
+#pragma unroll
+  for (int l = 0; l < 3; ++l)
+    cl[l] = valid ? counts[b * 4 + 1 + l] : (float)(steps - lags[l]);
+  const float *srow = s + b * steps * M2;
+  float *orow = dS + b * steps * M2;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    const float ge = g[m];
+    float dr[3], di[3];
+#pragma unroll
     for (int l = 0; l < 3; ++l) {
-      const int lag = lags[l];
-      if (steps <= lag) continue;
-      const float dr = g[(1 + 2 * l) * modes + m], di = g[(2 + 2 * l) * modes + m];
-      const float cl = valid ? counts[b * 4 + 1 + l] : (float)(steps - lag);
-      if (t >= lag) {  // t as the current state, s_{t-lag} as the earlier one
-        const float *pr_ = row - lag * M2;
-        const float pr = pr_[m], pi = pr_[modes + m];
-        const float w = valid ? vt * valid[tok - lag] : 1.f;
-        gr += (dr * pr - di * pi) * w / cl;
-        gi += (dr * pi + di * pr) * w / cl;
-      }
-      if (t + lag < steps) {  // t as the earlier state of s_{t+lag}
-        const float *nx = row + lag * M2;
-        const float nr = nx[m], ni = nx[modes + m];
-        const float w = valid ? vt * valid[tok + lag] : 1.f;
-        gr += (dr * nr + di * ni) * w / cl;
-        gi += (dr * ni - di * nr) * w / cl;
-      }
+      dr[l] = g[(1 + 2 * l) * modes + m];
+      di[l] = g[(2 + 2 * l) * modes + m];
     }
-    float *out = dS + tok * M2;
-    if (accumulate) {
-      out[m] += gr;
-      out[modes + m] += gi;
-    } else {
-      out[m] = gr;
-      out[modes + m] = gi;
+    // w[0..8] = steps t-4 .. t+4; w[9..12] = t+5 .. t+8, loaded four steps
+    // before they enter the window
+    float wr[13], wi[13];
+#pragma unroll
+    for (int j = 0; j < 12; ++j) {  // steps t_begin - 4 .. t_begin + 7
+      const int64_t t = t_begin - 4 + j;
+      const bool in = t >= 0 && t < steps;
+      wr[j] = in ? srow[t * M2 + m] : 0.f;
+      wi[j] = in ? srow[t * M2 + modes + m] : 0.f;
+    }
+    for (int64_t t = t_begin; t < t_end; ++t) {
+      const int64_t tn = t + 8;
+      const bool in = tn < steps;
+      wr[12] = in ? srow[tn * M2 + m] : 0.f;
+      wi[12] = in ? srow[tn * M2 + modes + m] : 0.f;
+      const float cr = wr[4], ci = wi[4];
+      const float vt = vrow ? vrow[t] : 1.f;
+      float gr = 2.f * cr * ge * vt / c0, gi = 2.f * ci * ge * vt / c0;
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        const int lag = lags[l];
+        if (steps <= lag) continue;
+        if (t >= lag) {  // t as the current state, s_{t-lag} as the earlier one
+          const float pr = wr[4 - lag], pi = wi[4 - lag];
+          const float w = vrow ? vt * vrow[t - lag] : 1.f;
+          gr += (dr[l] * pr - di[l] * pi) * w / cl[l];
+          gi += (dr[l] * pi + di[l] * pr) * w / cl[l];
+        }
+        if (t + lag < steps) {  // t as the earlier state of s_{t+lag}
+          const float nr = wr[4 + lag], ni = wi[4 + lag];
+          const float w = vrow ? vt * vrow[t + lag] : 1.f;
+          gr += (dr[l] * nr + di[l] * ni) * w / cl[l];
+          gi += (dr[l] * ni - di[l] * nr) * w / cl[l];
+        }
+      }
+      float *out = orow + t * M2;
+      if (accumulate) {
+        out[m] += gr;
+        out[modes + m] += gi;
+      } else {
+        out[m] = gr;
+        out[modes + m] = gi;
+      }
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        wr[j] = wr[j + 1];
+        wi[j] = wi[j + 1];
+      }
     }
   }
 }
@@ -394,15 +472,15 @@ __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restri
 // d raw_decay, d raw_frequency from the summed da, dg of every (row, chunk):
 // dL/dp by the Cauchy-Riemann form of a'(p) = a and g'(p) = (a p - (a - 1)) / p^2
 // (dt = 1), then damping = dmin + (dmax - dmin) sigmoid(raw), freq = pi tanh(raw).
-__global__ void pole_backward_kernel(const float *__restrict__ polepart, int64_t parts, int modes,
+// `sums` [4][M]: da re, da im, dg re, dg im summed over every (row, chunk).
+__global__ void pole_backward_kernel(const float *__restrict__ sums, int modes,
                                      const float *__restrict__ raw_decay,
                                      const float *__restrict__ raw_freq,
                                      float *__restrict__ d_decay, float *__restrict__ d_freq) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= modes) return;
-  double s[4] = {0, 0, 0, 0};
-  for (int64_t q = 0; q < parts; ++q)
-    for (int k = 0; k < 4; ++k) s[k] += (double)polepart[(q * 4 + k) * modes + m];
+  double s[4];
+  for (int k = 0; k < 4; ++k) s[k] = (double)sums[k * modes + m];
   const double sig = 1.0 / (1.0 + exp(-(double)raw_decay[m]));
   const double damping = kDampingMin + (kDampingMax - kDampingMin) * sig;
   const double th = tanh((double)raw_freq[m]);
@@ -458,26 +536,32 @@ __global__ void conv_dz_kernel(const float *__restrict__ in, const float *__rest
                                const float *__restrict__ out_mask, const float *__restrict__ dy,
                                float *__restrict__ dz, int64_t batch, int64_t steps, int dim,
                                int taps, int dil) {
-  const int64_t n = batch * steps * dim;
+  // block = (row, kBwdTile steps), threads over channels
   const int pad = dil * (taps - 1) / 2;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tok = i / dim;
-    const int d = (int)(i - tok * dim);
-    const int64_t b = tok / steps, t = tok - b * steps;
-    float z = 0.f;
-    for (int k = 0; k < taps; ++k) {
-      const int64_t s = t + (int64_t)k * dil - pad;
-      if (s < 0 || s >= steps) continue;
-      float v = in[(b * steps + s) * dim + d];
-      if (in_mask) v *= in_mask[b * steps + s];
-      z = fmaf(w[d * taps + k], v, z);
+  const unsigned tiles = (unsigned)((steps + kBwdTile - 1) / kBwdTile);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t t_begin = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kBwdTile;
+  const int64_t t_end = min(steps, t_begin + kBwdTile);
+  const float *rin = in + b * steps * dim;
+  const float *im = in_mask ? in_mask + b * steps : nullptr;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    const float bd = bias[d];
+    for (int64_t t = t_begin; t < t_end; ++t) {
+      float z = 0.f;
+      for (int k = 0; k < taps; ++k) {
+        const int64_t sidx = t + (int64_t)k * dil - pad;
+        if (sidx < 0 || sidx >= steps) continue;
+        float v = rin[sidx * dim + d];
+        if (im) v *= im[sidx];
+        z = fmaf(w[d * taps + k], v, z);
+      }
+      z += bd;
+      const float sg = 1.0f / (1.0f + expf(-z));
+      const int64_t i = (b * steps + t) * dim + d;
+      float gz = dy[i] * sg * (1.0f + z * (1.0f - sg));
+      if (out_mask) gz *= out_mask[b * steps + t];
+      dz[i] = gz;
     }
-    z += bias[d];
-    const float sg = 1.0f / (1.0f + expf(-z));
-    float gz = dy[i] * sg * (1.0f + z * (1.0f - sg));
-    if (out_mask) gz *= out_mask[tok];
-    dz[i] = gz;
   }
 }
 
@@ -485,22 +569,177 @@ __global__ void conv_dz_kernel(const float *__restrict__ in, const float *__rest
 __global__ void conv_dx_kernel(const float *__restrict__ dz, const float *__restrict__ w,
                                const float *__restrict__ in_mask, float *__restrict__ dx,
                                int64_t batch, int64_t steps, int dim, int taps, int dil) {
-  const int64_t n = batch * steps * dim;
   const int pad = dil * (taps - 1) / 2;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tok = i / dim;
-    const int d = (int)(i - tok * dim);
-    const int64_t b = tok / steps, s = tok - b * steps;
-    float acc = 0.f;
-    for (int k = 0; k < taps; ++k) {
-      const int64_t t = s - (int64_t)k * dil + pad;
-      if (t < 0 || t >= steps) continue;
-      acc = fmaf(w[d * taps + k], dz[(b * steps + t) * dim + d], acc);
+  const unsigned tiles = (unsigned)((steps + kBwdTile - 1) / kBwdTile);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t s_begin = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kBwdTile;
+  const int64_t s_end = min(steps, s_begin + kBwdTile);
+  const float *rz = dz + b * steps * dim;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    for (int64_t si = s_begin; si < s_end; ++si) {
+      float acc = 0.f;
+      for (int k = 0; k < taps; ++k) {
+        const int64_t t = si - (int64_t)k * dil + pad;
+        if (t < 0 || t >= steps) continue;
+        acc = fmaf(w[d * taps + k], rz[t * dim + d], acc);
+      }
+      if (in_mask) acc *= in_mask[b * steps + si];
+      dx[(b * steps + si) * dim + d] = acc;
     }
-    if (in_mask) acc *= in_mask[tok];
-    dx[i] = acc;
   }
+}
+
+// Conv weight and bias gradient partials: block = (row, kWgTile steps),
+// threads over channels; each thread accumulates, over its tile, dz[t] x
+// xin[t + k dil - pad] (masked input) for every tap and dz[t] for the bias,
+// and writes partial[part][d * (taps + 1) + j] (j = taps: the bias).
+template <int TAPS>
+__global__ void conv_wgrad_kernel(const float *__restrict__ dz, const float *__restrict__ xin,
+                                  const float *__restrict__ in_mask, float *__restrict__ partial,
+                                  int64_t steps, int dim, int dil) {
+  constexpr int taps = TAPS;
+  const int pad = dil * (taps - 1) / 2;
+  const unsigned tiles = (unsigned)((steps + kWgTile - 1) / kWgTile);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t t_begin = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kWgTile;
+  const int64_t t_end = min(steps, t_begin + kWgTile);
+  const float *rz = dz + b * steps * dim;
+  const float *rx = xin + b * steps * dim;
+  const float *im = in_mask ? in_mask + b * steps : nullptr;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    float acc[TAPS + 1];
+#pragma unroll
+    for (int k = 0; k <= TAPS; ++k) acc[k] = 0.f;
+    for (int64_t t = t_begin; t < t_end; ++t) {
+      const float g = rz[t * dim + d];
+      acc[taps] += g;
+#pragma unroll
+      for (int k = 0; k < taps; ++k) {
+        const int64_t sidx = t + (int64_t)k * dil - pad;
+        if (sidx < 0 || sidx >= steps) continue;
+        float x = rx[sidx * dim + d];
+        if (im) x *= im[sidx];
+        acc[k] = fmaf(g, x, acc[k]);
+      }
+    }
+    float *out = partial + (int64_t)blockIdx.x * dim * (taps + 1) + d * (taps + 1);
+#pragma unroll
+    for (int k = 0; k <= taps; ++k) out[k] = acc[k];
+  }
+}
+
+// 16-byte asynchronous global -> shared copy (zero-filled when `bytes` is 0);
+// completion is awaited with cp.async.wait_group (a hardware wait).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sm100::smem_u32(dst)),
+               "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// The conv + SiLU VJP in one pass for a row's kCbTile steps (TAPS taps,
+// 4 | dim <= 256): stage the input of steps [s0 - 2 pad, s0 + kCbTile + 2 pad)
+// and dy of [s0 - pad, s0 + kCbTile + pad) in shared memory with 16-byte
+// asynchronous copies (zero outside the sequence), form dz = dy out_mask
+// silu'(z) in place (z recomputed from the masked input), then per channel the
+// input gradient of the core steps and the weight / bias partial sums over
+// them (partial[block][d (TAPS + 1) + j]).
+template <int TAPS>
+__global__ void __launch_bounds__(256) conv_backward_kernel(
+    const float *__restrict__ in, const float *__restrict__ w, const float *__restrict__ bias,
+    const float *__restrict__ in_mask, const float *__restrict__ out_mask,
+    const float *__restrict__ dy, float *__restrict__ dx, float *__restrict__ partial,
+    int64_t steps, int dim, int dil) {
+  extern __shared__ float4 cb_smem4[];
+  float *cb_smem = reinterpret_cast<float *>(cb_smem4);
+  const int pad = dil * (TAPS - 1) / 2;
+  const int xrows = kCbTile + 4 * pad, zrows = kCbTile + 2 * pad;
+  const int quads = dim >> 2;
+  float *sx = cb_smem;          // [xrows][dim] masked input
+  float *sz = sx + xrows * dim; // [zrows][dim] dy, then dz
+  const unsigned tiles = (unsigned)((steps + kCbTile - 1) / kCbTile);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t s0 = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kCbTile;
+  const float *rin = in + b * steps * dim;
+  const float *rdy = dy + b * steps * dim;
+  const float *im = in_mask ? in_mask + b * steps : nullptr;
+  const float *om = out_mask ? out_mask + b * steps : nullptr;
+  for (int i = threadIdx.x; i < xrows * quads; i += blockDim.x) {
+    const int r = i / quads, q = i - (i / quads) * quads;
+    const int64_t t = s0 - 2 * pad + r;
+    const bool live = t >= 0 && t < steps;
+    cp_async16(sx + r * dim + 4 * q, rin + (live ? t : 0) * dim + 4 * q, live ? 16 : 0);
+  }
+  for (int i = threadIdx.x; i < zrows * quads; i += blockDim.x) {
+    const int r = i / quads, q = i - (i / quads) * quads;
+    const int64_t t = s0 - pad + r;
+    const bool live = t >= 0 && t < steps;
+    cp_async16(sz + r * dim + 4 * q, rdy + (live ? t : 0) * dim + 4 * q, live ? 16 : 0);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (im) {
+    for (int i = threadIdx.x; i < xrows * dim; i += blockDim.x) {
+      const int64_t t = s0 - 2 * pad + i / dim;
+      if (t >= 0 && t < steps) sx[i] *= im[t];
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < zrows * dim; i += blockDim.x) {
+    const int r = i / dim, d = i - (i / dim) * dim;
+    const int64_t t = s0 - pad + r;
+    float gz = 0.f;
+    if (t >= 0 && t < steps) {
+      float z = 0.f;
+#pragma unroll
+      for (int k = 0; k < TAPS; ++k) z = fmaf(w[d * TAPS + k], sx[(r + k * dil) * dim + d], z);
+      z += bias[d];
+      const float sg = 1.0f / (1.0f + expf(-z));
+      gz = sz[i] * sg * (1.0f + z * (1.0f - sg));
+      if (om) gz *= om[t];
+    }
+    sz[i] = gz;
+  }
+  __syncthreads();
+  const int n_core = (int)min((int64_t)kCbTile, steps - s0);
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    float wk[TAPS], aw[TAPS];
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) {
+      wk[k] = w[d * TAPS + k];
+      aw[k] = 0.f;
+    }
+    float ab = 0.f;
+    for (int r = 0; r < n_core; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < TAPS; ++k) acc = fmaf(wk[k], sz[(r - k * dil + 2 * pad) * dim + d], acc);
+      if (im) acc *= im[s0 + r];
+      dx[(b * steps + s0 + r) * dim + d] = acc;
+      const float g = sz[(r + pad) * dim + d];
+      ab += g;
+#pragma unroll
+      for (int k = 0; k < TAPS; ++k) aw[k] = fmaf(g, sx[(r + pad + k * dil) * dim + d], aw[k]);
+    }
+    float *out = partial + (int64_t)blockIdx.x * dim * (TAPS + 1) + d * (TAPS + 1);
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) out[k] = aw[k];
+    out[TAPS] = ab;
+  }
+}
+
+// Spread [D][taps + 1] sums into the weight [D, taps] and bias [D] gradients.
+__global__ void conv_wgrad_split_kernel(const float *__restrict__ sums, float *__restrict__ dw,
+                                        float *__restrict__ db, int dim, int taps) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= dim * (taps + 1)) return;
+  const int d = i / (taps + 1), k = i - d * (taps + 1);
+  if (k < taps)
+    dw[d * taps + k] = sums[i];
+  else
+    db[d] = sums[i];
 }
 
 // dxh_res = dv ls ds (the residual's xhat path).
@@ -519,7 +758,7 @@ __global__ void residual_dxh_kernel(const float *__restrict__ dv, const float *_
 // C[n1, n2] (row-major) = sum_r A[r, n1] Bm[r, n2] (+ beta C): the weight
 // gradients (A [R, n1], Bm [R, n2] row-major).
 static int gemm_wgrad(cudaStream_t st, const float *A, int64_t n1, const float *Bm, int64_t n2,
-                      float *C, int64_t R, float beta, const char *what) {
+                      float *C, int64_t R, float beta, bool tf32, const char *what) {
   if (R == 0 || n1 == 0 || n2 == 0) return LNET_OK;
   if (R > INT32_MAX) return fail(LNET_ERR_UNSUPPORTED, "%s: %lld rows", what, (long long)R);
   cublasHandle_t h;
@@ -530,7 +769,8 @@ static int gemm_wgrad(cudaStream_t st, const float *A, int64_t n1, const float *
   const float alpha = 1.f;
   const cublasStatus_t s = cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_T, (int)n2, (int)n1, (int)R,
                                         &alpha, Bm, CUDA_R_32F, (int)n2, A, CUDA_R_32F, (int)n1,
-                                        &beta, C, CUDA_R_32F, (int)n2, CUBLAS_COMPUTE_32F,
+                                        &beta, C, CUDA_R_32F, (int)n2,
+                                        tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F,
                                         CUBLAS_GEMM_DEFAULT);
   if (s != CUBLAS_STATUS_SUCCESS) return fail(LNET_ERR_CUDA, "%s: cublasGemmEx status %d", what, (int)s);
   return after_library(what);
@@ -545,7 +785,7 @@ static int block_backward(const TrainPlan &tp, const float *states, const float 
                           const float *a_re, const float *a_im, const float *g_re,
                           const float *g_im, float *dxh, float dxh_beta, float *dframe,
                           float frame_beta, float *d_decay, float *d_freq, int64_t B, int64_t T,
-                          int D, int M, cudaStream_t st) {
+                          int D, int M, bool tf32, cudaStream_t st) {
   const int64_t n_scan = cdiv(T, kScanChunk);
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   const dim3 gs((unsigned)n_scan, (unsigned)B);
@@ -558,14 +798,15 @@ static int block_backward(const TrainPlan &tp, const float *states, const float 
   rscan_apply_kernel<<<gs, threads, 0, st>>>(tp.dS, states, a_re, a_im, g_re, g_im, tp.carries,
                                              tp.polepart, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("rscan_apply_kernel"));
-  pole_backward_kernel<<<(unsigned)cdiv(M, 64), 64, 0, st>>>(tp.polepart, B * n_scan, M,
-                                                             raw_decay, raw_freq, d_decay,
-                                                             d_freq);
+  LNET_TRY(colsum(ColPlain{tp.polepart, 4 * M}, B * n_scan, 4 * M, tp.colpart, tp.polesum, st,
+                  "colsum(pole)"));
+  pole_backward_kernel<<<(unsigned)cdiv(M, 64), 64, 0, st>>>(tp.polesum, M, raw_decay, raw_freq,
+                                                             d_decay, d_freq);
   LNET_TRY(after_launch("pole_backward_kernel"));
   const int64_t bt = B * T;
   LNET_TRY(gemm_rows(st, tp.dS, CUDA_R_32F, 2 * M, frame, CUDA_R_32F, 2 * M, 1, dxh, D, bt, D,
-                     2 * M, false, "cublas(d xhat)", dxh_beta));
-  return gemm_wgrad(st, xh, D, tp.dS, 2 * M, dframe, bt, frame_beta, "cublas(d frame)");
+                     2 * M, tf32, "cublas(d xhat)", dxh_beta));
+  return gemm_wgrad(st, xh, D, tp.dS, 2 * M, dframe, bt, frame_beta, tf32, "cublas(d frame)");
 }
 
 static int conv_backward(const TrainPlan &tp, const float *in, const float *w, const float *bias,
@@ -573,15 +814,44 @@ static int conv_backward(const TrainPlan &tp, const float *in, const float *w, c
                          float *dw, float *db, int64_t B, int64_t T, int D, int taps, int dil,
                          cudaStream_t st) {
   const int64_t bt = B * T;
+  if (taps == 5 && D <= 256 && D % 4 == 0) {  // one fused pass
+    const int pad = dil * (taps - 1) / 2;
+    const size_t smem = (size_t)(2 * kCbTile + 6 * pad) * D * sizeof(float);
+    if (smem > 227 * 1024) return fail(LNET_ERR_UNSUPPORTED, "conv backward: dilation too large");
+    LNET_TRY(cuda_check(cudaFuncSetAttribute(conv_backward_kernel<5>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem),
+                        "cudaFuncSetAttribute(conv_backward_kernel)"));
+    const unsigned cb_grid = (unsigned)(B * cdiv(T, kCbTile));
+    const unsigned cb_threads = (unsigned)std::min(256, (int)cdiv(D, 32) * 32);
+    conv_backward_kernel<5><<<cb_grid, cb_threads, smem, st>>>(in, w, bias, in_mask, out_mask,
+                                                                dy, dx, tp.colpart, T, D, dil);
+    LNET_TRY(after_launch("conv_backward_kernel"));
+    LNET_TRY(colsum_finish(tp.colpart, (int)cb_grid, D * (taps + 1), tp.polesum, st));
+    conv_wgrad_split_kernel<<<(unsigned)cdiv(D * (taps + 1), 256), 256, 0, st>>>(tp.polesum, dw,
+                                                                                db, D, taps);
+    return after_launch("conv_wgrad_split_kernel");
+  }
   float *dz = tp.dY;  // dy is consumed element-wise in place
-  conv_dz_kernel<<<grid_for(bt * D), 256, 0, st>>>(in, w, bias, in_mask, out_mask, dy, dz, B, T,
-                                                   D, taps, dil);
+  const unsigned grid = (unsigned)(B * cdiv(T, kBwdTile));
+  const unsigned threads = (unsigned)std::min(256, (int)cdiv(D, 32) * 32);
+  conv_dz_kernel<<<grid, threads, 0, st>>>(in, w, bias, in_mask, out_mask, dy, dz, B, T, D, taps,
+                                           dil);
   LNET_TRY(after_launch("conv_dz_kernel"));
-  conv_dx_kernel<<<grid_for(bt * D), 256, 0, st>>>(dz, w, in_mask, dx, B, T, D, taps, dil);
+  conv_dx_kernel<<<grid, threads, 0, st>>>(dz, w, in_mask, dx, B, T, D, taps, dil);
   LNET_TRY(after_launch("conv_dx_kernel"));
-  LNET_TRY(colsum(ColConvW{dz, in, in_mask, T, D, taps, dil}, bt, D * taps, tp.colpart, dw, st,
-                  "colsum(conv w)"));
-  return colsum(ColPlain{dz, D}, bt, D, tp.colpart, db, st, "colsum(conv b)");
+  if (taps != 5) {  // other kernel sizes: the generic column sums
+    LNET_TRY(colsum(ColConvW{dz, in, in_mask, T, D, taps, dil}, bt, D * taps, tp.colpart, dw, st,
+                    "colsum(conv w)"));
+    return colsum(ColPlain{dz, D}, bt, D, tp.colpart, db, st, "colsum(conv b)");
+  }
+  const unsigned wg_grid = (unsigned)(B * cdiv(T, kWgTile));
+  conv_wgrad_kernel<5><<<wg_grid, threads, 0, st>>>(dz, in, in_mask, tp.colpart, T, D, dil);
+  LNET_TRY(after_launch("conv_wgrad_kernel"));
+  LNET_TRY(colsum_finish(tp.colpart, (int)wg_grid, D * (taps + 1), tp.polesum, st));
+  conv_wgrad_split_kernel<<<(unsigned)cdiv(D * (taps + 1), 256), 256, 0, st>>>(tp.polesum, dw, db,
+                                                                              D, taps);
+  return after_launch("conv_wgrad_split_kernel");
 }
 
 static int train_backward_impl(const lnet_b200_alphabet_params *p,
@@ -592,8 +862,9 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   const int C = p->raw_input_dim, D = p->model_dim, M = p->modes, K = p->output_dim;
   const int taps = p->conv_kernel, dil = p->conv_dilation;
   const float *valid = r->valid_mask;
+  const bool tf32 = r->act_dtype == LNET_BF16;  // as the training forward
   // head
-  LNET_TRY(gemm_wgrad(st, dlogits, K, tp.feats, 14 * M, gd->head_weight, B, 0.f,
+  LNET_TRY(gemm_wgrad(st, dlogits, K, tp.feats, 14 * M, gd->head_weight, B, 0.f, false,
                       "cublas(d head)"));
   LNET_TRY(colsum(ColPlain{dlogits, K}, B, K, tp.colpart, gd->head_bias, st, "colsum(head b)"));
   LNET_TRY(gemm_rows(st, dlogits, CUDA_R_32F, K, p->head_weight, CUDA_R_32F, 1, 14 * M, tp.dfeats,
@@ -607,13 +878,15 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   }
   const float *dm1 = tp.dm, *dm2 = tp.dm + B * 7 * M;
   // reader block
-  moments_backward_kernel<<<grid_for(bt * M), 256, 0, st>>>(tp.s2, dm2, valid, tp.counts, tp.dS,
-                                                            B, T, M, 0);
+  const unsigned mb_grid = (unsigned)(B * cdiv(T, kMbTile));
+  const unsigned mb_threads = (unsigned)std::min(128, (int)cdiv(M, 32) * 32);
+  moments_backward_kernel<<<mb_grid, mb_threads, 0, st>>>(tp.s2, dm2, valid, tp.counts, tp.dS, B,
+                                                          T, M, 0);
   LNET_TRY(after_launch("moments_backward_kernel"));
   LNET_TRY(block_backward(tp, tp.s2, tp.xh2, p->reader_frame, p->reader_raw_decay,
                           p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
                           tp.a_tab + 6 * M, tp.a_tab + 7 * M, tp.dX, 0.f, gd->reader_frame, 0.f,
-                          gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, st));
+                          gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, tf32, st));
   rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y2, tp.dX, p->reader_norm,
                                                              nullptr, tp.dY, tp.rs, bt, D);
   LNET_TRY(after_launch("rms_backward_kernel"));
@@ -632,14 +905,14 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(p->writer_frame, ls, tp.wls, D,
                                                                    2 * M);
   LNET_TRY(after_launch("scale_rows_kernel"));
-  // dS1 = dv (ls F) + moments VJP
-  LNET_TRY(gemm_rows(st, tp.dV, CUDA_R_32F, D, tp.wls, CUDA_R_32F, 1, 2 * M, tp.dS, 2 * M, bt,
-                     2 * M, D, false, "cublas(d states synth)"));
-  moments_backward_kernel<<<grid_for(bt * M), 256, 0, st>>>(tp.s1, dm1, valid, tp.counts, tp.dS,
-                                                            B, T, M, 1);
+  // dS1 = moments VJP + dv (ls F) (the GEMM accumulates, beta = 1)
+  moments_backward_kernel<<<mb_grid, mb_threads, 0, st>>>(tp.s1, dm1, valid, tp.counts, tp.dS, B,
+                                                          T, M, 0);
   LNET_TRY(after_launch("moments_backward_kernel"));
+  LNET_TRY(gemm_rows(st, tp.dV, CUDA_R_32F, D, tp.wls, CUDA_R_32F, 1, 2 * M, tp.dS, 2 * M, bt,
+                     2 * M, D, tf32, "cublas(d states synth)", /*beta=*/1.f));
   // dF1 = ls (dv^T s1) (+ the drive part below)
-  LNET_TRY(gemm_wgrad(st, tp.dV, D, tp.s1, 2 * M, gd->writer_frame, bt, 0.f,
+  LNET_TRY(gemm_wgrad(st, tp.dV, D, tp.s1, 2 * M, gd->writer_frame, bt, 0.f, tf32,
                       "cublas(d frame synth)"));
   scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(gd->writer_frame, ls,
                                                                    gd->writer_frame, D, 2 * M);
@@ -649,7 +922,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(block_backward(tp, tp.s1, tp.xh1, p->writer_frame, p->writer_raw_decay,
                           p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
                           tp.a_tab + 5 * M, tp.dX, 1.f, gd->writer_frame, 1.f,
-                          gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, st));
+                          gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, tf32, st));
   // writer RMSNorm: dy1 = rms VJP + dv (residual identity)
   rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y1, tp.dX, p->writer_norm, tp.dV,
                                                              tp.dY, tp.rs, bt, D);
@@ -660,7 +933,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(conv_backward(tp, tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, valid,
                          tp.dY, tp.dV, gd->stem_conv_weight, gd->stem_conv_bias, B, T, D, taps,
                          dil, st));
-  return gemm_wgrad(st, tp.dV, D, tp.x32, C, gd->stem_projection, bt, 0.f,
+  return gemm_wgrad(st, tp.dV, D, tp.x32, C, gd->stem_projection, bt, 0.f, tf32,
                     "cublas(d projection)");
 }
 

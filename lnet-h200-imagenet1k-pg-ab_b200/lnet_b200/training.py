@@ -73,8 +73,10 @@ class AlphabetTrainFunction(torch.autograd.Function):
         )
         x = x.detach().contiguous()
         dtype = _lib.LNET_BF16 if x.dtype == torch.bfloat16 else _lib.LNET_F32
+        # fp32 inputs: exact fp32 GEMMs; bf16 inputs: TF32 tensor cores (the
+        # precision policy of the inference route)
         req = _lib.AlphabetRequest(batch=x.shape[0], steps=x.shape[1], x_dtype=dtype,
-                                   act_dtype=_lib.LNET_F32, x=x.data_ptr(), obs_channels=1,
+                                   act_dtype=dtype, x=x.data_ptr(), obs_channels=1,
                                    valid_mask=None if valid is None else valid.data_ptr())
         n = ctypes.c_size_t(0)
         _lib.check(lib.lnet_b200_alphabet_train_workspace_size(ctypes.byref(params),

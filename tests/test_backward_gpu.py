@@ -106,6 +106,18 @@ def test_backward_larger_case_against_oracle(cuda_device):
         assert rel_err(got, gref) <= 5e-4, (name, rel_err(got, gref))
 
 
+def test_backward_bf16_inputs_tf32(cuda_device):
+    """bf16 inputs train with TF32 GEMMs: gradients within 2e-2 of the fp32 ones."""
+    z = load_golden("grad_long")
+    model = _model(z, cuda_device)
+    x = torch.from_numpy(z["in.x"]).to(cuda_device).to(torch.bfloat16)
+    dl = torch.from_numpy(z["in.dlogits"]).to(cuda_device)
+    _, g16 = _grads(model, x, dl)
+    _, g32 = _grads(model, x.float(), dl)
+    for name, ref in g32.items():
+        assert rel_err(g16[name].cpu().numpy(), ref.cpu().numpy()) <= 2e-2, name
+
+
 def test_training_rejects_unsupported_metadata(cuda_device):
     z = load_golden("grad_plain")
     model = _model(z, cuda_device)
