@@ -321,6 +321,96 @@ def run_reference(args, cfg):
     return 0
 
 
+TRAIN_METRIC = "ALPHABET train step tokens/sec"
+
+
+def run_train(args, cfg):
+    """Training step (``--mode train``, one GPU): forward + backward of
+    ``sum(logits * dlogits)`` + an SGD update through the module API
+    (``B200Alphabet.train()``: lnet_b200_alphabet_train_forward /
+    lnet_b200_alphabet_backward), inputs resident in HBM, L2 flushed between
+    steps.  The reference arm times the numpy backward oracle (forward with
+    the saved activations + VJP, float32) on ``--ref-rows`` rows per step."""
+    import torch
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        from oracle import alphabet_grad_oracle as G
+
+        rows = args.ref_rows
+        p = params_numpy(cfg)
+        rng = np.random.default_rng(3)
+        x = rng.standard_normal((rows, cfg["T"], cfg["C"])).astype(np.float32)
+        dl = rng.standard_normal((rows, cfg["K"])).astype(np.float32)
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            G.alphabet_backward(x, p, dl, dtype=np.float32)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+        total = sum(times)
+        value = rows * cfg["T"] * args.steps / total
+        print(json.dumps({
+            "metric": TRAIN_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": cfg["workload"], "sample_rows_per_step": rows},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                             "sample": f"{rows} of {cfg['B']} rows x T={cfg['T']} per step, numpy "
+                                       "backward oracle (forward + VJP) in fp32"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    from lnet_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    model = build_model(cfg, dev).train()
+    x = make_inputs(cfg, dev)
+    B, T = cfg["B"], cfg["T"]
+    dl = torch.randn(B, cfg["K"], generator=torch.Generator(device=dev).manual_seed(9), device=dev)
+    opt = torch.optim.SGD(model.parameters(), lr=1e-4, foreach=True)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        (model(x) * dl).sum().backward()
+        opt.step()
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    _lib.profile_enable(True)
+    launches = 0
+    with ClockSampler(0) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            step()
+            launches += _lib.last_launch_count()
+            stops[i].record()
+        torch.cuda.synchronize()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    total_ms = sum(a.elapsed_time(b) for a, b in zip(starts, stops))
+    print(json.dumps({
+        "metric": TRAIN_METRIC, "value": B * T * args.steps / (total_ms / 1e3), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (TF32 GEMMs for bf16 inputs)" if cfg["dtype"] == "bf16"
+        else "f32", "data": "synthetic",
+        "config": {"workload": cfg["workload"], "path": "module API, training step (SGD)",
+                   "l2": "256 MiB flush between steps, outside the per-step event pair"},
+        "clocks": clocks.summary(), "gpu_launches_backward": launches,
+        "kernels": _lib_kernels(prof)}), flush=True)
+    return 0
+
+
 def run_module(args, cfg):
     """Configs 1 and 3 (one GPU): K forwards through the module API with the
     inputs resident in HBM, L2 flushed between steps, CUDA events per step.
@@ -628,6 +718,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override (small cases for profiling only)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
+    ap.add_argument("--mode", choices=["forward", "train"], default="forward",
+                    help="train: forward + backward + SGD step (one GPU, ALPHABET configs)")
     ap.add_argument("--trace", action="store_true",
                     help="after the timed region, one traced forward: per-phase cycles per item")
     args = ap.parse_args()
@@ -639,6 +731,11 @@ def main():
         cfg["B"] = args.batch
         cfg["workload"] = cfg["workload"].replace(f"_b{CONFIGS[args.config]['B']}_",
                                                   f"_b{args.batch}_")
+    if args.mode == "train":
+        if cfg.get("meta") or cfg.get("laplace"):
+            log("--mode train covers the static-pole ALPHABET configs (2, 4, 5)")
+            return 2
+        return run_train(args, cfg)
     if args.impl == "reference" and not (cfg.get("meta") or cfg.get("laplace")):
         return run_reference(args, cfg)
     if cfg.get("meta") or cfg.get("laplace"):
