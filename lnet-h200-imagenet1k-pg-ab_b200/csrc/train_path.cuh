@@ -1,6 +1,6 @@
 // Training path of the general route: a forward that keeps its activations
 // and the backward pass (VJP) of every stage, for static-pole requests
-// without observation masks (valid masks allowed), all in fp32.
+// (observation and valid masks allowed), all in fp32.
 //
 // Forward (lnet_b200_alphabet_train_forward): the general-route stages with
 // separate buffers per block, full-fp32 GEMMs.  Kept in the workspace:
@@ -78,9 +78,7 @@ static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params
   tp.wls = f((size_t)D * 2 * M);
 }
 
-static bool train_supported(const lnet_b200_alphabet_request *r) {
-  return !r->time_delta && !r->observation_mask;
-}
+static bool train_supported(const lnet_b200_alphabet_request *r) { return !r->time_delta; }
 
 // A Plan view of the training buffers for block_scan_moments.
 static Plan block_view(const TrainPlan &tp, float *xhat, float *states) {
@@ -105,7 +103,7 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
   const bool tf32 = r->act_dtype == LNET_BF16;
   const lnet_b200_alphabet_request rq = *r;
   mask_inputs_kernel<TX><<<token_grid(bt), token_block(C), 0, st>>>(
-      (const TX *)r->x, nullptr, 1, r->valid_mask, tp.x32, bt, C);
+      (const TX *)r->x, r->observation_mask, r->obs_channels, r->valid_mask, tp.x32, bt, C);
   LNET_TRY(after_launch("mask_inputs_kernel"));
   LNET_TRY(gemm_rows(st, tp.x32, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, tp.proj, D,
                      bt, D, C, tf32, "cublas(stem)"));
@@ -115,8 +113,8 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
   Plan pw = block_view(tp, tp.xh1, tp.s1);
   LNET_TRY(block_scan_moments(tp.y1, p->writer_norm, p->writer_frame, p->writer_raw_decay,
                               p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
-                              tp.a_tab + 5 * M, nullptr, 1, &rq, D, M, pw, tp.m1,
-                              /*write_states=*/true, st));
+                              tp.a_tab + 5 * M, r->observation_mask, r->obs_channels, &rq, D, M,
+                              pw, tp.m1, /*write_states=*/true, st));
   LNET_TRY(gemm_rows(st, tp.s1, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
                      tp.modal, D, bt, D, 2 * M, tf32, "cublas(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
@@ -421,15 +419,17 @@ __global__ void rscan_local_kernel(const float *__restrict__ dS, const float *__
 }
 
 // Reverse scan, apply pass: walks each chunk backwards from the lambda that
-// enters it, writes de = conj(g) lambda over dS, and sums per (row, chunk,
-// mode) da = lambda x s_{t-1} and dg = lambda x e_t (real-pair form; e_t =
-// (s_t - a s_{t-1}) / g) into polepart [B, nchunk, 4, M].
+// enters it, writes de = conj(g) lambda (times the writer's event mask) over
+// dS, and sums per (row, chunk, mode) da = lambda x s_{t-1} and dg = lambda x
+// u_t / g (real-pair form; u_t = s_t - a s_{t-1}, the masked drive) into
+// polepart [B, nchunk, 4, M].
 __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restrict__ s,
                                    const float *__restrict__ a_re, const float *__restrict__ a_im,
                                    const float *__restrict__ g_re, const float *__restrict__ g_im,
                                    const float *__restrict__ rec_all,
                                    float *__restrict__ polepart, int64_t steps, int modes,
-                                   int chunk, int64_t n_chunks) {
+                                   int chunk, int64_t n_chunks,
+                                   const float *__restrict__ event_mask, int obs_channels) {
   const int64_t c = blockIdx.x, b = blockIdx.y;
   const int64_t t0 = c * chunk, t1 = min(steps, t0 + chunk);
   const int64_t M2 = 2 * modes;
@@ -458,8 +458,14 @@ __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restri
       const float er = (ur * gr + ui * gi) / gden, ei = (ui * gr - ur * gi) / gden;
       dgr += lr * er + li * ei;
       dgi += -lr * ei + li * er;
-      row[m] = lr * gr + li * gi;  // de = conj(g) lambda
-      row[modes + m] = -lr * gi + li * gr;
+      float ev = 1.f;  // u = event g e: de carries the event mask (amax over channels)
+      if (event_mask) {
+        const float *om = event_mask + (b * steps + t) * obs_channels;
+        ev = om[0];
+        for (int c2 = 1; c2 < obs_channels; ++c2) ev = fmaxf(ev, om[c2]);
+      }
+      row[m] = (lr * gr + li * gi) * ev;  // de = conj(g) lambda
+      row[modes + m] = (-lr * gi + li * gr) * ev;
     }
     float *pp = polepart + (b * n_chunks + c) * 4 * modes;
     pp[m] = dar;
@@ -785,7 +791,8 @@ static int block_backward(const TrainPlan &tp, const float *states, const float 
                           const float *a_re, const float *a_im, const float *g_re,
                           const float *g_im, float *dxh, float dxh_beta, float *dframe,
                           float frame_beta, float *d_decay, float *d_freq, int64_t B, int64_t T,
-                          int D, int M, bool tf32, cudaStream_t st) {
+                          int D, int M, bool tf32, const float *event_mask, int obs_channels,
+                          cudaStream_t st) {
   const int64_t n_scan = cdiv(T, kScanChunk);
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   const dim3 gs((unsigned)n_scan, (unsigned)B);
@@ -796,7 +803,8 @@ static int block_backward(const TrainPlan &tp, const float *states, const float 
       tp.carries, B, M, n_scan, nullptr);
   LNET_TRY(after_launch("scan_carry_kernel"));
   rscan_apply_kernel<<<gs, threads, 0, st>>>(tp.dS, states, a_re, a_im, g_re, g_im, tp.carries,
-                                             tp.polepart, T, M, kScanChunk, n_scan);
+                                             tp.polepart, T, M, kScanChunk, n_scan, event_mask,
+                                             obs_channels);
   LNET_TRY(after_launch("rscan_apply_kernel"));
   LNET_TRY(colsum(ColPlain{tp.polepart, 4 * M}, B * n_scan, 4 * M, tp.colpart, tp.polesum, st,
                   "colsum(pole)"));
@@ -886,7 +894,8 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(block_backward(tp, tp.s2, tp.xh2, p->reader_frame, p->reader_raw_decay,
                           p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
                           tp.a_tab + 6 * M, tp.a_tab + 7 * M, tp.dX, 0.f, gd->reader_frame, 0.f,
-                          gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, tf32, st));
+                          gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, tf32,
+                          nullptr, 1, st));
   rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y2, tp.dX, p->reader_norm,
                                                              nullptr, tp.dY, tp.rs, bt, D);
   LNET_TRY(after_launch("rms_backward_kernel"));
@@ -922,7 +931,8 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(block_backward(tp, tp.s1, tp.xh1, p->writer_frame, p->writer_raw_decay,
                           p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
                           tp.a_tab + 5 * M, tp.dX, 1.f, gd->writer_frame, 1.f,
-                          gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, tf32, st));
+                          gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, tf32,
+                          r->observation_mask, r->obs_channels, st));
   // writer RMSNorm: dy1 = rms VJP + dv (residual identity)
   rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y1, tp.dX, p->writer_norm, tp.dV,
                                                              tp.dY, tp.rs, bt, D);
@@ -942,8 +952,7 @@ static int train_entry(const lnet_b200_alphabet_params *p, const lnet_b200_alpha
   LNET_TRY(check_params(p));
   LNET_TRY(check_request(p, r));
   if (!train_supported(r))
-    return fail(LNET_ERR_UNSUPPORTED,
-                "training path: time_delta and observation_mask are not supported");
+    return fail(LNET_ERR_UNSUPPORTED, "training path: time_delta is not supported");
   Arena ar(ws, ws_bytes);
   plan_train(ar, tp, p, r);
   if (!ws || !ar.ok())

@@ -315,16 +315,15 @@ class B200Alphabet(nn.Module):
             raise TypeError(f"inputs must be float32 or bfloat16, got {inputs.dtype}")
         if self.training and torch.is_grad_enabled():
             # training: the fp32 forward that keeps its activations, with the
-            # B200 backward (lnet_b200.training); static poles, no observation mask
-            if time_delta is not None or observation_mask is not None:
-                raise NotImplementedError(
-                    "training supports valid_mask only (no time_delta / observation_mask)")
+            # B200 backward (lnet_b200.training); static poles
+            if time_delta is not None:
+                raise NotImplementedError("training supports static poles only (no time_delta)")
             if return_moments:
                 raise NotImplementedError("return_moments is an inference option")
-            _, _, valid = self._prepare_metadata(inputs, None, None, valid_mask)
+            _, obs, valid = self._prepare_metadata(inputs, None, observation_mask, valid_mask)
             from .training import train_forward
 
-            return train_forward(self, inputs, valid).to(self.head.classifier.weight.dtype)
+            return train_forward(self, inputs, valid, obs).to(self.head.classifier.weight.dtype)
         delta, obs, valid = self._prepare_metadata(inputs, time_delta, observation_mask,
                                                    valid_mask)
         x = inputs.contiguous()

@@ -4,8 +4,8 @@ TEST INFRASTRUCTURE ONLY, like ``alphabet_oracle``: the ``-m gpu`` tests use
 it to check ``lnet_b200_alphabet_backward``; the product never imports it.
 
 Scope: the eager ``Alphabet.forward`` (src/lnet/alphabet.py:350-416) with
-static poles (no ``time_delta``), no observation mask, optional
-``valid_mask``; gradients of ``L = sum(logits * dlogits)`` with respect to
+static poles (no ``time_delta``), optional ``observation_mask`` (channel or
+event form) and ``valid_mask``; gradients of ``L = sum(logits * dlogits)`` with respect to
 every parameter, each frame's gradient taken at the materialised [D, 2M]
 weight.  It is pinned against gradients that the reference's own autograd
 produces (``tests/golden/make_grad_golden.py``,
@@ -143,9 +143,11 @@ def moments_backward(s_re, s_im, dm, valid=None):
     return gr, gi
 
 
-def scan_backward(a_re, a_im, g_re, g_im, s_re, s_im, ds_re, ds_im):
-    """Adjoint of ``s_t = a s_{t-1} + g e_t``: returns de (re, im) [B, T, M] and
-    the per-mode real-pair sums da, dg ([M] each, re and im)."""
+def scan_backward(a_re, a_im, g_re, g_im, s_re, s_im, ds_re, ds_im, event=None):
+    """Adjoint of ``s_t = a s_{t-1} + event_t g e_t``: returns de (re, im) [B, T, M]
+    and the per-mode real-pair sums da, dg ([M] each, re and im).  dg uses
+    u_t / g with u_t = s_t - a s_{t-1} (the masked drive, so no division by
+    the mask)."""
     b, t, m = s_re.shape
     lr = np.zeros((b, m), dtype=s_re.dtype)
     li = np.zeros((b, m), dtype=s_re.dtype)
@@ -169,6 +171,9 @@ def scan_backward(a_re, a_im, g_re, g_im, s_re, s_im, ds_re, ds_im):
     dg_im = np.sum(-lam_re * e_im + lam_im * e_re, axis=(0, 1))
     de_re = lam_re * g_re + lam_im * g_im
     de_im = -lam_re * g_im + lam_im * g_re
+    if event is not None:
+        de_re = de_re * event
+        de_im = de_im * event
     return de_re, de_im, (da_re, da_im), (dg_re, dg_im)
 
 
@@ -188,7 +193,7 @@ def pole_backward(raw_decay, raw_frequency, da, dg):
     return d_raw_decay, d_raw_frequency
 
 
-def _block_forward(x, params, prefix, valid):
+def _block_forward(x, params, prefix, valid, event=None):
     g = params[prefix + ".norm.weight"]
     frame = params[prefix + ".frame.weight"]
     m = frame.shape[1] // 2
@@ -199,9 +204,12 @@ def _block_forward(x, params, prefix, valid):
     a_re, a_im, g_re, g_im = discrete_pole_real2d(dmp, frq, 1.0, dtype=x.dtype)
     u_re = g_re * e[..., :m] - g_im * e[..., m:]
     u_im = g_re * e[..., m:] + g_im * e[..., :m]
+    if event is not None:
+        u_re, u_im = event * u_re, event * u_im
     s_re, s_im = recurrence(a_re, a_im, u_re, u_im)
     mom = modal_moments(s_re, s_im) if valid is None else masked_modal_moments(s_re, s_im, valid)
-    return dict(xh=xh, rs=rs, a=(a_re, a_im), g=(g_re, g_im), s=(s_re, s_im), mom=mom)
+    return dict(xh=xh, rs=rs, a=(a_re, a_im), g=(g_re, g_im), s=(s_re, s_im), mom=mom,
+                event=event)
 
 
 def _block_backward(x, params, prefix, st, dmom, valid, extra_ds=None):
@@ -212,7 +220,7 @@ def _block_backward(x, params, prefix, st, dmom, valid, extra_ds=None):
     if extra_ds is not None:
         gr = gr + extra_ds[..., :m]
         gi = gi + extra_ds[..., m:]
-    de_re, de_im, da, dg = scan_backward(*st["a"], *st["g"], s_re, s_im, gr, gi)
+    de_re, de_im, da, dg = scan_backward(*st["a"], *st["g"], s_re, s_im, gr, gi, st["event"])
     de = np.concatenate([de_re, de_im], axis=-1)
     dxh = de @ frame.T
     dframe = np.einsum("btd,btj->dj", st["xh"], de)
@@ -220,20 +228,27 @@ def _block_backward(x, params, prefix, st, dmom, valid, extra_ds=None):
     return dxh, dframe, draw
 
 
-def alphabet_backward(x, params, dlogits, *, valid_mask=None, dtype=np.float64):
+def alphabet_backward(x, params, dlogits, *, observation_mask=None, valid_mask=None,
+                      dtype=np.float64):
     """Gradients of ``sum(logits * dlogits)``, keyed like ``state_dict``."""
     p = {k: np.asarray(v, dtype=dtype) for k, v in params.items()}
     x = np.asarray(x, dtype=dtype)
     dlogits = np.asarray(dlogits, dtype=dtype)
     valid = None if valid_mask is None else np.asarray(valid_mask, dtype=dtype)[..., None]
     vm = 1.0 if valid is None else valid
+    raw_obs = event = None
+    if observation_mask is not None:  # src/lnet/alphabet_backbone.py:538-569
+        raw_obs = np.asarray(observation_mask, dtype=dtype)
+        if raw_obs.ndim == 2:
+            raw_obs = raw_obs[..., None]
+        event = raw_obs if raw_obs.shape[-1] == 1 else raw_obs.max(axis=-1, keepdims=True)
     m = p["forward_block.frame.weight"].shape[1] // 2
     # forward with the saved activations
-    stem_in = x * vm
+    stem_in = x * vm if raw_obs is None else x * raw_obs * vm
     proj = stem_in @ p["stem.projection.weight"].T
     z1 = same_length_dwconv(proj, p["stem.local.weight"], p["stem.local.bias"])
     y1 = z1 * sigmoid(z1) * vm
-    w_st = _block_forward(y1, p, "forward_block", valid)
+    w_st = _block_forward(y1, p, "forward_block", valid, event)
     s1 = np.concatenate(w_st["s"], axis=-1)
     modal = s1 @ p["forward_block.frame.weight"].T
     ls, ds = p["forward_block.layer_scale"], p["forward_block.direct_scale"]

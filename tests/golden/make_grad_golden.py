@@ -9,7 +9,8 @@ Each case builds the same seeded, perturbed ``lnet.Alphabet`` as
 forward with autograd and differentiates ``L = sum(logits * dlogits)`` for a
 seeded ``dlogits``.  Stored in ``tests/golden/<case>.npz``:
 
-* ``in.x``, ``in.dlogits`` (and ``in.valid_mask`` when present),
+* ``in.x``, ``in.dlogits`` (and ``in.valid_mask`` / ``in.observation_mask``
+  when present),
 * ``p.*``  parameters keyed by ``state_dict`` name (float32 values; the
            float64 model is built from exactly these), with each block frame
            materialised as ``p.<block>.frame.weight`` ([D, 2M]),
@@ -42,9 +43,9 @@ from make_golden import build_alphabet, make_inputs, params_of  # noqa: E402
 torch.set_num_threads(4)
 
 
-def run_grad_case(name, *, b, t, cin, d, m, k, seed, real_poles=False, valid=False):
+def run_grad_case(name, *, b, t, cin, d, m, k, seed, real_poles=False, valid=False, obs=None):
     model = build_alphabet(cin=cin, d=d, m=m, k=k, t=t, seed=seed, real_poles=real_poles)
-    x, meta = make_inputs(b=b, t=t, cin=cin, seed=seed, valid=valid)
+    x, meta = make_inputs(b=b, t=t, cin=cin, seed=seed, valid=valid, obs=obs)
     params = params_of(model)  # float32 values, the pin for both sides
     model = model.double()
     # evaluate the reference's float32 function at exactly these values, in
@@ -85,6 +86,8 @@ def main():
     run_grad_case("grad_real_poles", b=2, t=67, seed=2, real_poles=True, **common)
     run_grad_case("grad_long", b=2, t=300, seed=8, **common)
     run_grad_case("grad_valid", b=4, t=45, seed=3, valid=True, **common)
+    run_grad_case("grad_obs_channel", b=3, t=70, seed=4, obs="channel", valid=True, **common)
+    run_grad_case("grad_obs_event", b=3, t=40, seed=5, obs="event", **common)
 
 
 if __name__ == "__main__":

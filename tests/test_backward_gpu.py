@@ -8,7 +8,7 @@ training mode runs ``lnet_b200_alphabet_train_forward`` and, on
 1e-5 relative, every parameter gradient 2e-4 relative (normwise per tensor;
 fp32 against float64 over sequences up to 300 steps).  Also: the training
 forward equals the inference forward; the oracle VJP agrees at a size the
-goldens do not cover; the unsupported metadata raises.
+goldens do not cover; time_delta (not supported in training) raises.
 """
 
 from __future__ import annotations
@@ -23,7 +23,8 @@ from oracle import alphabet_grad_oracle as G
 
 pytestmark = pytest.mark.gpu
 
-CASES = ["grad_plain", "grad_real_poles", "grad_long", "grad_valid"]
+CASES = ["grad_plain", "grad_real_poles", "grad_long", "grad_valid", "grad_obs_channel",
+         "grad_obs_event"]
 
 
 def _model(z, device):
@@ -33,9 +34,9 @@ def _model(z, device):
     return model.to(device).train()
 
 
-def _grads(model, x, dlogits, valid=None):
+def _grads(model, x, dlogits, valid=None, obs=None):
     model.zero_grad(set_to_none=True)
-    logits = model(x, valid_mask=valid)
+    logits = model(x, valid_mask=valid, observation_mask=obs)
     (logits * dlogits).sum().backward()
     out = {name: p.grad for name, p in model.named_parameters() if p.grad is not None}
     return logits.detach(), out
@@ -48,7 +49,9 @@ def test_backward_matches_reference_autograd(name, cuda_device):
     x = torch.from_numpy(z["in.x"]).to(cuda_device)
     dl = torch.from_numpy(z["in.dlogits"]).to(cuda_device)
     valid = torch.from_numpy(z["in.valid_mask"]).to(cuda_device) if "in.valid_mask" in z else None
-    logits, grads = _grads(model, x, dl, valid)
+    obs = (torch.from_numpy(z["in.observation_mask"]).to(cuda_device)
+           if "in.observation_mask" in z else None)
+    logits, grads = _grads(model, x, dl, valid, obs)
     assert rel_err(logits.cpu().numpy(), z["out.logits"]) <= 1e-5
     checked = 0
     for key in z:
