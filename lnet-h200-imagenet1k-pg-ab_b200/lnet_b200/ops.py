@@ -21,6 +21,12 @@ known output shape.  This module gives the B200 path the same surface:
 * ``lnet_b200::patchify_images(images, mean, std, patch, dtype) -> tokens`` —
   ``lnet_b200_patchify_images``.
 
+``lnet_b200::alphabet_forward`` also carries ``register_autograd`` (the
+reference's ops register their VJPs the same way,
+src/lnet/pac_triton_recurrence_op.py:646-684): its backward reruns the fp32
+training forward on the saved inputs and calls ``lnet_b200_alphabet_backward``
+(static poles; the op itself keeps no activations).
+
 Launches are ordered on the current torch stream with no host synchronisation.
 There is no CPU implementation: a CPU input raises ``RuntimeError``.
 """
@@ -134,6 +140,35 @@ def _alphabet_forward_fake(x, weights, dims, time_delta=None, observation_mask=N
                            valid_mask=None):
     _check_alphabet_args(x, weights, dims, time_delta, observation_mask, valid_mask)
     return x.new_empty((x.shape[0], int(dims[3])), dtype=torch.float32)
+
+
+def _alphabet_setup_context(ctx, inputs, output):
+    x, weights, dims, time_delta, observation_mask, valid_mask = inputs
+    ctx.save_for_backward(x, *weights)
+    ctx.dims = tuple(int(v) for v in dims)
+    ctx.meta = (time_delta, observation_mask, valid_mask)
+
+
+def _alphabet_backward(ctx, dlogits):
+    """Gradients for the 17 weights: the training forward is rerun on the saved
+    inputs (the op keeps no activations, like activation checkpointing), then
+    lnet_b200_alphabet_backward.  Static poles only (no time_delta)."""
+    from .training import AlphabetTrainFunction
+
+    x, *weights = ctx.saved_tensors
+    time_delta, obs, valid = ctx.meta
+    if time_delta is not None:
+        raise NotImplementedError("lnet_b200::alphabet_forward: no backward for time_delta")
+    with torch.enable_grad():
+        leaves = [w.detach().requires_grad_(True) for w in weights]
+        logits = AlphabetTrainFunction.apply(x, valid, obs, ctx.dims, *leaves)
+        grads = torch.autograd.grad(logits, leaves, dlogits)
+    # the structure of the arguments actually passed (optional arguments left
+    # at their defaults are not part of it): x, weights, dims, [metadata...]
+    return (None, list(grads)) + (None,) * (len(ctx.needs_input_grad) - 2)
+
+
+alphabet_forward.register_autograd(_alphabet_backward, setup_context=_alphabet_setup_context)
 
 
 def _check_laplace_args(x, raw_decay, residues, direct_term, bias) -> None:

@@ -79,6 +79,25 @@ def test_opcheck_and_compile(cuda_device):
     assert rel_err(got.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
 
 
+def test_alphabet_op_autograd(cuda_device):
+    """Gradients through the op (register_autograd) equal the module's training
+    gradients of the same loss."""
+    cfg, model = _small(cuda_device, b=2, dtype="fp32")
+    x = bench.make_inputs(cfg, cuda_device)
+    dl = torch.randn(2, cfg["K"], device=cuda_device)
+    weights, dims = model.op_arguments()
+    leaves = [w.detach().clone().requires_grad_(True) for w in weights]
+    logits = torch.ops.lnet_b200.alphabet_forward(x, leaves, dims)
+    op_grads = torch.autograd.grad((logits * dl).sum(), leaves)
+    from lnet_b200.training import AlphabetTrainFunction
+
+    leaves2 = [w.detach().clone().requires_grad_(True) for w in weights]
+    ref = AlphabetTrainFunction.apply(x, None, None, tuple(dims), *leaves2)
+    ref_grads = torch.autograd.grad((ref * dl).sum(), leaves2)
+    for a, b in zip(op_grads, ref_grads):
+        assert rel_err(a.cpu().numpy(), b.cpu().numpy()) <= 1e-6
+
+
 def test_laplace_op_bit_identical(cuda_device):
     c, per = 4, 3
     g = torch.Generator().manual_seed(1)
