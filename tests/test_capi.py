@@ -48,3 +48,47 @@ def test_error_paths_without_gpu():
     st = lib.lnet_b200_laplace_workspace_size(2, 8, 4, 3, ctypes.byref(n))
     assert st == _lib.LNET_OK and n.value > 0
     assert lib.lnet_b200_version().startswith(b"lnet_b200")
+
+
+def _struct_fields(name: str) -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "lnet_b200.h").read_text(), flags=re.S)
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), text, flags=re.S)
+    assert body, name
+    return re.findall(r"(\w+)\s*;", body.group(1))
+
+
+def test_struct_layouts_match_header():
+    """The ctypes mirrors list the header's fields in the header's order."""
+    from lnet_b200 import _lib
+
+    for cname, py in (("lnet_b200_alphabet_params", _lib.AlphabetParams),
+                      ("lnet_b200_alphabet_request", _lib.AlphabetRequest),
+                      ("lnet_b200_alphabet_grads", _lib.AlphabetGrads)):
+        assert _struct_fields(cname) == [f for f, _ in py._fields_], cname
+
+
+def test_training_error_paths_without_gpu():
+    """The training entry points validate before any CUDA call: time_delta is
+    refused (LNET_ERR_UNSUPPORTED), a missing workspace is reported, and the
+    workspace size is computed on the host."""
+    from lnet_b200 import _lib
+
+    lib = _lib.load()
+    dummy = 256  # non-NULL pointers are never dereferenced on these paths
+    params = _lib.AlphabetParams(raw_input_dim=4, model_dim=8, modes=4, output_dim=3,
+                                 conv_kernel=5, conv_dilation=4,
+                                 **{n: dummy for n in _lib.PARAM_POINTER_FIELDS})
+    req = _lib.AlphabetRequest(batch=2, steps=10, x_dtype=_lib.LNET_F32, act_dtype=_lib.LNET_F32,
+                               x=dummy, obs_channels=1)
+    n = ctypes.c_size_t(0)
+    assert lib.lnet_b200_alphabet_train_workspace_size(ctypes.byref(params), ctypes.byref(req),
+                                                       ctypes.byref(n)) == _lib.LNET_OK
+    assert n.value > 0
+    st = lib.lnet_b200_alphabet_train_forward(ctypes.byref(params), ctypes.byref(req), None, 0,
+                                              dummy, None)
+    assert st == _lib.LNET_ERR_WORKSPACE
+    req.time_delta = dummy
+    st = lib.lnet_b200_alphabet_train_forward(ctypes.byref(params), ctypes.byref(req), None, 0,
+                                              dummy, None)
+    assert st == _lib.LNET_ERR_UNSUPPORTED
+    assert "time_delta" in _lib.last_error()
