@@ -71,7 +71,10 @@ static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params
   tp.dm = f((size_t)2 * B * 7 * M);
   tp.counts = f((size_t)B * 4);
   const int64_t wg_parts = B * cdiv(std::max<int64_t>(r->steps, 1), kCbTile);
-  tp.colpart = f((size_t)std::max<int64_t>((int64_t)kColParts * 6 * std::max({D, C, 14 * M, K}),
+  // widest column reduction: 4M pole sums, D * taps conv weights (generic
+  // kernels), 14M / K / C / D otherwise; or the fused conv VJP's partials
+  const int64_t widest = std::max<int64_t>({(int64_t)D * (p->conv_kernel + 1), 14 * M, 4 * M, C, K});
+  tp.colpart = f((size_t)std::max<int64_t>((int64_t)kColParts * widest,
                                            wg_parts * D * (p->conv_kernel + 1)));
   tp.polepart = f((size_t)B * n_scan * 4 * M);
   tp.polesum = f((size_t)std::max(4 * M, D * (p->conv_kernel + 1)));
