@@ -229,7 +229,7 @@ def _block_backward(x, params, prefix, st, dmom, valid, extra_ds=None):
 
 
 def alphabet_backward(x, params, dlogits, *, observation_mask=None, valid_mask=None,
-                      dtype=np.float64):
+                      dilation=4, dtype=np.float64):
     """Gradients of ``sum(logits * dlogits)``, keyed like ``state_dict``."""
     p = {k: np.asarray(v, dtype=dtype) for k, v in params.items()}
     x = np.asarray(x, dtype=dtype)
@@ -246,7 +246,7 @@ def alphabet_backward(x, params, dlogits, *, observation_mask=None, valid_mask=N
     # forward with the saved activations
     stem_in = x * vm if raw_obs is None else x * raw_obs * vm
     proj = stem_in @ p["stem.projection.weight"].T
-    z1 = same_length_dwconv(proj, p["stem.local.weight"], p["stem.local.bias"])
+    z1 = same_length_dwconv(proj, p["stem.local.weight"], p["stem.local.bias"], dilation)
     y1 = z1 * sigmoid(z1) * vm
     w_st = _block_forward(y1, p, "forward_block", valid, event)
     s1 = np.concatenate(w_st["s"], axis=-1)
@@ -254,7 +254,7 @@ def alphabet_backward(x, params, dlogits, *, observation_mask=None, valid_mask=N
     ls, ds = p["forward_block.layer_scale"], p["forward_block.direct_scale"]
     v = y1 + ls * (modal + ds * w_st["xh"])
     rin = v * vm
-    z2 = same_length_dwconv(rin, p["second_local.weight"], p["second_local.bias"])
+    z2 = same_length_dwconv(rin, p["second_local.weight"], p["second_local.bias"], dilation)
     y2 = z2 * sigmoid(z2) * vm
     r_st = _block_forward(y2, p, "backward_block", valid)
     feats = np.concatenate([radial_log_lag124(w_st["mom"], m),
@@ -273,7 +273,7 @@ def alphabet_backward(x, params, dlogits, *, observation_mask=None, valid_mask=N
         y2, r_st["rs"], p["backward_block.norm.weight"], dxh2)
     dz2 = dy2 * vm * silu_grad(z2)
     drin, grads["second_local.weight"], grads["second_local.bias"] = conv_backward(
-        rin, p["second_local.weight"], dz2)
+        rin, p["second_local.weight"], dz2, dilation)
     dv = drin * vm
     # writer: synthesis + residual, then the block
     dmodal = ls * dv
@@ -290,7 +290,7 @@ def alphabet_backward(x, params, dlogits, *, observation_mask=None, valid_mask=N
     dy1 = dv + dy1_norm
     dz1 = dy1 * vm * silu_grad(z1)
     dproj, grads["stem.local.weight"], grads["stem.local.bias"] = conv_backward(
-        proj, p["stem.local.weight"], dz1)
+        proj, p["stem.local.weight"], dz1, dilation)
     grads["stem.projection.weight"] = np.einsum("btd,btc->dc", dproj, stem_in)
     return grads
 

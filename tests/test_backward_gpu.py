@@ -75,12 +75,18 @@ def test_training_forward_equals_inference(cuda_device):
     assert rel_err(train_logits.cpu().numpy(), infer.cpu().numpy()) <= 1e-5
 
 
-def test_backward_larger_case_against_oracle(cuda_device):
-    """Several scan chunks per row, D = 32, M = 16, a valid mask with ragged
-    lengths: the CUDA backward against the float64 oracle VJP."""
+@pytest.mark.parametrize("shape", [
+    dict(b=3, t=517, cin=8, d=32, m=16, k=6, ksize=5, dil=4),  # several chunks, fused conv VJP
+    dict(b=2, t=150, cin=5, d=30, m=8, k=4, ksize=3, dil=2),   # generic conv kernels, 4 !| D
+])
+def test_backward_larger_case_against_oracle(cuda_device, shape):
+    """Several scan chunks per row and a valid mask with ragged lengths (and a
+    non-canonical conv that takes the generic kernels): the CUDA backward
+    against the float64 oracle VJP."""
     g = torch.Generator().manual_seed(21)
-    b, t, cin, d, m, k = 3, 517, 8, 32, 16, 6
-    model = B200Alphabet(AlphabetConfig(cin, d, m, k), k)
+    b, t, cin, d, m, k = (shape[n] for n in ("b", "t", "cin", "d", "m", "k"))
+    model = B200Alphabet(AlphabetConfig(cin, d, m, k), k, dwconv_kernel_size=shape["ksize"],
+                         dwconv_dilation=shape["dil"])
     with torch.no_grad():
         for blk in (model.forward_block, model.backward_block):
             blk.raw_decay.copy_(torch.randn(m, generator=g) * 2.0)
@@ -94,7 +100,7 @@ def test_backward_larger_case_against_oracle(cuda_device):
     for blk in (model.forward_block, model.backward_block):  # plain frames: comparable grads
         B200Alphabet._set_frame(blk, blk.frame_matrix().detach())
     x = torch.randn(b, t, cin, generator=g)
-    lengths = torch.tensor([t, 300, 77])
+    lengths = torch.tensor([t, 300, 77][:b])
     valid = (torch.arange(t).view(1, -1) < lengths.view(-1, 1)).float()
     dl = torch.randn(b, k, generator=g)
     model = model.to(cuda_device).train()
@@ -102,7 +108,8 @@ def test_backward_larger_case_against_oracle(cuda_device):
     params = {n: p.detach().cpu().numpy() for n, p in model.named_parameters()}
     params.update({n: model.get_buffer(n).cpu().numpy()
                    for n in ("backward_block.direct_scale", "backward_block.layer_scale")})
-    ref = G.alphabet_backward(x.numpy(), params, dl.numpy(), valid_mask=valid.numpy())
+    ref = G.alphabet_backward(x.numpy(), params, dl.numpy(), valid_mask=valid.numpy(),
+                              dilation=shape["dil"])
     assert len(ref) == 17
     for name, gref in ref.items():
         got = grads[name].cpu().numpy().reshape(gref.shape)
