@@ -9,8 +9,8 @@ Each case builds the same seeded, perturbed ``lnet.Alphabet`` as
 forward with autograd and differentiates ``L = sum(logits * dlogits)`` for a
 seeded ``dlogits``.  Stored in ``tests/golden/<case>.npz``:
 
-* ``in.x``, ``in.dlogits`` (and ``in.valid_mask`` / ``in.observation_mask``
-  when present),
+* ``in.x``, ``in.dlogits`` (and ``in.time_delta`` / ``in.valid_mask`` /
+  ``in.observation_mask`` when present),
 * ``p.*``  parameters keyed by ``state_dict`` name (float32 values; the
            float64 model is built from exactly these), with each block frame
            materialised as ``p.<block>.frame.weight`` ([D, 2M]),
@@ -43,9 +43,10 @@ from make_golden import build_alphabet, make_inputs, params_of  # noqa: E402
 torch.set_num_threads(4)
 
 
-def run_grad_case(name, *, b, t, cin, d, m, k, seed, real_poles=False, valid=False, obs=None):
+def run_grad_case(name, *, b, t, cin, d, m, k, seed, real_poles=False, valid=False, obs=None,
+                  delta=False):
     model = build_alphabet(cin=cin, d=d, m=m, k=k, t=t, seed=seed, real_poles=real_poles)
-    x, meta = make_inputs(b=b, t=t, cin=cin, seed=seed, valid=valid, obs=obs)
+    x, meta = make_inputs(b=b, t=t, cin=cin, seed=seed, valid=valid, obs=obs, delta=delta)
     params = params_of(model)  # float32 values, the pin for both sides
     model = model.double()
     # evaluate the reference's float32 function at exactly these values, in
@@ -88,6 +89,9 @@ def main():
     run_grad_case("grad_valid", b=4, t=45, seed=3, valid=True, **common)
     run_grad_case("grad_obs_channel", b=3, t=70, seed=4, obs="channel", valid=True, **common)
     run_grad_case("grad_obs_event", b=3, t=40, seed=5, obs="event", **common)
+    run_grad_case("grad_delta", b=3, t=60, seed=6, delta=True, **common)
+    run_grad_case("grad_all_meta", b=3, t=64, seed=7, delta=True, obs="channel", valid=True,
+                  **common)
 
 
 if __name__ == "__main__":

@@ -16,7 +16,7 @@ from conftest import golden_params, load_golden, rel_err
 from oracle import alphabet_grad_oracle as G
 
 CASES = ["grad_plain", "grad_real_poles", "grad_long", "grad_valid", "grad_obs_channel",
-         "grad_obs_event"]
+         "grad_obs_event", "grad_delta", "grad_all_meta"]
 
 
 @pytest.mark.parametrize("name", CASES)
@@ -24,6 +24,7 @@ def test_grad_oracle_matches_reference(name):
     z = load_golden(name)
     params = golden_params(z)
     grads = G.alphabet_backward(z["in.x"], params, z["in.dlogits"],
+                                time_delta=z.get("in.time_delta"),
                                 observation_mask=z.get("in.observation_mask"),
                                 valid_mask=z.get("in.valid_mask"))
     for key in z:
