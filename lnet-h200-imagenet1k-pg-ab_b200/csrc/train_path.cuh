@@ -1,6 +1,6 @@
 // Training path of the general route: a forward that keeps its activations
-// and the backward pass (VJP) of every stage, for static-pole requests
-// (observation and valid masks allowed), all in fp32.
+// and the backward pass (VJP) of every stage, for every metadata combination
+// (time_delta, observation and valid masks), all in fp32.
 //
 // Forward (lnet_b200_alphabet_train_forward): the general-route stages with
 // separate buffers per block, full-fp32 GEMMs.  Kept in the workspace:
@@ -28,7 +28,7 @@ struct TrainPlan {
   float *x32, *proj, *y1, *xh1, *s1, *modal, *v, *y2, *xh2, *s2;
   float *m1, *m2, *feats, *a_tab;  // a_tab: [8][M] as in the general route
   // scratch
-  float *carries, *partial, *wfold, *head_partial;
+  float *carries, *partial, *wfold, *head_partial, *ts, *ptcounts;
   float *dS, *dX, *dY, *dV, *rs, *dfeats, *dm, *counts, *colpart, *polepart, *polesum, *wls;
 };
 
@@ -59,7 +59,9 @@ static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params
   tp.feats = f((size_t)B * 14 * M);
   tp.a_tab = f((size_t)8 * M);
   tp.carries = f((size_t)B * n_scan * kRecFloats * M);
-  tp.partial = f((size_t)B * n_scan * 7 * M);
+  tp.partial = f((size_t)B * n_scan * (8 * M + 5));  // physical-time partials are widest
+  tp.ts = f((size_t)bt);
+  tp.ptcounts = f((size_t)B * 8);
   tp.wfold = f((size_t)D * 2 * M);
   tp.head_partial = f(head_partial_floats(B, K));
   tp.dS = f((size_t)bt * 2 * M);
@@ -81,11 +83,12 @@ static void plan_train(Arena &ar, TrainPlan &tp, const lnet_b200_alphabet_params
   tp.wls = f((size_t)D * 2 * M);
 }
 
-static bool train_supported(const lnet_b200_alphabet_request *r) { return !r->time_delta; }
+static bool train_supported(const lnet_b200_alphabet_request *) { return true; }
 
 // A Plan view of the training buffers for block_scan_moments.
 static Plan block_view(const TrainPlan &tp, float *xhat, float *states) {
   Plan pl;
+  pl.ts = tp.ts;
   pl.xhat = xhat;
   pl.drive = states;
   pl.carries = tp.carries;
@@ -110,9 +113,18 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(after_launch("mask_inputs_kernel"));
   LNET_TRY(gemm_rows(st, tp.x32, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, tp.proj, D,
                      bt, D, C, tf32, "cublas(stem)"));
-  LNET_TRY(depthwise_conv(tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
-                          tp.y1, B, T, D, p->conv_kernel, p->conv_dilation, st,
-                          "depthwise_conv(stem)"));
+  if (r->time_delta) {  // physical-time convs and moments
+    timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, tp.ts, B, T);
+    LNET_TRY(after_launch("timestamps_kernel"));
+    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
+        tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, tp.ts, r->valid_mask, tp.y1, T,
+        D, p->conv_kernel, p->conv_dilation);
+    LNET_TRY(after_launch("dwconv_physical_kernel(stem)"));
+  } else {
+    LNET_TRY(depthwise_conv(tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr,
+                            r->valid_mask, tp.y1, B, T, D, p->conv_kernel, p->conv_dilation, st,
+                            "depthwise_conv(stem)"));
+  }
   Plan pw = block_view(tp, tp.xh1, tp.s1);
   LNET_TRY(block_scan_moments(tp.y1, p->writer_norm, p->writer_frame, p->writer_raw_decay,
                               p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
@@ -123,9 +135,16 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
       tp.y1, tp.xh1, tp.modal, p->writer_direct_scale, p->writer_layer_scale, tp.v, bt, D);
   LNET_TRY(after_launch("residual_kernel"));
-  LNET_TRY(depthwise_conv(tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
-                          r->valid_mask, tp.y2, B, T, D, p->conv_kernel, p->conv_dilation, st,
-                          "depthwise_conv(reader)"));
+  if (r->time_delta) {
+    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
+        tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, tp.ts, r->valid_mask,
+        tp.y2, T, D, p->conv_kernel, p->conv_dilation);
+    LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
+  } else {
+    LNET_TRY(depthwise_conv(tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
+                            r->valid_mask, tp.y2, B, T, D, p->conv_kernel, p->conv_dilation, st,
+                            "depthwise_conv(reader)"));
+  }
   Plan pr = block_view(tp, tp.xh2, tp.s2);
   LNET_TRY(block_scan_moments(tp.y2, p->reader_norm, p->reader_frame, p->reader_raw_decay,
                               p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
@@ -390,28 +409,55 @@ __global__ void moments_backward_kernel(const float *__restrict__ s, const float
 }
 
 // Reverse scan, local pass: per (chunk, row), lambda from a zero state after
-// the chunk walked backwards; records at the reversed chunk index so that
-// scan_carry_kernel (forward composition order) yields each chunk's lambda
-// entering from the later steps.  Record: E = local lambda at the chunk start,
-// P = conj(a)^len.
+// the chunk walked backwards (lambda_t = dS_t + conj(a_{t+1}) lambda_{t+1};
+// a per mode, or per step from dt); records at the reversed chunk index so
+// that scan_carry_kernel (forward composition order) yields each chunk's
+// lambda entering from the later steps.  Record: E = local lambda at the
+// chunk start, P = the product of the conj(a_{t+1}) of the chunk.
+// Pole coefficients of step `tok` for mode m: the per-mode tables, or the ZOH
+// of that step's dt (double, rounded once).
+__device__ __forceinline__ Zoh step_zoh(const float *a_re, const float *a_im, const float *g_re,
+                                        const float *g_im, const float *raw_decay,
+                                        const float *raw_freq, const float *dt, int64_t tok,
+                                        int m) {
+  if (!dt) return Zoh{a_re[m], a_im[m], g_re ? g_re[m] : 0.f, g_im ? g_im[m] : 0.f};
+  double damping, frequency;
+  mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+  return zoh_eval(damping, frequency, (double)dt[tok]);
+}
+
 __global__ void rscan_local_kernel(const float *__restrict__ dS, const float *__restrict__ a_re,
-                                   const float *__restrict__ a_im, float *__restrict__ rec_all,
+                                   const float *__restrict__ a_im,
+                                   const float *__restrict__ raw_decay,
+                                   const float *__restrict__ raw_freq,
+                                   const float *__restrict__ dt, float *__restrict__ rec_all,
                                    int64_t steps, int modes, int chunk, int64_t n_chunks) {
   const int64_t c = blockIdx.x, b = blockIdx.y;
   const int64_t t0 = c * chunk, t1 = min(steps, t0 + chunk);
   const int64_t M2 = 2 * modes;
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    const float ar = a_re[m], ai = a_im[m];
+    // (nar, nai) = a_{t+1}, the coefficient that carries lambda_{t+1} back to t
+    float nar = 0.f, nai = 0.f;
+    if (t1 < steps) {
+      const Zoh z = step_zoh(a_re, a_im, nullptr, nullptr, raw_decay, raw_freq, dt,
+                             b * steps + t1, m);
+      nar = z.a_re;
+      nai = z.a_im;
+    }
     float lr = 0.f, li = 0.f, pr = 1.f, pi = 0.f;
     for (int64_t t = t1 - 1; t >= t0; --t) {
       const float *row = dS + (b * steps + t) * M2;
-      const float nr = row[m] + ar * lr + ai * li;
-      const float ni = row[modes + m] + ar * li - ai * lr;
+      const float nr = row[m] + nar * lr + nai * li;
+      const float ni = row[modes + m] + nar * li - nai * lr;
       lr = nr;
       li = ni;
-      const float qr = ar * pr + ai * pi, qi = ar * pi - ai * pr;  // conj(a) P
+      const float qr = nar * pr + nai * pi, qi = nar * pi - nai * pr;  // conj(a_{t+1}) P
       pr = qr;
       pi = qi;
+      const Zoh z = step_zoh(a_re, a_im, nullptr, nullptr, raw_decay, raw_freq, dt,
+                             b * steps + t, m);
+      nar = z.a_re;
+      nai = z.a_im;
     }
     float *rec = rec_all + (b * n_chunks + (n_chunks - 1 - c)) * kRecFloats * modes;
     rec[m] = lr;
@@ -422,14 +468,17 @@ __global__ void rscan_local_kernel(const float *__restrict__ dS, const float *__
 }
 
 // Reverse scan, apply pass: walks each chunk backwards from the lambda that
-// enters it, writes de = conj(g) lambda (times the writer's event mask) over
+// enters it, writes de = conj(g_t) lambda (times the writer's event mask) over
 // dS, and sums per (row, chunk, mode) da = lambda x s_{t-1} and dg = lambda x
-// u_t / g (real-pair form; u_t = s_t - a s_{t-1}, the masked drive) into
-// polepart [B, nchunk, 4, M].
+// u_t / g_t (real-pair form; u_t = s_t - a_t s_{t-1}, the masked drive) into
+// polepart [B, nchunk, 4, M].  With per-step coefficients (dt) it sums dL/dp
+// directly instead (slots 0, 1), the derivatives of a and g depending on dt.
 __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restrict__ s,
                                    const float *__restrict__ a_re, const float *__restrict__ a_im,
                                    const float *__restrict__ g_re, const float *__restrict__ g_im,
-                                   const float *__restrict__ rec_all,
+                                   const float *__restrict__ raw_decay,
+                                   const float *__restrict__ raw_freq,
+                                   const float *__restrict__ dt, const float *__restrict__ rec_all,
                                    float *__restrict__ polepart, int64_t steps, int modes,
                                    int chunk, int64_t n_chunks,
                                    const float *__restrict__ event_mask, int obs_channels) {
@@ -437,44 +486,88 @@ __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restri
   const int64_t t0 = c * chunk, t1 = min(steps, t0 + chunk);
   const int64_t M2 = 2 * modes;
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    const float ar = a_re[m], ai = a_im[m], gr = g_re[m], gi = g_im[m];
-    const float gden = gr * gr + gi * gi;
+    double pdr = 0.0, pdi = 0.0;  // dL/dp (dt) or the da, dg sums (static)
+    double pr_ = 0.0, pi_ = 0.0;  // the pole p (dt)
+    if (dt) {
+      double damping, frequency;
+      mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+      pr_ = -damping;
+      pi_ = frequency;
+    }
     const float *rec = rec_all + (b * n_chunks + (n_chunks - 1 - c)) * kRecFloats * modes;
     float lr = rec[m], li = rec[modes + m];  // lambda_{t1}
+    float nar = 0.f, nai = 0.f;                // a_{t+1}
+    if (t1 < steps) {
+      const Zoh z = step_zoh(a_re, a_im, g_re, g_im, raw_decay, raw_freq, dt, b * steps + t1, m);
+      nar = z.a_re;
+      nai = z.a_im;
+    }
     float dar = 0.f, dai = 0.f, dgr = 0.f, dgi = 0.f;
     for (int64_t t = t1 - 1; t >= t0; --t) {
-      float *row = dS + (b * steps + t) * M2;
-      const float nr = row[m] + ar * lr + ai * li;
-      const float ni = row[modes + m] + ar * li - ai * lr;
+      const int64_t tok = b * steps + t;
+      float *row = dS + tok * M2;
+      const float nr = row[m] + nar * lr + nai * li;
+      const float ni = row[modes + m] + nar * li - nai * lr;
       lr = nr;
       li = ni;
-      const float *st_ = s + (b * steps + t) * M2;
+      const Zoh z = step_zoh(a_re, a_im, g_re, g_im, raw_decay, raw_freq, dt, tok, m);
+      const float ar = z.a_re, ai = z.a_im, gr = z.g_re, gi = z.g_im;
+      const float *st_ = s + tok * M2;
       const float sr = st_[m], si = st_[modes + m];
       float pr = 0.f, pi = 0.f;
       if (t > 0) {
         pr = st_[m - M2];
         pi = st_[modes + m - M2];
       }
-      dar += lr * pr + li * pi;
-      dai += -lr * pi + li * pr;
+      const float ddr = lr * pr + li * pi, ddi = -lr * pi + li * pr;  // da at this step
       const float ur = sr - (ar * pr - ai * pi), ui = si - (ai * pr + ar * pi);
+      const float gden = gr * gr + gi * gi;
       const float er = (ur * gr + ui * gi) / gden, ei = (ui * gr - ur * gi) / gden;
-      dgr += lr * er + li * ei;
-      dgi += -lr * ei + li * er;
+      const float dgr_ = lr * er + li * ei, dgi_ = -lr * ei + li * er;  // dg at this step
+      if (dt) {
+        // dL/dp += Re/Im pairs with a'(p) = dt a and g'(p) = (dt a p - (a - 1)) / p^2
+        const double h = (double)dt[tok];
+        const double far = h * ar, fai = h * ai;
+        double fgr = 0.0, fgi = 0.0;
+        if (sqrt(pr_ * pr_ + pi_ * pi_) * h >= 1.0e-6) {
+          const double apr = ar * pr_ - ai * pi_, api = ar * pi_ + ai * pr_;
+          const double nr2 = h * apr - (ar - 1.0), ni2 = h * api - ai;
+          const double p2r = pr_ * pr_ - pi_ * pi_, p2i = 2.0 * pr_ * pi_;
+          const double den = p2r * p2r + p2i * p2i;
+          fgr = (nr2 * p2r + ni2 * p2i) / den;
+          fgi = (ni2 * p2r - nr2 * p2i) / den;
+        }
+        pdr += ddr * far + ddi * fai + dgr_ * fgr + dgi_ * fgi;
+        pdi += -ddr * fai + ddi * far - dgr_ * fgi + dgi_ * fgr;
+      } else {
+        dar += ddr;
+        dai += ddi;
+        dgr += dgr_;
+        dgi += dgi_;
+      }
       float ev = 1.f;  // u = event g e: de carries the event mask (amax over channels)
       if (event_mask) {
-        const float *om = event_mask + (b * steps + t) * obs_channels;
+        const float *om = event_mask + tok * obs_channels;
         ev = om[0];
         for (int c2 = 1; c2 < obs_channels; ++c2) ev = fmaxf(ev, om[c2]);
       }
       row[m] = (lr * gr + li * gi) * ev;  // de = conj(g) lambda
       row[modes + m] = (-lr * gi + li * gr) * ev;
+      nar = ar;
+      nai = ai;
     }
     float *pp = polepart + (b * n_chunks + c) * 4 * modes;
-    pp[m] = dar;
-    pp[modes + m] = dai;
-    pp[2 * modes + m] = dgr;
-    pp[3 * modes + m] = dgi;
+    if (dt) {
+      pp[m] = (float)pdr;
+      pp[modes + m] = (float)pdi;
+      pp[2 * modes + m] = 0.f;
+      pp[3 * modes + m] = 0.f;
+    } else {
+      pp[m] = dar;
+      pp[modes + m] = dai;
+      pp[2 * modes + m] = dgr;
+      pp[3 * modes + m] = dgi;
+    }
   }
 }
 
@@ -482,14 +575,23 @@ __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restri
 // dL/dp by the Cauchy-Riemann form of a'(p) = a and g'(p) = (a p - (a - 1)) / p^2
 // (dt = 1), then damping = dmin + (dmax - dmin) sigmoid(raw), freq = pi tanh(raw).
 // `sums` [4][M]: da re, da im, dg re, dg im summed over every (row, chunk).
+// `per_step`: sums hold dL/dp (re, im) already (time_delta requests).
 __global__ void pole_backward_kernel(const float *__restrict__ sums, int modes,
                                      const float *__restrict__ raw_decay,
                                      const float *__restrict__ raw_freq,
-                                     float *__restrict__ d_decay, float *__restrict__ d_freq) {
+                                     float *__restrict__ d_decay, float *__restrict__ d_freq,
+                                     int per_step) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= modes) return;
   double s[4];
   for (int k = 0; k < 4; ++k) s[k] = (double)sums[k * modes + m];
+  if (per_step) {
+    const double sig = 1.0 / (1.0 + exp(-(double)raw_decay[m]));
+    const double th = tanh((double)raw_freq[m]);
+    d_decay[m] = (float)(-s[0] * (kDampingMax - kDampingMin) * sig * (1.0 - sig));
+    d_freq[m] = (float)(s[1] * kPi * (1.0 - th * th));
+    return;
+  }
   const double sig = 1.0 / (1.0 + exp(-(double)raw_decay[m]));
   const double damping = kDampingMin + (kDampingMax - kDampingMin) * sig;
   const double th = tanh((double)raw_freq[m]);
@@ -763,6 +865,220 @@ __global__ void residual_dxh_kernel(const float *__restrict__ dv, const float *_
   }
 }
 
+// ---------------------------------------------------------------- physical time (time_delta)
+// Sample position of a physical-time lookup at `q` in one row's timestamps:
+// lower / upper index, interpolation weight and whether q lies inside the row
+// (the arithmetic of dwconv_physical_kernel and pt_moments_partial_kernel).
+struct PtPos {
+  int64_t lo, hi;
+  float w;
+  bool in;
+};
+__device__ __forceinline__ PtPos pt_position(const float *row, int64_t steps, float q) {
+  const int64_t up_u = lower_bound_f(row, steps, q);
+  PtPos r;
+  r.hi = up_u < steps - 1 ? up_u : steps - 1;
+  int64_t lo = up_u - 1;
+  r.lo = lo < 0 ? 0 : (lo > steps - 1 ? steps - 1 : lo);
+  const float lt = row[r.lo], ut = row[r.hi];
+  const float span = ut - lt;
+  const float ip = span > 0.f ? (q - lt) / fmaxf(span, kFp32Tiny) : 0.f;
+  r.w = fminf(fmaxf(ip, 0.f), 1.f);
+  r.in = (q >= row[0]) && (q <= row[steps - 1]);
+  return r;
+}
+__device__ __forceinline__ float pt_support(const float *vrow, const PtPos &p) {
+  if (!vrow) return 1.f;
+  const float lv = vrow[p.lo], uv = vrow[p.hi];
+  const float eps8 = 8.0f * kFp32Eps;
+  return p.w <= eps8 ? lv : (p.w >= 1.0f - eps8 ? uv : lv * uv);
+}
+
+// Per-row normalisers of the physical-time moments: counts[b] = {energy count
+// ec, use-duration flag, pair weights pc_1, pc_2, pc_4} (as
+// pt_moments_finalize_kernel forms them).  One block per row.
+__global__ void pt_counts_kernel(const float *__restrict__ ts, const float *__restrict__ dt,
+                                 const float *__restrict__ valid, int64_t steps,
+                                 float *__restrict__ counts) {
+  const int64_t b = blockIdx.x;
+  const float *row = ts + b * steps;
+  const float *vrow = valid ? valid + b * steps : nullptr;
+  const int lags[3] = {1, 2, 4};
+  __shared__ double red[5][32];
+  double c[5] = {0, 0, 0, 0, 0};
+  for (int64_t t = threadIdx.x; t < steps; t += blockDim.x) {
+    const float vt = vrow ? vrow[t] : 1.f;
+    c[0] += (double)(dt[b * steps + t] * vt);
+    c[1] += (double)vt;
+    for (int l = 0; l < 3; ++l) {
+      const PtPos pp = pt_position(row, steps, row[t] - (float)lags[l]);
+      const float sup = pt_support(vrow, pp) * (pp.in ? 1.f : 0.f);
+      c[2 + l] += (double)(dt[b * steps + t] * vt * sup);
+    }
+  }
+  for (int k = 0; k < 5; ++k) {
+    double x = c[k];
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if ((threadIdx.x & 31) == 0) red[k][threadIdx.x >> 5] = x;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot[5] = {0, 0, 0, 0, 0};
+    for (int k = 0; k < 5; ++k)
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot[k] += red[k][w];
+    const bool use_d = tot[0] > 0.0;
+    counts[b * 8 + 0] = fmaxf((float)(use_d ? tot[0] : tot[1]), 1.0f);
+    counts[b * 8 + 1] = use_d ? 1.f : 0.f;
+    for (int l = 0; l < 3; ++l) counts[b * 8 + 2 + l] = fmaxf((float)tot[2 + l], 1.0f);
+  }
+}
+
+// State gradient of the physical-time moments, added with atomics into a zeroed
+// dS: per (row, chunk) block with threads over modes; for each step the energy
+// term (duration-weighted when the row's durations sum above zero), and for
+// each lag the pair with the state interpolated at t - lag: the current-state
+// term at t and the interpolated-state term scattered onto its lower / upper
+// samples with weights 1 - w and w.
+__global__ void pt_moments_backward_kernel(const float *__restrict__ s, const float *__restrict__ ts,
+                                           const float *__restrict__ dt,
+                                           const float *__restrict__ valid,
+                                           const float *__restrict__ counts,
+                                           const float *__restrict__ dm, float *__restrict__ dS,
+                                           int64_t steps, int modes) {
+  __shared__ int64_t s_lo[3][kPtChunk], s_hi[3][kPtChunk];
+  __shared__ float s_ip[3][kPtChunk], s_pw[3][kPtChunk], s_ew[kPtChunk];
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  const int64_t t0 = c * kPtChunk;
+  const int n = (int)min((int64_t)kPtChunk, steps - t0);
+  const float *row = ts + b * steps;
+  const float *vrow = valid ? valid + b * steps : nullptr;
+  const float *cnt = counts + b * 8;
+  const int lags[3] = {1, 2, 4};
+  for (int j = threadIdx.x; j < n * 3; j += blockDim.x) {
+    const int i = j / 3, l = j - (j / 3) * 3;
+    const int64_t t = t0 + i;
+    const PtPos pp = pt_position(row, steps, row[t] - (float)lags[l]);
+    const float vt = vrow ? vrow[t] : 1.f;
+    s_lo[l][i] = b * steps + pp.lo;
+    s_hi[l][i] = b * steps + pp.hi;
+    s_ip[l][i] = pp.w;
+    s_pw[l][i] = dt[b * steps + t] * vt * pt_support(vrow, pp) * (pp.in ? 1.f : 0.f) / cnt[2 + l];
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float vt = vrow ? vrow[t0 + i] : 1.f;
+    s_ew[i] = (cnt[1] > 0.f ? dt[b * steps + t0 + i] * vt : vt) / cnt[0];
+  }
+  __syncthreads();
+  const int64_t M2 = 2 * modes;
+  const float *g = dm + b * 7 * modes;
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    const float ge = g[m];
+    float dr[3], di[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      dr[l] = g[(1 + 2 * l) * modes + m];
+      di[l] = g[(2 + 2 * l) * modes + m];
+    }
+    for (int i = 0; i < n; ++i) {
+      const int64_t tok = b * steps + t0 + i;
+      const float cr = s[tok * M2 + m], ci = s[tok * M2 + modes + m];
+      float gr = 2.f * cr * ge * s_ew[i], gi = 2.f * ci * ge * s_ew[i];
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        const float pw = s_pw[l][i];
+        if (pw == 0.f) continue;
+        const float *lo = s + s_lo[l][i] * M2, *hi = s + s_hi[l][i] * M2;
+        const float w = s_ip[l][i];
+        const float pr = lerp_torch(lo[m], hi[m], w), pi = lerp_torch(lo[modes + m], hi[modes + m], w);
+        gr += (dr[l] * pr - di[l] * pi) * pw;
+        gi += (dr[l] * pi + di[l] * pr) * pw;
+        const float hr = (dr[l] * cr + di[l] * ci) * pw, hi_ = (dr[l] * ci - di[l] * cr) * pw;
+        atomicAdd(dS + s_lo[l][i] * M2 + m, (1.f - w) * hr);
+        atomicAdd(dS + s_lo[l][i] * M2 + modes + m, (1.f - w) * hi_);
+        atomicAdd(dS + s_hi[l][i] * M2 + m, w * hr);
+        atomicAdd(dS + s_hi[l][i] * M2 + modes + m, w * hi_);
+      }
+      atomicAdd(dS + tok * M2 + m, gr);
+      atomicAdd(dS + tok * M2 + modes + m, gi);
+    }
+  }
+}
+
+// The physical-time conv + SiLU VJP for a row's kCbTile steps (threads over
+// channels): sample positions of every (step, tap) in shared memory, the
+// pre-activation recomputed on the masked input, dz = dy out_mask silu'(z),
+// the input gradient scattered onto the lower / upper samples with atomics
+// (times the input mask there), and weight / bias partial sums
+// (partial[block][d (taps + 1) + j]).
+constexpr int kPcTaps = 8;
+__global__ void pconv_backward_kernel(const float *__restrict__ in, const float *__restrict__ w,
+                                      const float *__restrict__ bias,
+                                      const float *__restrict__ in_mask,
+                                      const float *__restrict__ ts,
+                                      const float *__restrict__ valid,
+                                      const float *__restrict__ out_mask,
+                                      const float *__restrict__ dy, float *__restrict__ dx,
+                                      float *__restrict__ partial, int64_t steps, int dim,
+                                      int taps, int dil) {
+  __shared__ int64_t s_lo[kCbTile][kPcTaps], s_hi[kCbTile][kPcTaps];
+  __shared__ float s_w[kCbTile][kPcTaps], s_on[kCbTile][kPcTaps];
+  const unsigned tiles = (unsigned)((steps + kCbTile - 1) / kCbTile);
+  const int64_t b = blockIdx.x / tiles;
+  const int64_t t0 = (int64_t)(blockIdx.x - (unsigned)b * tiles) * kCbTile;
+  const int n = (int)min((int64_t)kCbTile, steps - t0);
+  const float *row = ts + b * steps;
+  const float *vrow = valid ? valid + b * steps : nullptr;
+  const int left = dil * (taps - 1) / 2;
+  for (int j = threadIdx.x; j < n * taps; j += blockDim.x) {
+    const int i = j / taps, k = j - (j / taps) * taps;
+    const PtPos pp = pt_position(row, steps, row[t0 + i] + (float)(k * dil - left));
+    bool on = pp.in;
+    if (vrow) on = on && (pt_support(vrow, pp) > 0.f);
+    s_lo[i][k] = b * steps + pp.lo;
+    s_hi[i][k] = b * steps + pp.hi;
+    s_w[i][k] = pp.w;
+    s_on[i][k] = on ? 1.f : 0.f;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    float aw[kPcTaps];
+    for (int k = 0; k < taps; ++k) aw[k] = 0.f;
+    float ab = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const int64_t tok = b * steps + t0 + i;
+      float samp[kPcTaps];
+      for (int k = 0; k < taps; ++k) {
+        float a = in[s_lo[i][k] * dim + d], c2 = in[s_hi[i][k] * dim + d];
+        if (in_mask) {
+          a *= in_mask[s_lo[i][k]];
+          c2 *= in_mask[s_hi[i][k]];
+        }
+        samp[k] = s_on[i][k] > 0.f ? lerp_torch(a, c2, s_w[i][k]) : 0.f;
+      }
+      float zf = 0.f;  // the forward's order: taps 0..K-1, then the bias
+      for (int k = 0; k < taps; ++k) zf = fmaf(samp[k], w[d * taps + k], zf);
+      zf += bias[d];
+      const float sg = 1.0f / (1.0f + expf(-zf));
+      float gz = dy[tok * dim + d] * sg * (1.0f + zf * (1.0f - sg));
+      if (out_mask) gz *= out_mask[tok];
+      ab += gz;
+      for (int k = 0; k < taps; ++k) {
+        aw[k] = fmaf(gz, samp[k], aw[k]);
+        const float g = gz * w[d * taps + k] * s_on[i][k];
+        if (g == 0.f) continue;
+        const float wl = s_w[i][k];
+        const float ml = in_mask ? in_mask[s_lo[i][k]] : 1.f;
+        const float mh = in_mask ? in_mask[s_hi[i][k]] : 1.f;
+        atomicAdd(dx + s_lo[i][k] * dim + d, (1.f - wl) * g * ml);
+        atomicAdd(dx + s_hi[i][k] * dim + d, wl * g * mh);
+      }
+    }
+    float *out = partial + (int64_t)blockIdx.x * dim * (taps + 1) + d * (taps + 1);
+    for (int k = 0; k < taps; ++k) out[k] = aw[k];
+    out[taps] = ab;
+  }
+}
+
 // ---------------------------------------------------------------- backward orchestration
 // C[n1, n2] (row-major) = sum_r A[r, n1] Bm[r, n2] (+ beta C): the weight
 // gradients (A [R, n1], Bm [R, n2] row-major).
@@ -795,24 +1111,24 @@ static int block_backward(const TrainPlan &tp, const float *states, const float 
                           const float *g_im, float *dxh, float dxh_beta, float *dframe,
                           float frame_beta, float *d_decay, float *d_freq, int64_t B, int64_t T,
                           int D, int M, bool tf32, const float *event_mask, int obs_channels,
-                          cudaStream_t st) {
+                          const float *dt, cudaStream_t st) {
   const int64_t n_scan = cdiv(T, kScanChunk);
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   const dim3 gs((unsigned)n_scan, (unsigned)B);
-  rscan_local_kernel<<<gs, threads, 0, st>>>(tp.dS, a_re, a_im, tp.carries, T, M, kScanChunk,
-                                             n_scan);
+  rscan_local_kernel<<<gs, threads, 0, st>>>(tp.dS, a_re, a_im, raw_decay, raw_freq, dt,
+                                             tp.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("rscan_local_kernel"));
   scan_carry_kernel<<<dim3((unsigned)cdiv(M, 32), (unsigned)B), 32 * kCarryParts, 0, st>>>(
       tp.carries, B, M, n_scan, nullptr);
   LNET_TRY(after_launch("scan_carry_kernel"));
-  rscan_apply_kernel<<<gs, threads, 0, st>>>(tp.dS, states, a_re, a_im, g_re, g_im, tp.carries,
-                                             tp.polepart, T, M, kScanChunk, n_scan, event_mask,
-                                             obs_channels);
+  rscan_apply_kernel<<<gs, threads, 0, st>>>(tp.dS, states, a_re, a_im, g_re, g_im, raw_decay,
+                                             raw_freq, dt, tp.carries, tp.polepart, T, M,
+                                             kScanChunk, n_scan, event_mask, obs_channels);
   LNET_TRY(after_launch("rscan_apply_kernel"));
   LNET_TRY(colsum(ColPlain{tp.polepart, 4 * M}, B * n_scan, 4 * M, tp.colpart, tp.polesum, st,
                   "colsum(pole)"));
   pole_backward_kernel<<<(unsigned)cdiv(M, 64), 64, 0, st>>>(tp.polesum, M, raw_decay, raw_freq,
-                                                             d_decay, d_freq);
+                                                             d_decay, d_freq, dt ? 1 : 0);
   LNET_TRY(after_launch("pole_backward_kernel"));
   const int64_t bt = B * T;
   LNET_TRY(gemm_rows(st, tp.dS, CUDA_R_32F, 2 * M, frame, CUDA_R_32F, 2 * M, 1, dxh, D, bt, D,
@@ -865,6 +1181,48 @@ static int conv_backward(const TrainPlan &tp, const float *in, const float *w, c
   return after_launch("conv_wgrad_split_kernel");
 }
 
+// The state gradient of one block's moments into tp.dS (overwritten).
+static int moments_vjp(const TrainPlan &tp, const lnet_b200_alphabet_request *r,
+                       const float *states, const float *dm, int64_t B, int64_t T, int M,
+                       cudaStream_t st) {
+  if (r->time_delta) {
+    LNET_TRY(cuda_check(cudaMemsetAsync(tp.dS, 0, (size_t)B * T * 2 * M * sizeof(float), st),
+                        "cudaMemsetAsync(dS)"));
+    const int threads = std::min(128, (int)cdiv(M, 32) * 32);
+    pt_moments_backward_kernel<<<dim3((unsigned)cdiv(T, kPtChunk), (unsigned)B), threads, 0,
+                                 st>>>(states, tp.ts, r->time_delta, r->valid_mask, tp.ptcounts,
+                                       dm, tp.dS, T, M);
+    return after_launch("pt_moments_backward_kernel");
+  }
+  const unsigned mb_grid = (unsigned)(B * cdiv(T, kMbTile));
+  const unsigned mb_threads = (unsigned)std::min(128, (int)cdiv(M, 32) * 32);
+  moments_backward_kernel<<<mb_grid, mb_threads, 0, st>>>(states, dm, r->valid_mask, tp.counts,
+                                                          tp.dS, B, T, M, 0);
+  return after_launch("moments_backward_kernel");
+}
+
+// The conv + SiLU VJP of one block (physical-time when the request has dt).
+static int conv_vjp(const TrainPlan &tp, const lnet_b200_alphabet_request *r, const float *in,
+                    const float *w, const float *bias, const float *in_mask,
+                    const float *out_mask, const float *dy, float *dx, float *dw, float *db,
+                    int64_t B, int64_t T, int D, int taps, int dil, cudaStream_t st) {
+  if (!r->time_delta)
+    return conv_backward(tp, in, w, bias, in_mask, out_mask, dy, dx, dw, db, B, T, D, taps, dil,
+                         st);
+  if (taps > kPcTaps) return fail(LNET_ERR_UNSUPPORTED, "physical-time conv: more than 8 taps");
+  LNET_TRY(cuda_check(cudaMemsetAsync(dx, 0, (size_t)B * T * D * sizeof(float), st),
+                      "cudaMemsetAsync(dx)"));
+  const unsigned grid = (unsigned)(B * cdiv(T, kCbTile));
+  const unsigned threads = (unsigned)std::min(256, (int)cdiv(D, 32) * 32);
+  pconv_backward_kernel<<<grid, threads, 0, st>>>(in, w, bias, in_mask, tp.ts, r->valid_mask,
+                                                  out_mask, dy, dx, tp.colpart, T, D, taps, dil);
+  LNET_TRY(after_launch("pconv_backward_kernel"));
+  LNET_TRY(colsum_finish(tp.colpart, (int)grid, D * (taps + 1), tp.polesum, st));
+  conv_wgrad_split_kernel<<<(unsigned)cdiv(D * (taps + 1), 256), 256, 0, st>>>(tp.polesum, dw, db,
+                                                                              D, taps);
+  return after_launch("conv_wgrad_split_kernel");
+}
+
 static int train_backward_impl(const lnet_b200_alphabet_params *p,
                                const lnet_b200_alphabet_request *r, TrainPlan &tp,
                                const float *dlogits, const lnet_b200_alphabet_grads *gd,
@@ -883,31 +1241,30 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   radial_backward_kernel<<<grid_for(2 * B * 7 * M), 256, 0, st>>>(tp.m1, tp.m2, tp.dfeats, tp.dm,
                                                                   B, M);
   LNET_TRY(after_launch("radial_backward_kernel"));
-  if (valid) {
+  if (r->time_delta) {
+    pt_counts_kernel<<<(unsigned)B, 256, 0, st>>>(tp.ts, r->time_delta, valid, T, tp.ptcounts);
+    LNET_TRY(after_launch("pt_counts_kernel"));
+  } else if (valid) {
     moment_counts_kernel<<<(unsigned)B, 256, 0, st>>>(valid, T, tp.counts);
     LNET_TRY(after_launch("moment_counts_kernel"));
   }
   const float *dm1 = tp.dm, *dm2 = tp.dm + B * 7 * M;
   // reader block
-  const unsigned mb_grid = (unsigned)(B * cdiv(T, kMbTile));
-  const unsigned mb_threads = (unsigned)std::min(128, (int)cdiv(M, 32) * 32);
-  moments_backward_kernel<<<mb_grid, mb_threads, 0, st>>>(tp.s2, dm2, valid, tp.counts, tp.dS, B,
-                                                          T, M, 0);
-  LNET_TRY(after_launch("moments_backward_kernel"));
+  LNET_TRY(moments_vjp(tp, r, tp.s2, dm2, B, T, M, st));
   LNET_TRY(block_backward(tp, tp.s2, tp.xh2, p->reader_frame, p->reader_raw_decay,
                           p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
                           tp.a_tab + 6 * M, tp.a_tab + 7 * M, tp.dX, 0.f, gd->reader_frame, 0.f,
                           gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, tf32,
-                          nullptr, 1, st));
+                          nullptr, 1, r->time_delta, st));
   rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y2, tp.dX, p->reader_norm,
                                                              nullptr, tp.dY, tp.rs, bt, D);
   LNET_TRY(after_launch("rms_backward_kernel"));
   LNET_TRY(colsum(ColRmsGamma{tp.dX, tp.y2, tp.rs, D}, bt, D, tp.colpart, gd->reader_norm, st,
                   "colsum(reader norm)"));
   // reader conv: input v (masked), dv out
-  LNET_TRY(conv_backward(tp, tp.v, p->reader_conv_weight, p->reader_conv_bias, valid, valid,
-                         tp.dY, tp.dV, gd->reader_conv_weight, gd->reader_conv_bias, B, T, D,
-                         taps, dil, st));
+  LNET_TRY(conv_vjp(tp, r, tp.v, p->reader_conv_weight, p->reader_conv_bias, valid, valid,
+                    tp.dY, tp.dV, gd->reader_conv_weight, gd->reader_conv_bias, B, T, D, taps,
+                    dil, st));
   // writer synthesis + residual: v = y1 + ls (s1 F^T + ds xh1)
   const float *ls = p->writer_layer_scale, *ds = p->writer_direct_scale;
   LNET_TRY(colsum(ColProd{tp.dV, tp.modal, tp.xh1, ls, ds, D, 0}, bt, D, tp.colpart,
@@ -918,9 +1275,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
                                                                    2 * M);
   LNET_TRY(after_launch("scale_rows_kernel"));
   // dS1 = moments VJP + dv (ls F) (the GEMM accumulates, beta = 1)
-  moments_backward_kernel<<<mb_grid, mb_threads, 0, st>>>(tp.s1, dm1, valid, tp.counts, tp.dS, B,
-                                                          T, M, 0);
-  LNET_TRY(after_launch("moments_backward_kernel"));
+  LNET_TRY(moments_vjp(tp, r, tp.s1, dm1, B, T, M, st));
   LNET_TRY(gemm_rows(st, tp.dV, CUDA_R_32F, D, tp.wls, CUDA_R_32F, 1, 2 * M, tp.dS, 2 * M, bt,
                      2 * M, D, tf32, "cublas(d states synth)", /*beta=*/1.f));
   // dF1 = ls (dv^T s1) (+ the drive part below)
@@ -935,7 +1290,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
                           p->writer_raw_frequency, tp.a_tab, tp.a_tab + M, tp.a_tab + 4 * M,
                           tp.a_tab + 5 * M, tp.dX, 1.f, gd->writer_frame, 1.f,
                           gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, tf32,
-                          r->observation_mask, r->obs_channels, st));
+                          r->observation_mask, r->obs_channels, r->time_delta, st));
   // writer RMSNorm: dy1 = rms VJP + dv (residual identity)
   rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y1, tp.dX, p->writer_norm, tp.dV,
                                                              tp.dY, tp.rs, bt, D);
@@ -943,9 +1298,9 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(colsum(ColRmsGamma{tp.dX, tp.y1, tp.rs, D}, bt, D, tp.colpart, gd->writer_norm, st,
                   "colsum(writer norm)"));
   // stem conv: input proj (no input mask), output mask valid; dproj -> tp.dV
-  LNET_TRY(conv_backward(tp, tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, valid,
-                         tp.dY, tp.dV, gd->stem_conv_weight, gd->stem_conv_bias, B, T, D, taps,
-                         dil, st));
+  LNET_TRY(conv_vjp(tp, r, tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, valid,
+                    tp.dY, tp.dV, gd->stem_conv_weight, gd->stem_conv_bias, B, T, D, taps, dil,
+                    st));
   return gemm_wgrad(st, tp.dV, D, tp.x32, C, gd->stem_projection, bt, 0.f, tf32,
                     "cublas(d projection)");
 }

@@ -315,15 +315,15 @@ class B200Alphabet(nn.Module):
             raise TypeError(f"inputs must be float32 or bfloat16, got {inputs.dtype}")
         if self.training and torch.is_grad_enabled():
             # training: the fp32 forward that keeps its activations, with the
-            # B200 backward (lnet_b200.training); static poles
-            if time_delta is not None:
-                raise NotImplementedError("training supports static poles only (no time_delta)")
+            # B200 backward (lnet_b200.training)
             if return_moments:
                 raise NotImplementedError("return_moments is an inference option")
-            _, obs, valid = self._prepare_metadata(inputs, None, observation_mask, valid_mask)
+            delta, obs, valid = self._prepare_metadata(inputs, time_delta, observation_mask,
+                                                       valid_mask)
             from .training import train_forward
 
-            return train_forward(self, inputs, valid, obs).to(self.head.classifier.weight.dtype)
+            return train_forward(self, inputs, valid, obs, delta).to(
+                self.head.classifier.weight.dtype)
         delta, obs, valid = self._prepare_metadata(inputs, time_delta, observation_mask,
                                                    valid_mask)
         x = inputs.contiguous()

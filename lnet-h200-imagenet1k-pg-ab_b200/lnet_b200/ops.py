@@ -25,7 +25,7 @@ known output shape.  This module gives the B200 path the same surface:
 reference's ops register their VJPs the same way,
 src/lnet/pac_triton_recurrence_op.py:646-684): its backward reruns the fp32
 training forward on the saved inputs and calls ``lnet_b200_alphabet_backward``
-(static poles; the op itself keeps no activations).
+(the op itself keeps no activations).
 
 Launches are ordered on the current torch stream with no host synchronisation.
 There is no CPU implementation: a CPU input raises ``RuntimeError``.
@@ -152,16 +152,14 @@ def _alphabet_setup_context(ctx, inputs, output):
 def _alphabet_backward(ctx, dlogits):
     """Gradients for the 17 weights: the training forward is rerun on the saved
     inputs (the op keeps no activations, like activation checkpointing), then
-    lnet_b200_alphabet_backward.  Static poles only (no time_delta)."""
+    lnet_b200_alphabet_backward."""
     from .training import AlphabetTrainFunction
 
     x, *weights = ctx.saved_tensors
     time_delta, obs, valid = ctx.meta
-    if time_delta is not None:
-        raise NotImplementedError("lnet_b200::alphabet_forward: no backward for time_delta")
     with torch.enable_grad():
         leaves = [w.detach().requires_grad_(True) for w in weights]
-        logits = AlphabetTrainFunction.apply(x, valid, obs, ctx.dims, *leaves)
+        logits = AlphabetTrainFunction.apply(x, valid, obs, time_delta, ctx.dims, *leaves)
         grads = torch.autograd.grad(logits, leaves, dlogits)
     # the structure of the arguments actually passed (optional arguments left
     # at their defaults are not part of it): x, weights, dims, [metadata...]

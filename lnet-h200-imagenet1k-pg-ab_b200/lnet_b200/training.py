@@ -15,8 +15,10 @@ Here one ``torch.autograd.Function`` wraps the two C-ABI calls:
 The function's inputs are the module's *effective* tensors built with
 differentiable torch ops (``frame_matrix()`` through the orthogonal
 parametrisation, conv weights reshaped), so torch chains the returned
-gradients back to the module's own parameters.  Scope: static poles
-(no ``time_delta``); ``observation_mask`` and ``valid_mask`` allowed.
+gradients back to the module's own parameters.  Every metadata combination
+(``time_delta``, ``observation_mask``, ``valid_mask``) is supported; with
+``time_delta`` the interpolation scatters use float atomics, so those
+gradients are reproducible to rounding, not bitwise.
 """
 
 from __future__ import annotations
@@ -63,8 +65,8 @@ class AlphabetTrainFunction(torch.autograd.Function):
     """logits = ALPHABET(x; tensors) with the B200 backward."""
 
     @staticmethod
-    def forward(ctx, x: Tensor, valid: Tensor | None, obs: Tensor | None, dims: tuple,
-                *tensors: Tensor) -> Tensor:
+    def forward(ctx, x: Tensor, valid: Tensor | None, obs: Tensor | None, delta: Tensor | None,
+                dims: tuple, *tensors: Tensor) -> Tensor:
         lib = _lib.load()
         keep = [t.detach().contiguous() for t in tensors]
         params = _lib.AlphabetParams(
@@ -78,6 +80,7 @@ class AlphabetTrainFunction(torch.autograd.Function):
         # precision policy of the inference route)
         req = _lib.AlphabetRequest(batch=x.shape[0], steps=x.shape[1], x_dtype=dtype,
                                    act_dtype=dtype, x=x.data_ptr(),
+                                   time_delta=None if delta is None else delta.data_ptr(),
                                    observation_mask=None if obs is None else obs.data_ptr(),
                                    obs_channels=1 if obs is None else obs.shape[-1],
                                    valid_mask=None if valid is None else valid.data_ptr())
@@ -94,13 +97,13 @@ class AlphabetTrainFunction(torch.autograd.Function):
                                                             int(n.value), logits.data_ptr(),
                                                             stream),
                        "lnet_b200_alphabet_train_forward")
-        ctx.state = (params, req, ws, int(n.value), keep, x, valid, obs)
+        ctx.state = (params, req, ws, int(n.value), keep, x, valid, obs, delta)
         return logits
 
     @staticmethod
     def backward(ctx, dlogits: Tensor):
         lib = _lib.load()
-        params, req, ws, nbytes, keep, x, valid, obs = ctx.state
+        params, req, ws, nbytes, keep, x, valid, obs, delta = ctx.state
         dl = dlogits.detach().float().contiguous()
         grads = [torch.empty_like(t) for t in keep]
         gs = _lib.AlphabetGrads(**{name: g.data_ptr()
@@ -112,13 +115,15 @@ class AlphabetTrainFunction(torch.autograd.Function):
                                                        ctypes.byref(gs), stream),
                        "lnet_b200_alphabet_backward")
         ctx.state = None  # the workspace is single-use
-        return (None, None, None, None, *grads)
+        return (None, None, None, None, None, *grads)
 
 
 def train_forward(model, x: Tensor, valid_mask: Tensor | None = None,
-                  observation_mask: Tensor | None = None) -> Tensor:
+                  observation_mask: Tensor | None = None,
+                  time_delta: Tensor | None = None) -> Tensor:
     """Differentiable logits of ``model`` (a ``B200Alphabet``) for ``x`` [B, T, C];
-    masks already normalised (fp32; valid [B, T], observation [B, T, 1 or C])."""
+    metadata already normalised (fp32; valid [B, T], observation [B, T, 1 or C],
+    time_delta [B, T])."""
     dims = (model.raw_input_dim, model.model_dim, model.modes,
             model.head.classifier.out_features, model.dwconv_kernel_size, model.dwconv_dilation)
     valid = None
@@ -127,7 +132,10 @@ def train_forward(model, x: Tensor, valid_mask: Tensor | None = None,
     obs = None
     if observation_mask is not None:
         obs = observation_mask.to(device=x.device, dtype=torch.float32).contiguous()
-    return AlphabetTrainFunction.apply(x, valid, obs, dims, *effective_tensors(model))
+    delta = None
+    if time_delta is not None:
+        delta = time_delta.to(device=x.device, dtype=torch.float32).reshape(x.shape[:2]).contiguous()
+    return AlphabetTrainFunction.apply(x, valid, obs, delta, dims, *effective_tensors(model))
 
 
 __all__ = ["AlphabetTrainFunction", "effective_tensors", "train_forward"]

@@ -8,7 +8,7 @@ training mode runs ``lnet_b200_alphabet_train_forward`` and, on
 1e-5 relative, every parameter gradient 2e-4 relative (normwise per tensor;
 fp32 against float64 over sequences up to 300 steps).  Also: the training
 forward equals the inference forward; the oracle VJP agrees at a size the
-goldens do not cover; time_delta (not supported in training) raises.
+goldens do not cover; return_moments (an inference option) raises in training.
 """
 
 from __future__ import annotations
@@ -24,7 +24,7 @@ from oracle import alphabet_grad_oracle as G
 pytestmark = pytest.mark.gpu
 
 CASES = ["grad_plain", "grad_real_poles", "grad_long", "grad_valid", "grad_obs_channel",
-         "grad_obs_event"]
+         "grad_obs_event", "grad_delta", "grad_all_meta"]
 
 
 def _model(z, device):
@@ -34,9 +34,9 @@ def _model(z, device):
     return model.to(device).train()
 
 
-def _grads(model, x, dlogits, valid=None, obs=None):
+def _grads(model, x, dlogits, valid=None, obs=None, delta=None):
     model.zero_grad(set_to_none=True)
-    logits = model(x, valid_mask=valid, observation_mask=obs)
+    logits = model(x, valid_mask=valid, observation_mask=obs, time_delta=delta)
     (logits * dlogits).sum().backward()
     out = {name: p.grad for name, p in model.named_parameters() if p.grad is not None}
     return logits.detach(), out
@@ -51,7 +51,8 @@ def test_backward_matches_reference_autograd(name, cuda_device):
     valid = torch.from_numpy(z["in.valid_mask"]).to(cuda_device) if "in.valid_mask" in z else None
     obs = (torch.from_numpy(z["in.observation_mask"]).to(cuda_device)
            if "in.observation_mask" in z else None)
-    logits, grads = _grads(model, x, dl, valid, obs)
+    delta = torch.from_numpy(z["in.time_delta"]).to(cuda_device) if "in.time_delta" in z else None
+    logits, grads = _grads(model, x, dl, valid, obs, delta)
     assert rel_err(logits.cpu().numpy(), z["out.logits"]) <= 1e-5
     checked = 0
     for key in z:
@@ -128,9 +129,9 @@ def test_backward_bf16_inputs_tf32(cuda_device):
         assert rel_err(g16[name].cpu().numpy(), ref.cpu().numpy()) <= 2e-2, name
 
 
-def test_training_rejects_unsupported_metadata(cuda_device):
+def test_training_rejects_return_moments(cuda_device):
     z = load_golden("grad_plain")
     model = _model(z, cuda_device)
     x = torch.from_numpy(z["in.x"]).to(cuda_device)
     with pytest.raises(NotImplementedError):
-        model(x, time_delta=torch.ones(x.shape[:2], device=cuda_device))
+        model(x, return_moments=True)

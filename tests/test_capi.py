@@ -68,9 +68,9 @@ def test_struct_layouts_match_header():
 
 
 def test_training_error_paths_without_gpu():
-    """The training entry points validate before any CUDA call: time_delta is
-    refused (LNET_ERR_UNSUPPORTED), a missing workspace is reported, and the
-    workspace size is computed on the host."""
+    """The training entry points validate before any CUDA call: a missing
+    workspace and malformed metadata are reported, and the workspace size is
+    computed on the host."""
     from lnet_b200 import _lib
 
     lib = _lib.load()
@@ -87,8 +87,12 @@ def test_training_error_paths_without_gpu():
     st = lib.lnet_b200_alphabet_train_forward(ctypes.byref(params), ctypes.byref(req), None, 0,
                                               dummy, None)
     assert st == _lib.LNET_ERR_WORKSPACE
-    req.time_delta = dummy
+    req.time_delta = dummy  # physical time is supported: validation reaches the workspace
     st = lib.lnet_b200_alphabet_train_forward(ctypes.byref(params), ctypes.byref(req), None, 0,
                                               dummy, None)
-    assert st == _lib.LNET_ERR_UNSUPPORTED
-    assert "time_delta" in _lib.last_error()
+    assert st == _lib.LNET_ERR_WORKSPACE
+    req.obs_channels = 3  # neither 1 nor C
+    req.observation_mask = dummy
+    st = lib.lnet_b200_alphabet_train_forward(ctypes.byref(params), ctypes.byref(req), None, 0,
+                                              dummy, None)
+    assert st == _lib.LNET_ERR_INVALID_ARGUMENT

@@ -92,7 +92,7 @@ def test_alphabet_op_autograd(cuda_device):
     from lnet_b200.training import AlphabetTrainFunction
 
     leaves2 = [w.detach().clone().requires_grad_(True) for w in weights]
-    ref = AlphabetTrainFunction.apply(x, None, None, tuple(dims), *leaves2)
+    ref = AlphabetTrainFunction.apply(x, None, None, None, tuple(dims), *leaves2)
     ref_grads = torch.autograd.grad((ref * dl).sum(), leaves2)
     for a, b in zip(op_grads, ref_grads):
         assert rel_err(a.cpu().numpy(), b.cpu().numpy()) <= 1e-6
