@@ -4,8 +4,8 @@ TEST INFRASTRUCTURE ONLY, like ``alphabet_oracle``: the ``-m gpu`` tests use
 it to check ``lnet_b200_alphabet_backward``; the product never imports it.
 
 Scope: the eager ``Alphabet.forward`` (src/lnet/alphabet.py:350-416) with
-static poles (no ``time_delta``), optional ``observation_mask`` (channel or
-event form) and ``valid_mask``; gradients of ``L = sum(logits * dlogits)`` with respect to
+every metadata combination (``time_delta``: physical-time convs and moments;
+``observation_mask``, channel or event form; ``valid_mask``); gradients of ``L = sum(logits * dlogits)`` with respect to
 every parameter, each frame's gradient taken at the materialised [D, 2M]
 weight.  It is pinned against gradients that the reference's own autograd
 produces (``tests/golden/make_grad_golden.py``,
