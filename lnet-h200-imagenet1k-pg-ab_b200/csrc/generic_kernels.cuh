@@ -161,8 +161,8 @@ __global__ void __launch_bounds__(kDwTileThreads) dwconv_tile_kernel(
 // `status`, waits once more for the copies still in flight, and the block
 // returns.  Shared memory: two input tiles [kDnSteps + 2 PAD][dim],
 // [kDnSteps][dim / 4] squares, [kDnSteps] scales, two mbarriers, a flag.
-constexpr int kDnSteps = 16, kDnThreads = 256, kDnMaxPer = 4, kDnParts = kDnThreads / kDnSteps;
-constexpr int kDnBlocksPerSM = 3;
+constexpr int kDnSteps = 32, kDnThreads = 256, kDnMaxPer = 8, kDnParts = kDnThreads / kDnSteps;
+constexpr int kDnBlocksPerSM = 2;
 constexpr uint32_t kErrBulk = 1u << 8;
 constexpr uint32_t kBulkSpinLimit = 1u << 20;
 __host__ __device__ constexpr size_t dwconv_norm_smem(int rows, int quads, int elem_bytes) {
