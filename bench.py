@@ -11,14 +11,22 @@ depthwise convs, 1000 classes; random-init weights rounded to bf16.
 
 * ``value``: device time of K forward passes through the C ABI with inputs
   resident in HBM (L2 flushed between steps, outside the per-step CUDA-event
-  pair), whole-job tokens/s over all ranks (each rank runs its own B=256
-  shard: weak scaling, no collective on the data path).
-* ``e2e``: the same metric through the public module API with the input copied
-  from pinned host memory and the logits copied back every step.
+  pair), whole-job tokens/s.  The batch is the configured global B=256 split
+  into contiguous row shards over the N ranks (strong scaling, as BASELINE
+  config 4 specifies; no collective on the data path); time = max over ranks.
+* ``prepared``: the same with the operands prepared once, eager and replayed
+  from a captured CUDA graph; ``weak_scaling``: every rank its own B=256 batch.
+* ``multi_gpu_check`` (N > 1): the gathered sharded logits against a
+  single-GPU forward of the same rows, and the config-5 time split against the
+  unsplit forward, as max relative errors.
+* ``e2e``: the same metric through the public module API with each rank's
+  input rows copied from pinned host memory and the logits copied back every
+  step.
 * ``roofline``: the dominant kernel's algorithmic bytes per launch / its
   average CUDA-event duration measured during the timed region.
-* ``cpu_baseline``: the CPU oracle (numpy restatement of the reference path) on a
-  bounded slice of the same batch, rank 0 only.
+* ``cpu_baseline``: the CPU oracle (numpy restatement of the reference path) on
+  the whole batch, rows split over one single-threaded worker per host core,
+  rank 0 at N = 1 only.
 
 ``--impl reference`` times that CPU path alone (rank 0; other ranks exit).
 """
@@ -267,8 +275,16 @@ def committed_traffic(kernel: str, cfg) -> float | None:
 
 
 # ---------------------------------------------------------------- CPU path
-def cpu_forward_time(cfg, rows: int, params_np, seed=3):
-    """Seconds for the numpy oracle (fp32, the reference's precision) on `rows` rows."""
+def _cpu_rows_worker(job):
+    """One worker process: the numpy oracle (fp32) on its rows; returns seconds.
+    Its BLAS pool is limited to one thread, so one worker = one core."""
+    cfg, rows, seed, params_np = job
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(1)
+    except ImportError:
+        pass
     from oracle import alphabet_oracle as A
 
     rng = np.random.default_rng(seed)
@@ -278,14 +294,39 @@ def cpu_forward_time(cfg, rows: int, params_np, seed=3):
     return time.perf_counter() - t0
 
 
-def cpu_threads() -> int:
-    try:
-        from threadpoolctl import threadpool_info
+class CpuBaseline:
+    """The CPU path of the reference restated by the numpy oracle, run on every host
+    core: `rows` rows split over one single-threaded worker process per core (the
+    oracle's loop over T is serial Python, so cores are used by splitting rows;
+    rows are independent).  A step = all `rows` rows; its time is the wall time of
+    the pool (the slowest worker bounds it)."""
 
-        n = [i.get("num_threads", 1) for i in threadpool_info()]
-        return max(n) if n else 1
-    except ImportError:
-        return 1
+    def __init__(self, cfg, rows: int, cores: int | None = None):
+        import multiprocessing as mp
+
+        self.cfg = {k: cfg[k] for k in ("T", "C", "D", "M", "K", "dtype")}
+        self.rows = rows
+        self.cores = max(1, min(cores or os.cpu_count() or 1, rows))
+        self.params = params_numpy(cfg)
+        base, extra = divmod(rows, self.cores)
+        self.split = [base + (1 if i < extra else 0) for i in range(self.cores)]
+        self.pool = mp.get_context("spawn").Pool(self.cores)
+
+    def step(self) -> float:
+        jobs = [(self.cfg, r, 3 + i, self.params) for i, r in enumerate(self.split) if r]
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_rows_worker, jobs, chunksize=1)
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+    def describe(self, secs: float, steps: int) -> str:
+        return (f"{self.rows} rows x T={self.cfg['T']} per step ({steps} step(s), {secs:.2f} s), "
+                f"numpy oracle restating the reference eager path in fp32, rows split over "
+                f"{self.cores} single-threaded worker processes (one per core; the oracle's loop "
+                f"over T is serial, rows are independent, so time scales linearly in rows)")
 
 
 def params_numpy(cfg):
@@ -297,24 +338,25 @@ def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    rows = args.ref_rows
-    p = params_numpy(cfg)
-    for _ in range(args.warmup):
-        cpu_forward_time(cfg, rows, p)
-    times = [cpu_forward_time(cfg, rows, p) for _ in range(args.steps)]
+    rows = args.ref_rows or cfg["B"]
+    cpu = CpuBaseline(cfg, rows)
+    try:
+        for _ in range(args.warmup):
+            cpu.step()
+        times = [cpu.step() for _ in range(args.steps)]
+    finally:
+        cpu.close()
     total = sum(times)
-    tokens = rows * cfg["T"] * args.steps
-    value = tokens / total
-    cores = cpu_threads()
+    value = rows * cfg["T"] * args.steps / total
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": cfg["workload"], "sample_rows_per_step": rows},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{rows} of {cfg['B']} rows x T={cfg['T']} per step, numpy "
-                                   "oracle restating the reference eager path in fp32"},
+        "config": {"workload": cfg["workload"], "global_batch": cfg["B"],
+                   "rows_per_step": rows, "same_config": rows == cfg["B"]},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.cores, "kind": "port",
+                         "sample": cpu.describe(total, args.steps)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -339,8 +381,14 @@ def run_train(args, cfg):
             return 0
         from oracle import alphabet_grad_oracle as G
 
-        rows = args.ref_rows
+        rows = args.ref_rows or 8
         p = params_numpy(cfg)
+        try:
+            from threadpoolctl import threadpool_limits
+
+            threadpool_limits(1)  # the line reports one core
+        except ImportError:
+            pass
         rng = np.random.default_rng(3)
         x = rng.standard_normal((rows, cfg["T"], cfg["C"])).astype(np.float32)
         dl = rng.standard_normal((rows, cfg["K"])).astype(np.float32)
@@ -358,7 +406,7 @@ def run_train(args, cfg):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
             "config": {"workload": cfg["workload"], "sample_rows_per_step": rows},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
                              "sample": f"{rows} of {cfg['B']} rows x T={cfg['T']} per step, numpy "
                                        "backward oracle (forward + VJP) in fp32"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -507,6 +555,65 @@ def run_module(args, cfg):
     return 0
 
 
+def _time_steps(fn, steps, stream, flush, world, dist, dev):
+    """K steps of `fn`, each bracketed by CUDA events on `stream` (L2 flushed before
+    each, outside the pair); barrier + synchronize on both sides; returns the total
+    device time in ms, max over ranks."""
+    import torch
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record(stream)
+        fn()
+        stops[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, stops))], device=dev,
+                     dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def multi_gpu_check(model, x_full, world, rank, dev, dist):
+    """Correctness of the multi-GPU paths inside the scaling run (rank 0 reports):
+    * batch sharding: sharded_forward's gathered logits of the 256 rows against
+      rank 0's single-GPU forward of the same rows;
+    * time split (BASELINE config 5's variant): timesplit_forward of one config-5
+      row over all ranks against the unsplit forward of that row.
+    Both are max relative errors (normwise); None at N=1."""
+    import torch
+
+    from lnet_b200.sharding import sharded_forward
+    from lnet_b200.timesplit import timesplit_forward
+
+    if world == 1:
+        return {"note": "single GPU: nothing to compare"}
+    with torch.no_grad():
+        gathered = sharded_forward(model, x_full)
+        out = {}
+        if rank == 0:
+            single = model(x_full)
+            out["batch_shard_rel_err"] = float((gathered - single).abs().max() /
+                                               single.abs().max())
+        c5 = CONFIGS["5"]
+        m5 = build_model(dict(c5), dev)
+        g = torch.Generator(device=dev).manual_seed(11)
+        x5 = torch.randn(1, c5["T"], c5["C"], generator=g, device=dev).to(torch.bfloat16)
+        split = timesplit_forward(m5, x5)
+        if rank == 0:
+            whole = m5(x5)
+            out["time_split_rel_err"] = float((split - whole).abs().max() / whole.abs().max())
+            out["time_split_case"] = f"config 5, 1 row x T={c5['T']}, {world} ranks"
+    return out if rank == 0 else None
+
+
 def run_b200(args, cfg):
     import ctypes
 
@@ -515,6 +622,8 @@ def run_b200(args, cfg):
 
     from lnet_b200 import _lib
     from lnet_b200.alphabet import _workspace_bytes
+    from lnet_b200.graph import CudaGraphForward
+    from lnet_b200.sharding import shard_bounds
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -527,86 +636,83 @@ def run_b200(args, cfg):
         dist.init_process_group("nccl", device_id=dev)
     lib = _lib.load()
     model = build_model(cfg, dev)
-    x = make_inputs(cfg, dev)
+    x_full = make_inputs(cfg, dev)  # the same seeded batch on every rank
     B, T = cfg["B"], cfg["T"]
+    lo, hi = shard_bounds(B, world, rank)  # strong scaling: this rank's rows of the batch
+    x = x_full[lo:hi].contiguous()
+    b_loc = hi - lo
     act = _lib.LNET_BF16 if cfg["dtype"] == "bf16" else _lib.LNET_F32
     params, _keep = model._effective(dev)
-    req = model._request(x, None, None, None, act)
-    nbytes = _workspace_bytes(params, req)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    logits = torch.empty(B, cfg["K"], device=dev, dtype=torch.float32)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def fwd():
-        st = lib.lnet_b200_alphabet_forward(ctypes.byref(params), ctypes.byref(req),
-                                            ws.data_ptr(), nbytes, logits.data_ptr(), None, None,
-                                            stream.cuda_stream)
-        _lib.check(st, "lnet_b200_alphabet_forward")
-        return _lib.last_launch_count()
+    def c_abi_forward(xt, prepared=False):
+        req = model._request(xt, None, None, None, act)
+        nbytes = _workspace_bytes(params, req)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        logits = torch.empty(xt.shape[0], cfg["K"], device=dev, dtype=torch.float32)
+        if prepared:
+            _lib.check(lib.lnet_b200_alphabet_prepare(ctypes.byref(params), ctypes.byref(req),
+                                                      ws.data_ptr(), nbytes, stream.cuda_stream),
+                       "lnet_b200_alphabet_prepare")
+        fn_c = lib.lnet_b200_alphabet_forward_prepared if prepared else \
+            lib.lnet_b200_alphabet_forward
 
+        def fwd():
+            _lib.check(fn_c(ctypes.byref(params), ctypes.byref(req), ws.data_ptr(), nbytes,
+                            logits.data_ptr(), None, None, stream.cuda_stream),
+                       "lnet_b200_alphabet_forward")
+            return _lib.last_launch_count()
+        return fwd
+
+    # ---- value: the configured workload (global B split over the ranks), C ABI, inputs in
+    # HBM, operands rebuilt in every step
+    fwd = c_abi_forward(x)
     for _ in range(max(args.warmup, 3)):
         fwd()
-    torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    launches = 0
+    launches = [0]
+
+    def counted():
+        launches[0] += fwd()
+
     _lib.profile_enable(True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        for i in range(args.steps):
-            flush.zero_()
-            starts[i].record(stream)
-            launches += fwd()
-            stops[i].record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+        total_ms = _time_steps(counted, args.steps, stream, flush, world, dist, dev)
     prof = _lib.profile_read()
     _lib.profile_enable(False)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
-    total_ms = sum(step_ms)
-    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    tokens_all = B * T * world * args.steps
+    tokens_all = B * T * args.steps
     value = tokens_all / (total_ms / 1e3)
 
-    # Steady-state serving with the operands prepared once (prepare_for_inference_ /
-    # lnet_b200_alphabet_prepare), timed the same way; reported beside `value`, which
-    # rebuilds them in every step.
-    _lib.check(lib.lnet_b200_alphabet_prepare(ctypes.byref(params), ctypes.byref(req),
-                                              ws.data_ptr(), nbytes, stream.cuda_stream),
-               "lnet_b200_alphabet_prepare")
-
-    def fwd_prepared():
-        _lib.check(lib.lnet_b200_alphabet_forward_prepared(
-            ctypes.byref(params), ctypes.byref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
-            None, None, stream.cuda_stream), "lnet_b200_alphabet_forward_prepared")
-
+    # ---- prepared operands (lnet_b200_alphabet_prepare once), eager launches, and the
+    # same prepared forward replayed from a captured CUDA graph
+    fwd_p = c_abi_forward(x, prepared=True)
     for _ in range(max(args.warmup, 3)):
-        fwd_prepared()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    for i in range(args.steps):
-        flush.zero_()
-        starts[i].record(stream)
-        fwd_prepared()
-        stops[i].record(stream)
-    torch.cuda.synchronize()
-    t = torch.tensor([sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, stops))], device=dev,
-                     dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    prepared_ms = float(t.item())
+        fwd_p()
+    prepared_ms = _time_steps(fwd_p, args.steps, stream, flush, world, dist, dev)
+    with torch.no_grad():
+        runner = CudaGraphForward(model, x)
+        for _ in range(max(args.warmup, 3)):
+            runner(x)
+        graph_ms = _time_steps(lambda: runner(x), args.steps, stream, flush, world, dist, dev)
     prepared = {"value": tokens_all / (prepared_ms / 1e3), "unit": UNIT,
                 "ms_per_step": prepared_ms / args.steps,
-                "note": "operands built once (prepare_for_inference_); `value` rebuilds them "
-                        "in every step"}
+                "graph_value": tokens_all / (graph_ms / 1e3),
+                "graph_ms_per_step": graph_ms / args.steps,
+                "note": "operands built once (lnet_b200_alphabet_prepare); `graph_*`: the "
+                        "prepared module forward replayed from a captured CUDA graph "
+                        "(lnet_b200.graph.CudaGraphForward, includes its input copy); `value` "
+                        "rebuilds the operands in every step"}
+
+    # ---- weak scaling: every rank its own full B-row batch (reported beside `value`)
+    weak = None
+    if world > 1 or args.weak:
+        fwd_w = c_abi_forward(x_full)
+        for _ in range(max(args.warmup, 3)):
+            fwd_w()
+        weak_ms = _time_steps(fwd_w, args.steps, stream, flush, world, dist, dev)
+        weak = {"value": B * T * world * args.steps / (weak_ms / 1e3), "unit": UNIT,
+                "ms_per_step": weak_ms / args.steps, "batch_per_gpu": B,
+                "global_batch": B * world}
 
     trace = None
     if args.trace:
@@ -617,23 +723,25 @@ def run_b200(args, cfg):
         _lib.trace_enable(False)
         trace = {k: {ph: round(c / max(v["items"], 1)) for ph, c in v.items() if ph != "items"}
                  | {"items": v["items"]} for k, v in raw.items()}
-    # ---- end to end through the public module API, host buffers, copies inside
+    check = multi_gpu_check(model, x_full, world, rank, dev, dist) if not args.skip_e2e else None
     if args.skip_e2e:
         if rank == 0:
             print(json.dumps({"value": value, "ms_per_step": total_ms / args.steps,
-                              "prepared_ms_per_step": prepared["ms_per_step"],
+                              "prepared": prepared, "weak_scaling": weak,
                               "kernels": _lib_kernels(prof), "trace_cycles_per_item": trace}),
                   flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return 0
-    # Image configs feed uint8 images (normalised + patchified on the GPU by
-    # forward_images); the others feed the token tensor.  Every step copies its
-    # input from pinned host memory and its logits back; lnet_b200.pipeline
-    # overlaps the copy of step k + 1 with the forward of step k.
+
+    # ---- end to end through the public module API: this rank's rows copied from pinned host
+    # memory (uint8 images for the image config, GPU normalise + patchify) and the logits
+    # copied back, every step; the copy of step k+1 overlaps the forward of step k
     from lnet_b200.pipeline import run_pipelined
 
-    model.prepare_for_inference_(sequence_length=T, batch_size=B)  # serving setup
+    model.prepare_for_inference_(sequence_length=T, batch_size=b_loc)  # serving setup
     if cfg["images"]:
-        src_host = make_images(cfg, "cpu").pin_memory()
+        src_host = make_images(cfg, "cpu")[lo:hi].contiguous().pin_memory()
         fn = model.forward_images
     else:
         src_host = x.cpu().pin_memory()
@@ -642,28 +750,34 @@ def run_b200(args, cfg):
     with torch.no_grad():
         warm = max(args.warmup, 3)
         run_pipelined(fn, [src_host] * warm,
-                      [torch.empty(B, cfg["K"]).pin_memory() for _ in range(warm)], dev)
+                      [torch.empty(b_loc, cfg["K"]).pin_memory() for _ in range(warm)], dev)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        outs = [torch.empty(B, cfg["K"], dtype=torch.float32).pin_memory()
+        outs = [torch.empty(b_loc, cfg["K"], dtype=torch.float32).pin_memory()
                 for _ in range(args.steps)]
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         run_pipelined(fn, [src_host] * args.steps, outs, dev, start_event=e0)
         e1.record(stream)
         torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    e2e_local_ms = e0.elapsed_time(e1)
+    e2e_ms = torch.tensor([e2e_local_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = tokens_all / (float(e2e_ms.item()) / 1e3)
+    h2d_gbs = torch.tensor([h2d_bytes * args.steps / (e2e_local_ms / 1e3) / 1e9], device=dev,
+                           dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(h2d_gbs, op=dist.ReduceOp.MIN)
 
     if rank == 0:
         # dominant kernel during the timed region
         dom = max(prof.items(), key=lambda kv: kv[1][0]) if prof else ("", (0.0, 1))
         name, (k_ms, k_n) = dom
         avg_s = k_ms / max(k_n, 1) / 1e3
-        alg = algorithmic_bytes(name, cfg)
+        kcfg = dict(cfg, B=b_loc)
+        alg = algorithmic_bytes(name, kcfg)
         peak, peak_kind = measured_peaks()
         achieved = alg / avg_s / 1e9 if alg and avg_s > 0 else None
         roofline = {
@@ -671,7 +785,7 @@ def run_b200(args, cfg):
             "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak if achieved else None,
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-            "traffic": committed_traffic(name, cfg),
+            "traffic": committed_traffic(name, kcfg),
             "algorithmic_bytes_per_launch": alg,
             "avg_launch_ms": avg_s * 1e3,
             "share_of_step": k_ms / sum(v[0] for v in prof.values()) if prof else None,
@@ -679,18 +793,22 @@ def run_b200(args, cfg):
         kernels = {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            p = params_numpy(cfg)
-            rows = args.cpu_rows
-            secs = cpu_forward_time(cfg, rows, p)
-            cpu = {"value": rows * T / secs, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                   "sample": f"{rows} of {B} rows x T={T} (one forward, {secs:.1f} s), numpy "
-                             "oracle restating the reference eager path in fp32"}
+            base = CpuBaseline(cfg, args.cpu_rows or B)
+            try:
+                base.step()  # worker start-up and imports, untimed
+                secs = base.step()
+            finally:
+                base.close()
+            cpu = {"value": base.rows * T / secs, "unit": UNIT, "cores": base.cores,
+                   "kind": "port", "sample": base.describe(secs, 1)}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic (uint8 images / N(0,1), random-init weights)",
-            "config": {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * world,
+            "config": {"workload": cfg["workload"], "global_batch": B,
+                       "batch_per_gpu": [shard_bounds(B, world, r)[1] - shard_bounds(B, world, r)[0]
+                                         for r in range(world)],
                        "seq_len": T, "raw_channels": cfg["C"], "model_dim": cfg["D"],
                        "modes": cfg["M"], "classes": cfg["K"], "parallelism": f"batch{world}",
                        "l2": "256 MiB flush between steps, outside the per-step event pair"},
@@ -699,10 +817,14 @@ def run_b200(args, cfg):
                              if cfg["images"] else "tokens",
                     "overlap": "copy of step k+1 overlaps the forward of step k",
                     "module": "B200Alphabet after prepare_for_inference_",
-                    "h2d_bytes_per_step": h2d_bytes,
+                    "h2d_bytes_per_step": h2d_bytes * world if B % world == 0 else None,
+                    "h2d_bytes_per_step_rank0": h2d_bytes,
+                    "h2d_gbs_per_rank_min": float(h2d_gbs.item()),
                     "d2h_bytes_per_step": B * cfg["K"] * 4},
             "prepared": prepared,
-            "gpu_launches": launches,
+            "weak_scaling": weak,
+            "multi_gpu_check": check,
+            "gpu_launches": launches[0],
             "roofline": roofline,
             "clocks": clocks.summary(),
             "kernels": kernels,
@@ -725,11 +847,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="4")
-    ap.add_argument("--cpu-rows", type=int, default=128)
-    ap.add_argument("--ref-rows", type=int, default=16)
+    ap.add_argument("--cpu-rows", type=int, default=0,
+                    help="rows of the CPU baseline step (default: the whole batch)")
+    ap.add_argument("--ref-rows", type=int, default=0,
+                    help="rows per reference-arm step (default: the whole batch)")
+    ap.add_argument("--weak", action="store_true",
+                    help="also time the weak-scaling workload at N=1 (always at N>1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
-                    help="per-GPU batch override (small cases for profiling only)")
+                    help="global batch override (small cases for profiling only)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
     ap.add_argument("--mode", choices=["forward", "train"], default="forward",
                     help="train: forward + backward + SGD step (one GPU, ALPHABET configs)")

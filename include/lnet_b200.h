@@ -104,6 +104,13 @@ int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
                                size_t workspace_bytes, float *logits, float *writer_moments,
                                float *reader_moments, lnet_stream_t stream);
 
+/* Test hook, one shot: the next fused-route forward in this process looks for
+ * look-back records under a tag that no record carries, so every look-back
+ * gives up after a short bounded wait (64 polls), sets the look-back error bit
+ * and the call writes NaN logits.  Used by the tests that check that a
+ * give-up surfaces; no reference counterpart. */
+int lnet_b200_debug_inject_lookback_miss(void);
+
 /* Route selection for lnet_b200_alphabet_forward (process-wide):
  * 0 = automatic (the fused unit-grid kernels when the request has no
  * metadata, bf16 activations and a compiled shape; the general route
@@ -140,8 +147,10 @@ int lnet_b200_alphabet_forward_prepared(const lnet_b200_alphabet_params *params,
  * (writer stem, writer drive, writer synthesis, reader drive), 1 << 4 / 1 << 5
  * look-back (writer / reader), 1 << 6 / 1 << 7 tile loads (writer / reader) on
  * the fused route; 1 << 8 a bulk input copy of the general route's conv +
- * RMSNorm kernel.  Nonzero means the results of that call are invalid.  No
- * reference counterpart (the reference has no device-side waits). */
+ * RMSNorm kernel.  Nonzero means the results of that call are invalid, and
+ * that call wrote NaN to every logit (the head reads this word before writing
+ * them), so a give-up never yields finite logits.  No reference counterpart
+ * (the reference has no device-side waits). */
 int lnet_b200_alphabet_device_status(const lnet_b200_alphabet_params *params,
                                      const lnet_b200_alphabet_request *req,
                                      const void *workspace, size_t workspace_bytes,
@@ -270,8 +279,10 @@ int lnet_b200_laplace_forward(const double *raw_decay, const double *residues,
  * library holds it until exit).  Shapes needing more scratch than that
  * (lnet_b200_laplace_workspace_size) fail with LNET_ERR_WORKSPACE.  The first
  * call on a device looks up the array's device address; make that first call
- * before any stream capture.  All calls share the array: calls that overlap
- * on the GPU race.  No counterpart in the reference. */
+ * before any stream capture.  The address is kept for the life of the
+ * process: do not use this entry point on a device after cudaDeviceReset of
+ * that device.  All calls share the array: calls that overlap on the GPU
+ * race.  No counterpart in the reference. */
 size_t lnet_b200_laplace_noalloc_max_scratch_bytes(void);
 int lnet_b200_laplace_forward_noalloc(const double *raw_decay, const double *residues,
                                       const double *direct, const double *bias,

@@ -22,19 +22,24 @@ namespace lnet {
 
 constexpr int kScanChunk = 64;
 
-// Host part of the look-back record tags (record_tag): starts from a
-// time-derived value and increments per call, so stale words left in a reused
-// workspace by earlier calls or processes do not match (0 is never used).
-static std::atomic<uint32_t> g_epoch{0};
-uint32_t next_epoch() {
-  uint32_t e = g_epoch.fetch_add(1) + 1;
-  if (e == 1) {
-    uint32_t seed = (uint32_t)std::chrono::steady_clock::now().time_since_epoch().count() | 1u;
-    g_epoch.store(seed);
-    e = seed;
-  }
-  return e == 0 ? next_epoch() : e;
+// Host part of the look-back record tags (record_tag): one time-derived,
+// nonzero value per process, mixed into every tag so that words left in reused
+// device memory by another process or by other data do not read as records.
+// The per-call part is the workspace's device counter, which only increases.
+uint32_t process_tag_seed() {
+  static const uint32_t seed = [] {
+    const uint32_t s =
+        (uint32_t)std::chrono::steady_clock::now().time_since_epoch().count() * 0x9E3779B1u;
+    return s == 0u ? 0x2545F491u : s;
+  }();
+  return seed;
 }
+
+// One-shot test hook (lnet_b200_debug_inject_lookback_miss): the next fused
+// forward's look-backs expect a tag no record carries and give up after a
+// short bounded wait, which sets the look-back error bit.
+static std::atomic<int> g_inject_miss{0};
+int take_lookback_injection() { return g_inject_miss.exchange(0); }
 
 int sm_count() {
   int dev = 0, n = 0;
@@ -442,12 +447,12 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
 
 static int head_run(const lnet_b200_alphabet_params *p, int64_t B, const float *wm,
                     const float *rm, float *feats, float *partial, float *logits,
-                    cudaStream_t st) {
+                    cudaStream_t st, const uint32_t *status) {
   const int M = p->modes;
   head_features_kernel<<<grid_for(B * 14 * M), 256, 0, st>>>(wm, rm, feats, B, M);
   LNET_TRY(after_launch("head_features_kernel"));
   return head_gemm(feats, B, 14 * M, p->head_weight, p->head_bias, logits, p->output_dim, partial,
-                   st);
+                   st, status);
 }
 
 static int plan_all(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
@@ -478,6 +483,11 @@ static bool use_fused(const lnet_b200_alphabet_params *p, const lnet_b200_alphab
 }  // namespace lnet
 
 using namespace lnet;
+
+extern "C" int lnet_b200_debug_inject_lookback_miss(void) {
+  g_inject_miss.store(1);
+  return LNET_OK;
+}
 
 extern "C" int lnet_b200_set_route(int route) {
   if (route != 0 && route != 1) return fail(LNET_ERR_INVALID_ARGUMENT, "route must be 0 or 1");
@@ -550,7 +560,7 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
     float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
     LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, prepared, st));
     return head_gemm(pl.fused.feats, B, 14 * M, params->head_weight, params->head_bias, logits,
-                     params->output_dim, pl.fused.head_partial, st);
+                     params->output_dim, pl.fused.head_partial, st, pl.fused.flags + 2);
   }
   LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
   float *wm = writer_moments ? writer_moments : pl.moments;
@@ -561,7 +571,7 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
       LNET_TRY(forward_generic_normed<__nv_bfloat16>(params, req, pl, wm, rm, st));
     else
       LNET_TRY(forward_generic_normed<float>(params, req, pl, wm, rm, st));
-    return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st);
+    return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st, pl.status);
   }
   if (req->x_dtype == LNET_BF16)
     LNET_TRY(stem_generic<__nv_bfloat16>(params, req, pl, pl.first_local, st));
@@ -569,7 +579,7 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
     LNET_TRY(stem_generic<float>(params, req, pl, pl.first_local, st));
   LNET_TRY(writer_generic(params, req, pl.first_local, pl, pl.stream, wm, st));
   LNET_TRY(reader_generic(params, req, pl.stream, pl, rm, st, /*ts_ready=*/true));
-  return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st);
+  return head_run(params, B, wm, rm, pl.feats, pl.head_partial, logits, st, pl.status);
 }
 
 extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,

@@ -284,8 +284,10 @@ struct FusedArgs {
   __nv_bfloat16 *out;       // writer stream
   double *rowsum;           // this block's per-row moment sums [B][7M]
   unsigned long long *rec;  // [B * nch][2][4][2][M] tagged look-back records
-  uint32_t epoch;           // host part of this call's record tag (fresh per call)
-  const uint32_t *epoch_word;  // device part (replay counter, see record_tag)
+  uint32_t epoch;           // host part of this call's record tag (per-process seed)
+  const uint32_t *epoch_word;  // device part (per-call counter, see record_tag)
+  uint32_t read_xor;        // 0; nonzero only under the look-back miss test hook
+  uint32_t spin_limit;      // polls before a look-back wait gives up
   uint32_t *counter;
   uint32_t *error;
   int trace;       // 1: accumulate per-phase cycles of CTA thread 0 into g_fused_trace
@@ -361,12 +363,14 @@ __device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, flo
   ci = fmaf(ar, bi, fmaf(ai, br, ci));
 }
 
-// Tag of one call's look-back records: the host's per-call epoch (time-seeded,
-// never repeated in a process) mixed with the workspace's replay counter (so
-// that replays of a captured graph differ too).  Never 0: zero-filled memory
-// must not read as a published record.
-__device__ __forceinline__ uint32_t record_tag(uint32_t host_epoch, const uint32_t *epoch_word) {
-  const uint32_t t = host_epoch ^ (__ldcg(epoch_word) * 0x9E3779B1u);
+// Tag of one call's look-back records: the workspace's call counter (advanced
+// on the device at the end of every call, so eager calls and replays of a
+// captured graph alike never reuse a tag within a workspace's lifetime, until
+// the 32-bit counter wraps) XOR a per-process seed (so that data that other
+// uses of the memory left behind does not read as records).  Never 0:
+// zero-filled memory must not read as a published record.
+__device__ __forceinline__ uint32_t record_tag(uint32_t host_seed, const uint32_t *epoch_word) {
+  const uint32_t t = host_seed ^ __ldcg(epoch_word);
   return t == 0u ? 0x5BD1E995u : t;
 }
 
@@ -443,8 +447,8 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
                                            int col_re, int col_im, int n, int64_t row,
                                            int64_t chunk, int64_t n_chunks, const float *K,
                                            unsigned long long *rec, uint32_t host_epoch,
-                                           const uint32_t *epoch_word,
-                                           uint32_t *error,
+                                           const uint32_t *epoch_word, uint32_t read_xor,
+                                           uint32_t spin, uint32_t *error,
                                            uint8_t *s_slab, int slab_s, float *sc,
                                            double *rowsum, int trace, int kid,
                                            const LookbackPrefetch &pre,
@@ -556,6 +560,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
   // the chunk's last state.
   if (publisher_group && live) {
     const uint32_t epoch = record_tag(host_epoch, epoch_word);  // this call's record tag
+    const uint32_t rtag = epoch ^ read_xor;  // the tag looked for (== epoch outside tests)
     const int64_t item = row * n_chunks + chunk;  // record index (row-major)
     unsigned long long *my = rec + item * 16 * M;
     float g_r[4], g_i[4];  // chunk-local last four states
@@ -575,7 +580,7 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const unsigned long long xr = pre.w[2 * k], xi = pre.w[2 * k + 1];
-        done &= (uint32_t)(xr >> 32) == epoch && (uint32_t)(xi >> 32) == epoch;
+        done &= (uint32_t)(xr >> 32) == rtag && (uint32_t)(xi >> 32) == rtag;
         p_r[k] = __uint_as_float((uint32_t)xr);
         p_i[k] = __uint_as_float((uint32_t)xi);
       }
@@ -583,12 +588,12 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         atomicAdd(&g_fused_trace[kid][9], 1ull);
         if (done) atomicAdd(&g_fused_trace[kid][8], 1ull);
       }
-      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+      for (uint32_t it = 0; it < spin && !done; ++it) {
         bool ok = true;  // inclusive record of the previous chunk
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          ok &= ld_tag(pv + 8 * M + (2 * k) * M + m, epoch, p_r[k]);
-          ok &= ld_tag(pv + 8 * M + (2 * k + 1) * M + m, epoch, p_i[k]);
+          ok &= ld_tag(pv + 8 * M + (2 * k) * M + m, rtag, p_r[k]);
+          ok &= ld_tag(pv + 8 * M + (2 * k + 1) * M + m, rtag, p_i[k]);
         }
         if (ok) {
           done = true;
@@ -597,8 +602,8 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         ok = true;  // its aggregate, completed by the true end X of chunk - 2
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          ok &= ld_tag(pv + (2 * k) * M + m, epoch, p_r[k]);
-          ok &= ld_tag(pv + (2 * k + 1) * M + m, epoch, p_i[k]);
+          ok &= ld_tag(pv + (2 * k) * M + m, rtag, p_r[k]);
+          ok &= ld_tag(pv + (2 * k + 1) * M + m, rtag, p_i[k]);
         }
         if (!ok) {
           __nanosleep(32);
@@ -609,15 +614,15 @@ __device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, 
         for (int64_t qq = chunk - 2; qq >= 0 && walk_ok; --qq) {
           const unsigned long long *qv = rec + (row * n_chunks + qq) * 16 * M;
           bool found = false;
-          for (uint32_t jt = 0; jt < kSpinLimit; ++jt) {
+          for (uint32_t jt = 0; jt < spin; ++jt) {
             float er, ei;
-            if (ld_tag(qv + 8 * M + m, epoch, er) && ld_tag(qv + 9 * M + m, epoch, ei)) {
+            if (ld_tag(qv + 8 * M + m, rtag, er) && ld_tag(qv + 9 * M + m, rtag, ei)) {
               cmac(mr, mi, er, ei, xr, xi);
               qq = -1;  // inclusive: the walk ends here
               found = true;
               break;
             }
-            if (ld_tag(qv + m, epoch, er) && ld_tag(qv + M + m, epoch, ei)) {
+            if (ld_tag(qv + m, rtag, er) && ld_tag(qv + M + m, rtag, ei)) {
               cmac(mr, mi, er, ei, xr, xi);
               float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
               mr = nr;
@@ -1020,7 +1025,8 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
     chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
-                                     a.n_chunks, s_k, a.rec, a.epoch, a.epoch_word, a.error,
+                                     a.n_chunks, s_k, a.rec, a.epoch, a.epoch_word, a.read_xor,
+                                     a.spin_limit, a.error,
                                      gs + P::G_XS,
                                      P::SLAB_S, s_scan,
                                      a.rowsum + b * 7 * M, a.trace,
@@ -1235,7 +1241,8 @@ __global__ void __launch_bounds__(kFusedThreads, 2)
     LNET_TRACE(4);
     // 4. scan + look-back + moments
     chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
-                            a.epoch, a.epoch_word, a.error, nullptr, 0, s_scan,
+                            a.epoch, a.epoch_word, a.read_xor, a.spin_limit, a.error, nullptr,
+                            0, s_scan,
                             a.rowsum + b * 7 * M, a.trace, a.kernel_id,
                             pre);
     sm100::tc_fence_before();
@@ -1264,14 +1271,13 @@ __device__ __forceinline__ float finalize_moment(const double *rs, int modes, in
 // One thread per (row, feature): raw moments [b][k*M + m] of both blocks and
 // the radial-log features of src/lnet/alphabet.py:29-46 (the arithmetic of
 // radial_feature) into feats[b][blk * 7M + j].
-// Also advances the look-back epoch for the next call (never 0).
+// Also advances the workspace's look-back call counter for the next call.
 __global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *__restrict__ wm,
                                       float *__restrict__ rm, float *__restrict__ feats,
                                       int64_t batch, int64_t steps, int modes,
                                       uint32_t *__restrict__ epoch_word) {
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    const uint32_t e = *epoch_word + 1u;
-    *epoch_word = e == 0u ? 1u : e;
+    *epoch_word = *epoch_word + 1u;
   }
   const int W = 7 * modes;
   const int64_t n = batch * 2 * W;
@@ -1320,7 +1326,8 @@ inline bool fused_supported(const lnet_b200_alphabet_params *p,
 }
 
 int sm_count();
-uint32_t next_epoch();
+uint32_t process_tag_seed();
+int take_lookback_injection();
 int fused_trace_enabled();
 
 // Tiled 3-D tensor map of a [B][T][W] bf16 tensor with an 8 x 144 x 1 box
@@ -1390,7 +1397,13 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.out = w.stream;
   wa.rowsum = w.rowsum;
   wa.rec = w.wrec;
-  wa.epoch = next_epoch();
+  wa.epoch = process_tag_seed();
+  wa.read_xor = 0;
+  wa.spin_limit = kSpinLimit;
+  if (take_lookback_injection()) {  // test hook: every look-back misses and gives up early
+    wa.read_xor = 0x80000000u;
+    wa.spin_limit = 64;
+  }
   wa.epoch_word = w.epoch_word;
   wa.counter = counters;
   wa.error = counters + 2;

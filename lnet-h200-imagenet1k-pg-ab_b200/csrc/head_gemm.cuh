@@ -195,13 +195,18 @@ __global__ void __launch_bounds__(kHeadThreads) head_gemm_kernel(
 }
 
 // logits[b, k] = bias[k] + sum_z partial[z][b][k], summed in a fixed order.
+// `status` (may be NULL): the forward's device error word; when any bounded
+// wait of the forward gave up (a look-back, a tile or an MMA completion), the
+// moments behind the logits are not trustworthy and every logit is NaN.
 __global__ void head_reduce_kernel(const float *__restrict__ partial, const float *__restrict__ bias,
-                                   float *__restrict__ logits, int64_t n, int K, int splits) {
+                                   float *__restrict__ logits, int64_t n, int K, int splits,
+                                   const uint32_t *__restrict__ status) {
+  const bool poisoned = status && __ldcg(status) != 0u;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     float acc = __ldg(bias + (int)(i % K));
     for (int z = 0; z < splits; ++z) acc += partial[z * n + i];
-    logits[i] = acc;
+    logits[i] = poisoned ? __int_as_float(0x7fc00000) : acc;
   }
 }
 
@@ -210,9 +215,11 @@ constexpr int kHeadSplits = 4;  // measured best at B=256, K=1000 (6 and 11 are 
 inline size_t head_partial_floats(int64_t B, int K) { return (size_t)kHeadSplits * B * K; }
 
 // logits [B, K] from features [B, width]; `partial` holds head_partial_floats(B, K)
-// floats.  A wait that gives up writes NaN logits.
+// floats.  A wait that gives up (here, or earlier in the forward: a nonzero
+// `status` word) writes NaN logits.
 inline int head_gemm(const float *feats, int64_t B, int width, const float *G, const float *bias,
-                     float *logits, int K, float *partial, cudaStream_t st) {
+                     float *logits, int K, float *partial, cudaStream_t st,
+                     const uint32_t *status = nullptr) {
   LNET_TRY(cuda_check(cudaFuncSetAttribute(head_gemm_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem),
                       "cudaFuncSetAttribute(head_gemm_kernel)"));
@@ -223,7 +230,7 @@ inline int head_gemm(const float *feats, int64_t B, int width, const float *G, c
   LNET_TRY(after_launch("head_gemm_kernel"));
   const int64_t n = B * K;
   const int blocks = (int)std::min<int64_t>(cdiv(n, 256), 148 * 8);
-  head_reduce_kernel<<<blocks, 256, 0, st>>>(partial, bias, logits, n, K, kHeadSplits);
+  head_reduce_kernel<<<blocks, 256, 0, st>>>(partial, bias, logits, n, K, kHeadSplits, status);
   return after_launch("head_reduce_kernel");
 }
 

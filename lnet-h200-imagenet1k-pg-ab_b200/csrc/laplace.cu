@@ -146,9 +146,19 @@ __global__ void laplace_reduce_kernel(const TX *__restrict__ x, const double *__
   }
 }
 
-static size_t laplace_partial_bytes(int64_t batch, int64_t steps, int dim, int modes) {
-  int64_t n_slices = cdiv((int64_t)modes * dim, kSlice);
-  return (size_t)n_slices * batch * steps * dim * sizeof(double);
+// Scratch bytes of one call (per-slice partial outputs), or false when the
+// product does not fit in 64 bits (the shape is refused before any launch).
+static bool laplace_partial_bytes(int64_t batch, int64_t steps, int dim, int modes,
+                                  size_t *bytes) {
+  const uint64_t n_slices = (uint64_t)cdiv((int64_t)modes * dim, kSlice);
+  uint64_t v = n_slices;
+  if (__builtin_mul_overflow(v, (uint64_t)batch, &v) ||
+      __builtin_mul_overflow(v, (uint64_t)steps, &v) ||
+      __builtin_mul_overflow(v, (uint64_t)dim, &v) ||
+      __builtin_mul_overflow(v, (uint64_t)sizeof(double), &v))
+    return false;
+  *bytes = (size_t)v;
+  return true;
 }
 
 template <typename TX>
@@ -186,7 +196,9 @@ extern "C" int lnet_b200_laplace_workspace_size(int64_t batch, int64_t steps, in
   if (!bytes) return fail(LNET_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
   if (batch < 0 || steps < 0 || model_dim < 1 || modes < 1)
     return fail(LNET_ERR_INVALID_ARGUMENT, "invalid laplace shape");
-  *bytes = laplace_partial_bytes(batch, steps, model_dim, modes);
+  if (!laplace_partial_bytes(batch, steps, model_dim, modes, bytes))
+    return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: workspace size overflows (B=%lld, T=%lld)",
+                (long long)batch, (long long)steps);
   return LNET_OK;
 }
 
@@ -204,7 +216,10 @@ extern "C" int lnet_b200_laplace_forward(const double *raw_decay, const double *
   if (!raw_decay || !residues || !direct || !bias || !x || !y)
     return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: NULL tensor pointer");
   if (batch > 65535) return fail(LNET_ERR_UNSUPPORTED, "laplace: batch > 65535");
-  size_t need = laplace_partial_bytes(batch, steps, model_dim, modes);
+  size_t need = 0;
+  if (!laplace_partial_bytes(batch, steps, model_dim, modes, &need))
+    return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: workspace size overflows (B=%lld, T=%lld)",
+                (long long)batch, (long long)steps);
   if (!workspace || workspace_bytes < need)
     return fail(LNET_ERR_WORKSPACE, "laplace: workspace of %zu bytes < required %zu",
                 workspace_bytes, need);
@@ -241,7 +256,10 @@ static __device__ __align__(256) double g_noalloc_scratch[kNoAllocScratchBytes /
 
 // Device address of g_noalloc_scratch per device.  In host code the symbol
 // name is only a host-side stand-in, so the address is looked up once per
-// device (with that device current) and reused.
+// device (with that device current, by the first call on that device) and
+// reused for the life of the process.  cudaDeviceReset ends the context that
+// address belongs to: do not call this entry point on a device after a
+// cudaDeviceReset of it.
 constexpr int kMaxDevices = 64;
 static double *g_noalloc_ptr[kMaxDevices] = {};
 static std::mutex g_noalloc_mutex;
@@ -283,7 +301,10 @@ extern "C" int lnet_b200_laplace_forward_noalloc(const double *raw_decay, const 
   if (batch > 65535) return fail(LNET_ERR_UNSUPPORTED, "laplace: batch > 65535");
   if (x_dtype != LNET_F64 && x_dtype != LNET_F32)
     return fail(LNET_ERR_UNSUPPORTED, "laplace: x dtype must be float32 or float64");
-  size_t need = laplace_partial_bytes(batch, steps, model_dim, modes);
+  size_t need = 0;
+  if (!laplace_partial_bytes(batch, steps, model_dim, modes, &need))
+    return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: scratch size overflows (B=%lld, T=%lld)",
+                (long long)batch, (long long)steps);
   if (need > kNoAllocScratchBytes)
     return fail(LNET_ERR_WORKSPACE,
                 "laplace (no-alloc): this shape needs %zu bytes of scratch but the built-in "

@@ -150,7 +150,7 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
                               p->reader_raw_frequency, tp.a_tab + 2 * M, tp.a_tab + 3 * M,
                               tp.a_tab + 6 * M, tp.a_tab + 7 * M, nullptr, 1, &rq, D, M, pr,
                               tp.m2, /*write_states=*/true, st));
-  return head_run(p, B, tp.m1, tp.m2, tp.feats, tp.head_partial, logits, st);
+  return head_run(p, B, tp.m1, tp.m2, tp.feats, tp.head_partial, logits, st, nullptr);
 }
 
 // ---------------------------------------------------------------- backward kernels

@@ -9,7 +9,11 @@ messages for malformed metadata (src/lnet/alphabet_backbone.py:163-201,
 522-591).  The forward pass itself is one call into the C ABI
 (``lnet_b200_alphabet_forward``); there is no CPU path: non-CUDA inputs raise.
 
-It is an inference module: the CUDA path computes no gradients.
+In eval mode (or under ``torch.no_grad``) the forward is that one call.  In
+training mode with gradients enabled it runs the autograd function of
+``lnet_b200.training`` instead: the fp32 training forward
+(``lnet_b200_alphabet_train_forward``) keeps the activations and
+``lnet_b200_alphabet_backward`` returns the parameter and input gradients.
 """
 
 from __future__ import annotations
@@ -427,7 +431,9 @@ def _prepared_workspace(model, params, req, need: int, device, stream):
         if prep is not None and prep["key"][0] == device and prep["cap"] >= cap:
             ws, cap = prep["ws"], prep["cap"]  # parameters changed: rebuild in place
         else:
-            ws = torch.empty(max(cap, 1), dtype=torch.uint8, device=device)
+            # zero-filled once: no word of a fresh persistent workspace can pose as a
+            # look-back record (tag 0 is never used)
+            ws = torch.zeros(max(cap, 1), dtype=torch.uint8, device=device)
         prep = model._prep = {"key": key, "ws": ws, "cap": cap, "fused": False}
     if fused and not prep["fused"]:
         with torch.cuda.device(device):

@@ -46,6 +46,35 @@ def rel_err(got, ref) -> float:
     return float(np.abs(got - ref).max()) / scale if ref.size else 0.0
 
 
+def elem_rel_err(got, ref, floor_frac: float = 1e-3) -> float:
+    """Max elementwise relative error, max_i |got_i - ref_i| / max(|ref_i|, floor),
+    with the floor at `floor_frac` x max|ref| so that entries near zero (moments of
+    nearly silent modes, logits near 0) are measured against a stated absolute
+    scale instead of dividing by ~0."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if not ref.size:
+        return 0.0
+    floor = max(floor_frac * float(np.abs(ref).max()), 1e-30)
+    return float((np.abs(got - ref) / np.maximum(np.abs(ref), floor)).max())
+
+
+def record_margin(case: str, got, ref, gate: float) -> tuple[float, float]:
+    """Normwise and elementwise (floor 1e-3 x max|ref|) errors of one parity check.
+    When LNET_PARITY_LOG names a file, one JSON line per check is appended to it
+    (case, both errors, the gate), which is how the achieved margins are collected."""
+    import json
+    import os
+
+    nw, ew = rel_err(got, ref), elem_rel_err(got, ref)
+    path = os.environ.get("LNET_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"case": case, "normwise": nw, "elementwise": ew,
+                                "gate": gate}) + "\n")
+    return nw, ew
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     import torch

@@ -31,7 +31,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("LNET_REFERENCE_SRC", "/root/reference/src"))
+# the reference checkout: LNET_REFERENCE_SRC, else a sibling `reference/src` of this repo
+sys.path.insert(0, os.environ.get("LNET_REFERENCE_SRC",
+                                  str(HERE.parents[2] / "reference" / "src")))
 
 from lnet import Alphabet  # noqa: E402
 from lnet.laplace import PoleResidueTemporalMixing  # noqa: E402

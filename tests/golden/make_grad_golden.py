@@ -36,7 +36,9 @@ from torch.nn.utils import parametrize
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-sys.path.insert(0, os.environ.get("LNET_REFERENCE_SRC", "/root/reference/src"))
+# the reference checkout: LNET_REFERENCE_SRC, else a sibling `reference/src` of this repo
+sys.path.insert(0, os.environ.get("LNET_REFERENCE_SRC",
+                                  str(HERE.parents[2] / "reference" / "src")))
 
 from make_golden import build_alphabet, make_inputs, params_of  # noqa: E402
 

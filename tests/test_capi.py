@@ -50,6 +50,26 @@ def test_error_paths_without_gpu():
     assert lib.lnet_b200_version().startswith(b"lnet_b200")
 
 
+def test_laplace_scratch_size_overflow_is_refused_without_gpu():
+    """A shape whose scratch size wraps 64 bits is refused before any launch, by the
+    size query and by both forward entry points (the no-alloc one must not let a
+    wrapped size pass its 8 MiB check)."""
+    from lnet_b200 import _lib
+
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    huge = 1 << 62
+    st = lib.lnet_b200_laplace_workspace_size(2, huge, 16, 8, ctypes.byref(n))
+    assert st == _lib.LNET_ERR_INVALID_ARGUMENT and "overflow" in _lib.last_error()
+    dummy = ctypes.c_void_p(256)  # never dereferenced: the shape is refused first
+    st = lib.lnet_b200_laplace_forward_noalloc(dummy, dummy, dummy, dummy, 16, 8, 1.0, 0.0,
+                                               _lib.LNET_F32, dummy, 2, huge, dummy, None)
+    assert st == _lib.LNET_ERR_INVALID_ARGUMENT and "overflow" in _lib.last_error()
+    st = lib.lnet_b200_laplace_forward(dummy, dummy, dummy, dummy, 16, 8, 1.0, 0.0,
+                                       _lib.LNET_F32, dummy, 2, huge, dummy, dummy, 1 << 20, None)
+    assert st == _lib.LNET_ERR_INVALID_ARGUMENT and "overflow" in _lib.last_error()
+
+
 def _struct_fields(name: str) -> list[str]:
     text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "lnet_b200.h").read_text(), flags=re.S)
     body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), text, flags=re.S)

@@ -24,7 +24,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 import torch
-from conftest import rel_err
+from conftest import record_margin, rel_err
 
 from lnet_b200 import B200PoleResidueTemporalMixing, _lib
 from lnet_b200.alphabet import _workspace_bytes
@@ -89,9 +89,11 @@ def test_config4_full_fused_route(cuda_device):
         sub, status_sub = _forward_with_status(model, x[rows].contiguous())
     assert status_sub == 0
     assert rel_err(sub.cpu().numpy(), logits[rows].cpu().numpy()) <= 1e-5
-    # oracle on full-length rows
-    ref = _oracle_rows(cfg, x, [0, 255])
-    assert rel_err(logits[[0, 255]].cpu().numpy(), ref) <= 2e-2
+    # oracle (float64) on 32 full-length rows spread over the batch
+    rows = [int(r) for r in np.linspace(0, cfg["B"] - 1, 32).round()]
+    ref = _oracle_rows(cfg, x, rows)
+    nw, _ = record_margin("config4:fused:32rows:logits", logits[rows].cpu().numpy(), ref, 2e-2)
+    assert nw <= 2e-2
     # general route on the same bf16 inputs
     _lib.set_route(_lib.ROUTE_GENERAL)
     try:
@@ -111,7 +113,8 @@ def test_config2_full_fp32(cuda_device):
     assert status == 0
     assert rel_err(sub.cpu().numpy(), logits[[3, 100]].cpu().numpy()) <= 1e-5
     ref = _oracle_rows(cfg, x, [3, 100])
-    assert rel_err(logits[[3, 100]].cpu().numpy(), ref) <= 1e-4
+    nw, _ = record_margin("config2:rows3,100:logits", logits[[3, 100]].cpu().numpy(), ref, 1e-4)
+    assert nw <= 1e-4
 
 
 def test_config3_full_irregular_metadata(cuda_device):
@@ -132,7 +135,8 @@ def test_config3_full_irregular_metadata(cuda_device):
         sub = model(x[rows].contiguous(), **{k: v[rows].contiguous() for k, v in meta.items()})
     assert rel_err(sub.cpu().numpy(), logits[rows].cpu().numpy()) <= 1e-5
     ref = _oracle_rows(cfg, x, rows, {k: v.cpu() for k, v in meta.items()})
-    assert rel_err(logits[rows].cpu().numpy(), ref) <= 1e-4
+    nw, _ = record_margin("config3:rows1,40:logits", logits[rows].cpu().numpy(), ref, 1e-4)
+    assert nw <= 1e-4
 
 
 def test_config5_full_long_sequence(cuda_device):
@@ -144,7 +148,8 @@ def test_config5_full_long_sequence(cuda_device):
     assert torch.isfinite(logits).all()
     assert rel_err(sub.cpu().numpy(), logits[[7]].cpu().numpy()) <= 1e-5
     ref = _oracle_rows(cfg, x, [7])
-    assert rel_err(logits[[7]].cpu().numpy(), ref) <= 2e-2
+    nw, _ = record_margin("config5:row7:logits", logits[[7]].cpu().numpy(), ref, 2e-2)
+    assert nw <= 2e-2
 
 
 def test_config1_full_laplace(cuda_device):
@@ -165,4 +170,5 @@ def test_config1_full_laplace(cuda_device):
     y = layer.to(cuda_device)(x.to(cuda_device))
     ref = L.laplace_forward(x.numpy(), layer.raw_decay.detach().cpu().numpy(),
                             residues.numpy(), direct.numpy(), np.zeros(c))
-    assert rel_err(y.cpu().numpy(), ref) <= 1e-6
+    nw, _ = record_margin("config1:laplace:y", y.cpu().numpy(), ref, 1e-6)
+    assert nw <= 1e-6

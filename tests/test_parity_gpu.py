@@ -13,7 +13,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 import torch
-from conftest import golden_names, golden_params, load_golden, rel_err
+from conftest import golden_names, golden_params, load_golden, record_margin, rel_err
 
 from lnet_b200 import AlphabetConfig, B200Alphabet, B200PoleResidueTemporalMixing
 from oracle import alphabet_oracle as A
@@ -49,13 +49,19 @@ def test_alphabet_matches_reference_golden(name, cuda_device):
         logits, wm, rm = model(x, **meta_of(z, cuda_device), return_moments=True)
     torch.cuda.synchronize()
     tol_l, tol_m = (2e-2, 2e-2) if bf16 else (1e-4, 5e-4)
-    assert rel_err(logits.cpu().numpy(), z["out.logits"]) <= tol_l
-    assert rel_err(wm.cpu().numpy(), z["out.writer_moments"]) <= tol_m
-    assert rel_err(rm.cpu().numpy(), z["out.reader_moments"]) <= tol_m
+    nw, _ = record_margin(f"golden:{name}:logits", logits.cpu().numpy(), z["out.logits"], tol_l)
+    assert nw <= tol_l
+    nw, _ = record_margin(f"golden:{name}:writer_moments", wm.cpu().numpy(),
+                          z["out.writer_moments"], tol_m)
+    assert nw <= tol_m
+    nw, _ = record_margin(f"golden:{name}:reader_moments", rm.cpu().numpy(),
+                          z["out.reader_moments"], tol_m)
+    assert nw <= tol_m
     ref64 = A.alphabet_forward(z["in.x"], golden_params(z), time_delta=z.get("in.time_delta"),
                                observation_mask=z.get("in.observation_mask"),
                                valid_mask=z.get("in.valid_mask"), dtype=np.float64)
-    assert rel_err(logits.cpu().numpy(), ref64) <= tol_l
+    nw, _ = record_margin(f"oracle64:{name}:logits", logits.cpu().numpy(), ref64, tol_l)
+    assert nw <= tol_l
 
 
 def test_padding_is_bit_identical(cuda_device):
