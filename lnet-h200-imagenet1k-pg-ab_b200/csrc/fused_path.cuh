@@ -6,33 +6,44 @@
 // of every item was claimed earlier by a running CTA: the decoupled look-back
 // below always makes progress.
 //
-// fused_writer_kernel (persistent, one CTA of 512 threads per SM = two
-// independent item streams of 256 threads sharing the weight operands):
+// Both block kernels are persistent, one CTA per SM, and run kSlots
+// independent ITEM SLOTS of 128 threads (4 warps; warp q reads TMEM lane
+// quarter q).  A slot carries one item through every phase on its own (its own
+// TMEM columns, mbarriers, named barrier and shared-memory tiles), so while one
+// slot waits for an MMA, a tile or a look-back, the other slots compute.  In
+// the token-major phases thread t of a slot owns token row t of the item; in
+// the scan phases thread (q, lane) owns one (mode, half) of the item.
+//
+// TMEM (128 columns per slot): the drive accumulator is MODE-MAJOR and PAIRED:
+// lane 32 q + l holds, for mode m = 16 q + (l & 15), the real (l < 16) or the
+// imaginary (l >= 16) drive component over the item's 128 steps (columns).
+// So a complex mode's two components sit in lanes l and l ^ 16 of one warp:
+// a shuffle joins them, every lane holds data (no padding modes), and one
+// item needs 128 columns, not 256.  The token-major stem and synthesis
+// accumulators use the first D columns of the slot.
+//
+// fused_writer_kernel, per item:
 //   1. x rows [t0 - 8, t0 + 136) by TMA (3-D tensor map, one 8-channel box per
 //      no-swizzle K-major slab, zero fill outside [0, T)), fetched one item
-//      ahead into the tile region;
+//      ahead into the slot's tile region (free once the stem GEMM has read it);
 //   2. stem projection + dilated depthwise conv as ONE tcgen05 GEMM:
 //        acc[t, d] = sum_k sum_c x[t + 4k - 8, c] * (w[d, k] P[d, c]),
 //      the five taps are five row-shifted descriptors over the same tile;
-//   3. +bias, SiLU, RMSNorm (thread per step, two threads per row), xhat ->
-//      bf16 slab; the bf16 stem output waits in the output rows (L2);
-//   4. drive GEMM in mode-major orientation: the A operand repeats the mode
-//      rows every 64 lanes, so every TMEM lane quarter holds the complex drive
-//      u_m(t) of 32 modes over all 128 steps (gamma is folded into the frame)
-//      and every warp can scan without a transpose;
-//   5. scan: each mode's 128 steps are cut into four sub-chunks of 32 scanned
-//      by four threads; sub-chunk end states combine in shared memory into the
-//      chunk aggregate, which the last sub-chunk's threads publish and then
-//      resolve against their predecessors (decoupled look-back over tagged
-//      records, the predecessor's inclusive record prefetched); a second pass
-//      from the true carries accumulates E, C1, C2, C4 and writes the states
-//      (bf16) as the A operand of
+//   3. +bias, SiLU, RMSNorm, thread per token (no cross-thread reduction):
+//      xhat -> bf16 slab; the bf16 stem output waits in the output rows (L2);
+//   4. drive GEMM (paired mode-major layout above; gamma folded into the frame);
+//   5. scan: the thread of lane l < 16 scans steps [0, 64) of its mode, the
+//      thread of lane l + 16 steps [64, 128); each loads its own TMEM lane and
+//      swaps halves with its partner by shuffles.  The partner pair combines its
+//      halves by shuffles, the upper-half thread publishes the chunk aggregate
+//      and resolves the carry by a decoupled look-back over tagged records; a
+//      second pass from the true carries accumulates E, C1, C2, C4 and writes
+//      the states (bf16) as the A operand of
 //   6. the synthesis GEMM (token-major), during which the chunk's moments are
 //      added to the row's fp64 sums, and the residual epilogue
 //      v = x + ls (s W^T + ds xhat), stored as bf16.
-// fused_reader_kernel (two CTAs of 256 threads per SM): the same skeleton on
-//   the writer stream: TMA tile, conv on CUDA cores, SiLU, RMSNorm, drive
-//   GEMM, scan, moments.
+// fused_reader_kernel: the same slots on the writer stream: TMA tile, conv on
+//   CUDA cores, SiLU, RMSNorm, drive GEMM, scan, moments.
 // fused_finalize_kernel: moments and radial-log features from the row sums.
 #pragma once
 
@@ -51,10 +62,13 @@
 namespace lnet {
 
 constexpr int kChunk = 128;
+constexpr int kHalf = kChunk / 2;  // steps per scan thread
 constexpr int kHalo = 8;
 constexpr int kTaps = 5;
 constexpr int kXRows = kChunk + 2 * kHalo;
-constexpr int kFusedThreads = 256;
+constexpr int kSlotThreads = 128;
+constexpr int kSlots = 3;
+constexpr int kSlotCols = 128;  // TMEM columns per slot
 constexpr uint32_t kSpinLimit = 1u << 20;
 // Device error bits (first error word of the fused route's flag block):
 // bit 0..3: an MMA completion wait gave up (writer stem, writer drive, writer
@@ -63,30 +77,14 @@ constexpr uint32_t kSpinLimit = 1u << 20;
 constexpr uint32_t kErrTile = 1u << 6;
 constexpr uint32_t kErrLookback = 1u << 4;
 
-// Per-block pole constants (floats, M entries each), SUB = steps per scan
-// sub-chunk of the block (64 writer, 32 reader):
-//   [0] a_re, [1] a_im, [2 + 2i] / [3 + 2i]  re/im of a^(128 - i),
-//   [10 + 2i] / [11 + 2i] re/im of a^(SUB - i)  (i = 0..3), [18]/[19] a^(2 SUB),
-//   [20]/[21] a^(3 SUB).
-constexpr int kConsts = 22;
-constexpr int KC_AL = 2, KC_AS = 10, KC_A2S = 18, KC_A3S = 20;
-constexpr int kWriterSub = 32, kReaderSub = 32;
-constexpr int kWriterNSub = 4;
-constexpr int kWriterDriveRows = 128, kReaderDriveRows = 128;
-// Thread (of an item stream) that issues the next tile's TMA copies: not
-// thread 0, whose async-unit instructions queue behind its MMAs.
+// Per-block pole constants (floats, M entries each):
+//   [0] a_re, [1] a_im, [2 + 2i] / [3 + 2i] re/im of a^(128 - i),
+//   [10 + 2i] / [11 + 2i] re/im of a^(64 - i)   (i = 0..3).
+constexpr int kConsts = 18;
+constexpr int KC_AL = 2, KC_AH = 10;
+// Thread (of a slot) that claims items and issues the tile copies: not thread
+// 0, whose async-unit instructions queue behind its MMAs.
 constexpr int kTileIssuer = 32;
-
-template <int NSUB>
-struct ScanLayout {
-  static constexpr int SUB = kChunk / NSUB;
-  static constexpr int END = 0;                   // [NSUB][2][64]
-  static constexpr int LAST = NSUB * 128;         // [NSUB][8][64]
-  static constexpr int CARRY = LAST + NSUB * 512; // [8][64]
-  static constexpr int MOM = CARRY + 512;         // [NSUB][7][64]
-  static constexpr int FLOATS = MOM + NSUB * 448;
-};
-
 
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
@@ -96,8 +94,8 @@ struct FusedWorkspace {
   float *feats = nullptr;              // [B][14M] radial-log features
   float *head_partial = nullptr;       // split-K partial logits
   __nv_bfloat16 *q = nullptr;          // stem B operand   [5][C/8][D][8]
-  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [2][D/8][64][8]
-  __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [2][D/8][128][8]
+  __nv_bfloat16 *wdrive = nullptr;     // writer drive A   [D/8][128][8]
+  __nv_bfloat16 *rdrive = nullptr;     // reader drive A   [D/8][128][8]
   __nv_bfloat16 *wsyn = nullptr;       // synthesis B      [2M/8][D][8]
   float *consts = nullptr;             // [2][kConsts * M]
   __nv_bfloat16 *stream = nullptr;     // [B, T, D]
@@ -108,13 +106,13 @@ struct FusedWorkspace {
   double *rowsum = nullptr;
   int64_t rowsum_len = 0;
   // look-back records [B * nch][2 (aggregate, inclusive)][4 states][2 (re, im)][M];
-  // each entry = (state bits) | (epoch << 32), single-copy atomic 8-byte words
+  // each entry = (state bits) | (tag << 32), single-copy atomic 8-byte words
   unsigned long long *wrec = nullptr;
   unsigned long long *rrec = nullptr;
   uint32_t *flags = nullptr;           // counters[2] + error[2]
   size_t flag_words = 0;
-  // Replay counter of the look-back tags, kept in the workspace and advanced
-  // on the device at the end of every call (fused_finalize_kernel), so that
+  // Call counter of the look-back tags, kept in the workspace and advanced on
+  // the device at the end of every call (fused_finalize_kernel), so that
   // replays of a captured CUDA graph (same host arguments) still tag their
   // records differently (record_tag).
   uint32_t *epoch_word = nullptr;
@@ -129,8 +127,8 @@ inline void plan_fused(Arena &ar, FusedWorkspace &w, const lnet_b200_alphabet_pa
   // prepared operands first: their offsets depend on (C, D, M) only, so a
   // workspace prepared once serves every batch and length it is large enough for
   w.q = ar.take<__nv_bfloat16>((size_t)kTaps * C * D);
-  w.wdrive = ar.take<__nv_bfloat16>((size_t)2 * D * kWriterDriveRows);
-  w.rdrive = ar.take<__nv_bfloat16>((size_t)2 * D * 128);
+  w.wdrive = ar.take<__nv_bfloat16>((size_t)D * 128);
+  w.rdrive = ar.take<__nv_bfloat16>((size_t)D * 128);
   w.wsyn = ar.take<__nv_bfloat16>((size_t)2 * M * D);
   w.consts = ar.take<float>((size_t)2 * kConsts * M);
   w.moments = ar.take<float>((size_t)2 * B * 7 * M);
@@ -156,6 +154,16 @@ __device__ __forceinline__ void cmul_d(double ar, double ai, double br, double b
   ci = ar * bi + ai * br;
 }
 
+// Drive A row r -> (mode, component) of the paired mode-major layout:
+// quarter q = r / 32 holds modes 16 q .. 16 q + 15, lanes l < 16 the real and
+// l >= 16 the imaginary component; -1 for rows past the modes.
+__host__ __device__ __forceinline__ int drive_row_mode(int r, int modes, int &comp) {
+  const int q = r >> 5, l = r & 31;
+  comp = l >> 4;
+  const int m = 16 * q + (l & 15);
+  return m < modes ? m : -1;
+}
+
 __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace w) {
   const int C = p.raw_input_dim, D = p.model_dim, M = p.modes, K5 = p.conv_kernel;
   // per-mode ZOH input gains of both blocks, once per CTA (M <= 64)
@@ -173,44 +181,44 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
   __syncthreads();
   // every index below 2^31 (operand sizes of one block): 32-bit arithmetic
   const int n_q = kTaps * C * D;
-  // drive A rows per block: 128 (modes repeated every 64 lanes)
-  const int n_wdrive = 2 * D * kWriterDriveRows;
-  const int n_rdrive = 2 * D * kReaderDriveRows;
+  const int n_drive = D * 128;  // per block: 128 paired mode-major rows
   const int n_syn = 2 * M * D;
-  const int total = n_q + n_wdrive + n_rdrive + n_syn + 2 * M;
+  const int total = n_q + 2 * n_drive + n_syn + 2 * M;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    if (i < n_q) {  // Q_k[d][c] = w[d][k] * P[d][c]
+    if (i < n_q) {  // Q_k[d][c] = w[d][k] * P[d][c] / 2 (the 1/2 of SiLU's tanh form, exact)
       const int k = i / (C * D);
       const int rem = i - k * C * D;
       int d = rem / C, c = rem - d * C;
-      double v = (double)p.stem_conv_weight[d * K5 + k] * (double)p.stem_projection[d * C + c];
+      double v = 0.5 * (double)p.stem_conv_weight[d * K5 + k] * (double)p.stem_projection[d * C + c];
       w.q[k * C * D + ((c / 8) * D + d) * 8 + (c % 8)] = __float2bfloat16_rn((float)v);
       continue;
     }
     int j = i - n_q;
-    if (j < n_wdrive + n_rdrive) {  // drive A: lane r holds mode r % 64 (zero if >= M), K = d
-      const int blk = j < n_wdrive ? 0 : 1;
-      const int R = blk == 0 ? kWriterDriveRows : kReaderDriveRows;
-      const int rem = blk == 0 ? j : j - n_wdrive;
-      const int part = rem / (D * R);
-      const int rem2 = rem - part * D * R;
-      int d = rem2 / R, r = rem2 - d * R;
-      int m = r % 64;
+    if (j < 2 * n_drive) {  // drive A: row r = (mode, component), K = d
+      const int blk = j < n_drive ? 0 : 1;
+      const int rem = blk == 0 ? j : j - n_drive;
+      const int d = rem / 128, r = rem - d * 128;
+      int comp;
+      const int m = drive_row_mode(r, M, comp);
       float out = 0.f;
-      if (m < M) {
+      if (m >= 0) {
+        // gamma-folded frame row d, times the RMSNorm weight g[d] (xhat = f rs g
+        // enters the drive as (f rs) (g W))
         const float *frame = blk == 0 ? p.writer_frame : p.reader_frame;
+        const double g = blk == 0 ? p.writer_norm[d] : p.reader_norm[d];
         const double gr = zg[blk][0][m], gi = zg[blk][1][m];
         double fr = frame[d * 2 * M + m], fi = frame[d * 2 * M + M + m];
-        out = (float)(part == 0 ? gr * fr - gi * fi : gr * fi + gi * fr);
+        out = (float)(g * (comp == 0 ? gr * fr - gi * fi : gr * fi + gi * fr));
       }
       __nv_bfloat16 *dst = blk == 0 ? w.wdrive : w.rdrive;
-      dst[part * D * R + ((d / 8) * R + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
+      dst[((d / 8) * 128 + r) * 8 + (d % 8)] = __float2bfloat16_rn(out);
       continue;
     }
-    j -= n_wdrive + n_rdrive;
-    if (j < n_syn) {  // synthesis B rows = d, K = 2M
+    j -= 2 * n_drive;
+    if (j < n_syn) {  // synthesis B rows = d, K = 2M: ls[d] W[d, j] (layer scale folded)
       const int d = j / (2 * M), jj = j - d * 2 * M;
-      w.wsyn[((jj / 8) * D + d) * 8 + (jj % 8)] = __float2bfloat16_rn(p.writer_frame[d * 2 * M + jj]);
+      w.wsyn[((jj / 8) * D + d) * 8 + (jj % 8)] = __float2bfloat16_rn(
+          (float)((double)p.writer_layer_scale[d] * (double)p.writer_frame[d * 2 * M + jj]));
       continue;
     }
     j -= n_syn;  // per-mode constants of both blocks
@@ -230,16 +238,12 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
       cmul_d(pr, pi, ar, ai, nr, ni);
       pr = nr;
       pi = ni;
-      const int sub = blk == 0 ? kWriterSub : kReaderSub;
-      int slots[4] = {-1, -1, -1, -1};
-      if (step >= kChunk - 3) slots[0] = KC_AL + 2 * (kChunk - step);
-      if (step >= sub - 3 && step <= sub) slots[1] = KC_AS + 2 * (sub - step);
-      if (step == 2 * sub) slots[2] = KC_A2S;
-      if (step == 3 * sub) slots[3] = KC_A3S;
-      for (int s = 0; s < 4; ++s) {
-        if (slots[s] < 0) continue;
-        k[slots[s] * M + m] = (float)pr;
-        k[(slots[s] + 1) * M + m] = (float)pi;
+      int slot = -1;
+      if (step >= kChunk - 3) slot = KC_AL + 2 * (kChunk - step);
+      if (step >= kHalf - 3 && step <= kHalf) slot = KC_AH + 2 * (kHalf - step);
+      if (slot >= 0) {
+        k[slot * M + m] = (float)pr;
+        k[(slot + 1) * M + m] = (float)pi;
       }
     }
     k[m] = z.a_re;
@@ -247,32 +251,7 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
   }
 }
 
-// ---------------------------------------------------------------- shared-memory plans
-template <int D, int M>
-struct ReaderPlan {
-  static_assert(D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
-  static constexpr int SLAB_AD = 128 * 16;
-  static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
-  static constexpr int SLAB_V = kXRows * 16;  // stream tile: K-major slabs of 8 channels (one TMA box)
-  static constexpr int V_BYTES = (D / 8) * SLAB_V;  // (the next item's after the conv)
-  static constexpr int SLAB_XH = kChunk * 16;
-  // xhat slab, then (once the drive GEMM has read it) the scan scratch
-  static constexpr int XH_BYTES = cmax((D / 8) * SLAB_XH, ScanLayout<4>::FLOATS * 4);
-  static constexpr int OFF_AD = 0;
-  static constexpr int OFF_V = OFF_AD + AD_BYTES;
-  static constexpr int OFF_XH = OFF_V + V_BYTES;
-  static constexpr int OFF_PAR = OFF_XH + XH_BYTES;               // float [7][D]: w(5), bias, g
-  static constexpr int OFF_K = OFF_PAR + 7 * D * 4;
-  static constexpr int OFF_RED = OFF_K + kConsts * M * 4;
-  static constexpr int OFF_MISC = OFF_RED + 2 * kChunk * 4;
-  static constexpr int BYTES = OFF_MISC + 64;
-  // at most two CTAs per SM so that two 256-column TMEM allocations always fit
-  static constexpr int LAUNCH_BYTES = cmax(BYTES, 100 * 1024);
-  static constexpr int TMEM_COLS = 256;  // [0,128) u re, [128,256) u im
-  static_assert(2 * (LAUNCH_BYTES + 1024) <= 228 * 1024, "two reader CTAs must fit one SM");
-  static_assert(OFF_V % 128 == 0 && SLAB_V % 128 == 0, "TMA destinations must be 128-byte aligned");
-};
-
+// ---------------------------------------------------------------- device helpers
 struct FusedArgs {
   CUtensorMap tmap;         // 3-D map of `in` ([B][T][W] bf16), box 8 x 144 x 1
   const __nv_bfloat16 *in;  // writer: x [B,T,C]; reader: stream [B,T,D]
@@ -290,22 +269,36 @@ struct FusedArgs {
   uint32_t spin_limit;      // polls before a look-back wait gives up
   uint32_t *counter;
   uint32_t *error;
-  int trace;       // 1: accumulate per-phase cycles of CTA thread 0 into g_fused_trace
+  int trace;       // 1: accumulate per-phase cycles of slot 0's thread 0 into g_fused_trace
   int kernel_id;   // 0 writer, 1 reader
 };
 
-// Per-phase cycle totals of thread 0 of every CTA (tracing; off by default).
-// Slots: 0 claim, 1 tile load, 2 first GEMM wait, 3 token epilogue, 4 drive GEMM
-// wait, 5 scan (whole), 6 synthesis wait, 7 residual epilogue, 8 look-backs
-// resolved by the prefetched record, 9 look-backs (chunk > 0), 10 scan pass 1,
-// 11 look-back, 12 scan pass 2, 15 items processed.
+// Per-phase cycle totals of thread 0 of slot 0 of every CTA (tracing; off by
+// default).  Slots: 0 claim, 1 tile wait, 2 first GEMM wait, 3 token epilogue,
+// 4 drive GEMM wait, 5 scan (whole), 6 synthesis wait, 7 residual epilogue,
+// 8 look-backs resolved by the prefetched record, 9 look-backs (chunk > 0),
+// 10 scan pass 1, 11 look-back, 12 scan pass 2, 13 CTAs, 14 CTAs done,
+// 15 items processed.
 static __device__ unsigned long long g_fused_trace[2][16];
+
+// The CTA's phase counters while tracing, in shared memory (no global atomics on
+// the traced path); flushed to g_fused_trace once when the CTA ends.
+__device__ __forceinline__ unsigned long long *cta_trace() {
+  __shared__ unsigned long long counters[16];
+  return counters;
+}
+__device__ __forceinline__ void trace_begin(int trace) {
+  if (trace && threadIdx.x < 16) cta_trace()[threadIdx.x] = 0ull;
+}
+__device__ __forceinline__ void trace_flush(int trace, int kid) {  // after a CTA barrier
+  if (trace && threadIdx.x < 16) atomicAdd(&g_fused_trace[kid][threadIdx.x], cta_trace()[threadIdx.x]);
+}
 
 #define LNET_TRACE(slot)                                                        \
   do {                                                                          \
     if (a.trace && threadIdx.x == 0) {                                          \
       unsigned long long _now = clock64();                                      \
-      atomicAdd(&g_fused_trace[a.kernel_id][slot], _now - t_last);              \
+      cta_trace()[slot] += _now - t_last;                                       \
       t_last = _now;                                                            \
     }                                                                           \
   } while (0)
@@ -333,19 +326,25 @@ __device__ __forceinline__ void bf16x8_to_float(const uint4 &v, float *f) {
 }
 
 // Two floats -> packed bf16x2 (a in the low half), round to nearest even.
-// (An integer-arithmetic rounding measured slower: the conversion pipe is not
-// the limit here.)
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+__device__ __forceinline__ uint4 pack_bf16x8(const float *v) {
+  uint4 r;
+  r.x = pack_bf16x2(v[0], v[1]);
+  r.y = pack_bf16x2(v[2], v[3]);
+  r.z = pack_bf16x2(v[4], v[5]);
+  r.w = pack_bf16x2(v[6], v[7]);
+  return r;
+}
 
 // SiLU for the bf16 route: v/2 + (v/2) tanh(v/2) with one tanh.approx, i.e.
 // one multi-function-unit operation per element instead of an exponential and
-// a reciprocal (the epilogues are bound by that unit: 9 % faster end to end).
-// Absolute error ~|v| 2^-11, below the bf16 rounding of the stored activation.
-// LNET_SILU_EXP2 selects the exponential form (relative error ~1e-6).
+// a reciprocal.  Absolute error ~|v| 2^-11, below the bf16 rounding of the
+// stored activation.  LNET_SILU_EXP2 selects the exponential form (relative
+// error ~1e-6).
 __device__ __forceinline__ float silu_fast(float v) {
 #if defined(LNET_SILU_EXP2)
   return __fdividef(v, 1.0f + __expf(-v));
@@ -374,435 +373,26 @@ __device__ __forceinline__ uint32_t record_tag(uint32_t host_seed, const uint32_
   return t == 0u ? 0x5BD1E995u : t;
 }
 
-// Tagged look-back words: (fp32 bits) | (epoch << 32), written and read as one
-// 64-bit access (single-copy atomic), so a reader that sees this call's epoch
+// Tagged look-back words: (fp32 bits) | (tag << 32), written and read as one
+// 64-bit access (single-copy atomic), so a reader that sees this call's tag
 // also sees the value written with it -- no flags and no fences are needed.
-__device__ __forceinline__ void st_tag(unsigned long long *p, float v, uint32_t epoch) {
-  __stcg(p, ((unsigned long long)epoch << 32) | __float_as_uint(v));
+__device__ __forceinline__ void st_tag(unsigned long long *p, float v, uint32_t tag) {
+  __stcg(p, ((unsigned long long)tag << 32) | __float_as_uint(v));
 }
-__device__ __forceinline__ bool ld_tag(const unsigned long long *p, uint32_t epoch, float &v) {
+__device__ __forceinline__ bool ld_tag(const unsigned long long *p, uint32_t tag, float &v) {
   const unsigned long long x = __ldcg(p);
   v = __uint_as_float((uint32_t)x);
-  return (uint32_t)(x >> 32) == epoch;
+  return (uint32_t)(x >> 32) == tag;
 }
 
-// ---------------------------------------------------------------- scan + look-back
-// Executed by the 256 threads of one item stream (local thread id `ltid`).
-// NSUB = 4 (writer and reader): the drive operand repeats the mode rows every
-//   64 lanes, so local warp w reads lane quarter w % 4 = modes 32 * (w % 2) +
-//   lane of sub-chunk q = (w % 4) / 2 + 2 * (w / 4): all four SM sub-partitions
-//   scan.
-// NSUB = 2 (drive rows in lanes 0..63 only): local warps with w % 4 < 2 scan
-//   modes 32 * (w % 4) + lane of sub-chunk q = w / 4; the others only join the
-//   barriers.
-// Sub-chunk q covers steps [SUB q, SUB q + SUB), SUB = 128 / NSUB.  u_re / u_im
-// live in TMEM columns [col_re, col_re + 128) / [col_im, ...).  Writes the chunk's
-// moment partial sums [7][M] to the row's sums `rowsum` (or leaves the
-// per-sub-chunk sums in `mom_out` for the caller to add with reduce_moments).
-
-// Named barrier over one 256-thread item stream.  The non-aligned form counts
-// threads, so it stays correct when a warp reaches it diverged (e.g. after a
-// single-lane MMA issue); the aligned `bar.sync` would count each divergent
-// part of a warp as a separate warp arrival.
-__device__ __forceinline__ void group_sync(int id) {
-  asm volatile("barrier.sync %0, 256;" ::"r"(id) : "memory");
+// Named barrier over the 128 threads of one slot (ids 1..kSlots; 0 is
+// __syncthreads).  The non-aligned form counts threads, so it stays correct
+// when a warp reaches it diverged (e.g. after a single-lane MMA issue).
+__device__ __forceinline__ void slot_sync(int id) {
+  asm volatile("barrier.sync %0, 128;" ::"r"(id) : "memory");
 }
 
-// The previous chunk's inclusive record, loaded by the publishing threads
-// before the scan starts (its producer has usually finished by then), so the
-// look-back costs no memory round trip when the tags already match.
-struct LookbackPrefetch {
-  unsigned long long w[8];  // [state k][re | im] of the inclusive record
-};
-
-template <int M, int NSUB>
-__device__ __forceinline__ void lookback_prefetch(int ltid, const unsigned long long *rec,
-                                                  int64_t row, int64_t chunk, int64_t n_chunks,
-                                                  LookbackPrefetch &p) {
-  const int lwarp = ltid >> 5, lane = ltid & 31, Q = lwarp & 3;
-  int q, m;
-  bool scanner;
-  if constexpr (NSUB == 4) {
-    q = (Q >> 1) + 2 * (lwarp >> 2);
-    m = 32 * (Q & 1) + lane;
-    scanner = true;
-  } else {
-    q = lwarp >> 2;
-    m = 32 * Q + lane;
-    scanner = Q < 2;
-  }
-#pragma unroll
-  for (int k = 0; k < 8; ++k) p.w[k] = 0ull;
-  if (scanner && q == NSUB - 1 && m < M && chunk > 0) {
-    const unsigned long long *pv = rec + (row * n_chunks + chunk - 1) * 16 * M + 8 * M + m;
-    // volatile: issued here, not sunk to the first use behind the scan's barriers
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(p.w[k]) : "l"(pv + k * M));
-  }
-}
-
-template <int M, bool WRITE_STATES, int NSUB>
-__device__ __forceinline__ void chunk_scan(int ltid, int bar_group, int bar_lb, uint32_t tbase,
-                                           int col_re, int col_im, int n, int64_t row,
-                                           int64_t chunk, int64_t n_chunks, const float *K,
-                                           unsigned long long *rec, uint32_t host_epoch,
-                                           const uint32_t *epoch_word, uint32_t read_xor,
-                                           uint32_t spin, uint32_t *error,
-                                           uint8_t *s_slab, int slab_s, float *sc,
-                                           double *rowsum, int trace, int kid,
-                                           const LookbackPrefetch &pre,
-                                           float *mom_out = nullptr) {
-  using L = ScanLayout<NSUB>;
-  constexpr int SUB = L::SUB;
-  unsigned long long t_scan = trace ? clock64() : 0;
-  auto mark = [&](int slot) {
-    if (trace && threadIdx.x == 0) {
-      unsigned long long now = clock64();
-      atomicAdd(&g_fused_trace[kid][slot], now - t_scan);
-      t_scan = now;
-    }
-  };
-  const int lwarp = ltid >> 5, lane = ltid & 31;
-  const int Q = lwarp & 3;
-  int q, m;
-  bool scanner;
-  if constexpr (NSUB == 4) {
-    q = (Q >> 1) + 2 * (lwarp >> 2);
-    m = 32 * (Q & 1) + lane;
-    scanner = true;
-  } else {
-    q = lwarp >> 2;
-    m = 32 * Q + lane;
-    scanner = Q < 2;
-  }
-  const bool live = scanner && m < M;
-  const int mk = live ? m : 0;
-  const bool publisher_group = scanner && q == NSUB - 1;
-  const uint32_t lane_addr = tbase + ((uint32_t)(32 * Q) << 16);
-  const int s0 = SUB * q;
-  const int len = scanner ? max(0, min(SUB, n - s0)) : 0;
-  const float ar = K[mk], ai = K[M + mk];
-
-  // ---- pass 1: sub-chunk local scan from zero (32-step pieces: 4 TMEM loads, one wait)
-  float sr = 0.f, si = 0.f;
-  float l_r[4] = {0, 0, 0, 0}, l_i[4] = {0, 0, 0, 0};  // l[0] = last state
-  for (int c0 = 0; c0 < len; c0 += 32) {
-    float ur[32], ui[32];
-    sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
-    sm100::tmem_ld16(lane_addr + col_re + s0 + c0 + 16, ur + 16);
-    sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
-    sm100::tmem_ld16(lane_addr + col_im + s0 + c0 + 16, ui + 16);
-    sm100::tmem_ld_wait();
-    if (c0 + 32 <= len) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
-        float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
-        sr = nr;
-        si = ni;
-        if (i >= 28) {
-          l_r[31 - i] = sr;
-          l_i[31 - i] = si;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (c0 + i < len) {
-          float nr = fmaf(ar, sr, fmaf(-ai, si, ur[i]));
-          float ni = fmaf(ai, sr, fmaf(ar, si, ui[i]));
-          sr = nr;
-          si = ni;
-          l_r[3] = l_r[2]; l_i[3] = l_i[2];
-          l_r[2] = l_r[1]; l_i[2] = l_i[1];
-          l_r[1] = l_r[0]; l_i[1] = l_i[0];
-          l_r[0] = sr; l_i[0] = si;
-        }
-      }
-    }
-  }
-  if (live) {
-    sc[L::END + (2 * q) * 64 + m] = sr;
-    sc[L::END + (2 * q + 1) * 64 + m] = si;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      sc[L::LAST + (8 * q + 2 * k) * 64 + m] = l_r[k];
-      sc[L::LAST + (8 * q + 2 * k + 1) * 64 + m] = l_i[k];
-    }
-  }
-  group_sync(bar_group);
-  mark(10);
-  // chunk-local state before sub-chunk j: c_0 = 0, c_{j+1} = a^SUB c_j + e_j
-  // (all end states loaded at once, then the short dependent chain)
-  const float asr = K[KC_AS * M + mk], asi = K[(KC_AS + 1) * M + mk];
-  float cr = 0.f, ci = 0.f, cpr = 0.f, cpi = 0.f;  // c_q and c_{q-1}
-  float e_r[NSUB - 1], e_i[NSUB - 1];
-#pragma unroll
-  for (int j = 0; j < NSUB - 1; ++j) {
-    e_r[j] = j < q ? sc[L::END + (2 * j) * 64 + mk] : 0.f;
-    e_i[j] = j < q ? sc[L::END + (2 * j + 1) * 64 + mk] : 0.f;
-  }
-#pragma unroll
-  for (int j = 0; j < NSUB - 1; ++j) {
-    if (j < q) {
-      cpr = cr;
-      cpi = ci;
-      float nr = e_r[j], ni = e_i[j];
-      cmac(asr, asi, cr, ci, nr, ni);
-      cr = nr;
-      ci = ni;
-    }
-  }
-
-  // ---- aggregate, look-back and inclusive record: threads of the last sub-chunk.
-  // Record layout per item: [agg | incl][state k = 0..3][re | im][M]; state 0 is
-  // the chunk's last state.
-  if (publisher_group && live) {
-    const uint32_t epoch = record_tag(host_epoch, epoch_word);  // this call's record tag
-    const uint32_t rtag = epoch ^ read_xor;  // the tag looked for (== epoch outside tests)
-    const int64_t item = row * n_chunks + chunk;  // record index (row-major)
-    unsigned long long *my = rec + item * 16 * M;
-    float g_r[4], g_i[4];  // chunk-local last four states
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      g_r[k] = l_r[k];
-      g_i[k] = l_i[k];
-      cmac(K[(KC_AS + 2 * k) * M + m], K[(KC_AS + 2 * k + 1) * M + m], cr, ci, g_r[k], g_i[k]);
-      st_tag(my + (2 * k) * M + m, g_r[k], epoch);
-      st_tag(my + (2 * k + 1) * M + m, g_i[k], epoch);
-    }
-    float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
-    if (chunk > 0) {
-      const unsigned long long *pv = rec + (item - 1) * 16 * M;
-      const float aLr = K[KC_AL * M + m], aLi = K[(KC_AL + 1) * M + m];
-      bool done = true;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const unsigned long long xr = pre.w[2 * k], xi = pre.w[2 * k + 1];
-        done &= (uint32_t)(xr >> 32) == rtag && (uint32_t)(xi >> 32) == rtag;
-        p_r[k] = __uint_as_float((uint32_t)xr);
-        p_i[k] = __uint_as_float((uint32_t)xi);
-      }
-      if (trace && m == 0) {
-        atomicAdd(&g_fused_trace[kid][9], 1ull);
-        if (done) atomicAdd(&g_fused_trace[kid][8], 1ull);
-      }
-      for (uint32_t it = 0; it < spin && !done; ++it) {
-        bool ok = true;  // inclusive record of the previous chunk
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          ok &= ld_tag(pv + 8 * M + (2 * k) * M + m, rtag, p_r[k]);
-          ok &= ld_tag(pv + 8 * M + (2 * k + 1) * M + m, rtag, p_i[k]);
-        }
-        if (ok) {
-          done = true;
-          break;
-        }
-        ok = true;  // its aggregate, completed by the true end X of chunk - 2
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          ok &= ld_tag(pv + (2 * k) * M + m, rtag, p_r[k]);
-          ok &= ld_tag(pv + (2 * k + 1) * M + m, rtag, p_i[k]);
-        }
-        if (!ok) {
-          __nanosleep(32);
-          continue;
-        }
-        float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
-        bool walk_ok = true;
-        for (int64_t qq = chunk - 2; qq >= 0 && walk_ok; --qq) {
-          const unsigned long long *qv = rec + (row * n_chunks + qq) * 16 * M;
-          bool found = false;
-          for (uint32_t jt = 0; jt < spin; ++jt) {
-            float er, ei;
-            if (ld_tag(qv + 8 * M + m, rtag, er) && ld_tag(qv + 9 * M + m, rtag, ei)) {
-              cmac(mr, mi, er, ei, xr, xi);
-              qq = -1;  // inclusive: the walk ends here
-              found = true;
-              break;
-            }
-            if (ld_tag(qv + m, rtag, er) && ld_tag(qv + M + m, rtag, ei)) {
-              cmac(mr, mi, er, ei, xr, xi);
-              float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
-              mr = nr;
-              mi = ni;
-              found = true;
-              break;
-            }
-            __nanosleep(32);
-          }
-          if (!found) walk_ok = false;
-        }
-        if (!walk_ok) break;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], xr, xi, p_r[k],
-               p_i[k]);
-        done = true;
-      }
-      if (!done) {
-        atomicOr(error, kErrLookback << kid);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) p_r[k] = p_i[k] = 0.f;
-      }
-    }
-    // inclusive record (only consumed when the chunk is full)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float vr = g_r[k], vi = g_i[k];
-      cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], p_r[0], p_i[0], vr, vi);
-      st_tag(my + 8 * M + (2 * k) * M + m, vr, epoch);
-      st_tag(my + 8 * M + (2 * k + 1) * M + m, vi, epoch);
-      sc[L::CARRY + (2 * k) * 64 + m] = p_r[k];
-      sc[L::CARRY + (2 * k + 1) * 64 + m] = p_i[k];
-    }
-  }
-  group_sync(bar_group);
-  mark(11);
-
-  // ---- pass 2 from the true state before this sub-chunk
-  const float car = sc[L::CARRY + mk], cai = sc[L::CARRY + 64 + mk];
-  // a^(SUB q) and a^(SUB (q - 1))
-  float pqr = 1.f, pqi = 0.f, pq1r = 1.f, pq1i = 0.f;
-  if (q == 1) { pqr = asr; pqi = asi; }
-  if (q == 2) { pqr = K[KC_A2S * M + mk]; pqi = K[(KC_A2S + 1) * M + mk]; pq1r = asr; pq1i = asi; }
-  if (q == 3) {
-    pqr = K[KC_A3S * M + mk]; pqi = K[(KC_A3S + 1) * M + mk];
-    pq1r = K[KC_A2S * M + mk]; pq1i = K[(KC_A2S + 1) * M + mk];
-  }
-  float h_r[4], h_i[4];  // true states at the four steps before this sub-chunk
-  if (q == 0) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      h_r[k] = sc[L::CARRY + (2 * k) * 64 + mk];
-      h_i[k] = sc[L::CARRY + (2 * k + 1) * 64 + mk];
-    }
-  } else {
-    float ipr = cpr, ipi = cpi;  // true state before sub-chunk q - 1
-    cmac(pq1r, pq1i, car, cai, ipr, ipi);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      h_r[k] = sc[L::LAST + (8 * (q - 1) + 2 * k) * 64 + mk];
-      h_i[k] = sc[L::LAST + (8 * (q - 1) + 2 * k + 1) * 64 + mk];
-      cmac(K[(KC_AS + 2 * k) * M + mk], K[(KC_AS + 2 * k + 1) * M + mk], ipr, ipi, h_r[k],
-           h_i[k]);
-    }
-  }
-  sr = cr;
-  si = ci;
-  cmac(pqr, pqi, car, cai, sr, si);
-  // History before the sequence start is exactly zero (the carry of chunk 0 is
-  // zero), so lag products that reach before step 0 contribute nothing and
-  // need no guard; the counts T - lag are applied when the moments are finalised.
-  float h1r = h_r[0], h1i = h_i[0], h2r = h_r[1], h2i = h_i[1];
-  float h3r = h_r[2], h3i = h_i[2], h4r = h_r[3], h4i = h_i[3];
-  float e = 0.f, c1r = 0.f, c1i = 0.f, c2r = 0.f, c2i = 0.f, c4r = 0.f, c4i = 0.f;
-  auto step2 = [&](float u_re, float u_im) {
-    float nr = fmaf(ar, sr, fmaf(-ai, si, u_re));
-    float ni = fmaf(ai, sr, fmaf(ar, si, u_im));
-    sr = nr;
-    si = ni;
-    e = fmaf(sr, sr, fmaf(si, si, e));
-    c1r = fmaf(sr, h1r, fmaf(si, h1i, c1r));
-    c1i = fmaf(si, h1r, fmaf(-sr, h1i, c1i));
-    c2r = fmaf(sr, h2r, fmaf(si, h2i, c2r));
-    c2i = fmaf(si, h2r, fmaf(-sr, h2i, c2i));
-    c4r = fmaf(sr, h4r, fmaf(si, h4i, c4r));
-    c4i = fmaf(si, h4r, fmaf(-sr, h4i, c4i));
-    h4r = h3r; h4i = h3i;
-    h3r = h2r; h3i = h2i;
-    h2r = h1r; h2i = h1i;
-    h1r = sr; h1i = si;
-  };
-  // State slab for the synthesis GEMM, M-major (steps contiguous): element
-  // (t, j) at (j / 8) * slab_s + (t / 8) * 128 + (j % 8) * 16 + (t % 8) * 2.
-  auto s_addr = [&](int t, int j) {
-    return s_slab + (j / 8) * slab_s + (t / 8) * 128 + (j % 8) * 16 + (t % 8) * 2;
-  };
-  for (int c0 = 0; c0 < len; c0 += 32) {
-    float ur[32], ui[32];
-    sm100::tmem_ld16(lane_addr + col_re + s0 + c0, ur);
-    sm100::tmem_ld16(lane_addr + col_re + s0 + c0 + 16, ur + 16);
-    sm100::tmem_ld16(lane_addr + col_im + s0 + c0, ui);
-    sm100::tmem_ld16(lane_addr + col_im + s0 + c0 + 16, ui + 16);
-    sm100::tmem_ld_wait();
-    if (c0 + 32 <= len) {
-#pragma unroll
-      for (int g8 = 0; g8 < 4; ++g8) {
-        float br[8], bi[8];
-#pragma unroll
-        for (int i8 = 0; i8 < 8; ++i8) {
-          step2(ur[8 * g8 + i8], ui[8 * g8 + i8]);
-          br[i8] = sr;
-          bi[i8] = si;
-        }
-        if constexpr (WRITE_STATES) {
-          if (live) {
-            const int t = s0 + c0 + 8 * g8;
-            uint4 vr, vi;
-            vr.x = pack_bf16x2(br[0], br[1]); vr.y = pack_bf16x2(br[2], br[3]);
-            vr.z = pack_bf16x2(br[4], br[5]); vr.w = pack_bf16x2(br[6], br[7]);
-            vi.x = pack_bf16x2(bi[0], bi[1]); vi.y = pack_bf16x2(bi[2], bi[3]);
-            vi.z = pack_bf16x2(bi[4], bi[5]); vi.w = pack_bf16x2(bi[6], bi[7]);
-            *reinterpret_cast<uint4 *>(s_addr(t, m)) = vr;
-            *reinterpret_cast<uint4 *>(s_addr(t, M + m)) = vi;
-          }
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (c0 + i < len) {
-          step2(ur[i], ui[i]);
-          if constexpr (WRITE_STATES) {
-            if (live) {
-              const int t = s0 + c0 + i;
-              *reinterpret_cast<__nv_bfloat16 *>(s_addr(t, m)) = __float2bfloat16_rn(sr);
-              *reinterpret_cast<__nv_bfloat16 *>(s_addr(t, M + m)) = __float2bfloat16_rn(si);
-            }
-          }
-        }
-      }
-    }
-  }
-  mark(12);
-  // moment partials per sub-chunk: [NSUB][7][64], reduced below, or by the
-  // caller from `mom_out` after its own barrier (no extra barrier here)
-  if (live) {
-    float *mo = (mom_out ? mom_out : sc + L::MOM) + q * 7 * 64 + m;
-    mo[0] = e;
-    mo[64] = c1r;
-    mo[128] = c1i;
-    mo[192] = c2r;
-    mo[256] = c2i;
-    mo[320] = c4r;
-    mo[384] = c4i;
-  }
-  if (mom_out) return;
-  group_sync(bar_group);
-  for (int j = ltid; j < 7 * M; j += 256) {
-    const int k = j / M, mm = j - (j / M) * M;
-    const float *mo = sc + L::MOM + k * 64 + mm;
-    float acc = 0.f;
-#pragma unroll
-    for (int qq = 0; qq < NSUB; ++qq) acc += mo[qq * 7 * 64];
-    atomicAdd(rowsum + j, (double)acc);
-  }
-}
-
-// Adds the per-sub-chunk moment partials [NSUB][7][64] of one chunk to the
-// row's sums rowsum[7][M].
-template <int M, int NSUB>
-__device__ __forceinline__ void reduce_moments(int ltid, const float *mom, double *rowsum) {
-  for (int j = ltid; j < 7 * M; j += kFusedThreads) {
-    const int k = j / M, mm = j - (j / M) * M;
-    float acc = 0.f;
-#pragma unroll
-    for (int qq = 0; qq < NSUB; ++qq) acc += mom[qq * 7 * 64 + k * 64 + mm];
-    atomicAdd(rowsum + j, (double)acc);
-  }
-}
+__device__ __forceinline__ float shfl16(float v) { return __shfl_xor_sync(0xffffffffu, v, 16); }
 
 // Issues one GEMM: `ksteps` K=16 steps of D[tmem] (+)= A * B^T.
 __device__ __forceinline__ void issue_gemm(uint32_t d_tmem, uint32_t a_addr, int a_slab,
@@ -815,29 +405,388 @@ __device__ __forceinline__ void issue_gemm(uint32_t d_tmem, uint32_t a_addr, int
   }
 }
 
+// Every thread of the slot polls the slot's MMA mbarrier (bounded).
 __device__ __forceinline__ void wait_mma(uint64_t *mbar, uint32_t &phase, uint32_t *error,
-                                         uint32_t site) {
+                                         uint32_t site, int ltid) {
   if (!sm100::mbar_wait_bounded(mbar, phase, kSpinLimit)) {
-    if (threadIdx.x % 256 == 0) atomicOr(error, 1u << site);
+    if (ltid == 0) atomicOr(error, 1u << site);
   }
   phase ^= 1u;
   sm100::tc_fence_after();
 }
 
-// ---------------------------------------------------------------- writer kernel
-// One CTA of 512 threads per SM runs two independent item streams (threads
-// [0, 256) and [256, 512)).  The streams share the weight operands in shared
-// memory; each owns half of the TMEM columns, an mbarrier, named barriers and
-// its tile buffers, so one stream's GEMM waits, look-back and global-memory
-// latencies overlap the other stream's arithmetic.
-constexpr int kWriterStreams = 2;
+// ---------------------------------------------------------------- scan + look-back
+// The previous chunk's inclusive record, loaded by the publishing threads
+// before the drive GEMM wait (its producer has usually finished by then), so
+// the look-back costs no memory round trip when the tags already match.
+struct LookbackPrefetch {
+  unsigned long long w[8];  // [state k][re | im] of the inclusive record
+};
 
+// Called by every thread of a slot; lane l >= 16 threads of live warps (the
+// publishers) load the predecessor's inclusive record.
+template <int M>
+__device__ __forceinline__ void lookback_prefetch(int warp, int lane,
+                                                  const unsigned long long *rec, int64_t row,
+                                                  int64_t chunk, int64_t n_chunks,
+                                                  LookbackPrefetch &p) {
+  const int m = 16 * warp + (lane & 15);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) p.w[k] = 0ull;
+  if (m < M && lane >= 16 && chunk > 0) {
+    const unsigned long long *pv = rec + (row * n_chunks + chunk - 1) * 16 * M + 8 * M + m;
+    // volatile: issued here, not sunk to the first use behind the MMA wait
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(p.w[k]) : "l"(pv + k * M));
+  }
+}
+
+// Carry of chunk `chunk` of `row` for mode m: the true states at the four steps
+// before the chunk (P[0] = the state right before it), by a decoupled
+// look-back over the tagged records of the earlier chunks.  Publishes this
+// chunk's aggregate (chunk-local last four states g) first and its inclusive
+// record (true last four states) after.  Executed by one thread per mode.
+template <int M>
+__device__ __forceinline__ void lookback(int m, int64_t row, int64_t chunk, int64_t n_chunks,
+                                         const float *K, unsigned long long *rec, uint32_t tag,
+                                         uint32_t rtag, uint32_t spin, uint32_t *error, int kid,
+                                         int trace, const float *g_r, const float *g_i,
+                                         const LookbackPrefetch &pre, float *p_r, float *p_i) {
+  const int64_t item = row * n_chunks + chunk;  // record index (row-major)
+  unsigned long long *my = rec + item * 16 * M;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    st_tag(my + (2 * k) * M + m, g_r[k], tag);
+    st_tag(my + (2 * k + 1) * M + m, g_i[k], tag);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) p_r[k] = p_i[k] = 0.f;
+  if (chunk > 0) {
+    const unsigned long long *pv = rec + (item - 1) * 16 * M;
+    const float aLr = K[KC_AL * M + m], aLi = K[(KC_AL + 1) * M + m];
+    bool done = true;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const unsigned long long xr = pre.w[2 * k], xi = pre.w[2 * k + 1];
+      done &= (uint32_t)(xr >> 32) == rtag && (uint32_t)(xi >> 32) == rtag;
+      p_r[k] = __uint_as_float((uint32_t)xr);
+      p_i[k] = __uint_as_float((uint32_t)xi);
+    }
+    if (trace && (m & 15) == 0) {
+      atomicAdd(&cta_trace()[9], 1ull);
+      if (done) atomicAdd(&cta_trace()[8], 1ull);
+    }
+    for (uint32_t it = 0; it < spin && !done; ++it) {
+      bool ok = true;  // inclusive record of the previous chunk
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        ok &= ld_tag(pv + 8 * M + (2 * k) * M + m, rtag, p_r[k]);
+        ok &= ld_tag(pv + 8 * M + (2 * k + 1) * M + m, rtag, p_i[k]);
+      }
+      if (ok) {
+        done = true;
+        break;
+      }
+      ok = true;  // its aggregate, completed by the true end X of chunk - 2
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        ok &= ld_tag(pv + (2 * k) * M + m, rtag, p_r[k]);
+        ok &= ld_tag(pv + (2 * k + 1) * M + m, rtag, p_i[k]);
+      }
+      if (!ok) {
+        __nanosleep(32);
+        continue;
+      }
+      float xr = 0.f, xi = 0.f, mr = 1.f, mi = 0.f;
+      bool walk_ok = true;
+      for (int64_t qq = chunk - 2; qq >= 0 && walk_ok; --qq) {
+        const unsigned long long *qv = rec + (row * n_chunks + qq) * 16 * M;
+        bool found = false;
+        for (uint32_t jt = 0; jt < spin; ++jt) {
+          float er, ei;
+          if (ld_tag(qv + 8 * M + m, rtag, er) && ld_tag(qv + 9 * M + m, rtag, ei)) {
+            cmac(mr, mi, er, ei, xr, xi);
+            qq = -1;  // inclusive: the walk ends here
+            found = true;
+            break;
+          }
+          if (ld_tag(qv + m, rtag, er) && ld_tag(qv + M + m, rtag, ei)) {
+            cmac(mr, mi, er, ei, xr, xi);
+            float nr = mr * aLr - mi * aLi, ni = mr * aLi + mi * aLr;
+            mr = nr;
+            mi = ni;
+            found = true;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (!found) walk_ok = false;
+      }
+      if (!walk_ok) break;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], xr, xi, p_r[k], p_i[k]);
+      done = true;
+    }
+    if (!done) {
+      atomicOr(error, kErrLookback << kid);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) p_r[k] = p_i[k] = 0.f;
+    }
+  }
+  // inclusive record (only consumed when the chunk is full)
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float vr = g_r[k], vi = g_i[k];
+    cmac(K[(KC_AL + 2 * k) * M + m], K[(KC_AL + 2 * k + 1) * M + m], p_r[0], p_i[0], vr, vi);
+    st_tag(my + 8 * M + (2 * k) * M + m, vr, tag);
+    st_tag(my + 8 * M + (2 * k + 1) * M + m, vi, tag);
+  }
+}
+
+// Steps [c0, c0 + 32) of the thread's half as (x, y) in its own frame: every
+// lane of the warp loads the same TMEM columns (tcgen05.ld takes one address
+// per warp) -- its own component at steps c0.. (the lower half) and 64 + c0..
+// (the upper half) -- keeps its own half as x and sends the other half to its
+// partner, whose component over this thread's half arrives as y.
+__device__ __forceinline__ void load_pair(uint32_t lane_addr, int c0, int upper, float *x,
+                                          float *y) {
+  sm100::tmem_ld32(lane_addr + (uint32_t)c0, x);
+  sm100::tmem_ld32(lane_addr + (uint32_t)(kHalf + c0), y);
+  sm100::tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float lo = x[i], hi = y[i];
+    x[i] = upper ? hi : lo;
+    y[i] = shfl16(upper ? lo : hi);
+  }
+}
+
+// One item's scan, executed by a warp of a slot (all 32 lanes together; warps
+// whose quarter holds no modes return at once).  Lane l < 16 ("lower") owns
+// steps [0, 64) of mode m = 16 warp + (l & 15), lane l + 16 ("upper") steps
+// [64, 128).  Each thread keeps its complex values in its OWN FRAME: the lower
+// thread in (re, im), the upper thread in (im, re), i.e. z -> i conj(z).  In
+// that frame the recurrence is the same code with the pole conjugated, because
+// i conj(a z) = conj(a) (i conj(z)); and a lag product s_t conj(s_{t-l}) comes
+// out conjugated, so the upper thread negates its imaginary moment parts.
+// Every thread reads only its own TMEM lane: the component it owns over both
+// halves, and the half it does not scan goes to its partner by a shuffle
+// (load_pair).
+//
+// WRITE_STATES: the true states are written (bf16, M-major) into `s_slab` as the
+// synthesis A operand: element (t, j) at (j / 8) * SLAB + (t / 8) * 128 +
+// (j % 8) * 16 + (t % 8) * 2, j = m (re) or M + m (im).
+template <int M, bool WRITE_STATES>
+__device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr, int n,
+                                          int64_t row, int64_t chunk, int64_t n_chunks,
+                                          const float *K, unsigned long long *rec, uint32_t tag,
+                                          uint32_t rtag, uint32_t spin, uint32_t *error, int kid,
+                                          int trace, uint8_t *s_slab, int slab_bytes,
+                                          double *rowsum, const LookbackPrefetch &pre) {
+  const int upper = lane >> 4;
+  const int m = 16 * warp + (lane & 15);
+  if (16 * warp >= M) return;  // warp-uniform
+  unsigned long long t_scan = trace ? clock64() : 0;
+  auto mark = [&](int slot) {
+    if (trace && threadIdx.x == 0) {
+      unsigned long long now = clock64();
+      cta_trace()[slot] += now - t_scan;
+      t_scan = now;
+    }
+  };
+  const float sg = upper ? -1.f : 1.f;  // conjugation of constants in the upper frame
+  const int s0 = kHalf * upper;
+  const int len = max(0, min(kHalf, n - s0));
+  const float ar = K[m], ai = sg * K[M + m];
+
+  // ---- pass 1: local scan of the thread's 64 steps from zero (own frame)
+  float sx = 0.f, sy = 0.f;
+  float lx[4] = {0, 0, 0, 0}, ly[4] = {0, 0, 0, 0};  // l[0] = last state
+#pragma unroll 1
+  for (int c0 = 0; c0 < kHalf; c0 += 32) {
+    float x[32], y[32];
+    load_pair(lane_addr, c0, upper, x, y);
+    if (c0 + 32 <= len) {
+      const bool last = c0 + 32 == kHalf;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float nx = fmaf(ar, sx, fmaf(-ai, sy, x[i]));
+        const float ny = fmaf(ai, sx, fmaf(ar, sy, y[i]));
+        sx = nx;
+        sy = ny;
+        if (i >= 28 && last) {
+          lx[31 - i] = sx;
+          ly[31 - i] = sy;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (c0 + i < len) {
+          const float nx = fmaf(ar, sx, fmaf(-ai, sy, x[i]));
+          const float ny = fmaf(ai, sx, fmaf(ar, sy, y[i]));
+          sx = nx;
+          sy = ny;
+          lx[3] = lx[2]; ly[3] = ly[2];
+          lx[2] = lx[1]; ly[2] = ly[1];
+          lx[1] = lx[0]; ly[1] = ly[0];
+          lx[0] = sx; ly[0] = sy;
+        }
+      }
+    }
+  }
+  mark(10);
+  // ---- combine the halves.  The lower half's last four local states, in the
+  // normal frame (lower thread: (x, y) = (re, im)), reach the upper thread.
+  float or_[4], oi_[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    or_[k] = shfl16(lx[k]);
+    oi_[k] = shfl16(ly[k]);
+  }
+  // true states at the four steps before the chunk (normal frame)
+  float p_r[4] = {0, 0, 0, 0}, p_i[4] = {0, 0, 0, 0};
+  if (upper) {
+    // chunk-local state before step 64: c1 = lower's last local state; the
+    // chunk-local last four states g_k = l_k + a^(64 - k) c1, back to (re, im)
+    const float c1r = or_[0], c1i = oi_[0];
+    float g_r[4], g_i[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      g_r[k] = ly[k];  // own frame (im, re) -> normal
+      g_i[k] = lx[k];
+      cmac(K[(KC_AH + 2 * k) * M + m], K[(KC_AH + 2 * k + 1) * M + m], c1r, c1i, g_r[k],
+           g_i[k]);
+    }
+    lookback<M>(m, row, chunk, n_chunks, K, rec, tag, rtag, spin, error, kid, trace, g_r, g_i,
+                pre, p_r, p_i);
+  }
+  mark(11);
+  // the carry reaches the lower thread
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float vr = shfl16(p_r[k]), vi = shfl16(p_i[k]);
+    if (!upper) {
+      p_r[k] = vr;
+      p_i[k] = vi;
+    }
+  }
+  // ---- pass 2 from the true state before the thread's half, with the four
+  // true states before it as the lag history (normal frame first)
+  float hr[4], hi[4];
+  if (!upper) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      hr[k] = p_r[k];
+      hi[k] = p_i[k];
+    }
+  } else {  // true state at step 63 - k = lower's local l_k + a^(64 - k) P
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      hr[k] = or_[k];
+      hi[k] = oi_[k];
+      cmac(K[(KC_AH + 2 * k) * M + m], K[(KC_AH + 2 * k + 1) * M + m], p_r[0], p_i[0], hr[k],
+           hi[k]);
+    }
+  }
+  // to the own frame: lower (re, im) = (x, y); upper (x, y) = (im, re)
+  float h1x = upper ? hi[0] : hr[0], h1y = upper ? hr[0] : hi[0];
+  float h2x = upper ? hi[1] : hr[1], h2y = upper ? hr[1] : hi[1];
+  float h3x = upper ? hi[2] : hr[2], h3y = upper ? hr[2] : hi[2];
+  float h4x = upper ? hi[3] : hr[3], h4y = upper ? hr[3] : hi[3];
+  sx = h1x;
+  sy = h1y;
+  // Moment sums: |s|^2 and Re(s conj(h)) = sx hx + sy hy add terms of one sign
+  // pattern, so they run in paired fp32 lanes (S = (sx, sy), H = an earlier S;
+  // the pair is summed at the end).  Im(s conj(h)) = sy hx - sx hy is a small
+  // difference of nearly equal products for slowly rotating modes, so it is
+  // accumulated per step, where the FMA cancels exactly.
+  float2 E2 = make_float2(0.f, 0.f);
+  float2 C1r = E2, C2r = E2, C4r = E2;
+  float c1i = 0.f, c2i = 0.f, c4i = 0.f;
+  float2 H1 = make_float2(h1x, h1y), H2 = make_float2(h2x, h2y);
+  float2 H3 = make_float2(h3x, h3y), H4 = make_float2(h4x, h4y);
+  auto step2 = [&](float ux, float uy) {
+    const float nx = fmaf(ar, sx, fmaf(-ai, sy, ux));
+    const float ny = fmaf(ai, sx, fmaf(ar, sy, uy));
+    sx = nx;
+    sy = ny;
+    const float2 S = make_float2(nx, ny);
+    E2 = __ffma2_rn(S, S, E2);
+    C1r = __ffma2_rn(S, H1, C1r);
+    C2r = __ffma2_rn(S, H2, C2r);
+    C4r = __ffma2_rn(S, H4, C4r);
+    c1i = fmaf(ny, H1.x, fmaf(-nx, H1.y, c1i));
+    c2i = fmaf(ny, H2.x, fmaf(-nx, H2.y, c2i));
+    c4i = fmaf(ny, H4.x, fmaf(-nx, H4.y, c4i));
+    H4 = H3;
+    H3 = H2;
+    H2 = H1;
+    H1 = S;
+  };
+  // state slab addresses: the own frame's x goes to component j = m (lower: re)
+  // or M + m (upper: im), y to the other one
+  const int jx = upper ? M + m : m, jy = upper ? m : M + m;
+  uint8_t *px = s_slab + (jx / 8) * slab_bytes + (jx % 8) * 16;
+  uint8_t *py = s_slab + (jy / 8) * slab_bytes + (jy % 8) * 16;
+#pragma unroll 1
+  for (int c0 = 0; c0 < kHalf; c0 += 32) {
+    float x[32], y[32];
+    load_pair(lane_addr, c0, upper, x, y);
+    if (c0 + 32 <= len) {
+#pragma unroll
+      for (int g8 = 0; g8 < 4; ++g8) {
+        float bx[8], by[8];
+#pragma unroll
+        for (int i8 = 0; i8 < 8; ++i8) {
+          step2(x[8 * g8 + i8], y[8 * g8 + i8]);
+          bx[i8] = sx;
+          by[i8] = sy;
+        }
+        if constexpr (WRITE_STATES) {
+          const int t = s0 + c0 + 8 * g8;
+          *reinterpret_cast<uint4 *>(px + (t / 8) * 128) = pack_bf16x8(bx);
+          *reinterpret_cast<uint4 *>(py + (t / 8) * 128) = pack_bf16x8(by);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (c0 + i < len) {
+          step2(x[i], y[i]);
+          if constexpr (WRITE_STATES) {
+            const int t = s0 + c0 + i;
+            *reinterpret_cast<__nv_bfloat16 *>(px + (t / 8) * 128 + (t % 8) * 2) =
+                __float2bfloat16_rn(sx);
+            *reinterpret_cast<__nv_bfloat16 *>(py + (t / 8) * 128 + (t % 8) * 2) =
+                __float2bfloat16_rn(sy);
+          }
+        }
+      }
+    }
+  }
+  mark(12);
+  // ---- moments: the upper thread's lag products are conjugated in its frame
+  float mom[7] = {E2.x + E2.y, C1r.x + C1r.y, sg * c1i, C2r.x + C2r.y, sg * c2i,
+                  C4r.x + C4r.y, sg * c4i};
+#pragma unroll
+  for (int k = 0; k < 7; ++k) mom[k] += shfl16(mom[k]);
+  // lower thread adds E, C1r, C1i, C2r; upper C2i, C4r, C4i (row sums [7][M])
+#pragma unroll
+  for (int k = 0; k < 7; ++k)
+    if ((k >= 4) == (upper != 0)) atomicAdd(rowsum + k * M + m, (double)mom[k]);
+}
+
+// ---------------------------------------------------------------- writer kernel
 template <int C, int D, int M>
 struct WriterPlan {
-  static_assert(C % 16 == 0 && D % 32 == 0 && M % 8 == 0 && M <= 64 && D <= 256, "shape");
-  // shared by both streams
-  static constexpr int SLAB_AD = 128 * 16;  // drive A rows: modes repeated every 64 lanes
-  static constexpr int AD_BYTES = 2 * (D / 8) * SLAB_AD;
+  static_assert(C % 16 == 0 && D % 32 == 0 && D <= kSlotCols && M % 16 == 0 && M <= 64,
+                "shape");
+  // shared by the slots
+  static constexpr int SLAB_AD = 128 * 16;  // drive A rows: paired mode-major
+  static constexpr int AD_BYTES = (D / 8) * SLAB_AD;
   static constexpr int SLAB_Q = D * 16;
   static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
   static constexpr int SLAB_WS = D * 16;
@@ -845,54 +794,48 @@ struct WriterPlan {
   static constexpr int OFF_AD = 0;
   static constexpr int OFF_Q = OFF_AD + AD_BYTES;
   static constexpr int OFF_WS = OFF_Q + Q_BYTES;
-  static constexpr int OFF_PAR = OFF_WS + WS_BYTES;            // float [4][D]: bias, g, ds, ls
-  static constexpr int OFF_K = OFF_PAR + 4 * D * 4;            // float [kConsts * M]
+  static constexpr int OFF_PAR = OFF_WS + WS_BYTES;            // float [2][D]: bias / 2, c
+  static constexpr int OFF_K = OFF_PAR + 2 * D * 4;            // float [kConsts * M]
   static constexpr int SHARED_END = (OFF_K + kConsts * M * 4 + 127) / 128 * 128;
-  // per stream
+  // per slot
   static constexpr int SLAB_X = kXRows * 16;  // one TMA box; 128-byte multiple
-  static constexpr int X_BYTES = cmax((C / 8) * SLAB_X, ScanLayout<kWriterNSub>::FLOATS * 4);
+  static constexpr int X_BYTES = (C / 8) * SLAB_X;
   static constexpr int SLAB_XH = kChunk * 16;
   static constexpr int SLAB_S = kChunk * 16;  // state slab: one 8-column K group, M-major
   static constexpr int XS_BYTES = cmax((D / 8) * SLAB_XH, (2 * M / 8) * SLAB_S);
-  static constexpr int G_X = 0;                       // x tile, scan scratch, next x tile
-  static constexpr int G_XS = G_X + X_BYTES;          // xhat slab, then state slab
-  static constexpr int G_RED = G_XS + XS_BYTES;       // float [2][128]
-  static constexpr int G_RS = G_RED + 2 * kChunk * 4; // float [128]
-  static constexpr int G_MOM = G_RS + kChunk * 4;     // float [NSUB][7][64] moment partials
-  static constexpr int G_MISC = G_MOM + kWriterNSub * 7 * 64 * 4;  // mbar, item
+  static constexpr int G_X = 0;                // x tile (the next item's once the stem read it)
+  static constexpr int G_XS = G_X + X_BYTES;   // xhat slab, then the state slab
+  static constexpr int G_MISC = G_XS + XS_BYTES;  // MMA mbar, tile mbar, item slots [2]
   static constexpr int G_BYTES = (G_MISC + 64 + 127) / 128 * 128;
-  static constexpr int OFF_TMEM_SLOT = SHARED_END + kWriterStreams * G_BYTES;
+  static constexpr int OFF_TMEM_SLOT = SHARED_END + kSlots * G_BYTES;
   static constexpr int BYTES = OFF_TMEM_SLOT + 16;
-  static constexpr int TMEM_COLS = 512;  // 256 per stream: u re [0,128), u im [128,256);
-                                         // stem and synthesis accumulators reuse [0, D)
   static_assert(BYTES <= 232448, "writer shared memory exceeds 227 KB");
   static_assert(SLAB_X % 128 == 0 && SHARED_END % 128 == 0 && G_BYTES % 128 == 0,
                 "TMA destinations must be 128-byte aligned");
 };
 
 template <int C, int D, int M>
-__global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
+__global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     fused_writer_kernel(const __grid_constant__ FusedArgs a) {
   using P = WriterPlan<C, D, M>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
-  const int g = tid / kFusedThreads, ltid = tid % kFusedThreads;
-  const int lwarp = ltid >> 5, lane = ltid & 31;
-  uint8_t *gs = smem + P::SHARED_END + g * P::G_BYTES;
+  const int slot = tid / kSlotThreads, ltid = tid % kSlotThreads;
+  const int warp = ltid >> 5, lane = ltid & 31;
+  uint8_t *gs = smem + P::SHARED_END + slot * P::G_BYTES;
   uint64_t *mbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC);
-  int64_t *item_slot = reinterpret_cast<int64_t *>(gs + P::G_MISC + 8);  // [2]
-  uint64_t *tbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC + 24);     // x tile arrival
+  uint64_t *tbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC + 8);  // x tile arrival
+  int64_t *item_slot = reinterpret_cast<int64_t *>(gs + P::G_MISC + 16);  // [2]
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_TMEM_SLOT);
-  float *red = reinterpret_cast<float *>(gs + P::G_RED);
-  float *rs_s = reinterpret_cast<float *>(gs + P::G_RS);
-  float *s_mom = reinterpret_cast<float *>(gs + P::G_MOM);
+  // per channel: the stem bias / 2 (the stem GEMM computes acc / 2, so h = v / 2 of
+  // SiLU's tanh form is acc + bias / 2) and c = ls ds g, with which the residual
+  // v = f + ls (s W^T + ds xhat), xhat = f rs g, is f (1 + c rs) + s (ls W)^T
   float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
-  const float *s_bias = par, *s_norm = par + D, *s_ds = par + 2 * D, *s_ls = par + 3 * D;
+  const float *s_hbias = par, *s_c = par + D;
   float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
-  float *s_scan = reinterpret_cast<float *>(gs + P::G_X);  // x tile is dead during the scan
   const uint32_t s_base = sm100::smem_u32(smem);
   const uint32_t g_base = sm100::smem_u32(gs);
-  const int bar_group = 1 + g, bar_lb = 3 + g;
+  const int bar = 1 + slot;
 
   if (ltid == 0) {
     sm100::mbar_init(mbar, 1);
@@ -900,37 +843,32 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
     sm100::fence_barrier_init();
   }
   if (tid < 32) {
-    sm100::tmem_alloc(tmem_slot, P::TMEM_COLS);
+    sm100::tmem_alloc(tmem_slot, 512);
     sm100::tmem_relinquish();
   }
+  trace_begin(a.trace);
   copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
   copy_smem(smem + P::OFF_Q, a.q, P::Q_BYTES);
   copy_smem(smem + P::OFF_WS, a.syn, P::WS_BYTES);
-  copy_floats(par, a.conv_b, D);
-  copy_floats(par + D, a.norm, D);
-  copy_floats(par + 2 * D, a.ds, D);
-  copy_floats(par + 3 * D, a.ls, D);
+  for (int i = tid; i < D; i += blockDim.x) {
+    par[i] = 0.5f * __ldg(a.conv_b + i);
+    par[D + i] = __ldg(a.ls + i) * __ldg(a.ds + i) * __ldg(a.norm + i);
+  }
   copy_floats(s_k, a.consts, kConsts * M);
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
-  const uint32_t tbase = *tmem_slot + 256u * g;
-  uint32_t phase = 0;
-  const int row = 32 * (lwarp & 3) + lane;  // step within the chunk (TMEM lane)
-  const int half = lwarp >> 2;              // column half of the token-major epilogues
-  constexpr int HD = D / 2;
-  const uint32_t lane_addr = tbase + ((uint32_t)(32 * (lwarp & 3)) << 16);
+  const uint32_t tslot = *tmem_slot + (uint32_t)(kSlotCols * slot);
+  const uint32_t lane_addr = tslot + ((uint32_t)(32 * warp) << 16);
+  const int row = 32 * warp + lane;  // token row of the item (TMEM lane)
   const int64_t total = a.B * a.n_chunks;
-  if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
-
+  const uint32_t tag = record_tag(a.epoch, a.epoch_word);
+  const uint32_t rtag = tag ^ a.read_xor;
+  uint32_t phase = 0, tphase = 0;
+  if (a.trace && tid == 0) cta_trace()[13] += 1ull;
   unsigned long long t_last = clock64();
-  // Items are claimed one ahead (alternating slots): iteration k processes
-  // item_slot[k & 1] and claims the next into item_slot[(k + 1) & 1].
-  // The x tile of an item is fetched one item ahead by TMA (one 8-channel box
-  // of rows [t0 - 8, t0 + 136) per K slab, zero outside [0, T)) into the x
-  // region, free once the previous item's scan has finished.  Thread 0 only.
-  uint32_t tphase = 0;
+
   auto issue_tile = [&](int64_t it) {
     const int64_t ch = (uint32_t)it / (uint32_t)a.B, bb = it - ch * a.B;  // items < 2^31
     sm100::mbar_arrive_expect_tx(tbar, (C / 8) * kXRows * 16);
@@ -939,322 +877,343 @@ __global__ void __launch_bounds__(kFusedThreads * kWriterStreams, 1)
       sm100::tma_load_3d(g_base + P::G_X + kc * P::SLAB_X, &a.tmap, tbar, kc * 8,
                          (int)(ch * kChunk - kHalo), (int)bb);
   };
-  if (ltid == 0) item_slot[0] = (int64_t)atomicAdd(a.counter, 1u);
-  group_sync(bar_group);
-  if (ltid == 0 && item_slot[0] < total) issue_tile(item_slot[0]);
+  if (ltid == kTileIssuer) {
+    const int64_t first = (int64_t)atomicAdd(a.counter, 1u);
+    item_slot[0] = first;
+    if (first < total) issue_tile(first);
+  }
+  slot_sync(bar);
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
+    // the next item is claimed now; its tile is fetched once this item's stem
+    // GEMM has read the tile region
+    uint32_t next = 0;
+    if (ltid == kTileIssuer) next = atomicAdd(a.counter, 1u);
     LNET_TRACE(0);
     const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
-    __nv_bfloat16 *out_row = a.out + ((b * a.T + t0 + row) * D + half * HD);
+    __nv_bfloat16 *out_row = a.out + (b * a.T + t0 + row) * D;
 
-    LNET_TRACE(1);
-    // 1-2. x tile (TMA, issued one item ahead), then the stem GEMM: five
-    // row-shifted views of the tile
+    // 1-2. x tile, then the stem GEMM: five row-shifted views of the tile
     if (ltid == 0) {
       if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit)) atomicOr(a.error, kErrTile);
-      tphase ^= 1u;
+      LNET_TRACE(1);
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
       for (int k = 0; k < kTaps; ++k)
-        issue_gemm(tbase, g_base + P::G_X + 4 * k * 16, P::SLAB_X,
+        issue_gemm(tslot, g_base + P::G_X + 4 * k * 16, P::SLAB_X,
                    s_base + P::OFF_Q + k * (C / 8) * P::SLAB_Q, P::SLAB_Q, C / 16, idesc, k > 0);
       sm100::mma_commit(mbar);
     }
-    wait_mma(mbar, phase, a.error, 0);
+    tphase ^= 1u;
+    wait_mma(mbar, phase, a.error, 0, ltid);
     LNET_TRACE(2);
-    // 3. bias + SiLU + RMSNorm (thread per step, two column halves)
+    if (ltid == kTileIssuer) {
+      item_slot[(iter + 1) & 1] = (int64_t)next;
+      if ((int64_t)next < total) issue_tile(next);
+    }
+    // 3. bias + SiLU + RMSNorm, thread per token: f = h + h tanh(h), h = v / 2, kept
+    // as bf16 (the value parked for the residual); xhat = f rs (g is in the drive
+    // frame).  Column pairs go through the paired fp32 pipe.
+    // f (packed bf16) stays in this thread's registers until the residual epilogue
+    // of the same row: no round trip through memory
+    float rs;
+    uint32_t fp[D / 2];
     {
-      float f[HD];
+      float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < HD / 16; ++j)
-        sm100::tmem_ld16(lane_addr + half * HD + 16 * j, f + 16 * j);
-      sm100::tmem_ld_wait();
-      float ss = 0.f;
+      for (int j = 0; j < D / 32; ++j) {
+        float acc[32];
+        sm100::tmem_ld32(lane_addr + 32 * j, acc);
+        sm100::tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < HD; ++i) {
-        f[i] = silu_fast(f[i] + s_bias[half * HD + i]);
-        ss = fmaf(f[i], f[i], ss);
+        for (int i = 0; i < 32; i += 2) {
+          const float2 h = __fadd2_rn(make_float2(acc[i], acc[i + 1]),
+                                      make_float2(s_hbias[32 * j + i], s_hbias[32 * j + i + 1]));
+          float t0, t1;
+          asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
+          asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
+          const float2 f = __ffma2_rn(h, make_float2(t0, t1), h);
+          ss2 = __ffma2_rn(f, f, ss2);
+          fp[16 * j + i / 2] = pack_bf16x2(f.x, f.y);
+        }
       }
-      red[half * kChunk + row] = ss;
-      group_sync(bar_group);
-      const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
-      if (half == 0) rs_s[row] = rs;
+      rs = rsqrtf((ss2.x + ss2.y) / (float)D + kFp32Eps);
+      const float2 rs2 = make_float2(rs, rs);
 #pragma unroll
-      for (int gq = 0; gq < HD / 8; ++gq) {
-        const int d0 = half * HD + 8 * gq;
-        uint4 xh, fl;
-        float h[8];
+      for (int gq = 0; gq < D / 8; ++gq) {
+        const uint4 fv = make_uint4(fp[4 * gq], fp[4 * gq + 1], fp[4 * gq + 2], fp[4 * gq + 3]);
+        float fl[8], h[8];
+        bf16x8_to_float(fv, fl);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) h[i] = f[8 * gq + i] * rs * s_norm[d0 + i];
-        xh.x = pack_bf16x2(h[0], h[1]);
-        xh.y = pack_bf16x2(h[2], h[3]);
-        xh.z = pack_bf16x2(h[4], h[5]);
-        xh.w = pack_bf16x2(h[6], h[7]);
-        fl.x = pack_bf16x2(f[8 * gq + 0], f[8 * gq + 1]);
-        fl.y = pack_bf16x2(f[8 * gq + 2], f[8 * gq + 3]);
-        fl.z = pack_bf16x2(f[8 * gq + 4], f[8 * gq + 5]);
-        fl.w = pack_bf16x2(f[8 * gq + 6], f[8 * gq + 7]);
-        *reinterpret_cast<uint4 *>(gs + P::G_XS + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
-        // the stem output waits in the output rows (L2) for the residual epilogue
-        if (row < n) *reinterpret_cast<uint4 *>(out_row + 8 * gq) = fl;
+        for (int i = 0; i < 8; i += 2) {
+          const float2 x2 = __fmul2_rn(make_float2(fl[i], fl[i + 1]), rs2);
+          h[i] = x2.x;
+          h[i + 1] = x2.y;
+        }
+        *reinterpret_cast<uint4 *>(gs + P::G_XS + gq * P::SLAB_XH + row * 16) = pack_bf16x8(h);
       }
     }
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
-    group_sync(bar_group);
+    slot_sync(bar);
     LNET_TRACE(3);
-    // 4. drive GEMM, mode-major: lanes = modes, columns = steps (overwrites the stem acc)
+    // 4. drive GEMM, paired mode-major (overwrites the stem accumulator)
     if (ltid == 0) {
       sm100::tc_fence_after();
-      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 128);
-      for (int part = 0; part < 2; ++part)
-        issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
-                   P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16, idesc, false);
-      sm100::mma_commit(mbar);
-    }
-    // the last thread claims the next item while the drive GEMM runs (off the
-    // MMA-issuing thread, whose barrier arrival gates the stream)
-    if (ltid == kFusedThreads - 1) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
-    LookbackPrefetch pre;
-    lookback_prefetch<M, kWriterNSub>(ltid, a.rec, b, chunk, a.n_chunks, pre);
-    wait_mma(mbar, phase, a.error, 1);
-    LNET_TRACE(4);
-    // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
-    chunk_scan<M, true, kWriterNSub>(ltid, bar_group, bar_lb, tbase, 0, 128, n, b, chunk,
-                                     a.n_chunks, s_k, a.rec, a.epoch, a.epoch_word, a.read_xor,
-                                     a.spin_limit, a.error,
-                                     gs + P::G_XS,
-                                     P::SLAB_S, s_scan,
-                                     a.rowsum + b * 7 * M, a.trace,
-                                     a.kernel_id, pre, s_mom);
-    sm100::fence_proxy_async_smem();
-    sm100::tc_fence_before();
-    group_sync(bar_group);
-    LNET_TRACE(5);
-    // 6. synthesis GEMM (token-major) into columns [0, D); meanwhile the next
-    // item's x tile and this row's stem output are fetched
-    if (ltid == 0) {
-      sm100::tc_fence_after();
-      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D, /*a_mn_major=*/true);
-      issue_gemm(tbase, g_base + P::G_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, kChunk);
+      issue_gemm(tslot, s_base + P::OFF_AD, P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
     }
-    if (ltid == kTileIssuer) {
-      const int64_t next = item_slot[(iter + 1) & 1];
-      if (next < total) issue_tile(next);
+    LookbackPrefetch pre;
+    lookback_prefetch<M>(warp, lane, a.rec, b, chunk, a.n_chunks, pre);
+    wait_mma(mbar, phase, a.error, 1, ltid);
+    LNET_TRACE(4);
+    // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
+    slot_scan<M, true>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag, rtag,
+                       a.spin_limit, a.error, a.kernel_id, a.trace, gs + P::G_XS, P::SLAB_S,
+                       a.rowsum + b * 7 * M, pre);
+    sm100::fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    slot_sync(bar);
+    LNET_TRACE(5);
+    // 6. synthesis GEMM (token-major) into columns [0, D)
+    if (ltid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D, /*a_mn_major=*/true);
+      issue_gemm(tslot, g_base + P::G_XS, P::SLAB_S, s_base + P::OFF_WS, P::SLAB_WS, 2 * M / 16,
+                 idesc, false);
+      sm100::mma_commit(mbar);
     }
-    uint4 flv[HD / 8];
-    if (row < n) {
-#pragma unroll
-      for (int gq = 0; gq < HD / 8; ++gq) flv[gq] = *reinterpret_cast<const uint4 *>(out_row + 8 * gq);
-    }
-    reduce_moments<M, kWriterNSub>(ltid, s_mom, a.rowsum + b * 7 * M);
-    wait_mma(mbar, phase, a.error, 2);
+    wait_mma(mbar, phase, a.error, 2, ltid);
     LNET_TRACE(6);
-    // 7. residual epilogue: v = fl + ls * (modal + ds * xhat), xhat = fl * rs * g
-    {
-      float modal[HD];
+    // 7. residual epilogue: v = f (1 + c rs) + s (ls W)^T
 #pragma unroll
-      for (int j = 0; j < HD / 16; ++j)
-        sm100::tmem_ld16(lane_addr + half * HD + 16 * j, modal + 16 * j);
+    for (int j = 0; j < D / 32; ++j) {
+      float modal[32];
+      sm100::tmem_ld32(lane_addr + 32 * j, modal);
       sm100::tmem_ld_wait();
-      const float rsr = rs_s[row];
       if (row < n) {
 #pragma unroll
-        for (int gq = 0; gq < HD / 8; ++gq) {
-          const int d0 = half * HD + 8 * gq;
-          float fv[8];
-          bf16x8_to_float(flv[gq], fv);
-          float o[8];
+        for (int g4 = 0; g4 < 4; ++g4) {
+          const int gq = 4 * j + g4;
+          float fv[8], o[8];
+          bf16x8_to_float(make_uint4(fp[4 * gq], fp[4 * gq + 1], fp[4 * gq + 2], fp[4 * gq + 3]),
+                          fv);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int d = d0 + i;
-            const float x = fv[i];
-            const float xh = x * rsr * s_norm[d];
-            o[i] = x + s_ls[d] * (modal[8 * gq + i] + s_ds[d] * xh);
+          for (int i = 0; i < 8; i += 2) {
+            const int d = 8 * gq + i;
+            const float2 k2 = __ffma2_rn(make_float2(s_c[d], s_c[d + 1]), make_float2(rs, rs),
+                                         make_float2(1.f, 1.f));
+            const float2 v2 = __ffma2_rn(make_float2(fv[i], fv[i + 1]), k2,
+                                         make_float2(modal[8 * g4 + i], modal[8 * g4 + i + 1]));
+            o[i] = v2.x;
+            o[i + 1] = v2.y;
           }
-          uint4 ov;
-          ov.x = pack_bf16x2(o[0], o[1]);
-          ov.y = pack_bf16x2(o[2], o[3]);
-          ov.z = pack_bf16x2(o[4], o[5]);
-          ov.w = pack_bf16x2(o[6], o[7]);
-          *reinterpret_cast<uint4 *>(out_row + 8 * gq) = ov;
+          *reinterpret_cast<uint4 *>(out_row + 8 * gq) = pack_bf16x8(o);
         }
       }
     }
     sm100::tc_fence_before();
-    group_sync(bar_group);
+    slot_sync(bar);  // TMEM columns and tiles free; the next item id is visible
     LNET_TRACE(7);
-    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
+    if (a.trace && tid == 0) cta_trace()[15] += 1ull;
   }
-  if (a.trace && ltid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
+  if (a.trace && tid == 0) cta_trace()[14] += 1ull;
+  sm100::tc_fence_before();
   __syncthreads();
+  trace_flush(a.trace, a.kernel_id);
   if (tid < 32) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(*tmem_slot, P::TMEM_COLS);
+    sm100::tmem_dealloc(*tmem_slot, 512);
   }
 }
 
 // ---------------------------------------------------------------- reader kernel
 template <int D, int M>
-__global__ void __launch_bounds__(kFusedThreads, 2)
+struct ReaderPlan {
+  static_assert(D % 32 == 0 && D <= kSlotCols && M % 16 == 0 && M <= 64, "shape");
+  static constexpr int SLAB_AD = 128 * 16;
+  static constexpr int AD_BYTES = (D / 8) * SLAB_AD;
+  static constexpr int OFF_AD = 0;
+  static constexpr int OFF_PAR = OFF_AD + AD_BYTES;  // float [6][D]: w(5), bias
+  static constexpr int OFF_K = OFF_PAR + 6 * D * 4;
+  static constexpr int SHARED_END = (OFF_K + kConsts * M * 4 + 127) / 128 * 128;
+  static constexpr int SLAB_V = kXRows * 16;  // stream tile: K-major slabs of 8 channels
+  static constexpr int V_BYTES = (D / 8) * SLAB_V;
+  static constexpr int SLAB_XH = kChunk * 16;
+  static constexpr int G_V = 0;
+  static constexpr int G_XH = G_V + V_BYTES;
+  static constexpr int G_MISC = G_XH + (D / 8) * SLAB_XH;
+  static constexpr int G_BYTES = (G_MISC + 64 + 127) / 128 * 128;
+  static constexpr int OFF_TMEM_SLOT = SHARED_END + kSlots * G_BYTES;
+  static constexpr int BYTES = OFF_TMEM_SLOT + 16;
+  static_assert(BYTES <= 232448, "reader shared memory exceeds 227 KB");
+  static_assert(SLAB_V % 128 == 0 && SHARED_END % 128 == 0 && G_BYTES % 128 == 0,
+                "TMA destinations must be 128-byte aligned");
+};
+
+template <int D, int M>
+__global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     fused_reader_kernel(const __grid_constant__ FusedArgs a) {
   using P = ReaderPlan<D, M>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_MISC + 8);
-  int64_t *item_slot = reinterpret_cast<int64_t *>(smem + P::OFF_MISC + 16);  // [2]
-  uint64_t *tbar = reinterpret_cast<uint64_t *>(smem + P::OFF_MISC + 32);      // tile arrival
-  float *red = reinterpret_cast<float *>(smem + P::OFF_RED);
+  const int tid = threadIdx.x;
+  const int slot = tid / kSlotThreads, ltid = tid % kSlotThreads;
+  const int warp = ltid >> 5, lane = ltid & 31;
+  uint8_t *gs = smem + P::SHARED_END + slot * P::G_BYTES;
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC);
+  uint64_t *tbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC + 8);  // tile arrival
+  int64_t *item_slot = reinterpret_cast<int64_t *>(gs + P::G_MISC + 16);  // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + P::OFF_TMEM_SLOT);
   float *par = reinterpret_cast<float *>(smem + P::OFF_PAR);
-  const float *s_w = par, *s_bias = par + kTaps * D, *s_norm = par + (kTaps + 1) * D;
+  const float *s_w = par, *s_bias = par + kTaps * D;
   float *s_k = reinterpret_cast<float *>(smem + P::OFF_K);
-  float *s_scan = reinterpret_cast<float *>(smem + P::OFF_XH);  // xhat is dead during the scan
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t s_base = sm100::smem_u32(smem);
+  const uint32_t g_base = sm100::smem_u32(gs);
+  const int bar = 1 + slot;
 
-  if (tid == 0) {
+  if (ltid == 0) {
     sm100::mbar_init(mbar, 1);
     sm100::mbar_init(tbar, 1);
     sm100::fence_barrier_init();
   }
-  if (warp == 0) {
-    sm100::tmem_alloc(tmem_slot, P::TMEM_COLS);
+  if (tid < 32) {
+    sm100::tmem_alloc(tmem_slot, 512);
     sm100::tmem_relinquish();
   }
+  trace_begin(a.trace);
   copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
-  // conv weights transposed to [tap][channel]
-  for (int i = tid; i < kTaps * D; i += kFusedThreads) {
+  // conv weights transposed to [tap][channel] and the bias, halved: the conv then
+  // yields h = v / 2 of SiLU's tanh form directly (exact scaling)
+  for (int i = tid; i < kTaps * D; i += blockDim.x) {
     const int k = i / D, d = i - (i / D) * D;
-    par[i] = __ldg(a.conv_w + d * kTaps + k);
+    par[i] = 0.5f * __ldg(a.conv_w + d * kTaps + k);
   }
-  copy_floats(par + kTaps * D, a.conv_b, D);
-  copy_floats(par + (kTaps + 1) * D, a.norm, D);
+  for (int i = tid; i < D; i += blockDim.x) par[kTaps * D + i] = 0.5f * __ldg(a.conv_b + i);
   copy_floats(s_k, a.consts, kConsts * M);
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
-  const uint32_t tbase = *tmem_slot;
-  uint32_t phase = 0;
-  const int row = 32 * (warp & 3) + lane;
-  const int half = warp >> 2;
-  constexpr int HD = D / 2;
+  const uint32_t tslot = *tmem_slot + (uint32_t)(kSlotCols * slot);
+  const uint32_t lane_addr = tslot + ((uint32_t)(32 * warp) << 16);
+  const int row = 32 * warp + lane;
   const int64_t total = a.B * a.n_chunks;
-  if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][13], 1ull);
-
+  const uint32_t tag = record_tag(a.epoch, a.epoch_word);
+  const uint32_t rtag = tag ^ a.read_xor;
+  uint32_t phase = 0, tphase = 0;
+  if (a.trace && tid == 0) cta_trace()[13] += 1ull;
   unsigned long long t_last = clock64();
-  // Stream tiles are fetched one item ahead by TMA (thread 0; one 8-channel
-  // box per K slab), issued as soon as the conv of the current item has read
-  // the tile region.
-  uint32_t tphase = 0;
+
   auto issue_tile = [&](int64_t it) {
     const int64_t ch = (uint32_t)it / (uint32_t)a.B, bb = it - ch * a.B;  // items < 2^31
     sm100::mbar_arrive_expect_tx(tbar, (D / 8) * kXRows * 16);
 #pragma unroll
     for (int kc = 0; kc < D / 8; ++kc)
-      sm100::tma_load_3d(s_base + P::OFF_V + kc * P::SLAB_V, &a.tmap, tbar, kc * 8,
+      sm100::tma_load_3d(g_base + P::G_V + kc * P::SLAB_V, &a.tmap, tbar, kc * 8,
                          (int)(ch * kChunk - kHalo), (int)bb);
   };
-  if (tid == 0) item_slot[0] = (int64_t)atomicAdd(a.counter, 1u);
-  __syncthreads();
-  if (tid == 0 && item_slot[0] < total) issue_tile(item_slot[0]);
+  if (ltid == kTileIssuer) {
+    const int64_t first = (int64_t)atomicAdd(a.counter, 1u);
+    item_slot[0] = first;
+    if (first < total) issue_tile(first);
+  }
+  slot_sync(bar);
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
+    uint32_t next = 0;
+    if (ltid == kTileIssuer) next = atomicAdd(a.counter, 1u);
     LNET_TRACE(0);
     const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
 
-    // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T), issued one item ahead
-    if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && tid == 0)
+    // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T), fetched one item ahead
+    if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && ltid == 0)
       atomicOr(a.error, kErrTile << 1);
     tphase ^= 1u;
-    // the last thread claims the next item (its latency overlaps the conv)
-    if (tid == kFusedThreads - 1) item_slot[(iter + 1) & 1] = (int64_t)atomicAdd(a.counter, 1u);
     LNET_TRACE(1);
-    // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm
-    float f[HD];
+    // 2. depthwise conv (K5, dilation 4) + bias + SiLU + RMSNorm, thread per token
+    {
+      float f[D];
 #pragma unroll
-    for (int i = 0; i < HD; ++i) f[i] = s_bias[half * HD + i];
+      for (int i = 0; i < D; ++i) f[i] = s_bias[i];
 #pragma unroll
-    for (int k = 0; k < kTaps; ++k) {
-      const uint8_t *src = smem + P::OFF_V + (half * HD / 8) * P::SLAB_V + (row + 4 * k) * 16;
-      const float *wk = s_w + k * D + half * HD;
+      for (int k = 0; k < kTaps; ++k) {
+        const uint8_t *src = gs + P::G_V + (row + 4 * k) * 16;
+        const float *wk = s_w + k * D;
 #pragma unroll
-      for (int g = 0; g < HD / 8; ++g) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(src + g * P::SLAB_V);
-        float vv[8];
-        bf16x8_to_float(v, vv);
+        for (int g = 0; g < D / 8; ++g) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(src + g * P::SLAB_V);
+          float vv[8];
+          bf16x8_to_float(v, vv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[8 * g + i] = fmaf(wk[8 * g + i], vv[i], f[8 * g + i]);
+          for (int i = 0; i < 8; ++i) f[8 * g + i] = fmaf(wk[8 * g + i], vv[i], f[8 * g + i]);
+        }
       }
-    }
-    float ss = 0.f;
+      float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < HD; ++i) {
-      f[i] = silu_fast(f[i]);
-      ss = fmaf(f[i], f[i], ss);
-    }
-    red[half * kChunk + row] = ss;
-    __syncthreads();
-    if (tid == kTileIssuer) {  // every thread has read the tile: fetch the next item's
-      const int64_t next = item_slot[(iter + 1) & 1];
-      if (next < total) issue_tile(next);
-    }
-    const float rs = rsqrtf((red[row] + red[kChunk + row]) / (float)D + kFp32Eps);
+      for (int i = 0; i < D; i += 2) {  // f = h + h tanh(h), h = v / 2
+        const float2 h = make_float2(f[i], f[i + 1]);
+        float t0, t1;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
+        const float2 v = __ffma2_rn(h, make_float2(t0, t1), h);
+        ss2 = __ffma2_rn(v, v, ss2);
+        f[i] = v.x;
+        f[i + 1] = v.y;
+      }
+      const float rs = rsqrtf((ss2.x + ss2.y) / (float)D + kFp32Eps);
 #pragma unroll
-    for (int g = 0; g < HD / 8; ++g) {
-      const int d0 = half * HD + 8 * g;
-      float h[8];
+      for (int g = 0; g < D / 8; ++g) {
+        float h[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs * s_norm[d0 + i];
-      uint4 xh;
-      xh.x = pack_bf16x2(h[0], h[1]);
-      xh.y = pack_bf16x2(h[2], h[3]);
-      xh.z = pack_bf16x2(h[4], h[5]);
-      xh.w = pack_bf16x2(h[6], h[7]);
-      *reinterpret_cast<uint4 *>(smem + P::OFF_XH + (d0 / 8) * P::SLAB_XH + row * 16) = xh;
+        for (int i = 0; i < 8; ++i) h[i] = f[8 * g + i] * rs;  // g is in the drive frame
+        *reinterpret_cast<uint4 *>(gs + P::G_XH + g * P::SLAB_XH + row * 16) = pack_bf16x8(h);
+      }
     }
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
-    __syncthreads();
+    slot_sync(bar);
     LNET_TRACE(3);
-    // 3. drive GEMM (mode-major)
-    if (tid == 0) {
+    // every thread has read the tile: fetch the next item's
+    if (ltid == kTileIssuer) {
+      item_slot[(iter + 1) & 1] = (int64_t)next;
+      if ((int64_t)next < total) issue_tile(next);
+    }
+    // 3. drive GEMM (paired mode-major)
+    if (ltid == 0) {
       sm100::tc_fence_after();
-      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 128);
-      for (int part = 0; part < 2; ++part)
-        issue_gemm(tbase + part * 128, s_base + P::OFF_AD + part * (D / 8) * P::SLAB_AD,
-                   P::SLAB_AD, s_base + P::OFF_XH, P::SLAB_XH, D / 16, idesc, false);
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, kChunk);
+      issue_gemm(tslot, s_base + P::OFF_AD, P::SLAB_AD, g_base + P::G_XH, P::SLAB_XH, D / 16,
+                 idesc, false);
       sm100::mma_commit(mbar);
     }
     LookbackPrefetch pre;
-    lookback_prefetch<M, 4>(tid, a.rec, b, chunk, a.n_chunks, pre);
-    wait_mma(mbar, phase, a.error, 3);
+    lookback_prefetch<M>(warp, lane, a.rec, b, chunk, a.n_chunks, pre);
+    wait_mma(mbar, phase, a.error, 3, ltid);
     LNET_TRACE(4);
     // 4. scan + look-back + moments
-    chunk_scan<M, false, 4>(tid, 0, 1, tbase, 0, 128, n, b, chunk, a.n_chunks, s_k, a.rec,
-                            a.epoch, a.epoch_word, a.read_xor, a.spin_limit, a.error, nullptr,
-                            0, s_scan,
-                            a.rowsum + b * 7 * M, a.trace, a.kernel_id,
-                            pre);
+    slot_scan<M, false>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag, rtag,
+                        a.spin_limit, a.error, a.kernel_id, a.trace, nullptr, 0,
+                        a.rowsum + b * 7 * M, pre);
     sm100::tc_fence_before();
-    __syncthreads();
+    slot_sync(bar);  // TMEM columns free; the next item id is visible
     LNET_TRACE(5);
-    if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][15], 1ull);
+    if (a.trace && tid == 0) cta_trace()[15] += 1ull;
   }
-  if (a.trace && tid == 0) atomicAdd(&g_fused_trace[a.kernel_id][14], 1ull);
+  if (a.trace && tid == 0) cta_trace()[14] += 1ull;
+  sm100::tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  trace_flush(a.trace, a.kernel_id);
+  if (tid < 32) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tbase, P::TMEM_COLS);
+    sm100::tmem_dealloc(*tmem_slot, 512);
   }
 }
 
@@ -1413,8 +1372,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, WP::BYTES),
                       "cudaFuncSetAttribute(fused_writer_kernel)"));
   const int64_t items = B * nch;
-  fused_writer_kernel<C, D, M><<<(unsigned)std::min<int64_t>(cdiv(items, kWriterStreams), sms),
-                                 kFusedThreads * kWriterStreams, WP::BYTES, st>>>(wa);
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(items, kSlots), sms);
+  fused_writer_kernel<C, D, M><<<grid, kSlots * kSlotThreads, WP::BYTES, st>>>(wa);
   LNET_TRY(after_launch("fused_writer_kernel"));
   FusedArgs ra = wa;
   ra.in = w.stream;
@@ -1433,11 +1392,9 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   ra.counter = counters + 1;
   ra.kernel_id = 1;
   LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_reader_kernel<D, M>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           RP::LAUNCH_BYTES),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, RP::BYTES),
                       "cudaFuncSetAttribute(fused_reader_kernel)"));
-  fused_reader_kernel<D, M><<<(unsigned)std::min<int64_t>(items, 2 * (int64_t)sms),
-                              kFusedThreads, RP::LAUNCH_BYTES, st>>>(ra);
+  fused_reader_kernel<D, M><<<grid, kSlots * kSlotThreads, RP::BYTES, st>>>(ra);
   LNET_TRY(after_launch("fused_reader_kernel"));
   fused_finalize_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * 14 * M, 256), 8 * sms), 256, 0,
                           st>>>(w.rowsum, wm, rm, w.feats, B, T, M, w.epoch_word);

@@ -8,6 +8,7 @@ raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -206,8 +207,10 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        path = _build.LIB
-        if auto_build and _build.needs_build():
+        # LNET_B200_LIBRARY: load that build of the library instead of the in-tree one
+        override = os.environ.get("LNET_B200_LIBRARY")
+        path = Path(override) if override else _build.LIB
+        if not override and auto_build and _build.needs_build():
             try:
                 _build.build()
             except RuntimeError:
