@@ -578,7 +578,7 @@ __device__ __forceinline__ void load_pair(uint32_t lane_addr, int c0, int upper,
 // WRITE_STATES: the true states are written (bf16, M-major) into `s_slab` as the
 // synthesis A operand: element (t, j) at (j / 8) * SLAB + (t / 8) * 128 +
 // (j % 8) * 16 + (t % 8) * 2, j = m (re) or M + m (im).
-template <int M, bool WRITE_STATES>
+template <int M, bool WRITE_STATES, bool REAL>
 __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr, int n,
                                           int64_t row, int64_t chunk, int64_t n_chunks,
                                           const float *K, unsigned long long *rec, uint32_t tag,
@@ -599,7 +599,9 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
   const float sg = upper ? -1.f : 1.f;  // conjugation of constants in the upper frame
   const int s0 = kHalf * upper;
   const int len = max(0, min(kHalf, n - s0));
-  const float ar = K[m], ai = sg * K[M + m];
+  // REAL: every pole of the block is real (a_im = 0), so the two components of a
+  // mode evolve independently and the recurrence is one FMA per component
+  const float ar = K[m], ai = REAL ? 0.f : sg * K[M + m];
 
   // ---- pass 1: local scan of the thread's 64 steps from zero (own frame)
   float sx = 0.f, sy = 0.f;
@@ -612,8 +614,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
       const bool last = c0 + 32 == kHalf;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float nx = fmaf(ar, sx, fmaf(-ai, sy, x[i]));
-        const float ny = fmaf(ai, sx, fmaf(ar, sy, y[i]));
+        const float nx = REAL ? fmaf(ar, sx, x[i]) : fmaf(ar, sx, fmaf(-ai, sy, x[i]));
+        const float ny = REAL ? fmaf(ar, sy, y[i]) : fmaf(ai, sx, fmaf(ar, sy, y[i]));
         sx = nx;
         sy = ny;
         if (i >= 28 && last) {
@@ -625,8 +627,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         if (c0 + i < len) {
-          const float nx = fmaf(ar, sx, fmaf(-ai, sy, x[i]));
-          const float ny = fmaf(ai, sx, fmaf(ar, sy, y[i]));
+          const float nx = REAL ? fmaf(ar, sx, x[i]) : fmaf(ar, sx, fmaf(-ai, sy, x[i]));
+          const float ny = REAL ? fmaf(ar, sy, y[i]) : fmaf(ai, sx, fmaf(ar, sy, y[i]));
           sx = nx;
           sy = ny;
           lx[3] = lx[2]; ly[3] = ly[2];
@@ -709,8 +711,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
   float2 H1 = make_float2(h1x, h1y), H2 = make_float2(h2x, h2y);
   float2 H3 = make_float2(h3x, h3y), H4 = make_float2(h4x, h4y);
   auto step2 = [&](float ux, float uy) {
-    const float nx = fmaf(ar, sx, fmaf(-ai, sy, ux));
-    const float ny = fmaf(ai, sx, fmaf(ar, sy, uy));
+    const float nx = REAL ? fmaf(ar, sx, ux) : fmaf(ar, sx, fmaf(-ai, sy, ux));
+    const float ny = REAL ? fmaf(ar, sy, uy) : fmaf(ai, sx, fmaf(ar, sy, uy));
     sx = nx;
     sy = ny;
     const float2 S = make_float2(nx, ny);
@@ -857,7 +859,9 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
   copy_floats(s_k, a.consts, kConsts * M);
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
-  __syncthreads();
+  // every pole of this block real (a_im = 0 for every mode): the real-pole scan
+  // (read from global: the shared copy is complete only after this barrier)
+  const bool real_poles = !__syncthreads_or(tid < M && __ldg(a.consts + M + tid) != 0.f);
   sm100::tc_fence_after();
   const uint32_t tslot = *tmem_slot + (uint32_t)(kSlotCols * slot);
   const uint32_t lane_addr = tslot + ((uint32_t)(32 * warp) << 16);
@@ -894,7 +898,6 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
     const int n = (int)min((int64_t)kChunk, a.T - t0);
-    __nv_bfloat16 *out_row = a.out + (b * a.T + t0 + row) * D;
 
     // 1-2. x tile, then the stem GEMM: five row-shifted views of the tile
     if (ltid == 0) {
@@ -905,6 +908,10 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
       for (int k = 0; k < kTaps; ++k)
         issue_gemm(tslot, g_base + P::G_X + 4 * k * 16, P::SLAB_X,
                    s_base + P::OFF_Q + k * (C / 8) * P::SLAB_Q, P::SLAB_Q, C / 16, idesc, k > 0);
+      // the previous item's output copy must have read the slab before anyone writes
+      // xhat into it; committing after this wait makes the stem GEMM's completion,
+      // which every thread waits for, imply it
+      sm100::bulk_wait_read();
       sm100::mma_commit(mbar);
     }
     tphase ^= 1u;
@@ -973,9 +980,14 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     wait_mma(mbar, phase, a.error, 1, ltid);
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
-    slot_scan<M, true>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag, rtag,
-                       a.spin_limit, a.error, a.kernel_id, a.trace, gs + P::G_XS, P::SLAB_S,
-                       a.rowsum + b * 7 * M, pre);
+    if (real_poles)
+      slot_scan<M, true, true>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+                               rtag, a.spin_limit, a.error, a.kernel_id, a.trace, gs + P::G_XS,
+                               P::SLAB_S, a.rowsum + b * 7 * M, pre);
+    else
+      slot_scan<M, true, false>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+                                rtag, a.spin_limit, a.error, a.kernel_id, a.trace, gs + P::G_XS,
+                                P::SLAB_S, a.rowsum + b * 7 * M, pre);
     sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     slot_sync(bar);
@@ -990,39 +1002,48 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     }
     wait_mma(mbar, phase, a.error, 2, ltid);
     LNET_TRACE(6);
-    // 7. residual epilogue: v = f (1 + c rs) + s (ls W)^T
+    // 7. residual epilogue: v = f (1 + c rs) + s (ls W)^T, staged row-major in the
+    // state slab (the synthesis GEMM has read it) and written by one bulk copy
+    uint8_t *stage = gs + P::G_XS + row * (D * 2);
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) {
       float modal[32];
       sm100::tmem_ld32(lane_addr + 32 * j, modal);
       sm100::tmem_ld_wait();
-      if (row < n) {
 #pragma unroll
-        for (int g4 = 0; g4 < 4; ++g4) {
-          const int gq = 4 * j + g4;
-          float fv[8], o[8];
-          bf16x8_to_float(make_uint4(fp[4 * gq], fp[4 * gq + 1], fp[4 * gq + 2], fp[4 * gq + 3]),
-                          fv);
+      for (int g4 = 0; g4 < 4; ++g4) {
+        const int gq = 4 * j + g4;
+        float fv[8], o[8];
+        bf16x8_to_float(make_uint4(fp[4 * gq], fp[4 * gq + 1], fp[4 * gq + 2], fp[4 * gq + 3]),
+                        fv);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            const int d = 8 * gq + i;
-            const float2 k2 = __ffma2_rn(make_float2(s_c[d], s_c[d + 1]), make_float2(rs, rs),
-                                         make_float2(1.f, 1.f));
-            const float2 v2 = __ffma2_rn(make_float2(fv[i], fv[i + 1]), k2,
-                                         make_float2(modal[8 * g4 + i], modal[8 * g4 + i + 1]));
-            o[i] = v2.x;
-            o[i + 1] = v2.y;
-          }
-          *reinterpret_cast<uint4 *>(out_row + 8 * gq) = pack_bf16x8(o);
+        for (int i = 0; i < 8; i += 2) {
+          const int d = 8 * gq + i;
+          const float2 k2 = __ffma2_rn(make_float2(s_c[d], s_c[d + 1]), make_float2(rs, rs),
+                                       make_float2(1.f, 1.f));
+          const float2 v2 = __ffma2_rn(make_float2(fv[i], fv[i + 1]), k2,
+                                       make_float2(modal[8 * g4 + i], modal[8 * g4 + i + 1]));
+          o[i] = v2.x;
+          o[i + 1] = v2.y;
         }
+        *reinterpret_cast<uint4 *>(stage + 16 * gq) = pack_bf16x8(o);
       }
     }
+    sm100::fence_proxy_async_smem();
     sm100::tc_fence_before();
     slot_sync(bar);  // TMEM columns and tiles free; the next item id is visible
+    // rows [t0, t0 + n) of the stream are contiguous: one bulk copy; thread 0 waits for
+    // its read of the slab before the next item's stem GEMM (whose completion every
+    // thread waits for before writing the slab again)
+    if (ltid == 0) {
+      sm100::bulk_store(a.out + (b * a.T + t0) * D, g_base + P::G_XS, (uint32_t)(n * D * 2));
+      sm100::bulk_commit();
+    }
     LNET_TRACE(7);
     if (a.trace && tid == 0) cta_trace()[15] += 1ull;
   }
   if (a.trace && tid == 0) cta_trace()[14] += 1ull;
+  if (ltid == 0) sm100::bulk_wait_all();  // the slot's output copies are complete
   sm100::tc_fence_before();
   __syncthreads();
   trace_flush(a.trace, a.kernel_id);
@@ -1097,7 +1118,9 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
   copy_floats(s_k, a.consts, kConsts * M);
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
-  __syncthreads();
+  // every pole of this block real (a_im = 0 for every mode): the real-pole scan
+  // (read from global: the shared copy is complete only after this barrier)
+  const bool real_poles = !__syncthreads_or(tid < M && __ldg(a.consts + M + tid) != 0.f);
   sm100::tc_fence_after();
   const uint32_t tslot = *tmem_slot + (uint32_t)(kSlotCols * slot);
   const uint32_t lane_addr = tslot + ((uint32_t)(32 * warp) << 16);
@@ -1153,7 +1176,13 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
           float vv[8];
           bf16x8_to_float(v, vv);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[8 * g + i] = fmaf(wk[8 * g + i], vv[i], f[8 * g + i]);
+          for (int i = 0; i < 8; i += 2) {
+            const float2 r = __ffma2_rn(make_float2(wk[8 * g + i], wk[8 * g + i + 1]),
+                                        make_float2(vv[i], vv[i + 1]),
+                                        make_float2(f[8 * g + i], f[8 * g + i + 1]));
+            f[8 * g + i] = r.x;
+            f[8 * g + i + 1] = r.y;
+          }
         }
       }
       float2 ss2 = make_float2(0.f, 0.f);
@@ -1199,9 +1228,14 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     wait_mma(mbar, phase, a.error, 3, ltid);
     LNET_TRACE(4);
     // 4. scan + look-back + moments
-    slot_scan<M, false>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag, rtag,
-                        a.spin_limit, a.error, a.kernel_id, a.trace, nullptr, 0,
-                        a.rowsum + b * 7 * M, pre);
+    if (real_poles)
+      slot_scan<M, false, true>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+                                rtag, a.spin_limit, a.error, a.kernel_id, a.trace, nullptr, 0,
+                                a.rowsum + b * 7 * M, pre);
+    else
+      slot_scan<M, false, false>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+                                 rtag, a.spin_limit, a.error, a.kernel_id, a.trace, nullptr, 0,
+                                 a.rowsum + b * 7 * M, pre);
     sm100::tc_fence_before();
     slot_sync(bar);  // TMEM columns free; the next item id is visible
     LNET_TRACE(5);

@@ -31,15 +31,30 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with `parity` to complete; gives up after `limit` polls.
-// test_wait never suspends the thread, so the bound is a bound in time too
-// (try_wait may block for an implementation-defined interval per poll).
+// One bounded suspending wait: true once the phase with `parity` has completed;
+// the thread may sleep up to `hint_ns` nanoseconds inside (waking early when the
+// phase completes) and returns false if it has not completed by then.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with `parity` to complete; gives up after `limit` tries.
+// Each try suspends the thread for at most 1 us (try_wait with an explicit
+// suspend-time hint), so a waiting warp takes no issue slots from the warps that
+// compute, and the wait is bounded by about limit microseconds.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   uint32_t limit) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    if (mbar_test(bar, parity)) return true;
-    if (i > 4096) __nanosleep(64);  // short waits (MMA completion) never sleep
-  }
+  if (mbar_test(bar, parity)) return true;
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity, 1000u)) return true;
   return false;
 }
 
@@ -71,6 +86,25 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
       ::"r"(dst), "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Untiled bulk copy this CTA's shared memory -> global (both addresses 16-byte
+// aligned, `bytes` a multiple of 16), tracked by the issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores have finished READING shared memory.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
