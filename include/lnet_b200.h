@@ -271,6 +271,24 @@ int lnet_b200_laplace_forward(const double *raw_decay, const double *residues,
                               const void *x, int64_t batch, int64_t steps, void *y,
                               void *workspace, size_t workspace_bytes, lnet_stream_t stream);
 
+/* The same layer when its residues are diagonal in channels (R[o, m, i] = 0
+ * for i != o, e.g. M real poles per channel): given, per output channel o, the
+ * indices mode_index[o, j] (int32 [Dm, K]) of the modes with a nonzero
+ * residue and those residues residue[o, j] = R[o, mode_index[o, j], o]
+ * (float64 [Dm, K]; unused slots: any valid index with residue 0), computes
+ * the same y with K state updates per channel instead of a dense [Dm, M Dm]
+ * contraction.  K <= 16; no workspace.  The caller (B200PoleResidueTemporalMixing)
+ * detects the structure from the dense residues.  A specialisation of
+ * PoleResidueTemporalMixing.forward (src/lnet/laplace.py:126-159) for the
+ * per-channel pole layout. */
+int lnet_b200_laplace_forward_channelwise(const double *raw_decay, const int32_t *mode_index,
+                                          const double *residue, const double *direct,
+                                          const double *bias, int32_t model_dim, int32_t modes,
+                                          int32_t modes_per_channel, double dt,
+                                          double min_decay, int32_t x_dtype, const void *x,
+                                          int64_t batch, int64_t steps, void *y,
+                                          lnet_stream_t stream);
+
 /* Allocation-free variant of lnet_b200_laplace_forward for callers that may
  * not allocate device memory (foreign memory pools, plugin hosts that forbid
  * cudaMalloc, real-time loops).  Same arguments minus the workspace: the

@@ -235,6 +235,171 @@ extern "C" int lnet_b200_laplace_forward(const double *raw_decay, const double *
   return fail(LNET_ERR_UNSUPPORTED, "laplace: x dtype must be float32 or float64");
 }
 
+namespace lnet {
+
+// ---------------------------------------------------------------- channel-diagonal residues
+// When R[o, m, i] = 0 for every i != o (each output reads only the states of its
+// own input channel -- the per-channel pole layout), the readout collapses to
+//   y_t[o] = sum_j r[o, j] s_t[m_j, o] + (D x_t)[o] + bias[o],
+// with only the K modes m_j = mode_index[o, j] whose residue is nonzero.  One
+// thread owns (row, channel, time chunk) with its K states in registers: a
+// local scan of its chunk from zero, the chunk carries combined in shared
+// memory (each chunk's true initial state = sum over earlier chunks of
+// a^(steps between) * their local end states), then a second scan from the true
+// carry that writes y.  The CTA first stages its row's input [T, D] in shared
+// memory (as double) when it fits, so the scans read no global memory.  No
+// scratch in global memory.
+constexpr int kDiagChunks = 32;   // time chunks per (row, channel)
+constexpr int kDiagChans = 8;     // channels per CTA
+// the row's input [T, D] as double in shared memory when it fits (else read from global)
+constexpr size_t kDiagStageBytes = 160 * 1024;
+constexpr int kDiagMaxModes = 16; // K bound (registers per thread)
+
+template <typename TX, int K, bool STAGED>
+__global__ void __launch_bounds__(kDiagChunks * kDiagChans) laplace_diag_kernel(
+    const TX *__restrict__ x, const double *__restrict__ raw_decay,
+    const int32_t *__restrict__ mode_index, const double *__restrict__ residue,
+    const double *__restrict__ direct, const double *__restrict__ bias, int dim, int kmodes,
+    double dt, double min_decay, int64_t steps, TX *__restrict__ y) {
+  __shared__ double s_end[kDiagChunks][kDiagChans][K];
+  const int o_loc = threadIdx.x % kDiagChans, c = threadIdx.x / kDiagChans;
+  const int o = blockIdx.x * kDiagChans + o_loc;
+  const int64_t b = blockIdx.y;
+  const bool live = o < dim;
+  const int64_t L = (steps + kDiagChunks - 1) / kDiagChunks;
+  const int64_t t_begin = c * L, t_end = min(steps, t_begin + L);
+  double a[K], g[K], r[K], s[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    a[j] = 0.0;
+    g[j] = 0.0;
+    r[j] = 0.0;
+    s[j] = 0.0;
+    if (live && j < kmodes) {
+      laplace_zoh(raw_decay[mode_index[o * kmodes + j]], dt, min_decay, a[j], g[j]);
+      r[j] = residue[o * kmodes + j];
+    }
+  }
+  const TX *xr = x + b * steps * dim;
+  extern __shared__ double s_x[];  // [T][D] when STAGED
+  if constexpr (STAGED) {
+    for (int64_t e = threadIdx.x; e < steps * dim; e += blockDim.x) s_x[e] = (double)load_f(xr, e);
+    __syncthreads();
+  }
+  auto xin = [&](int64_t e) -> double {
+    if constexpr (STAGED)
+      return s_x[e];
+    else
+      return (double)load_f(xr, e);
+  };
+  // ---- pass 1: local scan from zero
+  for (int64_t t = t_begin; t < t_end; ++t) {
+    const double xv = live ? xin(t * dim + o) : 0.0;
+#pragma unroll
+    for (int j = 0; j < K; ++j) s[j] = fma(a[j], s[j], g[j] * xv);
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) s_end[c][o_loc][j] = s[j];
+  __syncthreads();
+  // ---- carry: the state before this chunk, from the earlier chunks' local ends
+  // (every earlier chunk is full, L steps)
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    double aL = 1.0;
+    for (int64_t k = 0; k < L; ++k) aL *= a[j];
+    double carry = 0.0;
+    for (int cc = 0; cc < c; ++cc) carry = fma(aL, carry, s_end[cc][o_loc][j]);
+    s[j] = carry;
+  }
+  // ---- pass 2: from the true carry, the readout
+  const double bo = live ? bias[o] : 0.0;
+  for (int64_t t = t_begin; t < t_end; ++t) {
+    const double xv = live ? xin(t * dim + o) : 0.0;
+    double acc = 0.0;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      s[j] = fma(a[j], s[j], g[j] * xv);
+      acc = fma(r[j], s[j], acc);
+    }
+    if (live) {
+      double dsum = 0.0;
+      for (int i = 0; i < dim; ++i)
+        dsum = fma(xin(t * dim + i), direct[o * dim + i], dsum);
+      const double v = acc + dsum + bo;
+      if constexpr (sizeof(TX) == 8)
+        y[(b * steps + t) * dim + o] = v;
+      else
+        y[(b * steps + t) * dim + o] = (TX)(float)v;
+    }
+  }
+}
+
+template <typename TX>
+static int laplace_diag_run(const double *raw_decay, const int32_t *mode_index,
+                            const double *residue, const double *direct, const double *bias,
+                            int dim, int kmodes, double dt, double min_decay, const TX *x,
+                            int64_t batch, int64_t steps, TX *y, cudaStream_t st) {
+  const dim3 grid((unsigned)cdiv(dim, kDiagChans), (unsigned)batch);
+  const int threads = kDiagChunks * kDiagChans;
+  const size_t stage = (size_t)steps * dim * sizeof(double);
+  const bool staged = stage <= kDiagStageBytes;
+#define LNET_DIAG_CASE(KK)                                                                    \
+  if (kmodes <= KK) {                                                                         \
+    if (staged) {                                                                             \
+      auto kern = laplace_diag_kernel<TX, KK, true>;                                          \
+      LNET_TRY(cuda_check(cudaFuncSetAttribute(kern,                                          \
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                               (int)kDiagStageBytes),                         \
+                          "cudaFuncSetAttribute(laplace_diag_kernel)"));                      \
+      kern<<<grid, threads, stage, st>>>(x, raw_decay, mode_index, residue, direct, bias, dim, \
+                                         kmodes, dt, min_decay, steps, y);                    \
+    } else {                                                                                  \
+      laplace_diag_kernel<TX, KK, false><<<grid, threads, 0, st>>>(                           \
+          x, raw_decay, mode_index, residue, direct, bias, dim, kmodes, dt, min_decay, steps, \
+          y);                                                                                 \
+    }                                                                                         \
+    return after_launch("laplace_diag_kernel");                                               \
+  }
+  LNET_DIAG_CASE(4)
+  LNET_DIAG_CASE(8)
+  LNET_DIAG_CASE(16)
+#undef LNET_DIAG_CASE
+  return fail(LNET_ERR_UNSUPPORTED, "laplace (channel-diagonal): %d modes per channel > %d",
+              kmodes, kDiagMaxModes);
+}
+
+}  // namespace lnet
+
+extern "C" int lnet_b200_laplace_forward_channelwise(
+    const double *raw_decay, const int32_t *mode_index, const double *residue,
+    const double *direct, const double *bias, int32_t model_dim, int32_t modes,
+    int32_t modes_per_channel, double dt, double min_decay, int32_t x_dtype, const void *x,
+    int64_t batch, int64_t steps, void *y, lnet_stream_t stream) {
+  reset_launches();
+  if (model_dim < 1 || modes < 1 || batch < 0 || steps < 0 || modes_per_channel < 1)
+    return fail(LNET_ERR_INVALID_ARGUMENT,
+                "invalid laplace shape (D=%d, M=%d, K=%d, B=%lld, T=%lld)", model_dim, modes,
+                modes_per_channel, (long long)batch, (long long)steps);
+  if (modes_per_channel > kDiagMaxModes)
+    return fail(LNET_ERR_UNSUPPORTED, "laplace (channel-diagonal): %d modes per channel > %d",
+                modes_per_channel, kDiagMaxModes);
+  if (batch == 0 || steps == 0) return LNET_OK;
+  if (!raw_decay || !mode_index || !residue || !direct || !bias || !x || !y)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "laplace: NULL tensor pointer");
+  if (batch > 65535) return fail(LNET_ERR_UNSUPPORTED, "laplace: batch > 65535");
+  auto st = (cudaStream_t)stream;
+  begin_entry(st);
+  if (x_dtype == LNET_F64)
+    return laplace_diag_run<double>(raw_decay, mode_index, residue, direct, bias, model_dim,
+                                    modes_per_channel, dt, min_decay, (const double *)x, batch,
+                                    steps, (double *)y, st);
+  if (x_dtype == LNET_F32)
+    return laplace_diag_run<float>(raw_decay, mode_index, residue, direct, bias, model_dim,
+                                   modes_per_channel, dt, min_decay, (const float *)x, batch,
+                                   steps, (float *)y, st);
+  return fail(LNET_ERR_UNSUPPORTED, "laplace: x dtype must be float32 or float64");
+}
+
 // ---------------------------------------------------------------- allocation-free variant
 // Some callers cannot allocate device memory at all: code running inside a
 // memory pool it does not own, plugins whose host framework forbids

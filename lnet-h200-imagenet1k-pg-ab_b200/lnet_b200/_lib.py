@@ -173,6 +173,11 @@ SIGNATURES = {
         [_c_p, _c_p, _c_p, _c_p, _i32, _i32, ctypes.c_double, ctypes.c_double, _i32, _c_p, _i64,
          _i64, _c_p, _c_p, ctypes.c_size_t, _c_p],
     ),
+    "lnet_b200_laplace_forward_channelwise": (
+        ctypes.c_int,
+        [_c_p, _c_p, _c_p, _c_p, _c_p, _i32, _i32, _i32, ctypes.c_double, ctypes.c_double, _i32,
+         _c_p, _i64, _i64, _c_p, _c_p],
+    ),
     "lnet_b200_laplace_noalloc_max_scratch_bytes": (ctypes.c_size_t, []),
     "lnet_b200_laplace_forward_noalloc": (
         ctypes.c_int,

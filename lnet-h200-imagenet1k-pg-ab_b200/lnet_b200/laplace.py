@@ -6,7 +6,11 @@ Mirrors src/lnet/laplace.py:55-159: the same float64 parameters
 reference's ``LaplaceParameterError`` checks, and ``forward`` raising
 ``LaplaceShapeError`` for bad ranks/widths.  The recurrence and the readout
 run in float64 in one kernel pair (``lnet_b200_laplace_forward``); the state
-never reaches HBM.
+never reaches HBM.  When the residues are diagonal in channels (each output
+reads only its own input channel's states, as with M real poles per channel)
+the layer runs ``lnet_b200_laplace_forward_channelwise`` instead: K state
+updates per channel and no [D, M D] contraction.  The structure is detected
+once per parameter version.
 """
 
 from __future__ import annotations
@@ -114,15 +118,72 @@ class B200PoleResidueTemporalMixing(nn.Module):
         return laplace_forward_raw(self, inputs.contiguous())
 
 
+MAX_MODES_PER_CHANNEL = 16  # bound of lnet_b200_laplace_forward_channelwise
+
+
+def channel_diagonal_form(residues: Tensor) -> tuple[Tensor, Tensor] | None:
+    """(mode_index [D, K] int32, residue [D, K] float64) when ``residues`` [D, M, D]
+    is zero off the channel diagonal (R[o, m, i] = 0 for i != o) and every output
+    has at most MAX_MODES_PER_CHANNEL nonzero R[o, m, o]; else None.  Padding slots
+    carry a valid mode with residue 0 (they add exactly 0)."""
+    d, m, d2 = residues.shape
+    if d != d2:
+        return None
+    r = residues.detach()
+    eye = torch.eye(d, dtype=torch.bool, device=r.device)
+    if bool((r.permute(0, 2, 1)[~eye] != 0).any()):  # [o, i, m] off the diagonal
+        return None
+    ar = torch.arange(d, device=r.device)
+    diag = r[ar, :, ar]  # [o, m] = R[o, m, o]
+    nz = diag != 0
+    k = max(1, int(nz.sum(dim=1).max()))
+    if k > MAX_MODES_PER_CHANNEL:
+        return None
+    # nonzero modes first (stable order), then padding
+    order = torch.argsort((~nz).to(torch.int8), dim=1, stable=True)[:, :k]
+    vals = torch.gather(diag, 1, order) * torch.gather(nz, 1, order)
+    return order.to(torch.int32).contiguous(), vals.to(torch.float64).contiguous()
+
+
 def laplace_forward_raw(layer: B200PoleResidueTemporalMixing, x: Tensor) -> Tensor:
-    """One ``lnet_b200_laplace_forward`` call with ``layer``'s parameters."""
+    """One ``lnet_b200_laplace_forward`` (or, for channel-diagonal residues,
+    ``lnet_b200_laplace_forward_channelwise``) call with ``layer``'s parameters."""
     dev = x.device
 
     def f64(p: Tensor) -> Tensor:
         return p.detach().to(device=dev, dtype=torch.float64).contiguous()
 
+    key = (dev, layer.residues._version, layer.residues.data_ptr())
+    cache = getattr(layer, "_diag_cache", None)
+    if cache is None or cache[0] != key:
+        layer._diag_cache = cache = (key, channel_diagonal_form(f64(layer.residues)))
+    if cache[1] is not None:
+        idx, vals = cache[1]
+        return _launch_channelwise(x, f64(layer.raw_decay), idx, vals, f64(layer.direct_term),
+                                   f64(layer.bias), layer.modes, float(layer.dt),
+                                   float(layer.min_decay))
     return _launch(x, f64(layer.raw_decay), f64(layer.residues), f64(layer.direct_term),
                    f64(layer.bias), layer.modes, float(layer.dt), float(layer.min_decay))
+
+
+def _launch_channelwise(x: Tensor, raw: Tensor, idx: Tensor, vals: Tensor, direct: Tensor,
+                        bias: Tensor, modes: int, dt: float, min_decay: float) -> Tensor:
+    """The channel-diagonal C-ABI call on the current stream."""
+    lib = _lib.load()
+    dev = x.device
+    b, t, d = x.shape
+    y = torch.empty_like(x)
+    if b == 0 or t == 0:
+        return y
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    dtype = _lib.LNET_F64 if x.dtype == torch.float64 else _lib.LNET_F32
+    with torch.cuda.device(dev):
+        st = lib.lnet_b200_laplace_forward_channelwise(
+            raw.data_ptr(), idx.data_ptr(), vals.data_ptr(), direct.data_ptr(), bias.data_ptr(),
+            d, modes, idx.shape[1], dt, min_decay, dtype, x.data_ptr(), b, t, y.data_ptr(),
+            stream)
+    _lib.check(st, "lnet_b200_laplace_forward_channelwise")
+    return y
 
 
 def _launch(x: Tensor, raw: Tensor, res: Tensor, direct: Tensor, bias: Tensor, modes: int,

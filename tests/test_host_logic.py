@@ -103,3 +103,30 @@ def test_patchify_reference_layout():
         u = torch.tensor(float(img[b, pr * 2 + i, pc * 2 + j, ch]))
         want = (u / 255.0 - torch.tensor(mean[ch])) / torch.tensor(std[ch])
         assert x[b, pr * 4 + pc, (i * 2 + j) * 3 + ch] == want
+
+
+def test_laplace_channel_diagonal_form():
+    """The per-channel (block-diagonal) residue layout is recognised: per output the
+    modes with a nonzero R[o, m, o], padded with residue 0; dense residues or too many
+    modes per channel fall back to the dense kernel (None)."""
+    import torch
+
+    from lnet_b200.laplace import MAX_MODES_PER_CHANNEL, channel_diagonal_form
+
+    d, per = 4, 3
+    r = torch.zeros(d, d * per, d, dtype=torch.float64)
+    for ch in range(d):
+        r[ch, ch * per:(ch + 1) * per, ch] = torch.arange(1, per + 1, dtype=torch.float64) + ch
+    r[2, 2 * per + 1, 2] = 0.0  # channel 2 has one mode fewer
+    idx, vals = channel_diagonal_form(r)
+    assert idx.shape == (d, per) and idx.dtype == torch.int32
+    for ch in range(d):
+        got = {(int(m), float(v)) for m, v in zip(idx[ch], vals[ch]) if v != 0}
+        want = {(m, float(r[ch, m, ch])) for m in range(d * per) if r[ch, m, ch] != 0}
+        assert got == want
+    assert float(vals[2].abs().min()) == 0.0  # the padding slot adds exactly zero
+    dense = r.clone()
+    dense[0, 0, 1] = 1.0
+    assert channel_diagonal_form(dense) is None
+    wide = torch.ones(1, MAX_MODES_PER_CHANNEL + 1, 1, dtype=torch.float64)
+    assert channel_diagonal_form(wide) is None
