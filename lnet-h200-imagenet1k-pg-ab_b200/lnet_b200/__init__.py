@@ -11,6 +11,8 @@ Laplace layer behind the reference ``lnet`` module API.
 * :mod:`lnet_b200.inference` — ``prepare_compiled_inference`` /
   ``prepare_maskless_inference`` with the reference's call surface.
 * :mod:`lnet_b200.sharding` — batch sharding over one process per GPU.
+* :mod:`lnet_b200.channelsplit` — mode (channel) split over ranks (one
+  all-reduce of the writer stream, one all-gather of moment sums).
 * :mod:`lnet_b200.timesplit` — sequence split over ranks (one carry exchange
   per block) for requests with fewer rows than GPUs.
 * :mod:`lnet_b200.images` — uint8 images -> normalised 4x4 patch tokens on the

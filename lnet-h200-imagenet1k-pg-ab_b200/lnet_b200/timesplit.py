@@ -260,10 +260,10 @@ def drive_program(prog, world: int, group=None):
             return stop.value
 
 
-def timesplit_emulate(model, x: Tensor, world: int) -> list[Tensor]:
-    """The `world` rank programs run in lockstep in this process (collectives
-    evaluated locally); returns every rank's logits."""
-    progs = [_rank_program(model, x, r, world) for r in range(world)]
+def run_lockstep(progs) -> list:
+    """Runs rank programs (generators yielding ("gather", t) / ("sum", t)) in lockstep
+    in this process, evaluating each collective locally; returns every rank's result."""
+    world = len(progs)
     reqs = [next(p) for p in progs]
     while True:
         kinds = {k for k, _ in reqs}
@@ -288,4 +288,10 @@ def timesplit_emulate(model, x: Tensor, world: int) -> list[Tensor]:
         reqs = out
 
 
-__all__ = ["drive_program", "timesplit_emulate", "timesplit_forward"]
+def timesplit_emulate(model, x: Tensor, world: int) -> list[Tensor]:
+    """The `world` rank programs run in lockstep in this process (collectives
+    evaluated locally); returns every rank's logits."""
+    return run_lockstep([_rank_program(model, x, r, world) for r in range(world)])
+
+
+__all__ = ["drive_program", "run_lockstep", "timesplit_emulate", "timesplit_forward"]
