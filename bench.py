@@ -247,9 +247,9 @@ def algorithmic_bytes(kernel: str, cfg) -> float | None:
         # fused route: stream v in (moments out are negligible)
         "fused_reader_kernel": bt * D * sa,
         # general route
-        "cublas(stem)": bt * (C * sx + D * 4),
-        "cublas(drive)": bt * (D * 4 + 2 * M * 4),
-        "cublas(synthesis)": bt * (2 * M * 4 + D * 4),
+        "gemm(stem)": bt * (C * sx + D * 4),
+        "gemm(drive)": bt * (D * 4 + 2 * M * 4),
+        "gemm(synthesis)": bt * (2 * M * 4 + D * 4),
         "scan_local_kernel": bt * 2 * M * 4,
         "scan_apply_kernel": bt * 2 * M * 8,
         "moments_partial_kernel": bt * 2 * M * 4,
@@ -836,6 +836,58 @@ def run_b200(args, cfg):
     return 0
 
 
+def run_split(args, cfg):
+    """``--split time|channel`` (config 5's multi-GPU variants): every rank holds the
+    whole request and runs its share of the split forward through the module-level
+    API (lnet_b200.timesplit / lnet_b200.channelsplit), collectives included in the
+    timed region; time = max over ranks of the summed per-step CUDA-event times.
+    Rank 0 also compares the split logits with its unsplit forward of the same rows."""
+    import torch
+    import torch.distributed as dist
+
+    from lnet_b200.channelsplit import channelsplit_forward
+    from lnet_b200.timesplit import timesplit_forward
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    model = build_model(cfg, dev)
+    x = make_inputs(cfg, dev)
+    fn = timesplit_forward if args.split == "time" else channelsplit_forward
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            fn(model, x)
+        with ClockSampler(local) as clocks:
+            total_ms = _time_steps(lambda: fn(model, x), args.steps, stream, flush, world, dist,
+                                   dev)
+        out = fn(model, x)
+        err = None
+        if rank == 0:
+            ref = model(x)
+            err = float((out - ref).abs().max() / ref.abs().max())
+    if rank == 0:
+        B, T = cfg["B"], cfg["T"]
+        print(json.dumps({
+            "metric": METRIC, "value": B * T * args.steps / (total_ms / 1e3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"],
+            "data": "synthetic", "config": {"workload": cfg["workload"],
+                                            "parallelism": f"{args.split}-split x{world}",
+                                            "path": f"lnet_b200.{args.split}split",
+                                            "l2": "256 MiB flush between steps"},
+            "split_vs_unsplit_rel_err": err, "clocks": clocks.summary()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def _lib_kernels(prof):
     return {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()}
 
@@ -851,6 +903,8 @@ def main():
                     help="rows of the CPU baseline step (default: the whole batch)")
     ap.add_argument("--ref-rows", type=int, default=0,
                     help="rows per reference-arm step (default: the whole batch)")
+    ap.add_argument("--split", choices=["batch", "time", "channel"], default="batch",
+                    help="time / channel: config 5's split variants across the ranks")
     ap.add_argument("--weak", action="store_true",
                     help="also time the weak-scaling workload at N=1 (always at N>1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -875,6 +929,12 @@ def main():
             log("--mode train covers the ALPHABET configs (2, 3, 4, 5)")
             return 2
         return run_train(args, cfg)
+    if args.split != "batch":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the split variants are timed on the GPU path only"}), flush=True)
+            return 0
+        return run_split(args, cfg)
     if args.impl == "reference" and not (cfg.get("meta") or cfg.get("laplace")):
         return run_reference(args, cfg)
     if cfg.get("meta") or cfg.get("laplace"):

@@ -111,6 +111,13 @@ int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
  * give-up surfaces; no reference counterpart. */
 int lnet_b200_debug_inject_lookback_miss(void);
 
+/* GEMM backend of the general route (process-wide): 0 = this library's tcgen05
+ * row GEMM wherever the shape fits it (n, k <= 128; bf16 x bf16 for bf16
+ * operands, split-bf16 x3 for fp32 operands), cuBLAS otherwise (default);
+ * 1 = cuBLAS for every GEMM (used by the tests to compare the two).  No
+ * reference counterpart: replaces the reference's torch matmuls on this path. */
+int lnet_b200_set_gemm_backend(int backend);
+
 /* Route selection for lnet_b200_alphabet_forward (process-wide):
  * 0 = automatic (the fused unit-grid kernels when the request has no
  * metadata, bf16 activations and a compiled shape; the general route

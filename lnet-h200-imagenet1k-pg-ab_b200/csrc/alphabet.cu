@@ -204,16 +204,16 @@ static int stem_projection(const lnet_b200_alphabet_params *p, const lnet_b200_a
         x, r->observation_mask, r->obs_channels, r->valid_mask, pl.xm, bt, C);
     LNET_TRY(after_launch("mask_inputs_kernel"));
     LNET_TRY(gemm_rows(st, pl.xm, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, pl.proj, D,
-                       bt, D, C, tf32, "cublas(stem)"));
+                       bt, D, C, tf32, "gemm(stem)"));
   } else if (std::is_same<TX, float>::value) {
     LNET_TRY(gemm_rows(st, x, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, pl.proj, D, bt,
-                       D, C, tf32, "cublas(stem)"));
+                       D, C, tf32, "gemm(stem)"));
   } else {  // bf16 x: bf16 x bf16 -> fp32 (the weights rounded to bf16, as under autocast)
     to_bf16_kernel<<<grid_for((int64_t)D * C), 256, 0, st>>>(p->stem_projection, pl.w_bf16,
                                                              (int64_t)D * C);
     LNET_TRY(after_launch("to_bf16_kernel"));
     LNET_TRY(gemm_rows(st, x, CUDA_R_16BF, C, pl.w_bf16, CUDA_R_16BF, C, 1, pl.proj, D, bt, D, C,
-                       false, "cublas(stem)"));
+                       false, "gemm(stem)"));
   }
   return LNET_OK;
 }
@@ -265,13 +265,13 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
     LNET_TRY(after_launch("fold_gain_kernel"));
     if (xhat_bf16)  // bf16 x bf16 tensor-core GEMM, fp32 accumulation
       LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_16BF, D, pl.wfold_bf16, CUDA_R_16BF, 1, 2 * M,
-                         pl.drive, 2 * M, bt, 2 * M, D, false, "cublas(drive)"));
+                         pl.drive, 2 * M, bt, 2 * M, D, false, "gemm(drive)"));
     else
       LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, pl.drive,
-                         2 * M, bt, 2 * M, D, tf32, "cublas(drive)"));
+                         2 * M, bt, 2 * M, D, tf32, "gemm(drive)"));
   } else {
     LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
-                       bt, 2 * M, D, tf32, "cublas(drive)"));
+                       bt, 2 * M, D, tf32, "gemm(drive)"));
     drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(pl.drive, raw_decay, raw_freq,
                                                             r->time_delta, g_re, g_im, event_mask,
                                                             obs_channels, bt, M);
@@ -384,7 +384,7 @@ static int forward_generic_normed(const lnet_b200_alphabet_params *p,
       p->writer_frame, p->writer_layer_scale, pl.wfold, D, 2 * M);
   LNET_TRY(after_launch("scale_rows_kernel"));
   LNET_TRY(gemm_rows(st, pl.drive, CUDA_R_32F, 2 * M, pl.wfold, CUDA_R_32F, 2 * M, 1, pl.stream,
-                     D, bt, D, 2 * M, tf32, "cublas(synthesis)", /*beta=*/1.f));
+                     D, bt, D, 2 * M, tf32, "gemm(synthesis)", /*beta=*/1.f));
   if (half)
     LNET_TRY(conv_norm((const float *)pl.stream, p->reader_conv_weight, p->reader_conv_bias,
                        r->valid_mask, r->valid_mask, p->reader_norm, nullptr, nullptr, xh16,
@@ -410,7 +410,7 @@ static int writer_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
                               r->observation_mask, r->obs_channels, r, D, M, pl, moments,
                               /*write_states=*/true, st));
   LNET_TRY(gemm_rows(st, pl.drive, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
-                     pl.modal, D, bt, D, 2 * M, r->act_dtype == LNET_BF16, "cublas(synthesis)"));
+                     pl.modal, D, bt, D, 2 * M, r->act_dtype == LNET_BF16, "gemm(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(first_local, pl.xhat, pl.modal,
                                                      p->writer_direct_scale,
                                                      p->writer_layer_scale, stream_out, bt, D);
@@ -486,6 +486,13 @@ using namespace lnet;
 
 extern "C" int lnet_b200_debug_inject_lookback_miss(void) {
   g_inject_miss.store(1);
+  return LNET_OK;
+}
+
+extern "C" int lnet_b200_set_gemm_backend(int backend) {
+  if (backend != 0 && backend != 1)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "gemm backend must be 0 or 1");
+  rowgemm_enabled() = backend == 0;
   return LNET_OK;
 }
 
@@ -733,10 +740,10 @@ extern "C" int lnet_b200_block_drive(const lnet_b200_alphabet_params *params,
     to_bf16_kernel<<<grid_for(bt * D), 256, 0, st>>>(xhat, xh16, bt * D);
     LNET_TRY(after_launch("to_bf16_kernel"));
     return gemm_rows(st, xh16, CUDA_R_16BF, D, pl.wfold_bf16, CUDA_R_16BF, 1, 2 * M, u_out, 2 * M,
-                     bt, 2 * M, D, false, "cublas(drive)");
+                     bt, 2 * M, D, false, "gemm(drive)");
   }
   return gemm_rows(st, xhat, CUDA_R_32F, D, pl.wfold, CUDA_R_32F, 1, 2 * M, u_out, 2 * M, bt,
-                   2 * M, D, req->act_dtype == LNET_BF16, "cublas(drive)");
+                   2 * M, D, req->act_dtype == LNET_BF16, "gemm(drive)");
 }
 
 extern "C" int lnet_b200_block_scan(const lnet_b200_alphabet_params *params,
@@ -814,10 +821,10 @@ extern "C" int lnet_b200_writer_output(const lnet_b200_alphabet_params *params,
         params->writer_frame, params->writer_layer_scale, pl.wfold, D, 2 * M);
     LNET_TRY(after_launch("scale_rows_kernel"));
     return gemm_rows(st, states, CUDA_R_32F, 2 * M, pl.wfold, CUDA_R_32F, 2 * M, 1, stream_out,
-                     D, bt, D, 2 * M, tf32, "cublas(synthesis)", /*beta=*/1.f);
+                     D, bt, D, 2 * M, tf32, "gemm(synthesis)", /*beta=*/1.f);
   }
   LNET_TRY(gemm_rows(st, states, CUDA_R_32F, 2 * M, params->writer_frame, CUDA_R_32F, 2 * M, 1,
-                     pl.modal, D, bt, D, 2 * M, tf32, "cublas(synthesis)"));
+                     pl.modal, D, bt, D, 2 * M, tf32, "gemm(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
       first_local, xhat, pl.modal, params->writer_direct_scale, params->writer_layer_scale,
       stream_out, bt, D);

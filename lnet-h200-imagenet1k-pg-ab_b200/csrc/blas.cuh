@@ -1,9 +1,9 @@
-// Plain library GEMMs of the general route (cuBLAS): the stem projection, the
-// drive projection and the synthesis of every request the fused route does
-// not take.  fp32 requests compute in fp32 (CUBLAS_COMPUTE_32F, no tensor-core
-// rounding, the precision of the reference's fp32 matmuls); bf16 requests use
-// TF32 tensor cores (more mantissa than the bf16 operands of the reference's
-// autocast matmuls).
+// GEMMs of the general route: the stem projection, the drive projection and the
+// synthesis of every request the fused route does not take.  gemm_rows runs
+// them on this library's tcgen05 row GEMM (rowgemm.cuh: bf16 x bf16 for bf16
+// operands, split-bf16 x3 -- fp32-level accuracy -- for fp32 operands) whenever
+// the shape fits it (n, k <= 128), and on cuBLAS otherwise (fp32 requests in
+// CUBLAS_COMPUTE_32F, bf16 requests on TF32 or bf16 tensor cores).
 #pragma once
 
 #include <cublas_v2.h>
@@ -12,6 +12,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "rowgemm.cuh"
 
 namespace lnet {
 
@@ -63,10 +64,18 @@ inline int gemm_rows_t(cudaStream_t st, const void *A, cudaDataType ta, int64_t 
   return after_library(what);
 }
 
+// Whether gemm_rows may use rowgemm (process-wide; tests compare both).
+inline bool &rowgemm_enabled() {
+  static bool on = true;
+  return on;
+}
+
 inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t lda, const void *Bm,
                      cudaDataType tb, int64_t ldbn, int64_t ldbk, float *C, int64_t ldc,
                      int64_t rows, int n, int k, bool tf32, const char *what,
-                     float beta = 0.f) {
+                     float beta = 0.f, uint32_t *status = nullptr) {
+  if (rowgemm_enabled() && rows > 0 && rowgemm_supported(ta, tb, n, k))
+    return rowgemm(st, A, ta, lda, Bm, ldbn, ldbk, C, ldc, rows, n, k, beta, status, what);
   return gemm_rows_t(st, A, ta, lda, Bm, tb, ldbn, ldbk, C, CUDA_R_32F, ldc, rows, n, k, tf32,
                      what, beta);
 }

@@ -112,7 +112,7 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
       (const TX *)r->x, r->observation_mask, r->obs_channels, r->valid_mask, tp.x32, bt, C);
   LNET_TRY(after_launch("mask_inputs_kernel"));
   LNET_TRY(gemm_rows(st, tp.x32, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, tp.proj, D,
-                     bt, D, C, tf32, "cublas(stem)"));
+                     bt, D, C, tf32, "gemm(stem)"));
   if (r->time_delta) {  // physical-time convs and moments
     timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, tp.ts, B, T);
     LNET_TRY(after_launch("timestamps_kernel"));
@@ -131,7 +131,7 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
                               tp.a_tab + 5 * M, r->observation_mask, r->obs_channels, &rq, D, M,
                               pw, tp.m1, /*write_states=*/true, st));
   LNET_TRY(gemm_rows(st, tp.s1, CUDA_R_32F, 2 * M, p->writer_frame, CUDA_R_32F, 2 * M, 1,
-                     tp.modal, D, bt, D, 2 * M, tf32, "cublas(synthesis)"));
+                     tp.modal, D, bt, D, 2 * M, tf32, "gemm(synthesis)"));
   residual_kernel<<<token_grid(bt), token_block(D), 0, st>>>(
       tp.y1, tp.xh1, tp.modal, p->writer_direct_scale, p->writer_layer_scale, tp.v, bt, D);
   LNET_TRY(after_launch("residual_kernel"));
@@ -1132,8 +1132,8 @@ static int block_backward(const TrainPlan &tp, const float *states, const float 
   LNET_TRY(after_launch("pole_backward_kernel"));
   const int64_t bt = B * T;
   LNET_TRY(gemm_rows(st, tp.dS, CUDA_R_32F, 2 * M, frame, CUDA_R_32F, 2 * M, 1, dxh, D, bt, D,
-                     2 * M, tf32, "cublas(d xhat)", dxh_beta));
-  return gemm_wgrad(st, xh, D, tp.dS, 2 * M, dframe, bt, frame_beta, tf32, "cublas(d frame)");
+                     2 * M, tf32, "gemm(d xhat)", dxh_beta));
+  return gemm_wgrad(st, xh, D, tp.dS, 2 * M, dframe, bt, frame_beta, tf32, "gemm(d frame)");
 }
 
 static int conv_backward(const TrainPlan &tp, const float *in, const float *w, const float *bias,
@@ -1234,10 +1234,10 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   const bool tf32 = r->act_dtype == LNET_BF16;  // as the training forward
   // head
   LNET_TRY(gemm_wgrad(st, dlogits, K, tp.feats, 14 * M, gd->head_weight, B, 0.f, false,
-                      "cublas(d head)"));
+                      "gemm(d head)"));
   LNET_TRY(colsum(ColPlain{dlogits, K}, B, K, tp.colpart, gd->head_bias, st, "colsum(head b)"));
   LNET_TRY(gemm_rows(st, dlogits, CUDA_R_32F, K, p->head_weight, CUDA_R_32F, 1, 14 * M, tp.dfeats,
-                     14 * M, B, 14 * M, K, false, "cublas(d feats)"));
+                     14 * M, B, 14 * M, K, false, "gemm(d feats)"));
   radial_backward_kernel<<<grid_for(2 * B * 7 * M), 256, 0, st>>>(tp.m1, tp.m2, tp.dfeats, tp.dm,
                                                                   B, M);
   LNET_TRY(after_launch("radial_backward_kernel"));
@@ -1277,10 +1277,10 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
   // dS1 = moments VJP + dv (ls F) (the GEMM accumulates, beta = 1)
   LNET_TRY(moments_vjp(tp, r, tp.s1, dm1, B, T, M, st));
   LNET_TRY(gemm_rows(st, tp.dV, CUDA_R_32F, D, tp.wls, CUDA_R_32F, 1, 2 * M, tp.dS, 2 * M, bt,
-                     2 * M, D, tf32, "cublas(d states synth)", /*beta=*/1.f));
+                     2 * M, D, tf32, "gemm(d states synth)", /*beta=*/1.f));
   // dF1 = ls (dv^T s1) (+ the drive part below)
   LNET_TRY(gemm_wgrad(st, tp.dV, D, tp.s1, 2 * M, gd->writer_frame, bt, 0.f, tf32,
-                      "cublas(d frame synth)"));
+                      "gemm(d frame synth)"));
   scale_rows_kernel<<<grid_for((int64_t)D * 2 * M), 256, 0, st>>>(gd->writer_frame, ls,
                                                                    gd->writer_frame, D, 2 * M);
   LNET_TRY(after_launch("scale_rows_kernel"));
@@ -1302,7 +1302,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
                     tp.dY, tp.dV, gd->stem_conv_weight, gd->stem_conv_bias, B, T, D, taps, dil,
                     st));
   return gemm_wgrad(st, tp.dV, D, tp.x32, C, gd->stem_projection, bt, 0.f, tf32,
-                    "cublas(d projection)");
+                    "gemm(d projection)");
 }
 
 static int train_entry(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,

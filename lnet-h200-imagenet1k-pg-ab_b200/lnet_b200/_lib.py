@@ -122,6 +122,7 @@ SIGNATURES = {
          ctypes.POINTER(ctypes.c_uint32)],
     ),
     "lnet_b200_set_route": (ctypes.c_int, [ctypes.c_int]),
+    "lnet_b200_set_gemm_backend": (ctypes.c_int, [ctypes.c_int]),
     "lnet_b200_debug_inject_lookback_miss": (ctypes.c_int, []),
     "lnet_b200_alphabet_route": (
         ctypes.c_int, [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest)]

@@ -58,7 +58,9 @@ def test_emulated_split_bf16(cuda_device):
     with torch.no_grad():
         ref = model(x).cpu().numpy()
         out = channelsplit_emulate(model, x, 2)[1]
-    assert rel_err(out.cpu().numpy(), ref) <= 1e-4
+    # bf16 drive operands are rounded after different kernels on the two paths
+    # (the unsplit conv + RMSNorm kernel vs the pieces' RMSNorm + conversion)
+    assert rel_err(out.cpu().numpy(), ref) <= 2e-4
 
 
 def test_more_ranks_than_modes_raises(cuda_device):
