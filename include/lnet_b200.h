@@ -148,6 +148,24 @@ int lnet_b200_alphabet_forward_prepared(const lnet_b200_alphabet_params *params,
                                         float *writer_moments, float *reader_moments,
                                         lnet_stream_t stream);
 
+/* lnet_b200_alphabet_forward (prepared = 0) or ..._forward_prepared (prepared =
+ * 1) for a right-padded request: `lengths` (int64 [B], device) holds each row's
+ * valid length L_b, meaning valid_mask[b, t] = 1 for t < L_b and 0 after, and
+ * req carries no metadata.  The result equals the forward with that valid mask
+ * (src/lnet/pac_tight_frame_models.py:1660-1702 masked moments,
+ * src/lnet/alphabet_backbone.py:649-676 / :872-992 stem and reader masking): a
+ * right-padded row computes exactly as an unpadded row of L_b steps, so the
+ * fused route serves it, skipping the padded chunks.  Fails with
+ * LNET_ERR_UNSUPPORTED when the request does not take the fused route (then
+ * pass the mask to lnet_b200_alphabet_forward).  The module
+ * (B200Alphabet.forward) detects right-padded masks and calls this. */
+int lnet_b200_alphabet_forward_lengths(const lnet_b200_alphabet_params *params,
+                                       const lnet_b200_alphabet_request *req,
+                                       const int64_t *lengths, int32_t prepared,
+                                       void *workspace, size_t workspace_bytes, float *logits,
+                                       float *writer_moments, float *reader_moments,
+                                       lnet_stream_t stream);
+
 /* Device-side status of the last lnet_b200_alphabet_forward in `workspace`
  * for this request's route (synchronises the device).  Every wait inside the
  * kernels is bounded; a wait that gave up sets a bit: 1 << 0..3 MMA completion

@@ -548,7 +548,8 @@ extern "C" int lnet_b200_alphabet_workspace_size(const lnet_b200_alphabet_params
 static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
                                  const lnet_b200_alphabet_request *req, void *workspace,
                                  size_t workspace_bytes, float *logits, float *writer_moments,
-                                 float *reader_moments, bool prepared, lnet_stream_t stream) {
+                                 float *reader_moments, bool prepared, lnet_stream_t stream,
+                                 const int64_t *lengths = nullptr) {
   reset_launches();
   LNET_TRY(check_params(params));
   LNET_TRY(check_request(params, req));
@@ -565,7 +566,7 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
     LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, true));
     float *wm = writer_moments ? writer_moments : pl.fused.moments;
     float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
-    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, prepared, st));
+    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, prepared, lengths, st));
     return head_gemm(pl.fused.feats, B, 14 * M, params->head_weight, params->head_bias, logits,
                      params->output_dim, pl.fused.head_partial, st, pl.fused.flags + 2);
   }
@@ -596,6 +597,27 @@ extern "C" int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *param
                                           lnet_stream_t stream) {
   return alphabet_forward_impl(params, req, workspace, workspace_bytes, logits, writer_moments,
                                reader_moments, false, stream);
+}
+
+extern "C" int lnet_b200_alphabet_forward_lengths(const lnet_b200_alphabet_params *params,
+                                                  const lnet_b200_alphabet_request *req,
+                                                  const int64_t *lengths, int32_t prepared,
+                                                  void *workspace, size_t workspace_bytes,
+                                                  float *logits, float *writer_moments,
+                                                  float *reader_moments, lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  LNET_TRY(check_request(params, req));
+  if (!lengths) return fail(LNET_ERR_INVALID_ARGUMENT, "lengths is NULL");
+  if (req->time_delta || req->observation_mask || req->valid_mask)
+    return fail(LNET_ERR_INVALID_ARGUMENT,
+                "forward_lengths: the lengths replace the valid mask; pass no other metadata");
+  if (req->batch > 0 && req->steps > 0 && !use_fused(params, req))
+    return fail(LNET_ERR_UNSUPPORTED,
+                "forward_lengths: this request does not take the fused route; pass the valid "
+                "mask to lnet_b200_alphabet_forward");
+  return alphabet_forward_impl(params, req, workspace, workspace_bytes, logits, writer_moments,
+                               reader_moments, prepared != 0, stream, lengths);
 }
 
 extern "C" int lnet_b200_alphabet_prepare(const lnet_b200_alphabet_params *params,

@@ -269,6 +269,9 @@ struct FusedArgs {
   uint32_t spin_limit;      // polls before a look-back wait gives up
   uint32_t *counter;
   uint32_t *error;
+  // per-row valid lengths [B] (right-padded valid masks) or NULL (every row T steps):
+  // steps at or past a row's length are treated as the zero padding past T
+  const int64_t *lengths;
   int trace;       // 1: accumulate per-phase cycles of slot 0's thread 0 into g_fused_trace
   int kernel_id;   // 0 writer, 1 reader
 };
@@ -371,6 +374,24 @@ __device__ __forceinline__ void cmac(float ar, float ai, float br, float bi, flo
 __device__ __forceinline__ uint32_t record_tag(uint32_t host_seed, const uint32_t *epoch_word) {
   const uint32_t t = host_seed ^ __ldcg(epoch_word);
   return t == 0u ? 0x5BD1E995u : t;
+}
+
+// Steps of row b: its valid length (clamped to [0, T]) or T.
+__device__ __forceinline__ int64_t row_steps(const int64_t *lengths, int64_t b, int64_t T) {
+  return lengths ? max((int64_t)0, min(__ldg(lengths + b), T)) : T;
+}
+
+// Claims the next item whose chunk starts before its row's length (items past a
+// right-padded row's valid steps do not exist); >= total when none is left.
+// Bounded by the number of items.
+__device__ __forceinline__ int64_t claim_item(uint32_t *counter, const int64_t *lengths,
+                                              int64_t B, int64_t T, int64_t total) {
+  for (;;) {
+    const int64_t it = (int64_t)atomicAdd(counter, 1u);
+    if (it >= total || !lengths) return it;
+    const int64_t ch = (uint32_t)it / (uint32_t)B, bb = it - ch * B;  // items < 2^31
+    if (ch * kChunk < row_steps(lengths, bb, T)) return it;
+  }
 }
 
 // Tagged look-back words: (fp32 bits) | (tag << 32), written and read as one
@@ -882,7 +903,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
                          (int)(ch * kChunk - kHalo), (int)bb);
   };
   if (ltid == kTileIssuer) {
-    const int64_t first = (int64_t)atomicAdd(a.counter, 1u);
+    const int64_t first = claim_item(a.counter, a.lengths, a.B, a.T, total);
     item_slot[0] = first;
     if (first < total) issue_tile(first);
   }
@@ -892,14 +913,28 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     if (item >= total) break;
     // the next item is claimed now; its tile is fetched once this item's stem
     // GEMM has read the tile region
-    uint32_t next = 0;
-    if (ltid == kTileIssuer) next = atomicAdd(a.counter, 1u);
+    int64_t next = 0;
+    if (ltid == kTileIssuer) next = claim_item(a.counter, a.lengths, a.B, a.T, total);
     LNET_TRACE(0);
     const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
-    const int n = (int)min((int64_t)kChunk, a.T - t0);
+    const int64_t tb = row_steps(a.lengths, b, a.T);  // this row's steps
+    const int n = (int)min((int64_t)kChunk, tb - t0);
 
-    // 1-2. x tile, then the stem GEMM: five row-shifted views of the tile
+    // 1-2. x tile, then the stem GEMM: five row-shifted views of the tile.  A row
+    // shorter than T (valid length) needs its tile rows past the length zeroed
+    // first (the TMA zero-fills only past T).
+    if (tb < a.T && t0 + kChunk + kHalo > tb) {
+      if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && ltid == 0)
+        atomicOr(a.error, kErrTile);
+      const int keep = (int)(tb - t0 + kHalo);  // tile rows [0, keep) are real steps
+      for (int e = ltid; e < (C / 8) * (kXRows - keep); e += kSlotThreads) {
+        const int kc = e / (kXRows - keep), r = keep + e % (kXRows - keep);
+        *reinterpret_cast<uint4 *>(gs + P::G_X + kc * P::SLAB_X + r * 16) = make_uint4(0, 0, 0, 0);
+      }
+      sm100::fence_proxy_async_smem();
+      slot_sync(bar);
+    }
     if (ltid == 0) {
       if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit)) atomicOr(a.error, kErrTile);
       LNET_TRACE(1);
@@ -918,8 +953,8 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     wait_mma(mbar, phase, a.error, 0, ltid);
     LNET_TRACE(2);
     if (ltid == kTileIssuer) {
-      item_slot[(iter + 1) & 1] = (int64_t)next;
-      if ((int64_t)next < total) issue_tile(next);
+      item_slot[(iter + 1) & 1] = next;
+      if (next < total) issue_tile(next);
     }
     // 3. bias + SiLU + RMSNorm, thread per token: f = h + h tanh(h), h = v / 2, kept
     // as bf16 (the value parked for the residual); xhat = f rs (g is in the drive
@@ -1141,7 +1176,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
                          (int)(ch * kChunk - kHalo), (int)bb);
   };
   if (ltid == kTileIssuer) {
-    const int64_t first = (int64_t)atomicAdd(a.counter, 1u);
+    const int64_t first = claim_item(a.counter, a.lengths, a.B, a.T, total);
     item_slot[0] = first;
     if (first < total) issue_tile(first);
   }
@@ -1149,12 +1184,13 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
-    uint32_t next = 0;
-    if (ltid == kTileIssuer) next = atomicAdd(a.counter, 1u);
+    int64_t next = 0;
+    if (ltid == kTileIssuer) next = claim_item(a.counter, a.lengths, a.B, a.T, total);
     LNET_TRACE(0);
     const int64_t chunk = (uint32_t)item / (uint32_t)a.B, b = item - chunk * a.B;
     const int64_t t0 = chunk * kChunk;
-    const int n = (int)min((int64_t)kChunk, a.T - t0);
+    const int64_t tb = row_steps(a.lengths, b, a.T);  // this row's steps
+    const int n = (int)min((int64_t)kChunk, tb - t0);
 
     // 1. stream tile rows [t0 - 8, t0 + 136), zero outside [0, T), fetched one item ahead
     if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && ltid == 0)
@@ -1166,8 +1202,11 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
       float f[D];
 #pragma unroll
       for (int i = 0; i < D; ++i) f[i] = s_bias[i];
+      // tile rows at or past the row's valid length are padding (zero)
+      const int64_t keep = tb - t0 + kHalo;
 #pragma unroll
       for (int k = 0; k < kTaps; ++k) {
+        if (row + 4 * k >= keep) continue;
         const uint8_t *src = gs + P::G_V + (row + 4 * k) * 16;
         const float *wk = s_w + k * D;
 #pragma unroll
@@ -1212,8 +1251,8 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     LNET_TRACE(3);
     // every thread has read the tile: fetch the next item's
     if (ltid == kTileIssuer) {
-      item_slot[(iter + 1) & 1] = (int64_t)next;
-      if ((int64_t)next < total) issue_tile(next);
+      item_slot[(iter + 1) & 1] = next;
+      if (next < total) issue_tile(next);
     }
     // 3. drive GEMM (paired mode-major)
     if (ltid == 0) {
@@ -1256,7 +1295,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
 __device__ __forceinline__ float finalize_moment(const double *rs, int modes, int j,
                                                  int64_t steps) {
   const int k = j / modes;
-  if (k == 0) return (float)(rs[j] / (double)steps);
+  if (k == 0) return (float)(rs[j] / (double)max(steps, (int64_t)1));  // count clamped at 1
   const int lag = k <= 2 ? 1 : (k <= 4 ? 2 : 4);
   return steps <= lag ? 0.f : (float)(rs[j] / (double)(steps - lag));
 }
@@ -1268,7 +1307,8 @@ __device__ __forceinline__ float finalize_moment(const double *rs, int modes, in
 __global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *__restrict__ wm,
                                       float *__restrict__ rm, float *__restrict__ feats,
                                       int64_t batch, int64_t steps, int modes,
-                                      uint32_t *__restrict__ epoch_word) {
+                                      uint32_t *__restrict__ epoch_word,
+                                      const int64_t *__restrict__ lengths) {
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *epoch_word = *epoch_word + 1u;
   }
@@ -1279,7 +1319,8 @@ __global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *
     const int64_t b = i / (2 * W);
     const int jj = (int)(i - b * 2 * W), blk = jj >= W ? 1 : 0, j = jj - blk * W;
     const double *rs = rowsum + (blk * batch + b) * W;
-    const float v = finalize_moment(rs, modes, j, steps);
+    const int64_t tb = row_steps(lengths, b, steps);
+    const float v = finalize_moment(rs, modes, j, tb);
     (blk == 0 ? wm : rm)[b * W + j] = v;
     float f;
     if (j < modes) {
@@ -1288,8 +1329,8 @@ __global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *
       const int pair = (j - modes) / (2 * modes);
       const int within = (j - modes) - pair * 2 * modes;
       const int base = modes + pair * 2 * modes, mm = within % modes;
-      const float re = finalize_moment(rs, modes, base + mm, steps);
-      const float im = finalize_moment(rs, modes, base + modes + mm, steps);
+      const float re = finalize_moment(rs, modes, base + mm, tb);
+      const float im = finalize_moment(rs, modes, base + modes + mm, tb);
       const float r = sqrtf(fmaxf(re * re + im * im, kFp32Tiny));
       const float scale = log1pf(r) / r;
       f = scale * (within < modes ? re : im);
@@ -1360,7 +1401,8 @@ inline int fused_prepare(const lnet_b200_alphabet_params *p, FusedWorkspace &w, 
 // parameters (lnet_b200_alphabet_prepare) and are not rebuilt.
 template <int C, int D, int M>
 int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
-                        FusedWorkspace &w, float *wm, float *rm, bool prepared, cudaStream_t st) {
+                        FusedWorkspace &w, float *wm, float *rm, bool prepared,
+                        const int64_t *lengths, cudaStream_t st) {
   using WP = WriterPlan<C, D, M>;
   using RP = ReaderPlan<D, M>;
   const int64_t B = r->batch, T = r->steps, nch = fused_chunks(T);
@@ -1402,6 +1444,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.error = counters + 2;
   wa.trace = fused_trace_enabled();
   wa.kernel_id = 0;
+  wa.lengths = lengths;
   LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_writer_kernel<C, D, M>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, WP::BYTES),
                       "cudaFuncSetAttribute(fused_writer_kernel)"));
@@ -1431,14 +1474,16 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   fused_reader_kernel<D, M><<<grid, kSlots * kSlotThreads, RP::BYTES, st>>>(ra);
   LNET_TRY(after_launch("fused_reader_kernel"));
   fused_finalize_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * 14 * M, 256), 8 * sms), 256, 0,
-                          st>>>(w.rowsum, wm, rm, w.feats, B, T, M, w.epoch_word);
+                          st>>>(w.rowsum, wm, rm, w.feats, B, T, M, w.epoch_word, lengths);
   return after_launch("fused_finalize_kernel");
 }
 
+// `lengths` (may be NULL): per-row valid lengths of a right-padded request.
 inline int fused_forward(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
-                         FusedWorkspace &w, float *wm, float *rm, bool prepared, cudaStream_t st) {
+                         FusedWorkspace &w, float *wm, float *rm, bool prepared,
+                         const int64_t *lengths, cudaStream_t st) {
   if (p->raw_input_dim == 48 && p->model_dim == 96 && p->modes == 48)
-    return fused_forward_shape<48, 96, 48>(p, r, w, wm, rm, prepared, st);
+    return fused_forward_shape<48, 96, 48>(p, r, w, wm, rm, prepared, lengths, st);
   return fail(LNET_ERR_UNSUPPORTED, "no fused kernel instance for C=%d D=%d M=%d",
               p->raw_input_dim, p->model_dim, p->modes);
 }

@@ -116,6 +116,11 @@ SIGNATURES = {
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,
          _c_p, _c_p, _c_p, _c_p],
     ),
+    "lnet_b200_alphabet_forward_lengths": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, _i32, _c_p,
+         ctypes.c_size_t, _c_p, _c_p, _c_p, _c_p],
+    ),
     "lnet_b200_alphabet_device_status": (
         ctypes.c_int,
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,

@@ -384,12 +384,31 @@ def _has_param(module: nn.Module, name: str) -> bool:
         return False
 
 
+def right_padded_lengths(valid: Tensor) -> Tensor | None:
+    """int64 [B] valid lengths when ``valid`` [B, T] is a right-padded 0/1 mask (ones,
+    then zeros), else None.  One synchronisation."""
+    t = valid.shape[1]
+    lengths = (valid != 0).sum(dim=1)
+    prefix = torch.arange(t, device=valid.device).unsqueeze(0) < lengths.unsqueeze(1)
+    if not torch.equal(valid, prefix.to(valid.dtype)):
+        return None
+    return lengths.to(torch.int64).contiguous()
+
+
 def alphabet_forward_raw(model: B200Alphabet, x: Tensor, delta, obs, valid, act_dtype: int,
                          want_moments: bool = False):
-    """One ``lnet_b200_alphabet_forward`` call on the current CUDA stream."""
+    """One ``lnet_b200_alphabet_forward`` call on the current CUDA stream.  A
+    right-padded valid mask on a request the fused route serves goes to
+    ``lnet_b200_alphabet_forward_lengths`` (per-row lengths; padded chunks skipped),
+    which computes the same result."""
     lib = _lib.load()
     params, _keep = model._effective(x.device)
-    req = model._request(x, delta, obs, valid, act_dtype)
+    lengths = None
+    if valid is not None and delta is None and obs is None:
+        req0 = model._request(x, None, None, None, act_dtype)
+        if lib.lnet_b200_alphabet_route(ctypes_ref(params), ctypes_ref(req0)) == 0:
+            lengths = right_padded_lengths(valid)
+    req = model._request(x, delta, obs, None if lengths is not None else valid, act_dtype)
     b = x.shape[0]
     m = model.modes
     logits = torch.empty(b, model.head.classifier.out_features, device=x.device,
@@ -400,16 +419,29 @@ def alphabet_forward_raw(model: B200Alphabet, x: Tensor, delta, obs, valid, act_
         rm = torch.empty(b, 7 * m, device=x.device, dtype=torch.float32)
     nbytes = _workspace_bytes(params, req)
     stream = torch.cuda.current_stream(x.device).cuda_stream
-    if getattr(model, "_prepare_spec", None) is not None:
+    prepared = getattr(model, "_prepare_spec", None) is not None
+    if prepared:
         ws, nbytes = _prepared_workspace(model, params, req, nbytes, x.device, stream)
-        fn, name = lib.lnet_b200_alphabet_forward_prepared, "lnet_b200_alphabet_forward_prepared"
     else:
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
-        fn, name = lib.lnet_b200_alphabet_forward, "lnet_b200_alphabet_forward"
+    wm_p = None if wm is None else wm.data_ptr()
+    rm_p = None if rm is None else rm.data_ptr()
     with torch.cuda.device(x.device):
-        st = fn(ctypes_ref(params), ctypes_ref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
-                None if wm is None else wm.data_ptr(), None if rm is None else rm.data_ptr(),
-                stream)
+        if lengths is not None:
+            name = "lnet_b200_alphabet_forward_lengths"
+            st = lib.lnet_b200_alphabet_forward_lengths(
+                ctypes_ref(params), ctypes_ref(req), lengths.data_ptr(), int(prepared),
+                ws.data_ptr(), nbytes, logits.data_ptr(), wm_p, rm_p, stream)
+        elif prepared:
+            name = "lnet_b200_alphabet_forward_prepared"
+            st = lib.lnet_b200_alphabet_forward_prepared(
+                ctypes_ref(params), ctypes_ref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
+                wm_p, rm_p, stream)
+        else:
+            name = "lnet_b200_alphabet_forward"
+            st = lib.lnet_b200_alphabet_forward(
+                ctypes_ref(params), ctypes_ref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
+                wm_p, rm_p, stream)
     _lib.check(st, name)
     return logits, wm, rm
 
