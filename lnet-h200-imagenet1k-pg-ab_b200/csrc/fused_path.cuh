@@ -1343,7 +1343,11 @@ __global__ void fused_finalize_kernel(const double *__restrict__ rowsum, float *
 struct FusedShapeKey {
   int C, D, M;
 };
-constexpr FusedShapeKey kFusedShapes[] = {{48, 96, 48}};
+// Compiled (C, D, M) instances: the config-4 shape and smaller ones whose three
+// slots fit the 227 KB of shared memory (D <= 96: the reader's 144-row stream
+// tile plus its xhat slab per slot).
+constexpr FusedShapeKey kFusedShapes[] = {
+    {48, 96, 48}, {32, 96, 48}, {64, 64, 32}, {32, 64, 32}, {16, 32, 16}};
 
 inline bool fused_supported(const lnet_b200_alphabet_params *p,
                             const lnet_b200_alphabet_request *r) {
@@ -1482,8 +1486,15 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 inline int fused_forward(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
                          FusedWorkspace &w, float *wm, float *rm, bool prepared,
                          const int64_t *lengths, cudaStream_t st) {
-  if (p->raw_input_dim == 48 && p->model_dim == 96 && p->modes == 48)
-    return fused_forward_shape<48, 96, 48>(p, r, w, wm, rm, prepared, lengths, st);
+#define LNET_FUSED_CASE(CC, DD, MM)                                                  \
+  if (p->raw_input_dim == CC && p->model_dim == DD && p->modes == MM)               \
+    return fused_forward_shape<CC, DD, MM>(p, r, w, wm, rm, prepared, lengths, st);
+  LNET_FUSED_CASE(48, 96, 48)
+  LNET_FUSED_CASE(32, 96, 48)
+  LNET_FUSED_CASE(64, 64, 32)
+  LNET_FUSED_CASE(32, 64, 32)
+  LNET_FUSED_CASE(16, 32, 16)
+#undef LNET_FUSED_CASE
   return fail(LNET_ERR_UNSUPPORTED, "no fused kernel instance for C=%d D=%d M=%d",
               p->raw_input_dim, p->model_dim, p->modes);
 }

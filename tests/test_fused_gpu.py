@@ -108,3 +108,62 @@ def test_fused_route_long_sequence_carries(cuda_device):
     assert rel_err(wm.cpu().numpy(), st["writer_moments"]) <= 2e-2
     assert rel_err(rm.cpu().numpy(), st["reader_moments"]) <= 2e-2
     assert rel_err(logits.cpu().numpy(), st["logits"]) <= 2e-2
+
+
+def shape_params(c, d, m, k, seed, real_poles):
+    g = torch.Generator().manual_seed(seed)
+
+    def rn(*shape, scale=1.0):
+        return torch.randn(*shape, generator=g) * scale
+
+    p = {
+        "stem.projection.weight": torch.linalg.qr(rn(d, c))[0] if d >= c
+        else torch.linalg.qr(rn(c, d))[0].T,
+        "stem.local.weight": rn(d, 1, 5, scale=1 / math.sqrt(5)),
+        "stem.local.bias": rn(d, scale=0.1),
+        "second_local.weight": rn(d, 1, 5, scale=1 / math.sqrt(5)),
+        "second_local.bias": rn(d, scale=0.1),
+        "forward_block.direct_scale": rn(d, scale=0.3),
+        "forward_block.layer_scale": rn(d, scale=0.3),
+        "head.classifier.weight": rn(k, 14 * m, scale=1 / math.sqrt(14 * m)),
+        "head.classifier.bias": rn(k, scale=0.1),
+    }
+    for blk in ("forward_block", "backward_block"):
+        if real_poles:
+            lam = torch.exp(torch.empty(m).uniform_(math.log(1.1e-3), 0.0, generator=g))
+            p[f"{blk}.raw_decay"] = torch.logit((lam - 1e-3) / (2 - 1e-3))
+            p[f"{blk}.raw_frequency"] = torch.zeros(m)
+        else:
+            p[f"{blk}.raw_decay"] = rn(m, scale=2.0)
+            p[f"{blk}.raw_frequency"] = rn(m, scale=0.8)
+        p[f"{blk}.norm.weight"] = 1 + rn(d, scale=0.1)
+        p[f"{blk}.frame.weight"] = torch.linalg.qr(rn(d, 2 * m))[0]
+    return {key: v.to(torch.bfloat16).float() for key, v in p.items()}
+
+
+@pytest.mark.parametrize("c,d,m", [(32, 96, 48), (64, 64, 32), (32, 64, 32), (16, 32, 16)])
+@pytest.mark.parametrize("real", [True, False])
+def test_other_compiled_shapes(c, d, m, real, cuda_device):
+    """The other compiled fused instances against the oracle and the general route."""
+    k = 11
+    params = shape_params(c, d, m, k, seed=c + d + m, real_poles=real)
+    model = B200Alphabet(AlphabetConfig(c, d, m, k), k).eval()
+    model.load_effective_parameters(params)
+    model = model.to(cuda_device)
+    g = torch.Generator().manual_seed(d)
+    x = torch.randn(3, 300, c, generator=g).to(torch.bfloat16)
+    xd = x.to(cuda_device)
+    assert route_of(model, xd) == 0, "the fused route must serve this shape"
+    with torch.no_grad():
+        logits, wm, rm = model(xd, return_moments=True)
+        _lib.set_route(_lib.ROUTE_GENERAL)
+        try:
+            general = model(xd)
+        finally:
+            _lib.set_route(_lib.ROUTE_AUTO)
+    pn = {key: v.numpy() for key, v in params.items()}
+    st = A.alphabet_forward(x.float().numpy(), pn, dtype=np.float64, return_stages=True)
+    assert rel_err(logits.cpu().numpy(), st["logits"]) <= 2e-2
+    assert rel_err(wm.cpu().numpy(), st["writer_moments"]) <= 2e-2
+    assert rel_err(rm.cpu().numpy(), st["reader_moments"]) <= 2e-2
+    assert rel_err(logits.cpu().numpy(), general.cpu().numpy()) <= 2e-2
