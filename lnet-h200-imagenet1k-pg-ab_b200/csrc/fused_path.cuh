@@ -228,23 +228,47 @@ __global__ void fused_prepare_kernel(lnet_b200_alphabet_params p, FusedWorkspace
               blk == 0 ? p.writer_raw_frequency[m] : p.reader_raw_frequency[m], damping,
               frequency);
     Zoh z = zoh_eval(damping, frequency, 1.0);
-    // Powers of the fp32 coefficient the scan multiplies by, accumulated in
-    // double so that carries match step-by-step propagation.
+    // Powers of the fp32 coefficient the scan multiplies by, in double (rounded
+    // once), by squaring: a^60 = a^32 a^16 a^8 a^4, then a^61..a^64 and
+    // a^124 = a^64 a^60, a^125..a^128 -- a chain of 18 products instead of 128.
     const double ar = (double)z.a_re, ai = (double)z.a_im;
-    double pr = 1.0, pi = 0.0;
     float *k = w.consts + blk * kConsts * M;
-    for (int step = 1; step <= kChunk; ++step) {
+    double sq_r[7], sq_i[7];  // a^(2^e), e = 0..6
+    sq_r[0] = ar;
+    sq_i[0] = ai;
+    for (int e = 1; e < 7; ++e)
+      cmul_d(sq_r[e - 1], sq_i[e - 1], sq_r[e - 1], sq_i[e - 1], sq_r[e], sq_i[e]);
+    double pr = sq_r[5], pi = sq_i[5];  // a^32
+    for (int e = 4; e >= 2; --e) {      // * a^16 * a^8 * a^4 = a^60
+      double nr, ni;
+      cmul_d(pr, pi, sq_r[e], sq_i[e], nr, ni);
+      pr = nr;
+      pi = ni;
+    }
+    const double p60r = pr, p60i = pi;
+    auto store = [&](int slot, double vr, double vi) {
+      k[slot * M + m] = (float)vr;
+      k[(slot + 1) * M + m] = (float)vi;
+    };
+    for (int step = 61; step <= kHalf; ++step) {  // a^61 .. a^64
       double nr, ni;
       cmul_d(pr, pi, ar, ai, nr, ni);
       pr = nr;
       pi = ni;
-      int slot = -1;
-      if (step >= kChunk - 3) slot = KC_AL + 2 * (kChunk - step);
-      if (step >= kHalf - 3 && step <= kHalf) slot = KC_AH + 2 * (kHalf - step);
-      if (slot >= 0) {
-        k[slot * M + m] = (float)pr;
-        k[(slot + 1) * M + m] = (float)pi;
-      }
+      store(KC_AH + 2 * (kHalf - step), pr, pi);
+    }
+    {
+      double nr, ni;
+      cmul_d(pr, pi, p60r, p60i, nr, ni);  // a^124
+      pr = nr;
+      pi = ni;
+    }
+    for (int step = kChunk - 3; step <= kChunk; ++step) {  // a^125 .. a^128
+      double nr, ni;
+      cmul_d(pr, pi, ar, ai, nr, ni);
+      pr = nr;
+      pi = ni;
+      store(KC_AL + 2 * (kChunk - step), pr, pi);
     }
     k[m] = z.a_re;
     k[M + m] = z.a_im;
