@@ -30,11 +30,11 @@
 //        acc[t, d] = sum_k sum_c x[t + 4k - 8, c] * (w[d, k] P[d, c]),
 //      the five taps are five row-shifted descriptors over the same tile;
 //   3. +bias, SiLU, RMSNorm, thread per token (no cross-thread reduction):
-//      xhat -> bf16 slab; the bf16 stem output waits in the output rows (L2);
+//      xhat -> bf16 slab; the stem output f waits in registers (packed bf16);
 //   4. drive GEMM (paired mode-major layout above; gamma folded into the frame);
 //   5. scan: the thread of lane l < 16 scans steps [0, 64) of its mode, the
-//      thread of lane l + 16 steps [64, 128); each loads its own TMEM lane and
-//      swaps halves with its partner by shuffles.  The partner pair combines its
+//      thread of lane l + 16 steps [64, 128); two half-split TMEM loads give
+//      each thread both parts of its mode over its half.  The partner pair combines its
 //      halves by shuffles, the upper-half thread publishes the chunk aggregate
 //      and resolves the carry by a decoupled look-back over tagged records; a
 //      second pass from the true carries accumulates E, C1, C2, C4 and writes
@@ -340,6 +340,36 @@ __device__ __forceinline__ void copy_floats(float *dst, const float *src, int n)
   for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
+// Drive frame rows per K slab in shared memory.  With fewer than 64 modes the
+// frame leaves lane quarter 3 empty; slot s then starts its A operand at row
+// 32 s of the frame followed by a copy of its first 96 rows, so in slot s lane
+// quarter j holds mode block (j + s) % 4.  A warp's TMEM quarter is also its
+// SM sub-partition (warp % 4), so the idle quarter of each slot falls on a
+// different sub-partition instead of all three on the last one.
+template <int M>
+struct DriveRotation {
+  static constexpr bool ON = M < 64;
+  static constexpr int ROWS = ON ? 128 + 96 : 128;
+  static constexpr int SLAB = ROWS * 16;
+  // mode block held by lane quarter `warp` of slot `slot`
+  static __device__ __forceinline__ int block(int warp, int slot) {
+    return ON ? (warp + slot) & 3 : warp;
+  }
+  static __device__ __forceinline__ uint32_t offset(int slot) {
+    return ON ? (uint32_t)(slot * 32 * 16) : 0u;
+  }
+};
+// The drive frame ([D / 8] slabs of 128 rows x 16 B) into the rotated layout.
+template <int M>
+__device__ __forceinline__ void copy_drive(uint8_t *dst, const void *src, int slabs) {
+  using R = DriveRotation<M>;
+  const uint4 *s = reinterpret_cast<const uint4 *>(src);
+  for (int i = threadIdx.x; i < slabs * (R::ROWS); i += blockDim.x) {
+    const int kc = i / R::ROWS, r = i - kc * R::ROWS;
+    reinterpret_cast<uint4 *>(dst + kc * R::SLAB)[r] = __ldg(s + kc * 128 + (r & 127));
+  }
+}
+
 // Eight bf16 (one 16-byte vector) -> float, exactly: a bf16 is the upper half
 // of the float with the same value, so the widening is a shift or a mask on
 // the integer pipe instead of a conversion instruction.
@@ -471,11 +501,11 @@ struct LookbackPrefetch {
 // Called by every thread of a slot; lane l >= 16 threads of live warps (the
 // publishers) load the predecessor's inclusive record.
 template <int M>
-__device__ __forceinline__ void lookback_prefetch(int warp, int lane,
+__device__ __forceinline__ void lookback_prefetch(int qblk, int lane,
                                                   const unsigned long long *rec, int64_t row,
                                                   int64_t chunk, int64_t n_chunks,
                                                   LookbackPrefetch &p) {
-  const int m = 16 * warp + (lane & 15);
+  const int m = 16 * qblk + (lane & 15);
 #pragma unroll
   for (int k = 0; k < 8; ++k) p.w[k] = 0ull;
   if (m < M && lane >= 16 && chunk > 0) {
@@ -590,49 +620,37 @@ __device__ __forceinline__ void lookback(int m, int64_t row, int64_t chunk, int6
   }
 }
 
-// Steps [c0, c0 + 32) of the thread's half as (x, y) in its own frame: every
-// lane of the warp loads the same TMEM columns (tcgen05.ld takes one address
-// per warp) -- its own component at steps c0.. (the lower half) and 64 + c0..
-// (the upper half) -- keeps its own half as x and sends the other half to its
-// partner, whose component over this thread's half arrives as y.
-__device__ __forceinline__ void load_pair(uint32_t lane_addr, int c0, int upper, float *x,
-                                          float *y) {
-  sm100::tmem_ld32(lane_addr + (uint32_t)c0, x);
-  sm100::tmem_ld32(lane_addr + (uint32_t)(kHalf + c0), y);
+// Steps [c0, c0 + 32) of the thread's half as (x, y) = (re, im): two half-split
+// loads of the warp's quarter (`quarter_addr` = its lane 0), the first over
+// lanes 0..15 (real parts), the second over lanes 16..31 (imaginary parts).
+// Threads 0..15 receive columns c0.. (steps [0, 64)), threads 16..31 columns
+// 64 + c0.. (steps [64, 128)) of the same mode.
+__device__ __forceinline__ void load_pair(uint32_t quarter_addr, int c0, float *x, float *y) {
+  sm100::tmem_ld32_split<kHalf>(quarter_addr + (uint32_t)c0, x);
+  sm100::tmem_ld32_split<kHalf>(quarter_addr + (16u << 16) + (uint32_t)c0, y);
   sm100::tmem_ld_wait();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float lo = x[i], hi = y[i];
-    x[i] = upper ? hi : lo;
-    y[i] = shfl16(upper ? lo : hi);
-  }
 }
 
 // One item's scan, executed by a warp of a slot (all 32 lanes together; warps
 // whose quarter holds no modes return at once).  Lane l < 16 ("lower") owns
-// steps [0, 64) of mode m = 16 warp + (l & 15), lane l + 16 ("upper") steps
-// [64, 128).  Each thread keeps its complex values in its OWN FRAME: the lower
-// thread in (re, im), the upper thread in (im, re), i.e. z -> i conj(z).  In
-// that frame the recurrence is the same code with the pole conjugated, because
-// i conj(a z) = conj(a) (i conj(z)); and a lag product s_t conj(s_{t-l}) comes
-// out conjugated, so the upper thread negates its imaginary moment parts.
-// Every thread reads only its own TMEM lane: the component it owns over both
-// halves, and the half it does not scan goes to its partner by a shuffle
-// (load_pair).
+// steps [0, 64) of mode m = 16 qblk + (l & 15), lane l + 16 ("upper") steps
+// [64, 128).  The warp's TMEM quarter holds the real parts of its 16 modes in
+// lanes 0..15 and the imaginary parts in lanes 16..31; half-split loads give
+// each thread both parts over its own half of the steps.
 //
 // WRITE_STATES: the true states are written (bf16, M-major) into `s_slab` as the
 // synthesis A operand: element (t, j) at (j / 8) * SLAB + (t / 8) * 128 +
 // (j % 8) * 16 + (t % 8) * 2, j = m (re) or M + m (im).
 template <int M, bool WRITE_STATES, bool REAL>
-__device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr, int n,
+__device__ __forceinline__ void slot_scan(int qblk, int lane, uint32_t lane_addr, int n,
                                           int64_t row, int64_t chunk, int64_t n_chunks,
                                           const float *K, unsigned long long *rec, uint32_t tag,
                                           uint32_t rtag, uint32_t spin, uint32_t *error, int kid,
                                           int trace, uint8_t *s_slab, int slab_bytes,
                                           double *rowsum, const LookbackPrefetch &pre) {
   const int upper = lane >> 4;
-  const int m = 16 * warp + (lane & 15);
-  if (16 * warp >= M) return;  // warp-uniform
+  const int m = 16 * qblk + (lane & 15);
+  if (16 * qblk >= M) return;  // warp-uniform
   unsigned long long t_scan = trace ? clock64() : 0;
   auto mark = [&](int slot) {
     if (trace && threadIdx.x == 0) {
@@ -641,20 +659,19 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
       t_scan = now;
     }
   };
-  const float sg = upper ? -1.f : 1.f;  // conjugation of constants in the upper frame
   const int s0 = kHalf * upper;
   const int len = max(0, min(kHalf, n - s0));
   // REAL: every pole of the block is real (a_im = 0), so the two components of a
   // mode evolve independently and the recurrence is one FMA per component
-  const float ar = K[m], ai = REAL ? 0.f : sg * K[M + m];
+  const float ar = K[m], ai = REAL ? 0.f : K[M + m];
 
-  // ---- pass 1: local scan of the thread's 64 steps from zero (own frame)
+  // ---- pass 1: local scan of the thread's 64 steps from zero
   float sx = 0.f, sy = 0.f;
   float lx[4] = {0, 0, 0, 0}, ly[4] = {0, 0, 0, 0};  // l[0] = last state
 #pragma unroll 1
   for (int c0 = 0; c0 < kHalf; c0 += 32) {
     float x[32], y[32];
-    load_pair(lane_addr, c0, upper, x, y);
+    load_pair(lane_addr, c0, x, y);
     if (c0 + 32 <= len) {
       const bool last = c0 + 32 == kHalf;
 #pragma unroll
@@ -685,8 +702,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
     }
   }
   mark(10);
-  // ---- combine the halves.  The lower half's last four local states, in the
-  // normal frame (lower thread: (x, y) = (re, im)), reach the upper thread.
+  // ---- combine the halves.  The lower half's last four local states reach the
+  // upper thread.
   float or_[4], oi_[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -702,8 +719,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
     float g_r[4], g_i[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      g_r[k] = ly[k];  // own frame (im, re) -> normal
-      g_i[k] = lx[k];
+      g_r[k] = lx[k];
+      g_i[k] = ly[k];
       cmac(K[(KC_AH + 2 * k) * M + m], K[(KC_AH + 2 * k + 1) * M + m], c1r, c1i, g_r[k],
            g_i[k]);
     }
@@ -738,11 +755,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
            hi[k]);
     }
   }
-  // to the own frame: lower (re, im) = (x, y); upper (x, y) = (im, re)
-  float h1x = upper ? hi[0] : hr[0], h1y = upper ? hr[0] : hi[0];
-  float h2x = upper ? hi[1] : hr[1], h2y = upper ? hr[1] : hi[1];
-  float h3x = upper ? hi[2] : hr[2], h3y = upper ? hr[2] : hi[2];
-  float h4x = upper ? hi[3] : hr[3], h4y = upper ? hr[3] : hi[3];
+  const float h1x = hr[0], h1y = hi[0], h2x = hr[1], h2y = hi[1];
+  const float h3x = hr[2], h3y = hi[2], h4x = hr[3], h4y = hi[3];
   sx = h1x;
   sy = h1y;
   // Moment sums: |s|^2 and Re(s conj(h)) = sx hx + sy hy add terms of one sign
@@ -773,15 +787,14 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
     H2 = H1;
     H1 = S;
   };
-  // state slab addresses: the own frame's x goes to component j = m (lower: re)
-  // or M + m (upper: im), y to the other one
-  const int jx = upper ? M + m : m, jy = upper ? m : M + m;
+  // state slab addresses: the real part is component j = m, the imaginary M + m
+  const int jx = m, jy = M + m;
   uint8_t *px = s_slab + (jx / 8) * slab_bytes + (jx % 8) * 16;
   uint8_t *py = s_slab + (jy / 8) * slab_bytes + (jy % 8) * 16;
 #pragma unroll 1
   for (int c0 = 0; c0 < kHalf; c0 += 32) {
     float x[32], y[32];
-    load_pair(lane_addr, c0, upper, x, y);
+    load_pair(lane_addr, c0, x, y);
     if (c0 + 32 <= len) {
 #pragma unroll
       for (int g8 = 0; g8 < 4; ++g8) {
@@ -815,9 +828,8 @@ __device__ __forceinline__ void slot_scan(int warp, int lane, uint32_t lane_addr
     }
   }
   mark(12);
-  // ---- moments: the upper thread's lag products are conjugated in its frame
-  float mom[7] = {E2.x + E2.y, C1r.x + C1r.y, sg * c1i, C2r.x + C2r.y, sg * c2i,
-                  C4r.x + C4r.y, sg * c4i};
+  // ---- moments of the two halves, summed over the thread pair
+  float mom[7] = {E2.x + E2.y, C1r.x + C1r.y, c1i, C2r.x + C2r.y, c2i, C4r.x + C4r.y, c4i};
 #pragma unroll
   for (int k = 0; k < 7; ++k) mom[k] += shfl16(mom[k]);
   // lower thread adds E, C1r, C1i, C2r; upper C2i, C4r, C4i (row sums [7][M])
@@ -832,7 +844,7 @@ struct WriterPlan {
   static_assert(C % 16 == 0 && D % 32 == 0 && D <= kSlotCols && M % 16 == 0 && M <= 64,
                 "shape");
   // shared by the slots
-  static constexpr int SLAB_AD = 128 * 16;  // drive A rows: paired mode-major
+  static constexpr int SLAB_AD = DriveRotation<M>::SLAB;  // drive A rows: paired mode-major
   static constexpr int AD_BYTES = (D / 8) * SLAB_AD;
   static constexpr int SLAB_Q = D * 16;
   static constexpr int Q_BYTES = kTaps * (C / 8) * SLAB_Q;
@@ -869,6 +881,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
   const int tid = threadIdx.x;
   const int slot = tid / kSlotThreads, ltid = tid % kSlotThreads;
   const int warp = ltid >> 5, lane = ltid & 31;
+  const int qblk = DriveRotation<M>::block(warp, slot);  // mode block of this warp's quarter
   uint8_t *gs = smem + P::SHARED_END + slot * P::G_BYTES;
   uint64_t *mbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC);
   uint64_t *tbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC + 8);  // x tile arrival
@@ -894,7 +907,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     sm100::tmem_relinquish();
   }
   trace_begin(a.trace);
-  copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
+  copy_drive<M>(smem + P::OFF_AD, a.drive, D / 8);
   copy_smem(smem + P::OFF_Q, a.q, P::Q_BYTES);
   copy_smem(smem + P::OFF_WS, a.syn, P::WS_BYTES);
   for (int i = tid; i < D; i += blockDim.x) {
@@ -1030,21 +1043,21 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     if (ltid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, kChunk);
-      issue_gemm(tslot, s_base + P::OFF_AD, P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16,
+      issue_gemm(tslot, s_base + P::OFF_AD + DriveRotation<M>::offset(slot), P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
     }
     LookbackPrefetch pre;
-    lookback_prefetch<M>(warp, lane, a.rec, b, chunk, a.n_chunks, pre);
+    lookback_prefetch<M>(qblk, lane, a.rec, b, chunk, a.n_chunks, pre);
     wait_mma(mbar, phase, a.error, 1, ltid);
     LNET_TRACE(4);
     // 5. scan + look-back + moments; states -> synthesis A operand (aliases xhat)
     if (real_poles)
-      slot_scan<M, true, true>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+      slot_scan<M, true, true>(qblk, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
                                rtag, a.spin_limit, a.error, a.kernel_id, a.trace, gs + P::G_XS,
                                P::SLAB_S, a.rowsum + b * 7 * M, pre);
     else
-      slot_scan<M, true, false>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+      slot_scan<M, true, false>(qblk, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
                                 rtag, a.spin_limit, a.error, a.kernel_id, a.trace, gs + P::G_XS,
                                 P::SLAB_S, a.rowsum + b * 7 * M, pre);
     sm100::fence_proxy_async_smem();
@@ -1116,7 +1129,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
 template <int D, int M>
 struct ReaderPlan {
   static_assert(D % 32 == 0 && D <= kSlotCols && M % 16 == 0 && M <= 64, "shape");
-  static constexpr int SLAB_AD = 128 * 16;
+  static constexpr int SLAB_AD = DriveRotation<M>::SLAB;
   static constexpr int AD_BYTES = (D / 8) * SLAB_AD;
   static constexpr int OFF_AD = 0;
   static constexpr int OFF_PAR = OFF_AD + AD_BYTES;  // float [6][D]: w(5), bias
@@ -1144,6 +1157,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
   const int tid = threadIdx.x;
   const int slot = tid / kSlotThreads, ltid = tid % kSlotThreads;
   const int warp = ltid >> 5, lane = ltid & 31;
+  const int qblk = DriveRotation<M>::block(warp, slot);  // mode block of this warp's quarter
   uint8_t *gs = smem + P::SHARED_END + slot * P::G_BYTES;
   uint64_t *mbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC);
   uint64_t *tbar = reinterpret_cast<uint64_t *>(gs + P::G_MISC + 8);  // tile arrival
@@ -1166,7 +1180,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     sm100::tmem_relinquish();
   }
   trace_begin(a.trace);
-  copy_smem(smem + P::OFF_AD, a.drive, P::AD_BYTES);
+  copy_drive<M>(smem + P::OFF_AD, a.drive, D / 8);
   // conv weights transposed to [tap][channel] and the bias, halved: the conv then
   // yields h = v / 2 of SiLU's tanh form directly (exact scaling)
   for (int i = tid; i < kTaps * D; i += blockDim.x) {
@@ -1282,21 +1296,21 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     if (ltid == 0) {
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, kChunk);
-      issue_gemm(tslot, s_base + P::OFF_AD, P::SLAB_AD, g_base + P::G_XH, P::SLAB_XH, D / 16,
+      issue_gemm(tslot, s_base + P::OFF_AD + DriveRotation<M>::offset(slot), P::SLAB_AD, g_base + P::G_XH, P::SLAB_XH, D / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
     }
     LookbackPrefetch pre;
-    lookback_prefetch<M>(warp, lane, a.rec, b, chunk, a.n_chunks, pre);
+    lookback_prefetch<M>(qblk, lane, a.rec, b, chunk, a.n_chunks, pre);
     wait_mma(mbar, phase, a.error, 3, ltid);
     LNET_TRACE(4);
     // 4. scan + look-back + moments
     if (real_poles)
-      slot_scan<M, false, true>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+      slot_scan<M, false, true>(qblk, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
                                 rtag, a.spin_limit, a.error, a.kernel_id, a.trace, nullptr, 0,
                                 a.rowsum + b * 7 * M, pre);
     else
-      slot_scan<M, false, false>(warp, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
+      slot_scan<M, false, false>(qblk, lane, lane_addr, n, b, chunk, a.n_chunks, s_k, a.rec, tag,
                                  rtag, a.spin_limit, a.error, a.kernel_id, a.trace, nullptr, 0,
                                  a.rowsum + b * 7 * M, pre);
     sm100::tc_fence_before();
