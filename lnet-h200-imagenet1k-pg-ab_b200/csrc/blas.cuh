@@ -1,9 +1,14 @@
 // GEMMs of the general route: the stem projection, the drive projection and the
 // synthesis of every request the fused route does not take.  gemm_rows runs
-// them on this library's tcgen05 row GEMM (rowgemm.cuh: bf16 x bf16 for bf16
-// operands, split-bf16 x3 -- fp32-level accuracy -- for fp32 operands) whenever
-// the shape fits it (n, k <= 128), and on cuBLAS otherwise (fp32 requests in
-// CUBLAS_COMPUTE_32F, bf16 requests on TF32 or bf16 tensor cores).
+// them on this library's tcgen05 row GEMMs (rowgemm.cuh: bf16 x bf16 for bf16
+// operands, split-bf16 x3 -- fp32-level accuracy -- for fp32 operands):
+//   * the warp-specialised TMA pipeline (rowgemm_ws_kernel) when the operands
+//     are TMA-addressable, n <= 256 and B fits in shared memory -- every
+//     BASELINE configuration;
+//   * the one-tile-at-a-time kernel (rowgemm_kernel) for other n, k <= 128
+//     (unaligned or odd-pitch operands);
+//   * cuBLAS otherwise (fp32 requests in CUBLAS_COMPUTE_32F, bf16 requests on
+//     TF32 or bf16 tensor cores), or when lnet_b200_set_gemm_backend(1) asks.
 #pragma once
 
 #include <cublas_v2.h>
@@ -74,6 +79,9 @@ inline int gemm_rows(cudaStream_t st, const void *A, cudaDataType ta, int64_t ld
                      cudaDataType tb, int64_t ldbn, int64_t ldbk, float *C, int64_t ldc,
                      int64_t rows, int n, int k, bool tf32, const char *what,
                      float beta = 0.f, uint32_t *status = nullptr) {
+  if (rowgemm_enabled() && rows > 0 && (beta == 0.f || beta == 1.f) &&
+      rowgemm_ws_supported(A, ta, tb, lda, n, k, C, ldc))
+    return rowgemm_ws(st, A, ta, lda, Bm, ldbn, ldbk, C, ldc, rows, n, k, beta, status, what);
   if (rowgemm_enabled() && rows > 0 && rowgemm_supported(ta, tb, n, k))
     return rowgemm(st, A, ta, lda, Bm, ldbn, ldbk, C, ldc, rows, n, k, beta, status, what);
   return gemm_rows_t(st, A, ta, lda, Bm, tb, ldbn, ldbk, C, CUDA_R_32F, ldc, rows, n, k, tf32,

@@ -58,6 +58,7 @@
 #include "generic_kernels.cuh"
 #include "head_gemm.cuh"
 #include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace lnet {
 
@@ -1407,20 +1408,10 @@ int take_lookback_injection();
 int fused_trace_enabled();
 
 // Tiled 3-D tensor map of a [B][T][W] bf16 tensor with an 8 x 144 x 1 box
-// (one K slab of a tile), zero fill outside the tensor.  The driver entry
-// point is resolved once through the runtime.
+// (one K slab of a tile), zero fill outside the tensor.
 inline int encode_tile_map(CUtensorMap *map, const void *base, int64_t B, int64_t T, int W) {
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *fn = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  });
-  if (!encode) return fail(LNET_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  PFN_cuTensorMapEncodeTiled_v12000 encode;
+  LNET_TRY(tensor_map_encoder(&encode));
   const cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[2] = {(cuuint64_t)W * 2, (cuuint64_t)T * W * 2};
   const cuuint32_t box[3] = {8, (cuuint32_t)kXRows, 1};

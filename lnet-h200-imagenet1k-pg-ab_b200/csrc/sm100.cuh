@@ -58,6 +58,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   return false;
 }
 
+// One plain arrival.
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier `id` over `threads` threads (a multiple of 32).
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // One arrival that also announces `bytes` of asynchronous transfers.
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
@@ -75,6 +85,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
       "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 2-D tiled tensor load (no multicast) into this CTA's shared memory; completes
+// its bytes on `bar`.  c0 (innermost) times the element size must be a multiple
+// of 16 bytes; coordinates past the tensor read zeros.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint64_t *bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -101,6 +123,20 @@ __device__ __forceinline__ void bulk_commit() {
 // Waits until this thread's committed bulk stores have finished READING shared memory.
 __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// 2-D tiled tensor store / reduce-add (f32) of a shared-memory box to global,
+// tracked by the issuing thread's bulk groups.  c0 (innermost) times the
+// element size is a multiple of 16 bytes and c0, c1 are not negative.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(tmap), "r"(c0), "r"(c1), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const void *tmap, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];"
+      ::"l"(tmap), "r"(c0), "r"(c1), "r"(src)
+      : "memory");
 }
 // Waits until this thread's committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() {
@@ -148,6 +184,20 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
   // base offset 0, lbo mode 0, layout type 0 (no swizzle)
+  return d;
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, K-major: atoms of 8 rows x
+// 128 bytes (64 bf16 along K) stacked every 1024 bytes along M/N, as a TMA load
+// with CU_TENSOR_MAP_SWIZZLE_128B writes them (1024-byte aligned).  A K=16 step
+// inside the atom starts 32 bytes further.
+__device__ __forceinline__ uint64_t make_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;            // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;            // layout type: 128-byte swizzle
   return d;
 }
 

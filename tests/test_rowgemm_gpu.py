@@ -4,7 +4,8 @@ and with the row GEMM (default) must agree -- fp32 requests to 1e-5 (split-bf16 
 is fp32-level), bf16 requests to 1e-3 (bf16 x bf16 products are exact, TF32
 rounds the fp32 operands) -- and each must stay within the parity gates against
 the float64 oracle.  Shapes: BASELINE configs 2, 3 (with all metadata) and 5 at
-reduced batch and length, plus a ragged shape (k, n not multiples of 16)."""
+reduced batch and length (config 5: n = k = 256 on the pipelined kernel), plus
+ragged shapes (k, n not multiples of 16; output pitches not multiples of 4)."""
 
 from __future__ import annotations
 
@@ -30,6 +31,12 @@ CASES = {
     "cfg5": dict(bench.CONFIGS["5"], B=2, T=700),
     "ragged": dict(workload="ragged", B=3, T=99, C=13, D=40, M=12, K=7, dtype="fp32",
                    images=False),
+    # output pitches D = 42 and 2M = 26 are not multiples of 4 floats: the
+    # non-pipelined row GEMM (plain stores) serves them
+    "ragged_pitch": dict(workload="ragged_pitch", B=2, T=131, C=11, D=42, M=13, K=5,
+                         dtype="fp32", images=False),
+    "ragged_bf16": dict(workload="ragged_bf16", B=2, T=140, C=24, D=56, M=20, K=5,
+                        dtype="bf16", images=False),
 }
 
 
