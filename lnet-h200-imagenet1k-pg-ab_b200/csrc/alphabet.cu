@@ -135,6 +135,7 @@ struct Plan {
   float *stream = nullptr;    // [BT, D]   writer stream
   float *modal = nullptr;     // [BT, D]
   float *ts = nullptr;        // [BT]
+  float *step_a = nullptr;    // [BT, 2M] per-step transitions (physical time only)
   float *carries = nullptr;   // [B, nchunk, kRecFloats, M] scan records
   float *partial = nullptr;   // moment partials
   float *wfold = nullptr;     // [D, 2M] drive frame with the ZOH gains folded in
@@ -162,6 +163,7 @@ static void plan_generic(Arena &ar, Plan &pl, const lnet_b200_alphabet_params *p
   pl.stream = ar.take<float>((size_t)bt * D);
   pl.modal = ar.take<float>((size_t)bt * D);
   pl.ts = ar.take<float>((size_t)bt);
+  if (r->time_delta) pl.step_a = ar.take<float>((size_t)bt * 2 * M);
   pl.carries = ar.take<float>((size_t)r->batch * n_scan * kRecFloats * M);
   pl.partial = ar.take<float>((size_t)r->batch * n_mom * (8 * M + 5));
   pl.wfold = ar.take<float>((size_t)D * 2 * M);
@@ -218,6 +220,30 @@ static int stem_projection(const lnet_b200_alphabet_params *p, const lnet_b200_a
   return LNET_OK;
 }
 
+// Physical-time depthwise conv of fp32 rows: the tiled kernel where the rows
+// allow it (4 | dim, 16-byte aligned, at most kPtMaxTaps taps), else the
+// per-token kernel.
+static int physical_conv(const float *in, const float *w, const float *bias, const float *in_mask,
+                         const float *ts, const float *valid, float *out, int64_t B, int64_t T,
+                         int D, int taps, int dilation, cudaStream_t st, const char *what) {
+  auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (D % 4 == 0 && al(in) && al(out) && taps <= kPtMaxTaps && T <= INT32_MAX) {
+    const dim3 grid((unsigned)cdiv(T, kPtTile), (unsigned)B);
+    const size_t sm = (size_t)(taps + 1) * D * sizeof(float);
+    dwconv_physical_tile_kernel<<<grid, kPtThreads, sm, st>>>(in, w, bias, in_mask, ts, valid, out,
+                                                             T, D, taps, dilation);
+    return after_launch(what);
+  }
+  dwconv_physical_kernel<float><<<(unsigned)(B * T), token_block(D), 0, st>>>(
+      in, w, bias, in_mask, ts, valid, out, T, D, taps, dilation);
+  return after_launch(what);
+}
+
+static int timestamps(const float *dt, float *ts, int64_t B, int64_t T, cudaStream_t st) {
+  timestamps_scan_kernel<<<(unsigned)B, kTsThreads, 0, st>>>(dt, ts, T);
+  return after_launch("timestamps_scan_kernel");
+}
+
 template <typename TX>
 static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
                         Plan &pl, float *first_local, cudaStream_t st) {
@@ -225,12 +251,10 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   const int D = p->model_dim;
   LNET_TRY(stem_projection<TX>(p, r, pl, st));
   if (r->time_delta) {
-    timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
-    LNET_TRY(after_launch("timestamps_kernel"));
-    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
-        pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, pl.ts, r->valid_mask,
-        first_local, T, D, p->conv_kernel, p->conv_dilation);
-    return after_launch("dwconv_physical_kernel(stem)");
+    LNET_TRY(timestamps(r->time_delta, pl.ts, B, T, st));
+    return physical_conv(pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, pl.ts,
+                         r->valid_mask, first_local, B, T, D, p->conv_kernel, p->conv_dilation,
+                         st, "dwconv_physical(stem)");
   }
   return depthwise_conv(pl.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, r->valid_mask,
                         first_local, B, T, D, p->conv_kernel, p->conv_dilation, st,
@@ -274,14 +298,14 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
                        bt, 2 * M, D, tf32, "gemm(drive)"));
     drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(pl.drive, raw_decay, raw_freq,
                                                             r->time_delta, g_re, g_im, event_mask,
-                                                            obs_channels, bt, M);
+                                                            obs_channels, bt, M, pl.step_a);
     LNET_TRY(after_launch("drive_kernel"));
   }
   const int64_t n_scan = cdiv(T, kScanChunk);
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   dim3 gs((unsigned)n_scan, (unsigned)B);
   scan_local_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
-                                            r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
+                                            r->time_delta, pl.step_a, pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_local_kernel"));
   scan_carry_kernel<<<carry_grid(B, M), 32 * kCarryParts, 0, st>>>(pl.carries, B, M, n_scan,
                                                                 nullptr);
@@ -300,7 +324,7 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
     return after_launch("moments_finalize_kernel");
   }
   scan_apply_kernel<<<gs, threads, 0, st>>>(pl.drive, raw_decay, raw_freq, a_re, a_im,
-                                            r->time_delta, pl.carries, T, M, kScanChunk, n_scan);
+                                            r->time_delta, pl.step_a, pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_apply_kernel"));
   const int64_t n_mom = cdiv(T, kMomChunk);
   dim3 gm((unsigned)n_mom, (unsigned)B);
@@ -425,14 +449,10 @@ static int reader_generic(const lnet_b200_alphabet_params *p, const lnet_b200_al
   const int D = p->model_dim, M = p->modes;
   if (r->time_delta) {
     if (!pl.ts) return fail(LNET_ERR_INVALID_ARGUMENT, "timestamps missing");
-    if (!ts_ready) {
-      timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, pl.ts, B, T);
-      LNET_TRY(after_launch("timestamps_kernel"));
-    }
-    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
-        first_stream, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, pl.ts,
-        r->valid_mask, pl.proj, T, D, p->conv_kernel, p->conv_dilation);
-    LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
+    if (!ts_ready) LNET_TRY(timestamps(r->time_delta, pl.ts, B, T, st));
+    LNET_TRY(physical_conv(first_stream, p->reader_conv_weight, p->reader_conv_bias,
+                           r->valid_mask, pl.ts, r->valid_mask, pl.proj, B, T, D, p->conv_kernel,
+                           p->conv_dilation, st, "dwconv_physical(reader)"));
   } else {
     LNET_TRY(depthwise_conv(first_stream, p->reader_conv_weight, p->reader_conv_bias,
                             r->valid_mask, r->valid_mask, pl.proj, B, T, D, p->conv_kernel,
@@ -671,9 +691,7 @@ extern "C" int lnet_b200_writer(const lnet_b200_alphabet_params *params,
   auto st = (cudaStream_t)stream;
   begin_entry(st);
   if (req->time_delta) {
-    timestamps_kernel<<<(unsigned)cdiv(req->batch, 4), 128, 0, st>>>(req->time_delta, pl.ts,
-                                                                       req->batch, req->steps);
-    LNET_TRY(after_launch("timestamps_kernel"));
+    LNET_TRY(timestamps(req->time_delta, pl.ts, req->batch, req->steps, st));
   }
   return writer_generic(params, req, first_local, pl, stream_out, moments, st);
 }
@@ -788,12 +806,12 @@ extern "C" int lnet_b200_block_scan(const lnet_b200_alphabet_params *params,
   const int threads = std::min(128, (int)cdiv(M, 32) * 32);
   dim3 gs((unsigned)n_scan, (unsigned)B);
   scan_local_kernel<<<gs, threads, 0, st>>>(u_states, bp.decay, bp.freq, a_re, a_im, nullptr,
-                                            pl.carries, T, M, kScanChunk, n_scan);
+                                            nullptr, pl.carries, T, M, kScanChunk, n_scan);
   LNET_TRY(after_launch("scan_local_kernel"));
   scan_carry_kernel<<<carry_grid(B, M), 32 * kCarryParts, 0, st>>>(pl.carries, B, M, n_scan, init);
   LNET_TRY(after_launch("scan_carry_kernel"));
   scan_apply_kernel<<<gs, threads, 0, st>>>(u_states, bp.decay, bp.freq, a_re, a_im, nullptr,
-                                            pl.carries, T, M, kScanChunk, n_scan);
+                                            nullptr, pl.carries, T, M, kScanChunk, n_scan);
   return after_launch("scan_apply_kernel");
 }
 

@@ -363,30 +363,6 @@ __global__ void scale_rows_kernel(const float *__restrict__ frame, const float *
     out[i] = scale[i / n] * frame[i];
 }
 
-// ---------------------------------------------------------------- timestamps
-// ts[b, t] = fp32(sum_{s<=t} double(dt[b, s]))  (CPU torch cumsum accumulates in double)
-// One warp per row: the lanes load 32 steps at once (coalesced), lane 0 adds
-// them in step order (the sequential double sum, bit for bit).
-__global__ void timestamps_kernel(const float *__restrict__ dt, float *__restrict__ ts,
-                                  int64_t batch, int64_t steps) {
-  const int64_t b = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (b >= batch) return;
-  double acc = 0.0;
-  for (int64_t t0 = 0; t0 < steps; t0 += 32) {
-    const int64_t t = t0 + lane;
-    const float v = t < steps ? dt[b * steps + t] : 0.f;
-    const int n = (int)min((int64_t)32, steps - t0);
-    for (int k = 0; k < n; ++k) {
-      const float vk = __shfl_sync(0xffffffffu, v, k);
-      if (lane == 0) {
-        acc += (double)vk;
-        ts[b * steps + t0 + k] = (float)acc;
-      }
-    }
-  }
-}
-
 // ---------------------------------------------------------------- physical-time depthwise conv
 // Restates _physical_time_depthwise_conv (src/lnet/alphabet_backbone.py:80-160).
 // One block per (token); threads over channels.  The sample positions are
@@ -449,6 +425,141 @@ __global__ void dwconv_physical_kernel(const TI *__restrict__ in, const float *_
   }
 }
 
+// Tiled form of the same conv for fp32 rows with 4 | dim and 16-byte aligned
+// rows: one block per (row, 32-token tile).  The sample positions, weights and
+// support of every (token, tap) of the tile are resolved once into shared
+// memory (binary search over the row's timestamps); then threads take
+// (token, 4-channel quad) pairs with 16-byte loads of the two interpolation
+// rows.  The per-element arithmetic is the per-token kernel's, in the same order.
+constexpr int kPtTile = 32, kPtMaxTaps = 8, kPtThreads = 256;
+__global__ void __launch_bounds__(kPtThreads) dwconv_physical_tile_kernel(
+    const float *__restrict__ in, const float *__restrict__ w, const float *__restrict__ bias,
+    const float *__restrict__ in_mask, const float *__restrict__ ts,
+    const float *__restrict__ valid, float *__restrict__ out, int64_t steps, int dim, int taps,
+    int dilation) {
+  __shared__ int s_lo[kPtTile][kPtMaxTaps], s_hi[kPtTile][kPtMaxTaps];
+  __shared__ float s_w[kPtTile][kPtMaxTaps], s_mlo[kPtTile][kPtMaxTaps], s_mhi[kPtTile][kPtMaxTaps];
+  __shared__ int s_on[kPtTile][kPtMaxTaps];
+  extern __shared__ float s_wt[];  // [taps][dim] weights, then [dim] bias
+  const int64_t b = blockIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.x * kPtTile;
+  const int n_tok = (int)min((int64_t)kPtTile, steps - t0);
+  const float *row = ts + b * steps;
+  const float first = row[0], last = row[steps - 1];
+  for (int i = threadIdx.x; i < taps * dim; i += blockDim.x) {
+    const int k = i / dim, d = i - k * dim;
+    s_wt[i] = w[d * taps + k];
+  }
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) s_wt[taps * dim + i] = bias[i];
+  for (int i = threadIdx.x; i < n_tok * taps; i += blockDim.x) {
+    const int j = i / taps, k = i - j * taps;
+    const int64_t t = t0 + j;
+    const float offset = (float)(k * dilation - dilation * (taps - 1) / 2);
+    const float q = row[t] + offset;
+    const int64_t up_u = lower_bound_f(row, steps, q);
+    const int64_t up = up_u < steps - 1 ? up_u : steps - 1;
+    int64_t lo = up_u - 1;
+    lo = lo < 0 ? 0 : (lo > steps - 1 ? steps - 1 : lo);
+    const float lt = row[lo], ut = row[up];
+    const float dur = ut - lt;
+    float interp = dur > 0.f ? (q - lt) / fmaxf(dur, kFp32Tiny) : 0.f;
+    interp = fminf(fmaxf(interp, 0.f), 1.f);
+    bool on = (q >= first) && (q <= last);
+    if (valid) {
+      const float lv = valid[b * steps + lo], uv = valid[b * steps + up];
+      const float eps8 = 8.0f * kFp32Eps;
+      const float support = interp <= eps8 ? lv : (interp >= 1.0f - eps8 ? uv : lv * uv);
+      on = on && (support > 0.f);
+    }
+    s_lo[j][k] = (int)lo;
+    s_hi[j][k] = (int)up;
+    s_w[j][k] = interp;
+    s_on[j][k] = on;
+    s_mlo[j][k] = in_mask ? in_mask[b * steps + lo] : 1.f;
+    s_mhi[j][k] = in_mask ? in_mask[b * steps + up] : 1.f;
+  }
+  __syncthreads();
+  const int quads = dim / 4;
+  const float *in_row = in + b * steps * dim;
+  for (int i = threadIdx.x; i < n_tok * quads; i += blockDim.x) {
+    const int j = i / quads, qd = i - j * quads, d0 = 4 * qd;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < taps; ++k) {
+      const float4 a4 = *reinterpret_cast<const float4 *>(in_row + (int64_t)s_lo[j][k] * dim + d0);
+      const float4 c4 = *reinterpret_cast<const float4 *>(in_row + (int64_t)s_hi[j][k] * dim + d0);
+      const float av[4] = {a4.x, a4.y, a4.z, a4.w}, cv[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float wk = s_w[j][k], ml = s_mlo[j][k], mh = s_mhi[j][k];
+      const bool on = s_on[j][k] != 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a = av[e], c = cv[e];
+        if (in_mask) {
+          a *= ml;
+          c *= mh;
+        }
+        const float v = on ? lerp_torch(a, c, wk) : 0.f;
+        acc[e] = fmaf(v, s_wt[k * dim + d0 + e], acc[e]);
+      }
+    }
+    const int64_t tok = b * steps + t0 + j;
+    const float vt = valid ? valid[tok] : 1.f;
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      y[e] = silu_f(acc[e] + s_wt[taps * dim + d0 + e]);
+      if (valid) y[e] *= vt;
+    }
+    *reinterpret_cast<float4 *>(out + tok * dim + d0) = make_float4(y[0], y[1], y[2], y[3]);
+  }
+}
+
+// ts[b, t] = fp32(sum_{s<=t} double(dt[b, s])) as a block scan in double, one
+// block per row: each thread sums eight consecutive steps, the block scans the
+// thread sums, and a running carry joins the 2048-step segments.  (A parallel
+// cumsum, as a GPU cumsum is; for step sizes whose partial sums are exact in
+// double -- every clipped Exponential(1) grid -- it equals the sequential sum.)
+constexpr int kTsThreads = 256;
+__global__ void __launch_bounds__(kTsThreads) timestamps_scan_kernel(const float *__restrict__ dt,
+                                                                    float *__restrict__ ts,
+                                                                    int64_t steps) {
+  __shared__ double s_warp[kTsThreads / 32];
+  const int64_t b = blockIdx.x;
+  const float *src = dt + b * steps;
+  float *dst = ts + b * steps;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  double carry = 0.0;
+  for (int64_t seg = 0; seg < steps; seg += 8 * kTsThreads) {
+    const int64_t t0 = seg + 8 * threadIdx.x;
+    double v[8], sum = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[e] = t0 + e < steps ? (double)src[t0 + e] : 0.0;
+      sum += v[e];
+    }
+    double incl = sum;  // inclusive scan of the thread sums: warp, then across warps
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_warp[wid] = incl;
+    __syncthreads();
+    double before = 0.0, total = 0.0;
+    for (int q = 0; q < kTsThreads / 32; ++q) {
+      if (q < wid) before += s_warp[q];
+      total += s_warp[q];
+    }
+    double run = carry + before + (incl - sum);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      run += v[e];
+      if (t0 + e < steps) dst[t0 + e] = (float)run;
+    }
+    carry += total;
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------- RMSNorm
 // One warp per token: out = x * rsqrt(mean(x^2) + eps) * g
 __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ g,
@@ -468,40 +579,46 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 // ---------------------------------------------------------------- drive (gamma (x) e * mask)
 // e[tok, 0:M] / e[tok, M:2M] -> u in place; gamma from the per-mode table or per step.
 // Without dt the gains are the per-mode table g_tab_re/im (zoh_kernel); with dt
-// they are evaluated per step.
+// they are evaluated per step, and `step_a` (when given) receives the step's
+// transition a = exp(p dt) as [tok][re M | im M] for the scans (the same
+// double evaluation, rounded once, that the scans would otherwise repeat).
 __global__ void drive_kernel(float *__restrict__ e, const float *__restrict__ raw_decay,
                              const float *__restrict__ raw_freq, const float *__restrict__ dt,
                              const float *__restrict__ g_tab_re, const float *__restrict__ g_tab_im,
                              const float *__restrict__ event_mask, int obs_channels,
-                             int64_t tokens, int modes) {
-  for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
-   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    float gr, gi;
-    if (dt) {
-      double damping, frequency;
-      mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
-      const Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
-      gr = z.g_re;
-      gi = z.g_im;
-    } else {
-      gr = g_tab_re[m];
-      gi = g_tab_im[m];
+                             int64_t tokens, int modes, float *__restrict__ step_a) {
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+    double damping = 0.0, frequency = 0.0;  // the mode's pole (per mode, not per step)
+    if (dt) mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+    for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+      float gr, gi;
+      float *row = e + tok * 2 * modes;
+      if (dt) {
+        const Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
+        gr = z.g_re;
+        gi = z.g_im;
+        if (step_a) {
+          step_a[tok * 2 * modes + m] = z.a_re;
+          step_a[tok * 2 * modes + modes + m] = z.a_im;
+        }
+      } else {
+        gr = g_tab_re[m];
+        gi = g_tab_im[m];
+      }
+      float er = row[m], ei = row[modes + m];
+      float ur = gr * er - gi * ei;
+      float ui = gr * ei + gi * er;
+      if (event_mask) {
+        // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
+        const float *om = event_mask + tok * obs_channels;
+        float mx = om[0];
+        for (int c = 1; c < obs_channels; ++c) mx = fmaxf(mx, om[c]);
+        ur *= mx;
+        ui *= mx;
+      }
+      row[m] = ur;
+      row[modes + m] = ui;
     }
-    float *row = e + tok * 2 * modes;
-    float er = row[m], ei = row[modes + m];
-    float ur = gr * er - gi * ei;
-    float ui = gr * ei + gi * er;
-    if (event_mask) {
-      // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
-      const float *om = event_mask + tok * obs_channels;
-      float mx = om[0];
-      for (int c = 1; c < obs_channels; ++c) mx = fmaxf(mx, om[c]);
-      ur *= mx;
-      ui *= mx;
-    }
-    row[m] = ur;
-    row[modes + m] = ui;
-   }
   }
 }
 
@@ -510,11 +627,15 @@ __global__ void drive_kernel(float *__restrict__ e, const float *__restrict__ ra
 //   local: chunk end state from zero + chunk transition product,
 //   carry: sequential combine over chunks,
 //   apply: rescan each chunk from its true carry-in (states overwrite u).
+// `step_a`: the per-step transitions written by drive_kernel (or NULL: evaluate).
 __device__ __forceinline__ void step_coeff(const float *raw_decay, const float *raw_freq,
                                            const float *a_tab_re, const float *a_tab_im,
-                                           const float *dt, int64_t tok, int m, float &ar,
-                                           float &ai) {
-  if (dt) {
+                                           const float *dt, const float *step_a, int modes,
+                                           int64_t tok, int m, float &ar, float &ai) {
+  if (dt && step_a) {
+    ar = step_a[tok * 2 * modes + m];
+    ai = step_a[tok * 2 * modes + modes + m];
+  } else if (dt) {
     double damping, frequency;
     mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
     Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
@@ -535,8 +656,9 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
                                   const float *__restrict__ raw_freq,
                                   const float *__restrict__ a_re_tab,
                                   const float *__restrict__ a_im_tab,
-                                  const float *__restrict__ dt, float *__restrict__ carries,
-                                  int64_t steps, int modes, int chunk, int64_t n_chunks) {
+                                  const float *__restrict__ dt, const float *__restrict__ step_a,
+                                  float *__restrict__ carries, int64_t steps, int modes, int chunk,
+                                  int64_t n_chunks) {
   const int64_t c = blockIdx.x, b = blockIdx.y;
   const int64_t t0 = c * chunk;
   const int64_t t1 = min(steps, t0 + chunk);
@@ -547,7 +669,7 @@ __global__ void scan_local_kernel(const float *__restrict__ u, const float *__re
     auto step = [&](int64_t t) {
       int64_t tok = b * steps + t;
       float ar, ai;
-      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, tok, m, ar, ai);
+      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, step_a, modes, tok, m, ar, ai);
       const float *row = u + tok * 2 * modes;
       float nr = ar * sr - ai * si + row[m];
       float ni = ai * sr + ar * si + row[modes + m];
@@ -641,7 +763,7 @@ __global__ void scan_apply_kernel(float *__restrict__ u, const float *__restrict
                                   const float *__restrict__ raw_freq,
                                   const float *__restrict__ a_re_tab,
                                   const float *__restrict__ a_im_tab,
-                                  const float *__restrict__ dt,
+                                  const float *__restrict__ dt, const float *__restrict__ step_a,
                                   const float *__restrict__ carries, int64_t steps, int modes,
                                   int chunk, int64_t n_chunks) {
   const int64_t c = blockIdx.x, b = blockIdx.y;
@@ -653,7 +775,7 @@ __global__ void scan_apply_kernel(float *__restrict__ u, const float *__restrict
     for (int64_t t = t0; t < t1; ++t) {
       int64_t tok = b * steps + t;
       float ar, ai;
-      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, tok, m, ar, ai);
+      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, step_a, modes, tok, m, ar, ai);
       float *row = u + tok * 2 * modes;
       float nr = ar * sr - ai * si + row[m];
       float ni = ai * sr + ar * si + row[modes + m];

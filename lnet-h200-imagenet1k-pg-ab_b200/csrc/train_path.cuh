@@ -114,12 +114,10 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
   LNET_TRY(gemm_rows(st, tp.x32, CUDA_R_32F, C, p->stem_projection, CUDA_R_32F, C, 1, tp.proj, D,
                      bt, D, C, tf32, "gemm(stem)"));
   if (r->time_delta) {  // physical-time convs and moments
-    timestamps_kernel<<<(unsigned)cdiv(B, 4), 128, 0, st>>>(r->time_delta, tp.ts, B, T);
-    LNET_TRY(after_launch("timestamps_kernel"));
-    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
-        tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, tp.ts, r->valid_mask, tp.y1, T,
-        D, p->conv_kernel, p->conv_dilation);
-    LNET_TRY(after_launch("dwconv_physical_kernel(stem)"));
+    LNET_TRY(timestamps(r->time_delta, tp.ts, B, T, st));
+    LNET_TRY(physical_conv(tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr, tp.ts,
+                           r->valid_mask, tp.y1, B, T, D, p->conv_kernel, p->conv_dilation, st,
+                           "dwconv_physical(stem)"));
   } else {
     LNET_TRY(depthwise_conv(tp.proj, p->stem_conv_weight, p->stem_conv_bias, nullptr,
                             r->valid_mask, tp.y1, B, T, D, p->conv_kernel, p->conv_dilation, st,
@@ -136,10 +134,9 @@ static int train_forward_impl(const lnet_b200_alphabet_params *p,
       tp.y1, tp.xh1, tp.modal, p->writer_direct_scale, p->writer_layer_scale, tp.v, bt, D);
   LNET_TRY(after_launch("residual_kernel"));
   if (r->time_delta) {
-    dwconv_physical_kernel<float><<<(unsigned)bt, token_block(D), 0, st>>>(
-        tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask, tp.ts, r->valid_mask,
-        tp.y2, T, D, p->conv_kernel, p->conv_dilation);
-    LNET_TRY(after_launch("dwconv_physical_kernel(reader)"));
+    LNET_TRY(physical_conv(tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
+                           tp.ts, r->valid_mask, tp.y2, B, T, D, p->conv_kernel, p->conv_dilation,
+                           st, "dwconv_physical(reader)"));
   } else {
     LNET_TRY(depthwise_conv(tp.v, p->reader_conv_weight, p->reader_conv_bias, r->valid_mask,
                             r->valid_mask, tp.y2, B, T, D, p->conv_kernel, p->conv_dilation, st,
