@@ -328,7 +328,7 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   LNET_TRY(after_launch("scan_apply_kernel"));
   const int64_t n_mom = cdiv(T, kMomChunk);
   dim3 gm((unsigned)n_mom, (unsigned)B);
-  pt_moments_partial_kernel<<<gm, threads, 0, st>>>(pl.drive, pl.ts, r->time_delta,
+  pt_moments_partial_kernel<<<gm, 256, 0, st>>>(pl.drive, pl.ts, r->time_delta,
                                                     r->valid_mask, pl.partial, T, M, n_mom);
   LNET_TRY(after_launch("pt_moments_partial_kernel"));
   pt_moments_finalize_kernel<<<dim3((unsigned)cdiv(M, 32), (unsigned)B), 32 * kPtFinalParts, 0,

@@ -1046,6 +1046,7 @@ __global__ void fold_gain_kernel(const float *__restrict__ frame, const float *_
 // [8 * M mode sums (E_duration, E_event, C1r, C1i, C2r, C2i, C4r, C4i)] + [5 scalars:
 //  sum(dt*valid), sum(valid), pair weights of lags 1, 2, 4].
 constexpr int kPtChunk = 64;
+constexpr int kPtRedFloats = 8 * 256;  // step-group partial sums (256 threads)
 __global__ void pt_moments_partial_kernel(const float *__restrict__ s,
                                           const float *__restrict__ ts,
                                           const float *__restrict__ dt,
@@ -1094,9 +1095,17 @@ __global__ void pt_moments_partial_kernel(const float *__restrict__ s,
   }
   __syncthreads();
   float *out = partial + (b * n_chunks + c) * rec;
-  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
+  // threads = (step group g, mode m): with modes <= blockDim / 2 the chunk's steps
+  // are split over `groups` interleaved groups whose sums meet in shared memory
+  __shared__ float s_red[kPtRedFloats];
+  const int groups = modes * 2 <= (int)blockDim.x && 8 * (int)blockDim.x <= kPtRedFloats
+                         ? (int)blockDim.x / modes : 1;
+  const int g = groups > 1 ? (int)threadIdx.x / modes : 0;
+  const int m0 = groups > 1 ? (int)threadIdx.x - g * modes : (int)threadIdx.x;
+  const int m_step = groups > 1 ? modes : (int)blockDim.x;
+  for (int m = m0; m < modes && g < groups; m += m_step) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int i = 0; i < n; ++i) {
+    for (int i = g; i < n; i += groups) {
       int64_t tok = b * steps + t0 + i;
       const float *cur = s + tok * 2 * modes;
       float cr = cur[m], ci = cur[modes + m];
@@ -1114,8 +1123,21 @@ __global__ void pt_moments_partial_kernel(const float *__restrict__ s,
         acc[3 + 2 * l] += (ci * pr - cr * pi) * w;
       }
     }
+    if (groups > 1) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) out[j * modes + m] = acc[j];
+      for (int j = 0; j < 8; ++j) s_red[(g * 8 + j) * modes + m] = acc[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j * modes + m] = acc[j];
+    }
+  }
+  if (groups > 1) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < 8 * modes; e += blockDim.x) {
+      float v = 0.f;
+      for (int q = 0; q < groups; ++q) v += s_red[q * 8 * modes + e];
+      out[e] = v;
+    }
   }
   if (threadIdx.x < 5) {
     float acc = 0.f;
