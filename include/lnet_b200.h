@@ -112,10 +112,11 @@ int lnet_b200_alphabet_forward(const lnet_b200_alphabet_params *params,
 int lnet_b200_debug_inject_lookback_miss(void);
 
 /* GEMM backend of the general route (process-wide): 0 = this library's tcgen05
- * row GEMM wherever the shape fits it (n, k <= 128; bf16 x bf16 for bf16
- * operands, split-bf16 x3 for fp32 operands), cuBLAS otherwise (default);
- * 1 = cuBLAS for every GEMM (used by the tests to compare the two).  No
- * reference counterpart: replaces the reference's torch matmuls on this path. */
+ * row GEMMs wherever the shape fits them (bf16 x bf16 for bf16 operands,
+ * split-bf16 x3 for fp32 operands; n <= 256 with TMA-addressable operands, or
+ * n, k <= 128 otherwise), cuBLAS for any other shape (default); 1 = cuBLAS for
+ * every GEMM (used by the tests to compare the two).  No reference
+ * counterpart: replaces the reference's torch matmuls on this path. */
 int lnet_b200_set_gemm_backend(int backend);
 
 /* Route selection for lnet_b200_alphabet_forward (process-wide):
