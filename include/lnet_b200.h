@@ -169,8 +169,9 @@ int lnet_b200_alphabet_forward_lengths(const lnet_b200_alphabet_params *params,
 
 /* Device-side status of the last lnet_b200_alphabet_forward in `workspace`
  * for this request's route (synchronises the device).  Every wait inside the
- * kernels is bounded; a wait that gave up sets a bit: 1 << 0..3 MMA completion
- * (writer stem, writer drive, writer synthesis, reader drive), 1 << 4 / 1 << 5
+ * kernels is bounded; a wait that gave up sets a bit: 1 << 0..3 and 1 << 9 MMA
+ * completion (writer stem, writer drive, writer synthesis, reader drive; reader
+ * conv), 1 << 4 / 1 << 5
  * look-back (writer / reader), 1 << 6 / 1 << 7 tile loads (writer / reader) on
  * the fused route; 1 << 8 a bulk input copy of the general route's conv +
  * RMSNorm kernel.  Nonzero means the results of that call are invalid, and
