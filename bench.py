@@ -703,6 +703,54 @@ def run_b200(args, cfg):
                         "(lnet_b200.graph.CudaGraphForward, includes its input copy); `value` "
                         "rebuilds the operands in every step"}
 
+    # ---- image configuration: the forward from uint8 images already in HBM, with the
+    # normalise + patchify inside the fused writer (lnet_b200_alphabet_forward_images)
+    # and, beside it, the two-kernel form (lnet_b200_patchify_images, then the forward
+    # on the bf16 tokens)
+    images_res = None
+    if cfg["images"] and b_loc > 0:
+        from lnet_b200.images import IMAGENET_MEAN, IMAGENET_STD
+
+        img_dev = make_images(cfg, dev)[lo:hi].contiguous()
+        hh, ww = int(img_dev.shape[1]), int(img_dev.shape[2])
+        mean_c = (ctypes.c_float * 3)(*IMAGENET_MEAN)
+        std_c = (ctypes.c_float * 3)(*IMAGENET_STD)
+        n_i = ctypes.c_size_t(0)
+        _lib.check(lib.lnet_b200_alphabet_images_workspace_size(
+            ctypes.byref(params), b_loc, hh, ww, ctypes.byref(n_i)),
+            "lnet_b200_alphabet_images_workspace_size")
+        ws_i = torch.zeros(max(int(n_i.value), 1), dtype=torch.uint8, device=dev)
+        logits_i = torch.empty(b_loc, cfg["K"], device=dev, dtype=torch.float32)
+
+        def fwd_images():
+            _lib.check(lib.lnet_b200_alphabet_forward_images(
+                ctypes.byref(params), img_dev.data_ptr(), b_loc, hh, ww, mean_c, std_c, 0,
+                ws_i.data_ptr(), int(n_i.value), logits_i.data_ptr(), None, None,
+                stream.cuda_stream), "lnet_b200_alphabet_forward_images")
+
+        tok = torch.empty(b_loc, T, cfg["C"], dtype=torch.bfloat16, device=dev)
+        fwd_tok = c_abi_forward(tok)
+
+        def fwd_two():
+            _lib.check(lib.lnet_b200_patchify_images(img_dev.data_ptr(), b_loc, hh, ww, 4,
+                                                     mean_c, std_c, tok.data_ptr(),
+                                                     _lib.LNET_BF16, stream.cuda_stream),
+                       "lnet_b200_patchify_images")
+            fwd_tok()
+
+        for fn_w in (fwd_images, fwd_two):
+            for _ in range(max(args.warmup, 3)):
+                fn_w()
+        img_ms = _time_steps(fwd_images, args.steps, stream, flush, world, dist, dev)
+        two_ms = _time_steps(fwd_two, args.steps, stream, flush, world, dist, dev)
+        images_res = {"value": tokens_all / (img_ms / 1e3), "unit": UNIT,
+                      "ms_per_step": img_ms / args.steps,
+                      "patchify_then_forward_ms_per_step": two_ms / args.steps,
+                      "note": "uint8 images resident in HBM; `value`: patchify inside the "
+                              "fused writer (lnet_b200_alphabet_forward_images); beside it "
+                              "the patchify kernel then the forward on bf16 tokens"}
+        del img_dev, ws_i, tok
+
     # ---- weak scaling: every rank its own full B-row batch (reported beside `value`)
     weak = None
     if world > 1 or args.weak:
@@ -727,7 +775,8 @@ def run_b200(args, cfg):
     if args.skip_e2e:
         if rank == 0:
             print(json.dumps({"value": value, "ms_per_step": total_ms / args.steps,
-                              "prepared": prepared, "weak_scaling": weak,
+                              "prepared": prepared, "images": images_res,
+                              "weak_scaling": weak,
                               "kernels": _lib_kernels(prof), "trace_cycles_per_item": trace}),
                   flush=True)
         if world > 1:
@@ -813,7 +862,8 @@ def run_b200(args, cfg):
                        "modes": cfg["M"], "classes": cfg["K"], "parallelism": f"batch{world}",
                        "l2": "256 MiB flush between steps, outside the per-step event pair"},
             "e2e": {"value": e2e_value, "unit": UNIT,
-                    "input": "uint8 images [B,224,224,3] (GPU normalise + patchify)"
+                    "input": "uint8 images [B,224,224,3] (normalise + patchify inside the "
+                             "fused writer)"
                              if cfg["images"] else "tokens",
                     "overlap": "copy of step k+1 overlaps the forward of step k",
                     "module": "B200Alphabet after prepare_for_inference_",
@@ -822,6 +872,7 @@ def run_b200(args, cfg):
                     "h2d_gbs_per_rank_min": float(h2d_gbs.item()),
                     "d2h_bytes_per_step": B * cfg["K"] * 4},
             "prepared": prepared,
+            "images": images_res,
             "weak_scaling": weak,
             "multi_gpu_check": check,
             "gpu_launches": launches[0],

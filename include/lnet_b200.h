@@ -226,6 +226,29 @@ int lnet_b200_head(const lnet_b200_alphabet_params *params, int64_t batch,
                    const float *writer_moments, const float *reader_moments, float *logits,
                    lnet_stream_t stream);
 
+/* The image configuration's whole forward from uint8 images [B, H, W, 3]
+ * (device, 16-byte aligned; H, W multiples of 4): the normalise + 4x4 patchify
+ * of lnet_b200_patchify_images (same arithmetic, so the same bf16 tokens) runs
+ * inside the fused writer, which builds each 144-token x tile from the image
+ * bytes instead of loading a token tensor, then the forward of
+ * lnet_b200_alphabet_forward (prepared = 0) or ..._forward_prepared (1) on
+ * those tokens.  No token tensor is written or read.  Replaces the harness
+ * transform (scripts/train_alphabet2d_imagenet100.py:292-310), its patchify
+ * reshape and Alphabet.forward (src/lnet/alphabet.py:350-416).  `mean`, `std`
+ * are HOST arrays of 3 floats.  Needs the fused route: raw_input_dim 48 and a
+ * compiled (C, D, M) shape, else LNET_ERR_UNSUPPORTED (then patchify and call
+ * lnet_b200_alphabet_forward).  Workspace size from
+ * lnet_b200_alphabet_images_workspace_size. */
+int lnet_b200_alphabet_images_workspace_size(const lnet_b200_alphabet_params *params,
+                                             int64_t batch, int32_t height, int32_t width,
+                                             size_t *bytes);
+int lnet_b200_alphabet_forward_images(const lnet_b200_alphabet_params *params,
+                                      const uint8_t *images, int64_t batch, int32_t height,
+                                      int32_t width, const float *mean, const float *std,
+                                      int32_t prepared, void *workspace, size_t workspace_bytes,
+                                      float *logits, float *writer_moments,
+                                      float *reader_moments, lnet_stream_t stream);
+
 /* Input pipeline of the image configuration: uint8 images [B, H, W, 3]
  * (device) -> tokens [B, (H/p)(W/p), 3 p^2] (`tokens_dtype` LNET_BF16 or
  * LNET_F32), per element v = (u / 255 - mean[ch]) / std[ch] in fp32 (IEEE

@@ -569,7 +569,8 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
                                  const lnet_b200_alphabet_request *req, void *workspace,
                                  size_t workspace_bytes, float *logits, float *writer_moments,
                                  float *reader_moments, bool prepared, lnet_stream_t stream,
-                                 const int64_t *lengths = nullptr) {
+                                 const int64_t *lengths = nullptr,
+                                 const ImageInput *img = nullptr) {
   reset_launches();
   LNET_TRY(check_params(params));
   LNET_TRY(check_request(params, req));
@@ -586,10 +587,11 @@ static int alphabet_forward_impl(const lnet_b200_alphabet_params *params,
     LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, true));
     float *wm = writer_moments ? writer_moments : pl.fused.moments;
     float *rm = reader_moments ? reader_moments : pl.fused.moments + B * 7 * M;
-    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, prepared, lengths, st));
+    LNET_TRY(fused_forward(params, req, pl.fused, wm, rm, prepared, lengths, st, img));
     return head_gemm(pl.fused.feats, B, 14 * M, params->head_weight, params->head_bias, logits,
                      params->output_dim, pl.fused.head_partial, st, pl.fused.flags + 2);
   }
+  if (img) return fail(LNET_ERR_UNSUPPORTED, "image input is served by the fused route only");
   LNET_TRY(plan_all(params, req, workspace, workspace_bytes, pl, false));
   float *wm = writer_moments ? writer_moments : pl.moments;
   float *rm = reader_moments ? reader_moments : pl.moments + B * 7 * M;
@@ -638,6 +640,60 @@ extern "C" int lnet_b200_alphabet_forward_lengths(const lnet_b200_alphabet_param
                 "mask to lnet_b200_alphabet_forward");
   return alphabet_forward_impl(params, req, workspace, workspace_bytes, logits, writer_moments,
                                reader_moments, prepared != 0, stream, lengths);
+}
+
+// The request an image forward stands for: tokens [B, (H/4)(W/4), 48] in bf16.
+static lnet_b200_alphabet_request image_request(const uint8_t *images, int64_t batch,
+                                                int32_t height, int32_t width) {
+  lnet_b200_alphabet_request r{};
+  r.batch = batch;
+  r.steps = (int64_t)(height / 4) * (width / 4);
+  r.x_dtype = LNET_BF16;
+  r.act_dtype = LNET_BF16;
+  r.x = images;
+  return r;
+}
+
+extern "C" int lnet_b200_alphabet_images_workspace_size(const lnet_b200_alphabet_params *params,
+                                                        int64_t batch, int32_t height,
+                                                        int32_t width, size_t *bytes) {
+  if (batch < 0 || height < 4 || width < 4 || height % 4 != 0 || width % 4 != 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "images_workspace_size: invalid image shape");
+  // any aligned non-null pointer stands for the images
+  const lnet_b200_alphabet_request rq =
+      image_request(reinterpret_cast<const uint8_t *>(uintptr_t(256)), batch, height, width);
+  return lnet_b200_alphabet_workspace_size(params, &rq, bytes);
+}
+
+extern "C" int lnet_b200_alphabet_forward_images(
+    const lnet_b200_alphabet_params *params, const uint8_t *images, int64_t batch,
+    int32_t height, int32_t width, const float *mean, const float *std, int32_t prepared,
+    void *workspace, size_t workspace_bytes, float *logits, float *writer_moments,
+    float *reader_moments, lnet_stream_t stream) {
+  reset_launches();
+  LNET_TRY(check_params(params));
+  if (batch < 0 || height < 4 || width < 4 || height % 4 != 0 || width % 4 != 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT,
+                "forward_images: images must be [B, H, W, 3] with H, W positive multiples of 4 "
+                "(got B=%lld, H=%d, W=%d)", (long long)batch, height, width);
+  if (!images || !mean || !std) return fail(LNET_ERR_INVALID_ARGUMENT, "forward_images: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(images) % 16 != 0)
+    return fail(LNET_ERR_INVALID_ARGUMENT, "forward_images: images must be 16-byte aligned");
+  ImageInput img{images, height, width, {}, {}};
+  for (int c = 0; c < 3; ++c) {
+    if (!(std[c] != 0.f)) return fail(LNET_ERR_INVALID_ARGUMENT, "forward_images: std must be nonzero");
+    img.mean[c] = mean[c];
+    img.std[c] = std[c];
+  }
+  const lnet_b200_alphabet_request r = image_request(images, batch, height, width);
+  LNET_TRY(check_request(params, &r));
+  if (batch > 0 && !use_fused(params, &r))
+    return fail(LNET_ERR_UNSUPPORTED,
+                "forward_images: these parameters do not take the fused route (48 raw channels "
+                "and a compiled shape are needed); patchify with lnet_b200_patchify_images and "
+                "call lnet_b200_alphabet_forward");
+  return alphabet_forward_impl(params, &r, workspace, workspace_bytes, logits, writer_moments,
+                               reader_moments, prepared != 0, stream, nullptr, &img);
 }
 
 extern "C" int lnet_b200_alphabet_prepare(const lnet_b200_alphabet_params *params,

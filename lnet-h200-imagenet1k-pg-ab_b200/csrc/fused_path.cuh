@@ -303,6 +303,20 @@ struct FusedArgs {
   const int64_t *lengths;
   int trace;       // 1: accumulate per-phase cycles of slot 0's thread 0 into g_fused_trace
   int kernel_id;   // 0 writer, 1 reader
+  // writer only: uint8 images [B][img_h][img_w][3] instead of x (NULL: x by TMA).
+  // Token t of a row is the 4 x 4 patch (t / (img_w / 4), t % (img_w / 4)); its
+  // channel (4 i + j) * 3 + ch is pixel (4 pr + i, 4 pc + j), channel ch, normalised
+  // as (u / 255 - mean[ch]) / std[ch] in fp32 and rounded to bf16.
+  const uint8_t *images;
+  int img_h, img_w;
+  float img_mean[3], img_std[3];
+};
+
+// Host description of an image request (lnet_b200_alphabet_forward_images).
+struct ImageInput {
+  const uint8_t *images;
+  int h, w;
+  float mean[3], std[3];
 };
 
 // Per-phase cycle totals of thread 0 of slot 0 of every CTA (tracing; off by
@@ -850,6 +864,83 @@ __device__ __forceinline__ void slot_scan(int qblk, int lane, uint32_t lane_addr
     if ((k >= 4) == (upper != 0)) atomicAdd(rowsum + k * M + m, (double)mom[k]);
 }
 
+// ---------------------------------------------------------------- image tiles
+// Image input: a byte u of channel ch becomes (u / 255 - mean[ch]) / std[ch] in
+// fp32 (IEEE divisions), rounded to bf16 -- the harness transform
+// (scripts/train_alphabet2d_imagenet100.py:292-310), so the tile equals the one
+// lnet_b200_patchify_images would have produced.  A byte has 256 values, so the
+// writer tabulates the 3 x 256 results in shared memory once per CTA.
+__device__ __forceinline__ void image_table(const FusedArgs &a, __nv_bfloat16 *lut) {
+  for (int i = threadIdx.x; i < 3 * 256; i += blockDim.x) {
+    const int ch = i >> 8;
+    lut[i] = __float2bfloat16_rn(((float)(i & 255) / 255.0f - a.img_mean[ch]) / a.img_std[ch]);
+  }
+}
+
+// The writer's x tile of `item` straight from the uint8 images: tile row r is
+// token t0 - 8 + r, stored as six K-major slabs of 8 bf16 channels (the layout
+// the TMA writes for x).  Rows outside [0, length) are zero.  Token t is the
+// 4 x 4 patch (t / (W / 4), t % (W / 4)); its channel (4 i + j) * 3 + ch is pixel
+// (4 pr + i, 4 pc + j), channel ch.  One (token, pixel row of its patch) pair at
+// a time: the pixel row's 12 bytes are three aligned 32-bit loads (all of a
+// thread's loads are issued before the first is used) and become channels
+// [12 i, 12 i + 12) through the table.
+template <int SLAB>
+__device__ __forceinline__ void image_tile(const FusedArgs &a, int64_t item, uint8_t *tile,
+                                           const __nv_bfloat16 *lut, int ltid) {
+  constexpr int kPairs = kXRows * 4;
+  constexpr int kIter = (kPairs + kSlotThreads - 1) / kSlotThreads;
+  const int64_t ch = (uint32_t)item / (uint32_t)a.B, bb = item - ch * a.B;
+  const int64_t t_lo = ch * kChunk - kHalo;
+  const int64_t tb = row_steps(a.lengths, bb, a.T);
+  const int pw = a.img_w / 4;
+  uint32_t w[kIter][3];
+  bool live[kIter];
+#pragma unroll
+  for (int j = 0; j < kIter; ++j) {
+    const int p = ltid + j * kSlotThreads;
+    const int r = p >> 2, i = p & 3;
+    const int64_t t = t_lo + r;
+    live[j] = p < kPairs && t >= 0 && t < tb;
+    w[j][0] = w[j][1] = w[j][2] = 0u;
+    if (live[j]) {
+      const int pr = (int)(t / pw), pc = (int)(t - (int64_t)pr * pw);
+      const uint32_t *src = reinterpret_cast<const uint32_t *>(
+          a.images + ((bb * a.img_h + 4 * pr + i) * (int64_t)a.img_w + 4 * pc) * 3);
+      w[j][0] = __ldg(src);
+      w[j][1] = __ldg(src + 1);
+      w[j][2] = __ldg(src + 2);
+    }
+  }
+  const uint16_t *tab = reinterpret_cast<const uint16_t *>(lut);
+#pragma unroll
+  for (int j = 0; j < kIter; ++j) {
+    const int p = ltid + j * kSlotThreads;
+    if (p >= kPairs) continue;
+    const int r = p >> 2, i = p & 3;
+    uint32_t pk[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+    if (live[j]) {
+#pragma unroll
+      for (int e = 0; e < 12; e += 2) {
+        const uint32_t u0 = (w[j][e / 4] >> (8 * (e % 4))) & 0xFFu;
+        const uint32_t u1 = (w[j][(e + 1) / 4] >> (8 * ((e + 1) % 4))) & 0xFFu;
+        pk[e / 2] = (uint32_t)tab[(e % 3) * 256 + u0] |
+                    ((uint32_t)tab[((e + 1) % 3) * 256 + u1] << 16);
+      }
+    }
+    // channels 12 i .. 12 i + 11: an even i starts a slab (16 bytes, then 8 bytes
+    // of the next), an odd i starts half way through one (8 bytes, then 16)
+    uint8_t *d0 = tile + ((12 * i) / 8) * SLAB + r * 16;
+    if ((i & 1) == 0) {
+      *reinterpret_cast<uint4 *>(d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint2 *>(d0 + SLAB) = make_uint2(pk[4], pk[5]);
+    } else {
+      *reinterpret_cast<uint2 *>(d0 + 8) = make_uint2(pk[0], pk[1]);
+      *reinterpret_cast<uint4 *>(d0 + SLAB) = make_uint4(pk[2], pk[3], pk[4], pk[5]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- writer kernel
 template <int C, int D, int M>
 struct WriterPlan {
@@ -867,7 +958,8 @@ struct WriterPlan {
   static constexpr int OFF_WS = OFF_Q + Q_BYTES;
   static constexpr int OFF_PAR = OFF_WS + WS_BYTES;            // float [2][D]: bias / 2, c
   static constexpr int OFF_K = OFF_PAR + 2 * D * 4;            // float [kConsts * M]
-  static constexpr int SHARED_END = (OFF_K + kConsts * M * 4 + 127) / 128 * 128;
+  static constexpr int OFF_LUT = OFF_K + kConsts * M * 4;      // bf16 [3][256]: image bytes
+  static constexpr int SHARED_END = (OFF_LUT + 3 * 256 * 2 + 127) / 128 * 128;
   // per slot
   static constexpr int SLAB_X = kXRows * 16;  // one TMA box; 128-byte multiple
   static constexpr int X_BYTES = (C / 8) * SLAB_X;
@@ -927,6 +1019,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     par[D + i] = __ldg(a.ls + i) * __ldg(a.ds + i) * __ldg(a.norm + i);
   }
   copy_floats(s_k, a.consts, kConsts * M);
+  if (a.images) image_table(a, reinterpret_cast<__nv_bfloat16 *>(smem + P::OFF_LUT));
   sm100::fence_proxy_async_smem();
   sm100::tc_fence_before();
   // every pole of this block real (a_im = 0 for every mode): the real-pole scan
@@ -951,12 +1044,19 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
       sm100::tma_load_3d(g_base + P::G_X + kc * P::SLAB_X, &a.tmap, tbar, kc * 8,
                          (int)(ch * kChunk - kHalo), (int)bb);
   };
+  const bool from_images = a.images != nullptr;  // x tiles built from uint8 images
+  const __nv_bfloat16 *lut = reinterpret_cast<const __nv_bfloat16 *>(smem + P::OFF_LUT);
   if (ltid == kTileIssuer) {
     const int64_t first = claim_item(a.counter, a.lengths, a.B, a.T, total);
     item_slot[0] = first;
-    if (first < total) issue_tile(first);
+    if (first < total && !from_images) issue_tile(first);
   }
   slot_sync(bar);
+  if (from_images) {
+    if (item_slot[0] < total) image_tile<P::SLAB_X>(a, item_slot[0], gs + P::G_X, lut, ltid);
+    sm100::fence_proxy_async_smem();
+    slot_sync(bar);
+  }
   for (int iter = 0;; ++iter) {
     const int64_t item = item_slot[iter & 1];
     if (item >= total) break;
@@ -973,7 +1073,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     // 1-2. x tile, then the stem GEMM: five row-shifted views of the tile.  A row
     // shorter than T (valid length) needs its tile rows past the length zeroed
     // first (the TMA zero-fills only past T).
-    if (tb < a.T && t0 + kChunk + kHalo > tb) {
+    if (!from_images && tb < a.T && t0 + kChunk + kHalo > tb) {
       if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && ltid == 0)
         atomicOr(a.error, kErrTile);
       const int keep = (int)(tb - t0 + kHalo);  // tile rows [0, keep) are real steps
@@ -985,7 +1085,8 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
       slot_sync(bar);
     }
     if (ltid == 0) {
-      if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit)) atomicOr(a.error, kErrTile);
+      if (!from_images && !sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit))
+        atomicOr(a.error, kErrTile);
       LNET_TRACE(1);
       sm100::tc_fence_after();
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, D);
@@ -1003,7 +1104,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     LNET_TRACE(2);
     if (ltid == kTileIssuer) {
       item_slot[(iter + 1) & 1] = next;
-      if (next < total) issue_tile(next);
+      if (next < total && !from_images) issue_tile(next);
     }
     // 3. bias + SiLU + RMSNorm, thread per token: f = h + h tanh(h), h = v / 2, kept
     // as bf16 (the value parked for the residual); xhat = f rs (g is in the drive
@@ -1058,6 +1159,12 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
       issue_gemm(tslot, s_base + P::OFF_AD + DriveRotation<M>::offset(slot), P::SLAB_AD, g_base + P::G_XS, P::SLAB_XH, D / 16,
                  idesc, false);
       sm100::mma_commit(mbar);
+    }
+    // image input: the next item's x tile, built under the drive GEMM (the stem GEMM
+    // has read the tile region; the item id became visible at the barrier above)
+    if (from_images) {
+      const int64_t nx = item_slot[(iter + 1) & 1];
+      if (nx < total) image_tile<P::SLAB_X>(a, nx, gs + P::G_X, lut, ltid);
     }
     LookbackPrefetch pre;
     lookback_prefetch<M>(qblk, lane, a.rec, b, chunk, a.n_chunks, pre);
@@ -1468,7 +1575,7 @@ inline int fused_prepare(const lnet_b200_alphabet_params *p, FusedWorkspace &w, 
 template <int C, int D, int M>
 int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
                         FusedWorkspace &w, float *wm, float *rm, bool prepared,
-                        const int64_t *lengths, cudaStream_t st) {
+                        const int64_t *lengths, cudaStream_t st, const ImageInput *img) {
   using WP = WriterPlan<C, D, M>;
   using RP = ReaderPlan<D, M>;
   const int64_t B = r->batch, T = r->steps, nch = fused_chunks(T);
@@ -1482,8 +1589,19 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                       "cudaMemsetAsync(row sums, flags)"));
   uint32_t *counters = w.flags;
   FusedArgs wa{};
-  wa.in = (const __nv_bfloat16 *)r->x;
-  LNET_TRY(encode_tile_map(&wa.tmap, r->x, B, T, C));
+  if (img) {  // x tiles built from the images inside the writer
+    if (C != 48) return fail(LNET_ERR_UNSUPPORTED, "image input needs 48 raw channels");
+    wa.images = img->images;
+    wa.img_h = img->h;
+    wa.img_w = img->w;
+    for (int c = 0; c < 3; ++c) {
+      wa.img_mean[c] = img->mean[c];
+      wa.img_std[c] = img->std[c];
+    }
+  } else {
+    wa.in = (const __nv_bfloat16 *)r->x;
+    LNET_TRY(encode_tile_map(&wa.tmap, r->x, B, T, C));
+  }
   wa.B = B;
   wa.T = T;
   wa.n_chunks = nch;
@@ -1519,6 +1637,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   fused_writer_kernel<C, D, M><<<grid, kSlots * kSlotThreads, WP::BYTES, st>>>(wa);
   LNET_TRY(after_launch("fused_writer_kernel"));
   FusedArgs ra = wa;
+  ra.images = nullptr;
   ra.in = w.stream;
   if (reinterpret_cast<uintptr_t>(w.stream) % 16 != 0)
     return fail(LNET_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
@@ -1547,10 +1666,11 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
 // `lengths` (may be NULL): per-row valid lengths of a right-padded request.
 inline int fused_forward(const lnet_b200_alphabet_params *p, const lnet_b200_alphabet_request *r,
                          FusedWorkspace &w, float *wm, float *rm, bool prepared,
-                         const int64_t *lengths, cudaStream_t st) {
+                         const int64_t *lengths, cudaStream_t st,
+                         const ImageInput *img = nullptr) {
 #define LNET_FUSED_CASE(CC, DD, MM)                                                  \
   if (p->raw_input_dim == CC && p->model_dim == DD && p->modes == MM)               \
-    return fused_forward_shape<CC, DD, MM>(p, r, w, wm, rm, prepared, lengths, st);
+    return fused_forward_shape<CC, DD, MM>(p, r, w, wm, rm, prepared, lengths, st, img);
   LNET_FUSED_CASE(48, 96, 48)
   LNET_FUSED_CASE(32, 96, 48)
   LNET_FUSED_CASE(64, 64, 32)

@@ -121,6 +121,15 @@ SIGNATURES = {
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, _i32, _c_p,
          ctypes.c_size_t, _c_p, _c_p, _c_p, _c_p],
     ),
+    "lnet_b200_alphabet_images_workspace_size": (
+        ctypes.c_int, [ctypes.POINTER(AlphabetParams), _i64, _i32, _i32,
+                       ctypes.POINTER(ctypes.c_size_t)],
+    ),
+    "lnet_b200_alphabet_forward_images": (
+        ctypes.c_int,
+        [ctypes.POINTER(AlphabetParams), _c_p, _i64, _i32, _i32, ctypes.POINTER(ctypes.c_float),
+         ctypes.POINTER(ctypes.c_float), _i32, _c_p, ctypes.c_size_t, _c_p, _c_p, _c_p, _c_p],
+    ),
     "lnet_b200_alphabet_device_status": (
         ctypes.c_int,
         [ctypes.POINTER(AlphabetParams), ctypes.POINTER(AlphabetRequest), _c_p, ctypes.c_size_t,

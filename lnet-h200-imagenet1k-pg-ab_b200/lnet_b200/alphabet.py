@@ -367,12 +367,28 @@ class B200Alphabet(nn.Module):
     def forward_images(self, images: Tensor, *, mean=None, std=None, patch: int = 4,
                        dtype: torch.dtype = torch.bfloat16, return_moments: bool = False):
         """Forward from uint8 images [B, H, W, 3] on CUDA: normalise + patchify on
-        the GPU (:func:`lnet_b200.images.patchify_images`, bit-identical to the
-        harness transform), then :meth:`forward` on the tokens."""
+        the GPU (bit-identical to the harness transform), then the forward on the
+        tokens.  Inference requests the fused route serves (4 x 4 patches, bf16,
+        48 raw channels) build the tokens inside the fused writer
+        (``lnet_b200_alphabet_forward_images``: no token tensor in HBM); every other
+        request patchifies first (:func:`lnet_b200.images.patchify_images`) and
+        calls :meth:`forward`."""
         from .images import IMAGENET_MEAN, IMAGENET_STD, patchify_images
 
-        x = patchify_images(images, mean=IMAGENET_MEAN if mean is None else mean,
-                            std=IMAGENET_STD if std is None else std, patch=patch, dtype=dtype)
+        mean = IMAGENET_MEAN if mean is None else mean
+        std = IMAGENET_STD if std is None else std
+        if images.dtype != torch.uint8 or images.ndim != 4 or images.shape[-1] != 3:
+            raise ValueError(f"images must be uint8 [B, H, W, 3], got {images.dtype} "
+                             f"{tuple(images.shape)}")
+        if (patch == 4 and dtype == torch.bfloat16 and images.is_cuda
+                and not (self.training and torch.is_grad_enabled())
+                and images.shape[1] % 4 == 0 and images.shape[2] % 4 == 0):
+            images = images.contiguous()
+            if images_route_fused(self, images):
+                logits, wm, rm = images_forward_raw(self, images, mean, std, return_moments)
+                logits = logits.to(self.head.classifier.weight.dtype)
+                return (logits, wm, rm) if return_moments else logits
+        x = patchify_images(images, mean=mean, std=std, patch=patch, dtype=dtype)
         return self.forward(x, return_moments=return_moments)
 
 
@@ -443,6 +459,61 @@ def alphabet_forward_raw(model: B200Alphabet, x: Tensor, delta, obs, valid, act_
                 ctypes_ref(params), ctypes_ref(req), ws.data_ptr(), nbytes, logits.data_ptr(),
                 wm_p, rm_p, stream)
     _lib.check(st, name)
+    return logits, wm, rm
+
+
+def _images_request(images: Tensor):
+    """The token request an image forward stands for: [B, (H/4)(W/4), 48] bf16."""
+    b, h, w, _ = images.shape
+    return _lib.AlphabetRequest(batch=b, steps=(h // 4) * (w // 4), x_dtype=_lib.LNET_BF16,
+                                act_dtype=_lib.LNET_BF16, x=images.data_ptr(), obs_channels=0)
+
+
+def images_route_fused(model: B200Alphabet, images: Tensor) -> bool:
+    """Whether ``lnet_b200_alphabet_forward_images`` serves these images (fused route)."""
+    if images.shape[0] == 0 or images.data_ptr() % 16 != 0:
+        return False
+    lib = _lib.load()
+    params, _keep = model._effective(images.device)
+    return lib.lnet_b200_alphabet_route(ctypes_ref(params),
+                                        ctypes_ref(_images_request(images))) == 0
+
+
+def images_forward_raw(model: B200Alphabet, images: Tensor, mean, std,
+                       want_moments: bool = False):
+    """One ``lnet_b200_alphabet_forward_images`` call on the current CUDA stream."""
+    import ctypes
+
+    lib = _lib.load()
+    params, _keep = model._effective(images.device)
+    req = _images_request(images)
+    b, h, w, _ = images.shape
+    m = model.modes
+    logits = torch.empty(b, model.head.classifier.out_features, device=images.device,
+                         dtype=torch.float32)
+    wm = rm = None
+    if want_moments:
+        wm = torch.empty(b, 7 * m, device=images.device, dtype=torch.float32)
+        rm = torch.empty(b, 7 * m, device=images.device, dtype=torch.float32)
+    n = ctypes.c_size_t(0)
+    _lib.check(lib.lnet_b200_alphabet_images_workspace_size(ctypes_ref(params), b, h, w,
+                                                            ctypes.byref(n)),
+               "lnet_b200_alphabet_images_workspace_size")
+    nbytes = int(n.value)
+    stream = torch.cuda.current_stream(images.device).cuda_stream
+    prepared = getattr(model, "_prepare_spec", None) is not None
+    if prepared:
+        ws, nbytes = _prepared_workspace(model, params, req, nbytes, images.device, stream)
+    else:
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=images.device)
+    mean_c = (ctypes.c_float * 3)(*[float(v) for v in mean])
+    std_c = (ctypes.c_float * 3)(*[float(v) for v in std])
+    with torch.cuda.device(images.device):
+        st = lib.lnet_b200_alphabet_forward_images(
+            ctypes_ref(params), images.data_ptr(), b, h, w, mean_c, std_c, int(prepared),
+            ws.data_ptr(), nbytes, logits.data_ptr(), None if wm is None else wm.data_ptr(),
+            None if rm is None else rm.data_ptr(), stream)
+    _lib.check(st, "lnet_b200_alphabet_forward_images")
     return logits, wm, rm
 
 
