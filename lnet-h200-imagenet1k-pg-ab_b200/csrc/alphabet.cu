@@ -296,7 +296,7 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   } else {
     LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
                        bt, 2 * M, D, tf32, "gemm(drive)"));
-    drive_kernel<<<token_grid(bt), token_block(M), 0, st>>>(pl.drive, raw_decay, raw_freq,
+    drive_kernel<<<(unsigned)cdiv(bt, kDriveTokens), 256, 0, st>>>(pl.drive, raw_decay, raw_freq,
                                                             r->time_delta, g_re, g_im, event_mask,
                                                             obs_channels, bt, M, pl.step_a);
     LNET_TRY(after_launch("drive_kernel"));

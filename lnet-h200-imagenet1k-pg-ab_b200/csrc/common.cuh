@@ -104,6 +104,33 @@ __device__ __forceinline__ Zoh zoh_eval(double damping, double frequency, double
   return Zoh{(float)ar, (float)ai, (float)gr, (float)gi};
 }
 
+// The same zero-order hold in fp32 for per-step evaluation (one (step, mode)
+// pair per call, where the double form's exp and sincos dominated the drive
+// pass).  a - 1 is formed without cancellation: with x = -damping dt and
+// phi = frequency dt, a - 1 = expm1(x) cos(phi) - 2 sin^2(phi / 2)
+// + i exp(x) sin(phi), and cos(phi), sin(phi) come from sincos(phi / 2).  Every
+// term is then a product of correctly rounded library results, a few fp32 ulp
+// from the double evaluation; gamma is one complex division by p.
+__device__ __forceinline__ Zoh zoh_eval_f32(float damping, float frequency, float step) {
+  const float x = -damping * step, ph = frequency * step;
+  const float em1 = expm1f(x), e = expf(x);
+  float s2, c2;
+  sincosf(0.5f * ph, &s2, &c2);
+  const float sn = 2.f * s2 * c2;
+  const float cs = fmaf(-2.f * s2, s2, 1.f);
+  const float ar = e * cs, ai = e * sn;
+  const float shr = fmaf(em1, cs, -2.f * s2 * s2), shi = ai;
+  const float pr = -damping, pi = frequency;
+  const float den = fmaf(pr, pr, pi * pi);
+  float gr = fmaf(shr, pr, shi * pi) / den;
+  float gi = fmaf(shi, pr, -shr * pi) / den;
+  if (sqrtf(fmaf(x, x, ph * ph)) < 1.0e-6f) {
+    gr = step;
+    gi = 0.f;
+  }
+  return Zoh{ar, ai, gr, gi};
+}
+
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -579,46 +579,84 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 // ---------------------------------------------------------------- drive (gamma (x) e * mask)
 // e[tok, 0:M] / e[tok, M:2M] -> u in place; gamma from the per-mode table or per step.
 // Without dt the gains are the per-mode table g_tab_re/im (zoh_kernel); with dt
-// they are evaluated per step, and `step_a` (when given) receives the step's
-// transition a = exp(p dt) as [tok][re M | im M] for the scans (the same
-// double evaluation, rounded once, that the scans would otherwise repeat).
-__global__ void drive_kernel(float *__restrict__ e, const float *__restrict__ raw_decay,
-                             const float *__restrict__ raw_freq, const float *__restrict__ dt,
-                             const float *__restrict__ g_tab_re, const float *__restrict__ g_tab_im,
-                             const float *__restrict__ event_mask, int obs_channels,
-                             int64_t tokens, int modes, float *__restrict__ step_a) {
-  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    double damping = 0.0, frequency = 0.0;  // the mode's pole (per mode, not per step)
-    if (dt) mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
-    for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
-      float gr, gi;
-      float *row = e + tok * 2 * modes;
-      if (dt) {
-        const Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
-        gr = z.g_re;
-        gi = z.g_im;
-        if (step_a) {
-          step_a[tok * 2 * modes + m] = z.a_re;
-          step_a[tok * 2 * modes + modes + m] = z.a_im;
-        }
-      } else {
-        gr = g_tab_re[m];
-        gi = g_tab_im[m];
-      }
-      float er = row[m], ei = row[modes + m];
-      float ur = gr * er - gi * ei;
-      float ui = gr * ei + gi * er;
-      if (event_mask) {
-        // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
-        const float *om = event_mask + tok * obs_channels;
-        float mx = om[0];
-        for (int c = 1; c < obs_channels; ++c) mx = fmaxf(mx, om[c]);
-        ur *= mx;
-        ui *= mx;
-      }
-      row[m] = ur;
-      row[modes + m] = ui;
+// they are evaluated per (step, mode) in fp32 (zoh_eval_f32), and `step_a`
+// (when given) receives the step's transition a = exp(p dt) as
+// [tok][re M | im M] for the scans.  A block takes kDriveTokens tokens: the
+// event masks (amax over the raw channels) are reduced once per token by a warp
+// into shared memory, the mode poles once per block, and then one thread per
+// (token, mode) pair, consecutive modes on consecutive lanes.
+constexpr int kDriveTokens = 32;
+constexpr int kDriveMaxModes = 256;
+__global__ void __launch_bounds__(256) drive_kernel(
+    float *__restrict__ e, const float *__restrict__ raw_decay, const float *__restrict__ raw_freq,
+    const float *__restrict__ dt, const float *__restrict__ g_tab_re,
+    const float *__restrict__ g_tab_im, const float *__restrict__ event_mask, int obs_channels,
+    int64_t tokens, int modes, float *__restrict__ step_a) {
+  // per mode: (damping, frequency) with dt, the gain table (re, im) without
+  __shared__ float s_pa[kDriveMaxModes], s_pb[kDriveMaxModes], s_mask[kDriveTokens];
+  const int64_t tok0 = (int64_t)blockIdx.x * kDriveTokens;
+  const int ntok = (int)(tokens - tok0 < kDriveTokens ? tokens - tok0 : kDriveTokens);
+  // (modes past kDriveMaxModes are looked up per pair instead)
+  auto mode_consts = [&](int m, float &pa, float &pb) {
+    if (dt) {
+      double damping, frequency;
+      mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
+      pa = (float)damping;
+      pb = (float)frequency;
+    } else {
+      pa = g_tab_re[m];
+      pb = g_tab_im[m];
     }
+  };
+  for (int m = threadIdx.x; m < min(modes, kDriveMaxModes); m += blockDim.x)
+    mode_consts(m, s_pa[m], s_pb[m]);
+  if (event_mask) {
+    // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < ntok; t += blockDim.x >> 5) {
+      const float *om = event_mask + (tok0 + t) * obs_channels;
+      float mx = -INFINITY;
+      for (int c = lane; c < obs_channels; c += 32) mx = fmaxf(mx, om[c]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) s_mask[t] = mx;
+    }
+  }
+  __syncthreads();
+  const int pairs = ntok * modes;
+  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
+    const int t = idx / modes, m = idx - t * modes;
+    const int64_t tok = tok0 + t;
+    float pa, pb;
+    if (m < kDriveMaxModes) {
+      pa = s_pa[m];
+      pb = s_pb[m];
+    } else {
+      mode_consts(m, pa, pb);
+    }
+    float gr, gi;
+    if (dt) {
+      const Zoh z = zoh_eval_f32(pa, pb, dt[tok]);
+      gr = z.g_re;
+      gi = z.g_im;
+      if (step_a) {
+        step_a[tok * 2 * modes + m] = z.a_re;
+        step_a[tok * 2 * modes + modes + m] = z.a_im;
+      }
+    } else {
+      gr = pa;
+      gi = pb;
+    }
+    float *row = e + tok * 2 * modes;
+    const float er = row[m], ei = row[modes + m];
+    float ur = gr * er - gi * ei;
+    float ui = gr * ei + gi * er;
+    if (event_mask) {
+      ur *= s_mask[t];
+      ui *= s_mask[t];
+    }
+    row[m] = ur;
+    row[modes + m] = ui;
   }
 }
 
@@ -638,12 +676,35 @@ __device__ __forceinline__ void step_coeff(const float *raw_decay, const float *
   } else if (dt) {
     double damping, frequency;
     mode_pole(raw_decay[m], raw_freq[m], damping, frequency);
-    Zoh z = zoh_eval(damping, frequency, (double)dt[tok]);
+    Zoh z = zoh_eval_f32((float)damping, (float)frequency, dt[tok]);
     ar = z.a_re;
     ai = z.a_im;
   } else {
     ar = a_tab_re[m];
     ai = a_tab_im[m];
+  }
+}
+
+// Loads (transitions and inputs) of `n` <= kScanGroup consecutive steps from
+// token `tok0` for mode m, all issued before the caller's dependent steps.
+constexpr int kScanGroup = 8;
+__device__ __forceinline__ void scan_group_load(const float *raw_decay, const float *raw_freq,
+                                                const float *a_tab_re, const float *a_tab_im,
+                                                const float *dt, const float *step_a,
+                                                const float *u, int modes, int64_t tok0, int n,
+                                                int m, float *ar, float *ai, float *xr,
+                                                float *xi) {
+#pragma unroll
+  for (int k = 0; k < kScanGroup; ++k) {
+    if (k < n) {
+      step_coeff(raw_decay, raw_freq, a_tab_re, a_tab_im, dt, step_a, modes, tok0 + k, m, ar[k],
+                 ai[k]);
+      const float *row = u + (tok0 + k) * 2 * modes;
+      xr[k] = row[m];
+      xi[k] = row[modes + m];
+    } else {
+      ar[k] = ai[k] = xr[k] = xi[k] = 0.f;
+    }
   }
 }
 
@@ -772,17 +833,22 @@ __global__ void scan_apply_kernel(float *__restrict__ u, const float *__restrict
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
     const float *rec = carries + (b * n_chunks + c) * kRecFloats * modes;
     float sr = rec[m], si = rec[modes + m];
-    for (int64_t t = t0; t < t1; ++t) {
-      int64_t tok = b * steps + t;
-      float ar, ai;
-      step_coeff(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, step_a, modes, tok, m, ar, ai);
-      float *row = u + tok * 2 * modes;
-      float nr = ar * sr - ai * si + row[m];
-      float ni = ai * sr + ar * si + row[modes + m];
-      sr = nr;
-      si = ni;
-      row[m] = sr;
-      row[modes + m] = si;
+    for (int64_t tg = t0; tg < t1; tg += kScanGroup) {
+      float ar[kScanGroup], ai[kScanGroup], xr[kScanGroup], xi[kScanGroup];
+      scan_group_load(raw_decay, raw_freq, a_re_tab, a_im_tab, dt, step_a, u, modes,
+                      b * steps + tg, (int)(t1 - tg < kScanGroup ? t1 - tg : kScanGroup), m, ar, ai, xr, xi);
+#pragma unroll
+      for (int k = 0; k < kScanGroup; ++k) {
+        if (tg + k < t1) {
+          const float nr = ar[k] * sr - ai[k] * si + xr[k];
+          const float ni = ai[k] * sr + ar[k] * si + xi[k];
+          sr = nr;
+          si = ni;
+          float *row = u + (b * steps + tg + k) * 2 * modes;
+          row[m] = sr;
+          row[modes + m] = si;
+        }
+      }
     }
   }
 }
