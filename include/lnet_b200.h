@@ -121,8 +121,9 @@ int lnet_b200_set_gemm_backend(int backend);
 
 /* Route selection for lnet_b200_alphabet_forward (process-wide):
  * 0 = automatic (the fused unit-grid kernels when the request has no
- * metadata, bf16 activations and a compiled shape; the general route
- * otherwise), 1 = general route only.  No reference counterpart: replaces the
+ * time_delta or valid mask (observation masks are served: the writer masks its
+ * input tiles and drive), bf16 activations and a compiled shape; the general
+ * route otherwise), 1 = general route only.  No reference counterpart: replaces the
  * reference's per-instance fused-inference gates (src/lnet/alphabet.py:190-223,
  * 257-348). */
 int lnet_b200_set_route(int route);
@@ -152,7 +153,7 @@ int lnet_b200_alphabet_forward_prepared(const lnet_b200_alphabet_params *params,
 /* lnet_b200_alphabet_forward (prepared = 0) or ..._forward_prepared (prepared =
  * 1) for a right-padded request: `lengths` (int64 [B], device) holds each row's
  * valid length L_b, meaning valid_mask[b, t] = 1 for t < L_b and 0 after, and
- * req carries no metadata.  The result equals the forward with that valid mask
+ * req carries no valid mask or time_delta (an observation mask is allowed).  The result equals the forward with that valid mask
  * (src/lnet/pac_tight_frame_models.py:1660-1702 masked moments,
  * src/lnet/alphabet_backbone.py:649-676 / :872-992 stem and reader masking): a
  * right-padded row computes exactly as an unpadded row of L_b steps, so the

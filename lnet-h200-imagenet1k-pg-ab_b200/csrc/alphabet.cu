@@ -631,9 +631,9 @@ extern "C" int lnet_b200_alphabet_forward_lengths(const lnet_b200_alphabet_param
   LNET_TRY(check_params(params));
   LNET_TRY(check_request(params, req));
   if (!lengths) return fail(LNET_ERR_INVALID_ARGUMENT, "lengths is NULL");
-  if (req->time_delta || req->observation_mask || req->valid_mask)
+  if (req->time_delta || req->valid_mask)
     return fail(LNET_ERR_INVALID_ARGUMENT,
-                "forward_lengths: the lengths replace the valid mask; pass no other metadata");
+                "forward_lengths: the lengths replace the valid mask; pass no time_delta");
   if (req->batch > 0 && req->steps > 0 && !use_fused(params, req))
     return fail(LNET_ERR_UNSUPPORTED,
                 "forward_lengths: this request does not take the fused route; pass the valid "

@@ -301,6 +301,12 @@ struct FusedArgs {
   // per-row valid lengths [B] (right-padded valid masks) or NULL (every row T steps):
   // steps at or past a row's length are treated as the zero padding past T
   const int64_t *lengths;
+  // writer only: observation mask [B][T][obs_channels] fp32 (obs_channels 1 or C) or
+  // NULL.  It scales the raw inputs before the stem and the drive by the event
+  // mask (its amax over the channels); the reader takes none
+  // (src/lnet/alphabet_backbone.py:649-676, 1170-1180)
+  const float *obs;
+  int obs_channels;
   int trace;       // 1: accumulate per-phase cycles of slot 0's thread 0 into g_fused_trace
   int kernel_id;   // 0 writer, 1 reader
   // writer only: uint8 images [B][img_h][img_w][3] instead of x (NULL: x by TMA).
@@ -941,6 +947,55 @@ __device__ __forceinline__ void image_tile(const FusedArgs &a, int64_t item, uin
   }
 }
 
+// ---------------------------------------------------------------- observation masks
+// Raw-channel masking of a landed x tile in place (x o, rounded to bf16 as a bf16
+// product is): tile row r is step t0 - kHalo + r of row b; rows before step 0 or
+// at/after the row's length tb are the zero padding and stay as they are.
+template <int C, int SLAB>
+__device__ __forceinline__ void mask_tile(const FusedArgs &a, int64_t b, int64_t t0, int64_t tb,
+                                          uint8_t *tile, int ltid) {
+  for (int e = ltid; e < (C / 8) * kXRows; e += kSlotThreads) {
+    const int kc = e / kXRows, r = e - kc * kXRows;
+    const int64_t t = t0 - kHalo + r;
+    if (t < 0 || t >= tb) continue;
+    const int64_t tok = b * a.T + t;
+    float o[8];
+    if (a.obs_channels == 1) {
+      const float v = __ldg(a.obs + tok);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v;
+    } else {
+      const float4 *src = reinterpret_cast<const float4 *>(a.obs + tok * C + 8 * kc);
+      const float4 lo = __ldg(src), hi = __ldg(src + 1);
+      o[0] = lo.x; o[1] = lo.y; o[2] = lo.z; o[3] = lo.w;
+      o[4] = hi.x; o[5] = hi.y; o[6] = hi.z; o[7] = hi.w;
+    }
+    uint4 *px = reinterpret_cast<uint4 *>(tile + kc * SLAB + r * 16);
+    float v[8];
+    bf16x8_to_float(*px, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] *= o[i];
+    *px = pack_bf16x8(v);
+  }
+}
+
+// Event mask of step t of row b: the observation mask's amax over its channels
+// (src/lnet/alphabet_backbone.py:568); 1 without a mask.
+template <int C>
+__device__ __forceinline__ float event_mask(const FusedArgs &a, int64_t b, int64_t t) {
+  if (!a.obs) return 1.f;
+  const int64_t tok = b * a.T + t;
+  if (a.obs_channels == 1) return __ldg(a.obs + tok);
+  const float4 *src = reinterpret_cast<const float4 *>(a.obs + tok * C);
+  float mx = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < C / 4; ++q) {
+    const float4 v = __ldg(src + q);
+    mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+  }
+  return mx;
+}
+
 // ---------------------------------------------------------------- writer kernel
 template <int C, int D, int M>
 struct WriterPlan {
@@ -1073,14 +1128,20 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     // 1-2. x tile, then the stem GEMM: five row-shifted views of the tile.  A row
     // shorter than T (valid length) needs its tile rows past the length zeroed
     // first (the TMA zero-fills only past T).
-    if (!from_images && tb < a.T && t0 + kChunk + kHalo > tb) {
+    // An observation mask scales the landed tile's rows in place the same way.
+    const bool tail = tb < a.T && t0 + kChunk + kHalo > tb;
+    if (!from_images && (tail || a.obs)) {
       if (!sm100::mbar_wait_bounded(tbar, tphase, kSpinLimit) && ltid == 0)
         atomicOr(a.error, kErrTile);
-      const int keep = (int)(tb - t0 + kHalo);  // tile rows [0, keep) are real steps
-      for (int e = ltid; e < (C / 8) * (kXRows - keep); e += kSlotThreads) {
-        const int kc = e / (kXRows - keep), r = keep + e % (kXRows - keep);
-        *reinterpret_cast<uint4 *>(gs + P::G_X + kc * P::SLAB_X + r * 16) = make_uint4(0, 0, 0, 0);
+      if (tail) {
+        const int keep = (int)(tb - t0 + kHalo);  // tile rows [0, keep) are real steps
+        for (int e = ltid; e < (C / 8) * (kXRows - keep); e += kSlotThreads) {
+          const int kc = e / (kXRows - keep), r = keep + e % (kXRows - keep);
+          *reinterpret_cast<uint4 *>(gs + P::G_X + kc * P::SLAB_X + r * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
       }
+      if (a.obs) mask_tile<C, P::SLAB_X>(a, b, t0, tb, gs + P::G_X, ltid);
       sm100::fence_proxy_async_smem();
       slot_sync(bar);
     }
@@ -1113,6 +1174,10 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
     // of the same row: no round trip through memory
     float rs;
     uint32_t fp[D / 2];
+    // event mask of this thread's step: scales its xhat row, the drive GEMM's
+    // operand, so the drive u = gamma (xhat W) is masked (the direct term keeps
+    // the unmasked xhat, folded into the residual constants)
+    const float ev = (a.obs && t0 + row < tb) ? event_mask<C>(a, b, t0 + row) : 1.f;
     {
       float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -1133,7 +1198,7 @@ __global__ void __launch_bounds__(kSlots * kSlotThreads, 1)
         }
       }
       rs = rsqrtf((ss2.x + ss2.y) / (float)D + kFp32Eps);
-      const float2 rs2 = make_float2(rs, rs);
+      const float2 rs2 = make_float2(rs * ev, rs * ev);
 #pragma unroll
       for (int gq = 0; gq < D / 8; ++gq) {
         const uint4 fv = make_uint4(fp[4 * gq], fp[4 * gq + 1], fp[4 * gq + 2], fp[4 * gq + 3]);
@@ -1530,7 +1595,11 @@ constexpr FusedShapeKey kFusedShapes[] = {
 
 inline bool fused_supported(const lnet_b200_alphabet_params *p,
                             const lnet_b200_alphabet_request *r) {
-  if (r->time_delta || r->observation_mask || r->valid_mask) return false;
+  if (r->time_delta || r->valid_mask) return false;
+  // observation masks: channel masks are read as float4 rows
+  if (r->observation_mask && r->obs_channels != 1 &&
+      reinterpret_cast<uintptr_t>(r->observation_mask) % 16 != 0)
+    return false;
   if (r->x_dtype != LNET_BF16 || r->act_dtype != LNET_BF16) return false;
   if (p->conv_kernel != kTaps || p->conv_dilation != 4) return false;
   if (r->steps < 1 || r->batch < 1) return false;
@@ -1629,6 +1698,8 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   wa.trace = fused_trace_enabled();
   wa.kernel_id = 0;
   wa.lengths = lengths;
+  wa.obs = img ? nullptr : r->observation_mask;
+  wa.obs_channels = r->obs_channels;
   LNET_TRY(cuda_check(cudaFuncSetAttribute(fused_writer_kernel<C, D, M>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, WP::BYTES),
                       "cudaFuncSetAttribute(fused_writer_kernel)"));
@@ -1638,6 +1709,7 @@ int fused_forward_shape(const lnet_b200_alphabet_params *p, const lnet_b200_alph
   LNET_TRY(after_launch("fused_writer_kernel"));
   FusedArgs ra = wa;
   ra.images = nullptr;
+  ra.obs = nullptr;  // the reader takes no observation mask
   ra.in = w.stream;
   if (reinterpret_cast<uintptr_t>(w.stream) % 16 != 0)
     return fail(LNET_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");

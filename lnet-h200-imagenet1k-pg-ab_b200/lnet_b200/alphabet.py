@@ -420,8 +420,8 @@ def alphabet_forward_raw(model: B200Alphabet, x: Tensor, delta, obs, valid, act_
     lib = _lib.load()
     params, _keep = model._effective(x.device)
     lengths = None
-    if valid is not None and delta is None and obs is None:
-        req0 = model._request(x, None, None, None, act_dtype)
+    if valid is not None and delta is None:
+        req0 = model._request(x, None, obs, None, act_dtype)
         if lib.lnet_b200_alphabet_route(ctypes_ref(params), ctypes_ref(req0)) == 0:
             lengths = right_padded_lengths(valid)
     req = model._request(x, delta, obs, None if lengths is not None else valid, act_dtype)
