@@ -448,6 +448,7 @@ def run_train(args, cfg):
     prof = _lib.profile_read()
     _lib.profile_enable(False)
     total_ms = sum(a.elapsed_time(b) for a, b in zip(starts, stops))
+    captured = captured_train_step(args, model, x, meta, flush)
     print(json.dumps({
         "metric": TRAIN_METRIC, "value": B * T * args.steps / (total_ms / 1e3), "unit": UNIT,
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -457,8 +458,54 @@ def run_train(args, cfg):
         "config": {"workload": cfg["workload"], "path": "module API, training step (SGD)",
                    "l2": "256 MiB flush between steps, outside the per-step event pair"},
         "clocks": clocks.summary(), "gpu_launches_backward": launches,
-        "kernels": _lib_kernels(prof)}), flush=True)
+        "captured": captured, "kernels": _lib_kernels(prof)}), flush=True)
     return 0
+
+
+def captured_train_step(args, model, x, meta, flush):
+    """The same model trained with a cross-entropy loss and SGD, eagerly and
+    through ``lnet_b200.prepare_exact_split_training`` (one CUDA-graph launch per
+    step), each timed by CUDA events over ``args.steps`` steps."""
+    import torch
+    from torch.nn import functional as F
+
+    from lnet_b200 import prepare_exact_split_training
+
+    dev = x.device
+    labels = torch.randint(0, model.head.classifier.out_features, (x.shape[0],),
+                           generator=torch.Generator(device=dev).manual_seed(2), device=dev)
+    opt = torch.optim.SGD(model.parameters(), lr=1e-4)
+
+    def eager():
+        opt.zero_grad(set_to_none=False)
+        F.cross_entropy(model(x, **meta), labels).backward()
+        opt.step()
+
+    rt = prepare_exact_split_training(
+        model, opt, x, labels, example_time_delta=meta.get("time_delta"),
+        example_observation_mask=meta.get("observation_mask"),
+        example_valid_mask=meta.get("valid_mask"))
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        for a, b in ev:
+            flush.zero_()
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev) / args.steps
+
+    eager_ms = timed(eager)
+    graph_ms = timed(rt.step_static)
+    rt.close()
+    return {"eager_ms_per_step": eager_ms, "graph_ms_per_step": graph_ms,
+            "note": "cross-entropy loss + SGD: module API eagerly, and one replay of the "
+                    "step captured by lnet_b200.prepare_exact_split_training"}
 
 
 def synthetic_metadata(cfg, dev, seed=5):

@@ -28,6 +28,11 @@ All compute runs in the C-ABI CUDA library ``_lib/liblnet_b200.so`` built by
 from . import ops  # registers the lnet_b200:: custom ops
 from .alphabet import AlphabetConfig, B200Alphabet
 from .inference import prepare_compiled_inference, prepare_maskless_inference
+from .train_runtime import (
+    AlphabetTrainingRuntime,
+    prepare_aggressive_training,
+    prepare_exact_split_training,
+)
 from .laplace import (
     B200PoleResidueTemporalMixing,
     LaplaceParameterError,
@@ -36,11 +41,14 @@ from .laplace import (
 
 __all__ = [
     "AlphabetConfig",
+    "AlphabetTrainingRuntime",
     "B200Alphabet",
     "B200PoleResidueTemporalMixing",
     "LaplaceParameterError",
     "LaplaceShapeError",
     "ops",
+    "prepare_aggressive_training",
     "prepare_compiled_inference",
+    "prepare_exact_split_training",
     "prepare_maskless_inference",
 ]

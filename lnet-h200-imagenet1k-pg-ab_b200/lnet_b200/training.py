@@ -36,6 +36,11 @@ def effective_tensors(model) -> list[Tensor]:
     differentiably from ``model``'s parameters."""
     fb, bb = model.forward_block, model.backward_block
     d, k = model.model_dim, model.dwconv_kernel_size
+    # lnet_b200.train_runtime swaps in a capture-safe frame builder
+    frame_fn = getattr(model, "_frame_fn", None)
+
+    def frame(block):
+        return frame_fn(block.frame) if frame_fn is not None else block.frame_matrix()
 
     def f(t: Tensor) -> Tensor:
         return t.float().contiguous()
@@ -45,7 +50,7 @@ def effective_tensors(model) -> list[Tensor]:
         f(model.stem.local.weight.reshape(d, k)),
         f(model.stem.local.bias),
         f(fb.norm.weight),
-        f(fb.frame_matrix()),
+        f(frame(fb)),
         f(fb.raw_decay),
         f(fb.raw_frequency),
         f(fb.direct_scale),
@@ -53,7 +58,7 @@ def effective_tensors(model) -> list[Tensor]:
         f(model.second_local.weight.reshape(d, k)),
         f(model.second_local.bias),
         f(bb.norm.weight),
-        f(bb.frame_matrix()),
+        f(frame(bb)),
         f(bb.raw_decay),
         f(bb.raw_frequency),
         f(model.head.classifier.weight),
