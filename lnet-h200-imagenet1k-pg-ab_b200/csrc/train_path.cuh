@@ -345,13 +345,19 @@ __global__ void moments_backward_kernel(const float *__restrict__ s, const float
     cl[l] = valid ? counts[b * 4 + 1 + l] : (float)(steps - lags[l]);
   const float *srow = s + b * steps * M2;
   float *orow = dS + b * steps * M2;
+  // the count normalisations folded into the per-mode cotangents (no division
+  // per step)
+  const float ic0 = 1.f / c0;
+  float icl[3];
+#pragma unroll
+  for (int l = 0; l < 3; ++l) icl[l] = 1.f / cl[l];
   for (int m = threadIdx.x; m < modes; m += blockDim.x) {
-    const float ge = g[m];
+    const float ge2 = 2.f * g[m] * ic0;
     float dr[3], di[3];
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
-      dr[l] = g[(1 + 2 * l) * modes + m];
-      di[l] = g[(2 + 2 * l) * modes + m];
+      dr[l] = g[(1 + 2 * l) * modes + m] * icl[l];
+      di[l] = g[(2 + 2 * l) * modes + m] * icl[l];
     }
     // w[0..8] = steps t-4 .. t+4; w[9..12] = t+5 .. t+8, loaded four steps
     // before they enter the window
@@ -370,7 +376,7 @@ __global__ void moments_backward_kernel(const float *__restrict__ s, const float
       wi[12] = in ? srow[tn * M2 + modes + m] : 0.f;
       const float cr = wr[4], ci = wi[4];
       const float vt = vrow ? vrow[t] : 1.f;
-      float gr = 2.f * cr * ge * vt / c0, gi = 2.f * ci * ge * vt / c0;
+      float gr = cr * ge2 * vt, gi = ci * ge2 * vt;
 #pragma unroll
       for (int l = 0; l < 3; ++l) {
         const int lag = lags[l];
@@ -378,14 +384,14 @@ __global__ void moments_backward_kernel(const float *__restrict__ s, const float
         if (t >= lag) {  // t as the current state, s_{t-lag} as the earlier one
           const float pr = wr[4 - lag], pi = wi[4 - lag];
           const float w = vrow ? vt * vrow[t - lag] : 1.f;
-          gr += (dr[l] * pr - di[l] * pi) * w / cl[l];
-          gi += (dr[l] * pi + di[l] * pr) * w / cl[l];
+          gr += (dr[l] * pr - di[l] * pi) * w;
+          gi += (dr[l] * pi + di[l] * pr) * w;
         }
         if (t + lag < steps) {  // t as the earlier state of s_{t+lag}
           const float nr = wr[4 + lag], ni = wi[4 + lag];
           const float w = vrow ? vt * vrow[t + lag] : 1.f;
-          gr += (dr[l] * nr + di[l] * ni) * w / cl[l];
-          gi += (dr[l] * ni - di[l] * nr) * w / cl[l];
+          gr += (dr[l] * nr + di[l] * ni) * w;
+          gi += (dr[l] * ni - di[l] * nr) * w;
         }
       }
       float *out = orow + t * M2;
@@ -500,58 +506,74 @@ __global__ void rscan_apply_kernel(float *__restrict__ dS, const float *__restri
       nai = z.a_im;
     }
     float dar = 0.f, dai = 0.f, dgr = 0.f, dgi = 0.f;
-    for (int64_t t = t1 - 1; t >= t0; --t) {
-      const int64_t tok = b * steps + t;
-      float *row = dS + tok * M2;
-      const float nr = row[m] + nar * lr + nai * li;
-      const float ni = row[modes + m] + nar * li - nai * lr;
-      lr = nr;
-      li = ni;
-      const Zoh z = step_zoh(a_re, a_im, g_re, g_im, raw_decay, raw_freq, dt, tok, m);
-      const float ar = z.a_re, ai = z.a_im, gr = z.g_re, gi = z.g_im;
-      const float *st_ = s + tok * M2;
-      const float sr = st_[m], si = st_[modes + m];
-      float pr = 0.f, pi = 0.f;
-      if (t > 0) {
-        pr = st_[m - M2];
-        pi = st_[modes + m - M2];
-      }
-      const float ddr = lr * pr + li * pi, ddi = -lr * pi + li * pr;  // da at this step
-      const float ur = sr - (ar * pr - ai * pi), ui = si - (ai * pr + ar * pi);
-      const float gden = gr * gr + gi * gi;
-      const float er = (ur * gr + ui * gi) / gden, ei = (ui * gr - ur * gi) / gden;
-      const float dgr_ = lr * er + li * ei, dgi_ = -lr * ei + li * er;  // dg at this step
-      if (dt) {
-        // dL/dp += Re/Im pairs with a'(p) = dt a and g'(p) = (dt a p - (a - 1)) / p^2
-        const double h = (double)dt[tok];
-        const double far = h * ar, fai = h * ai;
-        double fgr = 0.0, fgi = 0.0;
-        if (sqrt(pr_ * pr_ + pi_ * pi_) * h >= 1.0e-6) {
-          const double apr = ar * pr_ - ai * pi_, api = ar * pi_ + ai * pr_;
-          const double nr2 = h * apr - (ar - 1.0), ni2 = h * api - ai;
-          const double p2r = pr_ * pr_ - pi_ * pi_, p2i = 2.0 * pr_ * pi_;
-          const double den = p2r * p2r + p2i * p2i;
-          fgr = (nr2 * p2r + ni2 * p2i) / den;
-          fgi = (ni2 * p2r - nr2 * p2i) / den;
+    // groups of up to 8 steps (descending): the group's dS and state loads (and
+    // the state one step before it) are issued before its dependent steps
+    for (int64_t tg = t1 - 1; tg >= t0; tg -= 8) {
+      const int n = (int)(tg - t0 + 1 < 8 ? tg - t0 + 1 : 8);
+      float xr[8], xi[8], svr[9], svi[9];
+#pragma unroll
+      for (int k = 0; k < 9; ++k) {
+        const int64_t t = tg - k;
+        const bool ld = k <= n && t >= 0;
+        const int64_t tok = b * steps + t;
+        svr[k] = ld ? s[tok * M2 + m] : 0.f;
+        svi[k] = ld ? s[tok * M2 + modes + m] : 0.f;
+        if (k < 8) {
+          xr[k] = k < n ? dS[tok * M2 + m] : 0.f;
+          xi[k] = k < n ? dS[tok * M2 + modes + m] : 0.f;
         }
-        pdr += ddr * far + ddi * fai + dgr_ * fgr + dgi_ * fgi;
-        pdi += -ddr * fai + ddi * far - dgr_ * fgi + dgi_ * fgr;
-      } else {
-        dar += ddr;
-        dai += ddi;
-        dgr += dgr_;
-        dgi += dgi_;
       }
-      float ev = 1.f;  // u = event g e: de carries the event mask (amax over channels)
-      if (event_mask) {
-        const float *om = event_mask + tok * obs_channels;
-        ev = om[0];
-        for (int c2 = 1; c2 < obs_channels; ++c2) ev = fmaxf(ev, om[c2]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k >= n) break;
+        const int64_t t = tg - k;
+        const int64_t tok = b * steps + t;
+        float *row = dS + tok * M2;
+        const float nr = xr[k] + nar * lr + nai * li;
+        const float ni = xi[k] + nar * li - nai * lr;
+        lr = nr;
+        li = ni;
+        const Zoh z = step_zoh(a_re, a_im, g_re, g_im, raw_decay, raw_freq, dt, tok, m);
+        const float ar = z.a_re, ai = z.a_im, gr = z.g_re, gi = z.g_im;
+        const float sr = svr[k], si = svi[k];
+        const float pr = svr[k + 1], pi = svi[k + 1];  // zero before step 0
+        const float ddr = lr * pr + li * pi, ddi = -lr * pi + li * pr;  // da at this step
+        const float ur = sr - (ar * pr - ai * pi), ui = si - (ai * pr + ar * pi);
+        const float igden = 1.f / (gr * gr + gi * gi);
+        const float er = (ur * gr + ui * gi) * igden, ei = (ui * gr - ur * gi) * igden;
+        const float dgr_ = lr * er + li * ei, dgi_ = -lr * ei + li * er;  // dg at this step
+        if (dt) {
+          // dL/dp += Re/Im pairs with a'(p) = dt a and g'(p) = (dt a p - (a - 1)) / p^2
+          const double h = (double)dt[tok];
+          const double far = h * ar, fai = h * ai;
+          double fgr = 0.0, fgi = 0.0;
+          if (sqrt(pr_ * pr_ + pi_ * pi_) * h >= 1.0e-6) {
+            const double apr = ar * pr_ - ai * pi_, api = ar * pi_ + ai * pr_;
+            const double nr2 = h * apr - (ar - 1.0), ni2 = h * api - ai;
+            const double p2r = pr_ * pr_ - pi_ * pi_, p2i = 2.0 * pr_ * pi_;
+            const double den = p2r * p2r + p2i * p2i;
+            fgr = (nr2 * p2r + ni2 * p2i) / den;
+            fgi = (ni2 * p2r - nr2 * p2i) / den;
+          }
+          pdr += ddr * far + ddi * fai + dgr_ * fgr + dgi_ * fgi;
+          pdi += -ddr * fai + ddi * far - dgr_ * fgi + dgi_ * fgr;
+        } else {
+          dar += ddr;
+          dai += ddi;
+          dgr += dgr_;
+          dgi += dgi_;
+        }
+        float ev = 1.f;  // u = event g e: de carries the event mask (amax over channels)
+        if (event_mask) {
+          const float *om = event_mask + tok * obs_channels;
+          ev = om[0];
+          for (int c2 = 1; c2 < obs_channels; ++c2) ev = fmaxf(ev, om[c2]);
+        }
+        row[m] = (lr * gr + li * gi) * ev;  // de = conj(g) lambda
+        row[modes + m] = (-lr * gi + li * gr) * ev;
+        nar = ar;
+        nai = ai;
       }
-      row[m] = (lr * gr + li * gi) * ev;  // de = conj(g) lambda
-      row[modes + m] = (-lr * gi + li * gr) * ev;
-      nar = ar;
-      nai = ai;
     }
     float *pp = polepart + (b * n_chunks + c) * 4 * modes;
     if (dt) {
@@ -774,67 +796,89 @@ __global__ void __launch_bounds__(256) conv_backward_kernel(
   const float *rdy = dy + b * steps * dim;
   const float *im = in_mask ? in_mask + b * steps : nullptr;
   const float *om = out_mask ? out_mask + b * steps : nullptr;
-  for (int i = threadIdx.x; i < xrows * quads; i += blockDim.x) {
-    const int r = i / quads, q = i - (i / quads) * quads;
-    const int64_t t = s0 - 2 * pad + r;
-    const bool live = t >= 0 && t < steps;
-    cp_async16(sx + r * dim + 4 * q, rin + (live ? t : 0) * dim + 4 * q, live ? 16 : 0);
-  }
-  for (int i = threadIdx.x; i < zrows * quads; i += blockDim.x) {
-    const int r = i / quads, q = i - (i / quads) * quads;
-    const int64_t t = s0 - pad + r;
-    const bool live = t >= 0 && t < steps;
-    cp_async16(sz + r * dim + 4 * q, rdy + (live ? t : 0) * dim + 4 * q, live ? 16 : 0);
+  // thread -> (row group, 16-byte column quad) for the copies and (row group,
+  // channel) for the arithmetic: no per-element index division
+  const int qgroups = max(1, (int)blockDim.x / quads);
+  const int qg = (int)threadIdx.x / quads, q = (int)threadIdx.x - qg * quads;
+  if (qg < qgroups) {
+    for (int r = qg; r < xrows; r += qgroups) {
+      const int64_t t = s0 - 2 * pad + r;
+      const bool live = t >= 0 && t < steps;
+      cp_async16(sx + r * dim + 4 * q, rin + (live ? t : 0) * dim + 4 * q, live ? 16 : 0);
+    }
+    for (int r = qg; r < zrows; r += qgroups) {
+      const int64_t t = s0 - pad + r;
+      const bool live = t >= 0 && t < steps;
+      cp_async16(sz + r * dim + 4 * q, rdy + (live ? t : 0) * dim + 4 * q, live ? 16 : 0);
+    }
   }
   cp_async_wait_all();
   __syncthreads();
+  const int groups = max(1, (int)blockDim.x / dim);
+  const int gid = (int)threadIdx.x / dim, d = (int)threadIdx.x - gid * dim;
   if (im) {
-    for (int i = threadIdx.x; i < xrows * dim; i += blockDim.x) {
-      const int64_t t = s0 - 2 * pad + i / dim;
-      if (t >= 0 && t < steps) sx[i] *= im[t];
-    }
+    if (gid < groups)
+      for (int r = gid; r < xrows; r += groups) {
+        const int64_t t = s0 - 2 * pad + r;
+        if (t >= 0 && t < steps) sx[r * dim + d] *= im[t];
+      }
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < zrows * dim; i += blockDim.x) {
-    const int r = i / dim, d = i - (i / dim) * dim;
-    const int64_t t = s0 - pad + r;
-    float gz = 0.f;
-    if (t >= 0 && t < steps) {
-      float z = 0.f;
+  if (gid < groups) {
+    float wk[TAPS];
 #pragma unroll
-      for (int k = 0; k < TAPS; ++k) z = fmaf(w[d * TAPS + k], sx[(r + k * dil) * dim + d], z);
-      z += bias[d];
-      const float sg = 1.0f / (1.0f + expf(-z));
-      gz = sz[i] * sg * (1.0f + z * (1.0f - sg));
-      if (om) gz *= om[t];
+    for (int k = 0; k < TAPS; ++k) wk[k] = w[d * TAPS + k];
+    const float bd = bias[d];
+    for (int r = gid; r < zrows; r += groups) {
+      const int64_t t = s0 - pad + r;
+      float gz = 0.f;
+      if (t >= 0 && t < steps) {
+        float z = 0.f;
+#pragma unroll
+        for (int k = 0; k < TAPS; ++k) z = fmaf(wk[k], sx[(r + k * dil) * dim + d], z);
+        z += bd;
+        const float sg = __fdividef(1.0f, 1.0f + __expf(-z));
+        gz = sz[r * dim + d] * sg * (1.0f + z * (1.0f - sg));
+        if (om) gz *= om[t];
+      }
+      sz[r * dim + d] = gz;
     }
-    sz[i] = gz;
   }
   __syncthreads();
   const int n_core = (int)min((int64_t)kCbTile, steps - s0);
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
-    float wk[TAPS], aw[TAPS];
+  // the core steps are dealt round-robin to the `groups` thread groups of each
+  // channel; their weight / bias sums meet in shared memory (the input tile's
+  // space, free once every thread has passed the barrier below)
+  float aw[TAPS + 1];
 #pragma unroll
-    for (int k = 0; k < TAPS; ++k) {
-      wk[k] = w[d * TAPS + k];
-      aw[k] = 0.f;
-    }
-    float ab = 0.f;
-    for (int r = 0; r < n_core; ++r) {
+  for (int k = 0; k <= TAPS; ++k) aw[k] = 0.f;
+  if (gid < groups) {
+    float wk[TAPS];
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) wk[k] = w[d * TAPS + k];
+    for (int r = gid; r < n_core; r += groups) {
       float acc = 0.f;
 #pragma unroll
       for (int k = 0; k < TAPS; ++k) acc = fmaf(wk[k], sz[(r - k * dil + 2 * pad) * dim + d], acc);
       if (im) acc *= im[s0 + r];
       dx[(b * steps + s0 + r) * dim + d] = acc;
       const float g = sz[(r + pad) * dim + d];
-      ab += g;
+      aw[TAPS] += g;
 #pragma unroll
       for (int k = 0; k < TAPS; ++k) aw[k] = fmaf(g, sx[(r + pad + k * dil) * dim + d], aw[k]);
     }
-    float *out = partial + (int64_t)blockIdx.x * dim * (TAPS + 1) + d * (TAPS + 1);
+  }
+  __syncthreads();
+  float *red = sx;  // [groups][dim][TAPS + 1]
+  if (gid < groups) {
 #pragma unroll
-    for (int k = 0; k < TAPS; ++k) out[k] = aw[k];
-    out[TAPS] = ab;
+    for (int k = 0; k <= TAPS; ++k) red[(gid * dim + d) * (TAPS + 1) + k] = aw[k];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < dim * (TAPS + 1); i += blockDim.x) {
+    float v = 0.f;
+    for (int q = 0; q < groups; ++q) v += red[q * dim * (TAPS + 1) + i];
+    partial[(int64_t)blockIdx.x * dim * (TAPS + 1) + i] = v;
   }
 }
 
@@ -1147,7 +1191,7 @@ static int conv_backward(const TrainPlan &tp, const float *in, const float *w, c
                                              (int)smem),
                         "cudaFuncSetAttribute(conv_backward_kernel)"));
     const unsigned cb_grid = (unsigned)(B * cdiv(T, kCbTile));
-    const unsigned cb_threads = (unsigned)std::min(256, (int)cdiv(D, 32) * 32);
+    const unsigned cb_threads = 256;  // D <= 256: every channel has at least one thread
     conv_backward_kernel<5><<<cb_grid, cb_threads, smem, st>>>(in, w, bias, in_mask, out_mask,
                                                                 dy, dx, tp.colpart, T, D, dil);
     LNET_TRY(after_launch("conv_backward_kernel"));
