@@ -261,6 +261,23 @@ static int stem_generic(const lnet_b200_alphabet_params *p, const lnet_b200_alph
                         "depthwise_conv(stem)");
 }
 
+// RMSNorm of [tokens, D] fp32 rows: the float4 kernel where the rows allow it.
+static int rmsnorm(const float *in, const float *g, float *out, int64_t tokens, int D,
+                   cudaStream_t st) {
+  auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  const int quads = D / 4;
+  const bool pow2 = quads > 0 && (quads & (quads - 1)) == 0;
+  if (D % 4 == 0 && (pow2 || quads % 32 == 0) && al(in) && al(g) && al(out)) {
+    const int per_warp = quads < 32 ? 32 / quads : 1;
+    rmsnorm4_kernel<<<(unsigned)cdiv(tokens, 8 * per_warp), 256, 0, st>>>(
+        reinterpret_cast<const float4 *>(in), reinterpret_cast<const float4 *>(g),
+        reinterpret_cast<float4 *>(out), tokens, quads);
+    return after_launch("rmsnorm_kernel");
+  }
+  rmsnorm_kernel<<<(unsigned)cdiv(tokens, 8), 256, 0, st>>>(in, g, out, tokens, D);
+  return after_launch("rmsnorm_kernel");
+}
+
 // Block body shared by writer and reader: RMSNorm -> drive -> ZOH gamma -> scan -> moments.
 // `write_states`: leave the states in pl.drive (the writer's synthesis reads them).
 // `normed`: pl.xhat already holds RMSNorm(in); `xhat_bf16`: in bf16 (static
@@ -275,8 +292,7 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   const int64_t B = r->batch, T = r->steps, bt = B * T;
   const bool tf32 = r->act_dtype == LNET_BF16;
   if (!normed) {  // else pl.xhat holds RMSNorm(in) already (conv_norm)
-    rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, norm, pl.xhat, bt, D);
-    LNET_TRY(after_launch("rmsnorm_kernel"));
+    LNET_TRY(rmsnorm(in, norm, pl.xhat, bt, D, st));
   }
   if (!r->time_delta) {  // per-mode a and gamma tables (static poles)
     zoh_kernel<<<1, 128, 0, st>>>(raw_decay, raw_freq, M, nullptr, 1, a_re, a_im, g_re, g_im);
@@ -296,7 +312,8 @@ static int block_scan_moments(const float *in, const float *norm, const float *f
   } else {
     LNET_TRY(gemm_rows(st, pl.xhat, CUDA_R_32F, D, frame, CUDA_R_32F, 1, 2 * M, pl.drive, 2 * M,
                        bt, 2 * M, D, tf32, "gemm(drive)"));
-    drive_kernel<<<(unsigned)cdiv(bt, kDriveTokens), 256, 0, st>>>(pl.drive, raw_decay, raw_freq,
+    const unsigned mx = (unsigned)std::min(256, (int)cdiv(M, 32) * 32);
+    drive_kernel<<<(unsigned)cdiv(bt, kDriveTokens), dim3(mx, 256 / mx), 0, st>>>(pl.drive, raw_decay, raw_freq,
                                                             r->time_delta, g_re, g_im, event_mask,
                                                             obs_channels, bt, M, pl.step_a);
     LNET_TRY(after_launch("drive_kernel"));
@@ -820,8 +837,7 @@ extern "C" int lnet_b200_block_drive(const lnet_b200_alphabet_params *params,
   const int D = params->model_dim, M = params->modes;
   const BlockParams bp = block_params(params, block);
   float *xhat = xhat_out ? xhat_out : pl.xhat;
-  rmsnorm_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(in, bp.norm, xhat, bt, D);
-  LNET_TRY(after_launch("rmsnorm_kernel"));
+  LNET_TRY(rmsnorm(in, bp.norm, xhat, bt, D, st));
   // the same arithmetic as the unsplit forward: one GEMM over the gain-folded
   // frame, bf16 operands for bf16 requests (half_drive)
   float *a_re = pl.a_tab, *a_im = pl.a_tab + M, *g_re = pl.a_tab + 4 * M, *g_im = pl.a_tab + 5 * M;

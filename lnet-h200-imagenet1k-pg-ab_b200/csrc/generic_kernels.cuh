@@ -576,6 +576,35 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
   for (int d = lane; d < dim; d += 32) out[tok * dim + d] = row[d] * rs * g[d];
 }
 
+// The same RMSNorm over float4 quads (dim % 4 == 0, 16-byte aligned rows):
+// `width` = min(dim / 4, 32) lanes per token (a power of two), 32 / width
+// tokens per warp, so short rows (D = 64: 16 quads) still fill the warp.
+__global__ void rmsnorm4_kernel(const float4 *__restrict__ x, const float4 *__restrict__ g,
+                                float4 *__restrict__ out, int64_t tokens, int quads) {
+  const int lane = threadIdx.x & 31;
+  const int width = quads < 32 ? quads : 32;
+  const int per_warp = 32 / width;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t tok = warp * per_warp + lane / width;
+  const int sl = lane & (width - 1);
+  const bool on = tok < tokens;
+  const float4 *row = x + tok * quads;
+  float ss = 0.f;
+  if (on)
+    for (int q = sl; q < quads; q += width) {
+      const float4 v = row[q];
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+  for (int o = width >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!on) return;
+  const float rs = rsqrtf(ss / (float)(4 * quads) + kFp32Eps);
+  for (int q = sl; q < quads; q += width) {
+    const float4 v = row[q], w = g[q];
+    out[tok * quads + q] = make_float4(v.x * rs * w.x, v.y * rs * w.y, v.z * rs * w.z,
+                                       v.w * rs * w.w);
+  }
+}
+
 // ---------------------------------------------------------------- drive (gamma (x) e * mask)
 // e[tok, 0:M] / e[tok, M:2M] -> u in place; gamma from the per-mode table or per step.
 // Without dt the gains are the per-mode table g_tab_re/im (zoh_kernel); with dt
@@ -584,7 +613,7 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 // [tok][re M | im M] for the scans.  A block takes kDriveTokens tokens: the
 // event masks (amax over the raw channels) are reduced once per token by a warp
 // into shared memory, the mode poles once per block, and then one thread per
-// (token, mode) pair, consecutive modes on consecutive lanes.
+// (token, mode) pair, consecutive modes on consecutive lanes (block x).
 constexpr int kDriveTokens = 32;
 constexpr int kDriveMaxModes = 256;
 __global__ void __launch_bounds__(256) drive_kernel(
@@ -608,12 +637,13 @@ __global__ void __launch_bounds__(256) drive_kernel(
       pb = g_tab_im[m];
     }
   };
-  for (int m = threadIdx.x; m < min(modes, kDriveMaxModes); m += blockDim.x)
+  const int tid = threadIdx.y * blockDim.x + threadIdx.x, nthreads = blockDim.x * blockDim.y;
+  for (int m = tid; m < min(modes, kDriveMaxModes); m += nthreads)
     mode_consts(m, s_pa[m], s_pb[m]);
   if (event_mask) {
     // event mask = amax over raw channels (src/lnet/alphabet_backbone.py:568)
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int t = warp; t < ntok; t += blockDim.x >> 5) {
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int t = warp; t < ntok; t += nthreads >> 5) {
       const float *om = event_mask + (tok0 + t) * obs_channels;
       float mx = -INFINITY;
       for (int c = lane; c < obs_channels; c += 32) mx = fmaxf(mx, om[c]);
@@ -623,9 +653,9 @@ __global__ void __launch_bounds__(256) drive_kernel(
     }
   }
   __syncthreads();
-  const int pairs = ntok * modes;
-  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-    const int t = idx / modes, m = idx - t * modes;
+  // 2-D block: x over modes, y over the block's tokens (no index division)
+  for (int t = threadIdx.y; t < ntok; t += blockDim.y)
+  for (int m = threadIdx.x; m < modes; m += blockDim.x) {
     const int64_t tok = tok0 + t;
     float pa, pb;
     if (m < kDriveMaxModes) {
