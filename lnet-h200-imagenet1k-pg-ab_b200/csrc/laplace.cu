@@ -255,7 +255,11 @@ constexpr int kDiagChans = 8;     // channels per CTA
 constexpr size_t kDiagStageBytes = 160 * 1024;
 constexpr int kDiagMaxModes = 16; // K bound (registers per thread)
 
-template <typename TX, int K, bool STAGED>
+// DIMC: the model width when it is a compile-time 16 (the direct-term row of D
+// then lives in registers), else 0 (read per step).  Staged rows are stored
+// per chunk with one double of padding between chunks, so the four chunks a
+// warp spans read different shared-memory banks.
+template <typename TX, int K, bool STAGED, int DIMC>
 __global__ void __launch_bounds__(kDiagChunks * kDiagChans) laplace_diag_kernel(
     const TX *__restrict__ x, const double *__restrict__ raw_decay,
     const int32_t *__restrict__ mode_index, const double *__restrict__ residue,
@@ -268,30 +272,61 @@ __global__ void __launch_bounds__(kDiagChunks * kDiagChans) laplace_diag_kernel(
   const bool live = o < dim;
   const int64_t L = (steps + kDiagChunks - 1) / kDiagChunks;
   const int64_t t_begin = c * L, t_end = min(steps, t_begin + L);
+  // the pole coefficients of the CTA's (channel, mode) pairs, evaluated once per
+  // CTA (not once per chunk thread): a, the input gain g and a^L (L = chunk length)
+  __shared__ double s_coef[3][kDiagChans][K];
+  for (int p = threadIdx.x; p < kDiagChans * K; p += blockDim.x) {
+    const int ol = p / K, j = p - ol * K, oo = blockIdx.x * kDiagChans + ol;
+    double ca = 0.0, cg = 0.0, caL = 1.0;
+    if (oo < dim && j < kmodes) {
+      laplace_zoh(raw_decay[mode_index[oo * kmodes + j]], dt, min_decay, ca, cg);
+      for (int64_t k = 0; k < L; ++k) caL *= ca;
+    }
+    s_coef[0][ol][j] = ca;
+    s_coef[1][ol][j] = cg;
+    s_coef[2][ol][j] = caL;
+  }
+  __syncthreads();
   double a[K], g[K], r[K], s[K];
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    a[j] = 0.0;
-    g[j] = 0.0;
-    r[j] = 0.0;
+    a[j] = s_coef[0][o_loc][j];
+    g[j] = s_coef[1][o_loc][j];
+    r[j] = live && j < kmodes ? residue[o * kmodes + j] : 0.0;
     s[j] = 0.0;
-    if (live && j < kmodes) {
-      laplace_zoh(raw_decay[mode_index[o * kmodes + j]], dt, min_decay, a[j], g[j]);
-      r[j] = residue[o * kmodes + j];
-    }
   }
   const TX *xr = x + b * steps * dim;
   extern __shared__ double s_x[];  // [T][D] when STAGED
   if constexpr (STAGED) {
-    for (int64_t e = threadIdx.x; e < steps * dim; e += blockDim.x) s_x[e] = (double)load_f(xr, e);
+    // eight independent loads in flight per thread per round
+    const int64_t n = steps * dim;
+    for (int64_t e0 = threadIdx.x; e0 < n; e0 += 8 * (int64_t)blockDim.x) {
+      double v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t e = e0 + u * (int64_t)blockDim.x;
+        v[u] = e < n ? (double)load_f(xr, e) : 0.0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t e = e0 + u * (int64_t)blockDim.x;
+        if (e < n) s_x[e + (e / dim) / L] = v[u];  // + one double per earlier chunk
+      }
+    }
     __syncthreads();
   }
+  const double *s_xc = s_x + c;  // this chunk's padded rows (STAGED)
   auto xin = [&](int64_t e) -> double {
     if constexpr (STAGED)
-      return s_x[e];
+      return s_xc[e];
     else
       return (double)load_f(xr, e);
   };
+  double drow[DIMC > 0 ? DIMC : 1];
+  if constexpr (DIMC > 0) {
+#pragma unroll
+    for (int i = 0; i < DIMC; ++i) drow[i] = live ? direct[o * DIMC + i] : 0.0;
+  }
   // ---- pass 1: local scan from zero
   for (int64_t t = t_begin; t < t_end; ++t) {
     const double xv = live ? xin(t * dim + o) : 0.0;
@@ -305,8 +340,7 @@ __global__ void __launch_bounds__(kDiagChunks * kDiagChans) laplace_diag_kernel(
   // (every earlier chunk is full, L steps)
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    double aL = 1.0;
-    for (int64_t k = 0; k < L; ++k) aL *= a[j];
+    const double aL = s_coef[2][o_loc][j];
     double carry = 0.0;
     for (int cc = 0; cc < c; ++cc) carry = fma(aL, carry, s_end[cc][o_loc][j]);
     s[j] = carry;
@@ -323,8 +357,12 @@ __global__ void __launch_bounds__(kDiagChunks * kDiagChans) laplace_diag_kernel(
     }
     if (live) {
       double dsum = 0.0;
-      for (int i = 0; i < dim; ++i)
-        dsum = fma(xin(t * dim + i), direct[o * dim + i], dsum);
+      if constexpr (DIMC > 0) {
+#pragma unroll
+        for (int i = 0; i < DIMC; ++i) dsum = fma(xin(t * DIMC + i), drow[i], dsum);
+      } else {
+        for (int i = 0; i < dim; ++i) dsum = fma(xin(t * dim + i), direct[o * dim + i], dsum);
+      }
       const double v = acc + dsum + bo;
       if constexpr (sizeof(TX) == 8)
         y[(b * steps + t) * dim + o] = v;
@@ -341,22 +379,28 @@ static int laplace_diag_run(const double *raw_decay, const int32_t *mode_index,
                             int64_t batch, int64_t steps, TX *y, cudaStream_t st) {
   const dim3 grid((unsigned)cdiv(dim, kDiagChans), (unsigned)batch);
   const int threads = kDiagChunks * kDiagChans;
-  const size_t stage = (size_t)steps * dim * sizeof(double);
+  const size_t stage = ((size_t)steps * dim + kDiagChunks) * sizeof(double);  // + chunk pads
   const bool staged = stage <= kDiagStageBytes;
+#define LNET_DIAG_LAUNCH(KK, DC)                                                              \
+  if (staged) {                                                                               \
+    auto kern = laplace_diag_kernel<TX, KK, true, DC>;                                        \
+    LNET_TRY(cuda_check(cudaFuncSetAttribute(kern,                                            \
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                                             (int)kDiagStageBytes),                           \
+                        "cudaFuncSetAttribute(laplace_diag_kernel)"));                        \
+    kern<<<grid, threads, stage, st>>>(x, raw_decay, mode_index, residue, direct, bias, dim,   \
+                                       kmodes, dt, min_decay, steps, y);                      \
+  } else {                                                                                    \
+    laplace_diag_kernel<TX, KK, false, DC><<<grid, threads, 0, st>>>(                         \
+        x, raw_decay, mode_index, residue, direct, bias, dim, kmodes, dt, min_decay, steps,   \
+        y);                                                                                   \
+  }
 #define LNET_DIAG_CASE(KK)                                                                    \
   if (kmodes <= KK) {                                                                         \
-    if (staged) {                                                                             \
-      auto kern = laplace_diag_kernel<TX, KK, true>;                                          \
-      LNET_TRY(cuda_check(cudaFuncSetAttribute(kern,                                          \
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,   \
-                                               (int)kDiagStageBytes),                         \
-                          "cudaFuncSetAttribute(laplace_diag_kernel)"));                      \
-      kern<<<grid, threads, stage, st>>>(x, raw_decay, mode_index, residue, direct, bias, dim, \
-                                         kmodes, dt, min_decay, steps, y);                    \
+    if (dim == 16) {                                                                          \
+      LNET_DIAG_LAUNCH(KK, 16)                                                                \
     } else {                                                                                  \
-      laplace_diag_kernel<TX, KK, false><<<grid, threads, 0, st>>>(                           \
-          x, raw_decay, mode_index, residue, direct, bias, dim, kmodes, dt, min_decay, steps, \
-          y);                                                                                 \
+      LNET_DIAG_LAUNCH(KK, 0)                                                                 \
     }                                                                                         \
     return after_launch("laplace_diag_kernel");                                               \
   }
@@ -364,6 +408,7 @@ static int laplace_diag_run(const double *raw_decay, const int32_t *mode_index,
   LNET_DIAG_CASE(8)
   LNET_DIAG_CASE(16)
 #undef LNET_DIAG_CASE
+#undef LNET_DIAG_LAUNCH
   return fail(LNET_ERR_UNSUPPORTED, "laplace (channel-diagonal): %d modes per channel > %d",
               kmodes, kDiagMaxModes);
 }
