@@ -267,8 +267,8 @@ static int rmsnorm(const float *in, const float *g, float *out, int64_t tokens, 
   auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
   const int quads = D / 4;
   const bool pow2 = quads > 0 && (quads & (quads - 1)) == 0;
-  if (D % 4 == 0 && (pow2 || quads % 32 == 0) && al(in) && al(g) && al(out)) {
-    const int per_warp = quads < 32 ? 32 / quads : 1;
+  if (D % 4 == 0 && quads > 0 && al(in) && al(g) && al(out)) {
+    const int per_warp = quads < 32 && pow2 ? 32 / quads : 1;
     rmsnorm4_kernel<<<(unsigned)cdiv(tokens, 8 * per_warp), 256, 0, st>>>(
         reinterpret_cast<const float4 *>(in), reinterpret_cast<const float4 *>(g),
         reinterpret_cast<float4 *>(out), tokens, quads);

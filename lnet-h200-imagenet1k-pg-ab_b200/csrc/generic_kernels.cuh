@@ -577,12 +577,13 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 }
 
 // The same RMSNorm over float4 quads (dim % 4 == 0, 16-byte aligned rows):
-// `width` = min(dim / 4, 32) lanes per token (a power of two), 32 / width
-// tokens per warp, so short rows (D = 64: 16 quads) still fill the warp.
+// `width` lanes per token -- dim / 4 when that is a power of two below 32, so
+// 32 / width tokens share a warp and short rows (D = 64: 16 quads) still fill
+// it; else 32 lanes striding over the quads.
 __global__ void rmsnorm4_kernel(const float4 *__restrict__ x, const float4 *__restrict__ g,
                                 float4 *__restrict__ out, int64_t tokens, int quads) {
   const int lane = threadIdx.x & 31;
-  const int width = quads < 32 ? quads : 32;
+  const int width = quads < 32 && (quads & (quads - 1)) == 0 ? quads : 32;
   const int per_warp = 32 / width;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t tok = warp * per_warp + lane / width;

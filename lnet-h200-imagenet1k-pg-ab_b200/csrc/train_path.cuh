@@ -659,6 +659,66 @@ __global__ void rms_backward_kernel(const float *__restrict__ y, const float *__
   if (lane == 0) rs_out[tok] = rs;
 }
 
+// The same VJP over float4 quads (dim % 4 == 0, 16-byte aligned rows), with the
+// lane layout of rmsnorm4_kernel: `width` lanes per token.
+__global__ void rms_backward4_kernel(const float4 *__restrict__ y, const float4 *__restrict__ dxh,
+                                     const float4 *__restrict__ g, const float4 *__restrict__ add,
+                                     float4 *__restrict__ dy, float *__restrict__ rs_out,
+                                     int64_t tokens, int quads) {
+  const int lane = threadIdx.x & 31;
+  const int width = quads < 32 && (quads & (quads - 1)) == 0 ? quads : 32;
+  const int per_warp = 32 / width;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t tok = warp * per_warp + lane / width;
+  const int sl = lane & (width - 1);
+  const bool on = tok < tokens;
+  const float4 *yr = y + tok * quads, *dr = dxh + tok * quads;
+  float ss = 0.f, dot = 0.f;
+  if (on)
+    for (int q = sl; q < quads; q += width) {
+      const float4 v = yr[q], d = dr[q], w = g[q];
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      dot = fmaf(d.x * w.x, v.x, fmaf(d.y * w.y, v.y, fmaf(d.z * w.z, v.z, fmaf(d.w * w.w, v.w, dot))));
+    }
+  for (int o = width >> 1; o > 0; o >>= 1) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  }
+  if (!on) return;
+  const float rs = rsqrtf(ss / (float)(4 * quads) + kFp32Eps);
+  const float k = rs * rs * rs * dot / (float)(4 * quads);
+  for (int q = sl; q < quads; q += width) {
+    const float4 v = yr[q], d = dr[q], w = g[q];
+    float4 o = make_float4(rs * w.x * d.x - v.x * k, rs * w.y * d.y - v.y * k,
+                           rs * w.z * d.z - v.z * k, rs * w.w * d.w - v.w * k);
+    if (add) {
+      const float4 a = add[tok * quads + q];
+      o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+    }
+    dy[tok * quads + q] = o;
+  }
+  if (sl == 0) rs_out[tok] = rs;
+}
+
+// rms_backward_kernel or, where the rows allow it, rms_backward4_kernel.
+static int rms_backward(const float *y, const float *dxh, const float *g, const float *add,
+                        float *dy, float *rs, int64_t tokens, int D, cudaStream_t st) {
+  auto al = [](const void *q) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  const int quads = D / 4;
+  if (D % 4 == 0 && quads > 0 && al(y) && al(dxh) && al(g) && al(add) && al(dy)) {
+    const bool pow2 = (quads & (quads - 1)) == 0;
+    const int per_warp = quads < 32 && pow2 ? 32 / quads : 1;
+    rms_backward4_kernel<<<(unsigned)cdiv(tokens, 8 * per_warp), 256, 0, st>>>(
+        reinterpret_cast<const float4 *>(y), reinterpret_cast<const float4 *>(dxh),
+        reinterpret_cast<const float4 *>(g), reinterpret_cast<const float4 *>(add),
+        reinterpret_cast<float4 *>(dy), rs, tokens, quads);
+  } else {
+    rms_backward_kernel<<<(unsigned)cdiv(tokens, 8), 256, 0, st>>>(y, dxh, g, add, dy, rs,
+                                                                  tokens, D);
+  }
+  return after_launch("rms_backward_kernel");
+}
+
 // Conv + SiLU VJP, pre-activation gradient: dz = dy * out_mask * silu'(z),
 // z = bias + sum_k w_k in[t + k dil - pad] * in_mask (recomputed).
 __global__ void conv_dz_kernel(const float *__restrict__ in, const float *__restrict__ w,
@@ -1297,9 +1357,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
                           tp.a_tab + 6 * M, tp.a_tab + 7 * M, tp.dX, 0.f, gd->reader_frame, 0.f,
                           gd->reader_raw_decay, gd->reader_raw_frequency, B, T, D, M, tf32,
                           nullptr, 1, r->time_delta, st));
-  rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y2, tp.dX, p->reader_norm,
-                                                             nullptr, tp.dY, tp.rs, bt, D);
-  LNET_TRY(after_launch("rms_backward_kernel"));
+  LNET_TRY(rms_backward(tp.y2, tp.dX, p->reader_norm, nullptr, tp.dY, tp.rs, bt, D, st));
   LNET_TRY(colsum(ColRmsGamma{tp.dX, tp.y2, tp.rs, D}, bt, D, tp.colpart, gd->reader_norm, st,
                   "colsum(reader norm)"));
   // reader conv: input v (masked), dv out
@@ -1333,9 +1391,7 @@ static int train_backward_impl(const lnet_b200_alphabet_params *p,
                           gd->writer_raw_decay, gd->writer_raw_frequency, B, T, D, M, tf32,
                           r->observation_mask, r->obs_channels, r->time_delta, st));
   // writer RMSNorm: dy1 = rms VJP + dv (residual identity)
-  rms_backward_kernel<<<(unsigned)cdiv(bt, 8), 256, 0, st>>>(tp.y1, tp.dX, p->writer_norm, tp.dV,
-                                                             tp.dY, tp.rs, bt, D);
-  LNET_TRY(after_launch("rms_backward_kernel"));
+  LNET_TRY(rms_backward(tp.y1, tp.dX, p->writer_norm, tp.dV, tp.dY, tp.rs, bt, D, st));
   LNET_TRY(colsum(ColRmsGamma{tp.dX, tp.y1, tp.rs, D}, bt, D, tp.colpart, gd->writer_norm, st,
                   "colsum(writer norm)"));
   // stem conv: input proj (no input mask), output mask valid; dproj -> tp.dV
